@@ -1,0 +1,424 @@
+"""CPU ORACLE (test infrastructure only): numpy restatement of the reference's
+graph interpreter and of the numpy-backend op kernels on the fwd+bwd hot path.
+
+Only ``tests/``, ``__graft_entry__.smoke()`` and ``bench.py``'s CPU-baseline leg may
+import this module, and only as the checker or as the timed CPU reference. The
+``b200`` backend never calls it.
+
+Interpreter: ``evaluate`` follows ``interpreter/evaluator.py:272-305`` (env = inputs,
+nodes in dependency order, every node evaluated, outputs read back) and
+``_evaluate_node`` (``evaluator.py:738-769``: Input / Output / Identity / Constant /
+dispatch) with the op aliases of ``_get_op_alias`` (``evaluator.py:771-791``) and the
+kwargs rules of ``_prepare_node_kwargs`` (``evaluator.py:793-832``).
+
+Op kernels: each ``_op_*`` cites the reference kernel it restates. numpy dtype
+behaviour is kept (fp32 stays fp32; a Python-float constant is a float64 0-d array,
+``evaluator.py:760-761``).
+
+Parity of this restatement is pinned by ``tests/test_oracle.py`` against the golden
+vectors that ``tests/golden/make_golden.py`` produced by running the reference's own
+``evaluate_graph`` on the same graphs, and against the reference's known-answer tests
+(``tests/backends/test_hardware_parity.py:164-205``,
+``tests/distributed/test_multi_process_collectives.py:83-103``).
+"""
+
+from __future__ import annotations
+
+import gzip
+import json
+import math
+import os
+from typing import Any
+
+import numpy as np
+
+GOLDEN_DIR = os.path.join(os.path.dirname(os.path.dirname(os.path.abspath(__file__))), "tests", "golden")
+
+_ALIASES = {  # evaluator.py:771-791
+    "Sub": "Subtract",
+    "Mul": "Multiply",
+    "Div": "TrueDivide",
+    "Neg": "Negative",
+    "Pow": "Power",
+    "MatMul": "Matmul",
+    "Expand": "BroadcastTo",
+    "Permute": "Transpose",
+}
+
+
+def load_graph(name_or_path: str) -> dict:
+    """Load a serialized LogicalGraph (``tests/golden/graphs/<name>.json.gz``)."""
+    path = name_or_path
+    if not os.path.exists(path):
+        path = os.path.join(GOLDEN_DIR, "graphs", name_or_path + ".json.gz")
+    with gzip.open(path, "rt", encoding="utf-8") as f:
+        return json.load(f)
+
+
+def topo_order(graph: dict) -> list[dict]:
+    """Dependency order over all nodes (``core/utils/graph_utils.py:29-100`` is a DFS;
+    any dependency order gives identical values for this side-effect-free graph)."""
+    nodes = {n["id"]: n for n in graph["nodes"]}
+    order, state = [], {}
+    for root in nodes:
+        if root in state:
+            continue
+        stack = [(root, 0)]
+        while stack:
+            nid, i = stack.pop()
+            if i == 0:
+                if state.get(nid) == 2:
+                    continue
+                state[nid] = 1
+            deps = [d for d in nodes[nid]["inputs"] if d in nodes]
+            if i < len(deps):
+                stack.append((nid, i + 1))
+                d = deps[i]
+                if state.get(d) == 1:
+                    raise ValueError("cycle in graph")  # CompilationError in the reference
+                if d not in state:
+                    stack.append((d, 0))
+            else:
+                state[nid] = 2
+                order.append(nodes[nid])
+    return order
+
+
+def _kwargs(node: dict, target: str) -> dict:
+    """``_prepare_node_kwargs`` (evaluator.py:793-832)."""
+    kw = {k: v for k, v in (node.get("attributes") or {}).items() if k not in ("var_name", "is_parameter", "param_name")}
+    conv_like = {"Conv", "Conv1D", "Conv2D", "Conv3D", "ConvTranspose", "ConvTranspose2D", "MaxPool2D", "AvgPool2D", "StridedSlice"}
+    if "strides" in kw and target not in conv_like:
+        kw.pop("strides")
+    meta = node.get("shape_metadata")
+    if meta:
+        mt = tuple(int(d) if isinstance(d, int) else str(d) for d in meta)
+        if target in ("Expand", "BroadcastTo", "ConstantOfShape", "Zeros", "Ones", "Full") and "shape" not in kw:
+            kw["shape"] = mt
+        if target == "Reshape" and "newshape" not in kw:
+            kw["newshape"] = mt
+    return kw
+
+
+# ----------------------------------------------------------------------------------
+# op kernels
+# ----------------------------------------------------------------------------------
+
+
+def _op_matmul(a, b, transpose_a=False, transpose_b=False, **_):
+    # backends/eager/core_math_ops/math_matrix.py:21-44
+    if transpose_a:
+        a = np.swapaxes(a, -1, -2)
+    if transpose_b:
+        b = np.swapaxes(b, -1, -2)
+    return np.matmul(a, b)
+
+
+def _op_gelu(x, **_):
+    # backends/eager/core_math_ops/math_nn.py:184-199 (tanh approximation)
+    return 0.5 * x * (1.0 + np.tanh(math.sqrt(2.0 / math.pi) * (x + 0.044715 * (x**3))))
+
+
+def _op_softmax(a, axis=-1, **_):
+    # backends/numpy/eager/math_advanced/math_signal.py:450-467
+    e = np.exp(a - np.max(a, axis=axis, keepdims=True))
+    return e / e.sum(axis=axis, keepdims=True)
+
+
+def _op_log_softmax(a, axis=-1, **_):
+    # backends/numpy/eager/math_advanced/math_log_exp.py:87-104
+    c = np.max(a, axis=axis, keepdims=True)
+    return a - c - np.log(np.sum(np.exp(a - c), axis=axis, keepdims=True))
+
+
+def _ln_stats(x, eps, axis):
+    mean = np.mean(x, axis=axis, keepdims=True)
+    var = np.var(x, axis=axis, keepdims=True)
+    return mean, var
+
+
+def _op_layer_norm(x, gamma=None, beta=None, eps=1e-5, axis=-1, **kw):
+    # backends/numpy/eager/nn_ops.py:219-241
+    eps = float(kw.get("epsilon", eps))
+    gamma = np.ones(x.shape[-1], x.dtype) if gamma is None else gamma
+    beta = np.zeros(x.shape[-1], x.dtype) if beta is None else beta
+    mean, var = _ln_stats(x, eps, axis)
+    return gamma * ((x - mean) / np.sqrt(var + eps)) + beta
+
+
+def _op_layer_norm_input_grad(d_out, x, gamma=None, eps=1e-5, axis=-1, **_):
+    # backends/numpy/eager/nn_ops.py:244-273
+    gamma = np.ones(x.shape[-1], x.dtype) if gamma is None else gamma
+    d = float(x.shape[int(axis)])
+    mean, var = _ln_stats(x, eps, axis)
+    inv_std = 1.0 / np.sqrt(var + eps)
+    x_hat = (x - mean) * inv_std
+    d_y = d_out * gamma
+    term2 = np.sum(d_y, axis=axis, keepdims=True)
+    term3 = x_hat * np.sum(d_y * x_hat, axis=axis, keepdims=True)
+    return (inv_std / d) * (d * d_y - term2 - term3)
+
+
+def _op_layer_norm_gamma_grad(d_out, x, eps=1e-5, axis=-1, **_):
+    # backends/numpy/eager/nn_ops.py:276-297
+    mean, var = _ln_stats(x, eps, axis)
+    x_hat = (x - mean) / np.sqrt(var + eps)
+    ax = x.ndim + int(axis) if int(axis) < 0 else int(axis)
+    return np.sum(d_out * x_hat, axis=tuple(i for i in range(x.ndim) if i != ax))
+
+
+def _op_layer_norm_beta_grad(d_out, axis=-1, **_):
+    # backends/numpy/eager/nn_ops.py:300-318
+    ax = d_out.ndim + int(axis) if int(axis) < 0 else int(axis)
+    return np.sum(d_out, axis=tuple(i for i in range(d_out.ndim) if i != ax))
+
+
+def _axis(axis):
+    return tuple(axis) if isinstance(axis, list) else axis
+
+
+def _op_reduce_sum(x, axis=None, keepdims=False, **_):
+    # backends/eager/core_math_ops/math_reduction.py:37-54
+    return np.sum(x, axis=_axis(axis), keepdims=keepdims)
+
+
+def _op_reduce_mean(x, axis=None, keepdims=False, **_):
+    # backends/eager/core_math_ops/math_reduction.py:57-74
+    return np.mean(x, axis=_axis(axis), keepdims=keepdims)
+
+
+def _op_reduce_max(x, axis=None, keepdims=False, **_):
+    # backends/eager/core_math_ops/math_reduction.py:97-114
+    return np.max(x, axis=_axis(axis), keepdims=keepdims)
+
+
+def _op_numel(x, **_):
+    # backends/eager/core_math_ops/math_reduction.py:156-173 (a Python float)
+    return float(np.asarray(x).size)
+
+
+def _op_broadcast_like(src, tgt, **_):
+    # backends/eager/core_math_ops/math_reduction.py:227-249
+    if np.shape(src) == np.shape(tgt):
+        return src
+    return np.broadcast_to(src, np.shape(tgt))
+
+
+def _op_broadcast_reduce(cot, tgt, **_):
+    # backends/eager/core_math_ops/math_reduction.py:192-224
+    cs, ts = np.shape(cot), np.shape(tgt)
+    if cs == ts:
+        return cot
+    res = cot
+    if len(cs) > len(ts):
+        res = np.sum(res, axis=tuple(range(len(cs) - len(ts))))
+    for i, (cd, td) in enumerate(zip(np.shape(res), ts)):
+        if td == 1 and cd > 1:
+            res = np.sum(res, axis=i, keepdims=True)
+    return res
+
+
+def _op_argmax(x, axis=None, **_):
+    # backends/numpy/eager/math_reductions.py:129-140 (np.argmax: first maximum wins)
+    return np.argmax(x, axis=axis)
+
+
+def _op_relu(x, **_):
+    # backends/numpy/eager/activation_ops.py:12 (np.maximum(x, 0))
+    return np.maximum(x, 0)
+
+
+def _op_transpose(x, axes=None, **_):
+    # backends/numpy/eager/array_manipulation.py:121
+    return np.transpose(x, axes)
+
+
+def _op_reshape(x, shape=None, newshape=None, **_):
+    # backends/numpy/eager/array_manipulation.py:87
+    return np.reshape(x, tuple(shape if shape is not None else newshape))
+
+
+def _op_take_along_axis(x, indices, axis=-1, **_):
+    # backends/numpy/eager/advanced_indexing.py:163-177
+    return np.take_along_axis(x, indices, axis=axis)
+
+
+def _op_scatter_add(inp, index, src, dim=0, **_):
+    # backends/numpy/eager/advanced_indexing.py:309-326 (put_along_axis of take+src;
+    # a repeated index along ``dim`` keeps the last write, as in the reference)
+    out = np.copy(inp)
+    np.put_along_axis(out, index, np.add(np.take_along_axis(out, index, axis=dim), src), axis=dim)
+    return out
+
+
+def _op_tensor_scatter_add(tensor, indices, updates, **_):
+    # backends/numpy/eager/math_scatter.py:39-60 (np.add.at accumulates repeats)
+    res = np.array(tensor)
+    idx = tuple(np.moveaxis(np.array(indices), -1, 0))
+    np.add.at(res, idx, np.array(updates))
+    return res
+
+
+def _op_take(a, indices, axis=None, **_):
+    # numpy-backend fallback to np.take (backends/numpy/eager/__init__.py:114-125)
+    return np.take(a, indices, axis=axis)
+
+
+def _conv_pads(in_hw, k_hw, s_hw, padding, out_hw):
+    # backends/numpy/eager/conv.py:590-633 (_compute_conv2d_padding_values, dilation 1)
+    if isinstance(padding, str) and padding.upper() == "SAME":
+        ph = max(0, (out_hw[0] - 1) * s_hw[0] + k_hw[0] - in_hw[0])
+        pw = max(0, (out_hw[1] - 1) * s_hw[1] + k_hw[1] - in_hw[1])
+        return ph // 2, ph - ph // 2, pw // 2, pw - pw // 2
+    return 0, 0, 0, 0
+
+
+def _conv_out_hw(in_hw, k_hw, s_hw, padding):
+    if isinstance(padding, str) and padding.upper() == "SAME":
+        return (-(-in_hw[0] // s_hw[0]), -(-in_hw[1] // s_hw[1]))
+    return ((in_hw[0] - k_hw[0]) // s_hw[0] + 1, (in_hw[1] - k_hw[1]) // s_hw[1] + 1)
+
+
+def _stride2(stride):
+    return (stride, stride) if isinstance(stride, int) else (int(stride[0]), int(stride[1]))
+
+
+def _op_conv2d(x, w, stride=(1, 1), padding="SAME", groups=1, **kw):
+    # backends/numpy/eager/conv.py:462-489 (NCHW x OIHW, no bias, no dilation)
+    s = _stride2(kw.get("strides", stride))
+    n, c, h, wd = x.shape
+    o, ci, kh, kw_ = w.shape
+    oh, ow = _conv_out_hw((h, wd), (kh, kw_), s, padding)
+    pt, pb, pl, pr = _conv_pads((h, wd), (kh, kw_), s, padding, (oh, ow))
+    xp = np.pad(x, ((0, 0), (0, 0), (pt, pb), (pl, pr))) if (pt or pb or pl or pr) else x
+    out = np.zeros((n, o, oh, ow), dtype=np.result_type(x, w))
+    for i in range(kh):
+        for j in range(kw_):
+            patch = xp[:, :, i : i + oh * s[0] : s[0], j : j + ow * s[1] : s[1]]
+            out += np.einsum("nihw,oi->nohw", patch, w[:, :, i, j])
+    return out
+
+
+def _op_conv2d_input_grad(d_out, w, stride=(1, 1), padding="SAME", target_shape=None, **kw):
+    # backends/numpy/eager/conv.py:634-697 (groups 1, dilation 1)
+    s = _stride2(kw.get("strides", stride))
+    n, c, h, wd = (int(v) for v in target_shape)
+    o, ci, kh, kw_ = w.shape
+    oh, ow = d_out.shape[2], d_out.shape[3]
+    pt, pb, pl, pr = _conv_pads((h, wd), (kh, kw_), s, padding, (oh, ow))
+    dx = np.zeros((n, c, h + pt + pb, wd + pl + pr), dtype=d_out.dtype)
+    for i in range(kh):
+        for j in range(kw_):
+            dx[:, :, i : i + oh * s[0] : s[0], j : j + ow * s[1] : s[1]] += np.einsum("nohw,oi->nihw", d_out, w[:, :, i, j])
+    return dx[:, :, pt : pt + h, pl : pl + wd]
+
+
+def _op_conv2d_weight_grad(x, d_out, stride=(1, 1), padding="SAME", target_shape=None, **kw):
+    # backends/numpy/eager/conv.py:699-764 (groups 1, dilation 1)
+    s = _stride2(kw.get("strides", stride))
+    o, ci, kh, kw_ = (int(v) for v in target_shape)
+    h, wd = x.shape[2], x.shape[3]
+    oh, ow = d_out.shape[2], d_out.shape[3]
+    pt, pb, pl, pr = _conv_pads((h, wd), (kh, kw_), s, padding, (oh, ow))
+    xp = np.pad(x, ((0, 0), (0, 0), (pt, pb), (pl, pr))) if (pt or pb or pl or pr) else x
+    dw = np.zeros((o, ci, kh, kw_), dtype=x.dtype)
+    for i in range(kh):
+        for j in range(kw_):
+            patch = xp[:, :, i : i + oh * s[0] : s[0], j : j + ow * s[1] : s[1]]
+            dw[:, :, i, j] = np.einsum("nohw,nihw->oi", d_out, patch)
+    return dw
+
+
+def _op_conv2d_bias_grad(d_out, **_):
+    # backends/numpy/eager/conv.py:766-779
+    return np.sum(d_out, axis=(0, 2, 3))
+
+
+OPS: dict[str, Any] = {
+    "Matmul": _op_matmul,
+    "BatchMatMul": _op_matmul,
+    "Add": lambda a, b, **_: np.add(a, b),  # backends/numpy/eager/math_binary.py:9-20
+    "Subtract": lambda a, b, **_: np.subtract(a, b),  # math_binary.py:23-36
+    "Multiply": lambda a, b, **_: np.multiply(a, b),  # math_binary.py:39-51
+    "TrueDivide": lambda a, b, **_: np.true_divide(a, b),  # math_binary.py:54-66
+    "Negative": lambda a, **_: np.negative(a),  # np fallback (numpy/eager/__init__.py:114-125)
+    "Exp": lambda a, **_: np.exp(a),  # numpy/eager/math_unary.py:11
+    "Log": lambda a, **_: np.log(a),  # np fallback
+    "Tanh": lambda a, **_: np.tanh(a),  # np fallback
+    "Sqrt": lambda a, **_: np.sqrt(a),  # np fallback
+    "Power": lambda a, b, **_: np.power(a, b),  # np fallback
+    "Greater": lambda a, b, **_: np.greater(a, b),  # numpy/eager/math_logical.py:26
+    "Where": lambda c, a, b, **_: np.where(c, a, b),  # math_logical.py:146
+    "Relu": _op_relu,
+    "Gelu": _op_gelu,
+    "Softmax": _op_softmax,
+    "LogSoftmax": _op_log_softmax,
+    "LayerNorm": _op_layer_norm,
+    "LayerNormInputGrad": _op_layer_norm_input_grad,
+    "LayerNormGammaGrad": _op_layer_norm_gamma_grad,
+    "LayerNormBetaGrad": _op_layer_norm_beta_grad,
+    "ReduceSum": _op_reduce_sum,
+    "ReduceMean": _op_reduce_mean,
+    "ReduceMax": _op_reduce_max,
+    "Numel": _op_numel,
+    "BroadcastLike": _op_broadcast_like,
+    "BroadcastReduce": _op_broadcast_reduce,
+    "Argmax": _op_argmax,
+    "Transpose": _op_transpose,
+    "Reshape": _op_reshape,
+    "TakeAlongAxis": _op_take_along_axis,
+    "ScatterAdd": _op_scatter_add,
+    "TensorScatterAdd": _op_tensor_scatter_add,
+    "Take": _op_take,
+    "ZerosLike": lambda a, **_: np.zeros_like(a),  # np fallback
+    "Conv2D": _op_conv2d,
+    "Conv2DInputGrad": _op_conv2d_input_grad,
+    "Conv2DWeightGrad": _op_conv2d_weight_grad,
+    "Conv2DBiasGrad": _op_conv2d_bias_grad,
+}
+
+
+class UnimplementedOp(KeyError):
+    """No restatement for this op (the reference raises UnimplementedMathError)."""
+
+
+def execute_op(op: str, *args, **kwargs):
+    target = _ALIASES.get(op, op)
+    fn = OPS.get(target)
+    if fn is None:
+        raise UnimplementedOp(target)
+    return fn(*args, **kwargs)
+
+
+def evaluate(graph: dict, inputs: dict[str, np.ndarray]) -> dict[str, Any]:
+    """``evaluate_graph`` (evaluator.py:272-305): every node, in dependency order."""
+    env: dict[str, Any] = dict(inputs)
+    for node in topo_order(graph):
+        op, nid = node["op_type"], node["id"]
+        if op == "Input":
+            if nid not in env:
+                raise ValueError(f"Missing input value for node '{nid}'")  # environment.py:33-48
+            continue
+        vals = [env[i] for i in node["inputs"] if i]
+        if op == "Output":
+            env[nid] = vals[0] if len(vals) == 1 else tuple(vals)
+        elif op == "Identity":
+            env[nid] = vals[0] if vals else None
+        elif op == "Constant":
+            env[nid] = np.array(node["attributes"]["value"], dtype=node.get("const_dtype"))
+        else:
+            target = _ALIASES.get(op, op)
+            env[nid] = execute_op(target, *vals, **_kwargs(node, target))
+    out = {}
+    for oid in graph["outputs"]:
+        if oid not in env:
+            raise RuntimeError(f"Output node '{oid}' was never evaluated.")
+        out[oid] = env[oid]
+    return out
+
+
+def evaluate_roles(graph: dict, role_inputs: dict[str, np.ndarray]) -> dict[str, Any]:
+    """Evaluate with inputs keyed by workload role; outputs keyed by output name."""
+    inputs = {nid: role_inputs[r] for r, nid in graph["roles"].items()}
+    res = evaluate(graph, inputs)
+    return {name: res[nid] for name, nid in graph["output_names"].items()}
