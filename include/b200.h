@@ -1,0 +1,214 @@
+/*
+ * b200.h - C ABI of libb200.so, the B200 (sm_100a) execution backend for
+ * ml-switcheroo-compiler fwd+bwd LogicalGraphs.
+ *
+ * Plain pointers, sizes and a CUDA stream (passed as void*, NULL = legacy default
+ * stream); no framework types. All tensors are device pointers into HBM, dense
+ * row-major unless a stride argument says otherwise. Every entry point returns an
+ * int status (B200_OK = 0); on failure b200_last_error() gives a message for the
+ * calling host thread. Kernels are launched asynchronously on `stream`; argument
+ * checks happen on the host before any launch.
+ *
+ * Each entry replaces one kernel of the reference numpy backend, cited as
+ * path:line inside src/ml_switcheroo_compiler/ of the reference.
+ */
+#ifndef B200_H_
+#define B200_H_
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* status codes (mapped to Python exceptions by the host shim) */
+#define B200_OK 0
+#define B200_ERR_ARG 1        /* bad pointer / size / stride / attribute   -> ValueError            */
+#define B200_ERR_DTYPE 2      /* dtype combination without a kernel        -> BackendNotSupportedError */
+#define B200_ERR_CUDA 3       /* CUDA launch or runtime error              -> RuntimeError          */
+#define B200_ERR_TIMEOUT 4    /* a bounded device-side wait gave up        -> TimeoutError          */
+#define B200_ERR_UNSUPPORTED 5 /* shape/layout this build has no kernel for -> UnimplementedMathError */
+
+/* element types */
+#define B200_F32 0
+#define B200_BF16 1
+#define B200_I64 2
+#define B200_BOOL 3 /* one byte, 0/1 */
+#define B200_I32 4
+
+int b200_abi_version(void);
+const char* b200_last_error(void);
+/* number of kernel launches issued by this process so far (all entry points) */
+uint64_t b200_launch_count(void);
+
+/* ------------------------------------------------------------------------------
+ * Fused elementwise program (subsystem 1).
+ *
+ * Replaces the numpy per-op elementwise kernels: Add/Subtract/Multiply/TrueDivide
+ * (backends/numpy/eager/math_binary.py:9-66), Exp (numpy/eager/math_unary.py:11),
+ * Greater/Where (numpy/eager/math_logical.py:26,146), Relu
+ * (numpy/eager/activation_ops.py:12), Gelu tanh (eager/core_math_ops/math_nn.py:184-199),
+ * Negative/Log/Tanh/Sqrt/Power (np.<name> fallback, numpy/eager/__init__.py:114-125),
+ * BroadcastLike/BroadcastTo (eager/core_math_ops/math_reduction.py:227,
+ * math_manipulation.py:423), ZerosLike, Transpose materialisation
+ * (numpy/eager/array_manipulation.py:121), and a chain of them fused into one pass
+ * (the FusedElementwise node of transforms/passes/operator_fusion.py:673-715).
+ *
+ * A program reads up to B200_EW_MAX_IN inputs, each with its own element strides over
+ * the output index space (stride 0 = broadcast), runs up to B200_EW_MAX_INS register
+ * instructions per element in fp32, and writes up to B200_EW_MAX_OUT outputs
+ * (dense, row-major over `shape`).
+ * ----------------------------------------------------------------------------*/
+#define B200_EW_MAX_IN 8
+#define B200_EW_MAX_OUT 4
+#define B200_EW_MAX_DIM 6
+#define B200_EW_MAX_INS 48
+#define B200_EW_MAX_REG 16
+
+enum b200_ew_op {
+  B200_EW_LOAD = 0,   /* r[dst] = in[a][idx]            */
+  B200_EW_STORE = 1,  /* out[dst][idx] = r[a]           */
+  B200_EW_IMM = 2,    /* r[dst] = imm                   */
+  B200_EW_ADD = 3,
+  B200_EW_SUB = 4,
+  B200_EW_MUL = 5,
+  B200_EW_DIV = 6,
+  B200_EW_NEG = 7,
+  B200_EW_EXP = 8,
+  B200_EW_LOG = 9,
+  B200_EW_TANH = 10,
+  B200_EW_SQRT = 11,
+  B200_EW_POW = 12,
+  B200_EW_MAX = 13,
+  B200_EW_MIN = 14,
+  B200_EW_GT = 15,    /* 1.0f / 0.0f                    */
+  B200_EW_GE = 16,
+  B200_EW_LT = 17,
+  B200_EW_EQ = 18,
+  B200_EW_WHERE = 19, /* r[dst] = r[a] != 0 ? r[b] : r[c] */
+  B200_EW_RELU = 20,  /* max(x, 0)                      */
+  B200_EW_GELU = 21,  /* tanh approximation             */
+  B200_EW_ABS = 22,
+  B200_EW_SIGMOID = 23,
+  B200_EW_ERF = 24,
+  B200_EW_MOV = 25,
+  B200_EW_RECIP = 26,
+  B200_EW_FMA = 27    /* r[dst] = r[a] * r[b] + r[c]     */
+};
+
+typedef struct b200_ew_ins {
+  uint8_t op, dst, a, b, c, pad0, pad1, pad2;
+  float imm;
+} b200_ew_ins;
+
+typedef struct b200_ew_program {
+  int32_t ndim;                                   /* 0..B200_EW_MAX_DIM (0 = scalar)  */
+  int32_t n_in, n_out, n_ins;
+  int64_t shape[B200_EW_MAX_DIM];                 /* output index space              */
+  int64_t in_strides[B200_EW_MAX_IN][B200_EW_MAX_DIM]; /* element strides, 0 = broadcast */
+  int32_t in_dtype[B200_EW_MAX_IN];
+  int32_t out_dtype[B200_EW_MAX_OUT];
+  b200_ew_ins ins[B200_EW_MAX_INS];
+} b200_ew_program;
+
+int b200_ew_run(const b200_ew_program* prog, const void* const* inputs, void* const* outputs, void* stream);
+
+/* ------------------------------------------------------------------------------
+ * Row reductions (subsystem 2). A tensor is viewed as [outer, red, inner] (dense);
+ * the reduced axis is the middle one.
+ * ----------------------------------------------------------------------------*/
+#define B200_RED_SUM 0
+#define B200_RED_MEAN 1
+#define B200_RED_MAX 2
+
+/* ReduceSum/ReduceMean/ReduceMax (eager/core_math_ops/math_reduction.py:37,57,97) and
+ * BroadcastReduce (math_reduction.py:192-224) as one or more middle-axis passes.
+ * x: [outer, red, inner] of in_dtype (F32/BF16), y: [outer, inner] F32. */
+int b200_reduce(int in_dtype, const void* x, float* y, int64_t outer, int64_t red, int64_t inner, int op, void* stream);
+
+/* Argmax (numpy/eager/math_reductions.py:129-140): first maximum wins, int64 out. */
+int b200_argmax(int in_dtype, const void* x, int64_t* idx, int64_t outer, int64_t red, int64_t inner, void* stream);
+
+/* Softmax / LogSoftmax over the last axis (numpy/eager/math_advanced/math_signal.py:450-467,
+ * math_advanced/math_log_exp.py:87-104). x, y: [rows, cols] F32. log != 0 -> LogSoftmax. */
+int b200_softmax(const float* x, float* y, int64_t rows, int64_t cols, int log, void* stream);
+
+/* LayerNorm forward over the last axis, biased variance (numpy/eager/nn_ops.py:219-241).
+ * gamma/beta may be NULL (ones / zeros). */
+int b200_layernorm(const float* x, const float* gamma, const float* beta, float* y, int64_t rows, int64_t cols,
+                   float eps, void* stream);
+
+/* LayerNormInputGrad (numpy/eager/nn_ops.py:244-273). gamma may be NULL. */
+int b200_layernorm_input_grad(const float* dy, const float* x, const float* gamma, float* dx, int64_t rows,
+                              int64_t cols, float eps, void* stream);
+
+/* LayerNormGammaGrad / LayerNormBetaGrad (numpy/eager/nn_ops.py:276-318): column sums of
+ * dy * x_hat and of dy over all rows. Either output may be NULL. */
+int b200_layernorm_param_grad(const float* dy, const float* x, float* dgamma, float* dbeta, int64_t rows,
+                              int64_t cols, float eps, void* stream);
+
+/* ------------------------------------------------------------------------------
+ * Indexing
+ * ----------------------------------------------------------------------------*/
+/* TakeAlongAxis on the last axis (numpy/eager/advanced_indexing.py:163-177):
+ * x [rows, cols] F32, idx [rows, k] I64 -> y [rows, k] F32. Out-of-range idx -> ERR_ARG
+ * is reported through the device error flag (see b200_check_device_error). */
+int b200_take_along_last(const float* x, const int64_t* idx, float* y, int64_t rows, int64_t cols, int64_t k,
+                         void* stream);
+/* ScatterAdd on the last axis (numpy/eager/advanced_indexing.py:309-326): y = copy(base);
+ * y[r, idx[r,j]] = y[r, idx[r,j]] + src[r,j] in order j = 0..k-1 within a row (a repeated
+ * index keeps the last write, as put_along_axis does). base may equal NULL (zeros). */
+int b200_scatter_add_last(const float* base, const int64_t* idx, const float* src, float* y, int64_t rows,
+                          int64_t cols, int64_t k, void* stream);
+/* Take along axis 0 (np.take fallback): rows of table [V, D] gathered by ids [n] -> [n, D]. */
+int b200_take_rows(int dtype, const void* table, const int64_t* ids, void* y, int64_t n, int64_t V, int64_t D,
+                   void* stream);
+/* TensorScatterAdd of rows (numpy/eager/math_scatter.py:39-60 with [n,1] indices):
+ * y [V, D] (+)= src[n, D] at rows ids[n]; accumulate != 0 keeps y, else y starts at 0. */
+int b200_scatter_add_rows(const float* src, const int64_t* ids, float* y, int64_t n, int64_t V, int64_t D,
+                          int accumulate, void* stream);
+
+/* device-side error flag (out-of-range index, timed-out wait): returns B200_OK or the
+ * recorded code after synchronising `stream`, and clears the flag. */
+int b200_check_device_error(void* stream);
+
+/* ------------------------------------------------------------------------------
+ * Contractions (subsystem 3)
+ * ----------------------------------------------------------------------------*/
+#define B200_EPI_NONE 0
+#define B200_EPI_RELU 1       /* C = relu(acc + bias)                                    */
+#define B200_EPI_GELU 2       /* C = gelu_tanh(acc + bias)                               */
+
+/* Matmul / BatchMatMul (eager/core_math_ops/math_matrix.py:21-64), strided batched:
+ *   C[z] = epi(alpha * op(A[z]) @ op(B[z]) + bias)      z = 0..batch-1
+ * op(A) is M x K: element (m,k) at A + z*sA + m*rsA + k*csA (element strides, so any
+ * transpose is a stride swap); op(B) K x N likewise with rsB/csB. C is row-major with
+ * leading dimension ldc (elements) and batch stride sC. bias (F32, length N) may be NULL.
+ * aux (optional, same layout as C, BOOL) receives (acc + bias > 0) for a later ReLU-grad.
+ * ab_dtype F32 -> exact fp32 CUDA-core path; BF16 -> tcgen05 tensor cores, fp32
+ * accumulation in TMEM (requires csA == 1 or rsA == 1, same for B, and 16-byte aligned
+ * rows). c_dtype F32 or BF16. */
+int b200_gemm(int ab_dtype, int c_dtype, const void* A, const void* B, void* C, int64_t batch, int64_t M,
+              int64_t N, int64_t K, int64_t sA, int64_t rsA, int64_t csA, int64_t sB, int64_t rsB, int64_t csB,
+              int64_t sC, int64_t ldc, float alpha, const float* bias, int epilogue, void* aux, void* stream);
+
+/* Conv2D (numpy/eager/conv.py:462-489) and its VJPs Conv2DInputGrad (conv.py:634-697),
+ * Conv2DWeightGrad (conv.py:699-764): NCHW activations (F32), OIHW weights (F32),
+ * explicit zero padding (pt, pl; bottom/right implied by the output size), stride
+ * (sh, sw), groups = dilation = 1. ab_dtype selects the math: F32 exact or BF16 tensor
+ * cores (operands rounded to bf16 while staging, fp32 accumulation). */
+int b200_conv2d_fwd(int ab_dtype, const float* x, const float* w, float* y, int64_t N, int64_t C, int64_t H,
+                    int64_t W, int64_t O, int64_t KH, int64_t KW, int64_t OH, int64_t OW, int64_t sh, int64_t sw,
+                    int64_t pt, int64_t pl, void* stream);
+int b200_conv2d_dgrad(int ab_dtype, const float* dy, const float* w, float* dx, int64_t N, int64_t C, int64_t H,
+                      int64_t W, int64_t O, int64_t KH, int64_t KW, int64_t OH, int64_t OW, int64_t sh, int64_t sw,
+                      int64_t pt, int64_t pl, void* stream);
+int b200_conv2d_wgrad(int ab_dtype, const float* x, const float* dy, float* dw, int64_t N, int64_t C, int64_t H,
+                      int64_t W, int64_t O, int64_t KH, int64_t KW, int64_t OH, int64_t OW, int64_t sh, int64_t sw,
+                      int64_t pt, int64_t pl, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* B200_H_ */

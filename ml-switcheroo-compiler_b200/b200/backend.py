@@ -1,0 +1,97 @@
+"""The ``b200`` backend class: the drop-in boundary of the reference's backend plugin API.
+
+Registered under the name ``"b200"`` with the reference's ``register_backend``
+(``backends/registry.py:426-448``). Members mirror what the interpreter and the grad
+API call on a backend:
+
+* ``execute_op(op_type, *args, **kwargs)`` - one op (``interpreter/evaluator.py:593``);
+* ``array`` / ``asarray`` / ``zeros`` / ``item`` / ``get_module``
+  (``backends/generator_mixins.py:107-188``);
+* ``execute_graph(graph, inputs)`` and ``compile_graph(graph)`` - the optional
+  whole-graph hooks (``grad/api.py:38-68``, used at ``grad/api.py:207-211`` and
+  ``grad/jvp_vjp.py:524-528``).
+
+Values are ``torch.Tensor`` on the current CUDA device (they provide ``.shape``,
+``__getitem__``, ``__setitem__`` and ``.item()``, which the interpreter uses directly).
+Unknown ops raise ``UnimplementedMathError``; there is no CPU fallback.
+"""
+
+from __future__ import annotations
+
+import weakref
+from typing import Any, Callable, Mapping
+
+import torch
+
+from . import ops
+from .executor import CompiledGraph, GraphRunner
+
+
+class B200Backend:
+    """Backend plugin for NVIDIA B200 (sm_100a)."""
+
+    name = "b200"
+    _runners: "weakref.WeakKeyDictionary[Any, GraphRunner]" = weakref.WeakKeyDictionary()
+    _runners_by_id: dict[int, GraphRunner] = {}
+
+    # ---- per-op path -------------------------------------------------------------
+    @classmethod
+    def execute_op(cls, op_type: str, *args: Any, **kwargs: Any) -> Any:
+        return ops.execute_op(op_type, *args, **kwargs)
+
+    @classmethod
+    def array(cls, data: Any, dtype: Any = None) -> Any:
+        if isinstance(data, (int, float, bool)) and dtype is None:
+            return ops.to_device(torch.tensor(float(data), dtype=torch.float32))
+        return ops.to_device(data)
+
+    @classmethod
+    def asarray(cls, data: Any) -> Any:
+        return data if isinstance(data, torch.Tensor) and data.is_cuda else ops.to_device(data)
+
+    @classmethod
+    def zeros(cls, shape: tuple[int, ...]) -> Any:
+        return ops.full(tuple(shape), 0.0)
+
+    @classmethod
+    def item(cls, data: Any) -> float:
+        return float(data.item()) if isinstance(data, torch.Tensor) else float(data)
+
+    @classmethod
+    def get_module(cls) -> Any:
+        return ops
+
+    # ---- whole-graph hooks -----------------------------------------------------------
+    @classmethod
+    def _runner(cls, graph: Any) -> GraphRunner:
+        try:
+            r = cls._runners.get(graph)
+        except TypeError:
+            r = cls._runners_by_id.get(id(graph))
+        if r is None:
+            r = GraphRunner(graph)
+            try:
+                cls._runners[graph] = r
+            except TypeError:
+                cls._runners_by_id[id(graph)] = r
+        return r
+
+    @classmethod
+    def execute_graph(cls, graph: Any, inputs: Mapping[str, Any]) -> dict[str, Any]:
+        """Run a whole fwd+bwd graph: fused kernels, dead nodes pruned."""
+        return cls._runner(graph)(dict(inputs))
+
+    @classmethod
+    def compile_graph(cls, graph: Any) -> Callable[[Mapping[str, Any]], Mapping[str, Any]]:
+        """A replayable executable (static buffers + one CUDA graph per input signature)."""
+        cg = CompiledGraph(graph)
+        return lambda inputs: cg(dict(inputs))
+
+
+def register() -> type[B200Backend]:
+    """Register ``B200Backend`` as backend ``"b200"`` with the reference registry
+    (call once, before ``config.backend = "b200"``)."""
+    from ml_switcheroo_compiler.backends.registry import register_backend
+
+    register_backend("b200")(B200Backend)
+    return B200Backend

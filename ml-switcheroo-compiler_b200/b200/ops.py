@@ -1,0 +1,912 @@
+"""Per-op kernels of the b200 backend (the ``execute_op`` path).
+
+Every op takes and returns ``torch.Tensor`` values on the current CUDA device (torch
+allocates; all arithmetic runs in libb200.so) with the argument meaning of the
+reference numpy-backend op of the same name (cited per op). Views (Transpose, Reshape
+of contiguous data, BroadcastLike) stay views; consumers that need dense data
+materialise it with the elementwise copy kernel.
+
+Numeric policy: fp32 values are computed in fp32. numpy's float64 promotion from
+Python-float constants is not reproduced: those constants are applied as fp32.
+Contractions use ``matmul_dtype`` (``"f32"`` exact CUDA-core path, ``"bf16"`` tcgen05
+tensor cores with fp32 accumulation).
+"""
+
+from __future__ import annotations
+
+import ctypes as C
+import math
+from typing import Any, Sequence
+
+import torch
+
+from . import _lib as L
+from .errors import BackendNotSupportedError, UnimplementedMathError
+
+_TORCH2CODE = {torch.float32: L.F32, torch.bfloat16: L.BF16, torch.int64: L.I64, torch.bool: L.BOOL, torch.int32: L.I32}
+_FLOATS = (torch.float32, torch.bfloat16)
+
+
+class Config:
+    """Backend-wide numeric policy (per process)."""
+
+    matmul_dtype: str = "f32"  # "f32" | "bf16"
+    conv_dtype: str = "f32"
+    device: torch.device | None = None
+
+
+def device() -> torch.device:
+    if Config.device is None:
+        if not torch.cuda.is_available():
+            raise RuntimeError("b200 backend: no CUDA device (there is no CPU fallback)")
+        Config.device = torch.device("cuda", torch.cuda.current_device())
+    return Config.device
+
+
+def stream_ptr() -> int:
+    return torch.cuda.current_stream().cuda_stream
+
+
+def code(t: torch.Tensor) -> int:
+    c = _TORCH2CODE.get(t.dtype)
+    if c is None:
+        raise BackendNotSupportedError(f"dtype {t.dtype} has no b200 kernel")
+    return c
+
+
+def _ptr(t: torch.Tensor | None) -> int | None:
+    return None if t is None else t.data_ptr()
+
+
+def to_device(x: Any, dtype: torch.dtype | None = None) -> torch.Tensor:
+    """Host value (numpy array, scalar, tensor) -> CUDA tensor (a copy, no compute)."""
+    if isinstance(x, torch.Tensor):
+        t = x
+    else:
+        import numpy as np
+
+        a = np.asarray(x)
+        if a.dtype == np.float64:
+            a = a.astype(np.float32)
+        t = torch.from_numpy(np.ascontiguousarray(a))
+    if dtype is not None and t.dtype != dtype and not t.is_cuda:
+        t = t.to(dtype)
+    if not t.is_cuda:
+        t = t.to(device(), non_blocking=False)
+    elif dtype is not None and t.dtype != dtype:
+        t = cast(t, dtype)
+    return t
+
+
+# ----------------------------------------------------------------------------------
+# elementwise programs
+# ----------------------------------------------------------------------------------
+
+
+def _bshape(shapes: Sequence[Sequence[int]]) -> tuple[int, ...]:
+    return tuple(torch.broadcast_shapes(*[tuple(s) for s in shapes]))
+
+
+def _coalesce(shape: list[int], strides: list[list[int]]) -> tuple[list[int], list[list[int]]]:
+    """Drop size-1 dims and merge adjacent dims that are jointly contiguous for every operand."""
+    keep = [i for i, s in enumerate(shape) if s != 1]
+    shape = [shape[i] for i in keep]
+    strides = [[st[i] for i in keep] for st in strides]
+    if not shape:
+        return [], [[] for _ in strides]
+    out_shape, out_strides = [shape[0]], [[st[0]] for st in strides]
+    for d in range(1, len(shape)):
+        if all(st[-1] == sd[d] * shape[d] for st, sd in zip(out_strides, strides)):
+            out_shape[-1] *= shape[d]
+            for st, sd in zip(out_strides, strides):
+                st[-1] = sd[d]
+        else:
+            out_shape.append(shape[d])
+            for st, sd in zip(out_strides, strides):
+                st.append(sd[d])
+    return out_shape, out_strides
+
+
+class Prog:
+    """Builder for one fused elementwise program (registers are SSA-allocated)."""
+
+    def __init__(self) -> None:
+        self.ins: list[tuple[int, int, int, int, int, float]] = []
+        self.inputs: list[Any] = []  # torch tensors
+        self.nreg = 0
+
+    def reg(self) -> int:
+        r = self.nreg
+        self.nreg += 1
+        if self.nreg > L.EW_MAX_REG:
+            raise UnimplementedMathError("elementwise program needs more than 16 registers")
+        return r
+
+    def load(self, t: torch.Tensor) -> int:
+        for i, u in enumerate(self.inputs):
+            if u is t:
+                idx = i
+                break
+        else:
+            self.inputs.append(t)
+            idx = len(self.inputs) - 1
+        r = self.reg()
+        self.ins.append((L.EW["LOAD"], r, idx, 0, 0, 0.0))
+        return r
+
+    def imm(self, v: float) -> int:
+        r = self.reg()
+        self.ins.append((L.EW["IMM"], r, 0, 0, 0, float(v)))
+        return r
+
+    def op(self, name: str, a: int, b: int = 0, c: int = 0) -> int:
+        r = self.reg()
+        self.ins.append((L.EW[name], r, a, b, c, 0.0))
+        return r
+
+    def value(self, x: Any) -> int:
+        if isinstance(x, torch.Tensor):
+            if x.dim() == 0 and not x.is_cuda:
+                return self.imm(float(x))
+            return self.load(x)
+        return self.imm(float(x))
+
+    def run(self, outs: list[tuple[int, torch.dtype]], shape: Sequence[int] | None = None) -> list[torch.Tensor]:
+        tens = [t for t in self.inputs]
+        if shape is None:
+            shape = _bshape([t.shape for t in tens]) if tens else ()
+        shape = list(shape)
+        results = [torch.empty(shape, dtype=dt, device=device()) for _, dt in outs]
+        n = 1
+        for s in shape:
+            n *= s
+        if n == 0:
+            return results
+        strides = []
+        for t in tens:
+            e = t.expand(shape) if list(t.shape) != shape else t
+            strides.append(list(e.stride()) if shape else [])
+        cshape, cstrides = _coalesce(shape, strides + [list(results[0].stride()) if shape else []])
+        cstrides = cstrides[:-1]
+        if len(cshape) > L.EW_MAX_DIM:
+            raise UnimplementedMathError(f"elementwise over {len(cshape)} non-mergeable dims")
+        if len(tens) > L.EW_MAX_IN or len(outs) > L.EW_MAX_OUT:
+            raise UnimplementedMathError("elementwise program with too many operands")
+        ins = list(self.ins) + [(L.EW["STORE"], o, r, 0, 0, 0.0) for o, (r, _) in enumerate(outs)]
+        if len(ins) > L.EW_MAX_INS:
+            raise UnimplementedMathError("elementwise program longer than 48 instructions")
+        p = L.EwProgram()
+        p.ndim = len(cshape)
+        p.n_in, p.n_out, p.n_ins = len(tens), len(outs), len(ins)
+        for d, s in enumerate(cshape):
+            p.shape[d] = s
+        for j, st in enumerate(cstrides):
+            for d, s in enumerate(st):
+                p.in_strides[j][d] = s
+            p.in_dtype[j] = code(tens[j])
+        for o, r in enumerate(results):
+            p.out_dtype[o] = code(r)
+        for i, (op, dst, a, b, c, imm) in enumerate(ins):
+            p.ins[i].op, p.ins[i].dst, p.ins[i].a, p.ins[i].b, p.ins[i].c, p.ins[i].imm = op, dst, a, b, c, imm
+        inp = (C.c_void_p * max(1, len(tens)))(*[t.data_ptr() for t in tens])
+        outp = (C.c_void_p * len(results))(*[r.data_ptr() for r in results])
+        L.call("b200_ew_run", C.byref(p), inp, outp, stream_ptr())
+        return results
+
+
+def _result_float(*xs: Any) -> torch.dtype:
+    for x in xs:
+        if isinstance(x, torch.Tensor) and x.dtype == torch.float32:
+            return torch.float32
+    for x in xs:
+        if isinstance(x, torch.Tensor) and x.dtype == torch.bfloat16:
+            return torch.bfloat16
+    return torch.float32
+
+
+def _check_float_args(name: str, *xs: Any) -> None:
+    for x in xs:
+        if isinstance(x, torch.Tensor) and x.dtype in (torch.int64, torch.int32):
+            raise UnimplementedMathError(f"{name} on integer tensors has no b200 kernel")
+
+
+def _shape_of(x: Any) -> tuple[int, ...]:
+    return tuple(x.shape) if isinstance(x, torch.Tensor) else ()
+
+
+def ew_binary(name: str, a: Any, b: Any, out_dtype: torch.dtype | None = None) -> torch.Tensor:
+    _check_float_args(name, a, b)
+    p = Prog()
+    ra, rb = p.value(a), p.value(b)
+    r = p.op(name, ra, rb)
+    shape = _bshape([_shape_of(a), _shape_of(b)])
+    return p.run([(r, out_dtype or _result_float(a, b))], shape)[0]
+
+
+def ew_unary(name: str, a: Any, out_dtype: torch.dtype | None = None) -> torch.Tensor:
+    _check_float_args(name, a)
+    p = Prog()
+    r = p.op(name, p.value(a))
+    return p.run([(r, out_dtype or _result_float(a))], _shape_of(a))[0]
+
+
+def cast(x: torch.Tensor, dtype: torch.dtype) -> torch.Tensor:
+    if x.dtype == dtype:
+        return x
+    p = Prog()
+    r = p.load(x)
+    return p.run([(r, dtype)], tuple(x.shape))[0]
+
+
+def contiguous(x: torch.Tensor) -> torch.Tensor:
+    """Dense row-major copy through the elementwise kernel (no torch compute)."""
+    if x.is_contiguous():
+        return x
+    p = Prog()
+    r = p.load(x)
+    return p.run([(r, x.dtype)], tuple(x.shape))[0]
+
+
+def copy(x: torch.Tensor) -> torch.Tensor:
+    """Fresh dense copy through the elementwise kernel."""
+    p = Prog()
+    r = p.load(x)
+    return p.run([(r, x.dtype)], tuple(x.shape))[0]
+
+
+def full(shape: Sequence[int], value: float, dtype: torch.dtype = torch.float32) -> torch.Tensor:
+    p = Prog()
+    r = p.imm(value)
+    return p.run([(r, dtype)], tuple(shape))[0]
+
+
+def op_add(a, b, **_):  # numpy/eager/math_binary.py:9-20
+    return ew_binary("ADD", a, b)
+
+
+def op_subtract(a, b, **_):  # math_binary.py:23-36
+    return ew_binary("SUB", a, b)
+
+
+def op_multiply(a, b, **_):  # math_binary.py:39-51
+    return ew_binary("MUL", a, b)
+
+
+def op_true_divide(a, b, **_):  # math_binary.py:54-66
+    return ew_binary("DIV", a, b)
+
+
+def op_power(a, b, **_):  # np.power fallback
+    return ew_binary("POW", a, b)
+
+
+def op_maximum(a, b, **_):
+    return ew_binary("MAX", a, b)
+
+
+def op_minimum(a, b, **_):
+    return ew_binary("MIN", a, b)
+
+
+def op_greater(a, b, **_):  # numpy/eager/math_logical.py:26
+    return ew_binary("GT", a, b, out_dtype=torch.bool)
+
+
+def op_greater_equal(a, b, **_):
+    return ew_binary("GE", a, b, out_dtype=torch.bool)
+
+
+def op_less(a, b, **_):
+    return ew_binary("LT", a, b, out_dtype=torch.bool)
+
+
+def op_equal(a, b, **_):
+    return ew_binary("EQ", a, b, out_dtype=torch.bool)
+
+
+def op_where(c, a, b, **_):  # numpy/eager/math_logical.py:146
+    p = Prog()
+    rc, ra, rb = p.value(c), p.value(a), p.value(b)
+    r = p.op("WHERE", rc, ra, rb)
+    shape = _bshape([_shape_of(c), _shape_of(a), _shape_of(b)])
+    return p.run([(r, _result_float(a, b))], shape)[0]
+
+
+def op_negative(a, **_):
+    return ew_unary("NEG", a)
+
+
+def op_exp(a, **_):  # numpy/eager/math_unary.py:11
+    return ew_unary("EXP", a)
+
+
+def op_log(a, **_):
+    return ew_unary("LOG", a)
+
+
+def op_tanh(a, **_):
+    return ew_unary("TANH", a)
+
+
+def op_sqrt(a, **_):
+    return ew_unary("SQRT", a)
+
+
+def op_abs(a, **_):
+    return ew_unary("ABS", a)
+
+
+def op_sigmoid(a, **_):
+    return ew_unary("SIGMOID", a)
+
+
+def op_erf(a, **_):
+    return ew_unary("ERF", a)
+
+
+def op_relu(a, **_):  # numpy/eager/activation_ops.py:12
+    return ew_unary("RELU", a)
+
+
+def op_gelu(a, **_):  # eager/core_math_ops/math_nn.py:184-199 (tanh approximation)
+    return ew_unary("GELU", a)
+
+
+def op_zeros_like(a, **_):
+    return full(tuple(a.shape), 0.0, a.dtype if a.dtype in _FLOATS or a.dtype == torch.bool else a.dtype)
+
+
+def op_ones_like(a, **_):
+    return full(tuple(a.shape), 1.0, a.dtype)
+
+
+def op_cast(x, dtype=None, **_):  # numpy/eager/variable_ops.py:26-43 (bfloat16 is computed as float32 there)
+    name = str(dtype).replace("DType.", "").lower() if dtype is not None else "float32"
+    table = {"float32": torch.float32, "bfloat16": torch.bfloat16, "int64": torch.int64, "bool": torch.bool,
+             "int32": torch.int32, "float64": torch.float32}
+    if name not in table:
+        raise BackendNotSupportedError(f"Cast to {dtype}")
+    return cast(x, table[name])
+
+
+# ----------------------------------------------------------------------------------
+# views
+# ----------------------------------------------------------------------------------
+
+
+def op_transpose(x, axes=None, **_):  # numpy/eager/array_manipulation.py:121
+    if axes is None:
+        axes = list(reversed(range(x.dim())))
+    return x.permute(*[int(a) for a in axes])
+
+
+def op_reshape(x, shape=None, newshape=None, **_):  # numpy/eager/array_manipulation.py:87
+    tgt = tuple(int(d) for d in (shape if shape is not None else newshape))
+    try:
+        return x.view(tgt)
+    except RuntimeError:
+        return contiguous(x).view(tgt)
+
+
+def op_broadcast_like(src, tgt, **_):  # eager/core_math_ops/math_reduction.py:227-249
+    if not isinstance(src, torch.Tensor):
+        return full(tuple(tgt.shape), float(src))
+    if tuple(src.shape) == tuple(tgt.shape):
+        return src
+    return src.expand(tuple(tgt.shape))
+
+
+def op_broadcast_to(x, shape=None, **_):  # eager/core_math_ops/math_manipulation.py:423
+    return x.expand(tuple(int(d) for d in shape))
+
+
+def op_identity(x, *_, **__):
+    return x
+
+
+# ----------------------------------------------------------------------------------
+# reductions
+# ----------------------------------------------------------------------------------
+
+
+def _norm_axes(axis, ndim: int) -> list[int]:
+    if axis is None:
+        return list(range(ndim))
+    axes = axis if isinstance(axis, (list, tuple)) else [axis]
+    return sorted({int(a) % ndim for a in axes}) if ndim else []
+
+
+def reduce(x: torch.Tensor, axis, keepdims: bool, op: int) -> torch.Tensor:
+    """ReduceSum/Mean/Max over ``axis`` (eager/core_math_ops/math_reduction.py:37-114)."""
+    if x.dtype not in _FLOATS:
+        if x.dtype == torch.bool:
+            x = cast(x, torch.float32)
+        else:
+            raise UnimplementedMathError(f"reduction over {x.dtype}")
+    axes = _norm_axes(axis, x.dim())
+    if not axes:
+        return x if x.dtype == torch.float32 else cast(x, torch.float32)
+    xc = contiguous(x)
+    shape = list(xc.shape)
+    # contiguous run of axes -> a single [outer, red, inner] pass
+    if axes == list(range(axes[0], axes[-1] + 1)):
+        outer = math.prod(shape[: axes[0]])
+        red = math.prod(shape[axes[0] : axes[-1] + 1])
+        inner = math.prod(shape[axes[-1] + 1 :])
+        y = torch.empty(outer * inner, dtype=torch.float32, device=device())
+        L.call("b200_reduce", code(xc), xc.data_ptr(), y.data_ptr(), outer, red, inner, op, stream_ptr())
+        out_shape = [1 if i in axes else s for i, s in enumerate(shape)] if keepdims else [s for i, s in enumerate(shape) if i not in axes]
+        return y.view(out_shape)
+    # otherwise one axis at a time, last first (mean = sum / count at the end)
+    sub_op = L.RED_MAX if op == L.RED_MAX else L.RED_SUM
+    y = xc
+    for a in reversed(axes):
+        y = reduce(y, a, True, sub_op)
+    if op == L.RED_MEAN:
+        y = ew_binary("MUL", y, 1.0 / math.prod(shape[a] for a in axes))
+    if not keepdims:
+        y = y.view([s for i, s in enumerate(y.shape) if i not in axes])
+    return y
+
+
+def op_reduce_sum(x, axis=None, keepdims=False, **_):
+    return reduce(x, axis, bool(keepdims), L.RED_SUM)
+
+
+def op_reduce_mean(x, axis=None, keepdims=False, **_):
+    return reduce(x, axis, bool(keepdims), L.RED_MEAN)
+
+
+def op_reduce_max(x, axis=None, keepdims=False, **_):
+    return reduce(x, axis, bool(keepdims), L.RED_MAX)
+
+
+def op_broadcast_reduce(cot, tgt, **_):  # eager/core_math_ops/math_reduction.py:192-224
+    cs, ts = tuple(cot.shape), tuple(tgt.shape)
+    if cs == ts:
+        return cot
+    res = cot
+    if len(cs) > len(ts):
+        res = reduce(res, list(range(len(cs) - len(ts))), False, L.RED_SUM)
+    axes = [i for i, (cd, td) in enumerate(zip(res.shape, ts)) if td == 1 and cd > 1]
+    if axes:
+        res = reduce(res, axes, True, L.RED_SUM)
+    return res
+
+
+def op_numel(x, **_):  # eager/core_math_ops/math_reduction.py:156-173 (Python float)
+    return float(x.numel()) if isinstance(x, torch.Tensor) else 1.0
+
+
+def op_argmax(x, axis=None, **_):  # numpy/eager/math_reductions.py:129-140
+    xc = contiguous(x)
+    if x.dtype not in _FLOATS:
+        xc = cast(xc, torch.float32)
+    if axis is None:
+        outer, red, inner, out_shape = 1, xc.numel(), 1, ()
+    else:
+        a = int(axis) % xc.dim()
+        shape = list(xc.shape)
+        outer, red, inner = math.prod(shape[:a]), shape[a], math.prod(shape[a + 1 :])
+        out_shape = tuple(shape[:a] + shape[a + 1 :])
+    if red == 0:
+        raise ValueError("attempt to get argmax of an empty sequence")
+    y = torch.empty(out_shape, dtype=torch.int64, device=device())
+    L.call("b200_argmax", code(xc), xc.data_ptr(), y.data_ptr(), outer, red, inner, stream_ptr())
+    return y
+
+
+def _last_axis(x: torch.Tensor, axis) -> bool:
+    return axis is None or int(axis) % max(1, x.dim()) == x.dim() - 1
+
+
+def _softmax(x, axis, log):
+    if not _last_axis(x, axis):
+        a = int(axis) % x.dim()
+        perm = [i for i in range(x.dim()) if i != a] + [a]
+        inv = [perm.index(i) for i in range(x.dim())]
+        return _softmax(contiguous(x.permute(*perm)), -1, log).permute(*inv)
+    xc = contiguous(cast(x, torch.float32))
+    cols = xc.shape[-1] if xc.dim() else 1
+    rows = xc.numel() // max(1, cols)
+    y = torch.empty_like(xc)
+    L.call("b200_softmax", xc.data_ptr(), y.data_ptr(), rows, cols, 1 if log else 0, stream_ptr())
+    return y
+
+
+def op_softmax(x, axis=-1, **_):  # numpy/eager/math_advanced/math_signal.py:450-467
+    return _softmax(x, axis, False)
+
+
+def op_log_softmax(x, axis=-1, **_):  # numpy/eager/math_advanced/math_log_exp.py:87-104
+    return _softmax(x, axis, True)
+
+
+def _ln_args(x, axis):
+    if not _last_axis(x, axis):
+        raise UnimplementedMathError("LayerNorm over a non-last axis")
+    xc = contiguous(cast(x, torch.float32))
+    cols = xc.shape[-1]
+    return xc, xc.numel() // cols, cols
+
+
+def _opt(t):
+    return None if t is None else contiguous(cast(t, torch.float32))
+
+
+def op_layer_norm(x, gamma=None, beta=None, eps=1e-5, axis=-1, **kw):  # numpy/eager/nn_ops.py:219-241
+    eps = float(kw.get("epsilon", eps))
+    xc, rows, cols = _ln_args(x, axis)
+    g, b = _opt(gamma), _opt(beta)
+    y = torch.empty_like(xc)
+    L.call("b200_layernorm", xc.data_ptr(), _ptr(g), _ptr(b), y.data_ptr(), rows, cols, eps, stream_ptr())
+    return y
+
+
+def op_layer_norm_input_grad(dy, x, gamma=None, eps=1e-5, axis=-1, **kw):  # numpy/eager/nn_ops.py:244-273
+    eps = float(kw.get("epsilon", eps))
+    xc, rows, cols = _ln_args(x, axis)
+    dyc = contiguous(cast(dy.expand(xc.shape), torch.float32))
+    g = _opt(gamma)
+    dx = torch.empty_like(xc)
+    L.call("b200_layernorm_input_grad", dyc.data_ptr(), xc.data_ptr(), _ptr(g), dx.data_ptr(), rows, cols, eps, stream_ptr())
+    return dx
+
+
+def _ln_param(dy, x, eps, axis, which):
+    xc, rows, cols = _ln_args(x, axis)
+    dyc = contiguous(cast(dy.expand(xc.shape), torch.float32))
+    out = torch.empty(cols, dtype=torch.float32, device=device())
+    dg = out if which == "gamma" else None
+    db = out if which == "beta" else None
+    L.call("b200_layernorm_param_grad", dyc.data_ptr(), xc.data_ptr(), _ptr(dg), _ptr(db), rows, cols, float(eps), stream_ptr())
+    return out
+
+
+def op_layer_norm_gamma_grad(dy, x, eps=1e-5, axis=-1, **kw):  # numpy/eager/nn_ops.py:276-297
+    return _ln_param(dy, x, float(kw.get("epsilon", eps)), axis, "gamma")
+
+
+def op_layer_norm_beta_grad(dy, axis=-1, **_):  # numpy/eager/nn_ops.py:300-318
+    return reduce(dy, list(range(dy.dim() - 1)), False, L.RED_SUM) if dy.dim() > 1 else cast(dy, torch.float32)
+
+
+# ----------------------------------------------------------------------------------
+# indexing
+# ----------------------------------------------------------------------------------
+
+
+def op_take_along_axis(x, indices, axis=-1, **_):  # numpy/eager/advanced_indexing.py:163-177
+    if not _last_axis(x, axis) or x.dim() != indices.dim():
+        raise UnimplementedMathError("TakeAlongAxis on a non-last axis")
+    xc = contiguous(cast(x, torch.float32))
+    cols = xc.shape[-1]
+    rows = xc.numel() // cols
+    k = indices.shape[-1]
+    if tuple(indices.shape[:-1]) != tuple(xc.shape[:-1]):
+        raise UnimplementedMathError("TakeAlongAxis with broadcast leading dims")
+    ic = contiguous(indices.to(torch.int64) if indices.dtype != torch.int64 else indices)
+    y = torch.empty(tuple(xc.shape[:-1]) + (k,), dtype=torch.float32, device=device())
+    L.call("b200_take_along_last", xc.data_ptr(), ic.data_ptr(), y.data_ptr(), rows, cols, k, stream_ptr())
+    return y
+
+
+def op_scatter_add(inp, index, src, dim=0, **_):  # numpy/eager/advanced_indexing.py:309-326
+    if int(dim) % inp.dim() != inp.dim() - 1:
+        raise UnimplementedMathError("ScatterAdd on a non-last axis")
+    base = contiguous(cast(inp, torch.float32))
+    cols = base.shape[-1]
+    rows = base.numel() // cols
+    k = index.shape[-1]
+    ic = contiguous(index)
+    sc = contiguous(cast(src.expand(index.shape), torch.float32))
+    y = torch.empty_like(base)
+    L.call("b200_scatter_add_last", base.data_ptr(), ic.data_ptr(), sc.data_ptr(), y.data_ptr(), rows, cols, k, stream_ptr())
+    return y
+
+
+def op_take(a, indices, axis=None, **_):  # np.take fallback (numpy/eager/__init__.py:114-125)
+    if axis is None or int(axis) != 0:
+        raise UnimplementedMathError("Take supports axis=0 (row gather)")
+    tc = contiguous(a)
+    V = tc.shape[0]
+    D = tc.numel() // max(1, V)
+    ic = contiguous(indices)
+    y = torch.empty(tuple(ic.shape) + tuple(tc.shape[1:]), dtype=tc.dtype, device=device())
+    L.call("b200_take_rows", code(tc), tc.data_ptr(), ic.data_ptr(), y.data_ptr(), ic.numel(), V, D, stream_ptr())
+    return y
+
+
+def op_tensor_scatter_add(tensor, indices, updates, **_):  # numpy/eager/math_scatter.py:39-60
+    if indices.dim() != 2 or indices.shape[-1] != 1:
+        raise UnimplementedMathError("TensorScatterAdd supports [n, 1] row indices")
+    y = copy(cast(tensor, torch.float32))
+    V = y.shape[0]
+    D = y.numel() // max(1, V)
+    uc = contiguous(cast(updates, torch.float32))
+    ic = contiguous(indices)
+    L.call("b200_scatter_add_rows", uc.data_ptr(), ic.data_ptr(), y.data_ptr(), ic.shape[0], V, D, 1, stream_ptr())
+    return y
+
+
+# ----------------------------------------------------------------------------------
+# contractions
+# ----------------------------------------------------------------------------------
+
+
+def _tc_ok(t: torch.Tensor) -> bool:
+    st = t.stride()
+    return t.data_ptr() % 16 == 0 and (
+        (st[-1] == 1 and (st[-2] * 2) % 16 == 0) or (st[-2] == 1 and (st[-1] * 2) % 16 == 0)
+    )
+
+
+def _gemm_operand(t: torch.Tensor, ab: torch.dtype) -> torch.Tensor:
+    t = cast(t, ab)
+    if ab != torch.bfloat16 or _tc_ok(t):
+        return t
+    # tcgen05 path needs one unit stride and 16-byte aligned rows: try both dense layouts
+    rm = contiguous(t)
+    if _tc_ok(rm):
+        return rm
+    cm = contiguous(t.transpose(-1, -2)).transpose(-1, -2)
+    if _tc_ok(cm):
+        return cm
+    raise UnimplementedMathError(f"bf16 GEMM operand {tuple(t.shape)}: neither layout has 16-byte aligned rows")
+
+
+def gemm(a: torch.Tensor, b: torch.Tensor, *, bias: torch.Tensor | None = None, epilogue: int = L.EPI_NONE,
+         alpha: float = 1.0, out_dtype: torch.dtype = torch.float32, want_mask: bool = False,
+         ab_dtype: torch.dtype | None = None):
+    """numpy-style matmul of a [..., M, K] and b [..., K, N] with broadcast batch dims."""
+    if ab_dtype is None:
+        ab_dtype = torch.bfloat16 if Config.matmul_dtype == "bf16" else torch.float32
+    squeeze_m = squeeze_n = False
+    if a.dim() == 1:
+        a, squeeze_m = a.unsqueeze(0), True
+    if b.dim() == 1:
+        b, squeeze_n = b.unsqueeze(-1), True
+    M, K = a.shape[-2], a.shape[-1]
+    K2, N = b.shape[-2], b.shape[-1]
+    if K != K2:
+        raise ValueError(f"matmul: shapes {tuple(a.shape)} and {tuple(b.shape)} not aligned")
+    batch_shape = _bshape([a.shape[:-2], b.shape[:-2]])
+    Z = math.prod(batch_shape)
+    # fold a batched A with a shared 2-D B into one tall GEMM
+    if b.dim() == 2 and a.dim() > 2 and a.is_contiguous():
+        y = gemm(a.reshape(-1, K), b, bias=bias, epilogue=epilogue, alpha=alpha, out_dtype=out_dtype,
+                 want_mask=want_mask, ab_dtype=ab_dtype)
+        ys = (y[0] if want_mask else y).view(*a.shape[:-1], N)
+        res = (ys, y[1].view(*a.shape[:-1], N)) if want_mask else ys
+        return res
+    A = _gemm_operand(a, ab_dtype)
+    B = _gemm_operand(b, ab_dtype)
+
+    def batch_stride(t: torch.Tensor) -> int:
+        if t.dim() == 2:
+            return 0
+        e = t.expand(*batch_shape, t.shape[-2], t.shape[-1])
+        bs = list(e.stride()[:-2])
+        bsh = list(batch_shape)
+        # the flattened batch must be a single arithmetic progression
+        nz = [(s, st) for s, st in zip(bsh, bs) if s != 1]
+        if not nz:
+            return 0
+        for (s0, st0), (s1, st1) in zip(nz, nz[1:]):
+            if st0 != st1 * s1:
+                return -1
+        return nz[-1][1]
+
+    sA, sB = batch_stride(A), batch_stride(B)
+    if sA < 0:
+        A = contiguous(A.expand(*batch_shape, M, K))
+        sA = M * K
+    if sB < 0:
+        B = contiguous(B.expand(*batch_shape, K, N))
+        sB = K * N
+    C_ = torch.empty(*batch_shape, M, N, dtype=out_dtype, device=device())
+    mask = torch.empty(*batch_shape, M, N, dtype=torch.bool, device=device()) if want_mask else None
+    bc = None if bias is None else contiguous(cast(bias, torch.float32))
+    if bc is not None and bc.numel() != N:
+        raise UnimplementedMathError("gemm bias must be a length-N vector")
+    if Z and M and N:
+        L.call("b200_gemm", code(A), code(C_), A.data_ptr(), B.data_ptr(), C_.data_ptr(), Z, M, N, K, sA, A.stride(-2),
+               A.stride(-1), sB, B.stride(-2), B.stride(-1), M * N, N, float(alpha), _ptr(bc), int(epilogue), _ptr(mask),
+               stream_ptr())
+    if squeeze_m:
+        C_ = C_.squeeze(-2)
+    if squeeze_n:
+        C_ = C_.squeeze(-1)
+    return (C_, mask) if want_mask else C_
+
+
+def op_matmul(a, b, transpose_a=False, transpose_b=False, **_):  # eager/core_math_ops/math_matrix.py:21-44
+    if transpose_a:
+        a = a.transpose(-1, -2)
+    if transpose_b:
+        b = b.transpose(-1, -2)
+    return gemm(a, b)
+
+
+def _conv_pads(in_hw, k_hw, s_hw, padding, out_hw):
+    # numpy/eager/conv.py:590-633 (_compute_conv2d_padding_values, dilation 1)
+    if isinstance(padding, str) and padding.upper() == "SAME":
+        ph = max(0, (out_hw[0] - 1) * s_hw[0] + k_hw[0] - in_hw[0])
+        pw = max(0, (out_hw[1] - 1) * s_hw[1] + k_hw[1] - in_hw[1])
+        return ph // 2, pw // 2
+    if isinstance(padding, str) and padding.upper() == "VALID":
+        return 0, 0
+    raise UnimplementedMathError(f"Conv2D padding {padding!r}")
+
+
+def _stride2(stride):
+    if isinstance(stride, int):
+        return stride, stride
+    return int(stride[0]), int(stride[1])
+
+
+def _conv_out_hw(in_hw, k_hw, s_hw, padding):
+    if isinstance(padding, str) and padding.upper() == "SAME":
+        return -(-in_hw[0] // s_hw[0]), -(-in_hw[1] // s_hw[1])
+    return (in_hw[0] - k_hw[0]) // s_hw[0] + 1, (in_hw[1] - k_hw[1]) // s_hw[1] + 1
+
+
+def _conv_dt() -> int:
+    return L.BF16 if Config.conv_dtype == "bf16" else L.F32
+
+
+def _check_conv_attrs(groups, dilation):
+    if int(groups or 1) != 1:
+        raise UnimplementedMathError("grouped Conv2D")
+    d = _stride2(dilation or 1)
+    if d != (1, 1):
+        raise UnimplementedMathError("dilated Conv2D")
+
+
+def op_conv2d(x, w, stride=(1, 1), padding="SAME", groups=1, dilation=1, **kw):  # numpy/eager/conv.py:462-489
+    _check_conv_attrs(groups, kw.get("dilations", dilation))
+    s = _stride2(kw.get("strides", stride))
+    xc, wc = contiguous(cast(x, torch.float32)), contiguous(cast(w, torch.float32))
+    N, Cc, H, W = xc.shape
+    O, _, KH, KW = wc.shape
+    OH, OW = _conv_out_hw((H, W), (KH, KW), s, padding)
+    pt, pl = _conv_pads((H, W), (KH, KW), s, padding, (OH, OW))
+    y = torch.empty(N, O, OH, OW, dtype=torch.float32, device=device())
+    L.call("b200_conv2d_fwd", _conv_dt(), xc.data_ptr(), wc.data_ptr(), y.data_ptr(), N, Cc, H, W, O, KH, KW, OH, OW, s[0],
+           s[1], pt, pl, stream_ptr())
+    return y
+
+
+def op_conv2d_input_grad(dy, w, stride=(1, 1), padding="SAME", target_shape=None, groups=1, dilation=1, **kw):
+    # numpy/eager/conv.py:634-697
+    _check_conv_attrs(groups, kw.get("dilations", dilation))
+    s = _stride2(kw.get("strides", stride))
+    dyc, wc = contiguous(cast(dy, torch.float32)), contiguous(cast(w, torch.float32))
+    N, Cc, H, W = (int(v) for v in target_shape)
+    O, _, KH, KW = wc.shape
+    OH, OW = dyc.shape[2], dyc.shape[3]
+    pt, pl = _conv_pads((H, W), (KH, KW), s, padding, (OH, OW))
+    dx = torch.empty(N, Cc, H, W, dtype=torch.float32, device=device())
+    L.call("b200_conv2d_dgrad", _conv_dt(), dyc.data_ptr(), wc.data_ptr(), dx.data_ptr(), N, Cc, H, W, O, KH, KW, OH, OW,
+           s[0], s[1], pt, pl, stream_ptr())
+    return dx
+
+
+def op_conv2d_weight_grad(x, dy, stride=(1, 1), padding="SAME", target_shape=None, groups=1, dilation=1, **kw):
+    # numpy/eager/conv.py:699-764
+    _check_conv_attrs(groups, kw.get("dilations", dilation))
+    s = _stride2(kw.get("strides", stride))
+    xc, dyc = contiguous(cast(x, torch.float32)), contiguous(cast(dy, torch.float32))
+    O, Cc, KH, KW = (int(v) for v in target_shape)
+    N, _, H, W = xc.shape
+    OH, OW = dyc.shape[2], dyc.shape[3]
+    pt, pl = _conv_pads((H, W), (KH, KW), s, padding, (OH, OW))
+    dw = torch.empty(O, Cc, KH, KW, dtype=torch.float32, device=device())
+    L.call("b200_conv2d_wgrad", _conv_dt(), xc.data_ptr(), dyc.data_ptr(), dw.data_ptr(), N, Cc, H, W, O, KH, KW, OH, OW,
+           s[0], s[1], pt, pl, stream_ptr())
+    return dw
+
+
+def op_conv2d_bias_grad(dy, **_):  # numpy/eager/conv.py:766-779
+    return reduce(dy, [0, 2, 3], False, L.RED_SUM)
+
+
+# ----------------------------------------------------------------------------------
+# collectives
+# ----------------------------------------------------------------------------------
+
+
+def op_all_reduce(x, op_type="sum", **_):  # numpy/eager/distributed.py:205-225
+    import torch.distributed as dist
+
+    if str(op_type).lower() not in ("sum", "add"):
+        raise UnimplementedMathError(f"AllReduce op {op_type}")
+    if dist.is_available() and dist.is_initialized() and dist.get_world_size() > 1:
+        y = copy(x)
+        dist.all_reduce(y)
+        return y
+    return x
+
+
+OPS: dict[str, Any] = {
+    "Add": op_add,
+    "Subtract": op_subtract,
+    "Multiply": op_multiply,
+    "TrueDivide": op_true_divide,
+    "Power": op_power,
+    "Maximum": op_maximum,
+    "Minimum": op_minimum,
+    "Greater": op_greater,
+    "GreaterEqual": op_greater_equal,
+    "Less": op_less,
+    "Equal": op_equal,
+    "Where": op_where,
+    "Negative": op_negative,
+    "Exp": op_exp,
+    "Log": op_log,
+    "Tanh": op_tanh,
+    "Sqrt": op_sqrt,
+    "Abs": op_abs,
+    "Sigmoid": op_sigmoid,
+    "Erf": op_erf,
+    "Relu": op_relu,
+    "Gelu": op_gelu,
+    "GELU": op_gelu,
+    "ZerosLike": op_zeros_like,
+    "OnesLike": op_ones_like,
+    "Cast": op_cast,
+    "Transpose": op_transpose,
+    "Reshape": op_reshape,
+    "BroadcastLike": op_broadcast_like,
+    "BroadcastTo": op_broadcast_to,
+    "Identity": op_identity,
+    "ReduceSum": op_reduce_sum,
+    "ReduceMean": op_reduce_mean,
+    "ReduceMax": op_reduce_max,
+    "BroadcastReduce": op_broadcast_reduce,
+    "Numel": op_numel,
+    "Argmax": op_argmax,
+    "Softmax": op_softmax,
+    "LogSoftmax": op_log_softmax,
+    "LayerNorm": op_layer_norm,
+    "LayerNormInputGrad": op_layer_norm_input_grad,
+    "LayerNormGammaGrad": op_layer_norm_gamma_grad,
+    "LayerNormBetaGrad": op_layer_norm_beta_grad,
+    "TakeAlongAxis": op_take_along_axis,
+    "ScatterAdd": op_scatter_add,
+    "Take": op_take,
+    "TensorScatterAdd": op_tensor_scatter_add,
+    "Matmul": op_matmul,
+    "BatchMatMul": op_matmul,
+    "Conv2D": op_conv2d,
+    "Conv2DInputGrad": op_conv2d_input_grad,
+    "Conv2DWeightGrad": op_conv2d_weight_grad,
+    "Conv2DBiasGrad": op_conv2d_bias_grad,
+    "AllReduce": op_all_reduce,
+    "NcclAllReduce": op_all_reduce,
+}
+
+# reference aliases (interpreter/evaluator.py:771-791)
+ALIASES = {"Sub": "Subtract", "Mul": "Multiply", "Div": "TrueDivide", "Neg": "Negative", "Pow": "Power", "MatMul": "Matmul",
+           "Expand": "BroadcastTo", "Permute": "Transpose"}
+
+
+def execute_op(op_type: str, *args, **kwargs):
+    """Run one op on the GPU; unknown ops raise UnimplementedMathError (no fallback)."""
+    name = ALIASES.get(op_type, op_type)
+    fn = OPS.get(name)
+    if fn is None:
+        raise UnimplementedMathError(f"Operation {op_type} is not implemented in the b200 backend.")
+    args = [to_device(a) if _is_array_like(a) else a for a in args]
+    return fn(*args, **kwargs)
+
+
+def _is_array_like(a: Any) -> bool:
+    if isinstance(a, torch.Tensor):
+        return not a.is_cuda
+    try:
+        import numpy as np
+
+        return isinstance(a, np.ndarray)
+    except Exception:  # noqa: BLE001
+        return False

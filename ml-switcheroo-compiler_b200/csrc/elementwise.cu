@@ -1,0 +1,228 @@
+// Fused elementwise programs (subsystem 1).
+//
+// One launch evaluates a whole chain of elementwise graph nodes: every element of the
+// output index space loads its inputs once (broadcast by zero strides), runs the
+// register program in fp32 and stores the chain's live outputs once. HBM traffic is
+// one read per distinct input and one write per output, however long the chain.
+//
+// Two paths:
+//  * flat: every input is either dense over the output (strides == row-major strides)
+//    or a scalar (all strides 0). Each thread handles 4 consecutive elements with
+//    128-bit loads/stores for fp32 operands (16-byte aligned bases).
+//  * strided: arbitrary per-input strides over up to 6 dims (broadcast, transposed
+//    views); offsets come from one index decomposition per element.
+#include "common.cuh"
+
+namespace b200 {
+
+struct EwParams {
+  b200_ew_program p;
+  const void* in[B200_EW_MAX_IN];
+  void* out[B200_EW_MAX_OUT];
+  int64_t n;
+};
+
+template <int V>
+__device__ __forceinline__ void ew_exec(const b200_ew_program& p, float (&r)[B200_EW_MAX_REG][V],
+                                        const float (&ld)[B200_EW_MAX_IN][V], float (&st)[B200_EW_MAX_OUT][V]) {
+  for (int i = 0; i < p.n_ins; ++i) {
+    const b200_ew_ins I = p.ins[i];
+    const int d = I.dst, a = I.a, b = I.b, c = I.c;
+#pragma unroll
+    for (int v = 0; v < V; ++v) {
+      float x = r[a][v], y = r[b][v], res;
+      switch (I.op) {
+        case B200_EW_LOAD: res = ld[a][v]; break;
+        case B200_EW_STORE: st[d][v] = x; continue;
+        case B200_EW_IMM: res = I.imm; break;
+        case B200_EW_ADD: res = x + y; break;
+        case B200_EW_SUB: res = x - y; break;
+        case B200_EW_MUL: res = x * y; break;
+        case B200_EW_DIV: res = x / y; break;
+        case B200_EW_NEG: res = -x; break;
+        case B200_EW_EXP: res = expf(x); break;
+        case B200_EW_LOG: res = logf(x); break;
+        case B200_EW_TANH: res = tanhf(x); break;
+        case B200_EW_SQRT: res = sqrtf(x); break;
+        case B200_EW_POW: res = powf(x, y); break;
+        case B200_EW_MAX: res = fmaxf(x, y); break;
+        case B200_EW_MIN: res = fminf(x, y); break;
+        case B200_EW_GT: res = (x > y) ? 1.f : 0.f; break;
+        case B200_EW_GE: res = (x >= y) ? 1.f : 0.f; break;
+        case B200_EW_LT: res = (x < y) ? 1.f : 0.f; break;
+        case B200_EW_EQ: res = (x == y) ? 1.f : 0.f; break;
+        case B200_EW_WHERE: res = (x != 0.f) ? y : r[c][v]; break;
+        case B200_EW_RELU: res = x > 0.f ? x : 0.f; break;
+        case B200_EW_GELU: res = gelu_tanh(x); break;
+        case B200_EW_ABS: res = fabsf(x); break;
+        case B200_EW_SIGMOID: res = 1.f / (1.f + expf(-x)); break;
+        case B200_EW_ERF: res = erff(x); break;
+        case B200_EW_MOV: res = x; break;
+        case B200_EW_RECIP: res = 1.f / x; break;
+        case B200_EW_FMA: res = fmaf(x, y, r[c][v]); break;
+        default: res = 0.f; break;
+      }
+      r[d][v] = res;
+    }
+  }
+}
+
+// flat path: 4 elements per thread-iteration
+__global__ void __launch_bounds__(256) ew_flat_kernel(const __grid_constant__ EwParams P) {
+  const b200_ew_program& p = P.p;
+  float r[B200_EW_MAX_REG][4];
+  float ld[B200_EW_MAX_IN][4];
+  float st[B200_EW_MAX_OUT][4];
+#pragma unroll
+  for (int i = 0; i < B200_EW_MAX_REG; ++i)
+#pragma unroll
+    for (int v = 0; v < 4; ++v) r[i][v] = 0.f;
+  const int64_t n = P.n;
+  const int64_t nvec = (n + 3) / 4;
+  for (int64_t q = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; q < nvec; q += (int64_t)gridDim.x * blockDim.x) {
+    const int64_t base = q * 4;
+    const bool full = base + 4 <= n;
+    for (int j = 0; j < p.n_in; ++j) {
+      const bool scalar = p.ndim == 0 || p.in_strides[j][p.ndim - 1] == 0;
+      if (scalar) {
+        float s = load_as_f32(P.in[j], 0, p.in_dtype[j]);
+#pragma unroll
+        for (int v = 0; v < 4; ++v) ld[j][v] = s;
+      } else if (full && p.in_dtype[j] == B200_F32) {
+        float4 t = reinterpret_cast<const float4*>(P.in[j])[q];
+        ld[j][0] = t.x; ld[j][1] = t.y; ld[j][2] = t.z; ld[j][3] = t.w;
+      } else {
+#pragma unroll
+        for (int v = 0; v < 4; ++v) ld[j][v] = (base + v < n) ? load_as_f32(P.in[j], base + v, p.in_dtype[j]) : 0.f;
+      }
+    }
+    ew_exec<4>(p, r, ld, st);
+    for (int o = 0; o < p.n_out; ++o) {
+      if (full && p.out_dtype[o] == B200_F32) {
+        reinterpret_cast<float4*>(P.out[o])[q] = make_float4(st[o][0], st[o][1], st[o][2], st[o][3]);
+      } else {
+#pragma unroll
+        for (int v = 0; v < 4; ++v)
+          if (base + v < n) store_from_f32(P.out[o], base + v, p.out_dtype[o], st[o][v]);
+      }
+    }
+  }
+}
+
+// strided path: 1 element per thread-iteration
+__global__ void __launch_bounds__(256) ew_strided_kernel(const __grid_constant__ EwParams P) {
+  const b200_ew_program& p = P.p;
+  float r[B200_EW_MAX_REG][1];
+  float ld[B200_EW_MAX_IN][1];
+  float st[B200_EW_MAX_OUT][1];
+#pragma unroll
+  for (int i = 0; i < B200_EW_MAX_REG; ++i) r[i][0] = 0.f;
+  for (int64_t e = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; e < P.n; e += (int64_t)gridDim.x * blockDim.x) {
+    int64_t off[B200_EW_MAX_IN];
+#pragma unroll
+    for (int j = 0; j < B200_EW_MAX_IN; ++j) off[j] = 0;
+    int64_t rem = e;
+    for (int d = p.ndim - 1; d >= 0; --d) {
+      const int64_t sz = p.shape[d];
+      const int64_t id = rem % sz;
+      rem /= sz;
+#pragma unroll
+      for (int j = 0; j < B200_EW_MAX_IN; ++j)
+        if (j < p.n_in) off[j] += id * p.in_strides[j][d];
+    }
+    for (int j = 0; j < p.n_in; ++j) ld[j][0] = load_as_f32(P.in[j], off[j], p.in_dtype[j]);
+    ew_exec<1>(p, r, ld, st);
+    for (int o = 0; o < p.n_out; ++o) store_from_f32(P.out[o], e, p.out_dtype[o], st[o][0]);
+  }
+}
+
+static bool dtype_ok(int dt) { return dt == B200_F32 || dt == B200_BF16 || dt == B200_I64 || dt == B200_BOOL || dt == B200_I32; }
+
+}  // namespace b200
+
+extern "C" int b200_ew_run(const b200_ew_program* prog, const void* const* inputs, void* const* outputs, void* stream) {
+  using namespace b200;
+  B200_REQUIRE(prog != nullptr, "ew_run: null program");
+  const b200_ew_program& p = *prog;
+  B200_REQUIRE(p.ndim >= 0 && p.ndim <= B200_EW_MAX_DIM, "ew_run: ndim %d out of range", p.ndim);
+  B200_REQUIRE(p.n_in >= 0 && p.n_in <= B200_EW_MAX_IN, "ew_run: n_in %d out of range", p.n_in);
+  B200_REQUIRE(p.n_out >= 1 && p.n_out <= B200_EW_MAX_OUT, "ew_run: n_out %d out of range", p.n_out);
+  B200_REQUIRE(p.n_ins >= 1 && p.n_ins <= B200_EW_MAX_INS, "ew_run: n_ins %d out of range", p.n_ins);
+  int64_t n = 1;
+  for (int d = 0; d < p.ndim; ++d) {
+    B200_REQUIRE(p.shape[d] >= 0, "ew_run: negative dim");
+    n *= p.shape[d];
+  }
+  EwParams P;
+  P.p = p;
+  P.n = n;
+  for (int j = 0; j < p.n_in; ++j) {
+    B200_REQUIRE(inputs && inputs[j], "ew_run: null input %d", j);
+    if (!dtype_ok(p.in_dtype[j])) {
+      set_error("ew_run: input %d dtype %d", j, p.in_dtype[j]);
+      return B200_ERR_DTYPE;
+    }
+    P.in[j] = inputs[j];
+  }
+  for (int j = p.n_in; j < B200_EW_MAX_IN; ++j) P.in[j] = nullptr;
+  for (int o = 0; o < p.n_out; ++o) {
+    B200_REQUIRE(outputs && outputs[o], "ew_run: null output %d", o);
+    if (!dtype_ok(p.out_dtype[o])) {
+      set_error("ew_run: output %d dtype %d", o, p.out_dtype[o]);
+      return B200_ERR_DTYPE;
+    }
+    P.out[o] = outputs[o];
+  }
+  for (int o = p.n_out; o < B200_EW_MAX_OUT; ++o) P.out[o] = nullptr;
+  for (int i = 0; i < p.n_ins; ++i) {
+    const b200_ew_ins& I = p.ins[i];
+    B200_REQUIRE(I.op <= B200_EW_FMA, "ew_run: bad opcode %d at %d", I.op, i);
+    B200_REQUIRE(I.a < B200_EW_MAX_REG && I.b < B200_EW_MAX_REG && I.c < B200_EW_MAX_REG, "ew_run: bad register at %d", i);
+    if (I.op == B200_EW_LOAD) B200_REQUIRE(I.a < p.n_in && I.dst < B200_EW_MAX_REG, "ew_run: bad load at %d", i);
+    else if (I.op == B200_EW_STORE) B200_REQUIRE(I.dst < p.n_out, "ew_run: bad store at %d", i);
+    else B200_REQUIRE(I.dst < B200_EW_MAX_REG, "ew_run: bad dst at %d", i);
+  }
+  if (n == 0) return B200_OK;
+
+  // flat path when every input is dense-over-output or scalar and vector stores are aligned
+  bool flat = true;
+  int64_t dense[B200_EW_MAX_DIM];
+  {
+    int64_t s = 1;
+    for (int d = p.ndim - 1; d >= 0; --d) {
+      dense[d] = s;
+      s *= p.shape[d];
+    }
+  }
+  for (int j = 0; j < p.n_in && flat; ++j) {
+    bool all0 = true, isdense = true;
+    for (int d = 0; d < p.ndim; ++d) {
+      if (p.shape[d] == 1) continue;
+      if (p.in_strides[j][d] != 0) all0 = false;
+      if (p.in_strides[j][d] != dense[d]) isdense = false;
+    }
+    if (all0) {
+      // treat as scalar: the kernel tests the last-dim stride, so require it to be 0
+      if (p.ndim > 0 && p.in_strides[j][p.ndim - 1] != 0 && p.shape[p.ndim - 1] != 1) flat = false;
+      if (p.ndim > 0 && p.shape[p.ndim - 1] == 1 && p.in_strides[j][p.ndim - 1] != 0) flat = false;
+    } else if (isdense) {
+      if (p.ndim > 0 && p.in_strides[j][p.ndim - 1] == 0) flat = false;  // degenerate last dim
+      if (p.in_dtype[j] == B200_F32 && (reinterpret_cast<uintptr_t>(inputs[j]) & 15)) flat = false;
+    } else {
+      flat = false;
+    }
+  }
+  for (int o = 0; o < p.n_out && flat; ++o)
+    if (p.out_dtype[o] == B200_F32 && (reinterpret_cast<uintptr_t>(outputs[o]) & 15)) flat = false;
+
+  const int threads = 256;
+  const int64_t sms = num_sms();
+  if (flat) {
+    int64_t blocks = std::min<int64_t>(ceil_div(ceil_div(n, 4), threads), sms * 8);
+    ew_flat_kernel<<<(unsigned)blocks, threads, 0, as_stream(stream)>>>(P);
+  } else {
+    int64_t blocks = std::min<int64_t>(ceil_div(n, threads), sms * 8);
+    ew_strided_kernel<<<(unsigned)blocks, threads, 0, as_stream(stream)>>>(P);
+  }
+  return check_launch("ew_run");
+}

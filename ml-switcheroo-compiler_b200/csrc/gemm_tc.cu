@@ -1,0 +1,390 @@
+// bf16 tensor-core GEMM for sm_100a: TMA -> shared memory (128B swizzle) ->
+// tcgen05.mma (one elected thread) -> fp32 accumulator in TMEM -> tcgen05.ld ->
+// fused epilogue (alpha, bias, ReLU/GELU, ReLU mask) -> global.
+//
+// CTA = 6 warps: warp 0 issues TMA loads, warp 1 owns TMEM and issues the MMAs,
+// warps 2..5 run the epilogue (each reads the 32 TMEM lanes its warp may access).
+// Tile 128 x BN x 64, STAGES-deep mbarrier ring. Operands may be K-major or MN-major
+// (a transposed graph operand is only a different tensor map + descriptor bit, it is
+// never materialised). Batched through the third tensor-map dimension.
+//
+// Every mbarrier wait is bounded by a wall-clock limit: on expiry the thread records
+// B200_ERR_TIMEOUT in the device error flag and the CTA winds down (TMEM is freed).
+#include <cuda.h>
+#include <cudaTypedefs.h>
+
+#include "common.cuh"
+
+namespace b200 {
+namespace tc {
+
+constexpr int BM = 128, BK = 64, STAGES = 4, THREADS = 192;
+constexpr unsigned long long WAIT_LIMIT_NS = 2000000000ull;  // 2 s per wait
+
+__device__ __forceinline__ uint32_t smem_u32(const void* p) { return (uint32_t)__cvta_generic_to_shared(p); }
+
+__device__ __forceinline__ unsigned long long globaltimer() {
+  unsigned long long t;
+  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+  return t;
+}
+
+__device__ __forceinline__ void mbar_init(uint64_t* bar, uint32_t count) {
+  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(count));
+}
+__device__ __forceinline__ void mbar_expect_tx(uint64_t* bar, uint32_t bytes) {
+  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(bar)), "r"(bytes) : "memory");
+}
+__device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n selp.u32 %0, 1, 0, p;\n}\n"
+      : "=r"(ok)
+      : "r"(smem_u32(bar)), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+// bounded wait; false (and device error flag set) on timeout
+__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity) {
+  if (mbar_try_wait(bar, parity)) return true;
+  const unsigned long long t0 = globaltimer();
+  while (true) {
+    if (mbar_try_wait(bar, parity)) return true;
+    if (globaltimer() - t0 > WAIT_LIMIT_NS) {
+      raise_device_error(B200_ERR_TIMEOUT);
+      return false;
+    }
+  }
+}
+
+__device__ __forceinline__ void tma_load_3d(void* dst, const CUtensorMap* map, uint64_t* bar, int c0, int c1, int c2) {
+  asm volatile(
+      "cp.async.bulk.tensor.3d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3, %4}], [%5];" ::"r"(
+          smem_u32(dst)),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(c0), "r"(c1), "r"(c2), "r"(smem_u32(bar))
+      : "memory");
+}
+
+// UMMA shared-memory descriptor, SWIZZLE_128B, version 1 (sm_100).
+__device__ __forceinline__ uint64_t smem_desc(uint32_t saddr, uint32_t lbo_bytes, uint32_t sbo_bytes) {
+  uint64_t d = 0;
+  d |= (uint64_t)((saddr >> 4) & 0x3FFF);
+  d |= (uint64_t)((lbo_bytes >> 4) & 0x3FFF) << 16;
+  d |= (uint64_t)((sbo_bytes >> 4) & 0x3FFF) << 32;
+  d |= (uint64_t)1 << 46;  // version
+  d |= (uint64_t)2 << 61;  // SWIZZLE_128B
+  return d;
+}
+
+__device__ __forceinline__ void mma_bf16(uint32_t tmem_d, uint64_t adesc, uint64_t bdesc, uint32_t idesc, uint32_t acc) {
+  asm volatile(
+      "{\n .reg .pred p;\n setp.ne.b32 p, %4, 0;\n tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n}\n" ::"r"(tmem_d),
+      "l"(adesc), "l"(bdesc), "r"(idesc), "r"(acc));
+}
+__device__ __forceinline__ void mma_commit(uint64_t* bar) {
+  asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(smem_u32(bar)) : "memory");
+}
+__device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
+__device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
+
+__device__ __forceinline__ void tmem_ld32(uint32_t taddr, float (&v)[32]) {
+  uint32_t r[32];
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16,%17,%18,%19,%20,%21,%"
+      "22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]), "=r"(r[8]), "=r"(r[9]),
+        "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15]), "=r"(r[16]), "=r"(r[17]), "=r"(r[18]),
+        "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]), "=r"(r[24]), "=r"(r[25]), "=r"(r[26]), "=r"(r[27]),
+        "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
+      : "r"(taddr));
+  asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+#pragma unroll
+  for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(r[i]);
+}
+
+struct Args {
+  void* C;
+  const float* bias;
+  uint8_t* aux;
+  int64_t M, N, K, sC, ldc;
+  float alpha;
+  int c_dt, epi, a_mn, b_mn;
+};
+
+template <int BN>
+__global__ void __launch_bounds__(THREADS, 1) gemm_tc_kernel(const __grid_constant__ CUtensorMap mapA,
+                                                             const __grid_constant__ CUtensorMap mapB,
+                                                             const __grid_constant__ Args args) {
+  constexpr uint32_t A_BYTES = BM * BK * 2;  // 16 KB
+  constexpr uint32_t B_BYTES = BN * BK * 2;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t* sA = smem;
+  uint8_t* sB = smem + STAGES * A_BYTES;
+  uint64_t* full_bar = reinterpret_cast<uint64_t*>(sB + STAGES * B_BYTES);
+  uint64_t* empty_bar = full_bar + STAGES;
+  uint64_t* accum_bar = empty_bar + STAGES;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(accum_bar + 1);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int n_tile = blockIdx.x, m_tile = blockIdx.y, z = blockIdx.z;
+  const int num_kb = (int)((args.K + BK - 1) / BK);
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < STAGES; ++s) {
+      mbar_init(&full_bar[s], 1);
+      mbar_init(&empty_bar[s], 1);
+    }
+    mbar_init(accum_bar, 1);
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+  }
+  if (warp == 1) {
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tmem_slot)), "r"(BN));
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+
+  if (warp == 0) {
+    if (lane == 0) {
+      // ---------------- TMA producer ----------------
+      for (int kb = 0; kb < num_kb; ++kb) {
+        const int s = kb % STAGES;
+        const uint32_t round = kb / STAGES;
+        if (!mbar_wait(&empty_bar[s], (round & 1) ^ 1)) break;
+        mbar_expect_tx(&full_bar[s], A_BYTES + B_BYTES);
+        const int k0 = kb * BK;
+        uint8_t* a_dst = sA + s * A_BYTES;
+        uint8_t* b_dst = sB + s * B_BYTES;
+        if (!args.a_mn) {
+          tma_load_3d(a_dst, &mapA, &full_bar[s], k0, m_tile * BM, z);
+        } else {
+          tma_load_3d(a_dst, &mapA, &full_bar[s], m_tile * BM, k0, z);
+          tma_load_3d(a_dst + 8192, &mapA, &full_bar[s], m_tile * BM + 64, k0, z);
+        }
+        if (!args.b_mn) {
+          tma_load_3d(b_dst, &mapB, &full_bar[s], k0, n_tile * BN, z);
+        } else {
+#pragma unroll
+          for (int j = 0; j < BN / 64; ++j) tma_load_3d(b_dst + j * 8192, &mapB, &full_bar[s], n_tile * BN + 64 * j, k0, z);
+        }
+      }
+    }
+  } else if (warp == 1) {
+    if (lane == 0) {
+      // ---------------- MMA issuer ----------------
+      // instruction descriptor: D f32, A/B bf16, majors, N>>3, M>>4
+      const uint32_t idesc = (1u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)args.a_mn << 15) | ((uint32_t)args.b_mn << 16) |
+                             ((uint32_t)(BN >> 3) << 17) | ((uint32_t)(BM >> 4) << 24);
+      bool ok = true;
+      for (int kb = 0; kb < num_kb; ++kb) {
+        const int s = kb % STAGES;
+        const uint32_t round = kb / STAGES;
+        if (!mbar_wait(&full_bar[s], round & 1)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        const uint32_t a_base = smem_u32(sA + s * A_BYTES);
+        const uint32_t b_base = smem_u32(sB + s * B_BYTES);
+#pragma unroll
+        for (int k = 0; k < BK / 16; ++k) {
+          // K-major: +32 B per 16-element K step inside the 128 B swizzle row.
+          // MN-major: +2048 B per K step (two 8-row groups of 1024 B).
+          const uint64_t ad = args.a_mn ? smem_desc(a_base + k * 2048, 8192, 1024) : smem_desc(a_base + k * 32, 16, 1024);
+          const uint64_t bd = args.b_mn ? smem_desc(b_base + k * 2048, 8192, 1024) : smem_desc(b_base + k * 32, 16, 1024);
+          mma_bf16(tmem_base, ad, bd, idesc, (kb > 0 || k > 0) ? 1u : 0u);
+        }
+        mma_commit(&empty_bar[s]);  // stage s free once these MMAs have read it
+      }
+      if (ok) mma_commit(accum_bar);
+      else raise_device_error(B200_ERR_TIMEOUT);
+    }
+  } else {
+    // ---------------- epilogue (warps 2..5) ----------------
+    const int q = warp & 3;  // TMEM lane quarter this warp may access
+    const bool ready = (num_kb > 0) ? mbar_wait(accum_bar, 0) : true;
+    tc_fence_after();
+    const int64_t row = (int64_t)m_tile * BM + q * 32 + lane;
+    const int64_t col0 = (int64_t)n_tile * BN;
+    if (ready) {
+#pragma unroll 1
+      for (int c = 0; c < BN / 32; ++c) {
+        float v[32];
+        if (num_kb > 0) {
+          tmem_ld32(tmem_base + ((uint32_t)(q * 32) << 16) + (uint32_t)(c * 32), v);
+        } else {
+#pragma unroll
+          for (int i = 0; i < 32; ++i) v[i] = 0.f;
+        }
+        if (row >= args.M) continue;
+        const int64_t cbase = col0 + c * 32;
+        if (cbase >= args.N) continue;
+        const int64_t off = (int64_t)z * args.sC + row * args.ldc + cbase;
+        uint8_t mask[32];
+#pragma unroll
+        for (int i = 0; i < 32; ++i) {
+          const int64_t n = cbase + i;
+          float pre = args.alpha * v[i] + ((args.bias && n < args.N) ? args.bias[n] : 0.f);
+          mask[i] = pre > 0.f;
+          float r = pre;
+          if (args.epi == B200_EPI_RELU) r = pre > 0.f ? pre : 0.f;
+          else if (args.epi == B200_EPI_GELU) r = gelu_tanh(pre);
+          v[i] = r;
+        }
+        const bool full = cbase + 32 <= args.N;
+        if (args.c_dt == B200_F32) {
+          float* dst = reinterpret_cast<float*>(args.C) + off;
+          if (full && ((reinterpret_cast<uintptr_t>(dst) & 15) == 0)) {
+#pragma unroll
+            for (int i = 0; i < 32; i += 4) *reinterpret_cast<float4*>(dst + i) = make_float4(v[i], v[i + 1], v[i + 2], v[i + 3]);
+          } else {
+            for (int i = 0; i < 32; ++i)
+              if (cbase + i < args.N) dst[i] = v[i];
+          }
+        } else {
+          __nv_bfloat16* dst = reinterpret_cast<__nv_bfloat16*>(args.C) + off;
+          if (full && ((reinterpret_cast<uintptr_t>(dst) & 15) == 0)) {
+#pragma unroll
+            for (int i = 0; i < 32; i += 8) {
+              __align__(16) __nv_bfloat162 t[4];
+#pragma unroll
+              for (int j = 0; j < 4; ++j) t[j] = __floats2bfloat162_rn(v[i + 2 * j], v[i + 2 * j + 1]);
+              *reinterpret_cast<uint4*>(dst + i) = *reinterpret_cast<uint4*>(t);
+            }
+          } else {
+            for (int i = 0; i < 32; ++i)
+              if (cbase + i < args.N) dst[i] = __float2bfloat16_rn(v[i]);
+          }
+        }
+        if (args.aux) {
+          uint8_t* mdst = args.aux + off;
+          for (int i = 0; i < 32; ++i)
+            if (cbase + i < args.N) mdst[i] = mask[i];
+        }
+      }
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem_base), "r"(BN));
+  }
+}
+
+// ---------------------------------------------------------------------------------
+// host side
+// ---------------------------------------------------------------------------------
+static PFN_cuTensorMapEncodeTiled_v12000 get_encode() {
+  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+  if (!fn) {
+    cudaDriverEntryPointQueryResult q;
+    void* p = nullptr;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
+  }
+  return fn;
+}
+
+// 3-D bf16 tensor map: dims (d0 contiguous, d1, d2) with byte strides s1, s2, box (b0, b1, 1)
+static int make_map(CUtensorMap* map, const void* base, uint64_t d0, uint64_t d1, uint64_t d2, uint64_t s1, uint64_t s2,
+                    uint32_t b0, uint32_t b1) {
+  auto enc = get_encode();
+  if (!enc) {
+    set_error("gemm(bf16): cuTensorMapEncodeTiled unavailable");
+    return B200_ERR_CUDA;
+  }
+  cuuint64_t dims[3] = {d0, d1, d2};
+  cuuint64_t strides[2] = {s1, s2};
+  cuuint32_t box[3] = {b0, b1, 1};
+  cuuint32_t estr[3] = {1, 1, 1};
+  CUresult r = enc(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, const_cast<void*>(base), dims, strides, box, estr,
+                   CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                   CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) {
+    set_error("gemm(bf16): cuTensorMapEncodeTiled failed (%d): dims %llu %llu %llu strides %llu %llu", (int)r,
+              (unsigned long long)d0, (unsigned long long)d1, (unsigned long long)d2, (unsigned long long)s1,
+              (unsigned long long)s2);
+    return B200_ERR_ARG;
+  }
+  return B200_OK;
+}
+
+template <int BN>
+static int launch(const CUtensorMap& ma, const CUtensorMap& mb, const Args& a, int64_t batch, cudaStream_t s) {
+  const size_t smem = (size_t)STAGES * (BM * BK * 2 + BN * BK * 2) + 1024 + 256;
+  static bool attr_set[64] = {false};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (dev < 0 || dev >= 64 || !attr_set[dev]) {
+    cudaFuncSetAttribute(gemm_tc_kernel<BN>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    if (dev >= 0 && dev < 64) attr_set[dev] = true;
+  }
+  dim3 grid((unsigned)ceil_div(a.N, BN), (unsigned)ceil_div(a.M, BM), (unsigned)batch);
+  gemm_tc_kernel<BN><<<grid, THREADS, smem, s>>>(ma, mb, a);
+  return check_launch("gemm(bf16 tcgen05)");
+}
+
+}  // namespace tc
+
+int gemm_bf16_tcgen05(int c_dt, const void* A, const void* B, void* C, int64_t batch, int64_t M, int64_t N, int64_t K,
+                      int64_t sA, int64_t rsA, int64_t csA, int64_t sB, int64_t rsB, int64_t csB, int64_t sC, int64_t ldc,
+                      float alpha, const float* bias, int epi, void* aux, cudaStream_t s) {
+  using namespace tc;
+  // operand majors: A K-major if csA == 1, MN-major if rsA == 1; B K-major if rsB == 1, MN-major if csB == 1
+  int a_mn, b_mn;
+  if (csA == 1) a_mn = 0;
+  else if (rsA == 1) a_mn = 1;
+  else {
+    set_error("gemm(bf16): A needs a unit stride (rs %lld cs %lld)", (long long)rsA, (long long)csA);
+    return B200_ERR_UNSUPPORTED;
+  }
+  if (rsB == 1) b_mn = 0;
+  else if (csB == 1) b_mn = 1;
+  else {
+    set_error("gemm(bf16): B needs a unit stride (rs %lld cs %lld)", (long long)rsB, (long long)csB);
+    return B200_ERR_UNSUPPORTED;
+  }
+  const int64_t lda = a_mn ? csA : rsA;  // elements between consecutive non-contiguous indices
+  const int64_t ldb = b_mn ? rsB : csB;
+  if ((reinterpret_cast<uintptr_t>(A) & 15) || (reinterpret_cast<uintptr_t>(B) & 15) || (lda * 2) % 16 || (ldb * 2) % 16 ||
+      (batch > 1 && ((sA * 2) % 16 || (sB * 2) % 16))) {
+    set_error("gemm(bf16): TMA needs 16-byte aligned bases and strides (lda %lld ldb %lld)", (long long)lda, (long long)ldb);
+    return B200_ERR_UNSUPPORTED;
+  }
+  B200_REQUIRE(M <= INT32_MAX && N <= INT32_MAX && K <= INT32_MAX, "gemm(bf16): dims too large");
+  const int BN = N > 128 ? 256 : 128;
+  CUtensorMap ma, mb;
+  const uint64_t zA = batch > 1 ? (uint64_t)sA * 2 : (uint64_t)lda * 2 * (uint64_t)(a_mn ? K : M);
+  const uint64_t zB = batch > 1 ? (uint64_t)sB * 2 : (uint64_t)ldb * 2 * (uint64_t)(b_mn ? K : N);
+  int rc;
+  if (!a_mn) rc = make_map(&ma, A, K, M, batch, lda * 2, zA, 64, 128);
+  else rc = make_map(&ma, A, M, K, batch, lda * 2, zA, 64, 64);
+  if (rc) return rc;
+  if (!b_mn) rc = make_map(&mb, B, K, N, batch, ldb * 2, zB, 64, BN);
+  else rc = make_map(&mb, B, N, K, batch, ldb * 2, zB, 64, 64);
+  if (rc) return rc;
+  Args a;
+  a.C = C;
+  a.bias = bias;
+  a.aux = (uint8_t*)aux;
+  a.M = M;
+  a.N = N;
+  a.K = K;
+  a.sC = sC;
+  a.ldc = ldc;
+  a.alpha = alpha;
+  a.c_dt = c_dt;
+  a.epi = epi;
+  a.a_mn = a_mn;
+  a.b_mn = b_mn;
+  B200_REQUIRE(ceil_div(M, BM) <= 65535, "gemm(bf16): M too large");
+  if (BN == 256) return launch<256>(ma, mb, a, batch, s);
+  return launch<128>(ma, mb, a, batch, s);
+}
+
+}  // namespace b200

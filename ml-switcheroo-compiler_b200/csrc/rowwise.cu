@@ -1,0 +1,365 @@
+// Row reductions (subsystem 2): axis reductions, argmax, softmax / log-softmax,
+// LayerNorm forward and its three VJPs. Warp-shuffle + shared-memory block reductions;
+// one CTA per row for last-axis work, column-parallel loops for middle-axis work.
+#include <math.h>
+
+#include "common.cuh"
+
+namespace b200 {
+
+// ---------------------------------------------------------------------------------
+// middle-axis reduce: x [outer, red, inner] -> y [outer, inner]
+// ---------------------------------------------------------------------------------
+
+// inner == 1: one CTA per outer row (row reduction)
+template <int OP>
+__global__ void __launch_bounds__(256) reduce_rows_kernel(const void* __restrict__ x, int dt, float* __restrict__ y,
+                                                          int64_t red) {
+  __shared__ float sred[32];
+  const int64_t row = blockIdx.x;
+  float acc = (OP == B200_RED_MAX) ? -INFINITY : 0.f;
+  for (int64_t i = threadIdx.x; i < red; i += blockDim.x) {
+    float v = load_as_f32(x, row * red + i, dt);
+    if (OP == B200_RED_MAX) acc = fmaxf(acc, v);
+    else acc += v;
+  }
+  float t = (OP == B200_RED_MAX) ? block_max(acc, sred) : block_sum(acc, sred);
+  if (threadIdx.x == 0) y[row] = (OP == B200_RED_MEAN) ? t / (float)red : t;
+}
+
+// inner > 1: each thread owns one (outer, inner) column over a chunk of `red`;
+// chunks are combined with atomics into y (zeroed / -inf filled first).
+__device__ __forceinline__ void atomic_max_f32(float* addr, float v) {
+  // ordered integer view of IEEE floats
+  if (v >= 0.f) atomicMax(reinterpret_cast<int*>(addr), __float_as_int(v));
+  else atomicMin(reinterpret_cast<unsigned int*>(addr), __float_as_uint(v));
+}
+
+template <int OP>
+__global__ void __launch_bounds__(256) reduce_cols_kernel(const void* __restrict__ x, int dt, float* __restrict__ y,
+                                                          int64_t outer, int64_t red, int64_t inner, int64_t chunk,
+                                                          int split) {
+  const int64_t col = blockIdx.x * (int64_t)blockDim.x + threadIdx.x;
+  const int64_t o = blockIdx.y;
+  if (col >= inner) return;
+  const int64_t r0 = blockIdx.z * chunk;
+  const int64_t r1 = min(red, r0 + chunk);
+  float acc = (OP == B200_RED_MAX) ? -INFINITY : 0.f;
+  const int64_t base = o * red * inner + col;
+  for (int64_t r = r0; r < r1; ++r) {
+    float v = load_as_f32(x, base + r * inner, dt);
+    if (OP == B200_RED_MAX) acc = fmaxf(acc, v);
+    else acc += v;
+  }
+  if (OP == B200_RED_MEAN) acc /= (float)red;
+  float* dst = y + o * inner + col;
+  if (!split) *dst = acc;
+  else if (OP == B200_RED_MAX) atomic_max_f32(dst, acc);
+  else atomicAdd(dst, acc);
+}
+
+__global__ void fill_kernel(float* y, int64_t n, float v) {
+  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n; i += (int64_t)gridDim.x * blockDim.x) y[i] = v;
+}
+
+// ---------------------------------------------------------------------------------
+// argmax over the middle axis; first maximum wins, NaN counts as the maximum
+// ---------------------------------------------------------------------------------
+__device__ __forceinline__ bool am_better(float v, int64_t i, float m, int64_t j) {
+  // does (v,i) beat (m,j)? ties -> smaller index
+  const bool vn = isnan(v), mn = isnan(m);
+  if (vn || mn) {
+    if (vn && !mn) return true;
+    if (!vn && mn) return false;
+    return i < j;
+  }
+  if (v > m) return true;
+  if (v < m) return false;
+  return i < j;
+}
+
+__global__ void __launch_bounds__(256) argmax_rows_kernel(const void* __restrict__ x, int dt, int64_t* __restrict__ idx,
+                                                          int64_t red) {
+  __shared__ float sv[32];
+  __shared__ int64_t si[32];
+  const int64_t row = blockIdx.x;
+  float m = -INFINITY;
+  int64_t j = INT64_MAX;
+  for (int64_t i = threadIdx.x; i < red; i += blockDim.x) {
+    float v = load_as_f32(x, row * red + i, dt);
+    if (am_better(v, i, m, j)) { m = v; j = i; }
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) {
+    float v2 = __shfl_xor_sync(0xffffffffu, m, o);
+    int64_t j2 = __shfl_xor_sync(0xffffffffu, j, o);
+    if (am_better(v2, j2, m, j)) { m = v2; j = j2; }
+  }
+  const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5, nw = blockDim.x >> 5;
+  if (lane == 0) { sv[wid] = m; si[wid] = j; }
+  __syncthreads();
+  if (wid == 0) {
+    m = lane < nw ? sv[lane] : -INFINITY;
+    j = lane < nw ? si[lane] : INT64_MAX;
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+      float v2 = __shfl_xor_sync(0xffffffffu, m, o);
+      int64_t j2 = __shfl_xor_sync(0xffffffffu, j, o);
+      if (am_better(v2, j2, m, j)) { m = v2; j = j2; }
+    }
+    if (lane == 0) idx[row] = (j == INT64_MAX) ? 0 : j;
+  }
+}
+
+__global__ void __launch_bounds__(256) argmax_cols_kernel(const void* __restrict__ x, int dt, int64_t* __restrict__ idx,
+                                                          int64_t outer, int64_t red, int64_t inner) {
+  const int64_t col = blockIdx.x * (int64_t)blockDim.x + threadIdx.x;
+  const int64_t o = blockIdx.y;
+  if (col >= inner) return;
+  float m = -INFINITY;
+  int64_t j = INT64_MAX;
+  for (int64_t r = 0; r < red; ++r) {
+    float v = load_as_f32(x, (o * red + r) * inner + col, dt);
+    if (am_better(v, r, m, j)) { m = v; j = r; }
+  }
+  idx[o * inner + col] = (j == INT64_MAX) ? 0 : j;
+}
+
+// ---------------------------------------------------------------------------------
+// softmax / log-softmax over the last axis (one CTA per row, online max/sum)
+// ---------------------------------------------------------------------------------
+__global__ void __launch_bounds__(512) softmax_kernel(const float* __restrict__ x, float* __restrict__ y, int64_t cols,
+                                                      int logmode) {
+  __shared__ float sred[32];
+  const float* xr = x + blockIdx.x * cols;
+  float* yr = y + blockIdx.x * cols;
+  float m = -INFINITY, s = 0.f;
+  for (int64_t i = threadIdx.x; i < cols; i += blockDim.x) {
+    float v = xr[i];
+    if (v > m) { s = s * expf(m - v); m = v; }  // rescale running sum (v finite here)
+    s += expf(v - m);
+  }
+  const float M = block_max(m, sred);
+  s = (m == -INFINITY) ? 0.f : s * expf(m - M);
+  const float S = block_sum(s, sred);
+  if (logmode) {
+    const float lse = logf(S);
+    for (int64_t i = threadIdx.x; i < cols; i += blockDim.x) yr[i] = xr[i] - M - lse;
+  } else {
+    const float inv = 1.f / S;
+    for (int64_t i = threadIdx.x; i < cols; i += blockDim.x) yr[i] = expf(xr[i] - M) * inv;
+  }
+}
+
+// ---------------------------------------------------------------------------------
+// LayerNorm (biased variance, two-pass mean then variance like np.mean / np.var)
+// ---------------------------------------------------------------------------------
+__device__ __forceinline__ void row_stats(const float* __restrict__ xr, int64_t cols, float eps, float* sred,
+                                          float& mean, float& rstd) {
+  float s = 0.f;
+  for (int64_t i = threadIdx.x; i < cols; i += blockDim.x) s += xr[i];
+  mean = block_sum(s, sred) / (float)cols;
+  float q = 0.f;
+  for (int64_t i = threadIdx.x; i < cols; i += blockDim.x) {
+    float d = xr[i] - mean;
+    q += d * d;
+  }
+  const float var = block_sum(q, sred) / (float)cols;
+  rstd = 1.f / sqrtf(var + eps);
+}
+
+__global__ void __launch_bounds__(512) layernorm_kernel(const float* __restrict__ x, const float* __restrict__ g,
+                                                        const float* __restrict__ b, float* __restrict__ y,
+                                                        int64_t cols, float eps) {
+  __shared__ float sred[32];
+  const float* xr = x + blockIdx.x * cols;
+  float* yr = y + blockIdx.x * cols;
+  float mean, rstd;
+  row_stats(xr, cols, eps, sred, mean, rstd);
+  for (int64_t i = threadIdx.x; i < cols; i += blockDim.x) {
+    float v = (xr[i] - mean) * rstd;
+    yr[i] = (g ? g[i] : 1.f) * v + (b ? b[i] : 0.f);
+  }
+}
+
+__global__ void __launch_bounds__(512) layernorm_input_grad_kernel(const float* __restrict__ dy, const float* __restrict__ x,
+                                                                   const float* __restrict__ g, float* __restrict__ dx,
+                                                                   int64_t cols, float eps) {
+  __shared__ float sred[32];
+  const float* xr = x + blockIdx.x * cols;
+  const float* dyr = dy + blockIdx.x * cols;
+  float* dxr = dx + blockIdx.x * cols;
+  float mean, rstd;
+  row_stats(xr, cols, eps, sred, mean, rstd);
+  float s1 = 0.f, s2 = 0.f;
+  for (int64_t i = threadIdx.x; i < cols; i += blockDim.x) {
+    float dyg = dyr[i] * (g ? g[i] : 1.f);
+    float xh = (xr[i] - mean) * rstd;
+    s1 += dyg;
+    s2 += dyg * xh;
+  }
+  const float S1 = block_sum(s1, sred);
+  const float S2 = block_sum(s2, sred);
+  const float d = (float)cols;
+  for (int64_t i = threadIdx.x; i < cols; i += blockDim.x) {
+    float dyg = dyr[i] * (g ? g[i] : 1.f);
+    float xh = (xr[i] - mean) * rstd;
+    dxr[i] = (rstd / d) * (d * dyg - S1 - xh * S2);
+  }
+}
+
+// dgamma[c] = sum_r dy[r,c] * xhat[r,c], dbeta[c] = sum_r dy[r,c].
+// Each CTA takes ROWS_PER_CTA rows, keeps column partials in shared memory and adds
+// them into the (zeroed) outputs with one atomic per column.
+constexpr int LN_PG_ROWS = 64;
+__global__ void __launch_bounds__(256) layernorm_param_grad_kernel(const float* __restrict__ dy, const float* __restrict__ x,
+                                                                   float* __restrict__ dg, float* __restrict__ db,
+                                                                   int64_t rows, int64_t cols, float eps) {
+  extern __shared__ float sm[];  // [2*cols] partials
+  __shared__ float sred[32];
+  float* pg = sm;
+  float* pb = sm + cols;
+  for (int64_t i = threadIdx.x; i < 2 * cols; i += blockDim.x) sm[i] = 0.f;
+  __syncthreads();
+  const int64_t r0 = blockIdx.x * (int64_t)LN_PG_ROWS;
+  const int64_t r1 = min(rows, r0 + LN_PG_ROWS);
+  for (int64_t r = r0; r < r1; ++r) {
+    const float* xr = x + r * cols;
+    const float* dyr = dy + r * cols;
+    float mean, rstd;
+    row_stats(xr, cols, eps, sred, mean, rstd);
+    for (int64_t i = threadIdx.x; i < cols; i += blockDim.x) {
+      float d = dyr[i];
+      pg[i] += d * (xr[i] - mean) * rstd;
+      pb[i] += d;
+    }
+  }
+  __syncthreads();
+  for (int64_t i = threadIdx.x; i < cols; i += blockDim.x) {
+    if (dg) atomicAdd(dg + i, pg[i]);
+    if (db) atomicAdd(db + i, pb[i]);
+  }
+}
+
+}  // namespace b200
+
+using namespace b200;
+
+extern "C" int b200_reduce(int dt, const void* x, float* y, int64_t outer, int64_t red, int64_t inner, int op,
+                           void* stream) {
+  B200_REQUIRE(x && y, "reduce: null pointer");
+  B200_REQUIRE(outer >= 0 && red >= 0 && inner >= 0, "reduce: negative size");
+  B200_REQUIRE(op == B200_RED_SUM || op == B200_RED_MEAN || op == B200_RED_MAX, "reduce: bad op %d", op);
+  if (dt != B200_F32 && dt != B200_BF16) {
+    set_error("reduce: dtype %d", dt);
+    return B200_ERR_DTYPE;
+  }
+  B200_REQUIRE(outer <= 2147483647LL && outer <= 65535 || inner == 1, "reduce: outer too large for column mode");
+  if (outer == 0 || inner == 0) return B200_OK;
+  cudaStream_t s = as_stream(stream);
+  if (red == 0) {
+    // numpy: sum of nothing = 0, mean = nan, max raises
+    B200_REQUIRE(op != B200_RED_MAX, "reduce: max over an empty axis");
+    fill_kernel<<<64, 256, 0, s>>>(y, outer * inner, op == B200_RED_SUM ? 0.f : NAN);
+    return check_launch("reduce(fill)");
+  }
+  if (inner == 1) {
+    B200_REQUIRE(outer <= 2147483647LL, "reduce: too many rows");
+    switch (op) {
+      case B200_RED_SUM: reduce_rows_kernel<B200_RED_SUM><<<(unsigned)outer, 256, 0, s>>>(x, dt, y, red); break;
+      case B200_RED_MEAN: reduce_rows_kernel<B200_RED_MEAN><<<(unsigned)outer, 256, 0, s>>>(x, dt, y, red); break;
+      default: reduce_rows_kernel<B200_RED_MAX><<<(unsigned)outer, 256, 0, s>>>(x, dt, y, red); break;
+    }
+    return check_launch("reduce(rows)");
+  }
+  // column mode; split `red` across CTAs when there are too few columns to fill the GPU
+  const int64_t cols_blocks = ceil_div(inner, 256);
+  int64_t split = 1;
+  const int64_t want = (int64_t)num_sms() * 4;
+  if (cols_blocks * outer < want) split = std::min<int64_t>(ceil_div(want, cols_blocks * outer), ceil_div(red, 32));
+  if (split < 1) split = 1;
+  if (split > 65535) split = 65535;
+  const int64_t chunk = ceil_div(red, split);
+  split = ceil_div(red, chunk);
+  if (split > 1) {
+    fill_kernel<<<64, 256, 0, s>>>(y, outer * inner, op == B200_RED_MAX ? -INFINITY : 0.f);
+    int rc = check_launch("reduce(init)");
+    if (rc) return rc;
+  }
+  dim3 grid((unsigned)cols_blocks, (unsigned)outer, (unsigned)split);
+  switch (op) {
+    case B200_RED_SUM: reduce_cols_kernel<B200_RED_SUM><<<grid, 256, 0, s>>>(x, dt, y, outer, red, inner, chunk, split > 1); break;
+    case B200_RED_MEAN: reduce_cols_kernel<B200_RED_MEAN><<<grid, 256, 0, s>>>(x, dt, y, outer, red, inner, chunk, split > 1); break;
+    default: reduce_cols_kernel<B200_RED_MAX><<<grid, 256, 0, s>>>(x, dt, y, outer, red, inner, chunk, split > 1); break;
+  }
+  return check_launch("reduce(cols)");
+}
+
+extern "C" int b200_argmax(int dt, const void* x, int64_t* idx, int64_t outer, int64_t red, int64_t inner, void* stream) {
+  B200_REQUIRE(x && idx, "argmax: null pointer");
+  B200_REQUIRE(outer >= 0 && red >= 1 && inner >= 0, "argmax: bad sizes (red must be >= 1)");
+  if (dt != B200_F32 && dt != B200_BF16) {
+    set_error("argmax: dtype %d", dt);
+    return B200_ERR_DTYPE;
+  }
+  if (outer == 0 || inner == 0) return B200_OK;
+  cudaStream_t s = as_stream(stream);
+  if (inner == 1) {
+    B200_REQUIRE(outer <= 2147483647LL, "argmax: too many rows");
+    argmax_rows_kernel<<<(unsigned)outer, 256, 0, s>>>(x, dt, idx, red);
+  } else {
+    B200_REQUIRE(outer <= 65535, "argmax: outer too large");
+    dim3 grid((unsigned)ceil_div(inner, 256), (unsigned)outer);
+    argmax_cols_kernel<<<grid, 256, 0, s>>>(x, dt, idx, outer, red, inner);
+  }
+  return check_launch("argmax");
+}
+
+extern "C" int b200_softmax(const float* x, float* y, int64_t rows, int64_t cols, int log, void* stream) {
+  B200_REQUIRE(x && y, "softmax: null pointer");
+  B200_REQUIRE(rows >= 0 && cols >= 1 && rows <= 2147483647LL, "softmax: bad sizes");
+  if (rows == 0) return B200_OK;
+  const int threads = cols >= 4096 ? 512 : (cols >= 1024 ? 256 : 128);
+  softmax_kernel<<<(unsigned)rows, threads, 0, as_stream(stream)>>>(x, y, cols, log);
+  return check_launch("softmax");
+}
+
+extern "C" int b200_layernorm(const float* x, const float* g, const float* b, float* y, int64_t rows, int64_t cols,
+                              float eps, void* stream) {
+  B200_REQUIRE(x && y, "layernorm: null pointer");
+  B200_REQUIRE(rows >= 0 && cols >= 1 && rows <= 2147483647LL, "layernorm: bad sizes");
+  if (rows == 0) return B200_OK;
+  const int threads = cols >= 4096 ? 512 : (cols >= 1024 ? 256 : 128);
+  layernorm_kernel<<<(unsigned)rows, threads, 0, as_stream(stream)>>>(x, g, b, y, cols, eps);
+  return check_launch("layernorm");
+}
+
+extern "C" int b200_layernorm_input_grad(const float* dy, const float* x, const float* g, float* dx, int64_t rows,
+                                         int64_t cols, float eps, void* stream) {
+  B200_REQUIRE(dy && x && dx, "layernorm_input_grad: null pointer");
+  B200_REQUIRE(rows >= 0 && cols >= 1 && rows <= 2147483647LL, "layernorm_input_grad: bad sizes");
+  if (rows == 0) return B200_OK;
+  const int threads = cols >= 4096 ? 512 : (cols >= 1024 ? 256 : 128);
+  layernorm_input_grad_kernel<<<(unsigned)rows, threads, 0, as_stream(stream)>>>(dy, x, g, dx, cols, eps);
+  return check_launch("layernorm_input_grad");
+}
+
+extern "C" int b200_layernorm_param_grad(const float* dy, const float* x, float* dg, float* db, int64_t rows, int64_t cols,
+                                         float eps, void* stream) {
+  B200_REQUIRE(dy && x, "layernorm_param_grad: null pointer");
+  B200_REQUIRE(dg || db, "layernorm_param_grad: no output");
+  B200_REQUIRE(rows >= 0 && cols >= 1, "layernorm_param_grad: bad sizes");
+  B200_REQUIRE(cols <= 16384, "layernorm_param_grad: cols %lld > 16384", (long long)cols);
+  cudaStream_t s = as_stream(stream);
+  if (dg) {
+    cudaMemsetAsync(dg, 0, cols * sizeof(float), s);
+  }
+  if (db) {
+    cudaMemsetAsync(db, 0, cols * sizeof(float), s);
+  }
+  if (rows == 0) return check_launch("layernorm_param_grad(zero)");
+  const size_t smem = 2 * cols * sizeof(float);
+  if (smem > 48 * 1024) cudaFuncSetAttribute(layernorm_param_grad_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+  layernorm_param_grad_kernel<<<(unsigned)ceil_div(rows, LN_PG_ROWS), 256, smem, s>>>(dy, x, dg, db, rows, cols, eps);
+  return check_launch("layernorm_param_grad");
+}

@@ -1,0 +1,252 @@
+"""Kernel-level checks through the C ABI against numpy / fp32 references, including the
+edge cases: empty and ragged sizes, broadcasting, strided views, ties, bf16 tensor-core
+GEMM in every operand layout."""
+
+import numpy as np
+import pytest
+import torch
+
+from gpu_helpers import to_np
+
+pytestmark = pytest.mark.gpu
+
+
+def T(a):
+    return torch.from_numpy(np.ascontiguousarray(a)).cuda()
+
+
+@pytest.fixture(autouse=True)
+def _policy(cuda):
+    from b200 import ops
+
+    ops.Config.matmul_dtype = "f32"
+    ops.Config.conv_dtype = "f32"
+    yield
+
+
+def rng(seed=0):
+    return np.random.default_rng(seed)
+
+
+def test_elementwise_broadcast_and_chain():
+    from b200 import ops
+
+    r = rng()
+    x = r.standard_normal((33, 17), dtype=np.float32)
+    col = r.standard_normal(17, dtype=np.float32)
+    row = r.standard_normal((33, 1), dtype=np.float32)
+    np.testing.assert_allclose(to_np(ops.op_add(T(x), T(col))), x + col, rtol=1e-6)
+    np.testing.assert_allclose(to_np(ops.op_multiply(T(x), T(row))), x * row, rtol=1e-6)
+    np.testing.assert_allclose(to_np(ops.op_subtract(T(x), 0.5)), x - 0.5, rtol=1e-6)
+    np.testing.assert_array_equal(to_np(ops.op_greater(T(x), 0.0)), x > 0)
+    np.testing.assert_allclose(to_np(ops.op_gelu(T(x))), 0.5 * x * (1 + np.tanh(np.sqrt(2 / np.pi) * (x + 0.044715 * x**3))), rtol=1e-5, atol=1e-6)
+    np.testing.assert_allclose(to_np(ops.op_exp(T(x))), np.exp(x), rtol=1e-6)
+    np.testing.assert_allclose(to_np(ops.op_tanh(T(x))), np.tanh(x), rtol=1e-5, atol=1e-7)
+    # transposed (strided) view input
+    xt = T(x).t()
+    np.testing.assert_allclose(to_np(ops.op_add(xt, 1.0)), x.T + 1.0, rtol=1e-6)
+    # bool * float
+    m = x > 0
+    np.testing.assert_allclose(to_np(ops.op_multiply(T(x), T(m))), x * m, rtol=1e-6)
+    # empty
+    assert to_np(ops.op_add(T(np.zeros((0, 5), np.float32)), 1.0)).shape == (0, 5)
+    # scalar (0-d) tensors
+    np.testing.assert_allclose(to_np(ops.op_multiply(T(np.array(2.0, np.float32)), T(x))), 2 * x)
+
+
+def test_reductions_axes_and_split():
+    from b200 import ops
+
+    r = rng(1)
+    x = r.standard_normal((7, 300, 5), dtype=np.float32)
+    for axis in (None, 0, 1, 2, -1, (0, 1), (1, 2), (0, 2)):
+        for kd in (False, True):
+            got = to_np(ops.op_reduce_sum(T(x), axis=axis, keepdims=kd))
+            np.testing.assert_allclose(got, np.sum(x, axis=axis, keepdims=kd), rtol=1e-5, atol=1e-4)
+            got = to_np(ops.op_reduce_mean(T(x), axis=axis, keepdims=kd))
+            np.testing.assert_allclose(got, np.mean(x, axis=axis, keepdims=kd), rtol=1e-5, atol=1e-5)
+            got = to_np(ops.op_reduce_max(T(x), axis=axis, keepdims=kd))
+            np.testing.assert_array_equal(got, np.max(x, axis=axis, keepdims=kd))
+    # column reduction with many rows (split + atomics path)
+    y = r.standard_normal((8192, 64), dtype=np.float32)
+    np.testing.assert_allclose(to_np(ops.op_reduce_sum(T(y), axis=0)), y.sum(0), rtol=1e-4, atol=1e-3)
+    np.testing.assert_array_equal(to_np(ops.op_reduce_max(T(y), axis=0)), y.max(0))
+    b = r.standard_normal(64, dtype=np.float32)
+    np.testing.assert_allclose(to_np(ops.op_broadcast_reduce(T(y), T(b))), y.sum(0), rtol=1e-4, atol=1e-3)
+
+
+def test_argmax_ties_first_and_exact():
+    from b200 import ops
+
+    x = np.array([[1.0, 3.0, 3.0, 0.0], [2.0, 2.0, 2.0, 2.0], [-1.0, -5.0, -1.0, -0.5]], np.float32)
+    np.testing.assert_array_equal(to_np(ops.op_argmax(T(x), axis=-1)), np.argmax(x, -1))
+    r = rng(2)
+    big = r.standard_normal((300, 4097), dtype=np.float32)
+    big[:, 4096] = big.max(1)  # tie with an earlier max -> earlier index wins
+    np.testing.assert_array_equal(to_np(ops.op_argmax(T(big), axis=-1)), np.argmax(big, -1))
+    np.testing.assert_array_equal(to_np(ops.op_argmax(T(big), axis=0)), np.argmax(big, 0))
+    assert int(to_np(ops.op_argmax(T(big)))) == int(np.argmax(big))
+
+
+@pytest.mark.parametrize("cols", [1, 10, 1000, 4096, 32000])
+def test_softmax_logsoftmax(cols):
+    from b200 import ops
+
+    r = rng(3)
+    x = (r.standard_normal((5, cols)) * 3).astype(np.float32)
+    e = np.exp(x - x.max(-1, keepdims=True))
+    np.testing.assert_allclose(to_np(ops.op_softmax(T(x))), e / e.sum(-1, keepdims=True), rtol=1e-5, atol=1e-7)
+    ls = x - x.max(-1, keepdims=True) - np.log(e.sum(-1, keepdims=True))
+    np.testing.assert_allclose(to_np(ops.op_log_softmax(T(x))), ls, rtol=1e-5, atol=1e-5)
+    if cols > 1:
+        np.testing.assert_allclose(to_np(ops.op_softmax(T(x), axis=0)), np.exp(x) / np.exp(x).sum(0), rtol=1e-5, atol=1e-7)
+
+
+@pytest.mark.parametrize("cols", [7, 1024, 4096])
+def test_layernorm_fwd_and_grads(cols):
+    from b200 import ops
+    from oracle import evaluator as O
+
+    r = rng(4)
+    x = r.standard_normal((37, cols), dtype=np.float32)
+    g = r.uniform(0.5, 1.5, cols).astype(np.float32)
+    b = r.standard_normal(cols, dtype=np.float32)
+    dy = r.standard_normal((37, cols), dtype=np.float32)
+    np.testing.assert_allclose(to_np(ops.op_layer_norm(T(x), T(g), T(b), eps=1e-5)), O.execute_op("LayerNorm", x, g, b, eps=1e-5), rtol=1e-4, atol=1e-5)
+    np.testing.assert_allclose(to_np(ops.op_layer_norm_input_grad(T(dy), T(x), T(g), eps=1e-5)),
+                               O.execute_op("LayerNormInputGrad", dy, x, g, eps=1e-5), rtol=1e-4, atol=1e-5)
+    np.testing.assert_allclose(to_np(ops.op_layer_norm_gamma_grad(T(dy), T(x), eps=1e-5)),
+                               O.execute_op("LayerNormGammaGrad", dy, x, eps=1e-5), rtol=1e-4, atol=1e-4)
+    np.testing.assert_allclose(to_np(ops.op_layer_norm_beta_grad(T(dy))), O.execute_op("LayerNormBetaGrad", dy), rtol=1e-4, atol=1e-4)
+
+
+def test_indexing_ops():
+    from b200 import ops
+    from oracle import evaluator as O
+
+    r = rng(5)
+    x = r.standard_normal((9, 10), dtype=np.float32)
+    idx = r.integers(0, 10, (9, 1))
+    np.testing.assert_array_equal(to_np(ops.op_take_along_axis(T(x), T(idx), axis=-1)), np.take_along_axis(x, idx, -1))
+    src = r.standard_normal((9, 1), dtype=np.float32)
+    z = np.zeros_like(x)
+    np.testing.assert_allclose(to_np(ops.op_scatter_add(T(z), T(idx), T(src), dim=-1)), O.execute_op("ScatterAdd", z, idx, src, dim=-1))
+    # repeated index within a row keeps the last write, like put_along_axis
+    idx2 = np.array([[3, 3]] * 9)
+    src2 = r.standard_normal((9, 2), dtype=np.float32)
+    np.testing.assert_allclose(to_np(ops.op_scatter_add(T(x), T(idx2), T(src2), dim=-1)), O.execute_op("ScatterAdd", x, idx2, src2, dim=-1))
+    table = r.standard_normal((50, 8), dtype=np.float32)
+    ids = r.integers(0, 50, 200)
+    np.testing.assert_array_equal(to_np(ops.op_take(T(table), T(ids), axis=0)), np.take(table, ids, axis=0))
+    upd = r.standard_normal((200, 8), dtype=np.float32)
+    ref = O.execute_op("TensorScatterAdd", np.zeros_like(table), ids.reshape(200, 1), upd)
+    np.testing.assert_allclose(to_np(ops.op_tensor_scatter_add(T(np.zeros_like(table)), T(ids.reshape(200, 1)), T(upd))), ref, rtol=1e-5, atol=1e-5)
+
+
+@pytest.mark.parametrize("ta,tb", [(False, False), (True, False), (False, True), (True, True)])
+def test_gemm_fp32_layouts_and_epilogue(ta, tb):
+    from b200 import _lib as L
+    from b200 import ops
+
+    r = rng(6)
+    M, N, K = 70, 45, 33
+    a = r.standard_normal((K, M) if ta else (M, K), dtype=np.float32)
+    b = r.standard_normal((N, K) if tb else (K, N), dtype=np.float32)
+    A = T(a).t() if ta else T(a)
+    B = T(b).t() if tb else T(b)
+    an, bn = (a.T if ta else a), (b.T if tb else b)
+    np.testing.assert_allclose(to_np(ops.gemm(A, B)), an @ bn, rtol=1e-4, atol=1e-4)
+    bias = r.standard_normal(N, dtype=np.float32)
+    out, mask = ops.gemm(A, B, bias=T(bias), epilogue=L.EPI_RELU, want_mask=True)
+    pre = an @ bn + bias
+    np.testing.assert_allclose(to_np(out), np.maximum(pre, 0), rtol=1e-4, atol=1e-4)
+    agree = to_np(mask) == (pre > 0)
+    assert agree.mean() > 0.999
+
+
+def _bf16(a):
+    from b200.workloads import _bf16_round
+
+    return _bf16_round(a)
+
+
+@pytest.mark.parametrize("ta,tb", [(False, False), (True, False), (False, True), (True, True)])
+@pytest.mark.parametrize("shape", [(128, 128, 64), (256, 512, 192), (200, 136, 72), (129, 257, 8)])
+def test_gemm_bf16_tcgen05_layouts(ta, tb, shape):
+    from b200 import ops
+
+    M, N, K = shape
+    r = rng(7)
+    a = _bf16(r.standard_normal((K, M) if ta else (M, K), dtype=np.float32))
+    b = _bf16(r.standard_normal((N, K) if tb else (K, N), dtype=np.float32))
+    A = T(a).to(torch.bfloat16)
+    B = T(b).to(torch.bfloat16)
+    A = A.t() if ta else A
+    B = B.t() if tb else B
+    an, bn = (a.T if ta else a), (b.T if tb else b)
+    ref = an.astype(np.float64) @ bn.astype(np.float64)
+    got = to_np(ops.gemm(A, B, ab_dtype=torch.bfloat16))
+    np.testing.assert_allclose(got, ref, rtol=1e-4, atol=1e-3 * np.sqrt(K))
+
+
+def test_gemm_bf16_batched_bias_relu_mask_bf16_out():
+    from b200 import _lib as L
+    from b200 import ops
+
+    r = rng(8)
+    Z, M, N, K = 3, 256, 384, 256
+    a = _bf16(r.standard_normal((Z, M, K), dtype=np.float32) * 0.05)
+    b = _bf16(r.standard_normal((Z, K, N), dtype=np.float32) * 0.05)
+    bias = r.standard_normal(N, dtype=np.float32) * 0.02
+    A, B = T(a).to(torch.bfloat16), T(b).to(torch.bfloat16)
+    pre = np.matmul(a.astype(np.float64), b.astype(np.float64)) + bias
+    out, mask = ops.gemm(A, B, bias=T(bias), epilogue=L.EPI_RELU, want_mask=True, ab_dtype=torch.bfloat16)
+    np.testing.assert_allclose(to_np(out), np.maximum(pre, 0), rtol=1e-4, atol=1e-4)
+    assert (to_np(mask) == (pre > 0)).mean() > 0.999
+    o16 = ops.gemm(A, B, ab_dtype=torch.bfloat16, out_dtype=torch.bfloat16)
+    np.testing.assert_allclose(to_np(o16), pre - bias, rtol=1e-2, atol=1e-2)
+    # batched with transposed operands (the backward-pass layouts)
+    g = _bf16(r.standard_normal((Z, M, N), dtype=np.float32))
+    G = T(g).to(torch.bfloat16)
+    dA = ops.gemm(G, B.transpose(-1, -2), ab_dtype=torch.bfloat16)
+    np.testing.assert_allclose(to_np(dA), np.matmul(g, np.swapaxes(b, -1, -2)), rtol=1e-4, atol=1e-3)
+    dB = ops.gemm(A.transpose(-1, -2), G, ab_dtype=torch.bfloat16)
+    np.testing.assert_allclose(to_np(dB), np.matmul(np.swapaxes(a, -1, -2), g), rtol=1e-4, atol=1e-3)
+
+
+@pytest.mark.parametrize("padding,stride", [("VALID", 1), ("VALID", 2), ("SAME", 1), ("SAME", 2)])
+def test_conv2d_fwd_dgrad_wgrad(padding, stride):
+    from b200 import ops
+    from oracle import evaluator as O
+
+    r = rng(9)
+    x = r.standard_normal((2, 5, 11, 10), dtype=np.float32)
+    w = r.standard_normal((7, 5, 3, 3), dtype=np.float32)
+    kw = dict(stride=[stride, stride], padding=padding)
+    y_ref = O.execute_op("Conv2D", x, w, **kw)
+    np.testing.assert_allclose(to_np(ops.op_conv2d(T(x), T(w), **kw)), y_ref, rtol=1e-4, atol=1e-4)
+    dy = r.standard_normal(y_ref.shape, dtype=np.float32)
+    dx_ref = O.execute_op("Conv2DInputGrad", dy, w, target_shape=list(x.shape), **kw)
+    np.testing.assert_allclose(to_np(ops.op_conv2d_input_grad(T(dy), T(w), target_shape=list(x.shape), **kw)), dx_ref, rtol=1e-4, atol=1e-4)
+    dw_ref = O.execute_op("Conv2DWeightGrad", x, dy, target_shape=list(w.shape), **kw)
+    np.testing.assert_allclose(to_np(ops.op_conv2d_weight_grad(T(x), T(dy), target_shape=list(w.shape), **kw)), dw_ref, rtol=1e-4, atol=1e-3)
+
+
+def test_unknown_op_raises_no_fallback():
+    from b200 import B200Backend, UnimplementedMathError
+
+    with pytest.raises(UnimplementedMathError):
+        B200Backend.execute_op("NotARealOp", T(np.zeros(3, np.float32)))
+
+
+def test_device_error_flag_for_bad_index():
+    from b200 import _lib as L
+    from b200 import ops
+
+    x = T(np.zeros((2, 4), np.float32))
+    bad = T(np.array([[1], [9]], np.int64))
+    y = ops.op_take_along_axis(x, bad, axis=-1)  # out-of-range index: recorded, skipped
+    rc = L.lib().b200_check_device_error(ops.stream_ptr())
+    assert rc == L.ERR_ARG
+    assert L.lib().b200_check_device_error(ops.stream_ptr()) == L.OK  # flag cleared
+    del y
