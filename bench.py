@@ -1,0 +1,429 @@
+"""Benchmark: fwd+bwd graph steps/sec of the b200 backend (one JSON line on rank 0).
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--workload NAME] [--impl b200|reference]
+
+A step is one evaluation of the workload's fwd+bwd LogicalGraph (the graph the
+reference's tracer + AD produced, stored under tests/golden/graphs) on one batch of
+seeded synthetic inputs. Default workload: the fused bandwidth-bound row graph
+(x[8192,4096]: affine -> GELU -> LayerNorm -> softmax + argmax, fwd+bwd w.r.t. x, a, b).
+
+Multi-GPU (torchrun, one process per GPU, NCCL): weak scaling - every rank runs one full
+batch per step and the replicated-parameter gradients are summed with NCCL AllReduce.
+``value`` = batches processed by all ranks / max-over-ranks device time.
+
+``--impl reference`` times the reference algorithm on the host CPU: the numpy
+restatement of the reference's evaluate_graph + numpy kernels (pinned bit-exact to the
+reference's own evaluation by tests/test_oracle.py), on a bounded row sample spread over
+all host cores, scaled to a full step.
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import math
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+PKG = os.path.join(ROOT, "ml-switcheroo-compiler_b200")
+for _p in (ROOT, PKG):
+    if _p not in sys.path:
+        sys.path.insert(0, _p)
+
+import numpy as np  # noqa: E402
+
+# workload -> (graph case at per-rank batch, metric config, dtype, dominant kernel, params)
+WORKLOADS = {
+    "rowfused": {
+        "graph": "rowfused_full",
+        "dtype": "f32",
+        "params": ["a", "b"],
+        "reduce": "sum",
+        "desc": "fused bandwidth-bound graph x[8192,4096]: gelu_tanh(x*a+b) -> LayerNorm -> softmax + argmax, fwd+bwd wrt x,a,b",
+    },
+    "bmm": {
+        "graph": "bmm_full",
+        "dtype": "bf16",
+        "params": ["bias"],
+        "reduce": "sum",
+        "desc": "batched contraction A,B[16,2048,2048] bf16: relu(A@B+bias) fwd+bwd (dA, dB, dbias)",
+    },
+    "mlp": {"graph": "mlp_full", "dtype": "f32", "params": ["W1", "b1", "W2", "b2"], "reduce": "mean",
+            "desc": "2-layer MLP x[64,784] 784->256->10 softmax CE fwd+bwd"},
+    "cnn": {"graph": "cnn_full", "dtype": "bf16", "params": ["w1", "w2", "w3", "Wl", "bl"], "reduce": "mean",
+            "desc": "small CNN [512,3,32,32] 3 conv3x3 + GAP + linear, softmax CE fwd+bwd"},
+}
+
+
+def env_int(name: str, default: int) -> int:
+    try:
+        return int(os.environ.get(name, default))
+    except ValueError:
+        return default
+
+
+def peaks() -> dict:
+    p = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    if os.path.exists(p):
+        d = json.load(open(p))
+        return {"hbm_gbs": d["hbm_gbs"], "bf16_tflops": d["bf16_tflops"],
+                "bf16_tflops_sustained": d.get("bf16_tflops_sustained"), "source": "measured"}
+    return {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0, "source": "fallback"}
+
+
+class ClockSampler:
+    """nvidia-smi clock / throttle sampling while the timed region runs."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,clocks_event_reasons.hw_slowdown,"
+              "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index: int) -> None:
+        self.gpu = gpu_index
+        self.proc = None
+        self.lines: list[str] = []
+
+    def __enter__(self):
+        try:
+            self.proc = subprocess.Popen(["nvidia-smi", f"--id={self.gpu}", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
+                                          "-lms", "100"], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            self.t = threading.Thread(target=self._read, daemon=True)
+            self.t.start()
+        except (OSError, FileNotFoundError):
+            self.proc = None
+        return self
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.lines.append(line.strip())
+
+    def __exit__(self, *a):
+        if self.proc is not None:
+            time.sleep(0.25)
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
+
+    def summary(self) -> dict:
+        sm, mx, reasons = [], None, set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for ln in self.lines:
+            parts = [x.strip() for x in ln.split(",")]
+            if len(parts) < 9:
+                continue
+            try:
+                sm.append(float(parts[1]))
+                mx = float(parts[2])
+            except ValueError:
+                continue
+            for nm, v in zip(names, parts[5:9]):
+                if v.lower() == "active":
+                    reasons.add(nm)
+        if not sm:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": [], "samples": 0}
+        return {"sm_mhz": statistics.median(sm), "sm_max_mhz": mx, "reasons": sorted(reasons), "samples": len(sm)}
+
+
+# ----------------------------------------------------------------------------------
+# CPU reference arm (the oracle port of the reference's numpy evaluation)
+# ----------------------------------------------------------------------------------
+def _cpu_eval_rows(args):
+    case, lo, hi = args
+    from b200.workloads import make_inputs  # noqa: F401  (inputs are re-drawn per worker)
+    from oracle import evaluator as O
+
+    g = O.load_graph(case)
+    arr = _row_slice_inputs(g, lo, hi)
+    t0 = time.perf_counter()
+    O.evaluate_roles(g, arr)
+    return time.perf_counter() - t0
+
+
+def _row_slice_inputs(g, lo, hi):
+    rng = np.random.default_rng(1000 + lo)
+    C = g["dims"]["C"]
+    n = hi - lo
+    f32 = np.float32
+    return {"x": rng.standard_normal((n, C), dtype=f32), "a": rng.uniform(0.5, 1.5, C).astype(f32),
+            "b": (rng.standard_normal(C) * 0.1).astype(f32), "gamma": np.ones(C, f32), "beta": np.zeros(C, f32),
+            "cotangent": rng.standard_normal((n, C), dtype=f32)}
+
+
+def cpu_reference(workload: str, budget_s: float = 20.0) -> dict:
+    """Time the CPU reference on a bounded sample; returns steps/s for a full step."""
+    import multiprocessing as mp
+
+    spec = WORKLOADS[workload]
+    cores = os.cpu_count() or 1
+    if workload != "rowfused":
+        # whole-graph sample on one core (BLAS may use more): the full batch / a slice of it
+        from b200 import graph as G
+        from b200.workloads import make_inputs
+        from oracle import evaluator as O
+
+        g = O.load_graph(spec["graph"])
+        gg = G.load(spec["graph"])
+        arr = make_inputs(gg.meta["workload"], gg.meta["dims"], seed=0)
+        t0 = time.perf_counter()
+        O.evaluate_roles(g, arr)
+        dt = time.perf_counter() - t0
+        return {"value": 1.0 / dt, "unit": "steps/s", "cores": cores, "kind": "port",
+                "sample": f"one full step of {spec['graph']} (numpy, BLAS threads={cores})"}
+    # rowfused: rows are independent -> shard a row sample over all cores
+    R = 8192
+    probe = _cpu_eval_rows(("rowfused_full", 0, 16))  # warm-up + per-row cost estimate
+    per_row = max(probe / 16, 1e-5)
+    rows_total = int(min(R, max(cores * 8, budget_s * cores / per_row / 2)))
+    chunk = max(8, rows_total // cores)
+    tasks = [("rowfused_full", lo, min(rows_total, lo + chunk)) for lo in range(0, rows_total, chunk)]
+    ctx = mp.get_context("spawn")
+    t0 = time.perf_counter()
+    with ctx.Pool(min(cores, len(tasks))) as pool:
+        pool.map(_cpu_eval_rows, tasks)
+    wall = time.perf_counter() - t0
+    rows_done = sum(hi - lo for _, lo, hi in tasks)
+    step_s = wall * R / rows_done
+    return {"value": 1.0 / step_s, "unit": "steps/s", "cores": min(cores, len(tasks)), "kind": "port",
+            "sample": f"{rows_done} of {R} rows (row-sharded over {min(cores, len(tasks))} processes), wall {wall:.2f}s, scaled to 8192 rows"}
+
+
+# ----------------------------------------------------------------------------------
+# GPU arm
+# ----------------------------------------------------------------------------------
+def algorithmic_bytes_rowfused(R: int, C: int) -> int:
+    # read x, cot; write y, dx (fp32) + argmax int64 + da, db (+ a, b, gamma, beta read)
+    return 4 * R * C * 4 + R * 8 + 2 * C * 4 + 4 * C * 4
+
+
+def run_gpu(args) -> None:
+    import torch
+
+    rank, world = env_int("RANK", 0), env_int("WORLD_SIZE", 1)
+    local = env_int("LOCAL_RANK", 0)
+    torch.cuda.set_device(local)
+    dist = None
+    if world > 1:
+        import datetime
+
+        import torch.distributed as dist
+
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=torch.device("cuda", local))
+    from b200 import _lib
+    from b200 import graph as G
+    from b200 import ops
+    from b200.backend import B200Backend
+    from b200.executor import CompiledGraph
+    from b200.workloads import make_inputs
+
+    spec = WORKLOADS[args.workload]
+    ops.Config.matmul_dtype = "bf16" if spec["dtype"] == "bf16" else "f32"
+    ops.Config.conv_dtype = ops.Config.matmul_dtype
+    g = G.load(spec["graph"])
+    arrays = make_inputs(g.meta["workload"], g.meta["dims"], seed=rank)  # each rank: its own batch
+    param_ids = [g.roles[r] for r in spec["params"]]
+    grad_ids = [g.output_names["d_" + r] for r in spec["params"]]
+
+    dev = torch.device("cuda", local)
+    dinputs = {nid: torch.from_numpy(np.ascontiguousarray(arrays[r])).to(dev) for r, nid in g.roles.items()}
+    cg = CompiledGraph(g)
+    out = cg(dinputs)  # plan + capture
+    torch.cuda.synchronize()
+    plan = cg.runner.plan_for(cg.static_in)
+    n_before = _lib.launch_count()
+    plan.run(dict(cg.static_in))  # one eager run of the fused plan: count its kernels
+    torch.cuda.synchronize()
+    launches_per_step = int(_lib.launch_count() - n_before)
+    n_capture = len(plan.steps)
+
+    def allreduce():
+        if dist is not None:
+            for gid in grad_ids:
+                dist.all_reduce(out[gid])
+
+    stream = torch.cuda.current_stream()
+    for _ in range(args.warmup):
+        out = cg(dinputs)
+        allreduce()
+    torch.cuda.synchronize()
+    if dist is not None:
+        dist.barrier()
+    torch.cuda.synchronize()
+    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with ClockSampler(local) as clk:
+        ev0.record(stream)
+        for _ in range(args.steps):
+            out = cg(dinputs)
+            allreduce()
+        ev1.record(stream)
+        torch.cuda.synchronize()
+    if dist is not None:
+        dist.barrier()
+    ms = ev0.elapsed_time(ev1)
+    t = torch.tensor([ms], device=dev)
+    if dist is not None:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    ms_max = float(t.item())
+    value = world * args.steps / (ms_max / 1000.0)
+
+    # dominant kernel alone, CUDA events on its stream (roofline)
+    roof = None
+    if args.workload == "rowfused":
+        R, C = g.meta["dims"]["R"], g.meta["dims"]["C"]
+        xs = [dinputs[g.roles[k]] for k in ("x", "a", "b", "gamma", "beta", "cotangent")]
+        y = torch.empty(R, C, device=dev)
+        dx = torch.empty(R, C, device=dev)
+        am = torch.empty(R, dtype=torch.int64, device=dev)
+        da, db = torch.empty(C, device=dev), torch.empty(C, device=dev)
+        wsb = int(_lib.lib().b200_rowfused_workspace_bytes(R, C))
+        ws = torch.empty(wsb, dtype=torch.uint8, device=dev)
+        s = ops.stream_ptr()
+
+        def launch():
+            _lib.call("b200_rowfused_fwd_bwd", *[x.data_ptr() for x in xs], y.data_ptr(), am.data_ptr(), dx.data_ptr(),
+                      da.data_ptr(), db.data_ptr(), None, None, R, C, 1e-5, ws.data_ptr(), wsb, s)
+
+        for _ in range(3):
+            launch()
+        torch.cuda.synchronize()
+        evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(max(5, args.steps))]
+        for a, b in evs:
+            a.record(stream)
+            launch()
+            b.record(stream)
+        torch.cuda.synchronize()
+        kms = statistics.mean(a.elapsed_time(b) for a, b in evs)
+        pk = peaks()
+        bytes_ = algorithmic_bytes_rowfused(R, C)
+        ach = bytes_ / (kms / 1000.0) / 1e9
+        roof = {"bound": "hbm", "kernel": "rowfused_fwd_bwd (+colsum)", "achieved": round(ach, 1), "peak": pk["hbm_gbs"],
+                "unit": "GB/s", "frac": round(ach / pk["hbm_gbs"], 4), "peak_source": pk["source"],
+                "algorithmic_bytes": bytes_, "kernel_ms": round(kms, 4), "traffic": args.traffic}
+
+    # end-to-end through the public API with host buffers
+    e2e = None
+    if not args.no_e2e:
+        host = {nid: torch.from_numpy(np.ascontiguousarray(arrays[r])).pin_memory() for r, nid in g.roles.items()}
+        res_ids = [g.output_names[k] for k in g.output_names if k.startswith("d_") and k[2:] in spec["params"]]
+        if "argmax" in g.output_names:
+            res_ids.append(g.output_names["argmax"])
+        if "loss" in g.output_names:
+            res_ids.append(g.output_names["loss"])
+        host_out = {k: torch.empty(out[k].shape, dtype=out[k].dtype).pin_memory() for k in res_ids}
+        h2d = sum(v.numel() * v.element_size() for v in host.values())
+        d2h = sum(v.numel() * v.element_size() for v in host_out.values())
+        fn = B200Backend.compile_graph(g)
+
+        def e2e_step():
+            dv = {k: v.to(dev, non_blocking=True) for k, v in host.items()}
+            o = fn(dv)
+            if dist is not None:
+                for gid in grad_ids:
+                    dist.all_reduce(o[gid])
+            for k in res_ids:
+                host_out[k].copy_(o[k], non_blocking=True)
+
+        for _ in range(max(2, args.warmup)):
+            e2e_step()
+        torch.cuda.synchronize()
+        if dist is not None:
+            dist.barrier()
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record(stream)
+        for _ in range(args.steps):
+            e2e_step()
+        b.record(stream)
+        torch.cuda.synchronize()
+        et = torch.tensor([a.elapsed_time(b)], device=dev)
+        if dist is not None:
+            dist.all_reduce(et, op=dist.ReduceOp.MAX)
+        e2e = {"value": round(world * args.steps / (float(et.item()) / 1000.0), 3), "unit": "steps/s",
+               "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h}
+
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu:
+        cpu = cpu_reference(args.workload)
+
+    if rank == 0:
+        line = {
+            "metric": "fwd+bwd graph steps/sec",
+            "value": round(value, 3),
+            "unit": "steps/s",
+            "n_gpus": world,
+            "steps": args.steps,
+            "warmup": args.warmup,
+            "ms_per_step": round(ms_max / args.steps, 4),
+            "higher_is_better": True,
+            "scaling": "weak",
+            "vs_baseline": None,
+            "dtype": spec["dtype"],
+            "data": "synthetic (seeded numpy, per-rank seed)",
+            "config": {"workload": spec["desc"], "graph": spec["graph"], "dims": g.meta["dims"],
+                       "parallelism": f"dp{world}" if world > 1 else "single",
+                       "l2": "inputs larger than the 126 MB L2 (no flush needed)" if args.workload in ("rowfused", "bmm") else "L2 not flushed",
+                       "replay": "CUDA graph of the fused plan"},
+            "gpu_launches": int(launches_per_step * args.steps),
+            "launches_per_step": launches_per_step,
+            "plan_steps": int(n_capture),
+            "plan": plan.describe(),
+            "clocks": clk.summary(),
+            "roofline": roof,
+            "cpu_baseline": cpu,
+            "e2e": e2e,
+        }
+        print(json.dumps(line), flush=True)
+    cg.cuda_graph = None
+    if dist is not None:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+def run_reference(args) -> None:
+    rank = env_int("RANK", 0)
+    if rank != 0:
+        return
+    spec = WORKLOADS[args.workload]
+    vals = []
+    info = None
+    for _ in range(max(1, args.warmup if args.workload != "rowfused" else 0)):
+        pass
+    for _ in range(max(1, min(args.steps, 3))):
+        info = cpu_reference(args.workload, budget_s=8.0)
+        vals.append(info["value"])
+    v = statistics.median(vals)
+    info["value"] = v
+    line = {"impl": "reference", "metric": "fwd+bwd graph steps/sec", "value": v, "unit": "steps/s",
+            "n_gpus": env_int("WORLD_SIZE", 1), "steps": args.steps, "warmup": args.warmup,
+            "ms_per_step": 1000.0 / v if v else None, "higher_is_better": True, "scaling": "weak",
+            "vs_baseline": None, "dtype": spec["dtype"], "data": "synthetic (seeded numpy)",
+            "config": {"workload": spec["desc"], "graph": spec["graph"]},
+            "cpu_baseline": info, "e2e": {"value": v, "unit": "steps/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+    print(json.dumps(line), flush=True)
+
+
+def main() -> None:
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--workload", default="rowfused", choices=sorted(WORKLOADS))
+    ap.add_argument("--impl", default="b200", choices=["b200", "reference"])
+    ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline leg")
+    ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--traffic", type=float, default=None, help="ncu dram bytes per launch of the dominant kernel")
+    args = ap.parse_args()
+    if args.warmup < 3:
+        args.warmup = 3
+    if args.impl == "reference":
+        run_reference(args)
+    else:
+        run_gpu(args)
+
+
+if __name__ == "__main__":
+    main()

@@ -208,6 +208,27 @@ int b200_conv2d_wgrad(int ab_dtype, const float* x, const float* dy, float* dw, 
                       int64_t W, int64_t O, int64_t KH, int64_t KW, int64_t OH, int64_t OW, int64_t sh, int64_t sw,
                       int64_t pt, int64_t pl, void* stream);
 
+/* ------------------------------------------------------------------------------
+ * Whole-row fused forward + backward (subsystems 1 + 2 in one pass over HBM):
+ *   y = Softmax(LayerNorm(Gelu(x * a + b); gamma, beta, eps)), am = Argmax(y, -1)
+ *   and, for the upstream gradient cot of y, the VJP graph of that chain:
+ *   dx [rows, cols], da = sum_rows(dp * x), db = sum_rows(dp) [cols],
+ *   optional dgamma / dbeta (LayerNormGammaGrad / BetaGrad) [cols].
+ * Replaces the per-node chain Multiply/Add (numpy/eager/math_binary.py:9-51), Gelu
+ * (eager/core_math_ops/math_nn.py:184-199), LayerNorm (numpy/eager/nn_ops.py:219-241),
+ * Softmax (numpy/eager/math_advanced/math_signal.py:450-467), Argmax
+ * (numpy/eager/math_reductions.py:129-140), LayerNormInputGrad/GammaGrad/BetaGrad
+ * (nn_ops.py:244-318) and BroadcastReduce (eager/core_math_ops/math_reduction.py:192-224).
+ * x, cot, y, dx: [rows, cols] fp32 dense; a, b, gamma, beta: [cols] fp32 (gamma/beta may
+ * be NULL = ones/zeros); am (int64 [rows]), dgamma, dbeta may be NULL. cols <= 16384.
+ * `workspace` holds per-CTA column partials (b200_rowfused_workspace_bytes); the column
+ * sums are reduced in a fixed order, so results are deterministic. */
+size_t b200_rowfused_workspace_bytes(int64_t rows, int64_t cols);
+int b200_rowfused_fwd_bwd(const float* x, const float* a, const float* b, const float* gamma, const float* beta,
+                          const float* cot, float* y, int64_t* am, float* dx, float* da, float* db, float* dgamma,
+                          float* dbeta, int64_t rows, int64_t cols, float eps, void* workspace, size_t workspace_bytes,
+                          void* stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -1,17 +1,608 @@
-"""Fusion planner: turns the live nodes of a graph into GPU steps.
+"""Fusion planner: turns the live nodes of a graph into fused GPU steps.
 
-Patterns are matched on the graph structure the reference AD emits (op types, edges,
-attributes) and replaced by one fused kernel step each; every node not covered by a
-pattern becomes a per-op step (``executor.node_step``).
+Planning uses the exact shape and dtype of every value, recorded from one unfused
+execution of the graph on the same input signature (``record_meta``). Then:
+
+1. pattern fusions: subgraphs matched structurally (op types, edges, attributes,
+   constants; Add/Multiply commutative) are replaced by one hand-written kernel each
+   (``PATTERNS``). A match is accepted only if every replaced node is live, no replaced
+   intermediate is needed outside the match, and the fused kernel's shape rules hold.
+2. elementwise clustering (subsystem 1): maximal convex groups of elementwise nodes over
+   one index space become one elementwise program (one HBM read per input, one write per
+   live output), the b200 counterpart of the FusedElementwise groups of
+   ``transforms/passes/operator_fusion.py:673-715``.
+3. everything else is one per-op step.
+
+Steps are then ordered by a topological sort of the condensed step graph.
 """
 
 from __future__ import annotations
 
-from typing import Any
+import math
+from typing import Any, Callable
 
-from .executor import Step, node_step
+import torch
+
+from . import _lib as L
+from . import ops
+from .executor import ALIASES, Step, node_kwargs, node_step
 from .graph import Graph, Node
 
 
+# ----------------------------------------------------------------------------------
+# value metadata from one unfused run
+# ----------------------------------------------------------------------------------
+class Meta:
+    __slots__ = ("shape", "dtype", "scalar")
+
+    def __init__(self, v: Any) -> None:
+        if isinstance(v, torch.Tensor):
+            self.shape, self.dtype, self.scalar = tuple(v.shape), v.dtype, False
+        else:
+            self.shape, self.dtype, self.scalar = (), None, True
+
+
+def record_meta(graph: Graph, nodes: list[Node], sample: dict[str, Any]) -> dict[str, Meta]:
+    env: dict[str, Any] = dict(graph.initializers)
+    env.update(sample)
+    meta = {k: Meta(v) for k, v in env.items()}
+    consumers: dict[str, int] = {}
+    for n in nodes:
+        for i in n.inputs:
+            consumers[i] = consumers.get(i, 0) + 1
+    for n in nodes:
+        node_step(n).fn(env)
+        meta[n.id] = Meta(env[n.id])
+        for i in n.inputs:
+            consumers[i] -= 1
+            if consumers[i] == 0 and i not in sample and i not in graph.outputs:
+                env.pop(i, None)
+    torch.cuda.synchronize()
+    return meta
+
+
+# ----------------------------------------------------------------------------------
+# structural pattern matcher
+# ----------------------------------------------------------------------------------
+COMMUTATIVE = {"Add", "Multiply"}
+
+
+class Pat:
+    """Base of pattern terms."""
+
+
+class Var(Pat):
+    def __init__(self, name: str) -> None:
+        self.name = name
+
+
+class Const(Pat):
+    def __init__(self, value: float, rtol: float = 1e-6) -> None:
+        self.value, self.rtol = value, rtol
+
+
+class Op(Pat):
+    def __init__(self, op: str, *args: Pat, name: str | None = None, attrs: dict | None = None) -> None:
+        self.op, self.args, self.name, self.attrs = op, args, name, attrs or {}
+
+
+def _op_name(n: Node) -> str:
+    return ALIASES.get(n.op_type, n.op_type)
+
+
+def match(p: Pat, nid: str, g: Graph, bind: dict[str, str], covered: set[str]) -> bool:
+    """Match pattern ``p`` rooted at node ``nid``; extends ``bind`` and ``covered`` on success."""
+    if isinstance(p, Var):
+        if p.name in bind:
+            return bind[p.name] == nid
+        bind[p.name] = nid
+        return True
+    node = g.nodes.get(nid)
+    if node is None:
+        return False
+    if isinstance(p, Const):
+        if node.op_type != "Constant":
+            return False
+        v = node.attributes.get("value")
+        if not isinstance(v, (int, float)):
+            return False
+        if abs(float(v) - p.value) > p.rtol * max(1.0, abs(p.value)):
+            return False
+        covered.add(nid)
+        return True
+    assert isinstance(p, Op)
+    if _op_name(node) != p.op or len(node.inputs) != len(p.args):
+        return False
+    for k, want in p.attrs.items():
+        have = node.attributes.get(k)
+        if callable(want):
+            if not want(have):
+                return False
+        elif have != want:
+            return False
+    if p.name is not None:
+        if p.name in bind and bind[p.name] != nid:
+            return False
+    orders = [list(range(len(p.args)))]
+    if p.op in COMMUTATIVE and len(p.args) == 2:
+        orders.append([1, 0])
+    for order in orders:
+        b2, c2 = dict(bind), set(covered)
+        if all(match(p.args[j], node.inputs[i], g, b2, c2) for i, j in enumerate(order)):
+            if p.name is not None:
+                b2[p.name] = nid
+            c2.add(nid)
+            bind.clear()
+            bind.update(b2)
+            covered.clear()
+            covered.update(c2)
+            return True
+    return False
+
+
+def _last_axis(ax: Any) -> bool:
+    return ax == -1 or ax is None
+
+
+def gelu_tanh_deriv(p: Pat) -> Pat:
+    """d/dp of 0.5 p (1 + tanh(k (p + c p^3))) as the corrected Gelu VJP rule emits it:
+    0.5 (1 + t) + 0.5 p (1 - t^2) k (1 + 3 c p^2)."""
+    k = math.sqrt(2.0 / math.pi)
+    c = 0.044715
+    p2 = Op("Multiply", p, p, name="_gd_p2")
+    p3 = Op("Multiply", p2, p)
+    t = Op("Tanh", Op("Multiply", Op("Add", p, Op("Multiply", p3, Const(c))), Const(k)), name="_gd_t")
+    left = Op("Multiply", Op("Add", t, Const(1.0)), Const(0.5))
+    sech2 = Op("Subtract", Const(1.0), Op("Multiply", t, t))
+    dinner = Op("Multiply", Op("Add", Op("Multiply", p2, Const(3.0 * c)), Const(1.0)), Const(k))
+    right = Op("Multiply", Op("Multiply", Op("Multiply", p, sech2), dinner), Const(0.5))
+    return Op("Add", left, right)
+
+
+# ----------------------------------------------------------------------------------
+# pattern: fused row chain  affine -> gelu -> LayerNorm -> softmax (+argmax) and its VJP
+# ----------------------------------------------------------------------------------
+def _rowfused_pattern():
+    x, a, b, gamma, beta, cot = (Var(n) for n in ("x", "a", "b", "gamma", "beta", "cot"))
+    p = Op("Add", Op("Multiply", x, a), b, name="p")
+    g = Op("Gelu", p, name="g")
+    n = Op("LayerNorm", g, gamma, beta, name="n")
+    y = Op("Softmax", n, name="y", attrs={"axis": _last_axis})
+    s = Op("ReduceSum", Op("Multiply", cot, y), attrs={"axis": _last_axis, "keepdims": True})
+    dn = Op("Multiply", y, Op("Subtract", cot, s), name="dn")
+    dg = Op("LayerNormInputGrad", dn, g, gamma, name="dg")
+    dp = Op("Multiply", dg, gelu_tanh_deriv(p), name="dp")
+    roots = {
+        "dx": Op("Multiply", dp, a, name="dx"),
+        "da": Op("BroadcastReduce", Op("Multiply", dp, x), a, name="da"),
+        "db": Op("BroadcastReduce", dp, b, name="db"),
+    }
+    optional = {
+        "am": Op("Argmax", y, name="am", attrs={"axis": _last_axis}),
+        "dgamma": Op("LayerNormGammaGrad", dn, g, name="dgamma"),
+        "dbeta": Op("LayerNormBetaGrad", dn, name="dbeta"),
+    }
+    return roots, optional
+
+
+class Match:
+    def __init__(self, kind: str, bind: dict[str, str], covered: set[str], outputs: dict[str, str]) -> None:
+        self.kind, self.bind, self.covered, self.outputs = kind, bind, covered, outputs
+
+
+def find_rowfused(g: Graph, live: dict[str, Node], meta: dict[str, Meta], users: dict[str, list[str]]) -> list[Match]:
+    roots, optional = _rowfused_pattern()
+    found = []
+    for nid, node in live.items():
+        if _op_name(node) != "Multiply":
+            continue
+        bind: dict[str, str] = {}
+        cov: set[str] = set()
+        if not match(roots["dx"], nid, g, bind, cov):
+            continue
+        ok = True
+        outs = {"dx": bind["dx"]}
+        for key in ("da", "db"):
+            cand = [u for u in users.get(bind["dp"], []) if u in live] + [
+                u for v in users.get(bind["dp"], []) for u in users.get(v, []) if u in live
+            ]
+            hit = False
+            for c in cand:
+                b2, c2 = dict(bind), set(cov)
+                if match(roots[key], c, g, b2, c2):
+                    bind, cov, hit = b2, c2, True
+                    outs[key] = bind[key]
+                    break
+            ok &= hit
+        if not ok:
+            continue
+        for key, pat in optional.items():
+            anchor = bind["y"] if key == "am" else bind["dn"]
+            for c in users.get(anchor, []):
+                if c not in live:
+                    continue
+                b2, c2 = dict(bind), set(cov)
+                if match(pat, c, g, b2, c2):
+                    bind, cov = b2, c2
+                    outs[key] = bind[key]
+                    break
+        # y is an output of the fused kernel too
+        outs["y"] = bind["y"]
+        # shape rules: x, cot [rows, C] fp32; a, b, gamma, beta [C] fp32
+        mx = meta.get(bind["x"])
+        if mx is None or mx.scalar or len(mx.shape) < 1 or mx.dtype != torch.float32:
+            continue
+        C = mx.shape[-1]
+        good = meta[bind["cot"]].shape == mx.shape and meta[bind["cot"]].dtype == torch.float32
+        for v in ("a", "b", "gamma", "beta"):
+            m = meta.get(bind[v])
+            good &= m is not None and not m.scalar and m.shape == (C,) and m.dtype == torch.float32
+        good &= C <= 16384 and meta[bind["y"]].shape == mx.shape
+        if not good:
+            continue
+        cov = {c for c in cov if c in live}
+        found.append(Match("rowfused", bind, cov, outs))
+    return found
+
+
+def rowfused_step(m: Match, meta: dict[str, Meta], eps: float) -> Step:
+    b, o = m.bind, m.outputs
+    shape = meta[b["x"]].shape
+    C = shape[-1]
+    R = math.prod(shape[:-1])
+    ins = [b[k] for k in ("x", "a", "b", "gamma", "beta", "cot")]
+    lib_ws = L.lib().b200_rowfused_workspace_bytes
+    ws_bytes = int(lib_ws(R, C))
+
+    def run(env: dict) -> None:
+        x, a, bb, ga, be, cot = (ops.contiguous(env[k]) for k in ins)
+        dev = ops.device()
+        y = torch.empty(shape, dtype=torch.float32, device=dev)
+        dx = torch.empty(shape, dtype=torch.float32, device=dev)
+        da = torch.empty(C, dtype=torch.float32, device=dev)
+        db = torch.empty(C, dtype=torch.float32, device=dev)
+        am = torch.empty(shape[:-1], dtype=torch.int64, device=dev) if "am" in o else None
+        dgam = torch.empty(C, dtype=torch.float32, device=dev) if "dgamma" in o else None
+        dbet = torch.empty(C, dtype=torch.float32, device=dev) if "dbeta" in o else None
+        ws = torch.empty(max(1, ws_bytes), dtype=torch.uint8, device=dev)
+        L.call("b200_rowfused_fwd_bwd", x.data_ptr(), a.data_ptr(), bb.data_ptr(), ga.data_ptr(), be.data_ptr(),
+               cot.data_ptr(), y.data_ptr(), None if am is None else am.data_ptr(), dx.data_ptr(), da.data_ptr(),
+               db.data_ptr(), None if dgam is None else dgam.data_ptr(), None if dbet is None else dbet.data_ptr(),
+               R, C, float(eps), ws.data_ptr(), ws_bytes, ops.stream_ptr())
+        env[o["y"]] = y
+        env[o["dx"]] = dx
+        env[o["da"]] = da
+        env[o["db"]] = db
+        if am is not None:
+            env[o["am"]] = am
+        if dgam is not None:
+            env[o["dgamma"]] = dgam
+        if dbet is not None:
+            env[o["dbeta"]] = dbet
+
+    return Step(list(o.values()), ins, run, "rowfused_fwd_bwd")
+
+
+# ----------------------------------------------------------------------------------
+# pattern: GEMM with fused bias + activation epilogue (+ ReLU-grad mask)
+#   act(Matmul(A, B) + bias), bias a [N] vector; the backward's Greater(pre, 0) mask is
+#   written by the same epilogue (one byte per element) instead of re-reading pre.
+# ----------------------------------------------------------------------------------
+def find_gemm_epilogue(g: Graph, live: dict[str, Node], meta: dict[str, Meta], users: dict[str, list[str]],
+                       outputs: set[str]) -> list[Match]:
+    found = []
+    for nid, node in live.items():
+        op = _op_name(node)
+        if op not in ("Relu", "Gelu", "GELU"):
+            continue
+        bind: dict[str, str] = {}
+        cov: set[str] = set()
+        pat = Op(op, Op("Add", Op("Matmul", Var("A"), Var("B"), name="mm"), Var("bias"), name="pre"), name="act")
+        if not match(pat, nid, g, bind, cov):
+            continue
+        mm = g.nodes[bind["mm"]]
+        if mm.attributes.get("transpose_a") or mm.attributes.get("transpose_b"):
+            continue
+        N = meta[bind["mm"]].shape[-1] if not meta[bind["mm"]].scalar else 0
+        mb = meta.get(bind["bias"])
+        if mb is None or mb.scalar or mb.shape != (N,):
+            continue
+        outs = {"act": bind["act"]}
+        # the ReLU-grad mask: Greater(pre, 0)
+        if op == "Relu":
+            for u in users.get(bind["pre"], []):
+                un = live.get(u)
+                if un is not None and _op_name(un) == "Greater" and un.inputs[0] == bind["pre"] and _const_value(g, un.inputs[1]) == 0.0:
+                    outs["mask"] = u
+                    cov.add(u)
+                    cov.add(un.inputs[1])
+        # mm and pre must not be needed elsewhere
+        inner = [bind["mm"], bind["pre"]]
+        if any(v in outputs or any(u not in cov for u in users.get(v, [])) for v in inner):
+            continue
+        if op != "Relu" and "mask" in outs:
+            continue
+        found.append(Match("gemm_" + op.lower(), bind, {c for c in cov if c in live or g.nodes[c].op_type == "Constant"}, outs))
+    return found
+
+
+def gemm_epilogue_step(m: Match) -> Step:
+    b, o = m.bind, m.outputs
+    epi = L.EPI_RELU if m.kind == "gemm_relu" else L.EPI_GELU
+    want_mask = "mask" in o
+    ins = [b["A"], b["B"], b["bias"]]
+
+    def run(env: dict) -> None:
+        res = ops.gemm(env[b["A"]], env[b["B"]], bias=env[b["bias"]], epilogue=epi, want_mask=want_mask)
+        if want_mask:
+            env[o["act"]], env[o["mask"]] = res
+        else:
+            env[o["act"]] = res
+
+    return Step(list(o.values()), ins, run, m.kind)
+
+
+# ----------------------------------------------------------------------------------
+# elementwise clustering (subsystem 1)
+# ----------------------------------------------------------------------------------
+EW_UNARY = {"Negative": "NEG", "Exp": "EXP", "Log": "LOG", "Tanh": "TANH", "Sqrt": "SQRT", "Relu": "RELU", "Gelu": "GELU",
+            "GELU": "GELU", "Abs": "ABS", "Sigmoid": "SIGMOID", "Erf": "ERF"}
+EW_BINARY = {"Add": "ADD", "Subtract": "SUB", "Multiply": "MUL", "TrueDivide": "DIV", "Power": "POW", "Maximum": "MAX",
+             "Minimum": "MIN", "Greater": "GT", "GreaterEqual": "GE", "Less": "LT", "Equal": "EQ"}
+EW_BOOL_OUT = {"Greater", "GreaterEqual", "Less", "Equal"}
+
+
+def _is_ew(n: Node) -> bool:
+    op = _op_name(n)
+    return op in EW_UNARY or op in EW_BINARY or op == "Where"
+
+
+def _const_value(g: Graph, nid: str) -> float | None:
+    n = g.nodes.get(nid)
+    if n is not None and n.op_type == "Constant" and isinstance(n.attributes.get("value"), (int, float)):
+        return float(n.attributes["value"])
+    return None
+
+
+def cluster_elementwise(g: Graph, order: list[Node], meta: dict[str, Meta], taken: set[str],
+                        users: dict[str, list[str]], outputs: set[str]) -> list[list[Node]]:
+    """Greedy convex clusters of elementwise nodes that share one output shape."""
+    clusters: list[list[Node]] = []
+    cid: dict[str, int] = {}
+    # anc[c] = set of cluster ids this cluster transitively depends on through non-members
+    for n in order:
+        if n.id in taken or not _is_ew(n):
+            continue
+        m = meta.get(n.id)
+        if m is None or m.scalar or m.dtype not in (torch.float32, torch.bool):
+            continue
+        # candidate clusters: those of elementwise producers with the same shape
+        cands = []
+        for i in n.inputs:
+            c = cid.get(i)
+            if c is not None and meta[clusters[c][-1].id].shape == m.shape and c not in cands:
+                cands.append(c)
+        placed = False
+        for c in cands:
+            members = {x.id for x in clusters[c]}
+            # convexity: no input of n may depend on the cluster through a non-member
+            if any(_depends_via_outside(g, i, members, taken_meta=meta) for i in n.inputs if i not in members):
+                continue
+            trial = clusters[c] + [n]
+            if _fits(g, trial, meta, users, outputs):
+                clusters[c].append(n)
+                cid[n.id] = c
+                placed = True
+                break
+        if not placed:
+            clusters.append([n])
+            cid[n.id] = len(clusters) - 1
+    return clusters
+
+
+def _depends_via_outside(g: Graph, start: str, members: set[str], taken_meta: dict, limit: int = 4096) -> bool:
+    """Does value ``start`` (not a member) depend on any member of ``members``?"""
+    stack, seen = [start], set()
+    while stack and len(seen) < limit:
+        v = stack.pop()
+        if v in seen:
+            continue
+        seen.add(v)
+        node = g.nodes.get(v)
+        if node is None:
+            continue
+        for i in node.inputs:
+            if i in members:
+                return True
+            stack.append(i)
+    return False
+
+
+def _cluster_io(g: Graph, nodes: list[Node], users: dict[str, list[str]], outputs: set[str]):
+    ids = {n.id for n in nodes}
+    ext_in: list[str] = []
+    for n in nodes:
+        for i in n.inputs:
+            if i not in ids and _const_value(g, i) is None and i not in ext_in:
+                ext_in.append(i)
+    outs = [n.id for n in nodes if n.id in outputs or any(u not in ids for u in users.get(n.id, []))]
+    return ext_in, outs
+
+
+def _fits(g: Graph, nodes: list[Node], meta: dict[str, Meta], users, outputs) -> bool:
+    ext_in, outs = _cluster_io(g, nodes, users, outputs)
+    if len(ext_in) > L.EW_MAX_IN or len(outs) > L.EW_MAX_OUT:
+        return False
+    n_ins = len(ext_in) + sum(1 + sum(1 for i in n.inputs if _const_value(g, i) is not None) for n in nodes) + len(outs)
+    if n_ins > L.EW_MAX_INS:
+        return False
+    return _alloc_registers(g, nodes, ext_in, outs) is not None
+
+
+def _alloc_registers(g: Graph, nodes: list[Node], ext_in: list[str], outs: list[str]):
+    """Linear-scan register allocation of the program; None if it needs > 16 registers."""
+    ids = [n.id for n in nodes]
+    last_use: dict[str, int] = {}
+    for k, n in enumerate(nodes):
+        for i in n.inputs:
+            last_use[i] = k
+    for o in outs:
+        last_use[o] = len(nodes)
+    free = list(range(L.EW_MAX_REG))
+    reg: dict[str, int] = {}
+    prog: list[tuple] = []
+
+    def get(v: str, k: int):
+        if v in reg:
+            return reg[v]
+        cv = _const_value(g, v)
+        if not free:
+            return None
+        r = free.pop(0)
+        if cv is not None:
+            prog.append(("IMM", r, 0, 0, 0, cv))
+            # constants are re-materialised per use; release right away after this node
+            return ("tmp", r)
+        prog.append(("LOAD", r, ext_in.index(v), 0, 0, 0.0))
+        reg[v] = r
+        return r
+
+    for k, n in enumerate(nodes):
+        srcs = []
+        tmps = []
+        for i in n.inputs:
+            r = get(i, k)
+            if r is None:
+                return None
+            if isinstance(r, tuple):
+                tmps.append(r[1])
+                r = r[1]
+            srcs.append(r)
+        # release inputs whose last use is this node (and temporaries)
+        for i in set(n.inputs):
+            if i in reg and last_use.get(i, -1) <= k and i not in outs:
+                free.insert(0, reg.pop(i))
+        for t in tmps:
+            free.insert(0, t)
+        if not free:
+            return None
+        d = free.pop(0)
+        reg[n.id] = d
+        op = _op_name(n)
+        if op in EW_UNARY:
+            prog.append((EW_UNARY[op], d, srcs[0], 0, 0, 0.0))
+        elif op in EW_BINARY:
+            prog.append((EW_BINARY[op], d, srcs[0], srcs[1], 0, 0.0))
+        else:  # Where
+            prog.append(("WHERE", d, srcs[0], srcs[1], srcs[2], 0.0))
+        if last_use.get(n.id, -1) <= k and n.id not in outs:
+            free.insert(0, reg.pop(n.id))
+    return prog, {o: reg[o] for o in outs}
+
+
+def ew_cluster_step(g: Graph, nodes: list[Node], meta: dict[str, Meta], users, outputs) -> Step:
+    ext_in, outs = _cluster_io(g, nodes, users, outputs)
+    prog, out_reg = _alloc_registers(g, nodes, ext_in, outs)
+    shape = meta[nodes[-1].id].shape
+    out_dtypes = [meta[o].dtype for o in outs]
+    ops_seq = [(L.EW[name], d, a, b, c, imm) for (name, d, a, b, c, imm) in prog]
+    label = "ew[" + ",".join(_op_name(n) for n in nodes) + "]"
+
+    def run(env: dict) -> None:
+        p = ops.Prog()
+        vals = []
+        for v in ext_in:
+            x = env[v]
+            if not isinstance(x, torch.Tensor):
+                x = ops.full((), float(x))
+            vals.append(x)
+        p.inputs = vals
+        p.ins = list(ops_seq)
+        p.nreg = L.EW_MAX_REG
+        res = p.run([(out_reg[o], dt) for o, dt in zip(outs, out_dtypes)], shape)
+        for o, r in zip(outs, res):
+            env[o] = r
+
+    return Step(outs, list(ext_in), run, label)
+
+
+# ----------------------------------------------------------------------------------
+# planning
+# ----------------------------------------------------------------------------------
 def plan_steps(graph: Graph, nodes: list[Node], sample: dict[str, Any]) -> list[Step]:
-    return [node_step(n) for n in nodes]
+    meta = record_meta(graph, nodes, sample)
+    live = {n.id: n for n in nodes}
+    users: dict[str, list[str]] = {}
+    for n in nodes:
+        for i in n.inputs:
+            users.setdefault(i, []).append(n.id)
+    outputs = set(graph.outputs)
+    taken: set[str] = set()
+    groups: list[tuple[list[str], Step]] = []
+
+    # 1. patterns
+    for m in find_rowfused(graph, live, meta, users):
+        if m.covered & taken:
+            continue
+        produced = set(m.outputs.values())
+        leak = [c for c in m.covered if c not in produced and (c in outputs or any(u not in m.covered for u in users.get(c, [])))]
+        if leak:
+            continue
+        eps = float(graph.nodes[m.bind["n"]].attributes.get("eps", graph.nodes[m.bind["n"]].attributes.get("epsilon", 1e-5)))
+        groups.append((sorted(m.covered), rowfused_step(m, meta, eps)))
+        taken |= m.covered
+
+    for m in find_gemm_epilogue(graph, live, meta, users, outputs):
+        if m.covered & taken:
+            continue
+        groups.append((sorted(m.covered), gemm_epilogue_step(m)))
+        taken |= m.covered
+
+    # 2. elementwise clusters
+    rest = [n for n in nodes if n.id not in taken]
+    for cl in cluster_elementwise(graph, rest, meta, taken, users, outputs):
+        if len(cl) == 1:
+            continue
+        groups.append(([n.id for n in cl], ew_cluster_step(graph, cl, meta, users, outputs)))
+        taken |= {n.id for n in cl}
+
+    # constants feeding only fused steps are folded into the programs
+    # 3. the rest, one step per node
+    for n in nodes:
+        if n.id not in taken:
+            if n.op_type == "Constant" and all(u in taken for u in users.get(n.id, [])) and n.id not in outputs:
+                continue
+            groups.append(([n.id], node_step(n)))
+    return _schedule(groups)
+
+
+def _schedule(groups: list[tuple[list[str], Step]]) -> list[Step]:
+    """Topological order of the condensed step graph."""
+    owner: dict[str, int] = {}
+    for k, (members, st) in enumerate(groups):
+        for v in members:
+            owner[v] = k
+        for v in st.outputs:
+            owner[v] = k
+    deps = []
+    for k, (_, st) in enumerate(groups):
+        deps.append({owner[i] for i in st.inputs if i in owner and owner[i] != k})
+    order, state = [], [0] * len(groups)
+    for root in range(len(groups)):
+        if state[root]:
+            continue
+        stack = [(root, iter(sorted(deps[root])))]
+        state[root] = 1
+        while stack:
+            k, it = stack[-1]
+            nxt = next(it, None)
+            if nxt is None:
+                stack.pop()
+                state[k] = 2
+                order.append(groups[k][1])
+            elif state[nxt] == 0:
+                state[nxt] = 1
+                stack.append((nxt, iter(sorted(deps[nxt]))))
+            elif state[nxt] == 1:
+                raise RuntimeError("fusion produced a cyclic step graph")
+    return order

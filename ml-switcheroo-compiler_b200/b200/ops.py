@@ -652,7 +652,7 @@ def _gemm_operand(t: torch.Tensor, ab: torch.dtype) -> torch.Tensor:
     cm = contiguous(t.transpose(-1, -2)).transpose(-1, -2)
     if _tc_ok(cm):
         return cm
-    raise UnimplementedMathError(f"bf16 GEMM operand {tuple(t.shape)}: neither layout has 16-byte aligned rows")
+    return None  # no TMA-legal layout (e.g. N = 10): caller uses the CUDA-core kernel
 
 
 def gemm(a: torch.Tensor, b: torch.Tensor, *, bias: torch.Tensor | None = None, epilogue: int = L.EPI_NONE,
@@ -680,7 +680,12 @@ def gemm(a: torch.Tensor, b: torch.Tensor, *, bias: torch.Tensor | None = None, 
         res = (ys, y[1].view(*a.shape[:-1], N)) if want_mask else ys
         return res
     A = _gemm_operand(a, ab_dtype)
-    B = _gemm_operand(b, ab_dtype)
+    B = _gemm_operand(b, ab_dtype) if A is not None else None
+    if A is None or B is None:
+        # TMA needs 16-byte aligned rows; tiny/odd GEMMs (e.g. a 128 -> 10 classifier) run
+        # on the CUDA-core kernel in fp32, which is at least as precise as bf16 math
+        ab_dtype = torch.float32
+        A, B = cast(a, torch.float32), cast(b, torch.float32)
 
     def batch_stride(t: torch.Tensor) -> int:
         if t.dim() == 2:

@@ -378,19 +378,34 @@ OPS: dict[str, Any] = {
 }
 
 
+CONTRACTIONS = ("Matmul", "BatchMatMul", "Conv2D", "Conv2DInputGrad", "Conv2DWeightGrad")
+
+
+def bf16_round(a):
+    """Round to the nearest bfloat16 (ties to even), returned as float32."""
+    u = np.ascontiguousarray(np.asarray(a, dtype=np.float32)).view(np.uint32)
+    r = ((u + 0x7FFF + ((u >> 16) & 1)) & 0xFFFF0000).astype(np.uint32)
+    return r.view(np.float32)
+
+
 class UnimplementedOp(KeyError):
     """No restatement for this op (the reference raises UnimplementedMathError)."""
 
 
-def execute_op(op: str, *args, **kwargs):
+def execute_op(op: str, *args, contraction_rounding: str | None = None, **kwargs):
+    """One op. ``contraction_rounding="bf16"`` rounds both operands of a contraction
+    (Matmul / Conv2D and its VJPs) to bfloat16 first: the reference algorithm under the
+    bf16-math policy of the bf16 workloads (fp32 accumulation, fp32 everything else)."""
     target = _ALIASES.get(op, op)
     fn = OPS.get(target)
     if fn is None:
         raise UnimplementedOp(target)
+    if contraction_rounding == "bf16" and target in CONTRACTIONS:
+        args = (bf16_round(args[0]), bf16_round(args[1])) + tuple(args[2:])
     return fn(*args, **kwargs)
 
 
-def evaluate(graph: dict, inputs: dict[str, np.ndarray]) -> dict[str, Any]:
+def evaluate(graph: dict, inputs: dict[str, np.ndarray], contraction_rounding: str | None = None) -> dict[str, Any]:
     """``evaluate_graph`` (evaluator.py:272-305): every node, in dependency order."""
     env: dict[str, Any] = dict(inputs)
     for node in topo_order(graph):
@@ -408,7 +423,7 @@ def evaluate(graph: dict, inputs: dict[str, np.ndarray]) -> dict[str, Any]:
             env[nid] = np.array(node["attributes"]["value"], dtype=node.get("const_dtype"))
         else:
             target = _ALIASES.get(op, op)
-            env[nid] = execute_op(target, *vals, **_kwargs(node, target))
+            env[nid] = execute_op(target, *vals, contraction_rounding=contraction_rounding, **_kwargs(node, target))
     out = {}
     for oid in graph["outputs"]:
         if oid not in env:
@@ -417,8 +432,8 @@ def evaluate(graph: dict, inputs: dict[str, np.ndarray]) -> dict[str, Any]:
     return out
 
 
-def evaluate_roles(graph: dict, role_inputs: dict[str, np.ndarray]) -> dict[str, Any]:
+def evaluate_roles(graph: dict, role_inputs: dict[str, np.ndarray], contraction_rounding: str | None = None) -> dict[str, Any]:
     """Evaluate with inputs keyed by workload role; outputs keyed by output name."""
     inputs = {nid: role_inputs[r] for r, nid in graph["roles"].items()}
-    res = evaluate(graph, inputs)
+    res = evaluate(graph, inputs, contraction_rounding=contraction_rounding)
     return {name: res[nid] for name, nid in graph["output_names"].items()}

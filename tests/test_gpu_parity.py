@@ -1,17 +1,24 @@
 """Whole-graph parity: every golden case (fwd+bwd graph traced and differentiated by the
 reference, evaluated by the reference numpy backend) run on the b200 backend.
 
-Tolerances (written per workload): fp32 workloads rtol 1e-4 of each output's max
-magnitude; bf16-math workloads rtol 2e-2; integer outputs (argmax) bit-exact.
+Tolerances (written per workload):
+* fp32 workloads (mlp, rowfused): rtol 1e-4 of each output's max magnitude against the
+  reference golden vectors; integer outputs (argmax) bit-exact.
+* bf16-math workloads (bmm, cnn, transformer): rtol 2e-2 of max magnitude against the
+  oracle evaluated under the same bf16 operand-rounding policy (contraction operands
+  rounded to bf16, fp32 accumulation); against the pure-fp32 reference golden the
+  norm-wise relative error must stay within 0.1 (bf16 rounding alone gives up to 0.057
+  on the cancellation-heavy first-conv weight gradient at batch 4).
 """
 
 import numpy as np
 import pytest
 
-from gpu_helpers import assert_close, run_case
+from gpu_helpers import assert_close, run_case, to_np
 
 CASES = ["mlp_small", "mlp_ragged", "rowfused_small", "rowfused_ragged", "bmm_small", "cnn_small", "transformer_small"]
 RTOL = {"mlp": 1e-4, "rowfused": 1e-4, "bmm": 2e-2, "cnn": 2e-2, "transformer": 2e-2}
+BF16 = {"bmm", "cnn", "transformer"}
 
 
 @pytest.mark.gpu
@@ -28,4 +35,17 @@ def test_graph_parity(cuda, case, mode):
             np.testing.assert_array_equal(am, np.argmax(y, axis=-1))
             np.testing.assert_array_equal(am, r)
             continue
+        if g.meta["workload"] in BF16:
+            continue
         assert_close(f"{case}:{name}", got[name], r, rtol)
+    if g.meta["workload"] in BF16:
+        from conftest import load_golden
+        from oracle import evaluator as O
+
+        ins, _ = load_golden(case)
+        emu = O.evaluate_roles(O.load_graph(case), ins, contraction_rounding="bf16")
+        for name, r in ref.items():
+            assert_close(f"{case}:{name}(bf16 policy)", got[name], np.asarray(emu[name], dtype=np.float32), rtol)
+            v = to_np(got[name]).astype(np.float64)
+            nrel = np.linalg.norm(v - r) / max(np.linalg.norm(r), 1e-30)
+            assert nrel <= 0.1, (name, nrel)
