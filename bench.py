@@ -50,6 +50,7 @@ WORKLOADS = {
         "graph": "bmm_full",
         "dtype": "bf16",
         "params": ["bias"],
+        "bf16_inputs": ["A", "B"],
         "reduce": "sum",
         "desc": "batched contraction A,B[16,2048,2048] bf16: relu(A@B+bias) fwd+bwd (dA, dB, dbias)",
     },
@@ -230,7 +231,11 @@ def run_gpu(args) -> None:
     grad_ids = [g.output_names["d_" + r] for r in spec["params"]]
 
     dev = torch.device("cuda", local)
+    # bf16 workloads feed their bf16 operands as bf16 tensors (the values are bf16-exact)
+    bf16_roles = set(spec.get("bf16_inputs", []))
     dinputs = {nid: torch.from_numpy(np.ascontiguousarray(arrays[r])).to(dev) for r, nid in g.roles.items()}
+    for r in bf16_roles:
+        dinputs[g.roles[r]] = dinputs[g.roles[r]].to(torch.bfloat16)
     cg = CompiledGraph(g)
     out = cg(dinputs)  # plan + capture
     torch.cuda.synchronize()
@@ -308,7 +313,10 @@ def run_gpu(args) -> None:
     # end-to-end through the public API with host buffers
     e2e = None
     if not args.no_e2e:
-        host = {nid: torch.from_numpy(np.ascontiguousarray(arrays[r])).pin_memory() for r, nid in g.roles.items()}
+        host = {nid: torch.from_numpy(np.ascontiguousarray(arrays[r])) for r, nid in g.roles.items()}
+        for r in bf16_roles:
+            host[g.roles[r]] = host[g.roles[r]].to(torch.bfloat16)
+        host = {k: v.pin_memory() for k, v in host.items()}
         res_ids = [g.output_names[k] for k in g.output_names if k.startswith("d_") and k[2:] in spec["params"]]
         if "argmax" in g.output_names:
             res_ids.append(g.output_names["argmax"])
@@ -383,6 +391,46 @@ def run_gpu(args) -> None:
         dist.destroy_process_group()
 
 
+def run_gemm_micro(args) -> None:
+    """Dominant-kernel microbenchmark: the bf16 tcgen05 GEMM in the three operand layouts
+    of the batched-contraction graph (forward NN with bias+ReLU+mask epilogue, dA = G B^T,
+    dB = A^T G), 16 x 2048^3 each, CUDA events on the launching stream."""
+    import torch
+
+    from b200 import _lib
+    from b200 import ops
+
+    torch.cuda.set_device(0)
+    Z, M, N, K = 16, 2048, 2048, 2048
+    gen = torch.Generator(device="cpu").manual_seed(0)
+    A = (torch.randn(Z, M, K, generator=gen) * 0.02).to(torch.bfloat16).cuda()
+    B = (torch.randn(Z, K, N, generator=gen) * 0.02).to(torch.bfloat16).cuda()
+    G = torch.randn(Z, M, N, generator=gen).to(torch.bfloat16).cuda()
+    bias = torch.zeros(N).cuda()
+    cases = {
+        "fwd_nn_bias_relu_mask": lambda: ops.gemm(A, B, bias=bias, epilogue=_lib.EPI_RELU, want_mask=True, ab_dtype=torch.bfloat16),
+        "dA_nt": lambda: ops.gemm(G, B.transpose(-1, -2), ab_dtype=torch.bfloat16),
+        "dB_tn": lambda: ops.gemm(A.transpose(-1, -2), G, ab_dtype=torch.bfloat16),
+    }
+    pk = peaks()
+    res = {}
+    for name, fn in cases.items():
+        for _ in range(args.warmup):
+            fn()
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for _ in range(args.steps):
+            fn()
+        e1.record()
+        torch.cuda.synchronize()
+        ms = e0.elapsed_time(e1) / args.steps
+        tf = 2.0 * Z * M * N * K / (ms / 1000.0) / 1e12
+        res[name] = {"ms": round(ms, 4), "tflops": round(tf, 1), "frac": round(tf / pk["bf16_tflops"], 4)}
+    print(json.dumps({"microbench": "gemm_bf16_tcgen05", "shape": [Z, M, N, K], "peak_tflops": pk["bf16_tflops"],
+                      "peak_source": pk["source"], "cases": res}), flush=True)
+
+
 def run_reference(args) -> None:
     rank = env_int("RANK", 0)
     if rank != 0:
@@ -411,7 +459,7 @@ def main() -> None:
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=20)
     ap.add_argument("--warmup", type=int, default=5)
-    ap.add_argument("--workload", default="rowfused", choices=sorted(WORKLOADS))
+    ap.add_argument("--workload", default="rowfused", choices=sorted(WORKLOADS) + ["gemm"])
     ap.add_argument("--impl", default="b200", choices=["b200", "reference"])
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline leg")
     ap.add_argument("--no-e2e", action="store_true")
@@ -419,7 +467,9 @@ def main() -> None:
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3
-    if args.impl == "reference":
+    if args.workload == "gemm":
+        run_gemm_micro(args)
+    elif args.impl == "reference":
         run_reference(args)
     else:
         run_gpu(args)

@@ -131,10 +131,14 @@ class Plan:
         for i in self.input_ids:
             if i not in env:
                 raise ValueError(f"Missing input value for node '{i}'")  # environment.py:33-48
-        for st, dead in zip(self.steps, self.free_after):
-            st.fn(env)
-            for v in dead:
-                env.pop(v, None)
+        ops.clear_cast_cache()
+        try:
+            for st, dead in zip(self.steps, self.free_after):
+                st.fn(env)
+                for v in dead:
+                    env.pop(v, None)
+        finally:
+            ops.clear_cast_cache()
         res = {}
         for oid in self.graph.outputs:
             if oid not in env:

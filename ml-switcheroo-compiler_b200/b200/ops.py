@@ -634,6 +634,35 @@ def op_tensor_scatter_add(tensor, indices, updates, **_):  # numpy/eager/math_sc
 # ----------------------------------------------------------------------------------
 
 
+# bf16 copies of fp32 GEMM operands made during one plan run, keyed by the source
+# storage: two GEMMs reading the same value (e.g. dA and dB both read the masked
+# cotangent) share one cast. Cleared by the executor at the start and end of each run.
+_CAST_CACHE: dict = {}
+
+
+def clear_cast_cache() -> None:
+    _CAST_CACHE.clear()
+
+
+def cast_operand(t: torch.Tensor, dtype: torch.dtype) -> torch.Tensor:
+    """Layout-preserving cast: a strided view of a dense tensor is cast in storage order
+    (coalesced) and re-viewed, never materialised through the strided path."""
+    if t.dtype == dtype:
+        return t
+    base = t._base if t._base is not None else t
+    if not base.is_contiguous():
+        return cast(t, dtype)
+    key = (base.data_ptr(), base.numel(), base.dtype, dtype)
+    hit = _CAST_CACHE.get(key)
+    if hit is not None and hit[0] is base:
+        cb = hit[1]
+    else:
+        cb = cast(base, dtype)
+        # the entry keeps `base` alive, so its storage cannot be recycled under the key
+        _CAST_CACHE[key] = (base, cb)
+    return cb.as_strided(t.size(), t.stride(), t.storage_offset() - base.storage_offset())
+
+
 def _tc_ok(t: torch.Tensor) -> bool:
     st = t.stride()
     return t.data_ptr() % 16 == 0 and (
@@ -642,7 +671,7 @@ def _tc_ok(t: torch.Tensor) -> bool:
 
 
 def _gemm_operand(t: torch.Tensor, ab: torch.dtype) -> torch.Tensor:
-    t = cast(t, ab)
+    t = cast_operand(t, ab)
     if ab != torch.bfloat16 or _tc_ok(t):
         return t
     # tcgen05 path needs one unit stride and 16-byte aligned rows: try both dense layouts

@@ -261,8 +261,18 @@ __global__ void __launch_bounds__(THREADS, 1) gemm_tc_kernel(const __grid_consta
         }
         if (args.aux) {
           uint8_t* mdst = args.aux + off;
-          for (int i = 0; i < 32; ++i)
-            if (cbase + i < args.N) mdst[i] = mask[i];
+          if (full && ((reinterpret_cast<uintptr_t>(mdst) & 15) == 0)) {
+            uint32_t wv[8];
+#pragma unroll
+            for (int q4 = 0; q4 < 8; ++q4)
+              wv[q4] = (uint32_t)mask[4 * q4] | ((uint32_t)mask[4 * q4 + 1] << 8) | ((uint32_t)mask[4 * q4 + 2] << 16) |
+                       ((uint32_t)mask[4 * q4 + 3] << 24);
+            reinterpret_cast<uint4*>(mdst)[0] = make_uint4(wv[0], wv[1], wv[2], wv[3]);
+            reinterpret_cast<uint4*>(mdst)[1] = make_uint4(wv[4], wv[5], wv[6], wv[7]);
+          } else {
+            for (int i = 0; i < 32; ++i)
+              if (cbase + i < args.N) mdst[i] = mask[i];
+          }
         }
       }
     }

@@ -180,58 +180,119 @@ __device__ __forceinline__ void ldg_pairs(F2 (&r)[V / 2], const float* __restric
   }
 }
 
+// cp.async (Ampere-style, per thread) into this thread's own shared-memory slot; the
+// issuing thread is also the only reader, so completion needs no block barrier.
+__device__ __forceinline__ void cp_async16(void* sdst, const void* gsrc) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"((uint32_t)__cvta_generic_to_shared(sdst)), "l"(gsrc) : "memory");
+}
+__device__ __forceinline__ void cp_async4(void* sdst, const void* gsrc, bool valid) {
+  // src-size 0 zero-fills the destination without reading global memory
+  asm volatile("cp.async.ca.shared.global [%0], [%1], 4, %2;" ::"r"((uint32_t)__cvta_generic_to_shared(sdst)), "l"(gsrc),
+               "r"(valid ? 4 : 0)
+               : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+template <int N>
+__device__ __forceinline__ void cp_async_wait() { asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory"); }
+
 // T threads, V consecutive columns per thread (cols <= T*V), V/2 packed pairs.
-// Registers hold x, c, one working row array w and the forward tanh t; a, b, gamma,
-// beta are re-read through L1; the da/db (and dgamma/dbeta) column accumulators of
-// this CTA live in shared memory, one slot per column, owned by one thread (no atomics).
+// Registers hold this thread's slice of the column vectors (a, b, gamma, beta, loaded
+// once per CTA), the forward tanh t, one working row array w and the column
+// accumulators. x and c of the current and the next row sit in this thread's own
+// shared-memory slot, prefetched with cp.async one row ahead (double-buffered).
 template <int T, int V, bool GB, bool RAGGED>
-__global__ void __launch_bounds__(T, T <= 256 ? 2 : 1) rowfused_kernel(const __grid_constant__ Params P) {
+__global__ void __launch_bounds__(T, T <= 512 ? 1024 / T : 1) rowfused_kernel(const __grid_constant__ Params P) {
   constexpr int NW = T / 32;
   constexpr int H = V / 2;
   __shared__ float sh[64];
   __shared__ int shi[32];
-  extern __shared__ float acc[];  // [2 or 4][cols]
+  extern __shared__ __align__(16) float sm[];  // [2 stages][T][2V]: x then c
   const int64_t C = P.cols;
   const int c0 = threadIdx.x * V;
-  const bool vec = (c0 + V <= C) && ((C & 3) == 0);
+  const bool full = c0 + V <= C;
+  const bool vec = full && ((C & 3) == 0);
   const bool any = c0 < C;
-  const int nacc = GB ? 4 : 2;
-  for (int64_t i = threadIdx.x; i < nacc * C; i += T) acc[i] = 0.f;
-  // valid-column mask of pair i (only rows that do not tile exactly need it)
-  auto msk = [&](int i) -> F2 {
-    return RAGGED ? pk(c0 + 2 * i < C ? 1.f : 0.f, c0 + 2 * i + 1 < C ? 1.f : 0.f) : sp(1.f);
-  };
+  auto msk = [&](int i) -> F2 { return RAGGED ? pk(c0 + 2 * i < C ? 1.f : 0.f, c0 + 2 * i + 1 < C ? 1.f : 0.f) : sp(1.f); };
   auto mul_mask = [&](F2 v, int i) -> F2 { return RAGGED ? mul2(v, msk(i)) : v; };
   const float invC = 1.f / (float)C;
-  const float KG2L = 2.f * K_GELU * LOG2E;  // 2 k log2(e)
+  const float KG2L = 2.f * K_GELU * LOG2E;
+  const int64_t G = gridDim.x;
 
-  for (int64_t row = blockIdx.x; row < P.rows; row += gridDim.x) {
-    const float* xr = P.x + row * C;
-    const float* cr = P.c + row * C;
-    F2 x[H], c[H], w[H], t[H];
+  F2 a[H], b[H], ga[H], be[H];
+  ldg_pairs<V>(a, P.a, c0, C, vec, 0.f);
+  ldg_pairs<V>(b, P.b, c0, C, vec, 0.f);
+  ldg_pairs<V>(ga, P.gamma, c0, C, vec, 1.f);
+  ldg_pairs<V>(be, P.beta, c0, C, vec, 0.f);
+  F2 acc_da[H], acc_db[H], acc_dg[GB ? H : 1], acc_dbe[GB ? H : 1];
+#pragma unroll
+  for (int i = 0; i < H; ++i) {
+    acc_da[i] = acc_db[i] = sp(0.f);
+    if (GB) acc_dg[i] = acc_dbe[i] = sp(0.f);
+  }
+
+  auto prefetch = [&](int64_t row, int stage) {
+    if (row < P.rows) {
+      float* dst = sm + ((size_t)stage * T + threadIdx.x) * 2 * V;
+      const float* xr = P.x + row * C + c0;
+      const float* cr = P.c + row * C + c0;
+      if (vec) {
+#pragma unroll
+        for (int i = 0; i < V; i += 4) {
+          cp_async16(dst + i, xr + i);
+          cp_async16(dst + V + i, cr + i);
+        }
+      } else {
+#pragma unroll
+        for (int i = 0; i < V; ++i) {
+          const bool ok = c0 + i < C;
+          cp_async4(dst + i, ok ? xr + i : P.x, ok);
+          cp_async4(dst + V + i, ok ? cr + i : P.c, ok);
+        }
+      }
+    }
+    cp_async_commit();
+  };
+  auto lds_pairs = [&](const float* src, F2 (&r)[H]) {
+#pragma unroll
+    for (int i = 0; i < V; i += 4) {
+      const float4 u = *reinterpret_cast<const float4*>(src + i);
+      r[i / 2] = pk(u.x, u.y);
+      r[i / 2 + 1] = pk(u.z, u.w);
+    }
+  };
+  auto store_row = [&](float* dst, const F2 (&r)[H]) {
     if (vec) {
 #pragma unroll
       for (int i = 0; i < V; i += 4) {
-        float4 u = __ldcs(reinterpret_cast<const float4*>(xr + c0 + i));
-        x[i / 2] = pk(u.x, u.y);
-        x[i / 2 + 1] = pk(u.z, u.w);
-        float4 q = __ldcs(reinterpret_cast<const float4*>(cr + c0 + i));
-        c[i / 2] = pk(q.x, q.y);
-        c[i / 2 + 1] = pk(q.z, q.w);
+        float u0, u1, u2, u3;
+        upk(r[i / 2], u0, u1);
+        upk(r[i / 2 + 1], u2, u3);
+        __stcs(reinterpret_cast<float4*>(dst + c0 + i), make_float4(u0, u1, u2, u3));
       }
-    } else {
+    } else if (any) {
 #pragma unroll
       for (int i = 0; i < V; i += 2) {
-        x[i / 2] = pk(c0 + i < C ? xr[c0 + i] : 0.f, c0 + i + 1 < C ? xr[c0 + i + 1] : 0.f);
-        c[i / 2] = pk(c0 + i < C ? cr[c0 + i] : 0.f, c0 + i + 1 < C ? cr[c0 + i + 1] : 0.f);
+        float u0, u1;
+        upk(r[i / 2], u0, u1);
+        if (c0 + i < C) dst[c0 + i] = u0;
+        if (c0 + i + 1 < C) dst[c0 + i + 1] = u1;
       }
     }
+  };
+
+  prefetch(blockIdx.x, 0);
+  int stage = 0;
+  for (int64_t row = blockIdx.x; row < P.rows; row += G, stage ^= 1) {
+    prefetch(row + G, stage ^ 1);
+    cp_async_wait<1>();
+    const float* xs = sm + ((size_t)stage * T + threadIdx.x) * 2 * V;
+    const float* cs = xs + V;
+    F2 w[H], t[H];
     // ---- forward: p = x a + b ; t = tanh(k p (1 + c p^2)) ; w = g = 0.5 p (1 + t)
-    F2 s2 = sp(0.f);
+    F2 s2 = sp(0.f), q2 = sp(0.f);
     {
-      F2 a[H], b[H];
-      ldg_pairs<V>(a, P.a, c0, C, vec, 0.f);
-      ldg_pairs<V>(b, P.b, c0, C, vec, 0.f);
+      F2 x[H];
+      lds_pairs(xs, x);
 #pragma unroll
       for (int i = 0; i < H; ++i) {
         const F2 p = fma2(x[i], a[i], b[i]);
@@ -240,34 +301,25 @@ __global__ void __launch_bounds__(T, T <= 256 ? 2 : 1) rowfused_kernel(const __g
         const F2 hp = mul2(p, sp(0.5f));
         w[i] = mul_mask(fma2(hp, t[i], hp), i);
         s2 = add2(s2, w[i]);
+        q2 = fma2(w[i], w[i], q2);
       }
     }
-    float sa, sb;
+    float sa, sb, qa, qb;
     upk(s2, sa, sb);
-    const float mean = bsum<NW>(sa + sb, sh) * invC;
-    F2 q2 = sp(0.f);
-#pragma unroll
-    for (int i = 0; i < H; ++i) {
-      const F2 d = mul_mask(add2(w[i], sp(-mean)), i);
-      q2 = fma2(d, d, q2);
-    }
-    upk(q2, sa, sb);
-    const float rstd = rsqrtf(bsum<NW>(sa + sb, sh) * invC + P.eps);
+    upk(q2, qa, qb);
+    const Red2 SG = bsum2<NW>(sa + sb, qa + qb, sh);
+    const float mean = SG.a * invC;
+    const float rstd = rsqrtf(fmaxf(SG.b * invC - mean * mean, 0.f) + P.eps);
+    const F2 nmr = sp(-mean * rstd), rs = sp(rstd);
     // w = n = LayerNorm(g); row max
     float m = -INFINITY;
-    {
-      F2 ga[H], be[H];
-      ldg_pairs<V>(ga, P.gamma, c0, C, vec, 1.f);
-      ldg_pairs<V>(be, P.beta, c0, C, vec, 0.f);
-      const F2 nmr = sp(-mean * rstd), rs = sp(rstd);
 #pragma unroll
-      for (int i = 0; i < H; ++i) {
-        w[i] = fma2(fma2(w[i], rs, nmr), ga[i], be[i]);
-        float u0, u1;
-        upk(w[i], u0, u1);
-        if (c0 + 2 * i < C) m = fmaxf(m, u0);
-        if (c0 + 2 * i + 1 < C) m = fmaxf(m, u1);
-      }
+    for (int i = 0; i < H; ++i) {
+      w[i] = fma2(fma2(w[i], rs, nmr), ga[i], be[i]);
+      float u0, u1;
+      upk(w[i], u0, u1);
+      if (!RAGGED || c0 + 2 * i < C) m = fmaxf(m, u0);
+      if (!RAGGED || c0 + 2 * i + 1 < C) m = fmaxf(m, u1);
     }
     const float M = bmax<NW>(m, sh);
     // w = exp(n - M)
@@ -289,6 +341,8 @@ __global__ void __launch_bounds__(T, T <= 256 ? 2 : 1) rowfused_kernel(const __g
     float ym = -INFINITY;
     int yj = 0x7fffffff;
     {
+      F2 c[H];
+      lds_pairs(cs, c);
       const F2 iv = sp(inv);
 #pragma unroll
       for (int i = 0; i < H; ++i) {
@@ -296,11 +350,11 @@ __global__ void __launch_bounds__(T, T <= 256 ? 2 : 1) rowfused_kernel(const __g
         cy2 = fma2(c[i], w[i], cy2);
         float u0, u1;
         upk(w[i], u0, u1);
-        if (c0 + 2 * i < C && u0 > ym) {
+        if ((!RAGGED || c0 + 2 * i < C) && u0 > ym) {
           ym = u0;
           yj = c0 + 2 * i;
         }
-        if (c0 + 2 * i + 1 < C && u1 > ym) {
+        if ((!RAGGED || c0 + 2 * i + 1 < C) && u1 > ym) {
           ym = u1;
           yj = c0 + 2 * i + 1;
         }
@@ -310,54 +364,21 @@ __global__ void __launch_bounds__(T, T <= 256 ? 2 : 1) rowfused_kernel(const __g
     float cy = sa + sb;
     bsum_argmax<NW>(cy, ym, yj, sh, shi);
     if (P.am && threadIdx.x == 0) P.am[row] = yj;
-    float* yr = P.y + row * C;
-    if (vec) {
-#pragma unroll
-      for (int i = 0; i < V; i += 4) {
-        float u0, u1, u2, u3;
-        upk(w[i / 2], u0, u1);
-        upk(w[i / 2 + 1], u2, u3);
-        __stcs(reinterpret_cast<float4*>(yr + c0 + i), make_float4(u0, u1, u2, u3));
-      }
-    } else if (any) {
-#pragma unroll
-      for (int i = 0; i < V; i += 2) {
-        float u0, u1;
-        upk(w[i / 2], u0, u1);
-        if (c0 + i < C) yr[c0 + i] = u0;
-        if (c0 + i + 1 < C) yr[c0 + i + 1] = u1;
-      }
-    }
-    // ---- backward. c = dn = y (c - cy) (y dies here); t = tanh recomputed from x
+    store_row(P.y + row * C, w);
+    // ---- backward 1: w = dn = y (c - cy) ; s1 = sum dn gamma ; s2 = sum dn gamma g_hat
     F2 s12 = sp(0.f), s22 = sp(0.f);
     {
+      F2 c[H], x[H];
+      lds_pairs(cs, c);
+      lds_pairs(xs, x);
       const F2 ncy = sp(-cy);
 #pragma unroll
-      for (int i = 0; i < H; ++i) c[i] = mul2(w[i], add2(c[i], ncy));
-    }
-    {
-      F2 a[H], b[H];
-      ldg_pairs<V>(a, P.a, c0, C, vec, 0.f);
-      ldg_pairs<V>(b, P.b, c0, C, vec, 0.f);
-#pragma unroll
       for (int i = 0; i < H; ++i) {
-        const F2 p = fma2(x[i], a[i], b[i]);
-        const F2 q = fma2(mul2(p, p), sp(C_GELU), sp(1.f));
-        t[i] = tanh2_from_scaled(mul2(mul2(p, q), sp(KG2L)));
-      }
-    }
-    {
-      F2 a[H], b[H], ga[H];
-      ldg_pairs<V>(a, P.a, c0, C, vec, 0.f);
-      ldg_pairs<V>(b, P.b, c0, C, vec, 0.f);
-      ldg_pairs<V>(ga, P.gamma, c0, C, vec, 1.f);
-      const F2 nmr = sp(-mean * rstd), rs = sp(rstd);
-#pragma unroll
-      for (int i = 0; i < H; ++i) {
+        w[i] = mul2(w[i], add2(c[i], ncy));
         const F2 p = fma2(x[i], a[i], b[i]);
         const F2 hp = mul2(p, sp(0.5f));
         const F2 gh = mul_mask(fma2(fma2(hp, t[i], hp), rs, nmr), i);
-        const F2 dyg = mul2(c[i], ga[i]);
+        const F2 dyg = mul2(w[i], ga[i]);
         s12 = add2(s12, dyg);
         s22 = fma2(dyg, gh, s22);
       }
@@ -366,78 +387,48 @@ __global__ void __launch_bounds__(T, T <= 256 ? 2 : 1) rowfused_kernel(const __g
     upk(s12, s1a, s1b);
     upk(s22, s2a, s2b);
     const Red2 S = bsum2<NW>(s1a + s1b, s2a + s2b, sh);
+    // ---- backward 2: dg, gelu', dp ; dx = dp a ; da += dp x ; db += dp
     {
-      F2 a[H], b[H], ga[H];
-      ldg_pairs<V>(a, P.a, c0, C, vec, 0.f);
-      ldg_pairs<V>(b, P.b, c0, C, vec, 0.f);
-      ldg_pairs<V>(ga, P.gamma, c0, C, vec, 1.f);
+      F2 x[H], dx[H];
+      lds_pairs(xs, x);
       const F2 k1 = sp(rstd * invC), fC = sp((float)C), nS1 = sp(-S.a), nS2 = sp(-S.b);
-      const F2 nmr = sp(-mean * rstd), rs = sp(rstd);
-      float* accda = acc;
-      float* accdb = acc + C;
 #pragma unroll
       for (int i = 0; i < H; ++i) {
         const F2 p = fma2(x[i], a[i], b[i]);
-        const F2 hp0 = mul2(p, sp(0.5f));
-        w[i] = mul_mask(fma2(fma2(hp0, t[i], hp0), rs, nmr), i);  // g_hat
-        // dg = rstd/C (C dyg - S1 - g_hat S2)
-        const F2 dg = mul2(k1, fma2(w[i], nS2, fma2(fC, mul2(c[i], ga[i]), nS1)));
+        const F2 hp = mul2(p, sp(0.5f));
+        const F2 gh = mul_mask(fma2(fma2(hp, t[i], hp), rs, nmr), i);
+        // dg = rstd/C (C dn gamma - S1 - g_hat S2)
+        const F2 dg = mul2(k1, fma2(gh, nS2, fma2(fC, mul2(w[i], ga[i]), nS1)));
         // gelu'(p) = 0.5 (1 + t) + 0.5 k p (1 - t^2) (1 + 3 c p^2)
         const F2 A = fma2(t[i], sp(0.5f), sp(0.5f));
         const F2 sech2 = fma2(t[i], mul2(t[i], sp(-1.f)), sp(1.f));
         const F2 Bq = fma2(mul2(p, p), sp(3.f * C_GELU), sp(1.f));
         const F2 gd = fma2(mul2(mul2(p, sp(0.5f * K_GELU)), sech2), Bq, A);
         const F2 dp = mul_mask(mul2(dg, gd), i);
-        const int col = c0 + 2 * i;
-        if (col < C) {
-          float d0, d1, x0, x1;
-          upk(dp, d0, d1);
-          upk(x[i], x0, x1);
-          accda[col] = fmaf(d0, x0, accda[col]);
-          accdb[col] += d0;
-          if (col + 1 < C) {
-            accda[col + 1] = fmaf(d1, x1, accda[col + 1]);
-            accdb[col + 1] += d1;
-          }
-          if (GB) {
-            float n0, n1, g0, g1;
-            upk(c[i], n0, n1);
-            upk(w[i], g0, g1);
-            acc[2 * C + col] = fmaf(n0, g0, acc[2 * C + col]);
-            acc[3 * C + col] += n0;
-            if (col + 1 < C) {
-              acc[2 * C + col + 1] = fmaf(n1, g1, acc[2 * C + col + 1]);
-              acc[3 * C + col + 1] += n1;
-            }
-          }
+        dx[i] = mul2(dp, a[i]);
+        acc_da[i] = fma2(dp, x[i], acc_da[i]);
+        acc_db[i] = add2(acc_db[i], dp);
+        if (GB) {
+          acc_dg[i] = fma2(w[i], gh, acc_dg[i]);
+          acc_dbe[i] = add2(acc_dbe[i], w[i]);
         }
-        x[i] = mul2(dp, a[i]);  // x now holds dx
       }
-    }
-    float* dxr = P.dx + row * C;
-    if (vec) {
-#pragma unroll
-      for (int i = 0; i < V; i += 4) {
-        float u0, u1, u2, u3;
-        upk(x[i / 2], u0, u1);
-        upk(x[i / 2 + 1], u2, u3);
-        __stcs(reinterpret_cast<float4*>(dxr + c0 + i), make_float4(u0, u1, u2, u3));
-      }
-    } else if (any) {
-#pragma unroll
-      for (int i = 0; i < V; i += 2) {
-        float u0, u1;
-        upk(x[i / 2], u0, u1);
-        if (c0 + i < C) dxr[c0 + i] = u0;
-        if (c0 + i + 1 < C) dxr[c0 + i + 1] = u1;
-      }
+      store_row(P.dx + row * C, dx);
     }
   }
-  // per-CTA column partials (each thread flushes the columns it owns)
-  __syncthreads();
-  const int64_t G = gridDim.x;
-  for (int64_t col = threadIdx.x; col < C; col += T) {
-    for (int k = 0; k < nacc; ++k) P.part[((int64_t)k * G + blockIdx.x) * C + col] = acc[(int64_t)k * C + col];
+  cp_async_wait<0>();
+  // per-CTA column partials (each thread writes the columns it owns)
+#pragma unroll
+  for (int i = 0; i < H; ++i) {
+    const int col = c0 + 2 * i;
+    float u0, u1;
+    F2 vals[4] = {acc_da[i], acc_db[i], GB ? acc_dg[GB ? i : 0] : sp(0.f), GB ? acc_dbe[GB ? i : 0] : sp(0.f)};
+#pragma unroll
+    for (int k = 0; k < (GB ? 4 : 2); ++k) {
+      upk(vals[k], u0, u1);
+      if (col < C) P.part[((int64_t)k * G + blockIdx.x) * C + col] = u0;
+      if (col + 1 < C) P.part[((int64_t)k * G + blockIdx.x) * C + col + 1] = u1;
+    }
   }
 }
 
@@ -457,7 +448,7 @@ __global__ void colsum_kernel(const float* __restrict__ part, float* __restrict_
 
 template <int T, int V>
 int launch(const Params& P, int64_t grid, cudaStream_t s) {
-  const size_t smem = (size_t)(P.want_gb ? 4 : 2) * P.cols * sizeof(float);
+  const size_t smem = (size_t)2 * 2 * T * V * sizeof(float);
   const bool ragged = P.cols != (int64_t)T * V;
 #define B200_RF_LAUNCH(GB_, RG_)                                                                                        \
   do {                                                                                                                   \
@@ -476,19 +467,19 @@ int launch(const Params& P, int64_t grid, cudaStream_t s) {
   return check_launch("rowfused");
 }
 
-// threads per CTA for a row length: 16 columns per thread (8 for short rows)
+// threads per CTA for a row length: 4 columns per thread up to 4096 columns
 inline void shape_for(int64_t cols, int& T, int& V) {
-  V = cols <= 512 ? 8 : 16;
+  V = cols <= 4096 ? 4 : (cols <= 8192 ? 8 : 16);
   const int64_t t = (cols + V - 1) / V;
   T = 32;
   while (T < t) T *= 2;
 }
 
-// two CTAs per SM (up to 256 threads, <= 128 registers each), one for bigger CTAs
+// 1024 resident threads per SM
 inline int64_t grid_for(int64_t rows, int64_t cols) {
   int T, V;
   shape_for(cols, T, V);
-  const int64_t per_sm = T <= 256 ? 2 : 1;
+  const int64_t per_sm = T <= 512 ? 1024 / T : 1;
   return std::max<int64_t>(1, std::min<int64_t>(rows, (int64_t)num_sms() * per_sm));
 }
 
@@ -534,20 +525,19 @@ extern "C" int b200_rowfused_fwd_bwd(const float* x, const float* a, const float
   shape_for(cols, T, V);
   const int64_t grid = grid_for(rows, cols);
   int rc;
-  if (V == 8) {
+  if (V == 4) {
     switch (T) {
-      case 32: rc = launch<32, 8>(P, grid, s); break;
-      default: rc = launch<64, 8>(P, grid, s); break;
+      case 32: rc = launch<32, 4>(P, grid, s); break;
+      case 64: rc = launch<64, 4>(P, grid, s); break;
+      case 128: rc = launch<128, 4>(P, grid, s); break;
+      case 256: rc = launch<256, 4>(P, grid, s); break;
+      case 512: rc = launch<512, 4>(P, grid, s); break;
+      default: rc = launch<1024, 4>(P, grid, s); break;
     }
+  } else if (V == 8) {
+    rc = launch<1024, 8>(P, grid, s);
   } else {
-    switch (T) {
-      case 32: rc = launch<32, 16>(P, grid, s); break;
-      case 64: rc = launch<64, 16>(P, grid, s); break;
-      case 128: rc = launch<128, 16>(P, grid, s); break;
-      case 256: rc = launch<256, 16>(P, grid, s); break;
-      case 512: rc = launch<512, 16>(P, grid, s); break;
-      default: rc = launch<1024, 16>(P, grid, s); break;
-    }
+    rc = launch<1024, 16>(P, grid, s);
   }
   if (rc) return rc;
   dim3 g2((unsigned)ceil_div(cols, 256), P.want_gb ? 4 : 2);

@@ -44,8 +44,13 @@ def test_graph_parity(cuda, case, mode):
 
         ins, _ = load_golden(case)
         emu = O.evaluate_roles(O.load_graph(case), ins, contraction_rounding="bf16")
+        # outputs that are zero in exact arithmetic (e.g. the key-bias gradient of softmax
+        # attention) are compared against an absolute floor: 1e-3 of the largest output
+        floor = 1e-3 * max(float(np.abs(np.asarray(v)).max()) for v in emu.values() if np.asarray(v).size)
         for name, r in ref.items():
-            assert_close(f"{case}:{name}(bf16 policy)", got[name], np.asarray(emu[name], dtype=np.float32), rtol)
+            e = np.asarray(emu[name], dtype=np.float32)
+            atol = rtol * max(float(np.abs(e).max()) if e.size else 0.0, floor)
+            assert_close(f"{case}:{name}(bf16 policy)", got[name], e, rtol, atol_scale=atol)
             v = to_np(got[name]).astype(np.float64)
-            nrel = np.linalg.norm(v - r) / max(np.linalg.norm(r), 1e-30)
+            nrel = np.linalg.norm(v - r) / max(np.linalg.norm(r), floor * np.sqrt(r.size), 1e-30)
             assert nrel <= 0.1, (name, nrel)
