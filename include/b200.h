@@ -229,6 +229,16 @@ int b200_rowfused_fwd_bwd(const float* x, const float* a, const float* b, const 
                           float* dbeta, int64_t rows, int64_t cols, float eps, void* workspace, size_t workspace_bytes,
                           void* stream);
 
+/* ReLU-with-bias backward in one pass: gp = g * mask (Multiply(cot, Greater(pre, 0)),
+ * the Relu VJP of transforms/autodiff_rules/vjp_rules.yaml:25-27 evaluated by
+ * numpy/eager/math_binary.py:39-51) and dbias = column sums of gp (BroadcastReduce,
+ * eager/core_math_ops/math_reduction.py:192-224). g [rows, cols] fp32, mask [rows, cols]
+ * bool bytes; outputs gp as bf16 and/or fp32 (either may be NULL) and colsum [cols] fp32
+ * (may be NULL). workspace >= b200_mask_mul_colsum_workspace_bytes(rows, cols). */
+size_t b200_mask_mul_colsum_workspace_bytes(int64_t rows, int64_t cols);
+int b200_mask_mul_colsum(const float* g, const uint8_t* mask, void* y_bf16, float* y_f32, float* colsum, int64_t rows,
+                         int64_t cols, void* workspace, size_t workspace_bytes, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -219,6 +219,8 @@ class CompiledGraph:
             self._capture(d)
         for k, v in d.items():
             dst = self.static_in[k]
+            # callers that fill the static buffers in place (inputs already resident)
+            # pass them back unchanged: nothing to copy
             if isinstance(dst, torch.Tensor) and v is not dst:
                 dst.copy_(v, non_blocking=True)  # device-to-device copy engine transfer
         if self.cuda_graph is not None:

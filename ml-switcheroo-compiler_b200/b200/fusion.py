@@ -343,6 +343,80 @@ def gemm_epilogue_step(m: Match) -> Step:
 
 
 # ----------------------------------------------------------------------------------
+# pattern: ReLU-with-bias backward  gp = cot * mask ; dbias = BroadcastReduce(gp, bias)
+# ----------------------------------------------------------------------------------
+def _only_gemm_consumers(g: Graph, v: str, live: dict[str, Node], users: dict[str, list[str]], skip: set[str]) -> bool:
+    for u in users.get(v, []):
+        if u in skip or u not in live:
+            continue
+        op = _op_name(live[u])
+        if op == "Matmul":
+            continue
+        if op in ("Transpose", "Reshape") and _only_gemm_consumers(g, u, live, users, skip):
+            continue
+        return False
+    return True
+
+
+def find_mask_bwd(g: Graph, live: dict[str, Node], meta: dict[str, Meta], users: dict[str, list[str]],
+                  outputs: set[str]) -> list[Match]:
+    found = []
+    for nid, node in live.items():
+        if _op_name(node) != "Multiply" or len(node.inputs) != 2:
+            continue
+        m0, m1 = meta.get(node.inputs[0]), meta.get(node.inputs[1])
+        if m0 is None or m1 is None or m0.scalar or m1.scalar:
+            continue
+        if m1.dtype == torch.bool and m0.dtype == torch.float32:
+            cot, mask = node.inputs
+        elif m0.dtype == torch.bool and m1.dtype == torch.float32:
+            mask, cot = node.inputs
+        else:
+            continue
+        mo = meta[nid]
+        if mo.shape != meta[cot].shape or mo.shape != meta[mask].shape or len(mo.shape) < 1:
+            continue
+        C = mo.shape[-1]
+        br = None
+        for u in users.get(nid, []):
+            un = live.get(u)
+            if un is not None and _op_name(un) == "BroadcastReduce" and un.inputs[0] == nid:
+                mb = meta.get(un.inputs[1])
+                if mb is not None and not mb.scalar and mb.shape == (C,) and meta[u].shape == (C,):
+                    br = u
+                    break
+        if br is None:
+            continue
+        bf16_only = ops.Config.matmul_dtype == "bf16" and nid not in outputs and _only_gemm_consumers(g, nid, live, users, {br})
+        found.append(Match("relu_bwd_bias", {"cot": cot, "mask": mask, "gp": nid, "db": br, "bf16": str(bf16_only)},
+                           {nid, br}, {"gp": nid, "db": br}))
+    return found
+
+
+def mask_bwd_step(m: Match, meta: dict[str, Meta]) -> Step:
+    b = m.bind
+    shape = meta[b["gp"]].shape
+    C = shape[-1]
+    R = math.prod(shape[:-1])
+    bf16_only = b["bf16"] == "True"
+    ws_bytes = int(L.lib().b200_mask_mul_colsum_workspace_bytes(R, C))
+
+    def run(env: dict) -> None:
+        g = ops.contiguous(env[b["cot"]])
+        mk = ops.contiguous(env[b["mask"]])
+        dev = ops.device()
+        gp = torch.empty(shape, dtype=torch.bfloat16 if bf16_only else torch.float32, device=dev)
+        db = torch.empty(C, dtype=torch.float32, device=dev)
+        ws = torch.empty(max(1, ws_bytes), dtype=torch.uint8, device=dev)
+        L.call("b200_mask_mul_colsum", g.data_ptr(), mk.data_ptr(), gp.data_ptr() if bf16_only else None,
+               None if bf16_only else gp.data_ptr(), db.data_ptr(), R, C, ws.data_ptr(), ws_bytes, ops.stream_ptr())
+        env[b["gp"]] = gp
+        env[b["db"]] = db
+
+    return Step([b["gp"], b["db"]], [b["cot"], b["mask"]], run, "relu_bwd_bias" + ("[bf16]" if bf16_only else ""))
+
+
+# ----------------------------------------------------------------------------------
 # elementwise clustering (subsystem 1)
 # ----------------------------------------------------------------------------------
 EW_UNARY = {"Negative": "NEG", "Exp": "EXP", "Log": "LOG", "Tanh": "TANH", "Sqrt": "SQRT", "Relu": "RELU", "Gelu": "GELU",
@@ -556,6 +630,12 @@ def plan_steps(graph: Graph, nodes: list[Node], sample: dict[str, Any]) -> list[
         if m.covered & taken:
             continue
         groups.append((sorted(m.covered), gemm_epilogue_step(m)))
+        taken |= m.covered
+
+    for m in find_mask_bwd(graph, live, meta, users, outputs):
+        if m.covered & taken:
+            continue
+        groups.append((sorted(m.covered), mask_bwd_step(m, meta)))
         taken |= m.covered
 
     # 2. elementwise clusters

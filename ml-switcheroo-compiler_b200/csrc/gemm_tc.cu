@@ -108,9 +108,18 @@ struct Args {
   uint8_t* aux;
   int64_t M, N, K, sC, ldc;
   float alpha;
-  int c_dt, epi, a_mn, b_mn;
+  int c_dt, epi, a_mn, b_mn, batch;
 };
 
+__device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
+  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
+}
+
+// Persistent kernel: gridDim.x CTAs (one per SM) walk the output tiles in a static
+// round-robin order (n fastest, then m, then batch: concurrent CTAs share operand panels
+// in L2). The TMEM accumulator is double-buffered (2 x BN columns), so the epilogue of
+// tile i (TMEM -> registers -> HBM) overlaps the MMAs of tile i+1, and the TMA/MMA
+// pipeline runs continuously across tile boundaries.
 template <int BN>
 __global__ void __launch_bounds__(THREADS, 1) gemm_tc_kernel(const __grid_constant__ CUtensorMap mapA,
                                                              const __grid_constant__ CUtensorMap mapB,
@@ -123,23 +132,30 @@ __global__ void __launch_bounds__(THREADS, 1) gemm_tc_kernel(const __grid_consta
   uint8_t* sB = smem + STAGES * A_BYTES;
   uint64_t* full_bar = reinterpret_cast<uint64_t*>(sB + STAGES * B_BYTES);
   uint64_t* empty_bar = full_bar + STAGES;
-  uint64_t* accum_bar = empty_bar + STAGES;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(accum_bar + 1);
+  uint64_t* acc_full = empty_bar + STAGES;  // [2]
+  uint64_t* acc_empty = acc_full + 2;       // [2]
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(acc_empty + 2);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int n_tile = blockIdx.x, m_tile = blockIdx.y, z = blockIdx.z;
   const int num_kb = (int)((args.K + BK - 1) / BK);
+  const int tiles_n = (int)((args.N + BN - 1) / BN);
+  const int tiles_m = (int)((args.M + BM - 1) / BM);
+  const int tiles_mn = tiles_n * tiles_m;
+  const int total = tiles_mn * args.batch;
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < STAGES; ++s) {
       mbar_init(&full_bar[s], 1);
       mbar_init(&empty_bar[s], 1);
     }
-    mbar_init(accum_bar, 1);
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(&acc_full[b], 1);
+      mbar_init(&acc_empty[b], 4);  // one arrive per epilogue warp
+    }
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
   }
   if (warp == 1) {
-    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tmem_slot)), "r"(BN));
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tmem_slot)), "r"(2 * BN));
     asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
   }
   tc_fence_before();
@@ -150,71 +166,91 @@ __global__ void __launch_bounds__(THREADS, 1) gemm_tc_kernel(const __grid_consta
   if (warp == 0) {
     if (lane == 0) {
       // ---------------- TMA producer ----------------
-      for (int kb = 0; kb < num_kb; ++kb) {
-        const int s = kb % STAGES;
-        const uint32_t round = kb / STAGES;
-        if (!mbar_wait(&empty_bar[s], (round & 1) ^ 1)) break;
-        mbar_expect_tx(&full_bar[s], A_BYTES + B_BYTES);
-        const int k0 = kb * BK;
-        uint8_t* a_dst = sA + s * A_BYTES;
-        uint8_t* b_dst = sB + s * B_BYTES;
-        if (!args.a_mn) {
-          tma_load_3d(a_dst, &mapA, &full_bar[s], k0, m_tile * BM, z);
-        } else {
-          tma_load_3d(a_dst, &mapA, &full_bar[s], m_tile * BM, k0, z);
-          tma_load_3d(a_dst + 8192, &mapA, &full_bar[s], m_tile * BM + 64, k0, z);
-        }
-        if (!args.b_mn) {
-          tma_load_3d(b_dst, &mapB, &full_bar[s], k0, n_tile * BN, z);
-        } else {
+      uint32_t it = 0;
+      bool ok = true;
+      for (int tile = blockIdx.x; tile < total && ok; tile += gridDim.x) {
+        const int z = tile / tiles_mn, r = tile % tiles_mn;
+        const int m_tile = r / tiles_n, n_tile = r % tiles_n;
+        for (int kb = 0; kb < num_kb; ++kb, ++it) {
+          const int s = it % STAGES;
+          const uint32_t round = it / STAGES;
+          if (!mbar_wait(&empty_bar[s], (round & 1) ^ 1)) {
+            ok = false;
+            break;
+          }
+          mbar_expect_tx(&full_bar[s], A_BYTES + B_BYTES);
+          const int k0 = kb * BK;
+          uint8_t* a_dst = sA + s * A_BYTES;
+          uint8_t* b_dst = sB + s * B_BYTES;
+          if (!args.a_mn) {
+            tma_load_3d(a_dst, &mapA, &full_bar[s], k0, m_tile * BM, z);
+          } else {
+            tma_load_3d(a_dst, &mapA, &full_bar[s], m_tile * BM, k0, z);
+            tma_load_3d(a_dst + 8192, &mapA, &full_bar[s], m_tile * BM + 64, k0, z);
+          }
+          if (!args.b_mn) {
+            tma_load_3d(b_dst, &mapB, &full_bar[s], k0, n_tile * BN, z);
+          } else {
 #pragma unroll
-          for (int j = 0; j < BN / 64; ++j) tma_load_3d(b_dst + j * 8192, &mapB, &full_bar[s], n_tile * BN + 64 * j, k0, z);
+            for (int j = 0; j < BN / 64; ++j) tma_load_3d(b_dst + j * 8192, &mapB, &full_bar[s], n_tile * BN + 64 * j, k0, z);
+          }
         }
       }
     }
   } else if (warp == 1) {
     if (lane == 0) {
       // ---------------- MMA issuer ----------------
-      // instruction descriptor: D f32, A/B bf16, majors, N>>3, M>>4
       const uint32_t idesc = (1u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)args.a_mn << 15) | ((uint32_t)args.b_mn << 16) |
                              ((uint32_t)(BN >> 3) << 17) | ((uint32_t)(BM >> 4) << 24);
+      uint32_t it = 0, local = 0;
       bool ok = true;
-      for (int kb = 0; kb < num_kb; ++kb) {
-        const int s = kb % STAGES;
-        const uint32_t round = kb / STAGES;
-        if (!mbar_wait(&full_bar[s], round & 1)) {
-          ok = false;
-          break;
-        }
+      for (int tile = blockIdx.x; tile < total && ok; tile += gridDim.x, ++local) {
+        const int b = local & 1;
+        const uint32_t use = local >> 1;
+        if (!mbar_wait(&acc_empty[b], (use & 1) ^ 1)) break;
         tc_fence_after();
-        const uint32_t a_base = smem_u32(sA + s * A_BYTES);
-        const uint32_t b_base = smem_u32(sB + s * B_BYTES);
+        const uint32_t d_tmem = tmem_base + (uint32_t)(b * BN);
+        for (int kb = 0; kb < num_kb; ++kb, ++it) {
+          const int s = it % STAGES;
+          const uint32_t round = it / STAGES;
+          if (!mbar_wait(&full_bar[s], round & 1)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint32_t a_base = smem_u32(sA + s * A_BYTES);
+          const uint32_t b_base = smem_u32(sB + s * B_BYTES);
 #pragma unroll
-        for (int k = 0; k < BK / 16; ++k) {
-          // K-major: +32 B per 16-element K step inside the 128 B swizzle row.
-          // MN-major: +2048 B per K step (two 8-row groups of 1024 B).
-          const uint64_t ad = args.a_mn ? smem_desc(a_base + k * 2048, 8192, 1024) : smem_desc(a_base + k * 32, 16, 1024);
-          const uint64_t bd = args.b_mn ? smem_desc(b_base + k * 2048, 8192, 1024) : smem_desc(b_base + k * 32, 16, 1024);
-          mma_bf16(tmem_base, ad, bd, idesc, (kb > 0 || k > 0) ? 1u : 0u);
+          for (int k = 0; k < BK / 16; ++k) {
+            // K-major: +32 B per 16-element K step inside the 128 B swizzle row.
+            // MN-major: +2048 B per K step (two 8-row groups of 1024 B).
+            const uint64_t ad = args.a_mn ? smem_desc(a_base + k * 2048, 8192, 1024) : smem_desc(a_base + k * 32, 16, 1024);
+            const uint64_t bd = args.b_mn ? smem_desc(b_base + k * 2048, 8192, 1024) : smem_desc(b_base + k * 32, 16, 1024);
+            mma_bf16(d_tmem, ad, bd, idesc, (kb > 0 || k > 0) ? 1u : 0u);
+          }
+          mma_commit(&empty_bar[s]);  // stage s free once these MMAs have read it
         }
-        mma_commit(&empty_bar[s]);  // stage s free once these MMAs have read it
+        if (ok) mma_commit(&acc_full[b]);  // accumulator b complete (also fires when num_kb == 0)
       }
-      if (ok) mma_commit(accum_bar);
-      else raise_device_error(B200_ERR_TIMEOUT);
     }
   } else {
     // ---------------- epilogue (warps 2..5) ----------------
     const int q = warp & 3;  // TMEM lane quarter this warp may access
-    const bool ready = (num_kb > 0) ? mbar_wait(accum_bar, 0) : true;
-    tc_fence_after();
-    const int64_t row = (int64_t)m_tile * BM + q * 32 + lane;
-    const int64_t col0 = (int64_t)n_tile * BN;
-    if (ready) {
+    uint32_t local = 0;
+    for (int tile = blockIdx.x; tile < total; tile += gridDim.x, ++local) {
+      const int z = tile / tiles_mn, r = tile % tiles_mn;
+      const int m_tile = r / tiles_n, n_tile = r % tiles_n;
+      const int b = local & 1;
+      const uint32_t use = local >> 1;
+      if (!mbar_wait(&acc_full[b], use & 1)) break;
+      tc_fence_after();
+      const int64_t row = (int64_t)m_tile * BM + q * 32 + lane;
+      const int64_t col0 = (int64_t)n_tile * BN;
 #pragma unroll 1
       for (int c = 0; c < BN / 32; ++c) {
         float v[32];
         if (num_kb > 0) {
-          tmem_ld32(tmem_base + ((uint32_t)(q * 32) << 16) + (uint32_t)(c * 32), v);
+          tmem_ld32(tmem_base + ((uint32_t)(q * 32) << 16) + (uint32_t)(b * BN + c * 32), v);
         } else {
 #pragma unroll
           for (int i = 0; i < 32; ++i) v[i] = 0.f;
@@ -229,10 +265,10 @@ __global__ void __launch_bounds__(THREADS, 1) gemm_tc_kernel(const __grid_consta
           const int64_t n = cbase + i;
           float pre = args.alpha * v[i] + ((args.bias && n < args.N) ? args.bias[n] : 0.f);
           mask[i] = pre > 0.f;
-          float r = pre;
-          if (args.epi == B200_EPI_RELU) r = pre > 0.f ? pre : 0.f;
-          else if (args.epi == B200_EPI_GELU) r = gelu_tanh(pre);
-          v[i] = r;
+          float rr = pre;
+          if (args.epi == B200_EPI_RELU) rr = pre > 0.f ? pre : 0.f;
+          else if (args.epi == B200_EPI_GELU) rr = gelu_tanh(pre);
+          v[i] = rr;
         }
         const bool full = cbase + 32 <= args.N;
         if (args.c_dt == B200_F32) {
@@ -275,13 +311,17 @@ __global__ void __launch_bounds__(THREADS, 1) gemm_tc_kernel(const __grid_consta
           }
         }
       }
+      // accumulator b may be overwritten once every epilogue warp has read it
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&acc_empty[b]);
     }
   }
   tc_fence_before();
   __syncthreads();
   if (warp == 1) {
     tc_fence_after();
-    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem_base), "r"(BN));
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem_base), "r"(2 * BN));
   }
 }
 
@@ -327,6 +367,7 @@ static int make_map(CUtensorMap* map, const void* base, uint64_t d0, uint64_t d1
 template <int BN>
 static int launch(const CUtensorMap& ma, const CUtensorMap& mb, const Args& a, int64_t batch, cudaStream_t s) {
   const size_t smem = (size_t)STAGES * (BM * BK * 2 + BN * BK * 2) + 1024 + 256;
+  const int64_t tiles = ceil_div(a.N, BN) * ceil_div(a.M, BM) * batch;
   static bool attr_set[64] = {false};
   int dev = 0;
   cudaGetDevice(&dev);
@@ -334,7 +375,7 @@ static int launch(const CUtensorMap& ma, const CUtensorMap& mb, const Args& a, i
     cudaFuncSetAttribute(gemm_tc_kernel<BN>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
     if (dev >= 0 && dev < 64) attr_set[dev] = true;
   }
-  dim3 grid((unsigned)ceil_div(a.N, BN), (unsigned)ceil_div(a.M, BM), (unsigned)batch);
+  const unsigned grid = (unsigned)std::max<int64_t>(1, std::min<int64_t>(tiles, num_sms()));
   gemm_tc_kernel<BN><<<grid, THREADS, smem, s>>>(ma, mb, a);
   return check_launch("gemm(bf16 tcgen05)");
 }
@@ -392,6 +433,8 @@ int gemm_bf16_tcgen05(int c_dt, const void* A, const void* B, void* C, int64_t b
   a.epi = epi;
   a.a_mn = a_mn;
   a.b_mn = b_mn;
+  a.batch = (int)batch;
+  B200_REQUIRE(ceil_div(N, 256) * ceil_div(M, BM) * batch < INT32_MAX, "gemm(bf16): too many tiles");
   B200_REQUIRE(ceil_div(M, BM) <= 65535, "gemm(bf16): M too large");
   if (BN == 256) return launch<256>(ma, mb, a, batch, s);
   return launch<128>(ma, mb, a, batch, s);

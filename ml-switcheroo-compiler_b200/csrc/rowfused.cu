@@ -39,74 +39,102 @@ struct Red2 {
   float a, b;
 };
 
+// Block reductions: shuffle within each warp, then warp 0 combines the NW partials and
+// broadcasts the result through shared memory (3 barriers' worth of latency, but only one
+// warp does the second level).
 template <int NW>
 __device__ __forceinline__ float bsum(float v, float* sh) {
   v = warp_sum(v);
   const int lane = threadIdx.x & 31, w = threadIdx.x >> 5;
-  __syncthreads();
   if (lane == 0) sh[w] = v;
   __syncthreads();
-  float t = lane < NW ? sh[lane] : 0.f;
-  return warp_sum(t);
+  if (w == 0) {
+    float t = lane < NW ? sh[lane] : 0.f;
+    t = warp_sum(t);
+    if (lane == 0) sh[32] = t;
+  }
+  __syncthreads();
+  const float r = sh[32];
+  __syncthreads();
+  return r;
 }
 template <int NW>
 __device__ __forceinline__ Red2 bsum2(float a, float b, float* sh) {
   a = warp_sum(a);
   b = warp_sum(b);
   const int lane = threadIdx.x & 31, w = threadIdx.x >> 5;
-  __syncthreads();
   if (lane == 0) {
     sh[w] = a;
     sh[32 + w] = b;
   }
   __syncthreads();
-  float ta = lane < NW ? sh[lane] : 0.f, tb = lane < NW ? sh[32 + lane] : 0.f;
-  return {warp_sum(ta), warp_sum(tb)};
+  if (w == 0) {
+    float ta = lane < NW ? sh[lane] : 0.f, tb = lane < NW ? sh[32 + lane] : 0.f;
+    ta = warp_sum(ta);
+    tb = warp_sum(tb);
+    if (lane == 0) {
+      sh[64] = ta;
+      sh[65] = tb;
+    }
+  }
+  __syncthreads();
+  const Red2 r = {sh[64], sh[65]};
+  __syncthreads();
+  return r;
+}
+// max of 64-bit keys (shared by row-max + argmax): key = (order-preserving bits of the
+// value) << 32 | ~index, so the largest key is the largest value at the smallest index.
+__device__ __forceinline__ unsigned long long order_key(float v, int idx) {
+  const uint32_t u = __float_as_uint(v);
+  const uint32_t o = (u & 0x80000000u) ? ~u : (u | 0x80000000u);
+  return ((unsigned long long)o << 32) | (uint32_t)(~idx);
+}
+__device__ __forceinline__ float key_value(unsigned long long k) {
+  const uint32_t o = (uint32_t)(k >> 32);
+  const uint32_t u = (o & 0x80000000u) ? (o & 0x7fffffffu) : ~o;
+  return __uint_as_float(u);
+}
+__device__ __forceinline__ int key_index(unsigned long long k) { return (int)~(uint32_t)k; }
+__device__ __forceinline__ unsigned long long warp_maxkey(unsigned long long k) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) {
+    const unsigned long long k2 = __shfl_xor_sync(0xffffffffu, k, o);
+    k = k2 > k ? k2 : k;
+  }
+  return k;
+}
+template <int NW>
+__device__ __forceinline__ unsigned long long bmaxkey(unsigned long long k, float* sh) {
+  unsigned long long* s64 = reinterpret_cast<unsigned long long*>(sh);
+  k = warp_maxkey(k);
+  const int lane = threadIdx.x & 31, w = threadIdx.x >> 5;
+  if (lane == 0) s64[w] = k;
+  __syncthreads();
+  if (w == 0) {
+    unsigned long long t = lane < NW ? s64[lane] : 0ull;
+    t = warp_maxkey(t);
+    if (lane == 0) s64[32] = t;
+  }
+  __syncthreads();
+  const unsigned long long r = s64[32];
+  __syncthreads();
+  return r;
 }
 template <int NW>
 __device__ __forceinline__ float bmax(float v, float* sh) {
   v = warp_max(v);
   const int lane = threadIdx.x & 31, w = threadIdx.x >> 5;
-  __syncthreads();
   if (lane == 0) sh[w] = v;
   __syncthreads();
-  float t = lane < NW ? sh[lane] : -INFINITY;
-  return warp_max(t);
-}
-// block argmax (first max wins) fused with a block sum
-template <int NW>
-__device__ __forceinline__ void bsum_argmax(float& s, float& m, int& j, float* sh, int* shi) {
-  s = warp_sum(s);
-#pragma unroll
-  for (int o = 16; o > 0; o >>= 1) {
-    float m2 = __shfl_xor_sync(0xffffffffu, m, o);
-    int j2 = __shfl_xor_sync(0xffffffffu, j, o);
-    if (m2 > m || (m2 == m && j2 < j)) {
-      m = m2;
-      j = j2;
-    }
-  }
-  const int lane = threadIdx.x & 31, w = threadIdx.x >> 5;
-  __syncthreads();
-  if (lane == 0) {
-    sh[w] = s;
-    sh[32 + w] = m;
-    shi[w] = j;
+  if (w == 0) {
+    float t = lane < NW ? sh[lane] : -INFINITY;
+    t = warp_max(t);
+    if (lane == 0) sh[32] = t;
   }
   __syncthreads();
-  s = lane < NW ? sh[lane] : 0.f;
-  m = lane < NW ? sh[32 + lane] : -INFINITY;
-  j = lane < NW ? shi[lane] : 0x7fffffff;
-  s = warp_sum(s);
-#pragma unroll
-  for (int o = 16; o > 0; o >>= 1) {
-    float m2 = __shfl_xor_sync(0xffffffffu, m, o);
-    int j2 = __shfl_xor_sync(0xffffffffu, j, o);
-    if (m2 > m || (m2 == m && j2 < j)) {
-      m = m2;
-      j = j2;
-    }
-  }
+  const float r = sh[32];
+  __syncthreads();
+  return r;
 }
 
 struct Params {
@@ -201,11 +229,10 @@ __device__ __forceinline__ void cp_async_wait() { asm volatile("cp.async.wait_gr
 // accumulators. x and c of the current and the next row sit in this thread's own
 // shared-memory slot, prefetched with cp.async one row ahead (double-buffered).
 template <int T, int V, bool GB, bool RAGGED>
-__global__ void __launch_bounds__(T, T <= 512 ? 1024 / T : 1) rowfused_kernel(const __grid_constant__ Params P) {
+__global__ void __launch_bounds__(T, T <= 256 ? 512 / T : 1) rowfused_kernel(const __grid_constant__ Params P) {
   constexpr int NW = T / 32;
   constexpr int H = V / 2;
-  __shared__ float sh[64];
-  __shared__ int shi[32];
+  __shared__ __align__(16) float sh[72];
   extern __shared__ __align__(16) float sm[];  // [2 stages][T][2V]: x then c
   const int64_t C = P.cols;
   const int c0 = threadIdx.x * V;
@@ -311,17 +338,25 @@ __global__ void __launch_bounds__(T, T <= 512 ? 1024 / T : 1) rowfused_kernel(co
     const float mean = SG.a * invC;
     const float rstd = rsqrtf(fmaxf(SG.b * invC - mean * mean, 0.f) + P.eps);
     const F2 nmr = sp(-mean * rstd), rs = sp(rstd);
-    // w = n = LayerNorm(g); row max
-    float m = -INFINITY;
+    // w = n = LayerNorm(g); row max and the index of its first occurrence
+    unsigned long long mk = 0ull;
 #pragma unroll
     for (int i = 0; i < H; ++i) {
       w[i] = fma2(fma2(w[i], rs, nmr), ga[i], be[i]);
       float u0, u1;
       upk(w[i], u0, u1);
-      if (!RAGGED || c0 + 2 * i < C) m = fmaxf(m, u0);
-      if (!RAGGED || c0 + 2 * i + 1 < C) m = fmaxf(m, u1);
+      if (!RAGGED || c0 + 2 * i < C) {
+        const unsigned long long k0 = order_key(u0, c0 + 2 * i);
+        mk = k0 > mk ? k0 : mk;
+      }
+      if (!RAGGED || c0 + 2 * i + 1 < C) {
+        const unsigned long long k1 = order_key(u1, c0 + 2 * i + 1);
+        mk = k1 > mk ? k1 : mk;
+      }
     }
-    const float M = bmax<NW>(m, sh);
+    mk = bmaxkey<NW>(mk, sh);
+    const float M = key_value(mk);
+    const int jn = key_index(mk);  // first index of max(n)
     // w = exp(n - M)
     F2 se2 = sp(0.f);
     {
@@ -336,10 +371,9 @@ __global__ void __launch_bounds__(T, T <= 512 ? 1024 / T : 1) rowfused_kernel(co
     }
     upk(se2, sa, sb);
     const float inv = 1.f / bsum<NW>(sa + sb, sh);
-    // w = y ; sum(c*y) ; argmax(y) (first max wins)
+    // w = y ; sum(c*y). argmax(y) is argmax(n) unless rounding made some y exactly equal to
+    // y[jn] at a smaller index: detected with one block-wide OR, then resolved exactly.
     F2 cy2 = sp(0.f);
-    float ym = -INFINITY;
-    int yj = 0x7fffffff;
     {
       F2 c[H];
       lds_pairs(cs, c);
@@ -348,21 +382,50 @@ __global__ void __launch_bounds__(T, T <= 512 ? 1024 / T : 1) rowfused_kernel(co
       for (int i = 0; i < H; ++i) {
         w[i] = mul2(w[i], iv);
         cy2 = fma2(c[i], w[i], cy2);
+      }
+    }
+    if (jn >= c0 && jn < c0 + V) {
+#pragma unroll
+      for (int i = 0; i < H; ++i) {
         float u0, u1;
         upk(w[i], u0, u1);
-        if ((!RAGGED || c0 + 2 * i < C) && u0 > ym) {
-          ym = u0;
-          yj = c0 + 2 * i;
-        }
-        if ((!RAGGED || c0 + 2 * i + 1 < C) && u1 > ym) {
-          ym = u1;
-          yj = c0 + 2 * i + 1;
-        }
+        if (c0 + 2 * i == jn) sh[70] = u0;
+        if (c0 + 2 * i + 1 == jn) sh[70] = u1;
       }
     }
     upk(cy2, sa, sb);
-    float cy = sa + sb;
-    bsum_argmax<NW>(cy, ym, yj, sh, shi);
+    const float cy = bsum<NW>(sa + sb, sh);  // its barriers also publish sh[70] = y[jn]
+    int yj = jn;
+    {
+      const float ymax = sh[70];
+      // any y that beats y[jn] under "first max wins": >= before jn, > after jn
+      int tie = 0;
+#pragma unroll
+      for (int i = 0; i < H; ++i) {
+        float u0, u1;
+        upk(w[i], u0, u1);
+        const int j0 = c0 + 2 * i, j1 = j0 + 1;
+        if ((!RAGGED || j0 < C) && (j0 < jn ? u0 >= ymax : (j0 > jn && u0 > ymax))) tie = 1;
+        if ((!RAGGED || j1 < C) && (j1 < jn ? u1 >= ymax : (j1 > jn && u1 > ymax))) tie = 1;
+      }
+      if (__syncthreads_or(tie)) {
+        unsigned long long yk = 0ull;
+#pragma unroll
+        for (int i = 0; i < H; ++i) {
+          float u0, u1;
+          upk(w[i], u0, u1);
+          if (!RAGGED || c0 + 2 * i < C) {
+            const unsigned long long k0 = order_key(u0, c0 + 2 * i);
+            yk = k0 > yk ? k0 : yk;
+          }
+          if (!RAGGED || c0 + 2 * i + 1 < C) {
+            const unsigned long long k1 = order_key(u1, c0 + 2 * i + 1);
+            yk = k1 > yk ? k1 : yk;
+          }
+        }
+        yj = key_index(bmaxkey<NW>(yk, sh));
+      }
+    }
     if (P.am && threadIdx.x == 0) P.am[row] = yj;
     store_row(P.y + row * C, w);
     // ---- backward 1: w = dn = y (c - cy) ; s1 = sum dn gamma ; s2 = sum dn gamma g_hat
@@ -467,19 +530,19 @@ int launch(const Params& P, int64_t grid, cudaStream_t s) {
   return check_launch("rowfused");
 }
 
-// threads per CTA for a row length: 4 columns per thread up to 4096 columns
+// threads per CTA for a row length: 8 columns per thread (16 above 4096 columns)
 inline void shape_for(int64_t cols, int& T, int& V) {
-  V = cols <= 4096 ? 4 : (cols <= 8192 ? 8 : 16);
+  V = cols <= 4096 ? 8 : 16;
   const int64_t t = (cols + V - 1) / V;
   T = 32;
   while (T < t) T *= 2;
 }
 
-// 1024 resident threads per SM
+// 512 resident threads per SM (128 registers each)
 inline int64_t grid_for(int64_t rows, int64_t cols) {
   int T, V;
   shape_for(cols, T, V);
-  const int64_t per_sm = T <= 512 ? 1024 / T : 1;
+  const int64_t per_sm = T <= 256 ? 512 / T : 1;
   return std::max<int64_t>(1, std::min<int64_t>(rows, (int64_t)num_sms() * per_sm));
 }
 
@@ -525,19 +588,19 @@ extern "C" int b200_rowfused_fwd_bwd(const float* x, const float* a, const float
   shape_for(cols, T, V);
   const int64_t grid = grid_for(rows, cols);
   int rc;
-  if (V == 4) {
+  if (V == 8) {
     switch (T) {
-      case 32: rc = launch<32, 4>(P, grid, s); break;
-      case 64: rc = launch<64, 4>(P, grid, s); break;
-      case 128: rc = launch<128, 4>(P, grid, s); break;
-      case 256: rc = launch<256, 4>(P, grid, s); break;
-      case 512: rc = launch<512, 4>(P, grid, s); break;
-      default: rc = launch<1024, 4>(P, grid, s); break;
+      case 32: rc = launch<32, 8>(P, grid, s); break;
+      case 64: rc = launch<64, 8>(P, grid, s); break;
+      case 128: rc = launch<128, 8>(P, grid, s); break;
+      case 256: rc = launch<256, 8>(P, grid, s); break;
+      default: rc = launch<512, 8>(P, grid, s); break;
     }
-  } else if (V == 8) {
-    rc = launch<1024, 8>(P, grid, s);
   } else {
-    rc = launch<1024, 16>(P, grid, s);
+    switch (T) {
+      case 512: rc = launch<512, 16>(P, grid, s); break;
+      default: rc = launch<1024, 16>(P, grid, s); break;
+    }
   }
   if (rc) return rc;
   dim3 g2((unsigned)ceil_div(cols, 256), P.want_gb ? 4 : 2);

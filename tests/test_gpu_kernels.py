@@ -250,3 +250,25 @@ def test_device_error_flag_for_bad_index():
     assert rc == L.ERR_ARG
     assert L.lib().b200_check_device_error(ops.stream_ptr()) == L.OK  # flag cleared
     del y
+
+
+def test_mask_mul_colsum_bf16_and_f32():
+    from b200 import _lib as L
+    from b200 import ops
+
+    r = rng(11)
+    for R, C in ((37, 2048), (5, 13), (1000, 24)):
+        g = r.standard_normal((R, C), dtype=np.float32)
+        m = r.random((R, C)) > 0.5
+        ref = g * m
+        ws_b = int(L.lib().b200_mask_mul_colsum_workspace_bytes(R, C))
+        ws = torch.empty(max(1, ws_b), dtype=torch.uint8, device="cuda")
+        yb = torch.empty(R, C, dtype=torch.bfloat16, device="cuda")
+        yf = torch.empty(R, C, dtype=torch.float32, device="cuda")
+        cs = torch.empty(C, dtype=torch.float32, device="cuda")
+        G, M = T(g), T(m)
+        L.call("b200_mask_mul_colsum", G.data_ptr(), M.data_ptr(), yb.data_ptr(), yf.data_ptr(), cs.data_ptr(), R, C,
+               ws.data_ptr(), ws_b, ops.stream_ptr())
+        np.testing.assert_array_equal(to_np(yf), ref)
+        np.testing.assert_allclose(to_np(yb), ref, rtol=8e-3, atol=1e-6)
+        np.testing.assert_allclose(to_np(cs), ref.sum(0), rtol=1e-5, atol=1e-4)
