@@ -57,7 +57,11 @@ WORKLOADS = {
     "mlp": {"graph": "mlp_full", "dtype": "f32", "params": ["W1", "b1", "W2", "b2"], "reduce": "mean",
             "desc": "2-layer MLP x[64,784] 784->256->10 softmax CE fwd+bwd"},
     "cnn": {"graph": "cnn_full", "dtype": "bf16", "params": ["w1", "w2", "w3", "Wl", "bl"], "reduce": "mean",
+            "dp_graphs": {2: "cnn_n256", 4: "cnn_n128", 8: "cnn_n64"},
             "desc": "small CNN [512,3,32,32] 3 conv3x3 + GAP + linear, softmax CE fwd+bwd"},
+    "transformer": {"graph": "transformer_full", "dtype": "bf16", "params": "all", "reduce": "mean",
+                    "dp_graphs": {2: "transformer_b32", 4: "transformer_b16", 8: "transformer_b8"},
+                    "desc": "pre-LN transformer encoder 4x(d1024,h16,ffn4096) seq 512, global batch 64, next-token CE fwd+bwd"},
 }
 
 
@@ -225,10 +229,14 @@ def run_gpu(args) -> None:
     spec = WORKLOADS[args.workload]
     ops.Config.matmul_dtype = "bf16" if spec["dtype"] == "bf16" else "f32"
     ops.Config.conv_dtype = ops.Config.matmul_dtype
-    g = G.load(spec["graph"])
-    arrays = make_inputs(g.meta["workload"], g.meta["dims"], seed=rank)  # each rank: its own batch
-    param_ids = [g.roles[r] for r in spec["params"]]
-    grad_ids = [g.output_names["d_" + r] for r in spec["params"]]
+    # strong scaling (fixed global batch split over ranks) where a per-rank graph exists,
+    # weak scaling (one full batch per rank) otherwise
+    strong = world > 1 and world in spec.get("dp_graphs", {})
+    g = G.load(spec["dp_graphs"][world] if strong else spec["graph"])
+    arrays = make_inputs(g.meta["workload"], g.meta["dims"], seed=rank)  # each rank: its own shard
+    params = [k[2:] for k in g.output_names if k.startswith("d_")] if spec["params"] == "all" else spec["params"]
+    grad_ids = [g.output_names["d_" + r] for r in params]
+    scale_grads = strong and spec.get("reduce") == "mean"
 
     dev = torch.device("cuda", local)
     # bf16 workloads feed their bf16 operands as bf16 tensors (the values are bf16-exact)
@@ -249,8 +257,10 @@ def run_gpu(args) -> None:
 
     def allreduce():
         if dist is not None:
+            # data-parallel gradient exchange over NCCL (NVLink); a mean loss over the global
+            # batch is the average of the per-shard means
             for gid in grad_ids:
-                dist.all_reduce(out[gid])
+                dist.all_reduce(out[gid], op=dist.ReduceOp.AVG if scale_grads else dist.ReduceOp.SUM)
 
     stream = torch.cuda.current_stream()
     for _ in range(args.warmup):
@@ -275,7 +285,7 @@ def run_gpu(args) -> None:
     if dist is not None:
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
     ms_max = float(t.item())
-    value = world * args.steps / (ms_max / 1000.0)
+    value = (1 if strong else world) * args.steps / (ms_max / 1000.0)
 
     # dominant kernel alone, CUDA events on its stream (roofline)
     roof = None
@@ -318,7 +328,7 @@ def run_gpu(args) -> None:
         for r in bf16_roles:
             host[g.roles[r]] = host[g.roles[r]].to(torch.bfloat16)
         host = {k: v.pin_memory() for k, v in host.items()}
-        res_ids = [g.output_names[k] for k in g.output_names if k.startswith("d_") and k[2:] in spec["params"]]
+        res_ids = [g.output_names[k] for k in g.output_names if k.startswith("d_") and k[2:] in params]
         if "argmax" in g.output_names:
             res_ids.append(g.output_names["argmax"])
         if "loss" in g.output_names:
@@ -351,7 +361,7 @@ def run_gpu(args) -> None:
         et = torch.tensor([a.elapsed_time(b)], device=dev)
         if dist is not None:
             dist.all_reduce(et, op=dist.ReduceOp.MAX)
-        e2e = {"value": round(world * args.steps / (float(et.item()) / 1000.0), 3), "unit": "steps/s",
+        e2e = {"value": round((1 if strong else world) * args.steps / (float(et.item()) / 1000.0), 3), "unit": "steps/s",
                "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h}
 
     cpu = None
@@ -368,11 +378,11 @@ def run_gpu(args) -> None:
             "warmup": args.warmup,
             "ms_per_step": round(ms_max / args.steps, 4),
             "higher_is_better": True,
-            "scaling": "weak",
+            "scaling": "strong" if strong else "weak",
             "vs_baseline": None,
             "dtype": spec["dtype"],
             "data": "synthetic (seeded numpy, per-rank seed)",
-            "config": {"workload": spec["desc"], "graph": spec["graph"], "dims": g.meta["dims"],
+            "config": {"workload": spec["desc"], "graph": spec["dp_graphs"][world] if strong else spec["graph"], "dims": g.meta["dims"],
                        "parallelism": f"dp{world}" if world > 1 else "single",
                        "l2": "inputs larger than the 126 MB L2 (no flush needed)" if args.workload in ("rowfused", "bmm") else "L2 not flushed",
                        "replay": "CUDA graph of the fused plan"},

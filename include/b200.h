@@ -239,6 +239,15 @@ size_t b200_mask_mul_colsum_workspace_bytes(int64_t rows, int64_t cols);
 int b200_mask_mul_colsum(const float* g, const uint8_t* mask, void* y_bf16, float* y_f32, float* colsum, int64_t rows,
                          int64_t cols, void* workspace, size_t workspace_bytes, void* stream);
 
+/* Fused LogSoftmax (numpy/eager/math_advanced/math_log_exp.py:87-104) -> TakeAlongAxis of
+ * one label per row (numpy/eager/advanced_indexing.py:163-177) and its VJP (ZerosLike +
+ * ScatterAdd advanced_indexing.py:309-326, then the LogSoftmax rule g - exp(ls) sum(g)):
+ *   picked[r] = ls[r, label[r]],  dx[r, j] = d[r] ([j == label[r]] - softmax(x)[r, j]).
+ * x [rows, cols] (F32 or BF16), label [rows] int64, d [rows] fp32 (cotangent of picked).
+ * picked, ls (the full log-softmax) and dx may each be NULL. */
+int b200_logsoftmax_pick(int x_dtype, const void* x, const int64_t* label, const float* d, float* picked, float* ls,
+                         float* dx, int64_t rows, int64_t cols, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -417,6 +417,70 @@ def mask_bwd_step(m: Match, meta: dict[str, Meta]) -> Step:
 
 
 # ----------------------------------------------------------------------------------
+# pattern: LogSoftmax -> TakeAlongAxis (label pick) and the VJP chain
+#   ZerosLike + ScatterAdd + (g - exp(ls) * sum(g))  ->  one kernel
+# ----------------------------------------------------------------------------------
+def find_xent(g: Graph, live: dict[str, Node], meta: dict[str, Meta], users: dict[str, list[str]],
+              outputs: set[str]) -> list[Match]:
+    x, labels, d = Var("x"), Var("labels"), Var("d")
+    ls = Op("LogSoftmax", x, name="ls", attrs={"axis": _last_axis})
+    dls = Op("ScatterAdd", Op("ZerosLike", ls, name="z"), labels, d, name="dls", attrs={"dim": lambda v: v in (-1, None) or v == -1})
+    s = Op("ReduceSum", dls, name="s", attrs={"axis": _last_axis, "keepdims": True})
+    root = Op("Subtract", dls, Op("Multiply", Op("Exp", ls, name="e"), s, name="es"), name="dx")
+    found = []
+    for nid, node in live.items():
+        if _op_name(node) != "Subtract":
+            continue
+        bind: dict[str, str] = {}
+        cov: set[str] = set()
+        if not match(root, nid, g, bind, cov):
+            continue
+        mx, ml, md = meta.get(bind["x"]), meta.get(bind["labels"]), meta.get(bind["d"])
+        if mx is None or mx.scalar or len(mx.shape) < 1 or mx.dtype not in (torch.float32, torch.bfloat16):
+            continue
+        R = math.prod(mx.shape[:-1])
+        if ml is None or ml.dtype != torch.int64 or ml.shape != tuple(mx.shape[:-1]) + (1,):
+            continue
+        if md is None or md.scalar or md.shape != ml.shape or md.dtype != torch.float32:
+            continue
+        outs = {"dx": bind["dx"]}
+        for u in users.get(bind["ls"], []):
+            un = live.get(u)
+            if un is not None and _op_name(un) == "TakeAlongAxis" and un.inputs == [bind["ls"], bind["labels"]] and _last_axis(un.attributes.get("axis", -1)):
+                outs["picked"] = u
+                cov.add(u)
+        produced = set(outs.values())
+        leak = [c for c in cov if c not in produced and (c in outputs or any(u not in cov for u in users.get(c, [])))]
+        if leak:
+            continue
+        del R
+        found.append(Match("xent", bind, cov, outs))
+    return found
+
+
+def xent_step(m: Match, meta: dict[str, Meta]) -> Step:
+    b, o = m.bind, m.outputs
+    shape = meta[b["x"]].shape
+    V = shape[-1]
+    R = math.prod(shape[:-1])
+
+    def run(env: dict) -> None:
+        x = ops.contiguous(env[b["x"]])
+        lab = ops.contiguous(env[b["labels"]])
+        d = ops.contiguous(ops.cast(env[b["d"]], torch.float32))
+        dev = ops.device()
+        dx = torch.empty(shape, dtype=torch.float32, device=dev)
+        picked = torch.empty(tuple(shape[:-1]) + (1,), dtype=torch.float32, device=dev) if "picked" in o else None
+        L.call("b200_logsoftmax_pick", ops.code(x), x.data_ptr(), lab.data_ptr(), d.data_ptr(),
+               None if picked is None else picked.data_ptr(), None, dx.data_ptr(), R, V, ops.stream_ptr())
+        env[o["dx"]] = dx
+        if picked is not None:
+            env[o["picked"]] = picked
+
+    return Step(list(o.values()), [b["x"], b["labels"], b["d"]], run, "xent_fwd_bwd")
+
+
+# ----------------------------------------------------------------------------------
 # elementwise clustering (subsystem 1)
 # ----------------------------------------------------------------------------------
 EW_UNARY = {"Negative": "NEG", "Exp": "EXP", "Log": "LOG", "Tanh": "TANH", "Sqrt": "SQRT", "Relu": "RELU", "Gelu": "GELU",
@@ -630,6 +694,12 @@ def plan_steps(graph: Graph, nodes: list[Node], sample: dict[str, Any]) -> list[
         if m.covered & taken:
             continue
         groups.append((sorted(m.covered), gemm_epilogue_step(m)))
+        taken |= m.covered
+
+    for m in find_xent(graph, live, meta, users, outputs):
+        if m.covered & taken:
+            continue
+        groups.append((sorted(m.covered), xent_step(m, meta)))
         taken |= m.covered
 
     for m in find_mask_bwd(graph, live, meta, users, outputs):

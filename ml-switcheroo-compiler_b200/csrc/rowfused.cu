@@ -229,7 +229,7 @@ __device__ __forceinline__ void cp_async_wait() { asm volatile("cp.async.wait_gr
 // accumulators. x and c of the current and the next row sit in this thread's own
 // shared-memory slot, prefetched with cp.async one row ahead (double-buffered).
 template <int T, int V, bool GB, bool RAGGED>
-__global__ void __launch_bounds__(T, T <= 256 ? 512 / T : 1) rowfused_kernel(const __grid_constant__ Params P) {
+__global__ void __launch_bounds__(T, (V == 4 ? 1024 : 512) / T > 0 ? (V == 4 ? 1024 : 512) / T : 1) rowfused_kernel(const __grid_constant__ Params P) {
   constexpr int NW = T / 32;
   constexpr int H = V / 2;
   __shared__ __align__(16) float sh[72];
@@ -530,19 +530,20 @@ int launch(const Params& P, int64_t grid, cudaStream_t s) {
   return check_launch("rowfused");
 }
 
-// threads per CTA for a row length: 8 columns per thread (16 above 4096 columns)
+// threads per CTA for a row length: 4 columns per thread up to 4096 columns (32 warps
+// per SM hide the reduction and transcendental latencies), 8 up to 8192, then 16
 inline void shape_for(int64_t cols, int& T, int& V) {
-  V = cols <= 4096 ? 8 : 16;
+  V = cols <= 4096 ? 4 : (cols <= 8192 ? 8 : 16);
   const int64_t t = (cols + V - 1) / V;
   T = 32;
   while (T < t) T *= 2;
 }
 
-// 512 resident threads per SM (128 registers each)
+// 1024 resident threads per SM for V = 4 (64 registers each), 512 otherwise
 inline int64_t grid_for(int64_t rows, int64_t cols) {
   int T, V;
   shape_for(cols, T, V);
-  const int64_t per_sm = T <= 256 ? 512 / T : 1;
+  const int64_t per_sm = V == 4 ? std::max(1, 1024 / T) : std::max(1, 512 / T);
   return std::max<int64_t>(1, std::min<int64_t>(rows, (int64_t)num_sms() * per_sm));
 }
 
@@ -588,19 +589,19 @@ extern "C" int b200_rowfused_fwd_bwd(const float* x, const float* a, const float
   shape_for(cols, T, V);
   const int64_t grid = grid_for(rows, cols);
   int rc;
-  if (V == 8) {
+  if (V == 4) {
     switch (T) {
-      case 32: rc = launch<32, 8>(P, grid, s); break;
-      case 64: rc = launch<64, 8>(P, grid, s); break;
-      case 128: rc = launch<128, 8>(P, grid, s); break;
-      case 256: rc = launch<256, 8>(P, grid, s); break;
-      default: rc = launch<512, 8>(P, grid, s); break;
+      case 32: rc = launch<32, 4>(P, grid, s); break;
+      case 64: rc = launch<64, 4>(P, grid, s); break;
+      case 128: rc = launch<128, 4>(P, grid, s); break;
+      case 256: rc = launch<256, 4>(P, grid, s); break;
+      case 512: rc = launch<512, 4>(P, grid, s); break;
+      default: rc = launch<1024, 4>(P, grid, s); break;
     }
+  } else if (V == 8) {
+    rc = launch<1024, 8>(P, grid, s);
   } else {
-    switch (T) {
-      case 512: rc = launch<512, 16>(P, grid, s); break;
-      default: rc = launch<1024, 16>(P, grid, s); break;
-    }
+    rc = launch<1024, 16>(P, grid, s);
   }
   if (rc) return rc;
   dim3 g2((unsigned)ceil_div(cols, 256), P.want_gb ? 4 : 2);

@@ -272,3 +272,28 @@ def test_mask_mul_colsum_bf16_and_f32():
         np.testing.assert_array_equal(to_np(yf), ref)
         np.testing.assert_allclose(to_np(yb), ref, rtol=8e-3, atol=1e-6)
         np.testing.assert_allclose(to_np(cs), ref.sum(0), rtol=1e-5, atol=1e-4)
+
+
+@pytest.mark.parametrize("R,V", [(7, 10), (64, 32000), (3, 1)])
+def test_logsoftmax_pick_fwd_bwd(R, V):
+    from b200 import _lib as L
+    from b200 import ops
+    from oracle import evaluator as O
+
+    r = rng(12)
+    x = (r.standard_normal((R, V)) * 3).astype(np.float32)
+    lab = r.integers(0, V, (R, 1))
+    d = r.standard_normal((R, 1)).astype(np.float32)
+    ls = O.execute_op("LogSoftmax", x, axis=-1)
+    picked_ref = O.execute_op("TakeAlongAxis", ls, lab, axis=-1)
+    dls = O.execute_op("ScatterAdd", np.zeros_like(ls), lab, d, dim=-1)
+    dx_ref = dls - np.exp(ls) * dls.sum(-1, keepdims=True)
+    X, LB, D = T(x), T(lab), T(d)
+    picked = torch.empty(R, 1, device="cuda")
+    dx = torch.empty(R, V, device="cuda")
+    lsd = torch.empty(R, V, device="cuda")
+    L.call("b200_logsoftmax_pick", L.F32, X.data_ptr(), LB.data_ptr(), D.data_ptr(), picked.data_ptr(), lsd.data_ptr(),
+           dx.data_ptr(), R, V, ops.stream_ptr())
+    np.testing.assert_allclose(to_np(picked), picked_ref, rtol=1e-5, atol=1e-5)
+    np.testing.assert_allclose(to_np(lsd), ls, rtol=1e-5, atol=1e-5)
+    np.testing.assert_allclose(to_np(dx), dx_ref, rtol=1e-4, atol=1e-6)

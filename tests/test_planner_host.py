@@ -131,3 +131,23 @@ def test_schedule_orders_fused_groups():
     s3 = Step(["d"], ["c", "a"], lambda e: None, "s3")
     order = _schedule([(["d"], s3), (["c"], s2), (["b"], s1)])
     assert [s.label for s in order] == ["s1", "s2", "s3"]
+
+
+@pytest.mark.parametrize("case", ["mlp_small", "cnn_small", "transformer_small"])
+def test_xent_pattern_matches_reference_graphs(case):
+    from b200.fusion import find_xent
+
+    g, meta = _meta_from_oracle(case)
+    need, stack = set(), list(g.outputs)
+    while stack:
+        v = stack.pop()
+        if v not in need and v in g.nodes:
+            need.add(v)
+            stack.extend(g.nodes[v].inputs)
+    live = {n.id: n for n in g.topo_order() if n.op_type != "Input" and n.id in need}
+    users = {}
+    for n in live.values():
+        for i in n.inputs:
+            users.setdefault(i, []).append(n.id)
+    found = find_xent(g, live, meta, users, set(g.outputs))
+    assert len(found) == 1 and set(found[0].outputs) == {"dx", "picked"}
