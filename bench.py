@@ -343,7 +343,7 @@ def run_gpu(args) -> None:
             o = fn(dv)
             if dist is not None:
                 for gid in grad_ids:
-                    dist.all_reduce(o[gid])
+                    dist.all_reduce(o[gid], op=dist.ReduceOp.AVG if scale_grads else dist.ReduceOp.SUM)
             for k in res_ids:
                 host_out[k].copy_(o[k], non_blocking=True)
 

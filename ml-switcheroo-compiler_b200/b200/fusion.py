@@ -665,6 +665,51 @@ def ew_cluster_step(g: Graph, nodes: list[Node], meta: dict[str, Meta], users, o
 
 
 # ----------------------------------------------------------------------------------
+# shape-only operands: BroadcastLike's target, ZerosLike/OnesLike/Numel's operand are
+# read for their shape only. With shapes fixed per plan, these edges are not data
+# dependencies (dropping them lets e.g. the loss cotangent be computed before the fused
+# cross-entropy kernel that produces the forward value it takes the shape of).
+# ----------------------------------------------------------------------------------
+SHAPE_ONLY = {"BroadcastLike": (1,), "ZerosLike": (0,), "OnesLike": (0,), "Numel": (0,)}
+
+
+def data_inputs(n: Node) -> list[str]:
+    so = SHAPE_ONLY.get(_op_name(n), ())
+    return [i for k, i in enumerate(n.inputs) if k not in so]
+
+
+def shape_only_step(n: Node, meta: dict[str, Meta]) -> Step:
+    op = _op_name(n)
+    nid = n.id
+    if op == "BroadcastLike":
+        src = n.inputs[0]
+        shape = meta[n.inputs[1]].shape
+
+        def run(env: dict) -> None:
+            v = env[src]
+            if not isinstance(v, torch.Tensor):
+                env[nid] = ops.full(shape, float(v))
+            else:
+                env[nid] = v if tuple(v.shape) == tuple(shape) else v.expand(shape)
+
+        return Step([nid], [src], run, "BroadcastLike")
+    if op in ("ZerosLike", "OnesLike"):
+        shape, dtype = meta[n.inputs[0]].shape, meta[n.inputs[0]].dtype
+        val = 0.0 if op == "ZerosLike" else 1.0
+
+        def run(env: dict) -> None:
+            env[nid] = ops.full(shape, val, dtype)
+
+        return Step([nid], [], run, op)
+    numel = float(math.prod(meta[n.inputs[0]].shape)) if not meta[n.inputs[0]].scalar else 1.0
+
+    def run_numel(env: dict) -> None:
+        env[nid] = numel
+
+    return Step([nid], [], run_numel, "Numel")
+
+
+# ----------------------------------------------------------------------------------
 # planning
 # ----------------------------------------------------------------------------------
 def plan_steps(graph: Graph, nodes: list[Node], sample: dict[str, Any]) -> list[Step]:
@@ -672,7 +717,7 @@ def plan_steps(graph: Graph, nodes: list[Node], sample: dict[str, Any]) -> list[
     live = {n.id: n for n in nodes}
     users: dict[str, list[str]] = {}
     for n in nodes:
-        for i in n.inputs:
+        for i in data_inputs(n):
             users.setdefault(i, []).append(n.id)
     outputs = set(graph.outputs)
     taken: set[str] = set()
@@ -722,7 +767,10 @@ def plan_steps(graph: Graph, nodes: list[Node], sample: dict[str, Any]) -> list[
         if n.id not in taken:
             if n.op_type == "Constant" and all(u in taken for u in users.get(n.id, [])) and n.id not in outputs:
                 continue
-            groups.append(([n.id], node_step(n)))
+            if _op_name(n) in SHAPE_ONLY:
+                groups.append(([n.id], shape_only_step(n, meta)))
+            else:
+                groups.append(([n.id], node_step(n)))
     return _schedule(groups)
 
 

@@ -120,6 +120,34 @@ __device__ __forceinline__ unsigned long long bmaxkey(unsigned long long k, floa
   __syncthreads();
   return r;
 }
+// sum of a float and max of a 64-bit key in one block reduction
+template <int NW>
+__device__ __forceinline__ void bsum_maxkey(float& v, unsigned long long& k, float* sh) {
+  unsigned long long* s64 = reinterpret_cast<unsigned long long*>(sh);
+  v = warp_sum(v);
+  k = warp_maxkey(k);
+  const int lane = threadIdx.x & 31, w = threadIdx.x >> 5;
+  if (lane == 0) {
+    s64[w] = k;        // keys in sh[0 .. 2 NW)
+    sh[68 + w] = v;    // sums in sh[68 .. 68 + NW)
+  }
+  __syncthreads();
+  if (w == 0) {
+    unsigned long long t = lane < NW ? s64[lane] : 0ull;
+    float f = lane < NW ? sh[68 + lane] : 0.f;
+    t = warp_maxkey(t);
+    f = warp_sum(f);
+    if (lane == 0) {
+      s64[32] = t;
+      sh[66] = f;
+    }
+  }
+  __syncthreads();
+  k = s64[32];
+  v = sh[66];
+  __syncthreads();
+}
+
 template <int NW>
 __device__ __forceinline__ float bmax(float v, float* sh) {
   v = warp_max(v);
@@ -232,8 +260,8 @@ template <int T, int V, bool GB, bool RAGGED>
 __global__ void __launch_bounds__(T, (V == 4 ? 1024 : 512) / T > 0 ? (V == 4 ? 1024 : 512) / T : 1) rowfused_kernel(const __grid_constant__ Params P) {
   constexpr int NW = T / 32;
   constexpr int H = V / 2;
-  __shared__ __align__(16) float sh[72];
-  extern __shared__ __align__(16) float sm[];  // [2 stages][T][2V]: x then c
+  __shared__ __align__(16) float sh[104];
+  extern __shared__ __align__(16) float sm[];  // [2 stages][x, c][T][V] (a warp's slices are contiguous)
   const int64_t C = P.cols;
   const int c0 = threadIdx.x * V;
   const bool full = c0 + V <= C;
@@ -250,6 +278,29 @@ __global__ void __launch_bounds__(T, (V == 4 ? 1024 : 512) / T > 0 ? (V == 4 ? 1
   ldg_pairs<V>(b, P.b, c0, C, vec, 0.f);
   ldg_pairs<V>(ga, P.gamma, c0, C, vec, 1.f);
   ldg_pairs<V>(be, P.beta, c0, C, vec, 0.f);
+  // Softmax shift: for n = gamma * x_hat + beta with every gamma >= 0, each row max lies in
+  // [min beta, max gamma * sqrt(C) + max beta] (|x_hat| <= sqrt(C), max x_hat >= 0). When
+  // that interval is at most 80 wide, exp(n - S) with S its top never overflows and the
+  // largest term never underflows, so the per-row max reduction is not needed.
+  float shiftS = 0.f;
+  bool use_shift;
+  {
+    float gmin = INFINITY, gmx = -INFINITY, bmn = INFINITY, bmx = -INFINITY;
+#pragma unroll
+    for (int i = 0; i < H; ++i) {
+      float g0, g1, b0, b1;
+      upk(ga[i], g0, g1);
+      upk(be[i], b0, b1);
+      if (c0 + 2 * i < C) { gmin = fminf(gmin, g0); gmx = fmaxf(gmx, g0); bmn = fminf(bmn, b0); bmx = fmaxf(bmx, b0); }
+      if (c0 + 2 * i + 1 < C) { gmin = fminf(gmin, g1); gmx = fmaxf(gmx, g1); bmn = fminf(bmn, b1); bmx = fmaxf(bmx, b1); }
+    }
+    gmin = -bmax<NW>(-gmin, sh);
+    gmx = bmax<NW>(gmx, sh);
+    bmn = -bmax<NW>(-bmn, sh);
+    bmx = bmax<NW>(bmx, sh);
+    shiftS = gmx * sqrtf((float)C) + bmx;
+    use_shift = gmin >= 0.f && (shiftS - bmn) <= 80.f && isfinite(shiftS);
+  }
   F2 acc_da[H], acc_db[H], acc_dg[GB ? H : 1], acc_dbe[GB ? H : 1];
 #pragma unroll
   for (int i = 0; i < H; ++i) {
@@ -259,21 +310,22 @@ __global__ void __launch_bounds__(T, (V == 4 ? 1024 : 512) / T > 0 ? (V == 4 ? 1
 
   auto prefetch = [&](int64_t row, int stage) {
     if (row < P.rows) {
-      float* dst = sm + ((size_t)stage * T + threadIdx.x) * 2 * V;
+      float* dx_ = sm + ((size_t)stage * 2 * T + threadIdx.x) * V;
+      float* dc_ = dx_ + (size_t)T * V;
       const float* xr = P.x + row * C + c0;
       const float* cr = P.c + row * C + c0;
       if (vec) {
 #pragma unroll
         for (int i = 0; i < V; i += 4) {
-          cp_async16(dst + i, xr + i);
-          cp_async16(dst + V + i, cr + i);
+          cp_async16(dx_ + i, xr + i);
+          cp_async16(dc_ + i, cr + i);
         }
       } else {
 #pragma unroll
         for (int i = 0; i < V; ++i) {
           const bool ok = c0 + i < C;
-          cp_async4(dst + i, ok ? xr + i : P.x, ok);
-          cp_async4(dst + V + i, ok ? cr + i : P.c, ok);
+          cp_async4(dx_ + i, ok ? xr + i : P.x, ok);
+          cp_async4(dc_ + i, ok ? cr + i : P.c, ok);
         }
       }
     }
@@ -312,8 +364,8 @@ __global__ void __launch_bounds__(T, (V == 4 ? 1024 : 512) / T > 0 ? (V == 4 ? 1
   for (int64_t row = blockIdx.x; row < P.rows; row += G, stage ^= 1) {
     prefetch(row + G, stage ^ 1);
     cp_async_wait<1>();
-    const float* xs = sm + ((size_t)stage * T + threadIdx.x) * 2 * V;
-    const float* cs = xs + V;
+    const float* xs = sm + ((size_t)stage * 2 * T + threadIdx.x) * V;
+    const float* cs = xs + (size_t)T * V;
     F2 w[H], t[H];
     // ---- forward: p = x a + b ; t = tanh(k p (1 + c p^2)) ; w = g = 0.5 p (1 + t)
     F2 s2 = sp(0.f), q2 = sp(0.f);
@@ -338,25 +390,32 @@ __global__ void __launch_bounds__(T, (V == 4 ? 1024 : 512) / T > 0 ? (V == 4 ? 1
     const float mean = SG.a * invC;
     const float rstd = rsqrtf(fmaxf(SG.b * invC - mean * mean, 0.f) + P.eps);
     const F2 nmr = sp(-mean * rstd), rs = sp(rstd);
-    // w = n = LayerNorm(g); row max and the index of its first occurrence
-    unsigned long long mk = 0ull;
+    // w = n = LayerNorm(g); row max (skipped on the shift path) with its first index
+    float M;
+    int jn = 0;
 #pragma unroll
-    for (int i = 0; i < H; ++i) {
-      w[i] = fma2(fma2(w[i], rs, nmr), ga[i], be[i]);
-      float u0, u1;
-      upk(w[i], u0, u1);
-      if (!RAGGED || c0 + 2 * i < C) {
-        const unsigned long long k0 = order_key(u0, c0 + 2 * i);
-        mk = k0 > mk ? k0 : mk;
+    for (int i = 0; i < H; ++i) w[i] = fma2(fma2(w[i], rs, nmr), ga[i], be[i]);
+    if (!use_shift) {
+      unsigned long long mk = 0ull;
+#pragma unroll
+      for (int i = 0; i < H; ++i) {
+        float u0, u1;
+        upk(w[i], u0, u1);
+        if (!RAGGED || c0 + 2 * i < C) {
+          const unsigned long long k0 = order_key(u0, c0 + 2 * i);
+          mk = k0 > mk ? k0 : mk;
+        }
+        if (!RAGGED || c0 + 2 * i + 1 < C) {
+          const unsigned long long k1 = order_key(u1, c0 + 2 * i + 1);
+          mk = k1 > mk ? k1 : mk;
+        }
       }
-      if (!RAGGED || c0 + 2 * i + 1 < C) {
-        const unsigned long long k1 = order_key(u1, c0 + 2 * i + 1);
-        mk = k1 > mk ? k1 : mk;
-      }
+      mk = bmaxkey<NW>(mk, sh);
+      M = key_value(mk);
+      jn = key_index(mk);  // first index of max(n)
+    } else {
+      M = shiftS;
     }
-    mk = bmaxkey<NW>(mk, sh);
-    const float M = key_value(mk);
-    const int jn = key_index(mk);  // first index of max(n)
     // w = exp(n - M)
     F2 se2 = sp(0.f);
     {
@@ -371,8 +430,7 @@ __global__ void __launch_bounds__(T, (V == 4 ? 1024 : 512) / T > 0 ? (V == 4 ? 1
     }
     upk(se2, sa, sb);
     const float inv = 1.f / bsum<NW>(sa + sb, sh);
-    // w = y ; sum(c*y). argmax(y) is argmax(n) unless rounding made some y exactly equal to
-    // y[jn] at a smaller index: detected with one block-wide OR, then resolved exactly.
+    // w = y ; sum(c*y) ; argmax(y), first max wins
     F2 cy2 = sp(0.f);
     {
       F2 c[H];
@@ -384,21 +442,42 @@ __global__ void __launch_bounds__(T, (V == 4 ? 1024 : 512) / T > 0 ? (V == 4 ? 1
         cy2 = fma2(c[i], w[i], cy2);
       }
     }
-    if (jn >= c0 && jn < c0 + V) {
+    upk(cy2, sa, sb);
+    float cy;
+    int yj;
+    if (use_shift) {
+      // exact argmax of y: its key max travels with the sum of c*y
+      unsigned long long yk = 0ull;
 #pragma unroll
       for (int i = 0; i < H; ++i) {
         float u0, u1;
         upk(w[i], u0, u1);
-        if (c0 + 2 * i == jn) sh[70] = u0;
-        if (c0 + 2 * i + 1 == jn) sh[70] = u1;
+        if (!RAGGED || c0 + 2 * i < C) {
+          const unsigned long long k0 = order_key(u0, c0 + 2 * i);
+          yk = k0 > yk ? k0 : yk;
+        }
+        if (!RAGGED || c0 + 2 * i + 1 < C) {
+          const unsigned long long k1 = order_key(u1, c0 + 2 * i + 1);
+          yk = k1 > yk ? k1 : yk;
+        }
       }
-    }
-    upk(cy2, sa, sb);
-    const float cy = bsum<NW>(sa + sb, sh);  // its barriers also publish sh[70] = y[jn]
-    int yj = jn;
-    {
+      cy = sa + sb;
+      bsum_maxkey<NW>(cy, yk, sh);
+      yj = key_index(yk);
+    } else {
+      // argmax(y) is argmax(n) unless rounding made some y beat y[jn]: one block-wide OR
+      if (jn >= c0 && jn < c0 + V) {
+#pragma unroll
+        for (int i = 0; i < H; ++i) {
+          float u0, u1;
+          upk(w[i], u0, u1);
+          if (c0 + 2 * i == jn) sh[70] = u0;
+          if (c0 + 2 * i + 1 == jn) sh[70] = u1;
+        }
+      }
+      cy = bsum<NW>(sa + sb, sh);  // its barriers also publish sh[70] = y[jn]
+      yj = jn;
       const float ymax = sh[70];
-      // any y that beats y[jn] under "first max wins": >= before jn, > after jn
       int tie = 0;
 #pragma unroll
       for (int i = 0; i < H; ++i) {

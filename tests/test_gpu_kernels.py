@@ -297,3 +297,51 @@ def test_logsoftmax_pick_fwd_bwd(R, V):
     np.testing.assert_allclose(to_np(picked), picked_ref, rtol=1e-5, atol=1e-5)
     np.testing.assert_allclose(to_np(lsd), ls, rtol=1e-5, atol=1e-5)
     np.testing.assert_allclose(to_np(dx), dx_ref, rtol=1e-4, atol=1e-6)
+
+
+@pytest.mark.parametrize("C,path", [(4096, "shift"), (4096, "general"), (1000, "general"), (77, "shift"), (6000, "general")])
+def test_rowfused_kernel_both_softmax_paths(C, path):
+    """The fused row kernel against the oracle: gamma = 1 / beta = 0 takes the fixed-shift
+    softmax path, signed gamma / wide beta the per-row max path; dgamma/dbeta outputs on."""
+    from b200 import _lib as L
+    from b200 import ops
+    from oracle import evaluator as O
+
+    r = rng(13)
+    R = 37
+    x = r.standard_normal((R, C), dtype=np.float32)
+    a = r.uniform(0.5, 1.5, C).astype(np.float32)
+    b = (r.standard_normal(C) * 0.1).astype(np.float32)
+    if path == "shift":
+        gamma, beta = np.ones(C, np.float32), np.zeros(C, np.float32)
+    else:
+        gamma = r.uniform(-1.5, 1.5, C).astype(np.float32)
+        beta = (r.standard_normal(C) * 30).astype(np.float32)
+    cot = r.standard_normal((R, C), dtype=np.float32)
+    g = O.execute_op("Gelu", x * a + b)
+    n = O.execute_op("LayerNorm", g, gamma, beta, eps=1e-5)
+    y = O.execute_op("Softmax", n, axis=-1)
+    dn = y * (cot - (cot * y).sum(-1, keepdims=True))
+    dg = O.execute_op("LayerNormInputGrad", dn, g, gamma, eps=1e-5)
+    p = x * a + b
+    k, c_ = np.sqrt(2 / np.pi), 0.044715
+    t = np.tanh(k * (p + c_ * p**3))
+    dp = dg * (0.5 * (1 + t) + 0.5 * p * (1 - t * t) * k * (1 + 3 * c_ * p * p))
+    refs = {"y": y, "dx": dp * a, "da": (dp * x).sum(0), "db": dp.sum(0),
+            "dgamma": O.execute_op("LayerNormGammaGrad", dn, g, eps=1e-5), "dbeta": dn.sum(0)}
+    dev = "cuda"
+    out = {k_: torch.empty(R, C, device=dev) for k_ in ("y", "dx")}
+    out.update({k_: torch.empty(C, device=dev) for k_ in ("da", "db", "dgamma", "dbeta")})
+    am = torch.empty(R, dtype=torch.int64, device=dev)
+    wsb = int(L.lib().b200_rowfused_workspace_bytes(R, C))
+    ws = torch.empty(wsb, dtype=torch.uint8, device=dev)
+    ins = [T(v) for v in (x, a, b, gamma, beta, cot)]
+    L.call("b200_rowfused_fwd_bwd", *[v.data_ptr() for v in ins], out["y"].data_ptr(), am.data_ptr(), out["dx"].data_ptr(),
+           out["da"].data_ptr(), out["db"].data_ptr(), out["dgamma"].data_ptr(), out["dbeta"].data_ptr(), R, C, 1e-5,
+           ws.data_ptr(), wsb, ops.stream_ptr())
+    for k_, ref in refs.items():
+        got = to_np(out[k_])
+        scale = float(np.abs(ref).max())
+        np.testing.assert_allclose(got, ref, rtol=1e-4, atol=1e-4 * scale, err_msg=k_)
+    ygot = to_np(out["y"])
+    np.testing.assert_array_equal(to_np(am), np.argmax(ygot, axis=-1))
