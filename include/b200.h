@@ -248,6 +248,23 @@ int b200_mask_mul_colsum(const float* g, const uint8_t* mask, void* y_bf16, floa
 int b200_logsoftmax_pick(int x_dtype, const void* x, const int64_t* label, const float* d, float* picked, float* ls,
                          float* dx, int64_t rows, int64_t cols, void* stream);
 
+/* Conv2D / Conv2DInputGrad / Conv2DWeightGrad (numpy/eager/conv.py:462-489, 634-697,
+ * 699-764) on the tcgen05 tensor cores: bf16 operands staged in `workspace` (im2col of
+ * the activations, packed weights / gradients), fp32 accumulation, fp32 NCHW / OIHW
+ * results. Same tensor arguments as the b200_conv2d_* entry points above; op = 0 fwd,
+ * 1 dgrad, 2 wgrad for the workspace query. */
+size_t b200_conv2d_tc_workspace_bytes(int op, int64_t N, int64_t C, int64_t H, int64_t W, int64_t O, int64_t KH, int64_t KW,
+                                      int64_t OH, int64_t OW, int64_t sh, int64_t sw, int64_t pt, int64_t pl);
+int b200_conv2d_fwd_tc(const float* x, const float* w, float* y, int64_t N, int64_t C, int64_t H, int64_t W, int64_t O,
+                       int64_t KH, int64_t KW, int64_t OH, int64_t OW, int64_t sh, int64_t sw, int64_t pt, int64_t pl,
+                       void* workspace, size_t workspace_bytes, void* stream);
+int b200_conv2d_dgrad_tc(const float* dy, const float* w, float* dx, int64_t N, int64_t C, int64_t H, int64_t W, int64_t O,
+                         int64_t KH, int64_t KW, int64_t OH, int64_t OW, int64_t sh, int64_t sw, int64_t pt, int64_t pl,
+                         void* workspace, size_t workspace_bytes, void* stream);
+int b200_conv2d_wgrad_tc(const float* x, const float* dy, float* dw, int64_t N, int64_t C, int64_t H, int64_t W, int64_t O,
+                         int64_t KH, int64_t KW, int64_t OH, int64_t OW, int64_t sh, int64_t sw, int64_t pt, int64_t pl,
+                         void* workspace, size_t workspace_bytes, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -87,6 +87,10 @@ SIGNATURES = {
     "b200_mask_mul_colsum_workspace_bytes": ([_I64, _I64], C.c_size_t),
     "b200_mask_mul_colsum": ([_P, _P, _P, _P, _P, _I64, _I64, _P, C.c_size_t, _P], C.c_int),
     "b200_logsoftmax_pick": ([_I32, _P, _P, _P, _P, _P, _P, _I64, _I64, _P], C.c_int),
+    "b200_conv2d_tc_workspace_bytes": ([_I32] + [_I64] * 13, C.c_size_t),
+    "b200_conv2d_fwd_tc": ([_P, _P, _P] + [_I64] * 13 + [_P, C.c_size_t, _P], C.c_int),
+    "b200_conv2d_dgrad_tc": ([_P, _P, _P] + [_I64] * 13 + [_P, C.c_size_t, _P], C.c_int),
+    "b200_conv2d_wgrad_tc": ([_P, _P, _P] + [_I64] * 13 + [_P, C.c_size_t, _P], C.c_int),
     "b200_conv2d_fwd": ([_I32, _P, _P, _P] + [_I64] * 13 + [_P], C.c_int),
     "b200_conv2d_dgrad": ([_I32, _P, _P, _P] + [_I64] * 13 + [_P], C.c_int),
     "b200_conv2d_wgrad": ([_I32, _P, _P, _P] + [_I64] * 13 + [_P], C.c_int),

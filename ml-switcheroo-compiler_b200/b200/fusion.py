@@ -293,19 +293,27 @@ def find_gemm_epilogue(g: Graph, live: dict[str, Node], meta: dict[str, Meta], u
     found = []
     for nid, node in live.items():
         op = _op_name(node)
-        if op not in ("Relu", "Gelu", "GELU"):
+        if op not in ("Relu", "Gelu", "GELU", "Add"):
             continue
         bind: dict[str, str] = {}
         cov: set[str] = set()
-        pat = Op(op, Op("Add", Op("Matmul", Var("A"), Var("B"), name="mm"), Var("bias"), name="pre"), name="act")
+        if op == "Add":
+            # bias epilogue without an activation: Add(Matmul(A, B), bias)
+            pat = Op("Add", Op("Matmul", Var("A"), Var("B"), name="mm"), Var("bias"), name="act")
+        else:
+            pat = Op(op, Op("Add", Op("Matmul", Var("A"), Var("B"), name="mm"), Var("bias"), name="pre"), name="act")
         if not match(pat, nid, g, bind, cov):
             continue
+        if op == "Add":
+            bind["pre"] = bind["act"]
         mm = g.nodes[bind["mm"]]
         if mm.attributes.get("transpose_a") or mm.attributes.get("transpose_b"):
             continue
         N = meta[bind["mm"]].shape[-1] if not meta[bind["mm"]].scalar else 0
         mb = meta.get(bind["bias"])
         if mb is None or mb.scalar or mb.shape != (N,):
+            continue
+        if meta[bind["act"]].shape != meta[bind["mm"]].shape:
             continue
         outs = {"act": bind["act"]}
         # the ReLU-grad mask: Greater(pre, 0)
@@ -317,18 +325,21 @@ def find_gemm_epilogue(g: Graph, live: dict[str, Node], meta: dict[str, Meta], u
                     cov.add(u)
                     cov.add(un.inputs[1])
         # mm and pre must not be needed elsewhere
-        inner = [bind["mm"], bind["pre"]]
+        inner = [bind["mm"]] if op == "Add" else [bind["mm"], bind["pre"]]
         if any(v in outputs or any(u not in cov for u in users.get(v, [])) for v in inner):
             continue
         if op != "Relu" and "mask" in outs:
             continue
-        found.append(Match("gemm_" + op.lower(), bind, {c for c in cov if c in live or g.nodes[c].op_type == "Constant"}, outs))
+        kind = "gemm_bias" if op == "Add" else "gemm_" + op.lower()
+        found.append(Match(kind, bind, {c for c in cov if c in live or g.nodes[c].op_type == "Constant"}, outs))
+    # activation epilogues first: a plain bias match must not pre-empt the ReLU/GELU one
+    found.sort(key=lambda m: m.kind == "gemm_bias")
     return found
 
 
 def gemm_epilogue_step(m: Match) -> Step:
     b, o = m.bind, m.outputs
-    epi = L.EPI_RELU if m.kind == "gemm_relu" else L.EPI_GELU
+    epi = {"gemm_relu": L.EPI_RELU, "gemm_gelu": L.EPI_GELU}.get(m.kind, L.EPI_NONE)
     want_mask = "mask" in o
     ins = [b["A"], b["B"], b["bias"]]
 

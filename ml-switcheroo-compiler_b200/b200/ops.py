@@ -789,6 +789,17 @@ def _conv_dt() -> int:
     return L.BF16 if Config.conv_dtype == "bf16" else L.F32
 
 
+def _conv_call(kind: int, a: torch.Tensor, b: torch.Tensor, out: torch.Tensor, dims: tuple) -> None:
+    """fp32 math: exact CUDA-core kernels; bf16 math: tcgen05 GEMMs over staged operands."""
+    names = ("b200_conv2d_fwd", "b200_conv2d_dgrad", "b200_conv2d_wgrad")
+    if Config.conv_dtype != "bf16":
+        L.call(names[kind], L.F32, a.data_ptr(), b.data_ptr(), out.data_ptr(), *dims, stream_ptr())
+        return
+    ws_bytes = int(L.lib().b200_conv2d_tc_workspace_bytes(kind, *dims))
+    ws = torch.empty(max(1, ws_bytes), dtype=torch.uint8, device=device())
+    L.call(names[kind] + "_tc", a.data_ptr(), b.data_ptr(), out.data_ptr(), *dims, ws.data_ptr(), ws_bytes, stream_ptr())
+
+
 def _check_conv_attrs(groups, dilation):
     if int(groups or 1) != 1:
         raise UnimplementedMathError("grouped Conv2D")
@@ -806,8 +817,7 @@ def op_conv2d(x, w, stride=(1, 1), padding="SAME", groups=1, dilation=1, **kw): 
     OH, OW = _conv_out_hw((H, W), (KH, KW), s, padding)
     pt, pl = _conv_pads((H, W), (KH, KW), s, padding, (OH, OW))
     y = torch.empty(N, O, OH, OW, dtype=torch.float32, device=device())
-    L.call("b200_conv2d_fwd", _conv_dt(), xc.data_ptr(), wc.data_ptr(), y.data_ptr(), N, Cc, H, W, O, KH, KW, OH, OW, s[0],
-           s[1], pt, pl, stream_ptr())
+    _conv_call(0, xc, wc, y, (N, Cc, H, W, O, KH, KW, OH, OW, s[0], s[1], pt, pl))
     return y
 
 
@@ -821,8 +831,7 @@ def op_conv2d_input_grad(dy, w, stride=(1, 1), padding="SAME", target_shape=None
     OH, OW = dyc.shape[2], dyc.shape[3]
     pt, pl = _conv_pads((H, W), (KH, KW), s, padding, (OH, OW))
     dx = torch.empty(N, Cc, H, W, dtype=torch.float32, device=device())
-    L.call("b200_conv2d_dgrad", _conv_dt(), dyc.data_ptr(), wc.data_ptr(), dx.data_ptr(), N, Cc, H, W, O, KH, KW, OH, OW,
-           s[0], s[1], pt, pl, stream_ptr())
+    _conv_call(1, dyc, wc, dx, (N, Cc, H, W, O, KH, KW, OH, OW, s[0], s[1], pt, pl))
     return dx
 
 
@@ -836,8 +845,7 @@ def op_conv2d_weight_grad(x, dy, stride=(1, 1), padding="SAME", target_shape=Non
     OH, OW = dyc.shape[2], dyc.shape[3]
     pt, pl = _conv_pads((H, W), (KH, KW), s, padding, (OH, OW))
     dw = torch.empty(O, Cc, KH, KW, dtype=torch.float32, device=device())
-    L.call("b200_conv2d_wgrad", _conv_dt(), xc.data_ptr(), dyc.data_ptr(), dw.data_ptr(), N, Cc, H, W, O, KH, KW, OH, OW,
-           s[0], s[1], pt, pl, stream_ptr())
+    _conv_call(2, xc, dyc, dw, (N, Cc, H, W, O, KH, KW, OH, OW, s[0], s[1], pt, pl))
     return dw
 
 

@@ -20,7 +20,27 @@ struct EwParams {
   const void* in[B200_EW_MAX_IN];
   void* out[B200_EW_MAX_OUT];
   int64_t n;
+  // 32-bit strided path: per-dim size, fast-division multiplier and shift, 32-bit strides
+  uint32_t dsz[B200_EW_MAX_DIM], dmul[B200_EW_MAX_DIM], dshr[B200_EW_MAX_DIM];
+  int32_t st32[B200_EW_MAX_IN][B200_EW_MAX_DIM];
+  // flat path: per-input mode (0 dense, 1 scalar, 2 vector along the last dim) and the
+  // last-dim length for mode 2 (fast division)
+  int32_t mode[B200_EW_MAX_IN];
+  int64_t lastdim;
+  uint32_t ld_mul, ld_shr;
 };
+
+// n / d for 32-bit n with a precomputed (mul, shr): q = (umulhi(n, mul) + n) >> shr
+__device__ __forceinline__ uint32_t fast_div(uint32_t n, uint32_t mul, uint32_t shr) {
+  return (uint32_t)(((uint64_t)__umulhi(n, mul) + n) >> shr);
+}
+static void fastdiv_params(uint32_t d, uint32_t& mul, uint32_t& shr) {
+  uint32_t l = 0;
+  while (((uint64_t)1 << l) < d) ++l;
+  mul = (uint32_t)((((uint64_t)1 << 32) * (((uint64_t)1 << l) - d)) / d + 1);
+  if (d == 1) mul = 0;
+  shr = l;
+}
 
 template <int V>
 __device__ __forceinline__ void ew_exec(const b200_ew_program& p, float (&r)[B200_EW_MAX_REG][V],
@@ -83,11 +103,21 @@ __global__ void __launch_bounds__(256) ew_flat_kernel(const __grid_constant__ Ew
     const int64_t base = q * 4;
     const bool full = base + 4 <= n;
     for (int j = 0; j < p.n_in; ++j) {
-      const bool scalar = p.ndim == 0 || p.in_strides[j][p.ndim - 1] == 0;
-      if (scalar) {
+      if (P.mode[j] == 1) {
         float s = load_as_f32(P.in[j], 0, p.in_dtype[j]);
 #pragma unroll
         for (int v = 0; v < 4; ++v) ld[j][v] = s;
+      } else if (P.mode[j] == 2) {
+        // column vector: element index modulo the last dim (lastdim % 4 == 0 here)
+        const uint32_t b32 = (uint32_t)base;  // n < 2^31 whenever a vector-mode input exists
+        const int64_t col = (int64_t)(b32 - fast_div(b32, P.ld_mul, P.ld_shr) * (uint32_t)P.lastdim);
+        if (full && p.in_dtype[j] == B200_F32) {
+          float4 t = *reinterpret_cast<const float4*>(reinterpret_cast<const float*>(P.in[j]) + col);
+          ld[j][0] = t.x; ld[j][1] = t.y; ld[j][2] = t.z; ld[j][3] = t.w;
+        } else {
+#pragma unroll
+          for (int v = 0; v < 4; ++v) ld[j][v] = (base + v < n) ? load_as_f32(P.in[j], col + v, p.in_dtype[j]) : 0.f;
+        }
       } else if (full && p.in_dtype[j] == B200_F32) {
         float4 t = reinterpret_cast<const float4*>(P.in[j])[q];
         ld[j][0] = t.x; ld[j][1] = t.y; ld[j][2] = t.z; ld[j][3] = t.w;
@@ -129,6 +159,34 @@ __global__ void __launch_bounds__(256) ew_strided_kernel(const __grid_constant__
 #pragma unroll
       for (int j = 0; j < B200_EW_MAX_IN; ++j)
         if (j < p.n_in) off[j] += id * p.in_strides[j][d];
+    }
+    for (int j = 0; j < p.n_in; ++j) ld[j][0] = load_as_f32(P.in[j], off[j], p.in_dtype[j]);
+    ew_exec<1>(p, r, ld, st);
+    for (int o = 0; o < p.n_out; ++o) store_from_f32(P.out[o], e, p.out_dtype[o], st[o][0]);
+  }
+}
+
+// strided path with 32-bit index arithmetic (fast division per dim)
+__global__ void __launch_bounds__(256) ew_strided32_kernel(const __grid_constant__ EwParams P) {
+  const b200_ew_program& p = P.p;
+  float r[B200_EW_MAX_REG][1];
+  float ld[B200_EW_MAX_IN][1];
+  float st[B200_EW_MAX_OUT][1];
+#pragma unroll
+  for (int i = 0; i < B200_EW_MAX_REG; ++i) r[i][0] = 0.f;
+  const uint32_t n = (uint32_t)P.n;
+  for (uint32_t e = blockIdx.x * blockDim.x + threadIdx.x; e < n; e += gridDim.x * blockDim.x) {
+    int32_t off[B200_EW_MAX_IN];
+#pragma unroll
+    for (int j = 0; j < B200_EW_MAX_IN; ++j) off[j] = 0;
+    uint32_t rem = e;
+    for (int d = p.ndim - 1; d >= 0; --d) {
+      const uint32_t q = fast_div(rem, P.dmul[d], P.dshr[d]);
+      const int32_t id = (int32_t)(rem - q * P.dsz[d]);
+      rem = q;
+#pragma unroll
+      for (int j = 0; j < B200_EW_MAX_IN; ++j)
+        if (j < p.n_in) off[j] += id * P.st32[j][d];
     }
     for (int j = 0; j < p.n_in; ++j) ld[j][0] = load_as_f32(P.in[j], off[j], p.in_dtype[j]);
     ew_exec<1>(p, r, ld, st);
@@ -194,20 +252,24 @@ extern "C" int b200_ew_run(const b200_ew_program* prog, const void* const* input
       s *= p.shape[d];
     }
   }
+  const int64_t lastdim = p.ndim > 0 ? p.shape[p.ndim - 1] : 1;
+  P.lastdim = lastdim;
+  fastdiv_params((uint32_t)std::min<int64_t>(lastdim, 0x7fffffff), P.ld_mul, P.ld_shr);
   for (int j = 0; j < p.n_in && flat; ++j) {
-    bool all0 = true, isdense = true;
+    bool all0 = true, isdense = true, isvec = p.ndim > 0;
     for (int d = 0; d < p.ndim; ++d) {
       if (p.shape[d] == 1) continue;
       if (p.in_strides[j][d] != 0) all0 = false;
       if (p.in_strides[j][d] != dense[d]) isdense = false;
+      if (d == p.ndim - 1 ? p.in_strides[j][d] != 1 : p.in_strides[j][d] != 0) isvec = false;
     }
+    const bool aligned = p.in_dtype[j] != B200_F32 || (reinterpret_cast<uintptr_t>(inputs[j]) & 15) == 0;
     if (all0) {
-      // treat as scalar: the kernel tests the last-dim stride, so require it to be 0
-      if (p.ndim > 0 && p.in_strides[j][p.ndim - 1] != 0 && p.shape[p.ndim - 1] != 1) flat = false;
-      if (p.ndim > 0 && p.shape[p.ndim - 1] == 1 && p.in_strides[j][p.ndim - 1] != 0) flat = false;
-    } else if (isdense) {
-      if (p.ndim > 0 && p.in_strides[j][p.ndim - 1] == 0) flat = false;  // degenerate last dim
-      if (p.in_dtype[j] == B200_F32 && (reinterpret_cast<uintptr_t>(inputs[j]) & 15)) flat = false;
+      P.mode[j] = 1;
+    } else if (isdense && aligned) {
+      P.mode[j] = 0;
+    } else if (isvec && aligned && lastdim % 4 == 0 && n < ((int64_t)1 << 31)) {
+      P.mode[j] = 2;
     } else {
       flat = false;
     }
@@ -221,8 +283,24 @@ extern "C" int b200_ew_run(const b200_ew_program* prog, const void* const* input
     int64_t blocks = std::min<int64_t>(ceil_div(ceil_div(n, 4), threads), sms * 8);
     ew_flat_kernel<<<(unsigned)blocks, threads, 0, as_stream(stream)>>>(P);
   } else {
+    // 32-bit index path when every offset fits
+    bool fits = n < ((int64_t)1 << 31);
+    for (int j = 0; j < p.n_in && fits; ++j) {
+      int64_t ext = 0;
+      for (int d = 0; d < p.ndim; ++d) ext += (p.shape[d] - 1) * (p.in_strides[j][d] < 0 ? -p.in_strides[j][d] : p.in_strides[j][d]);
+      if (ext >= ((int64_t)1 << 31)) fits = false;
+    }
     int64_t blocks = std::min<int64_t>(ceil_div(n, threads), sms * 8);
-    ew_strided_kernel<<<(unsigned)blocks, threads, 0, as_stream(stream)>>>(P);
+    if (fits) {
+      for (int d = 0; d < p.ndim; ++d) {
+        P.dsz[d] = (uint32_t)p.shape[d];
+        fastdiv_params(P.dsz[d], P.dmul[d], P.dshr[d]);
+        for (int j = 0; j < p.n_in; ++j) P.st32[j][d] = (int32_t)p.in_strides[j][d];
+      }
+      ew_strided32_kernel<<<(unsigned)blocks, threads, 0, as_stream(stream)>>>(P);
+    } else {
+      ew_strided_kernel<<<(unsigned)blocks, threads, 0, as_stream(stream)>>>(P);
+    }
   }
   return check_launch("ew_run");
 }

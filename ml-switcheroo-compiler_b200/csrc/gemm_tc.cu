@@ -109,6 +109,7 @@ struct Args {
   int64_t M, N, K, sC, ldc;
   float alpha;
   int c_dt, epi, a_mn, b_mn, batch;
+  int a_bcast, b_bcast;  // operand shared by every batch entry (batch stride 0)
 };
 
 __device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
@@ -182,17 +183,18 @@ __global__ void __launch_bounds__(THREADS, 1) gemm_tc_kernel(const __grid_consta
           const int k0 = kb * BK;
           uint8_t* a_dst = sA + s * A_BYTES;
           uint8_t* b_dst = sB + s * B_BYTES;
+          const int za = args.a_bcast ? 0 : z, zb = args.b_bcast ? 0 : z;
           if (!args.a_mn) {
-            tma_load_3d(a_dst, &mapA, &full_bar[s], k0, m_tile * BM, z);
+            tma_load_3d(a_dst, &mapA, &full_bar[s], k0, m_tile * BM, za);
           } else {
-            tma_load_3d(a_dst, &mapA, &full_bar[s], m_tile * BM, k0, z);
-            tma_load_3d(a_dst + 8192, &mapA, &full_bar[s], m_tile * BM + 64, k0, z);
+            tma_load_3d(a_dst, &mapA, &full_bar[s], m_tile * BM, k0, za);
+            tma_load_3d(a_dst + 8192, &mapA, &full_bar[s], m_tile * BM + 64, k0, za);
           }
           if (!args.b_mn) {
-            tma_load_3d(b_dst, &mapB, &full_bar[s], k0, n_tile * BN, z);
+            tma_load_3d(b_dst, &mapB, &full_bar[s], k0, n_tile * BN, zb);
           } else {
 #pragma unroll
-            for (int j = 0; j < BN / 64; ++j) tma_load_3d(b_dst + j * 8192, &mapB, &full_bar[s], n_tile * BN + 64 * j, k0, z);
+            for (int j = 0; j < BN / 64; ++j) tma_load_3d(b_dst + j * 8192, &mapB, &full_bar[s], n_tile * BN + 64 * j, k0, zb);
           }
         }
       }
@@ -403,21 +405,24 @@ int gemm_bf16_tcgen05(int c_dt, const void* A, const void* B, void* C, int64_t b
   const int64_t lda = a_mn ? csA : rsA;  // elements between consecutive non-contiguous indices
   const int64_t ldb = b_mn ? rsB : csB;
   if ((reinterpret_cast<uintptr_t>(A) & 15) || (reinterpret_cast<uintptr_t>(B) & 15) || (lda * 2) % 16 || (ldb * 2) % 16 ||
-      (batch > 1 && ((sA * 2) % 16 || (sB * 2) % 16))) {
+      (batch > 1 && ((sA * 2) % 16 || (sB * 2) % 16)) || sA < 0 || sB < 0) {
     set_error("gemm(bf16): TMA needs 16-byte aligned bases and strides (lda %lld ldb %lld)", (long long)lda, (long long)ldb);
     return B200_ERR_UNSUPPORTED;
   }
   B200_REQUIRE(M <= INT32_MAX && N <= INT32_MAX && K <= INT32_MAX, "gemm(bf16): dims too large");
   const int BN = N > 128 ? 256 : 128;
   CUtensorMap ma, mb;
-  const uint64_t zA = batch > 1 ? (uint64_t)sA * 2 : (uint64_t)lda * 2 * (uint64_t)(a_mn ? K : M);
-  const uint64_t zB = batch > 1 ? (uint64_t)sB * 2 : (uint64_t)ldb * 2 * (uint64_t)(b_mn ? K : N);
+  // an operand with batch stride 0 is shared by all batch entries: a 1-deep third dim
+  const int a_bcast = (batch > 1 && sA == 0), b_bcast = (batch > 1 && sB == 0);
+  const uint64_t bA = a_bcast ? 1 : (uint64_t)batch, bB = b_bcast ? 1 : (uint64_t)batch;
+  const uint64_t zA = bA > 1 ? (uint64_t)sA * 2 : (uint64_t)lda * 2 * (uint64_t)(a_mn ? K : M);
+  const uint64_t zB = bB > 1 ? (uint64_t)sB * 2 : (uint64_t)ldb * 2 * (uint64_t)(b_mn ? K : N);
   int rc;
-  if (!a_mn) rc = make_map(&ma, A, K, M, batch, lda * 2, zA, 64, 128);
-  else rc = make_map(&ma, A, M, K, batch, lda * 2, zA, 64, 64);
+  if (!a_mn) rc = make_map(&ma, A, K, M, bA, lda * 2, zA, 64, 128);
+  else rc = make_map(&ma, A, M, K, bA, lda * 2, zA, 64, 64);
   if (rc) return rc;
-  if (!b_mn) rc = make_map(&mb, B, K, N, batch, ldb * 2, zB, 64, BN);
-  else rc = make_map(&mb, B, N, K, batch, ldb * 2, zB, 64, 64);
+  if (!b_mn) rc = make_map(&mb, B, K, N, bB, ldb * 2, zB, 64, BN);
+  else rc = make_map(&mb, B, N, K, bB, ldb * 2, zB, 64, 64);
   if (rc) return rc;
   Args a;
   a.C = C;
@@ -434,6 +439,8 @@ int gemm_bf16_tcgen05(int c_dt, const void* A, const void* B, void* C, int64_t b
   a.a_mn = a_mn;
   a.b_mn = b_mn;
   a.batch = (int)batch;
+  a.a_bcast = a_bcast;
+  a.b_bcast = b_bcast;
   B200_REQUIRE(ceil_div(N, 256) * ceil_div(M, BM) * batch < INT32_MAX, "gemm(bf16): too many tiles");
   B200_REQUIRE(ceil_div(M, BM) <= 65535, "gemm(bf16): M too large");
   if (BN == 256) return launch<256>(ma, mb, a, batch, s);

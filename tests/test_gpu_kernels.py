@@ -316,7 +316,7 @@ def test_rowfused_kernel_both_softmax_paths(C, path):
         gamma, beta = np.ones(C, np.float32), np.zeros(C, np.float32)
     else:
         gamma = r.uniform(-1.5, 1.5, C).astype(np.float32)
-        beta = (r.standard_normal(C) * 30).astype(np.float32)
+        beta = r.standard_normal(C).astype(np.float32)  # signed gamma -> per-row max path
     cot = r.standard_normal((R, C), dtype=np.float32)
     g = O.execute_op("Gelu", x * a + b)
     n = O.execute_op("LayerNorm", g, gamma, beta, eps=1e-5)
@@ -345,3 +345,30 @@ def test_rowfused_kernel_both_softmax_paths(C, path):
         np.testing.assert_allclose(got, ref, rtol=1e-4, atol=1e-4 * scale, err_msg=k_)
     ygot = to_np(out["y"])
     np.testing.assert_array_equal(to_np(am), np.argmax(ygot, axis=-1))
+
+
+@pytest.mark.parametrize("N,C,H,O,k,stride,padding", [(2, 3, 32, 64, 3, 1, "VALID"), (3, 64, 30, 64, 3, 2, "VALID"),
+                                                      (2, 64, 14, 128, 3, 2, "VALID"), (2, 5, 11, 7, 3, 2, "SAME")])
+def test_conv2d_tensor_core_path(N, C, H, O, k, stride, padding):
+    """bf16 tcgen05 convolutions against the oracle with the same operand rounding."""
+    from b200 import ops
+    from oracle import evaluator as O_
+
+    r = rng(14)
+    x = r.standard_normal((N, C, H, H), dtype=np.float32)
+    w = (r.standard_normal((O, C, k, k)) * np.sqrt(2.0 / (C * k * k))).astype(np.float32)
+    kw = dict(stride=[stride, stride], padding=padding)
+    ops.Config.conv_dtype = "bf16"
+    try:
+        y = ops.op_conv2d(T(x), T(w), **kw)
+        y_ref = O_.execute_op("Conv2D", x, w, contraction_rounding="bf16", **kw)
+        np.testing.assert_allclose(to_np(y), y_ref, rtol=1e-3, atol=1e-3 * np.abs(y_ref).max())
+        dy = r.standard_normal(y_ref.shape, dtype=np.float32)
+        dx = ops.op_conv2d_input_grad(T(dy), T(w), target_shape=list(x.shape), **kw)
+        dx_ref = O_.execute_op("Conv2DInputGrad", dy, w, target_shape=list(x.shape), contraction_rounding="bf16", **kw)
+        np.testing.assert_allclose(to_np(dx), dx_ref, rtol=1e-3, atol=1e-3 * np.abs(dx_ref).max())
+        dw = ops.op_conv2d_weight_grad(T(x), T(dy), target_shape=list(w.shape), **kw)
+        dw_ref = O_.execute_op("Conv2DWeightGrad", x, dy, target_shape=list(w.shape), contraction_rounding="bf16", **kw)
+        np.testing.assert_allclose(to_np(dw), dw_ref, rtol=1e-3, atol=2e-3 * np.abs(dw_ref).max())
+    finally:
+        ops.Config.conv_dtype = "f32"
