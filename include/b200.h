@@ -193,6 +193,15 @@ int b200_gemm(int ab_dtype, int c_dtype, const void* A, const void* B, void* C, 
               int64_t N, int64_t K, int64_t sA, int64_t rsA, int64_t csA, int64_t sB, int64_t rsB, int64_t csB,
               int64_t sC, int64_t ldc, float alpha, const float* bias, int epilogue, void* aux, void* stream);
 
+/* Matmul over a two-level batch on the tcgen05 tensor cores (bf16 operands): batch
+ * entry (zo, zi), zo < b_out, zi < b_in, reads A at zo*sA_out + zi*sA_in and B, C likewise
+ * (a stride 0 shares that operand along the level). Covers matmuls of permuted views
+ * such as attention's [B, H, S, hd] head split (math_matrix.py:21-64) without copies. */
+int b200_gemm_batched2(int ab_dtype, int c_dtype, const void* A, const void* B, void* C, int64_t b_out, int64_t b_in,
+                       int64_t M, int64_t N, int64_t K, int64_t sA_out, int64_t sA_in, int64_t rsA, int64_t csA,
+                       int64_t sB_out, int64_t sB_in, int64_t rsB, int64_t csB, int64_t sC_out, int64_t sC_in, int64_t ldc,
+                       float alpha, const float* bias, int epilogue, void* aux, void* stream);
+
 /* Conv2D (numpy/eager/conv.py:462-489) and its VJPs Conv2DInputGrad (conv.py:634-697),
  * Conv2DWeightGrad (conv.py:699-764): NCHW activations (F32), OIHW weights (F32),
  * explicit zero padding (pt, pl; bottom/right implied by the output size), stride

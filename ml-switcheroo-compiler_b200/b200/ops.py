@@ -715,38 +715,45 @@ def gemm(a: torch.Tensor, b: torch.Tensor, *, bias: torch.Tensor | None = None, 
         # on the CUDA-core kernel in fp32, which is at least as precise as bf16 math
         ab_dtype = torch.float32
         A, B = cast(a, torch.float32), cast(b, torch.float32)
-
-    def batch_stride(t: torch.Tensor) -> int:
-        if t.dim() == 2:
-            return 0
-        e = t.expand(*batch_shape, t.shape[-2], t.shape[-1])
-        bs = list(e.stride()[:-2])
-        bsh = list(batch_shape)
-        # the flattened batch must be a single arithmetic progression
-        nz = [(s, st) for s, st in zip(bsh, bs) if s != 1]
-        if not nz:
-            return 0
-        for (s0, st0), (s1, st1) in zip(nz, nz[1:]):
-            if st0 != st1 * s1:
-                return -1
-        return nz[-1][1]
-
-    sA, sB = batch_stride(A), batch_stride(B)
-    if sA < 0:
-        A = contiguous(A.expand(*batch_shape, M, K))
-        sA = M * K
-    if sB < 0:
-        B = contiguous(B.expand(*batch_shape, K, N))
-        sB = K * N
     C_ = torch.empty(*batch_shape, M, N, dtype=out_dtype, device=device())
     mask = torch.empty(*batch_shape, M, N, dtype=torch.bool, device=device()) if want_mask else None
     bc = None if bias is None else contiguous(cast(bias, torch.float32))
     if bc is not None and bc.numel() != N:
         raise UnimplementedMathError("gemm bias must be a length-N vector")
-    if Z and M and N:
-        L.call("b200_gemm", code(A), code(C_), A.data_ptr(), B.data_ptr(), C_.data_ptr(), Z, M, N, K, sA, A.stride(-2),
-               A.stride(-1), sB, B.stride(-2), B.stride(-1), M * N, N, float(alpha), _ptr(bc), int(epilogue), _ptr(mask),
-               stream_ptr())
+    if not (Z and M and N):
+        pass
+    else:
+        nb = len(batch_shape)
+        sa = list(A.expand(*batch_shape, M, K).stride()[:nb]) if A.dim() > 2 else [0] * nb
+        sb = list(B.expand(*batch_shape, K, N).stride()[:nb]) if B.dim() > 2 else [0] * nb
+        sc = list(C_.stride()[:nb])
+        # coalesce the batch dims jointly (drop size-1 dims, merge contiguous neighbours)
+        dims = [(sz, x, y, z) for sz, x, y, z in zip(batch_shape, sa, sb, sc) if sz != 1]
+        merged: list[list[int]] = []
+        for sz, x, y, z in dims:
+            if merged and merged[-1][1] == x * sz and merged[-1][2] == y * sz and merged[-1][3] == z * sz:
+                merged[-1] = [merged[-1][0] * sz, x, y, z]
+            else:
+                merged.append([sz, x, y, z])
+        if ab_dtype == torch.bfloat16 and len(merged) <= 2:
+            while len(merged) < 2:
+                merged.insert(0, [1, 0, 0, 0])
+            (bo, sao, sbo, sco), (bi, sai, sbi, sci) = merged
+            L.call("b200_gemm_batched2", code(A), code(C_), A.data_ptr(), B.data_ptr(), C_.data_ptr(), bo, bi, M, N, K, sao,
+                   sai, A.stride(-2), A.stride(-1), sbo, sbi, B.stride(-2), B.stride(-1), sco, sci, N, float(alpha), _ptr(bc),
+                   int(epilogue), _ptr(mask), stream_ptr())
+        else:
+            if len(merged) > 1:
+                A = contiguous(A.expand(*batch_shape, M, K))
+                B = contiguous(B.expand(*batch_shape, K, N))
+                sA = M * K if A.dim() > 2 else 0
+                sB = K * N if B.dim() > 2 else 0
+            else:
+                sA = merged[0][1] if merged else 0
+                sB = merged[0][2] if merged else 0
+            L.call("b200_gemm", code(A), code(C_), A.data_ptr(), B.data_ptr(), C_.data_ptr(), Z, M, N, K, sA, A.stride(-2),
+                   A.stride(-1), sB, B.stride(-2), B.stride(-1), M * N, N, float(alpha), _ptr(bc), int(epilogue), _ptr(mask),
+                   stream_ptr())
     if squeeze_m:
         C_ = C_.squeeze(-2)
     if squeeze_n:

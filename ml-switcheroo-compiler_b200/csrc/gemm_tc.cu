@@ -65,6 +65,14 @@ __device__ __forceinline__ void tma_load_3d(void* dst, const CUtensorMap* map, u
       : "memory");
 }
 
+__device__ __forceinline__ void tma_load_4d(void* dst, const CUtensorMap* map, uint64_t* bar, int c0, int c1, int c2, int c3) {
+  asm volatile(
+      "cp.async.bulk.tensor.4d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3, %4, %5}], [%6];" ::"r"(
+          smem_u32(dst)),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(c0), "r"(c1), "r"(c2), "r"(c3), "r"(smem_u32(bar))
+      : "memory");
+}
+
 // UMMA shared-memory descriptor, SWIZZLE_128B, version 1 (sm_100).
 __device__ __forceinline__ uint64_t smem_desc(uint32_t saddr, uint32_t lbo_bytes, uint32_t sbo_bytes) {
   uint64_t d = 0;
@@ -108,8 +116,10 @@ struct Args {
   uint8_t* aux;
   int64_t M, N, K, sC, ldc;
   float alpha;
-  int c_dt, epi, a_mn, b_mn, batch;
-  int a_bcast, b_bcast;  // operand shared by every batch entry (batch stride 0)
+  int c_dt, epi, a_mn, b_mn, batch;  // batch = b_out * b_in tiles-of-matrices
+  int b_in;                          // inner batch count (z = z_out * b_in + z_in)
+  int a_bc_out, a_bc_in, b_bc_out, b_bc_in;  // operand shared along that batch level (stride 0)
+  int64_t sC_in;                     // C stride of the inner batch level (sC = outer)
 };
 
 __device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
@@ -183,18 +193,20 @@ __global__ void __launch_bounds__(THREADS, 1) gemm_tc_kernel(const __grid_consta
           const int k0 = kb * BK;
           uint8_t* a_dst = sA + s * A_BYTES;
           uint8_t* b_dst = sB + s * B_BYTES;
-          const int za = args.a_bcast ? 0 : z, zb = args.b_bcast ? 0 : z;
+          const int zo = z / args.b_in, zi = z % args.b_in;
+          const int ai = args.a_bc_in ? 0 : zi, ao = args.a_bc_out ? 0 : zo;
+          const int bi = args.b_bc_in ? 0 : zi, bo = args.b_bc_out ? 0 : zo;
           if (!args.a_mn) {
-            tma_load_3d(a_dst, &mapA, &full_bar[s], k0, m_tile * BM, za);
+            tma_load_4d(a_dst, &mapA, &full_bar[s], k0, m_tile * BM, ai, ao);
           } else {
-            tma_load_3d(a_dst, &mapA, &full_bar[s], m_tile * BM, k0, za);
-            tma_load_3d(a_dst + 8192, &mapA, &full_bar[s], m_tile * BM + 64, k0, za);
+            tma_load_4d(a_dst, &mapA, &full_bar[s], m_tile * BM, k0, ai, ao);
+            tma_load_4d(a_dst + 8192, &mapA, &full_bar[s], m_tile * BM + 64, k0, ai, ao);
           }
           if (!args.b_mn) {
-            tma_load_3d(b_dst, &mapB, &full_bar[s], k0, n_tile * BN, zb);
+            tma_load_4d(b_dst, &mapB, &full_bar[s], k0, n_tile * BN, bi, bo);
           } else {
 #pragma unroll
-            for (int j = 0; j < BN / 64; ++j) tma_load_3d(b_dst + j * 8192, &mapB, &full_bar[s], n_tile * BN + 64 * j, k0, zb);
+            for (int j = 0; j < BN / 64; ++j) tma_load_4d(b_dst + j * 8192, &mapB, &full_bar[s], n_tile * BN + 64 * j, k0, bi, bo);
           }
         }
       }
@@ -260,7 +272,7 @@ __global__ void __launch_bounds__(THREADS, 1) gemm_tc_kernel(const __grid_consta
         if (row >= args.M) continue;
         const int64_t cbase = col0 + c * 32;
         if (cbase >= args.N) continue;
-        const int64_t off = (int64_t)z * args.sC + row * args.ldc + cbase;
+        const int64_t off = (int64_t)(z / args.b_in) * args.sC + (int64_t)(z % args.b_in) * args.sC_in + row * args.ldc + cbase;
         uint8_t mask[32];
 #pragma unroll
         for (int i = 0; i < 32; ++i) {
@@ -342,25 +354,26 @@ static PFN_cuTensorMapEncodeTiled_v12000 get_encode() {
   return fn;
 }
 
-// 3-D bf16 tensor map: dims (d0 contiguous, d1, d2) with byte strides s1, s2, box (b0, b1, 1)
-static int make_map(CUtensorMap* map, const void* base, uint64_t d0, uint64_t d1, uint64_t d2, uint64_t s1, uint64_t s2,
-                    uint32_t b0, uint32_t b1) {
+// 4-D bf16 tensor map: dims (d0 contiguous, d1, d2, d3) with byte strides s1, s2, s3,
+// box (b0, b1, 1, 1). Dims of size 1 get a harmless stride equal to the previous extent.
+static int make_map(CUtensorMap* map, const void* base, uint64_t d0, uint64_t d1, uint64_t d2, uint64_t d3, uint64_t s1,
+                    uint64_t s2, uint64_t s3, uint32_t b0, uint32_t b1) {
   auto enc = get_encode();
   if (!enc) {
     set_error("gemm(bf16): cuTensorMapEncodeTiled unavailable");
     return B200_ERR_CUDA;
   }
-  cuuint64_t dims[3] = {d0, d1, d2};
-  cuuint64_t strides[2] = {s1, s2};
-  cuuint32_t box[3] = {b0, b1, 1};
-  cuuint32_t estr[3] = {1, 1, 1};
-  CUresult r = enc(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, const_cast<void*>(base), dims, strides, box, estr,
+  cuuint64_t dims[4] = {d0, d1, d2, d3};
+  cuuint64_t strides[3] = {s1, s2, s3};
+  cuuint32_t box[4] = {b0, b1, 1, 1};
+  cuuint32_t estr[4] = {1, 1, 1, 1};
+  CUresult r = enc(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 4, const_cast<void*>(base), dims, strides, box, estr,
                    CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
                    CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   if (r != CUDA_SUCCESS) {
-    set_error("gemm(bf16): cuTensorMapEncodeTiled failed (%d): dims %llu %llu %llu strides %llu %llu", (int)r,
-              (unsigned long long)d0, (unsigned long long)d1, (unsigned long long)d2, (unsigned long long)s1,
-              (unsigned long long)s2);
+    set_error("gemm(bf16): cuTensorMapEncodeTiled failed (%d): dims %llu %llu %llu %llu strides %llu %llu %llu", (int)r,
+              (unsigned long long)d0, (unsigned long long)d1, (unsigned long long)d2, (unsigned long long)d3,
+              (unsigned long long)s1, (unsigned long long)s2, (unsigned long long)s3);
     return B200_ERR_ARG;
   }
   return B200_OK;
@@ -369,7 +382,7 @@ static int make_map(CUtensorMap* map, const void* base, uint64_t d0, uint64_t d1
 template <int BN>
 static int launch(const CUtensorMap& ma, const CUtensorMap& mb, const Args& a, int64_t batch, cudaStream_t s) {
   const size_t smem = (size_t)STAGES * (BM * BK * 2 + BN * BK * 2) + 1024 + 256;
-  const int64_t tiles = ceil_div(a.N, BN) * ceil_div(a.M, BM) * batch;
+  const int64_t tiles = ceil_div(a.N, BN) * ceil_div(a.M, BM) * batch;  // batch = b_out * b_in
   static bool attr_set[64] = {false};
   int dev = 0;
   cudaGetDevice(&dev);
@@ -384,9 +397,10 @@ static int launch(const CUtensorMap& ma, const CUtensorMap& mb, const Args& a, i
 
 }  // namespace tc
 
-int gemm_bf16_tcgen05(int c_dt, const void* A, const void* B, void* C, int64_t batch, int64_t M, int64_t N, int64_t K,
-                      int64_t sA, int64_t rsA, int64_t csA, int64_t sB, int64_t rsB, int64_t csB, int64_t sC, int64_t ldc,
-                      float alpha, const float* bias, int epi, void* aux, cudaStream_t s) {
+int gemm_bf16_tcgen05_b2(int c_dt, const void* A, const void* B, void* C, int64_t b_out, int64_t b_in, int64_t M, int64_t N,
+                         int64_t K, int64_t sA_out, int64_t sA_in, int64_t rsA, int64_t csA, int64_t sB_out, int64_t sB_in,
+                         int64_t rsB, int64_t csB, int64_t sC_out, int64_t sC_in, int64_t ldc, float alpha, const float* bias,
+                         int epi, void* aux, cudaStream_t s) {
   using namespace tc;
   // operand majors: A K-major if csA == 1, MN-major if rsA == 1; B K-major if rsB == 1, MN-major if csB == 1
   int a_mn, b_mn;
@@ -404,25 +418,33 @@ int gemm_bf16_tcgen05(int c_dt, const void* A, const void* B, void* C, int64_t b
   }
   const int64_t lda = a_mn ? csA : rsA;  // elements between consecutive non-contiguous indices
   const int64_t ldb = b_mn ? rsB : csB;
-  if ((reinterpret_cast<uintptr_t>(A) & 15) || (reinterpret_cast<uintptr_t>(B) & 15) || (lda * 2) % 16 || (ldb * 2) % 16 ||
-      (batch > 1 && ((sA * 2) % 16 || (sB * 2) % 16)) || sA < 0 || sB < 0) {
+  auto bad16 = [](int64_t v) { return ((v * 2) % 16) != 0; };
+  if ((reinterpret_cast<uintptr_t>(A) & 15) || (reinterpret_cast<uintptr_t>(B) & 15) || bad16(lda) || bad16(ldb) ||
+      (b_out > 1 && (bad16(sA_out) || bad16(sB_out))) || (b_in > 1 && (bad16(sA_in) || bad16(sB_in))) || sA_out < 0 ||
+      sA_in < 0 || sB_out < 0 || sB_in < 0) {
     set_error("gemm(bf16): TMA needs 16-byte aligned bases and strides (lda %lld ldb %lld)", (long long)lda, (long long)ldb);
     return B200_ERR_UNSUPPORTED;
   }
-  B200_REQUIRE(M <= INT32_MAX && N <= INT32_MAX && K <= INT32_MAX, "gemm(bf16): dims too large");
+  B200_REQUIRE(M <= INT32_MAX && N <= INT32_MAX && K <= INT32_MAX && b_out >= 1 && b_in >= 1, "gemm(bf16): bad dims");
   const int BN = N > 128 ? 256 : 128;
+  const int64_t batch = b_out * b_in;
+  B200_REQUIRE(ceil_div(N, 256) * ceil_div(M, BM) * batch < INT32_MAX && batch < INT32_MAX, "gemm(bf16): too many tiles");
+  // a batch level with stride 0 (or count 1) is a 1-deep tensor-map dim read at index 0
+  const int a_bc_out = (b_out == 1 || sA_out == 0), a_bc_in = (b_in == 1 || sA_in == 0);
+  const int b_bc_out = (b_out == 1 || sB_out == 0), b_bc_in = (b_in == 1 || sB_in == 0);
+  const uint64_t rowsA = a_mn ? K : M, rowsB = b_mn ? K : N;
+  const uint64_t spanA = (uint64_t)lda * 2 * rowsA, spanB = (uint64_t)ldb * 2 * rowsB;
+  const uint64_t aIn = a_bc_in ? 1 : b_in, aOut = a_bc_out ? 1 : b_out;
+  const uint64_t bIn = b_bc_in ? 1 : b_in, bOut = b_bc_out ? 1 : b_out;
+  const uint64_t sAi = a_bc_in ? spanA : (uint64_t)sA_in * 2, sAo = a_bc_out ? sAi * aIn : (uint64_t)sA_out * 2;
+  const uint64_t sBi = b_bc_in ? spanB : (uint64_t)sB_in * 2, sBo = b_bc_out ? sBi * bIn : (uint64_t)sB_out * 2;
   CUtensorMap ma, mb;
-  // an operand with batch stride 0 is shared by all batch entries: a 1-deep third dim
-  const int a_bcast = (batch > 1 && sA == 0), b_bcast = (batch > 1 && sB == 0);
-  const uint64_t bA = a_bcast ? 1 : (uint64_t)batch, bB = b_bcast ? 1 : (uint64_t)batch;
-  const uint64_t zA = bA > 1 ? (uint64_t)sA * 2 : (uint64_t)lda * 2 * (uint64_t)(a_mn ? K : M);
-  const uint64_t zB = bB > 1 ? (uint64_t)sB * 2 : (uint64_t)ldb * 2 * (uint64_t)(b_mn ? K : N);
   int rc;
-  if (!a_mn) rc = make_map(&ma, A, K, M, bA, lda * 2, zA, 64, 128);
-  else rc = make_map(&ma, A, M, K, bA, lda * 2, zA, 64, 64);
+  if (!a_mn) rc = make_map(&ma, A, K, M, aIn, aOut, lda * 2, sAi, sAo, 64, 128);
+  else rc = make_map(&ma, A, M, K, aIn, aOut, lda * 2, sAi, sAo, 64, 64);
   if (rc) return rc;
-  if (!b_mn) rc = make_map(&mb, B, K, N, bB, ldb * 2, zB, 64, BN);
-  else rc = make_map(&mb, B, N, K, bB, ldb * 2, zB, 64, 64);
+  if (!b_mn) rc = make_map(&mb, B, K, N, bIn, bOut, ldb * 2, sBi, sBo, 64, BN);
+  else rc = make_map(&mb, B, N, K, bIn, bOut, ldb * 2, sBi, sBo, 64, 64);
   if (rc) return rc;
   Args a;
   a.C = C;
@@ -431,7 +453,8 @@ int gemm_bf16_tcgen05(int c_dt, const void* A, const void* B, void* C, int64_t b
   a.M = M;
   a.N = N;
   a.K = K;
-  a.sC = sC;
+  a.sC = sC_out;
+  a.sC_in = sC_in;
   a.ldc = ldc;
   a.alpha = alpha;
   a.c_dt = c_dt;
@@ -439,12 +462,44 @@ int gemm_bf16_tcgen05(int c_dt, const void* A, const void* B, void* C, int64_t b
   a.a_mn = a_mn;
   a.b_mn = b_mn;
   a.batch = (int)batch;
-  a.a_bcast = a_bcast;
-  a.b_bcast = b_bcast;
-  B200_REQUIRE(ceil_div(N, 256) * ceil_div(M, BM) * batch < INT32_MAX, "gemm(bf16): too many tiles");
+  a.b_in = (int)b_in;
+  a.a_bc_out = a_bc_out;
+  a.a_bc_in = a_bc_in;
+  a.b_bc_out = b_bc_out;
+  a.b_bc_in = b_bc_in;
   B200_REQUIRE(ceil_div(M, BM) <= 65535, "gemm(bf16): M too large");
   if (BN == 256) return launch<256>(ma, mb, a, batch, s);
   return launch<128>(ma, mb, a, batch, s);
 }
 
+int gemm_bf16_tcgen05(int c_dt, const void* A, const void* B, void* C, int64_t batch, int64_t M, int64_t N, int64_t K,
+                      int64_t sA, int64_t rsA, int64_t csA, int64_t sB, int64_t rsB, int64_t csB, int64_t sC, int64_t ldc,
+                      float alpha, const float* bias, int epi, void* aux, cudaStream_t s) {
+  return gemm_bf16_tcgen05_b2(c_dt, A, B, C, batch, 1, M, N, K, sA, 0, rsA, csA, sB, 0, rsB, csB, sC, 0, ldc, alpha, bias, epi,
+                              aux, s);
+}
+
 }  // namespace b200
+
+using namespace b200;
+
+extern "C" int b200_gemm_batched2(int ab_dt, int c_dt, const void* A, const void* B, void* C, int64_t b_out, int64_t b_in,
+                                  int64_t M, int64_t N, int64_t K, int64_t sA_out, int64_t sA_in, int64_t rsA, int64_t csA,
+                                  int64_t sB_out, int64_t sB_in, int64_t rsB, int64_t csB, int64_t sC_out, int64_t sC_in,
+                                  int64_t ldc, float alpha, const float* bias, int epi, void* aux, void* stream) {
+  B200_REQUIRE(A && B && C, "gemm_batched2: null operand");
+  B200_REQUIRE(b_out >= 0 && b_in >= 0 && M >= 0 && N >= 0 && K >= 0, "gemm_batched2: negative size");
+  B200_REQUIRE(ldc >= N, "gemm_batched2: ldc < N");
+  B200_REQUIRE(epi == B200_EPI_NONE || epi == B200_EPI_RELU || epi == B200_EPI_GELU, "gemm_batched2: bad epilogue %d", epi);
+  if (c_dt != B200_F32 && c_dt != B200_BF16) {
+    set_error("gemm_batched2: output dtype %d", c_dt);
+    return B200_ERR_DTYPE;
+  }
+  if (ab_dt != B200_BF16) {
+    set_error("gemm_batched2: tensor-core operands must be bf16 (dtype %d)", ab_dt);
+    return B200_ERR_DTYPE;
+  }
+  if (b_out == 0 || b_in == 0 || M == 0 || N == 0) return B200_OK;
+  return gemm_bf16_tcgen05_b2(c_dt, A, B, C, b_out, b_in, M, N, K, sA_out, sA_in, rsA, csA, sB_out, sB_in, rsB, csB, sC_out,
+                              sC_in, ldc, alpha, bias, epi, aux, as_stream(stream));
+}

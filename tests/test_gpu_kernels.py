@@ -372,3 +372,23 @@ def test_conv2d_tensor_core_path(N, C, H, O, k, stride, padding):
         np.testing.assert_allclose(to_np(dw), dw_ref, rtol=1e-3, atol=2e-3 * np.abs(dw_ref).max())
     finally:
         ops.Config.conv_dtype = "f32"
+
+
+def test_gemm_bf16_two_level_batch_views():
+    """Attention-style head-split views go to the tensor cores without copies."""
+    from b200 import ops
+
+    r = rng(15)
+    B_, S, H, hd = 2, 128, 4, 64
+    y = _bf16(r.standard_normal((B_ * S, H * hd), dtype=np.float32))
+    Y = T(y).to(torch.bfloat16)
+    q = Y.view(B_, S, H, hd).permute(0, 2, 1, 3)          # [B, H, S, hd], strides (S*d, hd, d, 1)
+    kT = Y.view(B_, S, H, hd).permute(0, 2, 3, 1)         # [B, H, hd, S]
+    qn = y.reshape(B_, S, H, hd).transpose(0, 2, 1, 3)
+    kn = y.reshape(B_, S, H, hd).transpose(0, 2, 3, 1)
+    ref = np.matmul(qn.astype(np.float64), kn.astype(np.float64))
+    got = to_np(ops.gemm(q, kT, ab_dtype=torch.bfloat16))
+    np.testing.assert_allclose(got, ref, rtol=1e-4, atol=1e-3)
+    att = _bf16(r.standard_normal((B_, H, S, S), dtype=np.float32))
+    ctx = to_np(ops.gemm(T(att).to(torch.bfloat16), q, ab_dtype=torch.bfloat16))
+    np.testing.assert_allclose(ctx, np.matmul(att.astype(np.float64), qn.astype(np.float64)), rtol=1e-4, atol=1e-3)
