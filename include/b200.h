@@ -130,6 +130,15 @@ int b200_reduce(int in_dtype, const void* x, float* y, int64_t outer, int64_t re
 /* Argmax (numpy/eager/math_reductions.py:129-140): first maximum wins, int64 out. */
 int b200_argmax(int in_dtype, const void* x, int64_t* idx, int64_t outer, int64_t red, int64_t inner, void* stream);
 
+/* LayerNorm forward (numpy/eager/nn_ops.py:219-241) and LayerNormInputGrad (nn_ops.py:244)
+ * over the last axis, writing fp32 (y / dx) and/or bf16 (y_bf16 / dx_bf16; either may be
+ * NULL, not both). Rows of up to 2048 columns are read from HBM once. gamma / beta may be
+ * NULL (ones / zeros). */
+int b200_layernorm_rows(const float* x, const float* gamma, const float* beta, float* y, void* y_bf16, int64_t rows,
+                        int64_t cols, float eps, void* stream);
+int b200_layernorm_input_grad_rows(const float* dy, const float* x, const float* gamma, float* dx, void* dx_bf16,
+                                   int64_t rows, int64_t cols, float eps, void* stream);
+
 /* Softmax / LogSoftmax over the last axis (numpy/eager/math_advanced/math_signal.py:450-467,
  * math_advanced/math_log_exp.py:87-104). x, y: [rows, cols] F32. log != 0 -> LogSoftmax. */
 int b200_softmax(const float* x, float* y, int64_t rows, int64_t cols, int log, void* stream);
@@ -196,11 +205,14 @@ int b200_gemm(int ab_dtype, int c_dtype, const void* A, const void* B, void* C, 
 /* Matmul over a two-level batch on the tcgen05 tensor cores (bf16 operands): batch
  * entry (zo, zi), zo < b_out, zi < b_in, reads A at zo*sA_out + zi*sA_in and B, C likewise
  * (a stride 0 shares that operand along the level). Covers matmuls of permuted views
- * such as attention's [B, H, S, hd] head split (math_matrix.py:21-64) without copies. */
+ * such as attention's [B, H, S, hd] head split (math_matrix.py:21-64) without copies.
+ * C2 (optional, bf16, same element offsets as C): receives act(pre) while C receives
+ * pre = alpha A.B + bias, for a bias-add whose activation input is also needed (the
+ * GELU of a transformer FFN, whose VJP reads the pre-activation). */
 int b200_gemm_batched2(int ab_dtype, int c_dtype, const void* A, const void* B, void* C, int64_t b_out, int64_t b_in,
                        int64_t M, int64_t N, int64_t K, int64_t sA_out, int64_t sA_in, int64_t rsA, int64_t csA,
                        int64_t sB_out, int64_t sB_in, int64_t rsB, int64_t csB, int64_t sC_out, int64_t sC_in, int64_t ldc,
-                       float alpha, const float* bias, int epilogue, void* aux, void* stream);
+                       float alpha, const float* bias, int epilogue, void* aux, void* C2, void* stream);
 
 /* Conv2D (numpy/eager/conv.py:462-489) and its VJPs Conv2DInputGrad (conv.py:634-697),
  * Conv2DWeightGrad (conv.py:699-764): NCHW activations (F32), OIHW weights (F32),
@@ -256,6 +268,30 @@ int b200_mask_mul_colsum(const float* g, const uint8_t* mask, void* y_bf16, floa
  * picked, ls (the full log-softmax) and dx may each be NULL. */
 int b200_logsoftmax_pick(int x_dtype, const void* x, const int64_t* label, const float* d, float* picked, float* ls,
                          float* dx, int64_t rows, int64_t cols, void* stream);
+
+/* LayerNorm forward (numpy/eager/nn_ops.py:219-241) and LayerNormInputGrad (nn_ops.py:244)
+ * over the last axis, writing fp32 (y / dx) and/or bf16 (y_bf16 / dx_bf16; either may be
+ * NULL, not both). Rows of up to 2048 columns are read from HBM once. gamma / beta may be
+ * NULL (ones / zeros). */
+int b200_layernorm_rows(const float* x, const float* gamma, const float* beta, float* y, void* y_bf16, int64_t rows,
+                        int64_t cols, float eps, void* stream);
+int b200_layernorm_input_grad_rows(const float* dy, const float* x, const float* gamma, float* dx, void* dx_bf16,
+                                   int64_t rows, int64_t cols, float eps, void* stream);
+
+/* Softmax / LogSoftmax over the last axis (numpy/eager/math_advanced/math_signal.py:450-467,
+ * math_advanced/math_log_exp.py:87-104) of t = x * scale[0], where `scale` is an optional
+ * device scalar (NULL = 1): the Multiply node that scales attention scores folds in.
+ * x [rows, cols] fp32 dense; writes y (fp32) and/or y_bf16 (either may be NULL, not both). */
+int b200_softmax_rows(const float* x, const float* scale, float* y, void* y_bf16, int64_t rows, int64_t cols, int log,
+                      void* stream);
+
+/* Softmax VJP as the AD pass composes it (Multiply, ReduceSum keepdims, Subtract, Multiply
+ * over numpy/eager/math_binary.py:9-51 and core_math_ops/math_reduction.py:37), times an
+ * optional device scalar (the VJP of the scaling Multiply):
+ *   dx = scale[0] * (y * (g - sum_j g * y)).
+ * y, g [rows, cols] fp32 dense; writes dx (fp32) and/or dx_bf16 (either may be NULL). */
+int b200_softmax_bwd_rows(const float* y, const float* g, const float* scale, float* dx, void* dx_bf16, int64_t rows,
+                          int64_t cols, void* stream);
 
 /* Conv2D / Conv2DInputGrad / Conv2DWeightGrad (numpy/eager/conv.py:462-489, 634-697,
  * 699-764) on the tcgen05 tensor cores: bf16 operands staged in `workspace` (im2col of

@@ -71,6 +71,10 @@ SIGNATURES = {
     "b200_reduce": ([_I32, _P, _P, _I64, _I64, _I64, _I32, _P], C.c_int),
     "b200_argmax": ([_I32, _P, _P, _I64, _I64, _I64, _P], C.c_int),
     "b200_softmax": ([_P, _P, _I64, _I64, _I32, _P], C.c_int),
+    "b200_layernorm_rows": ([_P, _P, _P, _P, _P, _I64, _I64, _F32, _P], C.c_int),
+    "b200_layernorm_input_grad_rows": ([_P, _P, _P, _P, _P, _I64, _I64, _F32, _P], C.c_int),
+    "b200_softmax_rows": ([_P, _P, _P, _P, _I64, _I64, _I32, _P], C.c_int),
+    "b200_softmax_bwd_rows": ([_P, _P, _P, _P, _P, _I64, _I64, _P], C.c_int),
     "b200_layernorm": ([_P, _P, _P, _P, _I64, _I64, _F32, _P], C.c_int),
     "b200_layernorm_input_grad": ([_P, _P, _P, _P, _I64, _I64, _F32, _P], C.c_int),
     "b200_layernorm_param_grad": ([_P, _P, _P, _P, _I64, _I64, _F32, _P], C.c_int),
@@ -83,7 +87,7 @@ SIGNATURES = {
         C.c_int,
     ),
     "b200_gemm_batched2": (
-        [_I32, _I32, _P, _P, _P] + [_I64] * 16 + [_F32, _P, _I32, _P, _P],
+        [_I32, _I32, _P, _P, _P] + [_I64] * 16 + [_F32, _P, _I32, _P, _P, _P],
         C.c_int,
     ),
     "b200_rowfused_workspace_bytes": ([_I64, _I64], C.c_size_t),

@@ -324,13 +324,24 @@ def find_gemm_epilogue(g: Graph, live: dict[str, Node], meta: dict[str, Meta], u
                     outs["mask"] = u
                     cov.add(u)
                     cov.add(un.inputs[1])
-        # mm and pre must not be needed elsewhere
-        inner = [bind["mm"]] if op == "Add" else [bind["mm"], bind["pre"]]
-        if any(v in outputs or any(u not in cov for u in users.get(v, [])) for v in inner):
+        # mm must not be needed elsewhere; pre either not, or it is kept as a second output
+        def leaks(v: str) -> bool:
+            return v in outputs or any(u not in cov for u in users.get(v, []))
+
+        if leaks(bind["mm"]):
             continue
         if op != "Relu" and "mask" in outs:
             continue
         kind = "gemm_bias" if op == "Add" else "gemm_" + op.lower()
+        bf, f32 = gemm_use(bind["act"], live, users, outputs)
+        bind["bf16"] = str(bf and not f32)
+        if op != "Add" and leaks(bind["pre"]):
+            # the VJP reads the pre-activation (GELU): the epilogue writes pre in fp32 and,
+            # when the activation only feeds bf16 GEMMs, the activation in bf16 beside it
+            if bind["bf16"] != "True":
+                continue
+            outs["pre"] = bind["pre"]
+            kind += "_dual"
         found.append(Match(kind, bind, {c for c in cov if c in live or g.nodes[c].op_type == "Constant"}, outs))
     # activation epilogues first: a plain bias match must not pre-empt the ReLU/GELU one
     found.sort(key=lambda m: m.kind == "gemm_bias")
@@ -339,18 +350,63 @@ def find_gemm_epilogue(g: Graph, live: dict[str, Node], meta: dict[str, Meta], u
 
 def gemm_epilogue_step(m: Match) -> Step:
     b, o = m.bind, m.outputs
-    epi = {"gemm_relu": L.EPI_RELU, "gemm_gelu": L.EPI_GELU}.get(m.kind, L.EPI_NONE)
+    kind = m.kind.replace("_dual", "")
+    epi = {"gemm_relu": L.EPI_RELU, "gemm_gelu": L.EPI_GELU}.get(kind, L.EPI_NONE)
     want_mask = "mask" in o
+    dual = m.kind.endswith("_dual")
+    out_dt = torch.bfloat16 if (b.get("bf16") == "True" and not dual) else torch.float32
     ins = [b["A"], b["B"], b["bias"]]
 
     def run(env: dict) -> None:
-        res = ops.gemm(env[b["A"]], env[b["B"]], bias=env[b["bias"]], epilogue=epi, want_mask=want_mask)
-        if want_mask:
+        res = ops.gemm(env[b["A"]], env[b["B"]], bias=env[b["bias"]], epilogue=epi, want_mask=want_mask, out_dtype=out_dt,
+                       act_bf16=dual)
+        if dual:
+            env[o["pre"]], env[o["act"]] = res[0], res[1]
+            if want_mask:
+                env[o["mask"]] = res[2]
+        elif want_mask:
             env[o["act"]], env[o["mask"]] = res
         else:
             env[o["act"]] = res
 
-    return Step(list(o.values()), ins, run, m.kind)
+    label = m.kind + ("[bf16]" if out_dt == torch.bfloat16 else "")
+    return Step(list(o.values()), ins, run, label)
+
+
+def layernorm_step(n: Node, f32: bool) -> Step:
+    """LayerNorm writing bf16 for its GEMM consumers (and fp32 only if something else
+    reads it)."""
+    kw = node_kwargs(n, "LayerNorm")
+    eps = float(kw.get("epsilon", kw.get("eps", 1e-5)))
+    axis = kw.get("axis", -1)
+    ins = list(n.inputs)
+
+    def run(env: dict) -> None:
+        args = [env[i] for i in ins]
+        y, yb = ops.layer_norm(args[0], args[1] if len(args) > 1 else None, args[2] if len(args) > 2 else None, eps, axis,
+                               f32=f32, bf16=True)
+        _publish(env, n.id, y, yb)
+
+    return Step([n.id], ins, run, "LayerNorm" + ("" if f32 else "[bf16]"))
+
+
+def matmul_step(n: Node, bf16_out: bool) -> Step:
+    """A Matmul node without a fused epilogue; its output is written in bf16 when it
+    only feeds bf16 GEMMs."""
+    kw = node_kwargs(n, "Matmul")
+    ta, tb = bool(kw.get("transpose_a")), bool(kw.get("transpose_b"))
+    a_id, b_id = n.inputs[0], n.inputs[1]
+    out_dt = torch.bfloat16 if bf16_out else torch.float32
+
+    def run(env: dict) -> None:
+        a, bb = env[a_id], env[b_id]
+        if ta:
+            a = a.transpose(-1, -2)
+        if tb:
+            bb = bb.transpose(-1, -2)
+        env[n.id] = ops.gemm(a, bb, out_dtype=out_dt)
+
+    return Step([n.id], [a_id, b_id], run, "Matmul" + ("[bf16]" if bf16_out else ""))
 
 
 # ----------------------------------------------------------------------------------
@@ -489,6 +545,178 @@ def xent_step(m: Match, meta: dict[str, Meta]) -> Step:
             env[o["picked"]] = picked
 
     return Step(list(o.values()), [b["x"], b["labels"], b["d"]], run, "xent_fwd_bwd")
+
+
+# ----------------------------------------------------------------------------------
+# operand dtype of values that feed the tensor cores
+# ----------------------------------------------------------------------------------
+def gemm_use(v: str, live: dict[str, Node], users: dict[str, list[str]], outputs: set[str],
+             skip: frozenset = frozenset()) -> tuple[bool, bool]:
+    """(feeds a bf16 GEMM, needed in fp32): walks the consumers of ``v`` through
+    Transpose/Reshape views. A value that only feeds bf16 GEMMs is produced in bf16 by
+    its kernel (the cast the GEMM would do, moved into the producer's store)."""
+    if ops.Config.matmul_dtype != "bf16":
+        return False, True
+    gemm = other = False
+    stack, seen = [v], set()
+    while stack:
+        x = stack.pop()
+        if x in seen:
+            continue
+        seen.add(x)
+        if x in outputs:
+            other = True
+        for u in users.get(x, []):
+            if u in skip or u not in live:
+                continue
+            op = _op_name(live[u])
+            if op == "Matmul":
+                gemm = True
+            elif op in ("Transpose", "Reshape"):
+                stack.append(u)
+            else:
+                other = True
+    return gemm, other or not gemm
+
+
+def _out_buffers(shape: tuple, f32: bool, bf16: bool) -> tuple[torch.Tensor | None, torch.Tensor | None]:
+    dev = ops.device()
+    y = torch.empty(shape, dtype=torch.float32, device=dev) if f32 else None
+    yb = torch.empty(shape, dtype=torch.bfloat16, device=dev) if bf16 else None
+    return y, yb
+
+
+def _publish(env: dict, key: str, y: torch.Tensor | None, yb: torch.Tensor | None) -> None:
+    """fp32 value in the environment with its bf16 twin registered for GEMM operands,
+    or the bf16 value alone when nothing needs fp32."""
+    if y is not None:
+        env[key] = y
+        if yb is not None:
+            ops.register_cast(y, yb)
+    else:
+        env[key] = yb
+
+
+def _scalar_tensor(m: Meta | None) -> bool:
+    return m is not None and not m.scalar and math.prod(m.shape) == 1 and m.dtype == torch.float32
+
+
+# ----------------------------------------------------------------------------------
+# pattern: [Multiply(x, s) ->] Softmax / LogSoftmax over the last axis, s a device scalar
+# ----------------------------------------------------------------------------------
+def find_softmax(g: Graph, live: dict[str, Node], meta: dict[str, Meta], users: dict[str, list[str]],
+                 outputs: set[str]) -> list[Match]:
+    found = []
+    for nid, node in live.items():
+        op = _op_name(node)
+        if op not in ("Softmax", "LogSoftmax") or len(node.inputs) != 1:
+            continue
+        x = node.inputs[0]
+        mx, my = meta.get(x), meta.get(nid)
+        if mx is None or mx.scalar or mx.dtype != torch.float32 or len(mx.shape) < 1 or my is None or my.shape != mx.shape:
+            continue
+        ax = node.attributes.get("axis", -1)
+        if not (ax is None or int(ax) % len(mx.shape) == len(mx.shape) - 1):
+            continue
+        cov, src, scale = {nid}, x, ""
+        xn = live.get(x)
+        if xn is not None and _op_name(xn) == "Multiply" and x not in outputs and users.get(x) == [nid]:
+            a, b = xn.inputs
+            for big, sm in ((a, b), (b, a)):
+                mb = meta.get(big)
+                if mb is not None and not mb.scalar and mb.shape == mx.shape and mb.dtype == torch.float32 and _scalar_tensor(meta.get(sm)):
+                    src, scale = big, sm
+                    cov.add(x)
+                    break
+        bf, f32 = gemm_use(nid, live, users, outputs)
+        bind = {"x": src, "scale": scale, "y": nid, "log": str(op == "LogSoftmax"), "bf16": str(bf), "f32": str(f32)}
+        found.append(Match("softmax", bind, cov, {"y": nid}))
+    return found
+
+
+def softmax_step(m: Match, meta: dict[str, Meta]) -> Step:
+    b = m.bind
+    shape = meta[b["y"]].shape
+    cols = shape[-1]
+    rows = math.prod(shape[:-1])
+    log, bf, f32 = b["log"] == "True", b["bf16"] == "True", b["f32"] == "True"
+    ins = [b["x"]] + ([b["scale"]] if b["scale"] else [])
+
+    def run(env: dict) -> None:
+        x = ops.contiguous(ops.cast(env[b["x"]], torch.float32))
+        sc = ops.contiguous(ops.cast(env[b["scale"]], torch.float32)) if b["scale"] else None
+        y, yb = _out_buffers(shape, f32, bf)
+        L.call("b200_softmax_rows", x.data_ptr(), None if sc is None else sc.data_ptr(), None if y is None else y.data_ptr(),
+               None if yb is None else yb.data_ptr(), rows, cols, 1 if log else 0, ops.stream_ptr())
+        _publish(env, b["y"], y, yb)
+
+    label = ("scaled_" if b["scale"] else "") + ("log_softmax" if log else "softmax") + ("[bf16]" if bf and not f32 else "")
+    return Step([b["y"]], ins, run, label)
+
+
+# ----------------------------------------------------------------------------------
+# pattern: softmax VJP  y * (g - ReduceSum(g * y, -1, keepdims)) [* s]
+# ----------------------------------------------------------------------------------
+def find_softmax_bwd(g: Graph, live: dict[str, Node], meta: dict[str, Meta], users: dict[str, list[str]],
+                     outputs: set[str]) -> list[Match]:
+    y, gv = Var("y"), Var("g")
+    s = Op("ReduceSum", Op("Multiply", gv, y, name="gy"), name="s", attrs={"axis": _last_axis, "keepdims": True})
+    inner = Op("Multiply", y, Op("Subtract", gv, s, name="d"), name="dx")
+    scaled = Op("Multiply", inner, Var("scale"), name="out")
+    cands = []
+    for nid, node in live.items():
+        if _op_name(node) != "Multiply":
+            continue
+        bind: dict[str, str] = {}
+        cov: set[str] = set()
+        if match(scaled, nid, g, bind, cov) and _scalar_tensor(meta.get(bind["scale"])):
+            cands.append((0, bind, cov, bind["out"]))
+            continue
+        bind, cov = {}, set()
+        if match(inner, nid, g, bind, cov):
+            bind["scale"] = ""
+            cands.append((1, bind, cov, bind["dx"]))
+    # a scaled match wins over the unscaled one nested inside it
+    cands.sort(key=lambda c: c[0])
+    found, claimed = [], set()
+    for _, bind, cov, out in cands:
+        if cov & claimed:
+            continue
+        my, mg = meta.get(bind["y"]), meta.get(bind["g"])
+        if my is None or mg is None or my.scalar or mg.scalar or my.shape != mg.shape or len(my.shape) < 1:
+            continue
+        if my.dtype != torch.float32 or mg.dtype != torch.float32 or meta[out].shape != my.shape:
+            continue
+        cov = {c for c in cov if c in live}
+        leak = [c for c in cov if c != out and (c in outputs or any(u not in cov for u in users.get(c, [])))]
+        if leak:
+            continue
+        bf, f32 = gemm_use(out, live, users, outputs)
+        bind.update({"outv": out, "bf16": str(bf), "f32": str(f32)})
+        found.append(Match("softmax_bwd", bind, cov, {"dx": out}))
+        claimed |= cov
+    return found
+
+
+def softmax_bwd_step(m: Match, meta: dict[str, Meta]) -> Step:
+    b = m.bind
+    shape = meta[b["outv"]].shape
+    cols = shape[-1]
+    rows = math.prod(shape[:-1])
+    bf, f32 = b["bf16"] == "True", b["f32"] == "True"
+    ins = [b["y"], b["g"]] + ([b["scale"]] if b["scale"] else [])
+
+    def run(env: dict) -> None:
+        y = ops.contiguous(ops.cast(env[b["y"]], torch.float32))
+        gg = ops.contiguous(ops.cast(env[b["g"]], torch.float32))
+        sc = ops.contiguous(ops.cast(env[b["scale"]], torch.float32)) if b["scale"] else None
+        dx, dxb = _out_buffers(shape, f32, bf)
+        L.call("b200_softmax_bwd_rows", y.data_ptr(), gg.data_ptr(), None if sc is None else sc.data_ptr(),
+               None if dx is None else dx.data_ptr(), None if dxb is None else dxb.data_ptr(), rows, cols, ops.stream_ptr())
+        _publish(env, b["outv"], dx, dxb)
+
+    label = "softmax_bwd" + ("_scaled" if b["scale"] else "") + ("[bf16]" if bf and not f32 else "")
+    return Step([b["outv"]], ins, run, label)
 
 
 # ----------------------------------------------------------------------------------
@@ -763,6 +991,42 @@ def plan_steps(graph: Graph, nodes: list[Node], sample: dict[str, Any]) -> list[
             continue
         groups.append((sorted(m.covered), mask_bwd_step(m, meta)))
         taken |= m.covered
+
+    for m in find_softmax_bwd(graph, live, meta, users, outputs):
+        if m.covered & taken:
+            continue
+        groups.append((sorted(m.covered), softmax_bwd_step(m, meta)))
+        taken |= m.covered
+
+    for m in find_softmax(graph, live, meta, users, outputs):
+        if m.covered & taken:
+            continue
+        groups.append((sorted(m.covered), softmax_step(m, meta)))
+        taken |= m.covered
+
+    # LayerNorms whose output feeds bf16 GEMMs also write (or only write) bf16
+    for n in nodes:
+        if n.id in taken or _op_name(n) != "LayerNorm":
+            continue
+        mo = meta.get(n.id)
+        if mo is None or mo.scalar:
+            continue
+        bf, f32 = gemm_use(n.id, live, users, outputs)
+        if bf:
+            groups.append(([n.id], layernorm_step(n, f32)))
+            taken.add(n.id)
+
+    # plain matmuls whose result only feeds bf16 GEMMs store bf16
+    for n in nodes:
+        if n.id in taken or _op_name(n) != "Matmul" or len(n.inputs) != 2:
+            continue
+        mo = meta.get(n.id)
+        if mo is None or mo.scalar or len(mo.shape) < 2:
+            continue
+        bf, f32 = gemm_use(n.id, live, users, outputs)
+        if bf and not f32:
+            groups.append(([n.id], matmul_step(n, True)))
+            taken.add(n.id)
 
     # 2. elementwise clusters
     rest = [n for n in nodes if n.id not in taken]

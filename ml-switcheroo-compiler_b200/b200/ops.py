@@ -510,7 +510,7 @@ def _softmax(x, axis, log):
     cols = xc.shape[-1] if xc.dim() else 1
     rows = xc.numel() // max(1, cols)
     y = torch.empty_like(xc)
-    L.call("b200_softmax", xc.data_ptr(), y.data_ptr(), rows, cols, 1 if log else 0, stream_ptr())
+    L.call("b200_softmax_rows", xc.data_ptr(), None, y.data_ptr(), None, rows, cols, 1 if log else 0, stream_ptr())
     return y
 
 
@@ -534,13 +534,18 @@ def _opt(t):
     return None if t is None else contiguous(cast(t, torch.float32))
 
 
-def op_layer_norm(x, gamma=None, beta=None, eps=1e-5, axis=-1, **kw):  # numpy/eager/nn_ops.py:219-241
-    eps = float(kw.get("epsilon", eps))
+def layer_norm(x, gamma=None, beta=None, eps=1e-5, axis=-1, f32=True, bf16=False):
+    """LayerNorm with fp32 and/or bf16 outputs: returns (y_f32 or None, y_bf16 or None)."""
     xc, rows, cols = _ln_args(x, axis)
     g, b = _opt(gamma), _opt(beta)
-    y = torch.empty_like(xc)
-    L.call("b200_layernorm", xc.data_ptr(), _ptr(g), _ptr(b), y.data_ptr(), rows, cols, eps, stream_ptr())
-    return y
+    y = torch.empty_like(xc) if f32 else None
+    yb = torch.empty(xc.shape, dtype=torch.bfloat16, device=device()) if bf16 else None
+    L.call("b200_layernorm_rows", xc.data_ptr(), _ptr(g), _ptr(b), _ptr(y), _ptr(yb), rows, cols, float(eps), stream_ptr())
+    return y, yb
+
+
+def op_layer_norm(x, gamma=None, beta=None, eps=1e-5, axis=-1, **kw):  # numpy/eager/nn_ops.py:219-241
+    return layer_norm(x, gamma, beta, float(kw.get("epsilon", eps)), axis)[0]
 
 
 def op_layer_norm_input_grad(dy, x, gamma=None, eps=1e-5, axis=-1, **kw):  # numpy/eager/nn_ops.py:244-273
@@ -549,7 +554,8 @@ def op_layer_norm_input_grad(dy, x, gamma=None, eps=1e-5, axis=-1, **kw):  # num
     dyc = contiguous(cast(dy.expand(xc.shape), torch.float32))
     g = _opt(gamma)
     dx = torch.empty_like(xc)
-    L.call("b200_layernorm_input_grad", dyc.data_ptr(), xc.data_ptr(), _ptr(g), dx.data_ptr(), rows, cols, eps, stream_ptr())
+    L.call("b200_layernorm_input_grad_rows", dyc.data_ptr(), xc.data_ptr(), _ptr(g), dx.data_ptr(), None, rows, cols, eps,
+           stream_ptr())
     return dx
 
 
@@ -644,6 +650,12 @@ def clear_cast_cache() -> None:
     _CAST_CACHE.clear()
 
 
+def register_cast(src: torch.Tensor, dst: torch.Tensor) -> None:
+    """Record ``dst`` (written by the kernel that produced ``src``) as the ``dst.dtype``
+    copy of the dense tensor ``src``; ``cast_operand`` then reuses it."""
+    _CAST_CACHE[(src.data_ptr(), src.numel(), src.dtype, dst.dtype)] = (src, dst)
+
+
 def cast_operand(t: torch.Tensor, dtype: torch.dtype) -> torch.Tensor:
     """Layout-preserving cast: a strided view of a dense tensor is cast in storage order
     (coalesced) and re-viewed, never materialised through the strided path."""
@@ -686,8 +698,15 @@ def _gemm_operand(t: torch.Tensor, ab: torch.dtype) -> torch.Tensor:
 
 def gemm(a: torch.Tensor, b: torch.Tensor, *, bias: torch.Tensor | None = None, epilogue: int = L.EPI_NONE,
          alpha: float = 1.0, out_dtype: torch.dtype = torch.float32, want_mask: bool = False,
-         ab_dtype: torch.dtype | None = None):
-    """numpy-style matmul of a [..., M, K] and b [..., K, N] with broadcast batch dims."""
+         ab_dtype: torch.dtype | None = None, act_bf16: bool = False):
+    """numpy-style matmul of a [..., M, K] and b [..., K, N] with broadcast batch dims.
+
+    Returns C = act(alpha a.b + bias) [, mask]. With ``act_bf16`` it returns
+    (pre, act_in_bf16[, mask]): C holds the pre-activation and the activation is written
+    in bf16 by the same epilogue."""
+    if act_bf16:
+        return _gemm_dual(a, b, bias=bias, epilogue=epilogue, alpha=alpha, out_dtype=out_dtype, want_mask=want_mask,
+                          ab_dtype=ab_dtype)
     if ab_dtype is None:
         ab_dtype = torch.bfloat16 if Config.matmul_dtype == "bf16" else torch.float32
     squeeze_m = squeeze_n = False
@@ -708,6 +727,7 @@ def gemm(a: torch.Tensor, b: torch.Tensor, *, bias: torch.Tensor | None = None, 
         ys = (y[0] if want_mask else y).view(*a.shape[:-1], N)
         res = (ys, y[1].view(*a.shape[:-1], N)) if want_mask else ys
         return res
+    act_bf16 = None
     A = _gemm_operand(a, ab_dtype)
     B = _gemm_operand(b, ab_dtype) if A is not None else None
     if A is None or B is None:
@@ -741,7 +761,7 @@ def gemm(a: torch.Tensor, b: torch.Tensor, *, bias: torch.Tensor | None = None, 
             (bo, sao, sbo, sco), (bi, sai, sbi, sci) = merged
             L.call("b200_gemm_batched2", code(A), code(C_), A.data_ptr(), B.data_ptr(), C_.data_ptr(), bo, bi, M, N, K, sao,
                    sai, A.stride(-2), A.stride(-1), sbo, sbi, B.stride(-2), B.stride(-1), sco, sci, N, float(alpha), _ptr(bc),
-                   int(epilogue), _ptr(mask), stream_ptr())
+                   int(epilogue), _ptr(mask), _ptr(act_bf16), stream_ptr())
         else:
             if len(merged) > 1:
                 A = contiguous(A.expand(*batch_shape, M, K))
@@ -759,6 +779,36 @@ def gemm(a: torch.Tensor, b: torch.Tensor, *, bias: torch.Tensor | None = None, 
     if squeeze_n:
         C_ = C_.squeeze(-1)
     return (C_, mask) if want_mask else C_
+
+
+def _gemm_dual(a, b, *, bias, epilogue, alpha, out_dtype, want_mask, ab_dtype):
+    """pre = alpha a.b + bias and act(pre) in bf16 from one tcgen05 epilogue; other
+    layouts compute pre first and apply the activation with an elementwise program."""
+    if ab_dtype is None:
+        ab_dtype = torch.bfloat16 if Config.matmul_dtype == "bf16" else torch.float32
+    squeeze = a.dim() == 1 or b.dim() == 1
+    A = _gemm_operand(a, ab_dtype) if ab_dtype == torch.bfloat16 and not squeeze else None
+    B = _gemm_operand(b, ab_dtype) if A is not None else None
+    if A is not None and B is not None and A.dim() == 2 and B.dim() == 2:
+        M, K = A.shape
+        N = B.shape[1]
+        pre = torch.empty(M, N, dtype=out_dtype, device=device())
+        act = torch.empty(M, N, dtype=torch.bfloat16, device=device())
+        mask = torch.empty(M, N, dtype=torch.bool, device=device()) if want_mask else None
+        bc = None if bias is None else contiguous(cast(bias, torch.float32))
+        if bc is not None and bc.numel() != N:
+            raise UnimplementedMathError("gemm bias must be a length-N vector")
+        if M and N:
+            L.call("b200_gemm_batched2", code(A), code(pre), A.data_ptr(), B.data_ptr(), pre.data_ptr(), 1, 1, M, N, K, 0, 0,
+                   A.stride(0), A.stride(1), 0, 0, B.stride(0), B.stride(1), 0, 0, N, float(alpha), _ptr(bc), int(epilogue),
+                   _ptr(mask), act.data_ptr(), stream_ptr())
+        return (pre, act, mask) if want_mask else (pre, act)
+    res = gemm(a, b, bias=bias, epilogue=L.EPI_NONE, alpha=alpha, out_dtype=torch.float32, ab_dtype=ab_dtype)
+    fn = {L.EPI_RELU: op_relu, L.EPI_GELU: op_gelu}.get(int(epilogue))
+    act = cast(fn(res) if fn else res, torch.bfloat16)
+    if want_mask:
+        return cast(res, out_dtype), act, op_greater(res, 0.0)
+    return cast(res, out_dtype), act
 
 
 def op_matmul(a, b, transpose_a=False, transpose_b=False, **_):  # eager/core_math_ops/math_matrix.py:21-44

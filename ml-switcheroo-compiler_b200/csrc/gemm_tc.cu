@@ -11,6 +11,7 @@
 // Every mbarrier wait is bounded by a wall-clock limit: on expiry the thread records
 // B200_ERR_TIMEOUT in the device error flag and the CTA winds down (TMEM is freed).
 #include <cuda.h>
+#include <string.h>
 #include <cudaTypedefs.h>
 
 #include "common.cuh"
@@ -73,6 +74,32 @@ __device__ __forceinline__ void tma_load_4d(void* dst, const CUtensorMap* map, u
       : "memory");
 }
 
+// TMA bulk-tensor store (shared -> global), tracked by the issuing thread's bulk group.
+__device__ __forceinline__ void tma_store_4d(const CUtensorMap* map, const void* src, int c0, int c1, int c2, int c3) {
+  asm volatile("cp.async.bulk.tensor.4d.global.shared::cta.bulk_group [%0, {%1, %2, %3, %4}], [%5];" ::"l"(
+                   reinterpret_cast<uint64_t>(map)),
+               "r"(c0), "r"(c1), "r"(c2), "r"(c3), "r"(smem_u32(src))
+               : "memory");
+}
+__device__ __forceinline__ void bulk_commit() { asm volatile("cp.async.bulk.commit_group;" ::: "memory"); }
+__device__ __forceinline__ void bulk_wait_read0() { asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory"); }
+__device__ __forceinline__ void bulk_wait0() { asm volatile("cp.async.bulk.wait_group 0;" ::: "memory"); }
+__device__ __forceinline__ void fence_proxy_async_smem() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
+__device__ __forceinline__ void st_shared_v4(uint32_t addr, uint32_t a, uint32_t b, uint32_t c, uint32_t d) {
+  asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(addr), "r"(a), "r"(b), "r"(c), "r"(d) : "memory");
+}
+__device__ __forceinline__ uint32_t pack_bf16(float a, float b) {
+  __nv_bfloat162 t = __floats2bfloat162_rn(a, b);
+  return *reinterpret_cast<uint32_t*>(&t);
+}
+
+// Epilogue staging per epilogue warp: a 32-row x 32-column chunk of C (fp32: 4 KB with
+// 128-byte rows, or bf16: 2 KB), of C2 (bf16, 2 KB) and of the mask (1 KB), each in the
+// swizzled layout its tensor map names (128B / 64B / 32B), so the 16-byte row pieces
+// the 32 lanes write land in distinct banks.
+constexpr uint32_t EPI_C_OFF = 0, EPI_C2_OFF = 4096, EPI_MASK_OFF = 6144, EPI_WARP_BYTES = 7168;
+constexpr uint32_t EPI_BYTES = 4 * EPI_WARP_BYTES;
+
 // UMMA shared-memory descriptor, SWIZZLE_128B, version 1 (sm_100).
 __device__ __forceinline__ uint64_t smem_desc(uint32_t saddr, uint32_t lbo_bytes, uint32_t sbo_bytes) {
   uint64_t d = 0;
@@ -112,8 +139,10 @@ __device__ __forceinline__ void tmem_ld32(uint32_t taddr, float (&v)[32]) {
 
 struct Args {
   void* C;
+  void* C2;  // optional bf16 copy of the activation; C then receives the pre-activation
   const float* bias;
   uint8_t* aux;
+  int tma_store;  // 1: C / C2 / aux leave through TMA bulk-tensor stores (mapC / mapC2 / mapAux)
   int64_t M, N, K, sC, ldc;
   float alpha;
   int c_dt, epi, a_mn, b_mn, batch;  // batch = b_out * b_in tiles-of-matrices
@@ -134,6 +163,9 @@ __device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
 template <int BN>
 __global__ void __launch_bounds__(THREADS, 1) gemm_tc_kernel(const __grid_constant__ CUtensorMap mapA,
                                                              const __grid_constant__ CUtensorMap mapB,
+                                                             const __grid_constant__ CUtensorMap mapC,
+                                                             const __grid_constant__ CUtensorMap mapC2,
+                                                             const __grid_constant__ CUtensorMap mapAux,
                                                              const __grid_constant__ Args args) {
   constexpr uint32_t A_BYTES = BM * BK * 2;  // 16 KB
   constexpr uint32_t B_BYTES = BN * BK * 2;
@@ -141,7 +173,8 @@ __global__ void __launch_bounds__(THREADS, 1) gemm_tc_kernel(const __grid_consta
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* sA = smem;
   uint8_t* sB = smem + STAGES * A_BYTES;
-  uint64_t* full_bar = reinterpret_cast<uint64_t*>(sB + STAGES * B_BYTES);
+  uint8_t* sEpi = sB + STAGES * B_BYTES;  // 1024-aligned
+  uint64_t* full_bar = reinterpret_cast<uint64_t*>(sEpi + EPI_BYTES);
   uint64_t* empty_bar = full_bar + STAGES;
   uint64_t* acc_full = empty_bar + STAGES;  // [2]
   uint64_t* acc_empty = acc_full + 2;       // [2]
@@ -250,6 +283,8 @@ __global__ void __launch_bounds__(THREADS, 1) gemm_tc_kernel(const __grid_consta
   } else {
     // ---------------- epilogue (warps 2..5) ----------------
     const int q = warp & 3;  // TMEM lane quarter this warp may access
+    const uint32_t stage = smem_u32(sEpi + q * EPI_WARP_BYTES);
+    const bool dual = args.C2 != nullptr;
     uint32_t local = 0;
     for (int tile = blockIdx.x; tile < total; tile += gridDim.x, ++local) {
       const int z = tile / tiles_mn, r = tile % tiles_mn;
@@ -258,8 +293,10 @@ __global__ void __launch_bounds__(THREADS, 1) gemm_tc_kernel(const __grid_consta
       const uint32_t use = local >> 1;
       if (!mbar_wait(&acc_full[b], use & 1)) break;
       tc_fence_after();
-      const int64_t row = (int64_t)m_tile * BM + q * 32 + lane;
+      const int row0 = m_tile * BM + q * 32;
+      const int64_t row = (int64_t)row0 + lane;
       const int64_t col0 = (int64_t)n_tile * BN;
+      const int zo = z / args.b_in, zi = z % args.b_in;
 #pragma unroll 1
       for (int c = 0; c < BN / 32; ++c) {
         float v[32];
@@ -269,21 +306,75 @@ __global__ void __launch_bounds__(THREADS, 1) gemm_tc_kernel(const __grid_consta
 #pragma unroll
           for (int i = 0; i < 32; ++i) v[i] = 0.f;
         }
-        if (row >= args.M) continue;
         const int64_t cbase = col0 + c * 32;
-        if (cbase >= args.N) continue;
-        const int64_t off = (int64_t)(z / args.b_in) * args.sC + (int64_t)(z % args.b_in) * args.sC_in + row * args.ldc + cbase;
-        uint8_t mask[32];
+        if (cbase >= args.N) continue;                    // warp-uniform
+        if (args.tma_store && row0 >= args.M) continue;  // nothing of this warp's rows exists
+        // pre = alpha * acc + bias; act = epi(pre); mask bit = pre > 0
+        uint32_t mbits = 0;
+        float act[32];
 #pragma unroll
         for (int i = 0; i < 32; ++i) {
           const int64_t n = cbase + i;
-          float pre = args.alpha * v[i] + ((args.bias && n < args.N) ? args.bias[n] : 0.f);
-          mask[i] = pre > 0.f;
-          float rr = pre;
-          if (args.epi == B200_EPI_RELU) rr = pre > 0.f ? pre : 0.f;
-          else if (args.epi == B200_EPI_GELU) rr = gelu_tanh(pre);
-          v[i] = rr;
+          const float pre = args.alpha * v[i] + ((args.bias && n < args.N) ? __ldg(args.bias + n) : 0.f);
+          mbits |= (pre > 0.f ? 1u : 0u) << i;
+          float a = pre;
+          if (args.epi == B200_EPI_RELU) a = pre > 0.f ? pre : 0.f;
+          else if (args.epi == B200_EPI_GELU) a = gelu_tanh(pre);
+          act[i] = a;
+          if (!dual) v[i] = a;
+          else v[i] = pre;
         }
+        if (args.tma_store) {
+          // previous chunk's bulk stores must have read the staging buffer
+          if (lane == 0) bulk_wait_read0();
+          __syncwarp();
+          if (args.c_dt == B200_F32) {
+            const uint32_t rb = stage + EPI_C_OFF + (uint32_t)lane * 128u;
+#pragma unroll
+            for (int j = 0; j < 8; ++j)
+              st_shared_v4(rb + ((uint32_t)(j ^ (lane & 7)) << 4), __float_as_uint(v[4 * j]), __float_as_uint(v[4 * j + 1]),
+                           __float_as_uint(v[4 * j + 2]), __float_as_uint(v[4 * j + 3]));
+          } else {
+            const uint32_t rb = stage + EPI_C_OFF + (uint32_t)lane * 64u;
+#pragma unroll
+            for (int j = 0; j < 4; ++j)
+              st_shared_v4(rb + ((uint32_t)(j ^ ((lane >> 1) & 3)) << 4), pack_bf16(v[8 * j], v[8 * j + 1]),
+                           pack_bf16(v[8 * j + 2], v[8 * j + 3]), pack_bf16(v[8 * j + 4], v[8 * j + 5]),
+                           pack_bf16(v[8 * j + 6], v[8 * j + 7]));
+          }
+          if (dual) {
+            const uint32_t rb = stage + EPI_C2_OFF + (uint32_t)lane * 64u;
+#pragma unroll
+            for (int j = 0; j < 4; ++j)
+              st_shared_v4(rb + ((uint32_t)(j ^ ((lane >> 1) & 3)) << 4), pack_bf16(act[8 * j], act[8 * j + 1]),
+                           pack_bf16(act[8 * j + 2], act[8 * j + 3]), pack_bf16(act[8 * j + 4], act[8 * j + 5]),
+                           pack_bf16(act[8 * j + 6], act[8 * j + 7]));
+          }
+          if (args.aux) {
+            // one byte per element: expand the 32 mask bits into 2 x 16 bytes
+            uint32_t w[8];
+#pragma unroll
+            for (int k = 0; k < 8; ++k) {
+              const uint32_t nib = (mbits >> (4 * k)) & 0xFu;
+              w[k] = (nib & 1u) | ((nib >> 1) & 1u) << 8 | ((nib >> 2) & 1u) << 16 | ((nib >> 3) & 1u) << 24;
+            }
+            const uint32_t rb = stage + EPI_MASK_OFF + (uint32_t)lane * 32u;
+            const uint32_t sw = (uint32_t)((lane >> 2) & 1);
+            st_shared_v4(rb + ((0u ^ sw) << 4), w[0], w[1], w[2], w[3]);
+            st_shared_v4(rb + ((1u ^ sw) << 4), w[4], w[5], w[6], w[7]);
+          }
+          fence_proxy_async_smem();
+          __syncwarp();
+          if (lane == 0) {
+            tma_store_4d(&mapC, sEpi + q * EPI_WARP_BYTES + EPI_C_OFF, (int)cbase, row0, zi, zo);
+            if (dual) tma_store_4d(&mapC2, sEpi + q * EPI_WARP_BYTES + EPI_C2_OFF, (int)cbase, row0, zi, zo);
+            if (args.aux) tma_store_4d(&mapAux, sEpi + q * EPI_WARP_BYTES + EPI_MASK_OFF, (int)cbase, row0, zi, zo);
+            bulk_commit();
+          }
+          continue;
+        }
+        if (row >= args.M) continue;
+        const int64_t off = (int64_t)zo * args.sC + (int64_t)zi * args.sC_in + row * args.ldc + cbase;
         const bool full = cbase + 32 <= args.N;
         if (args.c_dt == B200_F32) {
           float* dst = reinterpret_cast<float*>(args.C) + off;
@@ -298,31 +389,30 @@ __global__ void __launch_bounds__(THREADS, 1) gemm_tc_kernel(const __grid_consta
           __nv_bfloat16* dst = reinterpret_cast<__nv_bfloat16*>(args.C) + off;
           if (full && ((reinterpret_cast<uintptr_t>(dst) & 15) == 0)) {
 #pragma unroll
-            for (int i = 0; i < 32; i += 8) {
-              __align__(16) __nv_bfloat162 t[4];
-#pragma unroll
-              for (int j = 0; j < 4; ++j) t[j] = __floats2bfloat162_rn(v[i + 2 * j], v[i + 2 * j + 1]);
-              *reinterpret_cast<uint4*>(dst + i) = *reinterpret_cast<uint4*>(t);
-            }
+            for (int i = 0; i < 32; i += 8)
+              *reinterpret_cast<uint4*>(dst + i) = make_uint4(pack_bf16(v[i], v[i + 1]), pack_bf16(v[i + 2], v[i + 3]),
+                                                              pack_bf16(v[i + 4], v[i + 5]), pack_bf16(v[i + 6], v[i + 7]));
           } else {
             for (int i = 0; i < 32; ++i)
               if (cbase + i < args.N) dst[i] = __float2bfloat16_rn(v[i]);
           }
         }
-        if (args.aux) {
-          uint8_t* mdst = args.aux + off;
-          if (full && ((reinterpret_cast<uintptr_t>(mdst) & 15) == 0)) {
-            uint32_t wv[8];
+        if (dual) {
+          __nv_bfloat16* dst = reinterpret_cast<__nv_bfloat16*>(args.C2) + off;
+          if (full && ((reinterpret_cast<uintptr_t>(dst) & 15) == 0)) {
 #pragma unroll
-            for (int q4 = 0; q4 < 8; ++q4)
-              wv[q4] = (uint32_t)mask[4 * q4] | ((uint32_t)mask[4 * q4 + 1] << 8) | ((uint32_t)mask[4 * q4 + 2] << 16) |
-                       ((uint32_t)mask[4 * q4 + 3] << 24);
-            reinterpret_cast<uint4*>(mdst)[0] = make_uint4(wv[0], wv[1], wv[2], wv[3]);
-            reinterpret_cast<uint4*>(mdst)[1] = make_uint4(wv[4], wv[5], wv[6], wv[7]);
+            for (int i = 0; i < 32; i += 8)
+              *reinterpret_cast<uint4*>(dst + i) = make_uint4(pack_bf16(act[i], act[i + 1]), pack_bf16(act[i + 2], act[i + 3]),
+                                                              pack_bf16(act[i + 4], act[i + 5]), pack_bf16(act[i + 6], act[i + 7]));
           } else {
             for (int i = 0; i < 32; ++i)
-              if (cbase + i < args.N) mdst[i] = mask[i];
+              if (cbase + i < args.N) dst[i] = __float2bfloat16_rn(act[i]);
           }
+        }
+        if (args.aux) {
+          uint8_t* mdst = args.aux + off;
+          for (int i = 0; i < 32; ++i)
+            if (cbase + i < args.N) mdst[i] = (uint8_t)((mbits >> i) & 1u);
         }
       }
       // accumulator b may be overwritten once every epilogue warp has read it
@@ -331,6 +421,7 @@ __global__ void __launch_bounds__(THREADS, 1) gemm_tc_kernel(const __grid_consta
       if (lane == 0) mbar_arrive(&acc_empty[b]);
     }
   }
+  if (warp >= 2 && lane == 0 && args.tma_store) bulk_wait0();  // this warp's bulk stores are complete
   tc_fence_before();
   __syncthreads();
   if (warp == 1) {
@@ -379,9 +470,34 @@ static int make_map(CUtensorMap* map, const void* base, uint64_t d0, uint64_t d1
   return B200_OK;
 }
 
+// Store map for C / C2 / mask: dims (N, M, b_in, b_out) with byte strides (ldc, sC_in,
+// sC_out) * esize, box 32 x 32 (one epilogue warp's chunk), swizzle matching the rows
+// the epilogue writes (128 B fp32 rows, 64 B bf16 rows, 32 B mask rows). Returns false
+// when TMA cannot address the layout (the epilogue then stores directly).
+static bool make_store_map(CUtensorMap* map, void* base, CUtensorMapDataType dt, uint32_t esize, int64_t N, int64_t M,
+                           int64_t b_in, int64_t b_out, int64_t ldc, int64_t sC_in, int64_t sC_out) {
+  auto enc = get_encode();
+  if (!enc || !base || (reinterpret_cast<uintptr_t>(base) & 15)) return false;
+  const uint64_t rowb = (uint64_t)ldc * esize;
+  const uint64_t s2 = b_in > 1 ? (uint64_t)sC_in * esize : rowb * (uint64_t)M;
+  const uint64_t s3 = b_out > 1 ? (uint64_t)sC_out * esize : s2 * (uint64_t)b_in;
+  if (rowb % 16 || s2 % 16 || s3 % 16 || rowb == 0 || s2 == 0 || s3 == 0) return false;
+  if (rowb >= (1ull << 40) || s2 >= (1ull << 40) || s3 >= (1ull << 40)) return false;
+  cuuint64_t dims[4] = {(cuuint64_t)N, (cuuint64_t)M, (cuuint64_t)b_in, (cuuint64_t)b_out};
+  cuuint64_t strides[3] = {rowb, s2, s3};
+  cuuint32_t box[4] = {32, 32, 1, 1};
+  cuuint32_t estr[4] = {1, 1, 1, 1};
+  const CUtensorMapSwizzle sw =
+      esize == 4 ? CU_TENSOR_MAP_SWIZZLE_128B : (esize == 2 ? CU_TENSOR_MAP_SWIZZLE_64B : CU_TENSOR_MAP_SWIZZLE_32B);
+  CUresult r = enc(map, dt, 4, base, dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, sw,
+                   CU_TENSOR_MAP_L2_PROMOTION_NONE, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS;
+}
+
 template <int BN>
-static int launch(const CUtensorMap& ma, const CUtensorMap& mb, const Args& a, int64_t batch, cudaStream_t s) {
-  const size_t smem = (size_t)STAGES * (BM * BK * 2 + BN * BK * 2) + 1024 + 256;
+static int launch(const CUtensorMap& ma, const CUtensorMap& mb, const CUtensorMap& mc, const CUtensorMap& mc2,
+                  const CUtensorMap& maux, const Args& a, int64_t batch, cudaStream_t s) {
+  const size_t smem = (size_t)STAGES * (BM * BK * 2 + BN * BK * 2) + EPI_BYTES + 1024 + 256;
   const int64_t tiles = ceil_div(a.N, BN) * ceil_div(a.M, BM) * batch;  // batch = b_out * b_in
   static bool attr_set[64] = {false};
   int dev = 0;
@@ -391,7 +507,7 @@ static int launch(const CUtensorMap& ma, const CUtensorMap& mb, const Args& a, i
     if (dev >= 0 && dev < 64) attr_set[dev] = true;
   }
   const unsigned grid = (unsigned)std::max<int64_t>(1, std::min<int64_t>(tiles, num_sms()));
-  gemm_tc_kernel<BN><<<grid, THREADS, smem, s>>>(ma, mb, a);
+  gemm_tc_kernel<BN><<<grid, THREADS, smem, s>>>(ma, mb, mc, mc2, maux, a);
   return check_launch("gemm(bf16 tcgen05)");
 }
 
@@ -400,7 +516,7 @@ static int launch(const CUtensorMap& ma, const CUtensorMap& mb, const Args& a, i
 int gemm_bf16_tcgen05_b2(int c_dt, const void* A, const void* B, void* C, int64_t b_out, int64_t b_in, int64_t M, int64_t N,
                          int64_t K, int64_t sA_out, int64_t sA_in, int64_t rsA, int64_t csA, int64_t sB_out, int64_t sB_in,
                          int64_t rsB, int64_t csB, int64_t sC_out, int64_t sC_in, int64_t ldc, float alpha, const float* bias,
-                         int epi, void* aux, cudaStream_t s) {
+                         int epi, void* aux, void* C2, cudaStream_t s) {
   using namespace tc;
   // operand majors: A K-major if csA == 1, MN-major if rsA == 1; B K-major if rsB == 1, MN-major if csB == 1
   int a_mn, b_mn;
@@ -448,6 +564,7 @@ int gemm_bf16_tcgen05_b2(int c_dt, const void* A, const void* B, void* C, int64_
   if (rc) return rc;
   Args a;
   a.C = C;
+  a.C2 = C2;
   a.bias = bias;
   a.aux = (uint8_t*)aux;
   a.M = M;
@@ -468,15 +585,27 @@ int gemm_bf16_tcgen05_b2(int c_dt, const void* A, const void* B, void* C, int64_
   a.b_bc_out = b_bc_out;
   a.b_bc_in = b_bc_in;
   B200_REQUIRE(ceil_div(M, BM) <= 65535, "gemm(bf16): M too large");
-  if (BN == 256) return launch<256>(ma, mb, a, batch, s);
-  return launch<128>(ma, mb, a, batch, s);
+  // epilogue through TMA stores when every output layout is TMA-addressable
+  CUtensorMap mc, mc2, maux;
+  memset(&mc, 0, sizeof(mc));
+  memset(&mc2, 0, sizeof(mc2));
+  memset(&maux, 0, sizeof(maux));
+  const bool c_f32 = c_dt == B200_F32;
+  bool tma = M <= INT32_MAX && N <= INT32_MAX &&
+             make_store_map(&mc, C, c_f32 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT32 : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, c_f32 ? 4 : 2, N,
+                            M, b_in, b_out, ldc, sC_in, sC_out);
+  if (tma && C2) tma = make_store_map(&mc2, C2, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, N, M, b_in, b_out, ldc, sC_in, sC_out);
+  if (tma && aux) tma = make_store_map(&maux, aux, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, N, M, b_in, b_out, ldc, sC_in, sC_out);
+  a.tma_store = tma ? 1 : 0;
+  if (BN == 256) return launch<256>(ma, mb, mc, mc2, maux, a, batch, s);
+  return launch<128>(ma, mb, mc, mc2, maux, a, batch, s);
 }
 
 int gemm_bf16_tcgen05(int c_dt, const void* A, const void* B, void* C, int64_t batch, int64_t M, int64_t N, int64_t K,
                       int64_t sA, int64_t rsA, int64_t csA, int64_t sB, int64_t rsB, int64_t csB, int64_t sC, int64_t ldc,
                       float alpha, const float* bias, int epi, void* aux, cudaStream_t s) {
   return gemm_bf16_tcgen05_b2(c_dt, A, B, C, batch, 1, M, N, K, sA, 0, rsA, csA, sB, 0, rsB, csB, sC, 0, ldc, alpha, bias, epi,
-                              aux, s);
+                              aux, nullptr, s);
 }
 
 }  // namespace b200
@@ -486,7 +615,7 @@ using namespace b200;
 extern "C" int b200_gemm_batched2(int ab_dt, int c_dt, const void* A, const void* B, void* C, int64_t b_out, int64_t b_in,
                                   int64_t M, int64_t N, int64_t K, int64_t sA_out, int64_t sA_in, int64_t rsA, int64_t csA,
                                   int64_t sB_out, int64_t sB_in, int64_t rsB, int64_t csB, int64_t sC_out, int64_t sC_in,
-                                  int64_t ldc, float alpha, const float* bias, int epi, void* aux, void* stream) {
+                                  int64_t ldc, float alpha, const float* bias, int epi, void* aux, void* C2, void* stream) {
   B200_REQUIRE(A && B && C, "gemm_batched2: null operand");
   B200_REQUIRE(b_out >= 0 && b_in >= 0 && M >= 0 && N >= 0 && K >= 0, "gemm_batched2: negative size");
   B200_REQUIRE(ldc >= N, "gemm_batched2: ldc < N");
@@ -501,5 +630,5 @@ extern "C" int b200_gemm_batched2(int ab_dt, int c_dt, const void* A, const void
   }
   if (b_out == 0 || b_in == 0 || M == 0 || N == 0) return B200_OK;
   return gemm_bf16_tcgen05_b2(c_dt, A, B, C, b_out, b_in, M, N, K, sA_out, sA_in, rsA, csA, sB_out, sB_in, rsB, csB, sC_out,
-                              sC_in, ldc, alpha, bias, epi, aux, as_stream(stream));
+                              sC_in, ldc, alpha, bias, epi, aux, C2, as_stream(stream));
 }

@@ -392,3 +392,86 @@ def test_gemm_bf16_two_level_batch_views():
     att = _bf16(r.standard_normal((B_, H, S, S), dtype=np.float32))
     ctx = to_np(ops.gemm(T(att).to(torch.bfloat16), q, ab_dtype=torch.bfloat16))
     np.testing.assert_allclose(ctx, np.matmul(att.astype(np.float64), qn.astype(np.float64)), rtol=1e-4, atol=1e-3)
+
+
+@pytest.mark.parametrize("rows,cols", [(37, 512), (16, 96), (9, 2048), (5, 1000), (3, 3000), (40, 4)])
+@pytest.mark.parametrize("log", [0, 1])
+def test_softmax_rows_scaled_dual_output(rows, cols, log):
+    from b200 import _lib as L
+
+    r = rng(rows * 7 + cols + log)
+    x = (r.standard_normal((rows, cols)) * 4).astype(np.float32)
+    s = np.float32(0.125)
+    t = (x * s).astype(np.float64)
+    e = np.exp(t - t.max(-1, keepdims=True))
+    ref = (t - t.max(-1, keepdims=True) - np.log(e.sum(-1, keepdims=True))) if log else e / e.sum(-1, keepdims=True)
+    X, S = T(x), T(np.array(s, np.float32))
+    Y = torch.empty_like(X)
+    YB = torch.empty(X.shape, dtype=torch.bfloat16, device=X.device)
+    L.call("b200_softmax_rows", X.data_ptr(), S.data_ptr(), Y.data_ptr(), YB.data_ptr(), rows, cols, log, 0)
+    torch.cuda.synchronize()
+    np.testing.assert_allclose(to_np(Y), ref, rtol=1e-4, atol=1e-6)
+    np.testing.assert_allclose(to_np(YB.float()), ref, rtol=1e-2, atol=1e-2 if log else 1e-4)
+
+
+@pytest.mark.parametrize("rows,cols", [(37, 512), (16, 96), (9, 2048), (5, 1000), (3, 3000)])
+def test_softmax_bwd_rows(rows, cols):
+    from b200 import _lib as L
+
+    r = rng(rows + cols)
+    x = r.standard_normal((rows, cols)).astype(np.float32)
+    y = np.exp(x - x.max(-1, keepdims=True))
+    y = (y / y.sum(-1, keepdims=True)).astype(np.float32)
+    g = r.standard_normal((rows, cols)).astype(np.float32)
+    s = np.float32(0.3)
+    y64, g64 = y.astype(np.float64), g.astype(np.float64)
+    ref = s * (y64 * (g64 - (g64 * y64).sum(-1, keepdims=True)))
+    Y, G, S = T(y), T(g), T(np.array(s, np.float32))
+    D = torch.empty_like(Y)
+    DB = torch.empty(Y.shape, dtype=torch.bfloat16, device=Y.device)
+    L.call("b200_softmax_bwd_rows", Y.data_ptr(), G.data_ptr(), S.data_ptr(), D.data_ptr(), DB.data_ptr(), rows, cols, 0)
+    torch.cuda.synchronize()
+    np.testing.assert_allclose(to_np(D), ref, rtol=1e-4, atol=1e-6)
+    np.testing.assert_allclose(to_np(DB.float()), ref, rtol=1e-2, atol=1e-4)
+
+
+@pytest.mark.parametrize("cols", [96, 1024, 2048, 1000])
+def test_layernorm_rows_bf16_output(cols):
+    from b200 import ops
+    from oracle import evaluator as O
+
+    r = rng(cols)
+    x = (r.standard_normal((45, cols)) * 3 + 1).astype(np.float32)
+    g = r.uniform(0.5, 1.5, cols).astype(np.float32)
+    b = r.standard_normal(cols).astype(np.float32)
+    ref = O.execute_op("LayerNorm", x, g, b, eps=1e-5)
+    y, yb = ops.layer_norm(T(x), T(g), T(b), 1e-5, -1, f32=True, bf16=True)
+    np.testing.assert_allclose(to_np(y), ref, rtol=1e-4, atol=1e-5)
+    np.testing.assert_allclose(to_np(yb.float()), ref, rtol=1e-2, atol=1e-2)
+    y2, yb2 = ops.layer_norm(T(x), T(g), T(b), 1e-5, -1, f32=False, bf16=True)
+    assert y2 is None and torch.equal(yb2, yb)
+
+
+@pytest.mark.parametrize("M,N,K", [(300, 384, 256), (200, 136, 72), (64, 40, 128)])
+@pytest.mark.parametrize("epi", ["gelu", "relu"])
+def test_gemm_dual_output_pre_and_bf16_activation(M, N, K, epi):
+    """pre = A.B + bias in fp32 and act(pre) in bf16 from one epilogue (ragged tiles are
+    clipped by the bulk stores)."""
+    from b200 import _lib as L
+    from b200 import ops
+    from oracle import evaluator as O
+
+    r = rng(M + N + K)
+    a = _bf16(r.standard_normal((M, K), dtype=np.float32) * 0.1)
+    b = _bf16(r.standard_normal((K, N), dtype=np.float32) * 0.1)
+    bias = (r.standard_normal(N) * 0.1).astype(np.float32)
+    pre = (a.astype(np.float64) @ b.astype(np.float64) + bias).astype(np.float32)
+    act = O.execute_op("Gelu", pre) if epi == "gelu" else np.maximum(pre, 0)
+    e = L.EPI_GELU if epi == "gelu" else L.EPI_RELU
+    res = ops.gemm(T(a).to(torch.bfloat16), T(b).to(torch.bfloat16), bias=T(bias), epilogue=e, act_bf16=True,
+                   want_mask=(epi == "relu"), ab_dtype=torch.bfloat16)
+    np.testing.assert_allclose(to_np(res[0]), pre, rtol=1e-4, atol=1e-4)
+    assert res[1].dtype == torch.bfloat16
+    np.testing.assert_allclose(to_np(res[1].float()), act, rtol=1e-2, atol=1e-2)
+    if epi == "relu":
+        assert (to_np(res[2]) == (pre > 0)).mean() > 0.999

@@ -151,3 +151,41 @@ def test_xent_pattern_matches_reference_graphs(case):
             users.setdefault(i, []).append(n.id)
     found = find_xent(g, live, meta, users, set(g.outputs))
     assert len(found) == 1 and set(found[0].outputs) == {"dx", "picked"}
+
+
+def test_attention_softmax_patterns_match_transformer_graph():
+    """Every attention softmax (scaled by the attn_scale input) and its VJP fuse; the
+    VJP output feeds only GEMMs, so it is produced in bf16 alone."""
+    from b200 import ops
+    from b200.fusion import find_softmax, find_softmax_bwd
+
+    g, meta = _meta_from_oracle("transformer_small")
+    need, stack = set(), list(g.outputs)
+    while stack:
+        v = stack.pop()
+        if v not in need and v in g.nodes:
+            need.add(v)
+            stack.extend(g.nodes[v].inputs)
+    live = {n.id: n for n in g.topo_order() if n.op_type != "Input" and n.id in need}
+    users = {}
+    for n in live.values():
+        for i in n.inputs:
+            users.setdefault(i, []).append(n.id)
+    old = ops.Config.matmul_dtype
+    ops.Config.matmul_dtype = "bf16"
+    try:
+        fwd = find_softmax(g, live, meta, users, set(g.outputs))
+        bwd = find_softmax_bwd(g, live, meta, users, set(g.outputs))
+    finally:
+        ops.Config.matmul_dtype = old
+    n_layers = 2
+    fwd = [m for m in fwd if m.bind["log"] == "False"]  # the LogSoftmax of the logits goes to the xent kernel
+    assert len(fwd) == n_layers and len(bwd) == n_layers
+    scale = g.roles["attn_scale"]
+    for m in fwd:
+        assert m.bind["scale"] == scale and m.bind["log"] == "False"
+        assert m.bind["bf16"] == "True" and m.bind["f32"] == "True"  # att@v GEMM + the VJP
+    for m in bwd:
+        assert m.bind["scale"] == scale
+        assert m.bind["bf16"] == "True" and m.bind["f32"] == "False"
+    assert {m.bind["y"] for m in bwd} == {m.bind["y"] for m in fwd}
