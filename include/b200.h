@@ -260,6 +260,17 @@ size_t b200_mask_mul_colsum_workspace_bytes(int64_t rows, int64_t cols);
 int b200_mask_mul_colsum(const float* g, const uint8_t* mask, void* y_bf16, float* y_f32, float* colsum, int64_t rows,
                          int64_t cols, void* workspace, size_t workspace_bytes, void* stream);
 
+/* GELU (tanh approximation) backward with its bias gradient in one pass: the VJP chain
+ * the AD pass emits for Gelu (eager/core_math_ops/math_nn.py:184-199 forward; elementwise
+ * ops numpy/eager/math_binary.py:9-51 and np.tanh) times the cotangent, and the column
+ * sums of the result (BroadcastReduce, eager/core_math_ops/math_reduction.py:192-224):
+ *   dp = g * (0.5 (1 + t) + 0.5 p (1 - t^2) k (1 + 3 c p^2)),  t = tanh(k (p + c p^3)).
+ * g, p [rows, cols] fp32; dp as bf16 and/or fp32 (either may be NULL), colsum [cols]
+ * (may be NULL). workspace >= b200_gelu_bwd_colsum_workspace_bytes(rows, cols). */
+size_t b200_gelu_bwd_colsum_workspace_bytes(int64_t rows, int64_t cols);
+int b200_gelu_bwd_colsum(const float* g, const float* p, void* y_bf16, float* y_f32, float* colsum, int64_t rows,
+                         int64_t cols, void* workspace, size_t workspace_bytes, void* stream);
+
 /* Fused LogSoftmax (numpy/eager/math_advanced/math_log_exp.py:87-104) -> TakeAlongAxis of
  * one label per row (numpy/eager/advanced_indexing.py:163-177) and its VJP (ZerosLike +
  * ScatterAdd advanced_indexing.py:309-326, then the LogSoftmax rule g - exp(ls) sum(g)):

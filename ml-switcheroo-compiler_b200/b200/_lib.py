@@ -71,6 +71,8 @@ SIGNATURES = {
     "b200_reduce": ([_I32, _P, _P, _I64, _I64, _I64, _I32, _P], C.c_int),
     "b200_argmax": ([_I32, _P, _P, _I64, _I64, _I64, _P], C.c_int),
     "b200_softmax": ([_P, _P, _I64, _I64, _I32, _P], C.c_int),
+    "b200_gelu_bwd_colsum_workspace_bytes": ([_I64, _I64], C.c_size_t),
+    "b200_gelu_bwd_colsum": ([_P, _P, _P, _P, _P, _I64, _I64, _P, C.c_size_t, _P], C.c_int),
     "b200_layernorm_rows": ([_P, _P, _P, _P, _P, _I64, _I64, _F32, _P], C.c_int),
     "b200_layernorm_input_grad_rows": ([_P, _P, _P, _P, _P, _I64, _I64, _F32, _P], C.c_int),
     "b200_softmax_rows": ([_P, _P, _P, _P, _I64, _I64, _I32, _P], C.c_int),

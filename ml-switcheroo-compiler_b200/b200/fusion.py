@@ -335,6 +335,7 @@ def find_gemm_epilogue(g: Graph, live: dict[str, Node], meta: dict[str, Meta], u
         kind = "gemm_bias" if op == "Add" else "gemm_" + op.lower()
         bf, f32 = gemm_use(bind["act"], live, users, outputs)
         bind["bf16"] = str(bf and not f32)
+        bind["twin"] = str(bf and f32)  # fp32 result plus a bf16 copy for the GEMM consumers
         if op != "Add" and leaks(bind["pre"]):
             # the VJP reads the pre-activation (GELU): the epilogue writes pre in fp32 and,
             # when the activation only feeds bf16 GEMMs, the activation in bf16 beside it
@@ -355,12 +356,18 @@ def gemm_epilogue_step(m: Match) -> Step:
     want_mask = "mask" in o
     dual = m.kind.endswith("_dual")
     out_dt = torch.bfloat16 if (b.get("bf16") == "True" and not dual) else torch.float32
+    twin = not dual and b.get("twin") == "True" and epi == L.EPI_NONE
     ins = [b["A"], b["B"], b["bias"]]
 
     def run(env: dict) -> None:
         res = ops.gemm(env[b["A"]], env[b["B"]], bias=env[b["bias"]], epilogue=epi, want_mask=want_mask, out_dtype=out_dt,
-                       act_bf16=dual)
-        if dual:
+                       act_bf16=dual or twin)
+        if twin:
+            env[o["act"]] = res[0]
+            ops.register_cast(res[0], res[1])
+            if want_mask:
+                env[o["mask"]] = res[2]
+        elif dual:
             env[o["pre"]], env[o["act"]] = res[0], res[1]
             if want_mask:
                 env[o["mask"]] = res[2]
@@ -369,8 +376,93 @@ def gemm_epilogue_step(m: Match) -> Step:
         else:
             env[o["act"]] = res
 
-    label = m.kind + ("[bf16]" if out_dt == torch.bfloat16 else "")
+    label = m.kind + ("[bf16]" if out_dt == torch.bfloat16 else ("[+bf16]" if twin else ""))
     return Step(list(o.values()), ins, run, label)
+
+
+def _perm_of(n: Node, ndim: int) -> list[int]:
+    axes = n.attributes.get("axes", n.attributes.get("perm"))
+    if axes is None:
+        return list(reversed(range(ndim)))
+    return [int(a) % ndim for a in axes]
+
+
+def _contig_strides(shape: tuple) -> list[int]:
+    st, acc = [], 1
+    for d in reversed(shape):
+        st.append(acc)
+        acc *= max(1, d)
+    return list(reversed(st))
+
+
+def find_matmul_transpose(g: Graph, live: dict[str, Node], meta: dict[str, Meta], users: dict[str, list[str]],
+                          outputs: set[str], taken: set[str]) -> list[Match]:
+    """Transpose(Matmul(a, b), perm) where the Matmul feeds nothing else: the GEMM writes
+    straight into the transposed (contiguous) layout, so the Transpose and any Reshape
+    after it are views (attention's head merge / split of q, k, v and their gradients)."""
+    found = []
+    for tid, tn in live.items():
+        if _op_name(tn) != "Transpose" or len(tn.inputs) != 1 or tid in taken:
+            continue
+        mm = tn.inputs[0]
+        mn = live.get(mm)
+        if mn is None or mm in taken or _op_name(mn) != "Matmul" or len(mn.inputs) != 2:
+            continue
+        if mm in outputs or users.get(mm) != [tid]:
+            continue
+        mo, to = meta.get(mm), meta.get(tid)
+        if mo is None or to is None or mo.scalar or len(mo.shape) < 3 or mo.dtype != torch.float32:
+            continue
+        nd = len(mo.shape)
+        perm = _perm_of(tn, nd)
+        inv = [perm.index(i) for i in range(nd)]
+        cst = [_contig_strides(to.shape)[inv[i]] for i in range(nd)]  # strides of C inside Y
+        if cst[-1] == 1:
+            swap = False
+        elif cst[-2] == 1:
+            swap = True
+        else:
+            continue
+        bf, f32 = gemm_use(tid, live, users, outputs)
+        bind = {"mm": mm, "t": tid, "a": mn.inputs[0], "b": mn.inputs[1], "perm": ",".join(map(str, perm)),
+                "swap": str(swap), "bf16": str(bf), "f32": str(f32)}
+        found.append(Match("matmul_transpose", bind, {mm, tid}, {"y": tid}))
+    return found
+
+
+def matmul_transpose_step(m: Match, meta: dict[str, Meta]) -> Step:
+    b = m.bind
+    mn = None
+    perm = [int(x) for x in b["perm"].split(",")]
+    inv = [perm.index(i) for i in range(len(perm))]
+    yshape = meta[b["t"]].shape
+    swap, bf, f32 = b["swap"] == "True", b["bf16"] == "True", b["f32"] == "True"
+    del mn
+
+    def run(env: dict, _kw=None) -> None:
+        a, bb = env[b["a"]], env[b["b"]]
+        kw = _kw or {}
+        if kw.get("transpose_a"):
+            a = a.transpose(-1, -2)
+        if kw.get("transpose_b"):
+            bb = bb.transpose(-1, -2)
+        y, yb = _out_buffers(yshape, f32, bf)
+        prim = y if y is not None else yb
+        out = prim.permute(*inv)
+        out2 = yb.permute(*inv) if (y is not None and yb is not None) else None
+        if swap:
+            ok = ops.gemm_out(bb.transpose(-1, -2), a.transpose(-1, -2), out.transpose(-1, -2),
+                              None if out2 is None else out2.transpose(-1, -2))
+        else:
+            ok = ops.gemm_out(a, bb, out, out2)
+        if not ok:
+            res = ops.gemm(a, bb)
+            yc = ops.contiguous(res.permute(*perm))
+            y = yc if f32 else None
+            yb = ops.cast(yc, torch.bfloat16) if bf else None
+        _publish(env, b["t"], y, yb)
+
+    return Step([b["t"]], [b["a"], b["b"]], run, "matmul_T" + ("[bf16]" if bf and not f32 else ("[+bf16]" if bf else "")))
 
 
 def layernorm_step(n: Node, f32: bool) -> Step:
@@ -390,9 +482,9 @@ def layernorm_step(n: Node, f32: bool) -> Step:
     return Step([n.id], ins, run, "LayerNorm" + ("" if f32 else "[bf16]"))
 
 
-def matmul_step(n: Node, bf16_out: bool) -> Step:
+def matmul_step(n: Node, bf16_out: bool, shape: tuple = (), twin: bool = False) -> Step:
     """A Matmul node without a fused epilogue; its output is written in bf16 when it
-    only feeds bf16 GEMMs."""
+    only feeds bf16 GEMMs, or in fp32 with a bf16 twin (``twin``) when both are read."""
     kw = node_kwargs(n, "Matmul")
     ta, tb = bool(kw.get("transpose_a")), bool(kw.get("transpose_b"))
     a_id, b_id = n.inputs[0], n.inputs[1]
@@ -404,9 +496,14 @@ def matmul_step(n: Node, bf16_out: bool) -> Step:
             a = a.transpose(-1, -2)
         if tb:
             bb = bb.transpose(-1, -2)
+        if twin:
+            y, yb = _out_buffers(shape, True, True)
+            if ops.gemm_out(a, bb, y, yb):
+                _publish(env, n.id, y, yb)
+                return
         env[n.id] = ops.gemm(a, bb, out_dtype=out_dt)
 
-    return Step([n.id], [a_id, b_id], run, "Matmul" + ("[bf16]" if bf16_out else ""))
+    return Step([n.id], [a_id, b_id], run, "Matmul" + ("[bf16]" if bf16_out else ("[+bf16]" if twin else "")))
 
 
 # ----------------------------------------------------------------------------------
@@ -545,6 +642,75 @@ def xent_step(m: Match, meta: dict[str, Meta]) -> Step:
             env[o["picked"]] = picked
 
     return Step(list(o.values()), [b["x"], b["labels"], b["d"]], run, "xent_fwd_bwd")
+
+
+# ----------------------------------------------------------------------------------
+# pattern: GELU backward  dp = g * gelu'(p)  (+ bias gradient BroadcastReduce(dp, bias))
+# ----------------------------------------------------------------------------------
+def find_gelu_bwd(g: Graph, live: dict[str, Node], meta: dict[str, Meta], users: dict[str, list[str]],
+                  outputs: set[str]) -> list[Match]:
+    root = Op("Multiply", Var("g"), gelu_tanh_deriv(Var("p")), name="dp")
+    found = []
+    for nid, node in live.items():
+        if _op_name(node) != "Multiply":
+            continue
+        bind: dict[str, str] = {}
+        cov: set[str] = set()
+        if not match(root, nid, g, bind, cov):
+            continue
+        mg, mp, mo = meta.get(bind["g"]), meta.get(bind["p"]), meta.get(nid)
+        if mg is None or mp is None or mo is None or mg.scalar or mp.scalar or len(mp.shape) < 1:
+            continue
+        if mg.shape != mp.shape or mo.shape != mp.shape or mg.dtype != torch.float32 or mp.dtype != torch.float32:
+            continue
+        cov = {c for c in cov if c in live or g.nodes[c].op_type == "Constant"}
+        inner = [c for c in cov if c != nid and c in live]
+        if any(c in outputs or any(u not in cov for u in users.get(c, [])) for c in inner):
+            continue
+        C = mp.shape[-1]
+        br = None
+        for u in users.get(nid, []):
+            un = live.get(u)
+            if un is not None and _op_name(un) == "BroadcastReduce" and un.inputs[0] == nid:
+                mb = meta.get(un.inputs[1])
+                if mb is not None and not mb.scalar and mb.shape == (C,) and meta[u].shape == (C,):
+                    br = u
+                    break
+        skip = frozenset([br]) if br else frozenset()
+        bf, f32 = gemm_use(nid, live, users, outputs, skip)
+        bind.update({"db": br or "", "bf16": str(bf), "f32": str(f32)})
+        outs = {"dp": nid}
+        if br:
+            outs["db"] = br
+            cov.add(br)
+        found.append(Match("gelu_bwd", bind, cov, outs))
+    return found
+
+
+def gelu_bwd_step(m: Match, meta: dict[str, Meta]) -> Step:
+    b, o = m.bind, m.outputs
+    shape = meta[o["dp"]].shape
+    C = shape[-1]
+    R = math.prod(shape[:-1])
+    bf, f32 = b["bf16"] == "True", b["f32"] == "True"
+    ws_bytes = int(L.lib().b200_gelu_bwd_colsum_workspace_bytes(R, C))
+
+    def run(env: dict) -> None:
+        gg = ops.contiguous(ops.cast(env[b["g"]], torch.float32))
+        pp = ops.contiguous(ops.cast(env[b["p"]], torch.float32))
+        dev = ops.device()
+        y, yb = _out_buffers(shape, f32, bf)
+        db = torch.empty(C, dtype=torch.float32, device=dev) if "db" in o else None
+        ws = torch.empty(max(1, ws_bytes), dtype=torch.uint8, device=dev)
+        L.call("b200_gelu_bwd_colsum", gg.data_ptr(), pp.data_ptr(), None if yb is None else yb.data_ptr(),
+               None if y is None else y.data_ptr(), None if db is None else db.data_ptr(), R, C, ws.data_ptr(), ws_bytes,
+               ops.stream_ptr())
+        _publish(env, o["dp"], y, yb)
+        if db is not None:
+            env[o["db"]] = db
+
+    label = "gelu_bwd" + ("_bias" if "db" in o else "") + ("[bf16]" if bf and not f32 else "")
+    return Step(list(o.values()), [b["g"], b["p"]], run, label)
 
 
 # ----------------------------------------------------------------------------------
@@ -877,13 +1043,26 @@ def _alloc_registers(g: Graph, nodes: list[Node], ext_in: list[str], outs: list[
     return prog, {o: reg[o] for o in outs}
 
 
-def ew_cluster_step(g: Graph, nodes: list[Node], meta: dict[str, Meta], users, outputs) -> Step:
+def ew_cluster_step(g: Graph, nodes: list[Node], meta: dict[str, Meta], users, outputs, live=None) -> Step:
     ext_in, outs = _cluster_io(g, nodes, users, outputs)
     prog, out_reg = _alloc_registers(g, nodes, ext_in, outs)
     shape = meta[nodes[-1].id].shape
     out_dtypes = [meta[o].dtype for o in outs]
+    # float outputs that feed bf16 GEMMs: stored in bf16 (alone, or as a registered twin)
+    twins: list[str] = []
+    if live is not None:
+        for i, o in enumerate(outs):
+            if out_dtypes[i] != torch.float32 or len(meta[o].shape) < 2:
+                continue
+            bf, f32 = gemm_use(o, live, users, outputs)
+            if bf and not f32:
+                out_dtypes[i] = torch.bfloat16
+            elif bf and len(outs) + len(twins) < L.EW_MAX_OUT:
+                twins.append(o)
     ops_seq = [(L.EW[name], d, a, b, c, imm) for (name, d, a, b, c, imm) in prog]
     label = "ew[" + ",".join(_op_name(n) for n in nodes) + "]"
+    if any(dt == torch.bfloat16 for dt in out_dtypes) or twins:
+        label += "[bf16]"
 
     def run(env: dict) -> None:
         p = ops.Prog()
@@ -896,9 +1075,12 @@ def ew_cluster_step(g: Graph, nodes: list[Node], meta: dict[str, Meta], users, o
         p.inputs = vals
         p.ins = list(ops_seq)
         p.nreg = L.EW_MAX_REG
-        res = p.run([(out_reg[o], dt) for o, dt in zip(outs, out_dtypes)], shape)
+        specs = [(out_reg[o], dt) for o, dt in zip(outs, out_dtypes)] + [(out_reg[o], torch.bfloat16) for o in twins]
+        res = p.run(specs, shape)
         for o, r in zip(outs, res):
             env[o] = r
+        for o, r in zip(twins, res[len(outs):]):
+            ops.register_cast(env[o], r)
 
     return Step(outs, list(ext_in), run, label)
 
@@ -992,6 +1174,12 @@ def plan_steps(graph: Graph, nodes: list[Node], sample: dict[str, Any]) -> list[
         groups.append((sorted(m.covered), mask_bwd_step(m, meta)))
         taken |= m.covered
 
+    for m in find_gelu_bwd(graph, live, meta, users, outputs):
+        if m.covered & taken:
+            continue
+        groups.append((sorted(m.covered), gelu_bwd_step(m, meta)))
+        taken |= m.covered
+
     for m in find_softmax_bwd(graph, live, meta, users, outputs):
         if m.covered & taken:
             continue
@@ -1002,6 +1190,19 @@ def plan_steps(graph: Graph, nodes: list[Node], sample: dict[str, Any]) -> list[
         if m.covered & taken:
             continue
         groups.append((sorted(m.covered), softmax_step(m, meta)))
+        taken |= m.covered
+
+    # GEMMs that write straight into a transposed layout
+    for m in find_matmul_transpose(graph, live, meta, users, outputs, taken):
+        if m.covered & taken:
+            continue
+        mm = graph.nodes[m.bind["mm"]]
+        st = matmul_transpose_step(m, meta)
+        kw = node_kwargs(mm, "Matmul")
+        if kw.get("transpose_a") or kw.get("transpose_b"):
+            fn = st.fn
+            st.fn = lambda env, _fn=fn, _kw=dict(kw): _fn(env, _kw)
+        groups.append((sorted(m.covered), st))
         taken |= m.covered
 
     # LayerNorms whose output feeds bf16 GEMMs also write (or only write) bf16
@@ -1024,16 +1225,20 @@ def plan_steps(graph: Graph, nodes: list[Node], sample: dict[str, Any]) -> list[
         if mo is None or mo.scalar or len(mo.shape) < 2:
             continue
         bf, f32 = gemm_use(n.id, live, users, outputs)
-        if bf and not f32:
-            groups.append(([n.id], matmul_step(n, True)))
+        if bf:
+            groups.append(([n.id], matmul_step(n, not f32, mo.shape, twin=f32)))
             taken.add(n.id)
 
     # 2. elementwise clusters
     rest = [n for n in nodes if n.id not in taken]
     for cl in cluster_elementwise(graph, rest, meta, taken, users, outputs):
         if len(cl) == 1:
-            continue
-        groups.append(([n.id for n in cl], ew_cluster_step(graph, cl, meta, users, outputs)))
+            mo = meta.get(cl[0].id)
+            if mo is None or mo.scalar or mo.dtype != torch.float32 or len(mo.shape) < 2:
+                continue
+            if not gemm_use(cl[0].id, live, users, outputs)[0]:
+                continue
+        groups.append(([n.id for n in cl], ew_cluster_step(graph, cl, meta, users, outputs, live)))
         taken |= {n.id for n in cl}
 
     # constants feeding only fused steps are folded into the programs

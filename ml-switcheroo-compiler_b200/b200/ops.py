@@ -735,6 +735,11 @@ def gemm(a: torch.Tensor, b: torch.Tensor, *, bias: torch.Tensor | None = None, 
         # on the CUDA-core kernel in fp32, which is at least as precise as bf16 math
         ab_dtype = torch.float32
         A, B = cast(a, torch.float32), cast(b, torch.float32)
+    if (ab_dtype == torch.bfloat16 and Z == 1 and bias is None and not want_mask and epilogue == L.EPI_NONE
+            and alpha == 1.0):
+        S = _split_k(M, N, K)
+        if S > 1:
+            return _gemm_split_k(A.reshape(M, K), B.reshape(K, N), S, out_dtype).view(*batch_shape, M, N)
     C_ = torch.empty(*batch_shape, M, N, dtype=out_dtype, device=device())
     mask = torch.empty(*batch_shape, M, N, dtype=torch.bool, device=device()) if want_mask else None
     bc = None if bias is None else contiguous(cast(bias, torch.float32))
@@ -779,6 +784,93 @@ def gemm(a: torch.Tensor, b: torch.Tensor, *, bias: torch.Tensor | None = None, 
     if squeeze_n:
         C_ = C_.squeeze(-1)
     return (C_, mask) if want_mask else C_
+
+
+_SMS: dict[int, int] = {}
+
+
+def _num_sms() -> int:
+    d = torch.cuda.current_device()
+    if d not in _SMS:
+        _SMS[d] = int(torch.cuda.get_device_properties(d).multi_processor_count)
+    return _SMS[d]
+
+
+def _split_k(M: int, N: int, K: int) -> int:
+    """Number of K chunks for a GEMM whose output tiles cannot fill the GPU (weight
+    gradients: small M x N, K = tokens). Chunks are equal, multiples of 64."""
+    tiles = -(-M // 128) * -(-N // (256 if N > 128 else 128))
+    sms = _num_sms()
+    if tiles * 2 > sms or K < 4096:
+        return 1
+    want = max(1, min(sms // tiles, K // 2048))
+    for S in range(want, 1, -1):
+        if K % S == 0 and (K // S) % 64 == 0:
+            return S
+    return 1
+
+
+def _gemm_split_k(A: torch.Tensor, B: torch.Tensor, S: int, out_dtype: torch.dtype) -> torch.Tensor:
+    """C = A.B as S partial products over equal K chunks (one batched tcgen05 launch, the
+    chunk index as the batch level) and a fixed-order sum of the partials."""
+    M, K = A.shape
+    N = B.shape[1]
+    Kc = K // S
+    part = torch.empty(S, M, N, dtype=torch.float32, device=device())
+    # chunk s of A is columns [s Kc, (s+1) Kc), of B rows [s Kc, (s+1) Kc)
+    L.call("b200_gemm_batched2", code(A), code(part), A.data_ptr(), B.data_ptr(), part.data_ptr(), 1, S, M, N, Kc, 0,
+           Kc * A.stride(1), A.stride(0), A.stride(1), 0, Kc * B.stride(0), B.stride(0), B.stride(1), 0, M * N, N, 1.0, None,
+           L.EPI_NONE, None, None, stream_ptr())
+    C_ = torch.empty(M, N, dtype=torch.float32, device=device())
+    L.call("b200_reduce", code(part), part.data_ptr(), C_.data_ptr(), 1, S, M * N, L.RED_SUM, stream_ptr())
+    return C_ if out_dtype == torch.float32 else cast(C_, out_dtype)
+
+
+def gemm_out(a: torch.Tensor, b: torch.Tensor, out: torch.Tensor, out2: torch.Tensor | None = None,
+             ab_dtype: torch.dtype | None = None) -> bool:
+    """a.b written into the preallocated view ``out`` (any batch / row strides, unit
+    column stride) and optionally its bf16 twin ``out2`` (same element strides), by the
+    tcgen05 kernel with <= 2 batch levels. Returns False, writing nothing, when the
+    operands or ``out`` do not fit that path."""
+    if ab_dtype is None:
+        ab_dtype = torch.bfloat16 if Config.matmul_dtype == "bf16" else torch.float32
+    if ab_dtype != torch.bfloat16 or a.dim() < 2 or b.dim() < 2:
+        return False
+    M, K = a.shape[-2], a.shape[-1]
+    K2, N = b.shape[-2], b.shape[-1]
+    if K != K2:
+        raise ValueError(f"matmul: shapes {tuple(a.shape)} and {tuple(b.shape)} not aligned")
+    batch_shape = _bshape([a.shape[:-2], b.shape[:-2]])
+    if tuple(out.shape) != (*batch_shape, M, N) or out.stride(-1) != 1 or out.stride(-2) < N:
+        return False
+    if out2 is not None and (out2.dtype != torch.bfloat16 or out2.stride() != out.stride() or out2.shape != out.shape):
+        return False
+    A = _gemm_operand(a, torch.bfloat16)
+    B = _gemm_operand(b, torch.bfloat16) if A is not None else None
+    if A is None or B is None:
+        return False
+    nb = len(batch_shape)
+    sa = list(A.expand(*batch_shape, M, K).stride()[:nb]) if A.dim() > 2 else [0] * nb
+    sb = list(B.expand(*batch_shape, K, N).stride()[:nb]) if B.dim() > 2 else [0] * nb
+    sc = list(out.stride()[:nb])
+    merged: list[list[int]] = []
+    for sz, x, y, z in zip(batch_shape, sa, sb, sc):
+        if sz == 1:
+            continue
+        if merged and merged[-1][1] == x * sz and merged[-1][2] == y * sz and merged[-1][3] == z * sz:
+            merged[-1] = [merged[-1][0] * sz, x, y, z]
+        else:
+            merged.append([sz, x, y, z])
+    if len(merged) > 2:
+        return False
+    while len(merged) < 2:
+        merged.insert(0, [1, 0, 0, 0])
+    (bo, sao, sbo, sco), (bi, sai, sbi, sci) = merged
+    if math.prod(batch_shape) and M and N:
+        L.call("b200_gemm_batched2", code(A), code(out), A.data_ptr(), B.data_ptr(), out.data_ptr(), bo, bi, M, N, K, sao, sai,
+               A.stride(-2), A.stride(-1), sbo, sbi, B.stride(-2), B.stride(-1), sco, sci, out.stride(-2), 1.0, None,
+               L.EPI_NONE, None, _ptr(out2), stream_ptr())
+    return True
 
 
 def _gemm_dual(a, b, *, bias, epilogue, alpha, out_dtype, want_mask, ab_dtype):

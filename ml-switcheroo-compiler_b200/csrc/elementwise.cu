@@ -11,36 +11,9 @@
 //    128-bit loads/stores for fp32 operands (16-byte aligned bases).
 //  * strided: arbitrary per-input strides over up to 6 dims (broadcast, transposed
 //    views); offsets come from one index decomposition per element.
-#include "common.cuh"
+#include "ew_common.cuh"
 
 namespace b200 {
-
-struct EwParams {
-  b200_ew_program p;
-  const void* in[B200_EW_MAX_IN];
-  void* out[B200_EW_MAX_OUT];
-  int64_t n;
-  // 32-bit strided path: per-dim size, fast-division multiplier and shift, 32-bit strides
-  uint32_t dsz[B200_EW_MAX_DIM], dmul[B200_EW_MAX_DIM], dshr[B200_EW_MAX_DIM];
-  int32_t st32[B200_EW_MAX_IN][B200_EW_MAX_DIM];
-  // flat path: per-input mode (0 dense, 1 scalar, 2 vector along the last dim) and the
-  // last-dim length for mode 2 (fast division)
-  int32_t mode[B200_EW_MAX_IN];
-  int64_t lastdim;
-  uint32_t ld_mul, ld_shr;
-};
-
-// n / d for 32-bit n with a precomputed (mul, shr): q = (umulhi(n, mul) + n) >> shr
-__device__ __forceinline__ uint32_t fast_div(uint32_t n, uint32_t mul, uint32_t shr) {
-  return (uint32_t)(((uint64_t)__umulhi(n, mul) + n) >> shr);
-}
-static void fastdiv_params(uint32_t d, uint32_t& mul, uint32_t& shr) {
-  uint32_t l = 0;
-  while (((uint64_t)1 << l) < d) ++l;
-  mul = (uint32_t)((((uint64_t)1 << 32) * (((uint64_t)1 << l) - d)) / d + 1);
-  if (d == 1) mul = 0;
-  shr = l;
-}
 
 template <int V>
 __device__ __forceinline__ void ew_exec(const b200_ew_program& p, float (&r)[B200_EW_MAX_REG][V],
@@ -83,58 +56,6 @@ __device__ __forceinline__ void ew_exec(const b200_ew_program& p, float (&r)[B20
         default: res = 0.f; break;
       }
       r[d][v] = res;
-    }
-  }
-}
-
-// flat path: 4 elements per thread-iteration
-__global__ void __launch_bounds__(256) ew_flat_kernel(const __grid_constant__ EwParams P) {
-  const b200_ew_program& p = P.p;
-  float r[B200_EW_MAX_REG][4];
-  float ld[B200_EW_MAX_IN][4];
-  float st[B200_EW_MAX_OUT][4];
-#pragma unroll
-  for (int i = 0; i < B200_EW_MAX_REG; ++i)
-#pragma unroll
-    for (int v = 0; v < 4; ++v) r[i][v] = 0.f;
-  const int64_t n = P.n;
-  const int64_t nvec = (n + 3) / 4;
-  for (int64_t q = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; q < nvec; q += (int64_t)gridDim.x * blockDim.x) {
-    const int64_t base = q * 4;
-    const bool full = base + 4 <= n;
-    for (int j = 0; j < p.n_in; ++j) {
-      if (P.mode[j] == 1) {
-        float s = load_as_f32(P.in[j], 0, p.in_dtype[j]);
-#pragma unroll
-        for (int v = 0; v < 4; ++v) ld[j][v] = s;
-      } else if (P.mode[j] == 2) {
-        // column vector: element index modulo the last dim (lastdim % 4 == 0 here)
-        const uint32_t b32 = (uint32_t)base;  // n < 2^31 whenever a vector-mode input exists
-        const int64_t col = (int64_t)(b32 - fast_div(b32, P.ld_mul, P.ld_shr) * (uint32_t)P.lastdim);
-        if (full && p.in_dtype[j] == B200_F32) {
-          float4 t = *reinterpret_cast<const float4*>(reinterpret_cast<const float*>(P.in[j]) + col);
-          ld[j][0] = t.x; ld[j][1] = t.y; ld[j][2] = t.z; ld[j][3] = t.w;
-        } else {
-#pragma unroll
-          for (int v = 0; v < 4; ++v) ld[j][v] = (base + v < n) ? load_as_f32(P.in[j], col + v, p.in_dtype[j]) : 0.f;
-        }
-      } else if (full && p.in_dtype[j] == B200_F32) {
-        float4 t = reinterpret_cast<const float4*>(P.in[j])[q];
-        ld[j][0] = t.x; ld[j][1] = t.y; ld[j][2] = t.z; ld[j][3] = t.w;
-      } else {
-#pragma unroll
-        for (int v = 0; v < 4; ++v) ld[j][v] = (base + v < n) ? load_as_f32(P.in[j], base + v, p.in_dtype[j]) : 0.f;
-      }
-    }
-    ew_exec<4>(p, r, ld, st);
-    for (int o = 0; o < p.n_out; ++o) {
-      if (full && p.out_dtype[o] == B200_F32) {
-        reinterpret_cast<float4*>(P.out[o])[q] = make_float4(st[o][0], st[o][1], st[o][2], st[o][3]);
-      } else {
-#pragma unroll
-        for (int v = 0; v < 4; ++v)
-          if (base + v < n) store_from_f32(P.out[o], base + v, p.out_dtype[o], st[o][v]);
-      }
     }
   }
 }
@@ -242,7 +163,8 @@ extern "C" int b200_ew_run(const b200_ew_program* prog, const void* const* input
   }
   if (n == 0) return B200_OK;
 
-  // flat path when every input is dense-over-output or scalar and vector stores are aligned
+  // flat path when every input is dense over the output, a scalar, a vector along the
+  // last dim or one value per row of the last dim
   bool flat = true;
   int64_t dense[B200_EW_MAX_DIM];
   {
@@ -253,36 +175,38 @@ extern "C" int b200_ew_run(const b200_ew_program* prog, const void* const* input
     }
   }
   const int64_t lastdim = p.ndim > 0 ? p.shape[p.ndim - 1] : 1;
+  const bool small = n < ((int64_t)1 << 31) && lastdim >= 1;
   P.lastdim = lastdim;
-  fastdiv_params((uint32_t)std::min<int64_t>(lastdim, 0x7fffffff), P.ld_mul, P.ld_shr);
+  fastdiv_params((uint32_t)std::min<int64_t>(std::max<int64_t>(lastdim, 1), 0x7fffffff), P.ld_mul, P.ld_shr);
+  P.ld8 = (lastdim % 8 == 0) ? 1 : 0;
+  auto al = [](const void* q, int bytes) { return (reinterpret_cast<uintptr_t>(q) % bytes) == 0; };
   for (int j = 0; j < p.n_in && flat; ++j) {
-    bool all0 = true, isdense = true, isvec = p.ndim > 0;
+    bool all0 = true, isdense = true, isvec = p.ndim > 0, isrow = p.ndim > 0 && lastdim > 1;
     for (int d = 0; d < p.ndim; ++d) {
       if (p.shape[d] == 1) continue;
-      if (p.in_strides[j][d] != 0) all0 = false;
-      if (p.in_strides[j][d] != dense[d]) isdense = false;
-      if (d == p.ndim - 1 ? p.in_strides[j][d] != 1 : p.in_strides[j][d] != 0) isvec = false;
+      const int64_t st = p.in_strides[j][d];
+      if (st != 0) all0 = false;
+      if (st != dense[d]) isdense = false;
+      if (d == p.ndim - 1 ? st != 1 : st != 0) isvec = false;
+      if (d == p.ndim - 1 ? st != 0 : st != dense[d] / lastdim) isrow = false;
     }
-    const bool aligned = p.in_dtype[j] != B200_F32 || (reinterpret_cast<uintptr_t>(inputs[j]) & 15) == 0;
-    if (all0) {
-      P.mode[j] = 1;
-    } else if (isdense && aligned) {
-      P.mode[j] = 0;
-    } else if (isvec && aligned && lastdim % 4 == 0 && n < ((int64_t)1 << 31)) {
-      P.mode[j] = 2;
-    } else {
-      flat = false;
-    }
+    const int dt = p.in_dtype[j];
+    P.vin[j] = ((dt == B200_F32 || dt == B200_BF16) && al(inputs[j], 16)) ? 1 : 0;
+    if (all0) P.mode[j] = 1;
+    else if (isdense) P.mode[j] = 0;
+    else if (isvec && small) P.mode[j] = 2;
+    else if (isrow && small) P.mode[j] = 3;
+    else flat = false;
   }
-  for (int o = 0; o < p.n_out && flat; ++o)
-    if (p.out_dtype[o] == B200_F32 && (reinterpret_cast<uintptr_t>(outputs[o]) & 15)) flat = false;
+  for (int o = 0; o < p.n_out; ++o) {
+    const int dt = p.out_dtype[o];
+    P.vout[o] = ((dt == B200_F32 || dt == B200_BF16) && al(outputs[o], 16)) || (dt == B200_BOOL && al(outputs[o], 8));
+  }
+  if (flat) return ew_flat_launch(P, as_stream(stream));
 
   const int threads = 256;
   const int64_t sms = num_sms();
-  if (flat) {
-    int64_t blocks = std::min<int64_t>(ceil_div(ceil_div(n, 4), threads), sms * 8);
-    ew_flat_kernel<<<(unsigned)blocks, threads, 0, as_stream(stream)>>>(P);
-  } else {
+  {
     // 32-bit index path when every offset fits
     bool fits = n < ((int64_t)1 << 31);
     for (int j = 0; j < p.n_in && fits; ++j) {

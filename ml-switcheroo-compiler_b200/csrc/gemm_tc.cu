@@ -19,7 +19,15 @@
 namespace b200 {
 namespace tc {
 
-constexpr int BM = 128, BK = 64, STAGES = 4, THREADS = 192;
+#ifndef B200_GEMM_EPI_WARPS
+#define B200_GEMM_EPI_WARPS 8
+#endif
+#ifndef B200_GEMM_EPI_SLEEP_NS
+#define B200_GEMM_EPI_SLEEP_NS 0
+#endif
+// epilogue warps: 4 (one per TMEM lane quarter) or 8 (two per quarter, splitting columns)
+constexpr int BM = 128, BK = 64, STAGES = 4, EPI_WARPS = B200_GEMM_EPI_WARPS, THREADS = 64 + 32 * EPI_WARPS;
+static_assert(EPI_WARPS == 4 || EPI_WARPS == 8, "4 or 8 epilogue warps");
 constexpr unsigned long long WAIT_LIMIT_NS = 2000000000ull;  // 2 s per wait
 
 __device__ __forceinline__ uint32_t smem_u32(const void* p) { return (uint32_t)__cvta_generic_to_shared(p); }
@@ -45,11 +53,13 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
       : "memory");
   return ok != 0;
 }
-// bounded wait; false (and device error flag set) on timeout
-__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity) {
+// bounded wait; false (and device error flag set) on timeout. `sleep_ns` backs off
+// between polls (for warps that wait a whole main loop, so they do not take issue slots).
+__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, int sleep_ns = 0) {
   if (mbar_try_wait(bar, parity)) return true;
   const unsigned long long t0 = globaltimer();
   while (true) {
+    if (sleep_ns) __nanosleep(sleep_ns);
     if (mbar_try_wait(bar, parity)) return true;
     if (globaltimer() - t0 > WAIT_LIMIT_NS) {
       raise_device_error(B200_ERR_TIMEOUT);
@@ -74,31 +84,10 @@ __device__ __forceinline__ void tma_load_4d(void* dst, const CUtensorMap* map, u
       : "memory");
 }
 
-// TMA bulk-tensor store (shared -> global), tracked by the issuing thread's bulk group.
-__device__ __forceinline__ void tma_store_4d(const CUtensorMap* map, const void* src, int c0, int c1, int c2, int c3) {
-  asm volatile("cp.async.bulk.tensor.4d.global.shared::cta.bulk_group [%0, {%1, %2, %3, %4}], [%5];" ::"l"(
-                   reinterpret_cast<uint64_t>(map)),
-               "r"(c0), "r"(c1), "r"(c2), "r"(c3), "r"(smem_u32(src))
-               : "memory");
-}
-__device__ __forceinline__ void bulk_commit() { asm volatile("cp.async.bulk.commit_group;" ::: "memory"); }
-__device__ __forceinline__ void bulk_wait_read0() { asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory"); }
-__device__ __forceinline__ void bulk_wait0() { asm volatile("cp.async.bulk.wait_group 0;" ::: "memory"); }
-__device__ __forceinline__ void fence_proxy_async_smem() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
-__device__ __forceinline__ void st_shared_v4(uint32_t addr, uint32_t a, uint32_t b, uint32_t c, uint32_t d) {
-  asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(addr), "r"(a), "r"(b), "r"(c), "r"(d) : "memory");
-}
 __device__ __forceinline__ uint32_t pack_bf16(float a, float b) {
   __nv_bfloat162 t = __floats2bfloat162_rn(a, b);
   return *reinterpret_cast<uint32_t*>(&t);
 }
-
-// Epilogue staging per epilogue warp: a 32-row x 32-column chunk of C (fp32: 4 KB with
-// 128-byte rows, or bf16: 2 KB), of C2 (bf16, 2 KB) and of the mask (1 KB), each in the
-// swizzled layout its tensor map names (128B / 64B / 32B), so the 16-byte row pieces
-// the 32 lanes write land in distinct banks.
-constexpr uint32_t EPI_C_OFF = 0, EPI_C2_OFF = 4096, EPI_MASK_OFF = 6144, EPI_WARP_BYTES = 7168;
-constexpr uint32_t EPI_BYTES = 4 * EPI_WARP_BYTES;
 
 // UMMA shared-memory descriptor, SWIZZLE_128B, version 1 (sm_100).
 __device__ __forceinline__ uint64_t smem_desc(uint32_t saddr, uint32_t lbo_bytes, uint32_t sbo_bytes) {
@@ -122,8 +111,9 @@ __device__ __forceinline__ void mma_commit(uint64_t* bar) {
 __device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
 __device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
 
-__device__ __forceinline__ void tmem_ld32(uint32_t taddr, float (&v)[32]) {
-  uint32_t r[32];
+// tcgen05.ld of 32 consecutive fp32 columns of this warp's 32 TMEM lanes (asynchronous:
+// the registers are valid after tmem_wait, which names them so no use moves above it)
+__device__ __forceinline__ void tmem_ld32_issue(uint32_t taddr, uint32_t (&r)[32]) {
   asm volatile(
       "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16,%17,%18,%19,%20,%21,%"
       "22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];"
@@ -132,9 +122,15 @@ __device__ __forceinline__ void tmem_ld32(uint32_t taddr, float (&v)[32]) {
         "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]), "=r"(r[24]), "=r"(r[25]), "=r"(r[26]), "=r"(r[27]),
         "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
       : "r"(taddr));
-  asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
-#pragma unroll
-  for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(r[i]);
+}
+__device__ __forceinline__ void tmem_wait(uint32_t (&r)[32]) {
+  asm volatile("tcgen05.wait::ld.sync.aligned;"
+               : "+r"(r[0]), "+r"(r[1]), "+r"(r[2]), "+r"(r[3]), "+r"(r[4]), "+r"(r[5]), "+r"(r[6]), "+r"(r[7]), "+r"(r[8]),
+                 "+r"(r[9]), "+r"(r[10]), "+r"(r[11]), "+r"(r[12]), "+r"(r[13]), "+r"(r[14]), "+r"(r[15]), "+r"(r[16]),
+                 "+r"(r[17]), "+r"(r[18]), "+r"(r[19]), "+r"(r[20]), "+r"(r[21]), "+r"(r[22]), "+r"(r[23]), "+r"(r[24]),
+                 "+r"(r[25]), "+r"(r[26]), "+r"(r[27]), "+r"(r[28]), "+r"(r[29]), "+r"(r[30]), "+r"(r[31])
+               :
+               : "memory");
 }
 
 struct Args {
@@ -142,7 +138,6 @@ struct Args {
   void* C2;  // optional bf16 copy of the activation; C then receives the pre-activation
   const float* bias;
   uint8_t* aux;
-  int tma_store;  // 1: C / C2 / aux leave through TMA bulk-tensor stores (mapC / mapC2 / mapAux)
   int64_t M, N, K, sC, ldc;
   float alpha;
   int c_dt, epi, a_mn, b_mn, batch;  // batch = b_out * b_in tiles-of-matrices
@@ -163,9 +158,6 @@ __device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
 template <int BN>
 __global__ void __launch_bounds__(THREADS, 1) gemm_tc_kernel(const __grid_constant__ CUtensorMap mapA,
                                                              const __grid_constant__ CUtensorMap mapB,
-                                                             const __grid_constant__ CUtensorMap mapC,
-                                                             const __grid_constant__ CUtensorMap mapC2,
-                                                             const __grid_constant__ CUtensorMap mapAux,
                                                              const __grid_constant__ Args args) {
   constexpr uint32_t A_BYTES = BM * BK * 2;  // 16 KB
   constexpr uint32_t B_BYTES = BN * BK * 2;
@@ -173,8 +165,7 @@ __global__ void __launch_bounds__(THREADS, 1) gemm_tc_kernel(const __grid_consta
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* sA = smem;
   uint8_t* sB = smem + STAGES * A_BYTES;
-  uint8_t* sEpi = sB + STAGES * B_BYTES;  // 1024-aligned
-  uint64_t* full_bar = reinterpret_cast<uint64_t*>(sEpi + EPI_BYTES);
+  uint64_t* full_bar = reinterpret_cast<uint64_t*>(sB + STAGES * B_BYTES);
   uint64_t* empty_bar = full_bar + STAGES;
   uint64_t* acc_full = empty_bar + STAGES;  // [2]
   uint64_t* acc_empty = acc_full + 2;       // [2]
@@ -194,7 +185,7 @@ __global__ void __launch_bounds__(THREADS, 1) gemm_tc_kernel(const __grid_consta
     }
     for (int b = 0; b < 2; ++b) {
       mbar_init(&acc_full[b], 1);
-      mbar_init(&acc_empty[b], 4);  // one arrive per epilogue warp
+      mbar_init(&acc_empty[b], EPI_WARPS);  // one arrive per epilogue warp
     }
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
   }
@@ -281,139 +272,115 @@ __global__ void __launch_bounds__(THREADS, 1) gemm_tc_kernel(const __grid_consta
       }
     }
   } else {
-    // ---------------- epilogue (warps 2..5) ----------------
-    const int q = warp & 3;  // TMEM lane quarter this warp may access
-    const uint32_t stage = smem_u32(sEpi + q * EPI_WARP_BYTES);
-    const bool dual = args.C2 != nullptr;
+    // ---------------- epilogue (warps 2 .. 2 + EPI_WARPS) ----------------
+    // A warp may only read the TMEM lanes of its quarter (warp id % 4); the two warps of a
+    // quarter split the tile's columns. TMEM loads are software-pipelined: the next
+    // 32-column chunk is in flight while the current one is finished and stored.
+    const int q = warp & 3;
+    constexpr int NHALF = EPI_WARPS / 4;
+    const int half = (warp - 2) >> 2;
+    constexpr int CH = BN / 32 / NHALF;  // chunks per warp per tile
     uint32_t local = 0;
     for (int tile = blockIdx.x; tile < total; tile += gridDim.x, ++local) {
       const int z = tile / tiles_mn, r = tile % tiles_mn;
       const int m_tile = r / tiles_n, n_tile = r % tiles_n;
       const int b = local & 1;
       const uint32_t use = local >> 1;
-      if (!mbar_wait(&acc_full[b], use & 1)) break;
+      if (!mbar_wait(&acc_full[b], use & 1, B200_GEMM_EPI_SLEEP_NS)) break;
       tc_fence_after();
-      const int row0 = m_tile * BM + q * 32;
-      const int64_t row = (int64_t)row0 + lane;
-      const int64_t col0 = (int64_t)n_tile * BN;
+      const int64_t row = (int64_t)m_tile * BM + q * 32 + lane;
+      const int64_t col0 = (int64_t)n_tile * BN + half * (BN / NHALF);
       const int zo = z / args.b_in, zi = z % args.b_in;
-#pragma unroll 1
-      for (int c = 0; c < BN / 32; ++c) {
-        float v[32];
-        if (num_kb > 0) {
-          tmem_ld32(tmem_base + ((uint32_t)(q * 32) << 16) + (uint32_t)(b * BN + c * 32), v);
-        } else {
+      const uint32_t tbase = tmem_base + ((uint32_t)(q * 32) << 16) + (uint32_t)(b * BN + half * (BN / NHALF));
+      uint32_t buf[2][32];
+      if (num_kb > 0) {
+        tmem_ld32_issue(tbase, buf[0]);
+        tmem_wait(buf[0]);
+      } else {
 #pragma unroll
-          for (int i = 0; i < 32; ++i) v[i] = 0.f;
+        for (int i = 0; i < 32; ++i) buf[0][i] = 0u;
+      }
+#pragma unroll
+      for (int c = 0; c < CH; ++c) {
+        uint32_t (&cur)[32] = buf[c & 1];
+        uint32_t (&nxt)[32] = buf[(c + 1) & 1];
+        if (c + 1 < CH) {
+          if (num_kb > 0) {
+            tmem_ld32_issue(tbase + (uint32_t)((c + 1) * 32), nxt);
+          } else {
+#pragma unroll
+            for (int i = 0; i < 32; ++i) nxt[i] = 0u;
+          }
         }
         const int64_t cbase = col0 + c * 32;
-        if (cbase >= args.N) continue;                    // warp-uniform
-        if (args.tma_store && row0 >= args.M) continue;  // nothing of this warp's rows exists
-        // pre = alpha * acc + bias; act = epi(pre); mask bit = pre > 0
-        uint32_t mbits = 0;
-        float act[32];
+        if (row < args.M && cbase < args.N) {
+          // pre = alpha * acc + bias; act = epi(pre); mask bit = pre > 0
+          float v[32], act[32];
+          uint32_t mbits = 0;
 #pragma unroll
-        for (int i = 0; i < 32; ++i) {
-          const int64_t n = cbase + i;
-          const float pre = args.alpha * v[i] + ((args.bias && n < args.N) ? __ldg(args.bias + n) : 0.f);
-          mbits |= (pre > 0.f ? 1u : 0u) << i;
-          float a = pre;
-          if (args.epi == B200_EPI_RELU) a = pre > 0.f ? pre : 0.f;
-          else if (args.epi == B200_EPI_GELU) a = gelu_tanh(pre);
-          act[i] = a;
-          if (!dual) v[i] = a;
-          else v[i] = pre;
-        }
-        if (args.tma_store) {
-          // previous chunk's bulk stores must have read the staging buffer
-          if (lane == 0) bulk_wait_read0();
-          __syncwarp();
-          if (args.c_dt == B200_F32) {
-            const uint32_t rb = stage + EPI_C_OFF + (uint32_t)lane * 128u;
-#pragma unroll
-            for (int j = 0; j < 8; ++j)
-              st_shared_v4(rb + ((uint32_t)(j ^ (lane & 7)) << 4), __float_as_uint(v[4 * j]), __float_as_uint(v[4 * j + 1]),
-                           __float_as_uint(v[4 * j + 2]), __float_as_uint(v[4 * j + 3]));
-          } else {
-            const uint32_t rb = stage + EPI_C_OFF + (uint32_t)lane * 64u;
-#pragma unroll
-            for (int j = 0; j < 4; ++j)
-              st_shared_v4(rb + ((uint32_t)(j ^ ((lane >> 1) & 3)) << 4), pack_bf16(v[8 * j], v[8 * j + 1]),
-                           pack_bf16(v[8 * j + 2], v[8 * j + 3]), pack_bf16(v[8 * j + 4], v[8 * j + 5]),
-                           pack_bf16(v[8 * j + 6], v[8 * j + 7]));
+          for (int i = 0; i < 32; ++i) {
+            const int64_t n = cbase + i;
+            const float pre = args.alpha * __uint_as_float(cur[i]) + ((args.bias && n < args.N) ? __ldg(args.bias + n) : 0.f);
+            mbits |= (pre > 0.f ? 1u : 0u) << i;
+            float a = pre;
+            if (args.epi == B200_EPI_RELU) a = pre > 0.f ? pre : 0.f;
+            else if (args.epi == B200_EPI_GELU) a = gelu_tanh(pre);
+            act[i] = a;
+            v[i] = args.C2 ? pre : a;
           }
-          if (dual) {
-            const uint32_t rb = stage + EPI_C2_OFF + (uint32_t)lane * 64u;
+          const int64_t off = (int64_t)zo * args.sC + (int64_t)zi * args.sC_in + row * args.ldc + cbase;
+          const bool full = cbase + 32 <= args.N;
+          if (args.c_dt == B200_F32) {
+            float* dst = reinterpret_cast<float*>(args.C) + off;
+            if (full && ((reinterpret_cast<uintptr_t>(dst) & 15) == 0)) {
 #pragma unroll
-            for (int j = 0; j < 4; ++j)
-              st_shared_v4(rb + ((uint32_t)(j ^ ((lane >> 1) & 3)) << 4), pack_bf16(act[8 * j], act[8 * j + 1]),
-                           pack_bf16(act[8 * j + 2], act[8 * j + 3]), pack_bf16(act[8 * j + 4], act[8 * j + 5]),
-                           pack_bf16(act[8 * j + 6], act[8 * j + 7]));
+              for (int i = 0; i < 32; i += 4) *reinterpret_cast<float4*>(dst + i) = make_float4(v[i], v[i + 1], v[i + 2], v[i + 3]);
+            } else {
+              for (int i = 0; i < 32; ++i)
+                if (cbase + i < args.N) dst[i] = v[i];
+            }
+          } else {
+            __nv_bfloat16* dst = reinterpret_cast<__nv_bfloat16*>(args.C) + off;
+            if (full && ((reinterpret_cast<uintptr_t>(dst) & 15) == 0)) {
+#pragma unroll
+              for (int i = 0; i < 32; i += 8)
+                *reinterpret_cast<uint4*>(dst + i) = make_uint4(pack_bf16(v[i], v[i + 1]), pack_bf16(v[i + 2], v[i + 3]),
+                                                                pack_bf16(v[i + 4], v[i + 5]), pack_bf16(v[i + 6], v[i + 7]));
+            } else {
+              for (int i = 0; i < 32; ++i)
+                if (cbase + i < args.N) dst[i] = __float2bfloat16_rn(v[i]);
+            }
+          }
+          if (args.C2) {
+            __nv_bfloat16* dst = reinterpret_cast<__nv_bfloat16*>(args.C2) + off;
+            if (full && ((reinterpret_cast<uintptr_t>(dst) & 15) == 0)) {
+#pragma unroll
+              for (int i = 0; i < 32; i += 8)
+                *reinterpret_cast<uint4*>(dst + i) = make_uint4(pack_bf16(act[i], act[i + 1]), pack_bf16(act[i + 2], act[i + 3]),
+                                                                pack_bf16(act[i + 4], act[i + 5]), pack_bf16(act[i + 6], act[i + 7]));
+            } else {
+              for (int i = 0; i < 32; ++i)
+                if (cbase + i < args.N) dst[i] = __float2bfloat16_rn(act[i]);
+            }
           }
           if (args.aux) {
-            // one byte per element: expand the 32 mask bits into 2 x 16 bytes
-            uint32_t w[8];
+            uint8_t* mdst = args.aux + off;
+            if (full && ((reinterpret_cast<uintptr_t>(mdst) & 15) == 0)) {
+              uint32_t w[8];
 #pragma unroll
-            for (int k = 0; k < 8; ++k) {
-              const uint32_t nib = (mbits >> (4 * k)) & 0xFu;
-              w[k] = (nib & 1u) | ((nib >> 1) & 1u) << 8 | ((nib >> 2) & 1u) << 16 | ((nib >> 3) & 1u) << 24;
+              for (int k = 0; k < 8; ++k) {
+                const uint32_t nib = (mbits >> (4 * k)) & 0xFu;
+                w[k] = (nib & 1u) | ((nib >> 1) & 1u) << 8 | ((nib >> 2) & 1u) << 16 | ((nib >> 3) & 1u) << 24;
+              }
+              reinterpret_cast<uint4*>(mdst)[0] = make_uint4(w[0], w[1], w[2], w[3]);
+              reinterpret_cast<uint4*>(mdst)[1] = make_uint4(w[4], w[5], w[6], w[7]);
+            } else {
+              for (int i = 0; i < 32; ++i)
+                if (cbase + i < args.N) mdst[i] = (uint8_t)((mbits >> i) & 1u);
             }
-            const uint32_t rb = stage + EPI_MASK_OFF + (uint32_t)lane * 32u;
-            const uint32_t sw = (uint32_t)((lane >> 2) & 1);
-            st_shared_v4(rb + ((0u ^ sw) << 4), w[0], w[1], w[2], w[3]);
-            st_shared_v4(rb + ((1u ^ sw) << 4), w[4], w[5], w[6], w[7]);
-          }
-          fence_proxy_async_smem();
-          __syncwarp();
-          if (lane == 0) {
-            tma_store_4d(&mapC, sEpi + q * EPI_WARP_BYTES + EPI_C_OFF, (int)cbase, row0, zi, zo);
-            if (dual) tma_store_4d(&mapC2, sEpi + q * EPI_WARP_BYTES + EPI_C2_OFF, (int)cbase, row0, zi, zo);
-            if (args.aux) tma_store_4d(&mapAux, sEpi + q * EPI_WARP_BYTES + EPI_MASK_OFF, (int)cbase, row0, zi, zo);
-            bulk_commit();
-          }
-          continue;
-        }
-        if (row >= args.M) continue;
-        const int64_t off = (int64_t)zo * args.sC + (int64_t)zi * args.sC_in + row * args.ldc + cbase;
-        const bool full = cbase + 32 <= args.N;
-        if (args.c_dt == B200_F32) {
-          float* dst = reinterpret_cast<float*>(args.C) + off;
-          if (full && ((reinterpret_cast<uintptr_t>(dst) & 15) == 0)) {
-#pragma unroll
-            for (int i = 0; i < 32; i += 4) *reinterpret_cast<float4*>(dst + i) = make_float4(v[i], v[i + 1], v[i + 2], v[i + 3]);
-          } else {
-            for (int i = 0; i < 32; ++i)
-              if (cbase + i < args.N) dst[i] = v[i];
-          }
-        } else {
-          __nv_bfloat16* dst = reinterpret_cast<__nv_bfloat16*>(args.C) + off;
-          if (full && ((reinterpret_cast<uintptr_t>(dst) & 15) == 0)) {
-#pragma unroll
-            for (int i = 0; i < 32; i += 8)
-              *reinterpret_cast<uint4*>(dst + i) = make_uint4(pack_bf16(v[i], v[i + 1]), pack_bf16(v[i + 2], v[i + 3]),
-                                                              pack_bf16(v[i + 4], v[i + 5]), pack_bf16(v[i + 6], v[i + 7]));
-          } else {
-            for (int i = 0; i < 32; ++i)
-              if (cbase + i < args.N) dst[i] = __float2bfloat16_rn(v[i]);
           }
         }
-        if (dual) {
-          __nv_bfloat16* dst = reinterpret_cast<__nv_bfloat16*>(args.C2) + off;
-          if (full && ((reinterpret_cast<uintptr_t>(dst) & 15) == 0)) {
-#pragma unroll
-            for (int i = 0; i < 32; i += 8)
-              *reinterpret_cast<uint4*>(dst + i) = make_uint4(pack_bf16(act[i], act[i + 1]), pack_bf16(act[i + 2], act[i + 3]),
-                                                              pack_bf16(act[i + 4], act[i + 5]), pack_bf16(act[i + 6], act[i + 7]));
-          } else {
-            for (int i = 0; i < 32; ++i)
-              if (cbase + i < args.N) dst[i] = __float2bfloat16_rn(act[i]);
-          }
-        }
-        if (args.aux) {
-          uint8_t* mdst = args.aux + off;
-          for (int i = 0; i < 32; ++i)
-            if (cbase + i < args.N) mdst[i] = (uint8_t)((mbits >> i) & 1u);
-        }
+        if (c + 1 < CH && num_kb > 0) tmem_wait(nxt);
       }
       // accumulator b may be overwritten once every epilogue warp has read it
       tc_fence_before();
@@ -421,7 +388,6 @@ __global__ void __launch_bounds__(THREADS, 1) gemm_tc_kernel(const __grid_consta
       if (lane == 0) mbar_arrive(&acc_empty[b]);
     }
   }
-  if (warp >= 2 && lane == 0 && args.tma_store) bulk_wait0();  // this warp's bulk stores are complete
   tc_fence_before();
   __syncthreads();
   if (warp == 1) {
@@ -470,34 +436,9 @@ static int make_map(CUtensorMap* map, const void* base, uint64_t d0, uint64_t d1
   return B200_OK;
 }
 
-// Store map for C / C2 / mask: dims (N, M, b_in, b_out) with byte strides (ldc, sC_in,
-// sC_out) * esize, box 32 x 32 (one epilogue warp's chunk), swizzle matching the rows
-// the epilogue writes (128 B fp32 rows, 64 B bf16 rows, 32 B mask rows). Returns false
-// when TMA cannot address the layout (the epilogue then stores directly).
-static bool make_store_map(CUtensorMap* map, void* base, CUtensorMapDataType dt, uint32_t esize, int64_t N, int64_t M,
-                           int64_t b_in, int64_t b_out, int64_t ldc, int64_t sC_in, int64_t sC_out) {
-  auto enc = get_encode();
-  if (!enc || !base || (reinterpret_cast<uintptr_t>(base) & 15)) return false;
-  const uint64_t rowb = (uint64_t)ldc * esize;
-  const uint64_t s2 = b_in > 1 ? (uint64_t)sC_in * esize : rowb * (uint64_t)M;
-  const uint64_t s3 = b_out > 1 ? (uint64_t)sC_out * esize : s2 * (uint64_t)b_in;
-  if (rowb % 16 || s2 % 16 || s3 % 16 || rowb == 0 || s2 == 0 || s3 == 0) return false;
-  if (rowb >= (1ull << 40) || s2 >= (1ull << 40) || s3 >= (1ull << 40)) return false;
-  cuuint64_t dims[4] = {(cuuint64_t)N, (cuuint64_t)M, (cuuint64_t)b_in, (cuuint64_t)b_out};
-  cuuint64_t strides[3] = {rowb, s2, s3};
-  cuuint32_t box[4] = {32, 32, 1, 1};
-  cuuint32_t estr[4] = {1, 1, 1, 1};
-  const CUtensorMapSwizzle sw =
-      esize == 4 ? CU_TENSOR_MAP_SWIZZLE_128B : (esize == 2 ? CU_TENSOR_MAP_SWIZZLE_64B : CU_TENSOR_MAP_SWIZZLE_32B);
-  CUresult r = enc(map, dt, 4, base, dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, sw,
-                   CU_TENSOR_MAP_L2_PROMOTION_NONE, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
-  return r == CUDA_SUCCESS;
-}
-
 template <int BN>
-static int launch(const CUtensorMap& ma, const CUtensorMap& mb, const CUtensorMap& mc, const CUtensorMap& mc2,
-                  const CUtensorMap& maux, const Args& a, int64_t batch, cudaStream_t s) {
-  const size_t smem = (size_t)STAGES * (BM * BK * 2 + BN * BK * 2) + EPI_BYTES + 1024 + 256;
+static int launch(const CUtensorMap& ma, const CUtensorMap& mb, const Args& a, int64_t batch, cudaStream_t s) {
+  const size_t smem = (size_t)STAGES * (BM * BK * 2 + BN * BK * 2) + 1024 + 256;
   const int64_t tiles = ceil_div(a.N, BN) * ceil_div(a.M, BM) * batch;  // batch = b_out * b_in
   static bool attr_set[64] = {false};
   int dev = 0;
@@ -507,7 +448,7 @@ static int launch(const CUtensorMap& ma, const CUtensorMap& mb, const CUtensorMa
     if (dev >= 0 && dev < 64) attr_set[dev] = true;
   }
   const unsigned grid = (unsigned)std::max<int64_t>(1, std::min<int64_t>(tiles, num_sms()));
-  gemm_tc_kernel<BN><<<grid, THREADS, smem, s>>>(ma, mb, mc, mc2, maux, a);
+  gemm_tc_kernel<BN><<<grid, THREADS, smem, s>>>(ma, mb, a);
   return check_launch("gemm(bf16 tcgen05)");
 }
 
@@ -585,20 +526,8 @@ int gemm_bf16_tcgen05_b2(int c_dt, const void* A, const void* B, void* C, int64_
   a.b_bc_out = b_bc_out;
   a.b_bc_in = b_bc_in;
   B200_REQUIRE(ceil_div(M, BM) <= 65535, "gemm(bf16): M too large");
-  // epilogue through TMA stores when every output layout is TMA-addressable
-  CUtensorMap mc, mc2, maux;
-  memset(&mc, 0, sizeof(mc));
-  memset(&mc2, 0, sizeof(mc2));
-  memset(&maux, 0, sizeof(maux));
-  const bool c_f32 = c_dt == B200_F32;
-  bool tma = M <= INT32_MAX && N <= INT32_MAX &&
-             make_store_map(&mc, C, c_f32 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT32 : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, c_f32 ? 4 : 2, N,
-                            M, b_in, b_out, ldc, sC_in, sC_out);
-  if (tma && C2) tma = make_store_map(&mc2, C2, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, N, M, b_in, b_out, ldc, sC_in, sC_out);
-  if (tma && aux) tma = make_store_map(&maux, aux, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, N, M, b_in, b_out, ldc, sC_in, sC_out);
-  a.tma_store = tma ? 1 : 0;
-  if (BN == 256) return launch<256>(ma, mb, mc, mc2, maux, a, batch, s);
-  return launch<128>(ma, mb, mc, mc2, maux, a, batch, s);
+  if (BN == 256) return launch<256>(ma, mb, a, batch, s);
+  return launch<128>(ma, mb, a, batch, s);
 }
 
 int gemm_bf16_tcgen05(int c_dt, const void* A, const void* B, void* C, int64_t batch, int64_t M, int64_t N, int64_t K,

@@ -475,3 +475,105 @@ def test_gemm_dual_output_pre_and_bf16_activation(M, N, K, epi):
     np.testing.assert_allclose(to_np(res[1].float()), act, rtol=1e-2, atol=1e-2)
     if epi == "relu":
         assert (to_np(res[2]) == (pre > 0)).mean() > 0.999
+
+
+@pytest.mark.parametrize("R,C", [(300, 4096), (37, 1000), (5, 7)])
+def test_gelu_bwd_colsum_matches_vjp_chain(R, C):
+    from b200 import _lib as L
+    from oracle import evaluator as O
+
+    r = rng(R + C)
+    g = r.standard_normal((R, C)).astype(np.float32)
+    p = (r.standard_normal((R, C)) * 2).astype(np.float32)
+    k, c = np.float32(np.sqrt(2.0 / np.pi)), np.float32(0.044715)
+    mul, add = (lambda a, b: O.execute_op("Multiply", a, b)), (lambda a, b: O.execute_op("Add", a, b))
+    p2 = mul(p, p)
+    t = O.execute_op("Tanh", mul(add(p, mul(mul(p2, p), c)), k))
+    left = mul(add(t, np.float32(1)), np.float32(0.5))
+    sech2 = O.execute_op("Subtract", np.float32(1), mul(t, t))
+    dinner = mul(add(mul(p2, np.float32(3 * 0.044715)), np.float32(1)), k)
+    ref = mul(g, add(left, mul(mul(mul(p, sech2), dinner), np.float32(0.5))))
+    G, P = T(g), T(p)
+    Y = torch.empty_like(G)
+    YB = torch.empty(G.shape, dtype=torch.bfloat16, device=G.device)
+    DB = torch.empty(C, dtype=torch.float32, device=G.device)
+    ws_n = int(L.lib().b200_gelu_bwd_colsum_workspace_bytes(R, C))
+    WS = torch.empty(max(ws_n, 1), dtype=torch.uint8, device=G.device)
+    L.call("b200_gelu_bwd_colsum", G.data_ptr(), P.data_ptr(), YB.data_ptr(), Y.data_ptr(), DB.data_ptr(), R, C,
+           WS.data_ptr(), ws_n, 0)
+    torch.cuda.synchronize()
+    np.testing.assert_allclose(to_np(Y), ref, rtol=1e-4, atol=1e-5)
+    np.testing.assert_allclose(to_np(YB.float()), ref, rtol=1e-2, atol=1e-2)
+    np.testing.assert_allclose(to_np(DB), ref.astype(np.float64).sum(0), rtol=1e-4, atol=1e-3)
+
+
+@pytest.mark.parametrize("ta", [False, True])
+def test_gemm_split_k_weight_gradient_shape(ta):
+    """Few output tiles and a long K (a weight gradient): split over K, summed in order."""
+    from b200 import ops
+
+    r = rng(21)
+    M, N, K = 256, 384, 16384
+    a = _bf16(r.standard_normal((K, M) if ta else (M, K), dtype=np.float32) * 0.05)
+    b = _bf16(r.standard_normal((K, N), dtype=np.float32) * 0.05)
+    A = T(a).to(torch.bfloat16)
+    A = A.t() if ta else A
+    an = a.T if ta else a
+    assert ops._split_k(M, N, K) > 1
+    got = to_np(ops.gemm(A, T(b).to(torch.bfloat16), ab_dtype=torch.bfloat16))
+    np.testing.assert_allclose(got, an.astype(np.float64) @ b.astype(np.float64), rtol=1e-4, atol=1e-3)
+
+
+def test_gemm_out_transposed_layout_and_twin():
+    """GEMM written through a permuted view (head merge) with a bf16 twin of the same strides."""
+    from b200 import ops
+
+    r = rng(22)
+    Bn, H, S, hd = 2, 4, 128, 64
+    att = _bf16(r.standard_normal((Bn, H, S, S), dtype=np.float32) * 0.1)
+    v = _bf16(r.standard_normal((Bn, H, S, hd), dtype=np.float32))
+    ref = np.matmul(att.astype(np.float64), v.astype(np.float64)).transpose(0, 2, 1, 3)
+    y = torch.empty(Bn, S, H, hd, dtype=torch.float32, device="cuda")
+    yb = torch.empty(Bn, S, H, hd, dtype=torch.bfloat16, device="cuda")
+    ok = ops.gemm_out(T(att).to(torch.bfloat16), T(v).to(torch.bfloat16), y.permute(0, 2, 1, 3), yb.permute(0, 2, 1, 3),
+                      ab_dtype=torch.bfloat16)
+    assert ok
+    np.testing.assert_allclose(to_np(y), ref, rtol=1e-4, atol=1e-3)
+    np.testing.assert_allclose(to_np(yb.float()), ref, rtol=1e-2, atol=1e-2)
+
+
+@pytest.mark.parametrize("shape", [(64, 1024), (37, 100), (5, 12), (3, 7, 8), (1001,), (2, 3)])
+def test_elementwise_flat_modes_dtypes(shape):
+    """Flat-path kernels: dense / scalar / last-dim vector / per-row operands, bf16 and
+    bool inputs and outputs, single-op kernels and multi-op register programs, ragged
+    group tails (n % 8 != 0) and rows that split 8-element groups."""
+    from b200 import ops
+
+    r = rng(sum(shape))
+    x = r.standard_normal(shape).astype(np.float32)
+    y = r.standard_normal(shape).astype(np.float32)
+    vec = r.standard_normal(shape[-1]).astype(np.float32)
+    rowv = r.standard_normal(shape[:-1] + (1,)).astype(np.float32)
+    X, Y = T(x), T(y)
+    np.testing.assert_allclose(to_np(ops.op_add(X, Y)), x + y, rtol=1e-6)
+    np.testing.assert_allclose(to_np(ops.op_subtract(X, T(vec))), x - vec, rtol=1e-6)
+    np.testing.assert_allclose(to_np(ops.op_multiply(X, T(rowv))), x * rowv, rtol=1e-6)
+    np.testing.assert_allclose(to_np(ops.op_true_divide(X, 3.0)), x / np.float32(3.0), rtol=1e-6)
+    np.testing.assert_array_equal(to_np(ops.op_greater(X, T(rowv))), x > rowv)
+    np.testing.assert_allclose(to_np(ops.op_relu(X)), np.maximum(x, 0))
+    # casts both ways
+    xb = ops.cast(X, torch.bfloat16)
+    np.testing.assert_array_equal(to_np(xb.float()), to_np(X.to(torch.bfloat16).float()))
+    np.testing.assert_array_equal(to_np(ops.cast(xb, torch.float32)), to_np(xb.float()))
+    # bf16 operand in a binary op, fp32 result
+    np.testing.assert_allclose(to_np(ops.op_add(xb, Y)), to_np(xb.float()) + y, rtol=1e-6)
+    # a multi-op register program with a row operand and two outputs
+    p = ops.Prog()
+    a, b, c = p.load(X), p.load(Y), p.load(T(rowv))
+    t1 = p.op("MUL", a, b)
+    t2 = p.op("ADD", t1, c)
+    t3 = p.op("TANH", t2)
+    out = p.run([(t3, torch.float32), (t3, torch.bfloat16)], shape)
+    ref = np.tanh(x * y + rowv)
+    np.testing.assert_allclose(to_np(out[0]), ref, rtol=1e-5, atol=1e-6)
+    np.testing.assert_allclose(to_np(out[1].float()), ref, rtol=1e-2, atol=1e-2)

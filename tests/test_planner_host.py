@@ -189,3 +189,33 @@ def test_attention_softmax_patterns_match_transformer_graph():
         assert m.bind["scale"] == scale
         assert m.bind["bf16"] == "True" and m.bind["f32"] == "False"
     assert {m.bind["y"] for m in bwd} == {m.bind["y"] for m in fwd}
+
+
+def test_gelu_bwd_pattern_matches_transformer_ffn():
+    """The GELU VJP chain of every FFN fuses with its bias gradient, and its output
+    (only read by the two weight/input-gradient GEMMs) is produced in bf16 alone."""
+    from b200 import ops
+    from b200.fusion import find_gelu_bwd
+
+    g, meta = _meta_from_oracle("transformer_small")
+    need, stack = set(), list(g.outputs)
+    while stack:
+        v = stack.pop()
+        if v not in need and v in g.nodes:
+            need.add(v)
+            stack.extend(g.nodes[v].inputs)
+    live = {n.id: n for n in g.topo_order() if n.op_type != "Input" and n.id in need}
+    users = {}
+    for n in live.values():
+        for i in n.inputs:
+            users.setdefault(i, []).append(n.id)
+    old = ops.Config.matmul_dtype
+    ops.Config.matmul_dtype = "bf16"
+    try:
+        found = find_gelu_bwd(g, live, meta, users, set(g.outputs))
+    finally:
+        ops.Config.matmul_dtype = old
+    assert len(found) == 2
+    for m in found:
+        assert "db" in m.outputs and m.outputs["db"] in set(g.outputs)
+        assert m.bind["bf16"] == "True" and m.bind["f32"] == "False"
