@@ -255,12 +255,15 @@ def run_gpu(args) -> None:
     launches_per_step = int(_lib.launch_count() - n_before)
     n_capture = len(plan.steps)
 
+    from b200.dp import GradAllReduce
+
+    sync = GradAllReduce("mean" if scale_grads else "sum")
+
     def allreduce():
         if dist is not None:
             # data-parallel gradient exchange over NCCL (NVLink); a mean loss over the global
             # batch is the average of the per-shard means
-            for gid in grad_ids:
-                dist.all_reduce(out[gid], op=dist.ReduceOp.AVG if scale_grads else dist.ReduceOp.SUM)
+            sync([out[gid] for gid in grad_ids])
 
     stream = torch.cuda.current_stream()
     for _ in range(args.warmup):

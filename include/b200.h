@@ -139,6 +139,16 @@ int b200_layernorm_rows(const float* x, const float* gamma, const float* beta, f
 int b200_layernorm_input_grad_rows(const float* dy, const float* x, const float* gamma, float* dx, void* dx_bf16,
                                    int64_t rows, int64_t cols, float eps, void* stream);
 
+/* The whole LayerNorm backward in one pass over dy and x: LayerNormInputGrad (dx, fp32
+ * and/or bf16), LayerNormGammaGrad (dgamma = sum_rows dy * xhat) and LayerNormBetaGrad
+ * (dbeta = sum_rows dy) of numpy/eager/nn_ops.py:244-318; any output may be NULL. Column
+ * sums go through per-CTA partials reduced in a fixed order (deterministic).
+ * workspace >= b200_layernorm_bwd_workspace_bytes(rows, cols). */
+size_t b200_layernorm_bwd_workspace_bytes(int64_t rows, int64_t cols);
+int b200_layernorm_bwd_rows(const float* dy, const float* x, const float* gamma, float* dx, void* dx_bf16, float* dgamma,
+                            float* dbeta, int64_t rows, int64_t cols, float eps, void* workspace, size_t workspace_bytes,
+                            void* stream);
+
 /* Softmax / LogSoftmax over the last axis (numpy/eager/math_advanced/math_signal.py:450-467,
  * math_advanced/math_log_exp.py:87-104). x, y: [rows, cols] F32. log != 0 -> LogSoftmax. */
 int b200_softmax(const float* x, float* y, int64_t rows, int64_t cols, int log, void* stream);
@@ -276,9 +286,10 @@ int b200_gelu_bwd_colsum(const float* g, const float* p, void* y_bf16, float* y_
  * ScatterAdd advanced_indexing.py:309-326, then the LogSoftmax rule g - exp(ls) sum(g)):
  *   picked[r] = ls[r, label[r]],  dx[r, j] = d[r] ([j == label[r]] - softmax(x)[r, j]).
  * x [rows, cols] (F32 or BF16), label [rows] int64, d [rows] fp32 (cotangent of picked).
- * picked, ls (the full log-softmax) and dx may each be NULL. */
+ * picked, ls (the full log-softmax), dx and dx_bf16 (dx in bf16, for fp32 x with cols % 4 == 0)
+ * may each be NULL. */
 int b200_logsoftmax_pick(int x_dtype, const void* x, const int64_t* label, const float* d, float* picked, float* ls,
-                         float* dx, int64_t rows, int64_t cols, void* stream);
+                         float* dx, void* dx_bf16, int64_t rows, int64_t cols, void* stream);
 
 /* LayerNorm forward (numpy/eager/nn_ops.py:219-241) and LayerNormInputGrad (nn_ops.py:244)
  * over the last axis, writing fp32 (y / dx) and/or bf16 (y_bf16 / dx_bf16; either may be
@@ -288,6 +299,16 @@ int b200_layernorm_rows(const float* x, const float* gamma, const float* beta, f
                         int64_t cols, float eps, void* stream);
 int b200_layernorm_input_grad_rows(const float* dy, const float* x, const float* gamma, float* dx, void* dx_bf16,
                                    int64_t rows, int64_t cols, float eps, void* stream);
+
+/* The whole LayerNorm backward in one pass over dy and x: LayerNormInputGrad (dx, fp32
+ * and/or bf16), LayerNormGammaGrad (dgamma = sum_rows dy * xhat) and LayerNormBetaGrad
+ * (dbeta = sum_rows dy) of numpy/eager/nn_ops.py:244-318; any output may be NULL. Column
+ * sums go through per-CTA partials reduced in a fixed order (deterministic).
+ * workspace >= b200_layernorm_bwd_workspace_bytes(rows, cols). */
+size_t b200_layernorm_bwd_workspace_bytes(int64_t rows, int64_t cols);
+int b200_layernorm_bwd_rows(const float* dy, const float* x, const float* gamma, float* dx, void* dx_bf16, float* dgamma,
+                            float* dbeta, int64_t rows, int64_t cols, float eps, void* workspace, size_t workspace_bytes,
+                            void* stream);
 
 /* Softmax / LogSoftmax over the last axis (numpy/eager/math_advanced/math_signal.py:450-467,
  * math_advanced/math_log_exp.py:87-104) of t = x * scale[0], where `scale` is an optional

@@ -73,6 +73,8 @@ SIGNATURES = {
     "b200_softmax": ([_P, _P, _I64, _I64, _I32, _P], C.c_int),
     "b200_gelu_bwd_colsum_workspace_bytes": ([_I64, _I64], C.c_size_t),
     "b200_gelu_bwd_colsum": ([_P, _P, _P, _P, _P, _I64, _I64, _P, C.c_size_t, _P], C.c_int),
+    "b200_layernorm_bwd_workspace_bytes": ([_I64, _I64], C.c_size_t),
+    "b200_layernorm_bwd_rows": ([_P, _P, _P, _P, _P, _P, _P, _I64, _I64, _F32, _P, C.c_size_t, _P], C.c_int),
     "b200_layernorm_rows": ([_P, _P, _P, _P, _P, _I64, _I64, _F32, _P], C.c_int),
     "b200_layernorm_input_grad_rows": ([_P, _P, _P, _P, _P, _I64, _I64, _F32, _P], C.c_int),
     "b200_softmax_rows": ([_P, _P, _P, _P, _I64, _I64, _I32, _P], C.c_int),
@@ -96,7 +98,7 @@ SIGNATURES = {
     "b200_rowfused_fwd_bwd": ([_P] * 13 + [_I64, _I64, _F32, _P, C.c_size_t, _P], C.c_int),
     "b200_mask_mul_colsum_workspace_bytes": ([_I64, _I64], C.c_size_t),
     "b200_mask_mul_colsum": ([_P, _P, _P, _P, _P, _I64, _I64, _P, C.c_size_t, _P], C.c_int),
-    "b200_logsoftmax_pick": ([_I32, _P, _P, _P, _P, _P, _P, _I64, _I64, _P], C.c_int),
+    "b200_logsoftmax_pick": ([_I32, _P, _P, _P, _P, _P, _P, _P, _I64, _I64, _P], C.c_int),
     "b200_conv2d_tc_workspace_bytes": ([_I32] + [_I64] * 13, C.c_size_t),
     "b200_conv2d_fwd_tc": ([_P, _P, _P] + [_I64] * 13 + [_P, C.c_size_t, _P], C.c_int),
     "b200_conv2d_dgrad_tc": ([_P, _P, _P] + [_I64] * 13 + [_P, C.c_size_t, _P], C.c_int),

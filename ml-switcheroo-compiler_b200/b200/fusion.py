@@ -622,26 +622,31 @@ def find_xent(g: Graph, live: dict[str, Node], meta: dict[str, Meta], users: dic
     return found
 
 
-def xent_step(m: Match, meta: dict[str, Meta]) -> Step:
+def xent_step(m: Match, meta: dict[str, Meta], bf16_dx: bool = False) -> Step:
     b, o = m.bind, m.outputs
     shape = meta[b["x"]].shape
     V = shape[-1]
     R = math.prod(shape[:-1])
+    # dx straight in bf16 when it only feeds the output-projection GEMMs (fp32 logits,
+    # whole 4-column groups: the register-row kernel)
+    bf = bf16_dx and V % 4 == 0 and meta[b["x"]].dtype == torch.float32
 
     def run(env: dict) -> None:
         x = ops.contiguous(env[b["x"]])
         lab = ops.contiguous(env[b["labels"]])
         d = ops.contiguous(ops.cast(env[b["d"]], torch.float32))
         dev = ops.device()
-        dx = torch.empty(shape, dtype=torch.float32, device=dev)
+        dx = None if bf else torch.empty(shape, dtype=torch.float32, device=dev)
+        dxb = torch.empty(shape, dtype=torch.bfloat16, device=dev) if bf else None
         picked = torch.empty(tuple(shape[:-1]) + (1,), dtype=torch.float32, device=dev) if "picked" in o else None
         L.call("b200_logsoftmax_pick", ops.code(x), x.data_ptr(), lab.data_ptr(), d.data_ptr(),
-               None if picked is None else picked.data_ptr(), None, dx.data_ptr(), R, V, ops.stream_ptr())
-        env[o["dx"]] = dx
+               None if picked is None else picked.data_ptr(), None, None if dx is None else dx.data_ptr(),
+               None if dxb is None else dxb.data_ptr(), R, V, ops.stream_ptr())
+        env[o["dx"]] = dxb if bf else dx
         if picked is not None:
             env[o["picked"]] = picked
 
-    return Step(list(o.values()), [b["x"], b["labels"], b["d"]], run, "xent_fwd_bwd")
+    return Step(list(o.values()), [b["x"], b["labels"], b["d"]], run, "xent_fwd_bwd" + ("[bf16]" if bf else ""))
 
 
 # ----------------------------------------------------------------------------------
@@ -711,6 +716,74 @@ def gelu_bwd_step(m: Match, meta: dict[str, Meta]) -> Step:
 
     label = "gelu_bwd" + ("_bias" if "db" in o else "") + ("[bf16]" if bf and not f32 else "")
     return Step(list(o.values()), [b["g"], b["p"]], run, label)
+
+
+# ----------------------------------------------------------------------------------
+# pattern: LayerNormInputGrad + LayerNormGammaGrad + LayerNormBetaGrad of one (dy, x)
+# ----------------------------------------------------------------------------------
+def find_ln_bwd(g: Graph, live: dict[str, Node], meta: dict[str, Meta], users: dict[str, list[str]],
+                outputs: set[str]) -> list[Match]:
+    found = []
+    for nid, node in live.items():
+        if _op_name(node) != "LayerNormInputGrad" or len(node.inputs) < 2:
+            continue
+        dy, x = node.inputs[0], node.inputs[1]
+        gamma = node.inputs[2] if len(node.inputs) > 2 else ""
+        mx, md = meta.get(x), meta.get(dy)
+        if mx is None or md is None or mx.scalar or md.scalar or md.shape != mx.shape or len(mx.shape) < 1:
+            continue
+        if mx.dtype != torch.float32 or md.dtype != torch.float32 or node.attributes.get("axis", -1) not in (-1, None):
+            continue
+        outs, cov = {"dx": nid}, {nid}
+        for u in users.get(dy, []):
+            un = live.get(u)
+            if un is None or u == nid or un.attributes.get("axis", -1) not in (-1, None):
+                continue
+            op = _op_name(un)
+            if op == "LayerNormGammaGrad" and un.inputs[:2] == [dy, x] and "dgamma" not in outs:
+                outs["dgamma"] = u
+                cov.add(u)
+            elif op == "LayerNormBetaGrad" and un.inputs[:1] == [dy] and "dbeta" not in outs:
+                outs["dbeta"] = u
+                cov.add(u)
+        eps = float(node.attributes.get("eps", node.attributes.get("epsilon", 1e-5)))
+        if "dgamma" in outs:
+            ge = float(live[outs["dgamma"]].attributes.get("eps", live[outs["dgamma"]].attributes.get("epsilon", 1e-5)))
+            if ge != eps:
+                cov.discard(outs.pop("dgamma"))
+        bind = {"dy": dy, "x": x, "gamma": gamma, "eps": repr(eps)}
+        found.append(Match("ln_bwd", bind, cov, outs))
+    return found
+
+
+def ln_bwd_step(m: Match, meta: dict[str, Meta]) -> Step:
+    b, o = m.bind, m.outputs
+    shape = meta[b["x"]].shape
+    C = shape[-1]
+    R = math.prod(shape[:-1])
+    eps = float(b["eps"])
+    ws_bytes = int(L.lib().b200_layernorm_bwd_workspace_bytes(R, C))
+    ins = [b["dy"], b["x"]] + ([b["gamma"]] if b["gamma"] else [])
+
+    def run(env: dict) -> None:
+        dy = ops.contiguous(ops.cast(env[b["dy"]], torch.float32))
+        x = ops.contiguous(ops.cast(env[b["x"]], torch.float32))
+        ga = ops.contiguous(ops.cast(env[b["gamma"]], torch.float32)) if b["gamma"] else None
+        dev = ops.device()
+        dx = torch.empty(shape, dtype=torch.float32, device=dev)
+        dg = torch.empty(C, dtype=torch.float32, device=dev) if "dgamma" in o else None
+        db = torch.empty(C, dtype=torch.float32, device=dev) if "dbeta" in o else None
+        ws = torch.empty(max(1, ws_bytes), dtype=torch.uint8, device=dev)
+        L.call("b200_layernorm_bwd_rows", dy.data_ptr(), x.data_ptr(), None if ga is None else ga.data_ptr(), dx.data_ptr(),
+               None, None if dg is None else dg.data_ptr(), None if db is None else db.data_ptr(), R, C, eps, ws.data_ptr(),
+               ws_bytes, ops.stream_ptr())
+        env[o["dx"]] = dx
+        if dg is not None:
+            env[o["dgamma"]] = dg
+        if db is not None:
+            env[o["dbeta"]] = db
+
+    return Step(list(o.values()), ins, run, "ln_bwd" + ("+params" if len(o) > 1 else ""))
 
 
 # ----------------------------------------------------------------------------------
@@ -1165,13 +1238,20 @@ def plan_steps(graph: Graph, nodes: list[Node], sample: dict[str, Any]) -> list[
     for m in find_xent(graph, live, meta, users, outputs):
         if m.covered & taken:
             continue
-        groups.append((sorted(m.covered), xent_step(m, meta)))
+        bf, f32 = gemm_use(m.outputs["dx"], live, users, outputs)
+        groups.append((sorted(m.covered), xent_step(m, meta, bf and not f32)))
         taken |= m.covered
 
     for m in find_mask_bwd(graph, live, meta, users, outputs):
         if m.covered & taken:
             continue
         groups.append((sorted(m.covered), mask_bwd_step(m, meta)))
+        taken |= m.covered
+
+    for m in find_ln_bwd(graph, live, meta, users, outputs):
+        if m.covered & taken:
+            continue
+        groups.append((sorted(m.covered), ln_bwd_step(m, meta)))
         taken |= m.covered
 
     for m in find_gelu_bwd(graph, live, meta, users, outputs):

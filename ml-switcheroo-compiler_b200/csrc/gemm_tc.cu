@@ -22,12 +22,15 @@ namespace tc {
 #ifndef B200_GEMM_EPI_WARPS
 #define B200_GEMM_EPI_WARPS 8
 #endif
-#ifndef B200_GEMM_EPI_SLEEP_NS
-#define B200_GEMM_EPI_SLEEP_NS 0
-#endif
-// epilogue warps: 4 (one per TMEM lane quarter) or 8 (two per quarter, splitting columns)
+// Epilogue: 8 warps, two per TMEM lane quarter, splitting the tile's columns. Store mode
+// (per launch): 0 = each lane stores its own row from registers (best when the tile's
+// main loop is short, K <= 128); 2 = the 32 x 32 chunk is staged in a swizzled 4 KB
+// shared-memory buffer per warp and leaves through a TMA bulk-tensor store; 1 = staged
+// the same way, then written back as whole row segments (when no store map fits).
 constexpr int BM = 128, BK = 64, STAGES = 4, EPI_WARPS = B200_GEMM_EPI_WARPS, THREADS = 64 + 32 * EPI_WARPS;
-static_assert(EPI_WARPS == 4 || EPI_WARPS == 8, "4 or 8 epilogue warps");
+constexpr uint32_t EPI_BUF = 4096;  // per epilogue warp
+constexpr uint32_t EPI_SMEM = EPI_WARPS * EPI_BUF;  // after the operand ring
+static_assert(EPI_WARPS == 4 || EPI_WARPS == 8, "4 or 8 epilogue warps (the staging buffers must fit)");
 constexpr unsigned long long WAIT_LIMIT_NS = 2000000000ull;  // 2 s per wait
 
 __device__ __forceinline__ uint32_t smem_u32(const void* p) { return (uint32_t)__cvta_generic_to_shared(p); }
@@ -84,6 +87,79 @@ __device__ __forceinline__ void tma_load_4d(void* dst, const CUtensorMap* map, u
       : "memory");
 }
 
+__device__ __forceinline__ void st_shared_v4(uint32_t addr, uint32_t a, uint32_t b, uint32_t c, uint32_t d) {
+  asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(addr), "r"(a), "r"(b), "r"(c), "r"(d) : "memory");
+}
+__device__ __forceinline__ uint4 ld_shared_v4(uint32_t addr) {
+  uint4 u;
+  asm volatile("ld.shared.v4.b32 {%0, %1, %2, %3}, [%4];" : "=r"(u.x), "=r"(u.y), "=r"(u.z), "=r"(u.w) : "r"(addr) : "memory");
+  return u;
+}
+__device__ __forceinline__ void tma_store_4d(const CUtensorMap* map, uint32_t src, int c0, int c1, int c2, int c3) {
+  asm volatile("cp.async.bulk.tensor.4d.global.shared::cta.bulk_group [%0, {%1, %2, %3, %4}], [%5];" ::"l"(
+                   reinterpret_cast<uint64_t>(map)),
+               "r"(c0), "r"(c1), "r"(c2), "r"(c3), "r"(src)
+               : "memory");
+}
+__device__ __forceinline__ void bulk_commit() { asm volatile("cp.async.bulk.commit_group;" ::: "memory"); }
+__device__ __forceinline__ void bulk_wait_read0() { asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory"); }
+__device__ __forceinline__ void bulk_wait0() { asm volatile("cp.async.bulk.wait_group 0;" ::: "memory"); }
+__device__ __forceinline__ void fence_proxy_async_smem() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
+
+// Stage a 32 x 32 chunk (lane = row, `w` = the row's 32 elements packed into 32-bit words)
+// into a swizzled buffer: ESZ-byte elements, rows of 32 * ESZ bytes, 16-byte pieces XORed
+// by the row index (the 128B / 64B / 32B TMA swizzle patterns), so both the row-per-lane
+// writes and the row-contiguous reads are free of bank conflicts.
+template <int ESZ>
+__device__ __forceinline__ void stage_chunk(uint32_t buf, int lane, const uint32_t (&w)[8 * ESZ]) {
+  constexpr int PIECES = 2 * ESZ;  // 16-byte pieces per row
+  const uint32_t rb = buf + (uint32_t)lane * (32u * ESZ);
+  const uint32_t sw = ESZ == 4 ? (uint32_t)(lane & 7) : (ESZ == 2 ? (uint32_t)((lane >> 1) & 3) : (uint32_t)((lane >> 2) & 1));
+#pragma unroll
+  for (int j = 0; j < PIECES; ++j)
+    st_shared_v4(rb + (((uint32_t)j ^ sw) << 4), w[4 * j], w[4 * j + 1], w[4 * j + 2], w[4 * j + 3]);
+}
+
+// store `n` (<= 16) bytes of a 16-byte piece at dst: one vector store when whole and aligned
+__device__ __forceinline__ void put_piece(uint8_t* dst, uint4 u, int64_t n) {
+  if (n >= 16 && (reinterpret_cast<uintptr_t>(dst) & 15) == 0) {
+    *reinterpret_cast<uint4*>(dst) = u;
+    return;
+  }
+  const uint32_t w[4] = {u.x, u.y, u.z, u.w};
+  if ((reinterpret_cast<uintptr_t>(dst) & 3) == 0) {
+#pragma unroll
+    for (int k = 0; k < 4; ++k)
+      if (4 * k + 4 <= n) reinterpret_cast<uint32_t*>(dst)[k] = w[k];
+      else {
+        for (int b = 4 * k; b < n && b < 4 * k + 4; ++b) dst[b] = (uint8_t)(w[k] >> (8 * (b & 3)));
+        break;
+      }
+    return;
+  }
+  for (int b = 0; b < 16 && b < n; ++b) dst[b] = (uint8_t)(w[b >> 2] >> (8 * (b & 3)));
+}
+
+// Write the staged chunk back row-contiguously: every warp store instruction covers
+// 512 / 32 / ... whole row segments. `base` = element (row0, cbase) of the output,
+// `ld` = row stride in elements, `rows` / `cols` = how much of the chunk is inside.
+template <int ESZ>
+__device__ __forceinline__ void write_chunk(uint32_t buf, int lane, uint8_t* base, int64_t ld, int rows, int64_t cols) {
+  constexpr int PIECES = 2 * ESZ;         // 16-byte pieces per row
+  constexpr int ROWS_PER = 32 / PIECES;   // rows one instruction covers
+  const int j = lane % PIECES;
+#pragma unroll
+  for (int i = 0; i < PIECES; ++i) {
+    const int rr = i * ROWS_PER + lane / PIECES;
+    if (rr >= rows) continue;
+    const uint32_t sw = ESZ == 4 ? (uint32_t)(rr & 7) : (ESZ == 2 ? (uint32_t)((rr >> 1) & 3) : (uint32_t)((rr >> 2) & 1));
+    const uint4 u = ld_shared_v4(buf + (uint32_t)rr * (32u * ESZ) + (((uint32_t)j ^ sw) << 4));
+    const int64_t left = (cols - (int64_t)j * (16 / ESZ)) * ESZ;  // bytes of this piece inside the row
+    if (left <= 0) continue;
+    put_piece(base + ((int64_t)rr * ld + (int64_t)j * (16 / ESZ)) * ESZ, u, left);
+  }
+}
+
 __device__ __forceinline__ uint32_t pack_bf16(float a, float b) {
   __nv_bfloat162 t = __floats2bfloat162_rn(a, b);
   return *reinterpret_cast<uint32_t*>(&t);
@@ -138,6 +214,7 @@ struct Args {
   void* C2;  // optional bf16 copy of the activation; C then receives the pre-activation
   const float* bias;
   uint8_t* aux;
+  int store_mode;  // 0 direct, 1 staged + row-segment stores, 2 staged + TMA bulk stores
   int64_t M, N, K, sC, ldc;
   float alpha;
   int c_dt, epi, a_mn, b_mn, batch;  // batch = b_out * b_in tiles-of-matrices
@@ -158,6 +235,9 @@ __device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
 template <int BN>
 __global__ void __launch_bounds__(THREADS, 1) gemm_tc_kernel(const __grid_constant__ CUtensorMap mapA,
                                                              const __grid_constant__ CUtensorMap mapB,
+                                                             const __grid_constant__ CUtensorMap mapC,
+                                                             const __grid_constant__ CUtensorMap mapC2,
+                                                             const __grid_constant__ CUtensorMap mapAux,
                                                              const __grid_constant__ Args args) {
   constexpr uint32_t A_BYTES = BM * BK * 2;  // 16 KB
   constexpr uint32_t B_BYTES = BN * BK * 2;
@@ -165,7 +245,8 @@ __global__ void __launch_bounds__(THREADS, 1) gemm_tc_kernel(const __grid_consta
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* sA = smem;
   uint8_t* sB = smem + STAGES * A_BYTES;
-  uint64_t* full_bar = reinterpret_cast<uint64_t*>(sB + STAGES * B_BYTES);
+  uint8_t* sEpi = sB + STAGES * B_BYTES;  // EPI_SMEM bytes, 1024-aligned
+  uint64_t* full_bar = reinterpret_cast<uint64_t*>(sEpi + EPI_SMEM);
   uint64_t* empty_bar = full_bar + STAGES;
   uint64_t* acc_full = empty_bar + STAGES;  // [2]
   uint64_t* acc_empty = acc_full + 2;       // [2]
@@ -286,101 +367,136 @@ __global__ void __launch_bounds__(THREADS, 1) gemm_tc_kernel(const __grid_consta
       const int m_tile = r / tiles_n, n_tile = r % tiles_n;
       const int b = local & 1;
       const uint32_t use = local >> 1;
-      if (!mbar_wait(&acc_full[b], use & 1, B200_GEMM_EPI_SLEEP_NS)) break;
+      if (!mbar_wait(&acc_full[b], use & 1)) break;
       tc_fence_after();
       const int64_t row = (int64_t)m_tile * BM + q * 32 + lane;
       const int64_t col0 = (int64_t)n_tile * BN + half * (BN / NHALF);
       const int zo = z / args.b_in, zi = z % args.b_in;
       const uint32_t tbase = tmem_base + ((uint32_t)(q * 32) << 16) + (uint32_t)(b * BN + half * (BN / NHALF));
-      uint32_t buf[2][32];
-      if (num_kb > 0) {
-        tmem_ld32_issue(tbase, buf[0]);
-        tmem_wait(buf[0]);
-      } else {
-#pragma unroll
-        for (int i = 0; i < 32; ++i) buf[0][i] = 0u;
-      }
-#pragma unroll
+#pragma unroll 1
       for (int c = 0; c < CH; ++c) {
-        uint32_t (&cur)[32] = buf[c & 1];
-        uint32_t (&nxt)[32] = buf[(c + 1) & 1];
-        if (c + 1 < CH) {
-          if (num_kb > 0) {
-            tmem_ld32_issue(tbase + (uint32_t)((c + 1) * 32), nxt);
-          } else {
+        uint32_t cur[32];
+        if (num_kb > 0) {
+          tmem_ld32_issue(tbase + (uint32_t)(c * 32), cur);
+          tmem_wait(cur);
+        } else {
 #pragma unroll
-            for (int i = 0; i < 32; ++i) nxt[i] = 0u;
-          }
+          for (int i = 0; i < 32; ++i) cur[i] = 0u;
         }
         const int64_t cbase = col0 + c * 32;
-        if (row < args.M && cbase < args.N) {
-          // pre = alpha * acc + bias; act = epi(pre); mask bit = pre > 0
-          float v[32], act[32];
-          uint32_t mbits = 0;
+        if (cbase >= args.N) continue;  // warp-uniform
+        // pre = alpha * acc + bias; act = epi(pre); mask bit = pre > 0
+        float v[32], act[32];
+        uint32_t mbits = 0;
 #pragma unroll
-          for (int i = 0; i < 32; ++i) {
-            const int64_t n = cbase + i;
-            const float pre = args.alpha * __uint_as_float(cur[i]) + ((args.bias && n < args.N) ? __ldg(args.bias + n) : 0.f);
-            mbits |= (pre > 0.f ? 1u : 0u) << i;
-            float a = pre;
-            if (args.epi == B200_EPI_RELU) a = pre > 0.f ? pre : 0.f;
-            else if (args.epi == B200_EPI_GELU) a = gelu_tanh(pre);
-            act[i] = a;
-            v[i] = args.C2 ? pre : a;
-          }
-          const int64_t off = (int64_t)zo * args.sC + (int64_t)zi * args.sC_in + row * args.ldc + cbase;
-          const bool full = cbase + 32 <= args.N;
-          if (args.c_dt == B200_F32) {
-            float* dst = reinterpret_cast<float*>(args.C) + off;
-            if (full && ((reinterpret_cast<uintptr_t>(dst) & 15) == 0)) {
-#pragma unroll
-              for (int i = 0; i < 32; i += 4) *reinterpret_cast<float4*>(dst + i) = make_float4(v[i], v[i + 1], v[i + 2], v[i + 3]);
-            } else {
-              for (int i = 0; i < 32; ++i)
-                if (cbase + i < args.N) dst[i] = v[i];
+        for (int i = 0; i < 32; ++i) {
+          const int64_t n = cbase + i;
+          const float pre = args.alpha * __uint_as_float(cur[i]) + ((args.bias && n < args.N) ? __ldg(args.bias + n) : 0.f);
+          mbits |= (pre > 0.f ? 1u : 0u) << i;
+          float a = pre;
+          if (args.epi == B200_EPI_RELU) a = pre > 0.f ? pre : 0.f;
+          else if (args.epi == B200_EPI_GELU) a = gelu_tanh(pre);
+          act[i] = a;
+          v[i] = args.C2 ? pre : a;
+        }
+        const int64_t zoff = (int64_t)zo * args.sC + (int64_t)zi * args.sC_in;
+        if (args.store_mode != 0) {
+          const int row0 = (int)(m_tile * BM + q * 32);
+          if (row0 >= args.M) continue;  // warp-uniform: none of this warp's rows exist
+          const int rows_in = (int)min((int64_t)32, args.M - row0);
+          const int64_t cols_in = min((int64_t)32, args.N - cbase);
+          const uint32_t buf = smem_u32(sEpi) + (uint32_t)(warp - 2) * EPI_BUF;
+          const bool tma = args.store_mode == 2;
+          // C (fp32 or bf16), then C2 (bf16), then the mask, through the same buffer
+#pragma unroll 1
+          for (int part = 0; part < 3; ++part) {
+            if (part == 1 && !args.C2) continue;
+            if (part == 2 && !args.aux) continue;
+            const int esz = part == 0 ? (args.c_dt == B200_F32 ? 4 : 2) : (part == 1 ? 2 : 1);
+            if (tma) {
+              if (lane == 0) bulk_wait_read0();  // the previous bulk store has read the buffer
             }
-          } else {
-            __nv_bfloat16* dst = reinterpret_cast<__nv_bfloat16*>(args.C) + off;
-            if (full && ((reinterpret_cast<uintptr_t>(dst) & 15) == 0)) {
+            __syncwarp();
+            if (esz == 4) {
+              uint32_t w[32];
 #pragma unroll
-              for (int i = 0; i < 32; i += 8)
-                *reinterpret_cast<uint4*>(dst + i) = make_uint4(pack_bf16(v[i], v[i + 1]), pack_bf16(v[i + 2], v[i + 3]),
-                                                                pack_bf16(v[i + 4], v[i + 5]), pack_bf16(v[i + 6], v[i + 7]));
-            } else {
-              for (int i = 0; i < 32; ++i)
-                if (cbase + i < args.N) dst[i] = __float2bfloat16_rn(v[i]);
-            }
-          }
-          if (args.C2) {
-            __nv_bfloat16* dst = reinterpret_cast<__nv_bfloat16*>(args.C2) + off;
-            if (full && ((reinterpret_cast<uintptr_t>(dst) & 15) == 0)) {
+              for (int i = 0; i < 32; ++i) w[i] = __float_as_uint(v[i]);
+              stage_chunk<4>(buf, lane, w);
+            } else if (esz == 2) {
+              const float* src = part == 0 ? v : act;
+              uint32_t w[16];
 #pragma unroll
-              for (int i = 0; i < 32; i += 8)
-                *reinterpret_cast<uint4*>(dst + i) = make_uint4(pack_bf16(act[i], act[i + 1]), pack_bf16(act[i + 2], act[i + 3]),
-                                                                pack_bf16(act[i + 4], act[i + 5]), pack_bf16(act[i + 6], act[i + 7]));
+              for (int i = 0; i < 16; ++i) w[i] = pack_bf16(src[2 * i], src[2 * i + 1]);
+              stage_chunk<2>(buf, lane, w);
             } else {
-              for (int i = 0; i < 32; ++i)
-                if (cbase + i < args.N) dst[i] = __float2bfloat16_rn(act[i]);
-            }
-          }
-          if (args.aux) {
-            uint8_t* mdst = args.aux + off;
-            if (full && ((reinterpret_cast<uintptr_t>(mdst) & 15) == 0)) {
               uint32_t w[8];
 #pragma unroll
               for (int k = 0; k < 8; ++k) {
                 const uint32_t nib = (mbits >> (4 * k)) & 0xFu;
                 w[k] = (nib & 1u) | ((nib >> 1) & 1u) << 8 | ((nib >> 2) & 1u) << 16 | ((nib >> 3) & 1u) << 24;
               }
-              reinterpret_cast<uint4*>(mdst)[0] = make_uint4(w[0], w[1], w[2], w[3]);
-              reinterpret_cast<uint4*>(mdst)[1] = make_uint4(w[4], w[5], w[6], w[7]);
-            } else {
-              for (int i = 0; i < 32; ++i)
-                if (cbase + i < args.N) mdst[i] = (uint8_t)((mbits >> i) & 1u);
+              stage_chunk<1>(buf, lane, w);
             }
+            if (tma) {
+              fence_proxy_async_smem();
+              __syncwarp();
+              if (lane == 0) {
+                const CUtensorMap* m = part == 0 ? &mapC : (part == 1 ? &mapC2 : &mapAux);
+                tma_store_4d(m, buf, (int)cbase, row0, zi, zo);
+                bulk_commit();
+              }
+              continue;
+            }
+            __syncwarp();
+            uint8_t* dst = part == 0 ? reinterpret_cast<uint8_t*>(args.C) : (part == 1 ? reinterpret_cast<uint8_t*>(args.C2) : args.aux);
+            dst += (zoff + (int64_t)row0 * args.ldc + cbase) * esz;
+            if (esz == 4) write_chunk<4>(buf, lane, dst, args.ldc, rows_in, cols_in);
+            else if (esz == 2) write_chunk<2>(buf, lane, dst, args.ldc, rows_in, cols_in);
+            else write_chunk<1>(buf, lane, dst, args.ldc, rows_in, cols_in);
+          }
+          continue;
+        }
+        if (row >= args.M) continue;
+        const int64_t off = zoff + row * args.ldc + cbase;
+        const bool full = cbase + 32 <= args.N;
+        if (args.c_dt == B200_F32) {
+          float* dst = reinterpret_cast<float*>(args.C) + off;
+          if (full && ((reinterpret_cast<uintptr_t>(dst) & 15) == 0)) {
+#pragma unroll
+            for (int i = 0; i < 32; i += 4) *reinterpret_cast<float4*>(dst + i) = make_float4(v[i], v[i + 1], v[i + 2], v[i + 3]);
+          } else {
+            for (int i = 0; i < 32; ++i)
+              if (cbase + i < args.N) dst[i] = v[i];
+          }
+        } else {
+          __nv_bfloat16* dst = reinterpret_cast<__nv_bfloat16*>(args.C) + off;
+          if (full && ((reinterpret_cast<uintptr_t>(dst) & 15) == 0)) {
+#pragma unroll
+            for (int i = 0; i < 32; i += 8)
+              *reinterpret_cast<uint4*>(dst + i) = make_uint4(pack_bf16(v[i], v[i + 1]), pack_bf16(v[i + 2], v[i + 3]),
+                                                              pack_bf16(v[i + 4], v[i + 5]), pack_bf16(v[i + 6], v[i + 7]));
+          } else {
+            for (int i = 0; i < 32; ++i)
+              if (cbase + i < args.N) dst[i] = __float2bfloat16_rn(v[i]);
           }
         }
-        if (c + 1 < CH && num_kb > 0) tmem_wait(nxt);
+        if (args.C2) {
+          __nv_bfloat16* dst = reinterpret_cast<__nv_bfloat16*>(args.C2) + off;
+          if (full && ((reinterpret_cast<uintptr_t>(dst) & 15) == 0)) {
+#pragma unroll
+            for (int i = 0; i < 32; i += 8)
+              *reinterpret_cast<uint4*>(dst + i) = make_uint4(pack_bf16(act[i], act[i + 1]), pack_bf16(act[i + 2], act[i + 3]),
+                                                              pack_bf16(act[i + 4], act[i + 5]), pack_bf16(act[i + 6], act[i + 7]));
+          } else {
+            for (int i = 0; i < 32; ++i)
+              if (cbase + i < args.N) dst[i] = __float2bfloat16_rn(act[i]);
+          }
+        }
+        if (args.aux) {
+          uint8_t* mdst = args.aux + off;
+          for (int i = 0; i < 32; ++i)
+            if (cbase + i < args.N) mdst[i] = (uint8_t)((mbits >> i) & 1u);
+        }
       }
       // accumulator b may be overwritten once every epilogue warp has read it
       tc_fence_before();
@@ -388,6 +504,7 @@ __global__ void __launch_bounds__(THREADS, 1) gemm_tc_kernel(const __grid_consta
       if (lane == 0) mbar_arrive(&acc_empty[b]);
     }
   }
+  if (args.store_mode == 2 && warp >= 2 && lane == 0) bulk_wait0();  // this warp's bulk stores are complete
   tc_fence_before();
   __syncthreads();
   if (warp == 1) {
@@ -436,9 +553,32 @@ static int make_map(CUtensorMap* map, const void* base, uint64_t d0, uint64_t d1
   return B200_OK;
 }
 
+// Store map for C / C2 / mask (store mode 2): dims (N, M, b_in, b_out), byte strides
+// (ldc, sC_in, sC_out) * esize, box 32 x 32 (one epilogue warp's chunk), swizzle matching
+// the staged rows (128 B fp32, 64 B bf16, 32 B mask rows). False when TMA cannot address it.
+static bool make_store_map(CUtensorMap* map, void* base, CUtensorMapDataType dt, uint32_t esize, int64_t N, int64_t M,
+                           int64_t b_in, int64_t b_out, int64_t ldc, int64_t sC_in, int64_t sC_out) {
+  auto enc = get_encode();
+  if (!enc || !base || (reinterpret_cast<uintptr_t>(base) & 15)) return false;
+  const uint64_t rowb = (uint64_t)ldc * esize;
+  const uint64_t s2 = b_in > 1 ? (uint64_t)sC_in * esize : rowb * (uint64_t)M;
+  const uint64_t s3 = b_out > 1 ? (uint64_t)sC_out * esize : s2 * (uint64_t)b_in;
+  if (rowb % 16 || s2 % 16 || s3 % 16 || rowb == 0 || s2 == 0 || s3 == 0) return false;
+  if (rowb >= (1ull << 40) || s2 >= (1ull << 40) || s3 >= (1ull << 40)) return false;
+  cuuint64_t dims[4] = {(cuuint64_t)N, (cuuint64_t)M, (cuuint64_t)b_in, (cuuint64_t)b_out};
+  cuuint64_t strides[3] = {rowb, s2, s3};
+  cuuint32_t box[4] = {32, 32, 1, 1};
+  cuuint32_t estr[4] = {1, 1, 1, 1};
+  const CUtensorMapSwizzle sw =
+      esize == 4 ? CU_TENSOR_MAP_SWIZZLE_128B : (esize == 2 ? CU_TENSOR_MAP_SWIZZLE_64B : CU_TENSOR_MAP_SWIZZLE_32B);
+  return enc(map, dt, 4, base, dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, sw, CU_TENSOR_MAP_L2_PROMOTION_NONE,
+             CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
 template <int BN>
-static int launch(const CUtensorMap& ma, const CUtensorMap& mb, const Args& a, int64_t batch, cudaStream_t s) {
-  const size_t smem = (size_t)STAGES * (BM * BK * 2 + BN * BK * 2) + 1024 + 256;
+static int launch(const CUtensorMap& ma, const CUtensorMap& mb, const CUtensorMap& mc, const CUtensorMap& mc2,
+                  const CUtensorMap& maux, const Args& a, int64_t batch, cudaStream_t s) {
+  const size_t smem = (size_t)STAGES * (BM * BK * 2 + BN * BK * 2) + EPI_SMEM + 1024 + 256;
   const int64_t tiles = ceil_div(a.N, BN) * ceil_div(a.M, BM) * batch;  // batch = b_out * b_in
   static bool attr_set[64] = {false};
   int dev = 0;
@@ -448,7 +588,7 @@ static int launch(const CUtensorMap& ma, const CUtensorMap& mb, const Args& a, i
     if (dev >= 0 && dev < 64) attr_set[dev] = true;
   }
   const unsigned grid = (unsigned)std::max<int64_t>(1, std::min<int64_t>(tiles, num_sms()));
-  gemm_tc_kernel<BN><<<grid, THREADS, smem, s>>>(ma, mb, a);
+  gemm_tc_kernel<BN><<<grid, THREADS, smem, s>>>(ma, mb, mc, mc2, maux, a);
   return check_launch("gemm(bf16 tcgen05)");
 }
 
@@ -526,8 +666,21 @@ int gemm_bf16_tcgen05_b2(int c_dt, const void* A, const void* B, void* C, int64_
   a.b_bc_out = b_bc_out;
   a.b_bc_in = b_bc_in;
   B200_REQUIRE(ceil_div(M, BM) <= 65535, "gemm(bf16): M too large");
-  if (BN == 256) return launch<256>(ma, mb, a, batch, s);
-  return launch<128>(ma, mb, a, batch, s);
+  CUtensorMap mc, mc2, maux;
+  memset(&mc, 0, sizeof(mc));
+  memset(&mc2, 0, sizeof(mc2));
+  memset(&maux, 0, sizeof(maux));
+  a.store_mode = K <= 128 ? 0 : 1;
+  if (a.store_mode && M <= INT32_MAX && N <= INT32_MAX) {
+    const bool f32 = c_dt == B200_F32;
+    bool ok = make_store_map(&mc, C, f32 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT32 : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, f32 ? 4 : 2, N, M,
+                             b_in, b_out, ldc, sC_in, sC_out);
+    if (ok && C2) ok = make_store_map(&mc2, C2, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, N, M, b_in, b_out, ldc, sC_in, sC_out);
+    if (ok && aux) ok = make_store_map(&maux, aux, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, N, M, b_in, b_out, ldc, sC_in, sC_out);
+    if (ok) a.store_mode = 2;
+  }
+  if (BN == 256) return launch<256>(ma, mb, mc, mc2, maux, a, batch, s);
+  return launch<128>(ma, mb, mc, mc2, maux, a, batch, s);
 }
 
 int gemm_bf16_tcgen05(int c_dt, const void* A, const void* B, void* C, int64_t batch, int64_t M, int64_t N, int64_t K,

@@ -14,6 +14,11 @@
 
 #include "common.cuh"
 
+extern "C" int b200_layernorm_input_grad_rows(const float* dy, const float* x, const float* gamma, float* dx, void* dx_bf16,
+                                              int64_t rows, int64_t cols, float eps, void* stream);
+extern "C" int b200_layernorm_param_grad(const float* dy, const float* x, float* dgamma, float* dbeta, int64_t rows,
+                                         int64_t cols, float eps, void* stream);
+
 namespace b200 {
 namespace lnr {
 
@@ -199,6 +204,122 @@ __global__ void __launch_bounds__(512) ln_dx_block_kernel(const float* __restric
   }
 }
 
+// Whole LayerNorm backward, warp per row, persistent: dx for every row, and per-CTA
+// column partials of dgamma = sum dy * xhat and dbeta = sum dy (LayerNormGammaGrad /
+// LayerNormBetaGrad, nn_ops.py:276-318) reduced across the CTA's warps in shared memory;
+// a second kernel sums the CTA partials in a fixed order (deterministic).
+template <int NC>
+__global__ void __launch_bounds__(WARPS * 32) ln_bwd_warp_kernel(const float* __restrict__ dy, const float* __restrict__ x,
+                                                                 const float* __restrict__ gamma, float* __restrict__ dx,
+                                                                 __nv_bfloat16* __restrict__ dxb, float* __restrict__ part,
+                                                                 int64_t rows, int cols, float eps) {
+  extern __shared__ float sp[];  // [WARPS][2][cols] per-warp column partials
+  const int lane = threadIdx.x & 31, w = threadIdx.x >> 5;
+  float pg[NC][4], pb[NC][4];
+#pragma unroll
+  for (int c = 0; c < NC; ++c)
+#pragma unroll
+    for (int k = 0; k < 4; ++k) pg[c][k] = pb[c][k] = 0.f;
+  float gm[NC][4];
+#pragma unroll
+  for (int c = 0; c < NC; ++c) {
+    const int col = (c * 32 + lane) * 4;
+    const float4 g = (gamma && col < cols) ? ld4(gamma + col) : make_float4(1.f, 1.f, 1.f, 1.f);
+    gm[c][0] = g.x; gm[c][1] = g.y; gm[c][2] = g.z; gm[c][3] = g.w;
+  }
+  for (int64_t row = (int64_t)blockIdx.x * WARPS + w; row < rows; row += (int64_t)gridDim.x * WARPS) {
+    const float* xr = x + row * cols;
+    const float* dr = dy + row * cols;
+    float v[NC][4], d[NC][4];
+    float s = 0.f;
+#pragma unroll
+    for (int c = 0; c < NC; ++c) {
+      const int col = (c * 32 + lane) * 4;
+      if (col < cols) {
+        const float4 t = __ldcs(reinterpret_cast<const float4*>(xr + col));
+        const float4 e = __ldcs(reinterpret_cast<const float4*>(dr + col));
+        v[c][0] = t.x; v[c][1] = t.y; v[c][2] = t.z; v[c][3] = t.w;
+        d[c][0] = e.x; d[c][1] = e.y; d[c][2] = e.z; d[c][3] = e.w;
+      } else {
+#pragma unroll
+        for (int k = 0; k < 4; ++k) v[c][k] = d[c][k] = 0.f;
+      }
+      s += (v[c][0] + v[c][1]) + (v[c][2] + v[c][3]);
+    }
+    const float mean = warp_sum(s) / (float)cols;
+    float q = 0.f;
+#pragma unroll
+    for (int c = 0; c < NC; ++c) {
+      const int col = (c * 32 + lane) * 4;
+      if (col < cols) {
+#pragma unroll
+        for (int k = 0; k < 4; ++k) {
+          const float t = v[c][k] - mean;
+          q += t * t;
+        }
+      }
+    }
+    const float rstd = 1.f / sqrtf(warp_sum(q) / (float)cols + eps);
+    float s1 = 0.f, s2 = 0.f;
+#pragma unroll
+    for (int c = 0; c < NC; ++c)
+#pragma unroll
+      for (int k = 0; k < 4; ++k) {
+        v[c][k] = (v[c][k] - mean) * rstd;  // xhat
+        const float gd = d[c][k] * gm[c][k];
+        s1 += gd;
+        s2 += gd * v[c][k];
+        pg[c][k] += d[c][k] * v[c][k];
+        pb[c][k] += d[c][k];
+      }
+    const float S1 = warp_sum(s1), S2 = warp_sum(s2);
+    const float fc = (float)cols, f = rstd / fc;
+#pragma unroll
+    for (int c = 0; c < NC; ++c) {
+      const int col = (c * 32 + lane) * 4;
+      if (col >= cols) continue;
+      float o[4];
+#pragma unroll
+      for (int k = 0; k < 4; ++k) o[k] = f * (fc * (d[c][k] * gm[c][k]) - S1 - v[c][k] * S2);
+      if (dx) *reinterpret_cast<float4*>(dx + row * cols + col) = make_float4(o[0], o[1], o[2], o[3]);
+      if (dxb) st_bf16x4(dxb + row * cols + col, o[0], o[1], o[2], o[3]);
+    }
+  }
+  // CTA partials: warps add their columns in a fixed order
+#pragma unroll
+  for (int c = 0; c < NC; ++c) {
+    const int col = (c * 32 + lane) * 4;
+    if (col >= cols) continue;
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {
+      sp[(w * 2 + 0) * cols + col + k] = pg[c][k];
+      sp[(w * 2 + 1) * cols + col + k] = pb[c][k];
+    }
+  }
+  __syncthreads();
+  for (int i = threadIdx.x; i < 2 * cols; i += blockDim.x) {
+    const int which = i / cols, col = i % cols;
+    float acc = 0.f;
+    for (int ww = 0; ww < WARPS; ++ww) acc += sp[(ww * 2 + which) * cols + col];
+    part[((int64_t)blockIdx.x * 2 + which) * cols + col] = acc;
+  }
+}
+
+__global__ void ln_colsum_kernel(const float* __restrict__ part, float* __restrict__ dg, float* __restrict__ db, int64_t G,
+                                 int64_t cols) {
+  const int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x;
+  if (i >= 2 * cols) return;
+  const int64_t which = i / cols, col = i % cols;
+  float acc = 0.f;
+  for (int64_t g = 0; g < G; ++g) acc += part[(g * 2 + which) * cols + col];
+  if (which == 0 && dg) dg[col] = acc;
+  if (which == 1 && db) db[col] = acc;
+}
+
+inline int64_t ln_bwd_grid(int64_t rows) {
+  return std::max<int64_t>(1, std::min<int64_t>(ceil_div(rows, (int64_t)WARPS), (int64_t)num_sms()));
+}
+
 inline int chunks_for(int64_t cols) {
   if (cols % 4) return 0;
   const int64_t nc = ceil_div(cols, 128);
@@ -264,4 +385,61 @@ extern "C" int b200_layernorm_input_grad_rows(const float* dy, const float* x, c
     }
   }
   return check_launch("layernorm_input_grad_rows");
+}
+
+extern "C" size_t b200_layernorm_bwd_workspace_bytes(int64_t rows, int64_t cols) {
+  if (rows <= 0 || cols <= 0) return 0;
+  return (size_t)ln_bwd_grid(rows) * 2 * (size_t)cols * sizeof(float);
+}
+
+extern "C" int b200_layernorm_bwd_rows(const float* dy, const float* x, const float* gamma, float* dx, void* dx_bf16,
+                                       float* dgamma, float* dbeta, int64_t rows, int64_t cols, float eps, void* workspace,
+                                       size_t workspace_bytes, void* stream) {
+  B200_REQUIRE(dy && x, "layernorm_bwd_rows: null input");
+  B200_REQUIRE(rows >= 0 && cols >= 1 && rows <= 2147483647LL && cols <= 2147483647LL, "layernorm_bwd_rows: bad sizes");
+  cudaStream_t s = as_stream(stream);
+  if (rows == 0) {
+    if (dgamma) cudaMemsetAsync(dgamma, 0, cols * 4, s);
+    if (dbeta) cudaMemsetAsync(dbeta, 0, cols * 4, s);
+    return check_launch("layernorm_bwd_rows(empty)");
+  }
+  auto* db = reinterpret_cast<__nv_bfloat16*>(dx_bf16);
+  const int nc = chunks_for(cols);
+  const bool fits = nc > 0 && nc <= 8 && al16(x) && al16(dy) && (!gamma || al16(gamma)) && (!dx || al16(dx)) && (!db || al8(db));
+  if (!fits) {
+    // general shapes: the separate input-gradient and parameter-gradient kernels
+    int rc = B200_OK;
+    if (dx || db) rc = b200_layernorm_input_grad_rows(dy, x, gamma, dx, dx_bf16, rows, cols, eps, stream);
+    if (rc == B200_OK && (dgamma || dbeta)) rc = b200_layernorm_param_grad(dy, x, dgamma, dbeta, rows, cols, eps, stream);
+    return rc;
+  }
+  const size_t need = b200_layernorm_bwd_workspace_bytes(rows, cols);
+  B200_REQUIRE(workspace && workspace_bytes >= need, "layernorm_bwd_rows: workspace %zu < %zu", workspace_bytes, need);
+  const int64_t G = ln_bwd_grid(rows);
+  const size_t smem = (size_t)WARPS * 2 * (size_t)cols * sizeof(float);
+  B200_REQUIRE(smem <= 200 * 1024, "layernorm_bwd_rows: %lld columns too many", (long long)cols);
+  float* part = reinterpret_cast<float*>(workspace);
+#define B200_LNB(NCV)                                                                                              \
+  case NCV: {                                                                                                      \
+    static bool attr = false;                                                                                      \
+    if (!attr) {                                                                                                   \
+      cudaFuncSetAttribute(ln_bwd_warp_kernel<NCV>, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);      \
+      attr = true;                                                                                                 \
+    }                                                                                                              \
+    ln_bwd_warp_kernel<NCV><<<(unsigned)G, WARPS * 32, smem, s>>>(dy, x, gamma, dx, db, part, rows, (int)cols, eps); \
+    break;                                                                                                         \
+  }
+  switch (nc) {
+    B200_LNB(1)
+    B200_LNB(2)
+    B200_LNB(4)
+    B200_LNB(8)
+    default: break;
+  }
+#undef B200_LNB
+  int rc = check_launch("layernorm_bwd_rows");
+  if (rc) return rc;
+  if (!dgamma && !dbeta) return B200_OK;
+  ln_colsum_kernel<<<(unsigned)ceil_div(2 * cols, (int64_t)256), 256, 0, s>>>(part, dgamma, dbeta, G, cols);
+  return check_launch("layernorm_bwd_rows(colsum)");
 }

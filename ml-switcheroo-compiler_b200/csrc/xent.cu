@@ -64,17 +64,104 @@ __global__ void __launch_bounds__(XE_T) xent_kernel(const T* __restrict__ x, con
   }
 }
 
+// Rows whose columns fit in registers (V % 4 == 0, V <= XR_T * VPT, fp32 logits): the row
+// is read from HBM once, exp(x - max) is evaluated once per element and kept, and dx is
+// written in fp32 and/or bf16 (bf16 when it only feeds the output-projection GEMMs).
+constexpr int XR_T = 512;
+
+template <int VPT>
+__global__ void __launch_bounds__(XR_T) xent_reg_kernel(const float* __restrict__ x, const int64_t* __restrict__ label,
+                                                        const float* __restrict__ d, float* __restrict__ picked,
+                                                        float* __restrict__ dx, __nv_bfloat16* __restrict__ dxb, int64_t V) {
+  __shared__ float red[32];
+  constexpr int NC = VPT / 4;
+  const int64_t r = blockIdx.x;
+  const float* xr = x + r * V;
+  float v[NC][4];
+  float m = -INFINITY;
+#pragma unroll
+  for (int c = 0; c < NC; ++c) {
+    const int64_t col = ((int64_t)c * XR_T + threadIdx.x) * 4;
+    if (col < V) {
+      const float4 t = __ldcs(reinterpret_cast<const float4*>(xr + col));
+      v[c][0] = t.x; v[c][1] = t.y; v[c][2] = t.z; v[c][3] = t.w;
+    } else {
+      v[c][0] = v[c][1] = v[c][2] = v[c][3] = -INFINITY;
+    }
+#pragma unroll
+    for (int k = 0; k < 4; ++k) m = fmaxf(m, v[c][k]);
+  }
+  const float M = block_max(m, red);
+  int64_t lab = label[r];
+  if (lab < 0) lab += V;
+  const bool ok = lab >= 0 && lab < V;
+  float xl = 0.f, s = 0.f;
+#pragma unroll
+  for (int c = 0; c < NC; ++c) {
+    const int64_t col = ((int64_t)c * XR_T + threadIdx.x) * 4;
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {
+      if (col + k == lab) xl = v[c][k];
+      const float e = (v[c][k] == -INFINITY) ? 0.f : expf(v[c][k] - M);
+      v[c][k] = e;
+      s += e;
+    }
+  }
+  const float S = block_sum(s, red);
+  const float lse = M + logf(S);
+  // the label's logit: exactly one thread holds it
+  const bool holder = ok && ((lab >> 2) % XR_T) == threadIdx.x;
+  if (holder && picked) picked[r] = xl - lse;
+  if (threadIdx.x == 0 && !ok) {
+    raise_device_error(B200_ERR_ARG);
+    if (picked) picked[r] = 0.f;
+  }
+  if (!dx && !dxb) return;
+  const float dr = d[r], inv = 1.f / S;
+#pragma unroll
+  for (int c = 0; c < NC; ++c) {
+    const int64_t col = ((int64_t)c * XR_T + threadIdx.x) * 4;
+    if (col >= V) continue;
+    float o[4];
+#pragma unroll
+    for (int k = 0; k < 4; ++k) o[k] = dr * ((col + k == lab ? 1.f : 0.f) - v[c][k] * inv);
+    if (dx) __stcs(reinterpret_cast<float4*>(dx + r * V + col), make_float4(o[0], o[1], o[2], o[3]));
+    if (dxb) {
+      __nv_bfloat162 lo = __floats2bfloat162_rn(o[0], o[1]), hi = __floats2bfloat162_rn(o[2], o[3]);
+      uint2 u;
+      u.x = *reinterpret_cast<uint32_t*>(&lo);
+      u.y = *reinterpret_cast<uint32_t*>(&hi);
+      *reinterpret_cast<uint2*>(dxb + r * V + col) = u;
+    }
+  }
+}
+
 }  // namespace b200
 
 using namespace b200;
 
 extern "C" int b200_logsoftmax_pick(int x_dtype, const void* x, const int64_t* label, const float* d, float* picked,
-                                    float* ls, float* dx, int64_t rows, int64_t cols, void* stream) {
+                                    float* ls, float* dx, void* dx_bf16, int64_t rows, int64_t cols, void* stream) {
   B200_REQUIRE(x && label, "logsoftmax_pick: null input");
-  B200_REQUIRE(!dx || d, "logsoftmax_pick: dx needs the cotangent d");
+  B200_REQUIRE(!(dx || dx_bf16) || d, "logsoftmax_pick: dx needs the cotangent d");
   B200_REQUIRE(rows >= 0 && cols >= 1 && rows <= 2147483647LL, "logsoftmax_pick: bad sizes");
   if (rows == 0) return B200_OK;
   cudaStream_t s = as_stream(stream);
+  auto al = [](const void* p, int b) { return (reinterpret_cast<uintptr_t>(p) % b) == 0; };
+  const bool reg = x_dtype == B200_F32 && !ls && cols % 4 == 0 && cols <= (int64_t)XR_T * 64 && al(x, 16) &&
+                   (!dx || al(dx, 16)) && (!dx_bf16 || al(dx_bf16, 8));
+  if (reg) {
+    const int vpt = (int)ceil_div(ceil_div(cols, (int64_t)XR_T), (int64_t)4) * 4;
+    auto* db = reinterpret_cast<__nv_bfloat16*>(dx_bf16);
+    const float* xf = (const float*)x;
+    if (vpt <= 4) xent_reg_kernel<4><<<(unsigned)rows, XR_T, 0, s>>>(xf, label, d, picked, dx, db, cols);
+    else if (vpt <= 8) xent_reg_kernel<8><<<(unsigned)rows, XR_T, 0, s>>>(xf, label, d, picked, dx, db, cols);
+    else if (vpt <= 16) xent_reg_kernel<16><<<(unsigned)rows, XR_T, 0, s>>>(xf, label, d, picked, dx, db, cols);
+    else if (vpt <= 32) xent_reg_kernel<32><<<(unsigned)rows, XR_T, 0, s>>>(xf, label, d, picked, dx, db, cols);
+    else xent_reg_kernel<64><<<(unsigned)rows, XR_T, 0, s>>>(xf, label, d, picked, dx, db, cols);
+    return check_launch("logsoftmax_pick(rows in registers)");
+  }
+  B200_REQUIRE(!dx_bf16, "logsoftmax_pick: bf16 dx needs fp32 logits with cols %% 4 == 0");
   if (x_dtype == B200_F32)
     xent_kernel<float><<<(unsigned)rows, XE_T, 0, s>>>((const float*)x, label, d, picked, ls, dx, cols);
   else if (x_dtype == B200_BF16)

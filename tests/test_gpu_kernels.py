@@ -293,7 +293,7 @@ def test_logsoftmax_pick_fwd_bwd(R, V):
     dx = torch.empty(R, V, device="cuda")
     lsd = torch.empty(R, V, device="cuda")
     L.call("b200_logsoftmax_pick", L.F32, X.data_ptr(), LB.data_ptr(), D.data_ptr(), picked.data_ptr(), lsd.data_ptr(),
-           dx.data_ptr(), R, V, ops.stream_ptr())
+           dx.data_ptr(), None, R, V, ops.stream_ptr())
     np.testing.assert_allclose(to_np(picked), picked_ref, rtol=1e-5, atol=1e-5)
     np.testing.assert_allclose(to_np(lsd), ls, rtol=1e-5, atol=1e-5)
     np.testing.assert_allclose(to_np(dx), dx_ref, rtol=1e-4, atol=1e-6)
@@ -577,3 +577,54 @@ def test_elementwise_flat_modes_dtypes(shape):
     ref = np.tanh(x * y + rowv)
     np.testing.assert_allclose(to_np(out[0]), ref, rtol=1e-5, atol=1e-6)
     np.testing.assert_allclose(to_np(out[1].float()), ref, rtol=1e-2, atol=1e-2)
+
+
+@pytest.mark.parametrize("R,V", [(33, 32000), (17, 1000), (9, 4096), (5, 12)])
+def test_logsoftmax_pick_register_rows_bf16_dx(R, V):
+    from b200 import _lib as L
+    from b200 import ops
+
+    r = rng(R * V)
+    x = (r.standard_normal((R, V)) * 3).astype(np.float32)
+    lab = r.integers(0, V, (R, 1)).astype(np.int64)
+    d = r.standard_normal((R, 1)).astype(np.float32)
+    x64 = x.astype(np.float64)
+    lse = np.log(np.exp(x64 - x64.max(-1, keepdims=True)).sum(-1, keepdims=True)) + x64.max(-1, keepdims=True)
+    sm = np.exp(x64 - lse)
+    onehot = np.zeros_like(sm)
+    onehot[np.arange(R), lab[:, 0]] = 1
+    dx_ref = d * (onehot - sm)
+    picked_ref = np.take_along_axis(x64 - lse, lab, -1)
+    X, LB, D = T(x), T(lab), T(d)
+    picked = torch.empty(R, 1, device=X.device)
+    dx = torch.empty(R, V, device=X.device)
+    dxb = torch.empty(R, V, dtype=torch.bfloat16, device=X.device)
+    L.call("b200_logsoftmax_pick", L.F32, X.data_ptr(), LB.data_ptr(), D.data_ptr(), picked.data_ptr(), None,
+           dx.data_ptr(), dxb.data_ptr(), R, V, ops.stream_ptr())
+    torch.cuda.synchronize()
+    np.testing.assert_allclose(to_np(picked), picked_ref, rtol=1e-5, atol=1e-5)
+    np.testing.assert_allclose(to_np(dx), dx_ref, rtol=1e-4, atol=1e-6)
+    np.testing.assert_allclose(to_np(dxb.float()), dx_ref, rtol=1e-2, atol=1e-3)
+
+
+@pytest.mark.parametrize("R,C", [(300, 1024), (77, 512), (9, 96), (5, 1000), (3, 4096)])
+def test_layernorm_bwd_rows_fused_matches_oracle(R, C):
+    from b200 import _lib as L
+    from oracle import evaluator as O
+
+    r = rng(R + C)
+    x = (r.standard_normal((R, C)) * 2 + 0.5).astype(np.float32)
+    dy = r.standard_normal((R, C)).astype(np.float32)
+    g = r.uniform(0.5, 1.5, C).astype(np.float32)
+    X, DY, G = T(x), T(dy), T(g)
+    dx = torch.empty_like(X)
+    dg = torch.empty(C, device=X.device)
+    db = torch.empty(C, device=X.device)
+    n = int(L.lib().b200_layernorm_bwd_workspace_bytes(R, C))
+    ws = torch.empty(max(n, 1), dtype=torch.uint8, device=X.device)
+    L.call("b200_layernorm_bwd_rows", DY.data_ptr(), X.data_ptr(), G.data_ptr(), dx.data_ptr(), None, dg.data_ptr(),
+           db.data_ptr(), R, C, 1e-5, ws.data_ptr(), n, 0)
+    torch.cuda.synchronize()
+    np.testing.assert_allclose(to_np(dx), O.execute_op("LayerNormInputGrad", dy, x, g, eps=1e-5), rtol=1e-4, atol=1e-5)
+    np.testing.assert_allclose(to_np(dg), O.execute_op("LayerNormGammaGrad", dy, x, eps=1e-5), rtol=1e-4, atol=1e-3)
+    np.testing.assert_allclose(to_np(db), O.execute_op("LayerNormBetaGrad", dy), rtol=1e-4, atol=1e-3)
