@@ -260,6 +260,21 @@ int b200_rowfused_fwd_bwd(const float* x, const float* a, const float* b, const 
                           float* dbeta, int64_t rows, int64_t cols, float eps, void* workspace, size_t workspace_bytes,
                           void* stream);
 
+/* b200_rowfused_fwd_bwd without a workspace argument, for callers that cannot allocate
+ * device memory per call: a serving process that reserves its whole HBM budget at
+ * start-up and forbids later allocations, or a C/C++ host that links only this library
+ * and has no device allocator of its own. No counterpart in the reference: its numpy
+ * path has no device memory to manage. The column-partial scratch lives in a static
+ * 16 MiB device array inside libb200.so (held by every GPU that loads the library), so
+ * sizes whose b200_rowfused_workspace_bytes exceeds 16 MiB are rejected with
+ * B200_ERR_ARG (use b200_rowfused_fwd_bwd then). The first call on each device looks up
+ * the array's device address (set-up, no allocation); make that first call before any
+ * stream capture. Nothing must be zeroed beforehand. Calls that overlap on the GPU share
+ * the array and race: serialise them. Outputs as b200_rowfused_fwd_bwd. */
+int b200_rowfused_fwd_bwd_noalloc(const float* x, const float* a, const float* b, const float* gamma, const float* beta,
+                                  const float* cot, float* y, int64_t* am, float* dx, float* da, float* db, float* dgamma,
+                                  float* dbeta, int64_t rows, int64_t cols, float eps, void* stream);
+
 /* ReLU-with-bias backward in one pass: gp = g * mask (Multiply(cot, Greater(pre, 0)),
  * the Relu VJP of transforms/autodiff_rules/vjp_rules.yaml:25-27 evaluated by
  * numpy/eager/math_binary.py:39-51) and dbias = column sums of gp (BroadcastReduce,

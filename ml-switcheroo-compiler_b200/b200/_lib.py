@@ -94,6 +94,7 @@ SIGNATURES = {
         [_I32, _I32, _P, _P, _P] + [_I64] * 16 + [_F32, _P, _I32, _P, _P, _P],
         C.c_int,
     ),
+    "b200_rowfused_fwd_bwd_noalloc": ([_P] * 13 + [_I64, _I64, _F32, _P], C.c_int),
     "b200_rowfused_workspace_bytes": ([_I64, _I64], C.c_size_t),
     "b200_rowfused_fwd_bwd": ([_P] * 13 + [_I64, _I64, _F32, _P, C.c_size_t, _P], C.c_int),
     "b200_mask_mul_colsum_workspace_bytes": ([_I64, _I64], C.c_size_t),

@@ -1,0 +1,61 @@
+"""The allocation-free variant of the fused row kernel, for callers that cannot allocate
+device memory per call (its scratch is a static device array in the library), checked
+against the workspace entry point: same outputs on two calls in a row with different
+inputs, and sizes beyond the static scratch rejected before anything runs."""
+
+import numpy as np
+import pytest
+import torch
+
+pytestmark = pytest.mark.gpu
+
+
+def _inputs(R, C, seed):
+    r = np.random.default_rng(seed)
+    f32 = np.float32
+    host = [r.standard_normal((R, C), dtype=f32), r.uniform(0.5, 1.5, C).astype(f32), (r.standard_normal(C) * 0.1).astype(f32),
+            r.uniform(0.5, 1.5, C).astype(f32), (r.standard_normal(C) * 0.1).astype(f32), r.standard_normal((R, C), dtype=f32)]
+    return [torch.from_numpy(a).cuda() for a in host]
+
+
+def _outputs(R, C):
+    dev = torch.device("cuda")
+    return (torch.empty(R, C, device=dev), torch.empty(R, dtype=torch.int64, device=dev), torch.empty(R, C, device=dev),
+            *[torch.empty(C, device=dev) for _ in range(4)])
+
+
+def _ptrs(ts):
+    return [t.data_ptr() for t in ts]
+
+
+@pytest.mark.parametrize("R,C", [(512, 4096), (8192, 4096), (37, 1000)])
+def test_rowfused_noalloc_matches_workspace_entry_point(cuda, R, C):
+    from b200 import _lib as L
+
+    need = int(L.lib().b200_rowfused_workspace_bytes(R, C))
+    assert need <= 16 << 20
+    for call, seed in enumerate((3, 4)):  # two calls in a row, different inputs
+        ins = _inputs(R, C, seed)
+        ref = _outputs(R, C)
+        ws = torch.empty(max(need, 1), dtype=torch.uint8, device="cuda")
+        L.call("b200_rowfused_fwd_bwd", *_ptrs(ins), *_ptrs(ref), R, C, 1e-5, ws.data_ptr(), need, 0)
+        got = _outputs(R, C)
+        L.call("b200_rowfused_fwd_bwd_noalloc", *_ptrs(ins), *_ptrs(got), R, C, 1e-5, 0)
+        torch.cuda.synchronize()
+        for name, a, b in zip(("y", "argmax", "dx", "da", "db", "dgamma", "dbeta"), got, ref):
+            if a.dtype == torch.int64:
+                assert torch.equal(a, b), (call, name)
+            else:
+                np.testing.assert_allclose(a.cpu().numpy(), b.cpu().numpy(), rtol=1e-4, atol=1e-6, err_msg=f"{call}:{name}")
+
+
+def test_rowfused_noalloc_rejects_sizes_above_its_scratch(cuda):
+    from b200 import _lib as L
+
+    R, C = 65536, 16384
+    assert int(L.lib().b200_rowfused_workspace_bytes(R, C)) > 16 << 20
+    dummy = torch.empty(16, device="cuda")
+    p = dummy.data_ptr()  # never dereferenced: the size check comes first
+    with pytest.raises(ValueError) as ei:
+        L.call("b200_rowfused_fwd_bwd_noalloc", *([p] * 13), R, C, 1e-5, 0)
+    assert "static maximum" in str(ei.value)
