@@ -345,8 +345,7 @@ def run_gpu(args) -> None:
             dv = {k: v.to(dev, non_blocking=True) for k, v in host.items()}
             o = fn(dv)
             if dist is not None:
-                for gid in grad_ids:
-                    dist.all_reduce(o[gid], op=dist.ReduceOp.AVG if scale_grads else dist.ReduceOp.SUM)
+                sync([o[gid] for gid in grad_ids])
             for k in res_ids:
                 host_out[k].copy_(o[k], non_blocking=True)
 

@@ -125,7 +125,11 @@ int b200_ew_run(const b200_ew_program* prog, const void* const* inputs, void* co
 /* ReduceSum/ReduceMean/ReduceMax (eager/core_math_ops/math_reduction.py:37,57,97) and
  * BroadcastReduce (math_reduction.py:192-224) as one or more middle-axis passes.
  * x: [outer, red, inner] of in_dtype (F32/BF16), y: [outer, inner] F32. */
-int b200_reduce(int in_dtype, const void* x, float* y, int64_t outer, int64_t red, int64_t inner, int op, void* stream);
+int b200_reduce(int in_dtype, const void* x, float* y, int64_t outer, int64_t red, int64_t inner, int op, void* workspace,
+                size_t workspace_bytes, void* stream);
+/* Scratch for b200_reduce: partial sums when `red` is split across CTAs (combined in a
+ * fixed order). With less workspace than this the reduction runs unsplit (same result). */
+size_t b200_reduce_workspace_bytes(int64_t outer, int64_t red, int64_t inner);
 
 /* Argmax (numpy/eager/math_reductions.py:129-140): first maximum wins, int64 out. */
 int b200_argmax(int in_dtype, const void* x, int64_t* idx, int64_t outer, int64_t red, int64_t inner, void* stream);
@@ -163,9 +167,11 @@ int b200_layernorm_input_grad(const float* dy, const float* x, const float* gamm
                               int64_t cols, float eps, void* stream);
 
 /* LayerNormGammaGrad / LayerNormBetaGrad (numpy/eager/nn_ops.py:276-318): column sums of
- * dy * x_hat and of dy over all rows. Either output may be NULL. */
+ * dy * x_hat and of dy over all rows, through per-CTA partials added in a fixed order.
+ * Either output may be NULL. workspace >= b200_layernorm_param_grad_workspace_bytes. */
+size_t b200_layernorm_param_grad_workspace_bytes(int64_t rows, int64_t cols);
 int b200_layernorm_param_grad(const float* dy, const float* x, float* dgamma, float* dbeta, int64_t rows,
-                              int64_t cols, float eps, void* stream);
+                              int64_t cols, float eps, void* workspace, size_t workspace_bytes, void* stream);
 
 /* ------------------------------------------------------------------------------
  * Indexing
@@ -186,7 +192,10 @@ int b200_take_rows(int dtype, const void* table, const int64_t* ids, void* y, in
 /* TensorScatterAdd of rows (numpy/eager/math_scatter.py:39-60 with [n,1] indices):
  * y [V, D] (+)= src[n, D] at rows ids[n]; accumulate != 0 keeps y, else y starts at 0. */
 int b200_scatter_add_rows(const float* src, const int64_t* ids, float* y, int64_t n, int64_t V, int64_t D,
-                          int accumulate, void* stream);
+                          int accumulate, void* workspace, size_t workspace_bytes, void* stream);
+/* Scratch for b200_scatter_add_rows: a stable bucketing of the positions by row id, so
+ * each output row adds its source rows in position order (deterministic). */
+size_t b200_scatter_add_rows_workspace_bytes(int64_t n, int64_t V);
 
 /* device-side error flag (out-of-range index, timed-out wait): returns B200_OK or the
  * recorded code after synchronising `stream`, and clears the flag. */

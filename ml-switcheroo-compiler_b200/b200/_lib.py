@@ -68,7 +68,8 @@ SIGNATURES = {
     "b200_launch_count": ([], C.c_uint64),
     "b200_check_device_error": ([_P], C.c_int),
     "b200_ew_run": ([C.POINTER(EwProgram), C.POINTER(_P), C.POINTER(_P), _P], C.c_int),
-    "b200_reduce": ([_I32, _P, _P, _I64, _I64, _I64, _I32, _P], C.c_int),
+    "b200_reduce": ([_I32, _P, _P, _I64, _I64, _I64, _I32, _P, C.c_size_t, _P], C.c_int),
+    "b200_reduce_workspace_bytes": ([_I64, _I64, _I64], C.c_size_t),
     "b200_argmax": ([_I32, _P, _P, _I64, _I64, _I64, _P], C.c_int),
     "b200_softmax": ([_P, _P, _I64, _I64, _I32, _P], C.c_int),
     "b200_gelu_bwd_colsum_workspace_bytes": ([_I64, _I64], C.c_size_t),
@@ -81,11 +82,13 @@ SIGNATURES = {
     "b200_softmax_bwd_rows": ([_P, _P, _P, _P, _P, _I64, _I64, _P], C.c_int),
     "b200_layernorm": ([_P, _P, _P, _P, _I64, _I64, _F32, _P], C.c_int),
     "b200_layernorm_input_grad": ([_P, _P, _P, _P, _I64, _I64, _F32, _P], C.c_int),
-    "b200_layernorm_param_grad": ([_P, _P, _P, _P, _I64, _I64, _F32, _P], C.c_int),
+    "b200_layernorm_param_grad": ([_P, _P, _P, _P, _I64, _I64, _F32, _P, C.c_size_t, _P], C.c_int),
+    "b200_layernorm_param_grad_workspace_bytes": ([_I64, _I64], C.c_size_t),
     "b200_take_along_last": ([_P, _P, _P, _I64, _I64, _I64, _P], C.c_int),
     "b200_scatter_add_last": ([_P, _P, _P, _P, _I64, _I64, _I64, _P], C.c_int),
     "b200_take_rows": ([_I32, _P, _P, _P, _I64, _I64, _I64, _P], C.c_int),
-    "b200_scatter_add_rows": ([_P, _P, _P, _I64, _I64, _I64, _I32, _P], C.c_int),
+    "b200_scatter_add_rows": ([_P, _P, _P, _I64, _I64, _I64, _I32, _P, C.c_size_t, _P], C.c_int),
+    "b200_scatter_add_rows_workspace_bytes": ([_I64, _I64], C.c_size_t),
     "b200_gemm": (
         [_I32, _I32, _P, _P, _P, _I64, _I64, _I64, _I64, _I64, _I64, _I64, _I64, _I64, _I64, _I64, _I64, _F32, _P, _I32, _P, _P],
         C.c_int,

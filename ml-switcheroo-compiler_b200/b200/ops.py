@@ -58,6 +58,11 @@ def _ptr(t: torch.Tensor | None) -> int | None:
     return None if t is None else t.data_ptr()
 
 
+def workspace(nbytes: int) -> torch.Tensor | None:
+    """Device scratch of `nbytes` for an entry point that takes a workspace (None if 0)."""
+    return torch.empty(int(nbytes), dtype=torch.uint8, device=device()) if nbytes > 0 else None
+
+
 def to_device(x: Any, dtype: torch.dtype | None = None) -> torch.Tensor:
     """Host value (numpy array, scalar, tensor) -> CUDA tensor (a copy, no compute)."""
     if isinstance(x, torch.Tensor):
@@ -434,7 +439,9 @@ def reduce(x: torch.Tensor, axis, keepdims: bool, op: int) -> torch.Tensor:
         red = math.prod(shape[axes[0] : axes[-1] + 1])
         inner = math.prod(shape[axes[-1] + 1 :])
         y = torch.empty(outer * inner, dtype=torch.float32, device=device())
-        L.call("b200_reduce", code(xc), xc.data_ptr(), y.data_ptr(), outer, red, inner, op, stream_ptr())
+        wn = int(L.lib().b200_reduce_workspace_bytes(outer, red, inner))
+        ws = workspace(wn)
+        L.call("b200_reduce", code(xc), xc.data_ptr(), y.data_ptr(), outer, red, inner, op, _ptr(ws), wn, stream_ptr())
         out_shape = [1 if i in axes else s for i, s in enumerate(shape)] if keepdims else [s for i, s in enumerate(shape) if i not in axes]
         return y.view(out_shape)
     # otherwise one axis at a time, last first (mean = sum / count at the end)
@@ -565,7 +572,10 @@ def _ln_param(dy, x, eps, axis, which):
     out = torch.empty(cols, dtype=torch.float32, device=device())
     dg = out if which == "gamma" else None
     db = out if which == "beta" else None
-    L.call("b200_layernorm_param_grad", dyc.data_ptr(), xc.data_ptr(), _ptr(dg), _ptr(db), rows, cols, float(eps), stream_ptr())
+    wn = int(L.lib().b200_layernorm_param_grad_workspace_bytes(rows, cols))
+    ws = workspace(wn)
+    L.call("b200_layernorm_param_grad", dyc.data_ptr(), xc.data_ptr(), _ptr(dg), _ptr(db), rows, cols, float(eps), _ptr(ws), wn,
+           stream_ptr())
     return out
 
 
@@ -631,7 +641,10 @@ def op_tensor_scatter_add(tensor, indices, updates, **_):  # numpy/eager/math_sc
     D = y.numel() // max(1, V)
     uc = contiguous(cast(updates, torch.float32))
     ic = contiguous(indices)
-    L.call("b200_scatter_add_rows", uc.data_ptr(), ic.data_ptr(), y.data_ptr(), ic.shape[0], V, D, 1, stream_ptr())
+    wn = int(L.lib().b200_scatter_add_rows_workspace_bytes(ic.shape[0], V))
+    ws = workspace(wn)
+    L.call("b200_scatter_add_rows", uc.data_ptr(), ic.data_ptr(), y.data_ptr(), ic.shape[0], V, D, 1, _ptr(ws), wn,
+           stream_ptr())
     return y
 
 
@@ -822,7 +835,8 @@ def _gemm_split_k(A: torch.Tensor, B: torch.Tensor, S: int, out_dtype: torch.dty
            Kc * A.stride(1), A.stride(0), A.stride(1), 0, Kc * B.stride(0), B.stride(0), B.stride(1), 0, M * N, N, 1.0, None,
            L.EPI_NONE, None, None, stream_ptr())
     C_ = torch.empty(M, N, dtype=torch.float32, device=device())
-    L.call("b200_reduce", code(part), part.data_ptr(), C_.data_ptr(), 1, S, M * N, L.RED_SUM, stream_ptr())
+    # S chunks summed in order (M N columns fill the GPU: no further split)
+    L.call("b200_reduce", code(part), part.data_ptr(), C_.data_ptr(), 1, S, M * N, L.RED_SUM, None, 0, stream_ptr())
     return C_ if out_dtype == torch.float32 else cast(C_, out_dtype)
 
 

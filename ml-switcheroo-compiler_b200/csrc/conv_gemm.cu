@@ -43,77 +43,104 @@ __global__ void pack_weight_kernel(const float* __restrict__ w, __nv_bfloat16* _
   }
 }
 
-__device__ __forceinline__ float x_at(const float* __restrict__ x, const Dims& d, int64_t n, int64_t k, int64_t p) {
-  if (k >= d.K() || p >= d.P()) return 0.f;
-  const int64_t c = k / (d.KH * d.KW), i = (k / d.KW) % d.KH, j = k % d.KW;
-  const int64_t oh = p / d.OW, ow = p % d.OW;
-  const int64_t h = oh * d.sh - d.pt + i, w = ow * d.sw - d.pl + j;
-  if (h < 0 || h >= d.H || w < 0 || w >= d.W) return 0.f;
-  return x[((n * d.C + c) * d.H + h) * d.W + w];
+// Staging kernels: blockIdx.y / blockIdx.z pick one tap row k (or output channel) and one
+// image (or split), so the tap decode (c, i, j) is block-uniform; threads run along the
+// contiguous pixel axis with 32-bit divisions only (offsets stay 64-bit).
+struct Tap {
+  int c, i, j;
+};
+__device__ __forceinline__ Tap tap_of(const Dims& d, int k) {
+  const int khw = (int)(d.KH * d.KW);
+  Tap t;
+  t.c = k / khw;
+  const int r = k - t.c * khw;
+  t.i = r / (int)d.KW;
+  t.j = r - t.i * (int)d.KW;
+  return t;
+}
+__device__ __forceinline__ float x_tap(const float* __restrict__ x, const Dims& d, int n, const Tap& t, int p) {
+  const int OW = (int)d.OW;
+  const int oh = p / OW, ow = p - oh * OW;
+  const int h = oh * (int)d.sh - (int)d.pt + t.i, w = ow * (int)d.sw - (int)d.pl + t.j;
+  if (h < 0 || h >= (int)d.H || w < 0 || w >= (int)d.W) return 0.f;
+  return __ldg(x + ((((int64_t)n * d.C + t.c) * d.H + h) * d.W + w));
 }
 
 // x -> col bf16 [N, Kp, Pp]   (fwd operand: rows are taps, contiguous pixels)
-__global__ void im2col_kp_kernel(const float* __restrict__ x, __nv_bfloat16* __restrict__ col, Dims d) {
-  const int64_t Kp = d.Kp(), Pp = d.Pp(), total = d.N * Kp * Pp;
-  for (int64_t e = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; e < total; e += (int64_t)gridDim.x * blockDim.x) {
-    const int64_t p = e % Pp, k = (e / Pp) % Kp, n = e / (Pp * Kp);
-    col[e] = bf(x_at(x, d, n, k, p));
-  }
+// grid (ceil(Pp / 256), Kp, N)
+__global__ void __launch_bounds__(256) im2col_kp_kernel(const float* __restrict__ x, __nv_bfloat16* __restrict__ col, Dims d) {
+  const int p = blockIdx.x * 256 + threadIdx.x, k = blockIdx.y, n = blockIdx.z;
+  const int Pp = (int)d.Pp();
+  if (p >= Pp) return;
+  float v = 0.f;
+  if (k < (int)d.K() && p < (int)d.P()) v = x_tap(x, d, n, tap_of(d, k), p);
+  col[((int64_t)n * d.Kp() + k) * Pp + p] = bf(v);
 }
 
-// x -> colT bf16 [Q, Kp], row q = n * Pp + p, Q >= N * Pp (zero rows past the data)
-__global__ void im2col_pk_kernel(const float* __restrict__ x, __nv_bfloat16* __restrict__ colT, Dims d, int64_t Q) {
-  const int64_t Kp = d.Kp(), Pp = d.Pp(), total = Q * Kp;
-  for (int64_t e = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; e < total; e += (int64_t)gridDim.x * blockDim.x) {
-    const int64_t k = e % Kp, q = e / Kp;
-    const int64_t n = q / Pp, p = q % Pp;
-    colT[e] = bf(n < d.N ? x_at(x, d, n, k, p) : 0.f);
-  }
+// x -> col bf16 [S, Kp, L]: split s holds pixels q = s * L + l, q = n * Pp + p (zero past
+// the data), so each split is a dense K-major weight-gradient operand
+// grid (ceil(L / 256), Kp, S)
+__global__ void __launch_bounds__(256) im2col_kq_kernel(const float* __restrict__ x, __nv_bfloat16* __restrict__ col, Dims d,
+                                                        int64_t L) {
+  const int l = blockIdx.x * 256 + threadIdx.x, k = blockIdx.y, sidx = blockIdx.z;
+  if (l >= L) return;
+  const int64_t q = (int64_t)sidx * L + l;
+  const int Pp = (int)d.Pp();
+  const int n = (int)(q / Pp), p = (int)(q - (int64_t)n * Pp);
+  float v = 0.f;
+  if (n < (int)d.N && k < (int)d.K() && p < (int)d.P()) v = x_tap(x, d, n, tap_of(d, k), p);
+  col[((int64_t)sidx * d.Kp() + k) * L + l] = bf(v);
 }
 
-// dy fp32 [N, O, P] -> bf16 [N, O, Pp]
-__global__ void pack_dy_nop_kernel(const float* __restrict__ dy, __nv_bfloat16* __restrict__ out, Dims d) {
-  const int64_t P = d.P(), Pp = d.Pp(), total = d.N * d.O * Pp;
-  for (int64_t e = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; e < total; e += (int64_t)gridDim.x * blockDim.x) {
-    const int64_t p = e % Pp, no = e / Pp;
-    out[e] = bf(p < P ? dy[no * P + p] : 0.f);
-  }
+// dy fp32 [N, O, P] -> bf16 [N, O, Pp]; grid (ceil(Pp / 256), O, N)
+__global__ void __launch_bounds__(256) pack_dy_nop_kernel(const float* __restrict__ dy, __nv_bfloat16* __restrict__ out, Dims d) {
+  const int p = blockIdx.x * 256 + threadIdx.x, o = blockIdx.y, n = blockIdx.z;
+  const int P = (int)d.P(), Pp = (int)d.Pp();
+  if (p >= Pp) return;
+  const int64_t no = (int64_t)n * d.O + o;
+  out[no * Pp + p] = bf(p < P ? __ldg(dy + no * P + p) : 0.f);
 }
 
 // dy fp32 [N, O, P] -> bf16 [S, O, L]: split s holds columns q = s * L + l, q = n * Pp + p
 // (zero past the data), so each split is a dense [O, L] K-major GEMM operand
-__global__ void pack_dy_sol_kernel(const float* __restrict__ dy, __nv_bfloat16* __restrict__ out, Dims d, int64_t S, int64_t L) {
-  const int64_t P = d.P(), Pp = d.Pp(), total = S * d.O * L;
-  for (int64_t e = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; e < total; e += (int64_t)gridDim.x * blockDim.x) {
-    const int64_t l = e % L, o = (e / L) % d.O, sidx = e / (L * d.O);
-    const int64_t q = sidx * L + l;
-    const int64_t n = q / Pp, p = q % Pp;
-    out[e] = bf((n < d.N && p < P) ? dy[(n * d.O + o) * P + p] : 0.f);
-  }
+// grid (ceil(L / 256), O, S)
+__global__ void __launch_bounds__(256) pack_dy_sol_kernel(const float* __restrict__ dy, __nv_bfloat16* __restrict__ out, Dims d,
+                                                          int64_t L) {
+  const int l = blockIdx.x * 256 + threadIdx.x, o = blockIdx.y, sidx = blockIdx.z;
+  if (l >= L) return;
+  const int64_t q = (int64_t)sidx * L + l;
+  const int P = (int)d.P(), Pp = (int)d.Pp();
+  const int n = (int)(q / Pp), p = (int)(q - (int64_t)n * Pp);
+  const float v = (n < (int)d.N && p < P) ? __ldg(dy + ((int64_t)n * d.O + o) * P + p) : 0.f;
+  out[((int64_t)sidx * d.O + o) * L + l] = bf(v);
 }
 
 // dxcol fp32 [N, Kp, P] -> dx [N, C, H, W]: every input pixel gathers the taps that read it
-__global__ void col2im_kernel(const float* __restrict__ dxcol, float* __restrict__ dx, Dims d) {
-  const int64_t total = d.N * d.C * d.H * d.W, Kp = d.Kp(), P = d.P();
-  for (int64_t e = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; e < total; e += (int64_t)gridDim.x * blockDim.x) {
-    const int64_t w = e % d.W, h = (e / d.W) % d.H, c = (e / (d.W * d.H)) % d.C, n = e / (d.W * d.H * d.C);
-    float acc = 0.f;
-    for (int64_t i = 0; i < d.KH; ++i) {
-      const int64_t th = h + d.pt - i;
-      if (th < 0 || th % d.sh) continue;
-      const int64_t oh = th / d.sh;
-      if (oh >= d.OH) continue;
-      for (int64_t j = 0; j < d.KW; ++j) {
-        const int64_t tw = w + d.pl - j;
-        if (tw < 0 || tw % d.sw) continue;
-        const int64_t ow = tw / d.sw;
-        if (ow >= d.OW) continue;
-        const int64_t k = (c * d.KH + i) * d.KW + j;
-        acc += dxcol[(n * Kp + k) * P + oh * d.OW + ow];
-      }
+// grid (ceil(H W / 256), C, N)
+__global__ void __launch_bounds__(256) col2im_kernel(const float* __restrict__ dxcol, float* __restrict__ dx, Dims d) {
+  const int hw = blockIdx.x * 256 + threadIdx.x, c = blockIdx.y, n = blockIdx.z;
+  const int H = (int)d.H, W = (int)d.W;
+  if (hw >= H * W) return;
+  const int h = hw / W, w = hw - h * W;
+  const int KH = (int)d.KH, KW = (int)d.KW, sh = (int)d.sh, sw = (int)d.sw, OH = (int)d.OH, OW = (int)d.OW;
+  const int P = OH * OW;
+  const float* base = dxcol + ((int64_t)n * d.Kp()) * P;
+  float acc = 0.f;
+  for (int i = 0; i < KH; ++i) {
+    const int th = h + (int)d.pt - i;
+    if (th < 0) break;  // th only decreases as i grows
+    const int oh = th / sh;
+    if (oh * sh != th || oh >= OH) continue;
+    for (int j = 0; j < KW; ++j) {
+      const int tw = w + (int)d.pl - j;
+      if (tw < 0) break;
+      const int ow = tw / sw;
+      if (ow * sw != tw || ow >= OW) continue;
+      const int k = (c * KH + i) * KW + j;
+      acc += __ldg(base + (int64_t)k * P + oh * OW + ow);
     }
-    dx[e] = acc;
   }
+  dx[(((int64_t)n * d.C + c) * H) * W + hw] = acc;
 }
 
 // partials [S, O, Kp] -> dw [O, K] (sum over S in order, drop the K padding)
@@ -144,7 +171,7 @@ inline size_t ws_bytes(int op, const Dims& d) {
   int64_t S, L;
   wgrad_split(d, S, L);
   const int64_t Q = S * L;
-  return al256((size_t)d.O * Q * 2) + al256((size_t)Q * Kp * 2) + al256((size_t)S * d.O * Kp * 4);
+  return al256((size_t)d.O * Q * 2) + al256((size_t)S * Kp * L * 2) + al256((size_t)S * d.O * Kp * 4);
 }
 
 inline int check(const void* a, const void* b, const void* c, const Dims& d) {
@@ -186,7 +213,8 @@ extern "C" int b200_conv2d_fwd_tc(const float* x, const float* w, float* y, int6
   auto* col = reinterpret_cast<__nv_bfloat16*>(reinterpret_cast<uint8_t*>(ws) + al256((size_t)O * Kp * 2));
   pack_weight_kernel<<<grid_of(O * Kp), 256, 0, s>>>(w, wp, O, d.K(), Kp);
   if ((rc = check_launch("conv2d_fwd_tc(pack w)"))) return rc;
-  im2col_kp_kernel<<<grid_of(N * Kp * Pp), 256, 0, s>>>(x, col, d);
+  B200_REQUIRE(Kp <= 65535 && N <= 65535, "conv2d_fwd_tc: too many taps or images");
+  im2col_kp_kernel<<<dim3((unsigned)ceil_div(Pp, (int64_t)256), (unsigned)Kp, (unsigned)N), 256, 0, s>>>(x, col, d);
   if ((rc = check_launch("conv2d_fwd_tc(im2col)"))) return rc;
   // Y_n [O, P] = Wp [O, Kp] (shared) . Xcol_n [Kp, Pp]
   return gemm_bf16_tcgen05(B200_F32, wp, col, y, N, O, P, Kp, 0, Kp, 1, Kp * Pp, Pp, 1, O * P, P, 1.f, nullptr,
@@ -211,13 +239,14 @@ extern "C" int b200_conv2d_dgrad_tc(const float* dy, const float* w, float* dx, 
   auto* dxcol = reinterpret_cast<float*>(base);
   pack_weight_kernel<<<grid_of(O * Kp), 256, 0, s>>>(w, wp, O, d.K(), Kp);
   if ((rc = check_launch("conv2d_dgrad_tc(pack w)"))) return rc;
-  pack_dy_nop_kernel<<<grid_of(N * O * Pp), 256, 0, s>>>(dy, dyp, d);
+  B200_REQUIRE(O <= 65535 && N <= 65535 && C <= 65535, "conv2d_dgrad_tc: too many channels or images");
+  pack_dy_nop_kernel<<<dim3((unsigned)ceil_div(Pp, (int64_t)256), (unsigned)O, (unsigned)N), 256, 0, s>>>(dy, dyp, d);
   if ((rc = check_launch("conv2d_dgrad_tc(pack dy)"))) return rc;
   // dXcol_n [Kp, P] = Wp^T [Kp, O] (shared, MN-major) . dY_n [O, Pp]
   rc = gemm_bf16_tcgen05(B200_F32, wp, dyp, dxcol, N, Kp, P, O, 0, 1, Kp, O * Pp, Pp, 1, Kp * P, P, 1.f, nullptr, B200_EPI_NONE,
                          nullptr, s);
   if (rc) return rc;
-  col2im_kernel<<<grid_of(N * C * H * W), 256, 0, s>>>(dxcol, dx, d);
+  col2im_kernel<<<dim3((unsigned)ceil_div(H * W, (int64_t)256), (unsigned)C, (unsigned)N), 256, 0, s>>>(dxcol, dx, d);
   return check_launch("conv2d_dgrad_tc(col2im)");
 }
 
@@ -240,15 +269,17 @@ extern "C" int b200_conv2d_wgrad_tc(const float* x, const float* dy, float* dw, 
   uint8_t* base = reinterpret_cast<uint8_t*>(ws);
   auto* dyt = reinterpret_cast<__nv_bfloat16*>(base);
   base += al256((size_t)O * Q * 2);
-  auto* colT = reinterpret_cast<__nv_bfloat16*>(base);
-  base += al256((size_t)Q * Kp * 2);
+  auto* col = reinterpret_cast<__nv_bfloat16*>(base);
+  base += al256((size_t)S * Kp * L * 2);
   auto* part = reinterpret_cast<float*>(base);
-  pack_dy_sol_kernel<<<grid_of(O * Q), 256, 0, s>>>(dy, dyt, d, S, L);
+  B200_REQUIRE(O <= 65535 && Kp <= 65535 && S <= 65535, "conv2d_wgrad_tc: too many channels or splits");
+  const unsigned gx = (unsigned)ceil_div(L, (int64_t)256);
+  pack_dy_sol_kernel<<<dim3(gx, (unsigned)O, (unsigned)S), 256, 0, s>>>(dy, dyt, d, L);
   if ((rc = check_launch("conv2d_wgrad_tc(pack dy)"))) return rc;
-  im2col_pk_kernel<<<grid_of(Q * Kp), 256, 0, s>>>(x, colT, d, Q);
+  im2col_kq_kernel<<<dim3(gx, (unsigned)Kp, (unsigned)S), 256, 0, s>>>(x, col, d, L);
   if ((rc = check_launch("conv2d_wgrad_tc(im2col)"))) return rc;
-  // partial_s [O, Kp] = dYt_s [O, L] . colT[s L : (s+1) L, :]
-  rc = gemm_bf16_tcgen05(B200_F32, dyt, colT, part, S, O, Kp, L, O * L, L, 1, L * Kp, Kp, 1, O * Kp, Kp, 1.f, nullptr,
+  // partial_s [O, Kp] = dYt_s [O, L] . col_s^T   (col_s [Kp, L]: K-major B operand)
+  rc = gemm_bf16_tcgen05(B200_F32, dyt, col, part, S, O, Kp, L, O * L, L, 1, Kp * L, 1, L, O * Kp, Kp, 1.f, nullptr,
                          B200_EPI_NONE, nullptr, s);
   if (rc) return rc;
   wgrad_sum_kernel<<<grid_of(O * d.K()), 256, 0, s>>>(part, dw, S, O, d.K(), Kp);

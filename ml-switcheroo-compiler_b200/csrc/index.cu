@@ -60,19 +60,103 @@ __global__ void take_rows_kernel(const T* __restrict__ table, const int64_t* __r
   }
 }
 
-__global__ void scatter_add_rows_kernel(const float* __restrict__ src, const int64_t* __restrict__ ids, float* __restrict__ y,
-                                        int64_t n, int64_t V, int64_t D) {
-  for (int64_t e = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; e < n * D; e += (int64_t)gridDim.x * blockDim.x) {
-    const int64_t i = e / D, d = e % D;
-    int64_t v = ids[i];
-    if (v < 0) v += V;
-    if (v < 0 || v >= V) {
-      raise_device_error(B200_ERR_ARG);
-      continue;
-    }
-    atomicAdd(y + v * D + d, src[e]);
+// Deterministic row scatter-add: positions are bucketed by their row id with a stable
+// counting sort (integer atomics only; stable order from in-block ranks), then every
+// output row sums its source rows in increasing position order. Float results therefore
+// do not depend on scheduling, unlike an atomic accumulation.
+constexpr int SA_B = 1024;  // positions per counting block
+
+// ranks / block histogram: rank[i] = earlier positions of block g with the same id,
+// cnt[g][v] = positions of block g with id v (cnt zeroed by the caller)
+__global__ void __launch_bounds__(SA_B) sa_rank_kernel(const int64_t* __restrict__ ids, int* __restrict__ rank,
+                                                       int* __restrict__ cnt, int64_t n, int64_t V) {
+  __shared__ int sid[SA_B];
+  const int64_t i = (int64_t)blockIdx.x * SA_B + threadIdx.x;
+  int v = -1;
+  if (i < n) {
+    int64_t x = ids[i];
+    if (x < 0) x += V;
+    if (x < 0 || x >= V) raise_device_error(B200_ERR_ARG);
+    else v = (int)x;
   }
+  sid[threadIdx.x] = v;
+  __syncthreads();
+  if (v < 0) return;
+  int r = 0, tot = 0;
+  const int lim = (int)min((int64_t)SA_B, n - (int64_t)blockIdx.x * SA_B);
+  for (int j = 0; j < lim; ++j) {
+    const int same = sid[j] == v;
+    tot += same;
+    if (j < (int)threadIdx.x) r += same;
+  }
+  rank[i] = r;
+  if (r == 0) cnt[(int64_t)blockIdx.x * V + v] = tot;
 }
+
+// per row id v: total count, and cnt[g][v] turned into the start of block g's run
+__global__ void sa_colscan_kernel(int* __restrict__ cnt, int* __restrict__ tot, int64_t G, int64_t V) {
+  const int64_t v = blockIdx.x * (int64_t)blockDim.x + threadIdx.x;
+  if (v >= V) return;
+  int run = 0;
+  for (int64_t g = 0; g < G; ++g) {
+    const int c = cnt[g * V + v];
+    cnt[g * V + v] = run;
+    run += c;
+  }
+  tot[v] = run;
+}
+
+// exclusive scan of tot[V] into off[V + 1] (one CTA, chunked)
+__global__ void __launch_bounds__(1024) sa_scan_kernel(const int* __restrict__ tot, int* __restrict__ off, int64_t V) {
+  __shared__ int part[1024];
+  __shared__ int carry;
+  if (threadIdx.x == 0) carry = 0;
+  __syncthreads();
+  for (int64_t base = 0; base < V; base += 1024) {
+    const int64_t v = base + threadIdx.x;
+    const int x = v < V ? tot[v] : 0;
+    part[threadIdx.x] = x;
+    __syncthreads();
+    for (int d = 1; d < 1024; d <<= 1) {  // inclusive Hillis-Steele scan
+      const int y = threadIdx.x >= d ? part[threadIdx.x - d] : 0;
+      __syncthreads();
+      part[threadIdx.x] += y;
+      __syncthreads();
+    }
+    if (v < V) off[v] = carry + part[threadIdx.x] - x;
+    __syncthreads();
+    if (threadIdx.x == 1023) carry += part[1023];
+    __syncthreads();
+  }
+  if (threadIdx.x == 0) off[V] = carry;
+}
+
+__global__ void sa_place_kernel(const int64_t* __restrict__ ids, const int* __restrict__ rank, const int* __restrict__ cnt,
+                                const int* __restrict__ off, int* __restrict__ perm, int64_t n, int64_t V) {
+  const int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x;
+  if (i >= n) return;
+  int64_t x = ids[i];
+  if (x < 0) x += V;
+  if (x < 0 || x >= V) return;
+  const int64_t g = i / SA_B;
+  perm[off[x] + cnt[g * V + x] + rank[i]] = (int)i;
+}
+
+// y[v, :] = (accumulate ? y[v, :] : 0) + sum over v's positions, in position order;
+// block (v, column chunk) = blockIdx.x / dblocks, blockIdx.x % dblocks
+__global__ void __launch_bounds__(256) sa_sum_kernel(const float* __restrict__ src, const int* __restrict__ perm,
+                                                     const int* __restrict__ off, float* __restrict__ y, int64_t D,
+                                                     int64_t dblocks, int accumulate) {
+  const int64_t v = blockIdx.x / dblocks;
+  const int64_t d = (blockIdx.x % dblocks) * 256 + threadIdx.x;
+  if (d >= D) return;
+  const int a = off[v], b = off[v + 1];
+  float acc = accumulate ? y[v * D + d] : 0.f;
+  for (int k = a; k < b; ++k) acc += __ldg(src + (int64_t)perm[k] * D + d);
+  y[v * D + d] = acc;
+}
+
+inline int64_t sa_blocks(int64_t n) { return ceil_div(n, (int64_t)SA_B); }
 
 static unsigned grid_for(int64_t n, int threads) {
   int64_t b = ceil_div(n, threads);
@@ -121,13 +205,50 @@ extern "C" int b200_take_rows(int dt, const void* table, const int64_t* ids, voi
   return check_launch("take_rows");
 }
 
+static size_t sa_al(size_t v) { return (v + 255) & ~size_t(255); }
+
+extern "C" size_t b200_scatter_add_rows_workspace_bytes(int64_t n, int64_t V) {
+  if (n <= 0 || V <= 0) return 0;
+  const size_t G = (size_t)sa_blocks(n);
+  // rank[n], cnt[G][V], tot[V], off[V + 1], perm[n]
+  return sa_al(n * 4) + sa_al(G * V * 4) + sa_al(V * 4) + sa_al((V + 1) * 4) + sa_al(n * 4);
+}
+
 extern "C" int b200_scatter_add_rows(const float* src, const int64_t* ids, float* y, int64_t n, int64_t V, int64_t D,
-                                     int accumulate, void* stream) {
+                                     int accumulate, void* workspace, size_t workspace_bytes, void* stream) {
   B200_REQUIRE(src && ids && y, "scatter_add_rows: null pointer");
   B200_REQUIRE(n >= 0 && V >= 1 && D >= 0, "scatter_add_rows: bad sizes");
+  B200_REQUIRE(n < 2147483647LL && V < 2147483647LL, "scatter_add_rows: too many rows");
+  B200_REQUIRE(V * ceil_div(std::max<int64_t>(D, 1), (int64_t)256) < 2147483647LL, "scatter_add_rows: output too large");
   cudaStream_t s = as_stream(stream);
-  if (!accumulate) cudaMemsetAsync(y, 0, (size_t)V * D * sizeof(float), s);
-  if (n * D == 0) return check_launch("scatter_add_rows(zero)");
-  scatter_add_rows_kernel<<<grid_for(n * D, 256), 256, 0, s>>>(src, ids, y, n, V, D);
-  return check_launch("scatter_add_rows");
+  if (n == 0 || D == 0) {
+    if (!accumulate) cudaMemsetAsync(y, 0, (size_t)V * D * sizeof(float), s);
+    return check_launch("scatter_add_rows(zero)");
+  }
+  const size_t need = b200_scatter_add_rows_workspace_bytes(n, V);
+  B200_REQUIRE(workspace && workspace_bytes >= need, "scatter_add_rows: workspace %zu < %zu", workspace_bytes, need);
+  const int64_t G = sa_blocks(n);
+  uint8_t* w = reinterpret_cast<uint8_t*>(workspace);
+  int* rank = reinterpret_cast<int*>(w);
+  w += sa_al(n * 4);
+  int* cnt = reinterpret_cast<int*>(w);
+  w += sa_al((size_t)G * V * 4);
+  int* tot = reinterpret_cast<int*>(w);
+  w += sa_al(V * 4);
+  int* off = reinterpret_cast<int*>(w);
+  w += sa_al((V + 1) * 4);
+  int* perm = reinterpret_cast<int*>(w);
+  cudaMemsetAsync(cnt, 0, (size_t)G * V * 4, s);
+  sa_rank_kernel<<<(unsigned)G, SA_B, 0, s>>>(ids, rank, cnt, n, V);
+  int rc = check_launch("scatter_add_rows(rank)");
+  if (rc) return rc;
+  sa_colscan_kernel<<<(unsigned)ceil_div(V, (int64_t)256), 256, 0, s>>>(cnt, tot, G, V);
+  if ((rc = check_launch("scatter_add_rows(colscan)"))) return rc;
+  sa_scan_kernel<<<1, 1024, 0, s>>>(tot, off, V);
+  if ((rc = check_launch("scatter_add_rows(scan)"))) return rc;
+  sa_place_kernel<<<(unsigned)ceil_div(n, (int64_t)256), 256, 0, s>>>(ids, rank, cnt, off, perm, n, V);
+  if ((rc = check_launch("scatter_add_rows(place)"))) return rc;
+  const int64_t dblocks = ceil_div(D, (int64_t)256);
+  sa_sum_kernel<<<(unsigned)(V * dblocks), 256, 0, s>>>(src, perm, off, y, D, dblocks, accumulate);
+  return check_launch("scatter_add_rows(sum)");
 }

@@ -17,7 +17,8 @@
 extern "C" int b200_layernorm_input_grad_rows(const float* dy, const float* x, const float* gamma, float* dx, void* dx_bf16,
                                               int64_t rows, int64_t cols, float eps, void* stream);
 extern "C" int b200_layernorm_param_grad(const float* dy, const float* x, float* dgamma, float* dbeta, int64_t rows,
-                                         int64_t cols, float eps, void* stream);
+                                         int64_t cols, float eps, void* workspace, size_t workspace_bytes, void* stream);
+extern "C" size_t b200_layernorm_param_grad_workspace_bytes(int64_t rows, int64_t cols);
 
 namespace b200 {
 namespace lnr {
@@ -389,7 +390,9 @@ extern "C" int b200_layernorm_input_grad_rows(const float* dy, const float* x, c
 
 extern "C" size_t b200_layernorm_bwd_workspace_bytes(int64_t rows, int64_t cols) {
   if (rows <= 0 || cols <= 0) return 0;
-  return (size_t)ln_bwd_grid(rows) * 2 * (size_t)cols * sizeof(float);
+  // the fused kernel's CTA partials, or the separate parameter-gradient kernel's
+  return std::max((size_t)ln_bwd_grid(rows) * 2 * (size_t)cols * sizeof(float),
+                  b200_layernorm_param_grad_workspace_bytes(rows, cols));
 }
 
 extern "C" int b200_layernorm_bwd_rows(const float* dy, const float* x, const float* gamma, float* dx, void* dx_bf16,
@@ -410,7 +413,8 @@ extern "C" int b200_layernorm_bwd_rows(const float* dy, const float* x, const fl
     // general shapes: the separate input-gradient and parameter-gradient kernels
     int rc = B200_OK;
     if (dx || db) rc = b200_layernorm_input_grad_rows(dy, x, gamma, dx, dx_bf16, rows, cols, eps, stream);
-    if (rc == B200_OK && (dgamma || dbeta)) rc = b200_layernorm_param_grad(dy, x, dgamma, dbeta, rows, cols, eps, stream);
+    if (rc == B200_OK && (dgamma || dbeta))
+      rc = b200_layernorm_param_grad(dy, x, dgamma, dbeta, rows, cols, eps, workspace, workspace_bytes, stream);
     return rc;
   }
   const size_t need = b200_layernorm_bwd_workspace_bytes(rows, cols);

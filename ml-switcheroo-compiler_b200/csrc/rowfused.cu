@@ -40,8 +40,10 @@ struct Red2 {
 };
 
 // Block reductions: shuffle within each warp, then warp 0 combines the NW partials and
-// broadcasts the result through shared memory (3 barriers' worth of latency, but only one
-// warp does the second level).
+// broadcasts the result through shared memory (2 barriers; only one warp does the second
+// level). Each reduction site in a row owns a separate shared-memory region, so no third
+// barrier is needed to protect the result from the next reduction's partials: a region is
+// written again only after later barriers every reader has passed.
 template <int NW>
 __device__ __forceinline__ float bsum(float v, float* sh) {
   v = warp_sum(v);
@@ -54,9 +56,7 @@ __device__ __forceinline__ float bsum(float v, float* sh) {
     if (lane == 0) sh[32] = t;
   }
   __syncthreads();
-  const float r = sh[32];
-  __syncthreads();
-  return r;
+  return sh[32];
 }
 template <int NW>
 __device__ __forceinline__ Red2 bsum2(float a, float b, float* sh) {
@@ -79,7 +79,6 @@ __device__ __forceinline__ Red2 bsum2(float a, float b, float* sh) {
   }
   __syncthreads();
   const Red2 r = {sh[64], sh[65]};
-  __syncthreads();
   return r;
 }
 // max of 64-bit keys (shared by row-max + argmax): key = (order-preserving bits of the
@@ -116,9 +115,7 @@ __device__ __forceinline__ unsigned long long bmaxkey(unsigned long long k, floa
     if (lane == 0) s64[32] = t;
   }
   __syncthreads();
-  const unsigned long long r = s64[32];
-  __syncthreads();
-  return r;
+  return s64[32];
 }
 // sum of a float and max of a 64-bit key in one block reduction
 template <int NW>
@@ -145,7 +142,6 @@ __device__ __forceinline__ void bsum_maxkey(float& v, unsigned long long& k, flo
   __syncthreads();
   k = s64[32];
   v = sh[66];
-  __syncthreads();
 }
 
 template <int NW>
@@ -260,7 +256,8 @@ template <int T, int V, bool GB, bool RAGGED>
 __global__ void __launch_bounds__(T, (V == 4 ? 1024 : 512) / T > 0 ? (V == 4 ? 1024 : 512) / T : 1) rowfused_kernel(const __grid_constant__ Params P) {
   constexpr int NW = T / 32;
   constexpr int H = V / 2;
-  __shared__ __align__(16) float sh[104];
+  __shared__ __align__(16) float sh[104];       // set-up reductions
+  __shared__ __align__(16) float shr[5][104];   // per-row reduction sites
   extern __shared__ __align__(16) float sm[];  // [2 stages][x, c][T][V] (a warp's slices are contiguous)
   const int64_t C = P.cols;
   const int c0 = threadIdx.x * V;
@@ -386,7 +383,7 @@ __global__ void __launch_bounds__(T, (V == 4 ? 1024 : 512) / T > 0 ? (V == 4 ? 1
     float sa, sb, qa, qb;
     upk(s2, sa, sb);
     upk(q2, qa, qb);
-    const Red2 SG = bsum2<NW>(sa + sb, qa + qb, sh);
+    const Red2 SG = bsum2<NW>(sa + sb, qa + qb, shr[0]);
     const float mean = SG.a * invC;
     const float rstd = rsqrtf(fmaxf(SG.b * invC - mean * mean, 0.f) + P.eps);
     const F2 nmr = sp(-mean * rstd), rs = sp(rstd);
@@ -410,7 +407,7 @@ __global__ void __launch_bounds__(T, (V == 4 ? 1024 : 512) / T > 0 ? (V == 4 ? 1
           mk = k1 > mk ? k1 : mk;
         }
       }
-      mk = bmaxkey<NW>(mk, sh);
+      mk = bmaxkey<NW>(mk, shr[1]);
       M = key_value(mk);
       jn = key_index(mk);  // first index of max(n)
     } else {
@@ -429,7 +426,7 @@ __global__ void __launch_bounds__(T, (V == 4 ? 1024 : 512) / T > 0 ? (V == 4 ? 1
       }
     }
     upk(se2, sa, sb);
-    const float inv = 1.f / bsum<NW>(sa + sb, sh);
+    const float inv = 1.f / bsum<NW>(sa + sb, shr[2]);
     // w = y ; sum(c*y) ; argmax(y), first max wins
     F2 cy2 = sp(0.f);
     {
@@ -462,7 +459,7 @@ __global__ void __launch_bounds__(T, (V == 4 ? 1024 : 512) / T > 0 ? (V == 4 ? 1
         }
       }
       cy = sa + sb;
-      bsum_maxkey<NW>(cy, yk, sh);
+      bsum_maxkey<NW>(cy, yk, shr[3]);
       yj = key_index(yk);
     } else {
       // argmax(y) is argmax(n) unless rounding made some y beat y[jn]: one block-wide OR
@@ -471,13 +468,13 @@ __global__ void __launch_bounds__(T, (V == 4 ? 1024 : 512) / T > 0 ? (V == 4 ? 1
         for (int i = 0; i < H; ++i) {
           float u0, u1;
           upk(w[i], u0, u1);
-          if (c0 + 2 * i == jn) sh[70] = u0;
-          if (c0 + 2 * i + 1 == jn) sh[70] = u1;
+          if (c0 + 2 * i == jn) shr[3][70] = u0;
+          if (c0 + 2 * i + 1 == jn) shr[3][70] = u1;
         }
       }
-      cy = bsum<NW>(sa + sb, sh);  // its barriers also publish sh[70] = y[jn]
+      cy = bsum<NW>(sa + sb, shr[3]);  // its barriers also publish shr[3][70] = y[jn]
       yj = jn;
-      const float ymax = sh[70];
+      const float ymax = shr[3][70];
       int tie = 0;
 #pragma unroll
       for (int i = 0; i < H; ++i) {
@@ -502,7 +499,7 @@ __global__ void __launch_bounds__(T, (V == 4 ? 1024 : 512) / T > 0 ? (V == 4 ? 1
             yk = k1 > yk ? k1 : yk;
           }
         }
-        yj = key_index(bmaxkey<NW>(yk, sh));
+        yj = key_index(bmaxkey<NW>(yk, shr[1]));
       }
     }
     if (P.am && threadIdx.x == 0) P.am[row] = yj;
@@ -528,7 +525,7 @@ __global__ void __launch_bounds__(T, (V == 4 ? 1024 : 512) / T > 0 ? (V == 4 ? 1
     float s1a, s1b, s2a, s2b;
     upk(s12, s1a, s1b);
     upk(s22, s2a, s2b);
-    const Red2 S = bsum2<NW>(s1a + s1b, s2a + s2b, sh);
+    const Red2 S = bsum2<NW>(s1a + s1b, s2a + s2b, shr[4]);
     // ---- backward 2: dg, gelu', dp ; dx = dp a ; da += dp x ; db += dp
     {
       F2 x[H], dx[H];
@@ -611,8 +608,11 @@ int launch(const Params& P, int64_t grid, cudaStream_t s) {
 
 // threads per CTA for a row length: 4 columns per thread up to 4096 columns (32 warps
 // per SM hide the reduction and transcendental latencies), 8 up to 8192, then 16
+#ifndef B200_RF_V4_MAX_COLS
+#define B200_RF_V4_MAX_COLS 4096
+#endif
 inline void shape_for(int64_t cols, int& T, int& V) {
-  V = cols <= 4096 ? 4 : (cols <= 8192 ? 8 : 16);
+  V = cols <= B200_RF_V4_MAX_COLS ? 4 : (cols <= 8192 ? 8 : 16);
   const int64_t t = (cols + V - 1) / V;
   T = 32;
   while (T < t) T *= 2;

@@ -27,18 +27,14 @@ __global__ void __launch_bounds__(256) reduce_rows_kernel(const void* __restrict
   if (threadIdx.x == 0) y[row] = (OP == B200_RED_MEAN) ? t / (float)red : t;
 }
 
-// inner > 1: each thread owns one (outer, inner) column over a chunk of `red`;
-// chunks are combined with atomics into y (zeroed / -inf filled first).
-__device__ __forceinline__ void atomic_max_f32(float* addr, float v) {
-  // ordered integer view of IEEE floats
-  if (v >= 0.f) atomicMax(reinterpret_cast<int*>(addr), __float_as_int(v));
-  else atomicMin(reinterpret_cast<unsigned int*>(addr), __float_as_uint(v));
-}
-
+// inner > 1: each thread owns one (outer, inner) column over a chunk of `red`. With one
+// chunk the result goes straight to y; with several, chunk z writes its partial to
+// part[z][outer][inner] and reduce_splits_kernel combines them in chunk order, so the
+// result does not depend on scheduling (no float atomics).
 template <int OP>
 __global__ void __launch_bounds__(256) reduce_cols_kernel(const void* __restrict__ x, int dt, float* __restrict__ y,
-                                                          int64_t outer, int64_t red, int64_t inner, int64_t chunk,
-                                                          int split) {
+                                                          float* __restrict__ part, int64_t outer, int64_t red, int64_t inner,
+                                                          int64_t chunk) {
   const int64_t col = blockIdx.x * (int64_t)blockDim.x + threadIdx.x;
   const int64_t o = blockIdx.y;
   if (col >= inner) return;
@@ -51,11 +47,25 @@ __global__ void __launch_bounds__(256) reduce_cols_kernel(const void* __restrict
     if (OP == B200_RED_MAX) acc = fmaxf(acc, v);
     else acc += v;
   }
-  if (OP == B200_RED_MEAN) acc /= (float)red;
-  float* dst = y + o * inner + col;
-  if (!split) *dst = acc;
-  else if (OP == B200_RED_MAX) atomic_max_f32(dst, acc);
-  else atomicAdd(dst, acc);
+  if (!part) {
+    y[o * inner + col] = (OP == B200_RED_MEAN) ? acc / (float)red : acc;
+  } else {
+    part[((int64_t)blockIdx.z * outer + o) * inner + col] = acc;
+  }
+}
+
+template <int OP>
+__global__ void reduce_splits_kernel(const float* __restrict__ part, float* __restrict__ y, int64_t n, int64_t split,
+                                     int64_t red) {
+  const int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x;
+  if (i >= n) return;
+  float acc = (OP == B200_RED_MAX) ? -INFINITY : 0.f;
+  for (int64_t z = 0; z < split; ++z) {
+    const float v = part[z * n + i];
+    if (OP == B200_RED_MAX) acc = fmaxf(acc, v);
+    else acc += v;
+  }
+  y[i] = (OP == B200_RED_MEAN) ? acc / (float)red : acc;
 }
 
 __global__ void fill_kernel(float* y, int64_t n, float v) {
@@ -209,12 +219,13 @@ __global__ void __launch_bounds__(512) layernorm_input_grad_kernel(const float* 
 }
 
 // dgamma[c] = sum_r dy[r,c] * xhat[r,c], dbeta[c] = sum_r dy[r,c].
-// Each CTA takes ROWS_PER_CTA rows, keeps column partials in shared memory and adds
-// them into the (zeroed) outputs with one atomic per column.
+// Each CTA takes LN_PG_ROWS rows, keeps column partials in shared memory and writes them
+// to part[cta][2][cols]; ln_pg_colsum_kernel adds the CTA partials in order
+// (deterministic, no float atomics).
 constexpr int LN_PG_ROWS = 64;
 __global__ void __launch_bounds__(256) layernorm_param_grad_kernel(const float* __restrict__ dy, const float* __restrict__ x,
-                                                                   float* __restrict__ dg, float* __restrict__ db,
-                                                                   int64_t rows, int64_t cols, float eps) {
+                                                                   float* __restrict__ part, int64_t rows, int64_t cols,
+                                                                   float eps) {
   extern __shared__ float sm[];  // [2*cols] partials
   __shared__ float sred[32];
   float* pg = sm;
@@ -235,9 +246,20 @@ __global__ void __launch_bounds__(256) layernorm_param_grad_kernel(const float* 
     }
   }
   __syncthreads();
-  for (int64_t i = threadIdx.x; i < cols; i += blockDim.x) {
-    if (dg) atomicAdd(dg + i, pg[i]);
-    if (db) atomicAdd(db + i, pb[i]);
+  float* out = part + (int64_t)blockIdx.x * 2 * cols;
+  for (int64_t i = threadIdx.x; i < 2 * cols; i += blockDim.x) out[i] = sm[i];
+}
+
+__global__ void ln_pg_colsum_kernel(const float* __restrict__ part, float* __restrict__ dg, float* __restrict__ db, int64_t G,
+                                    int64_t cols) {
+  const int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x;
+  if (i >= 2 * cols) return;
+  float acc = 0.f;
+  for (int64_t g = 0; g < G; ++g) acc += part[g * 2 * cols + i];
+  if (i < cols) {
+    if (dg) dg[i] = acc;
+  } else if (db) {
+    db[i - cols] = acc;
   }
 }
 
@@ -245,8 +267,27 @@ __global__ void __launch_bounds__(256) layernorm_param_grad_kernel(const float* 
 
 using namespace b200;
 
+static void reduce_plan(int64_t outer, int64_t red, int64_t inner, int64_t& split, int64_t& chunk) {
+  // split `red` across CTAs when there are too few columns to fill the GPU
+  const int64_t cols_blocks = ceil_div(inner, 256);
+  split = 1;
+  const int64_t want = (int64_t)num_sms() * 4;
+  if (cols_blocks * outer < want) split = std::min<int64_t>(ceil_div(want, cols_blocks * outer), ceil_div(red, 32));
+  if (split < 1) split = 1;
+  if (split > 65535) split = 65535;
+  chunk = ceil_div(std::max<int64_t>(red, 1), split);
+  split = ceil_div(std::max<int64_t>(red, 1), chunk);
+}
+
+extern "C" size_t b200_reduce_workspace_bytes(int64_t outer, int64_t red, int64_t inner) {
+  if (outer <= 0 || red <= 0 || inner <= 1) return 0;
+  int64_t split, chunk;
+  reduce_plan(outer, red, inner, split, chunk);
+  return split > 1 ? (size_t)split * (size_t)outer * (size_t)inner * sizeof(float) : 0;
+}
+
 extern "C" int b200_reduce(int dt, const void* x, float* y, int64_t outer, int64_t red, int64_t inner, int op,
-                           void* stream) {
+                           void* workspace, size_t workspace_bytes, void* stream) {
   B200_REQUIRE(x && y, "reduce: null pointer");
   B200_REQUIRE(outer >= 0 && red >= 0 && inner >= 0, "reduce: negative size");
   B200_REQUIRE(op == B200_RED_SUM || op == B200_RED_MEAN || op == B200_RED_MAX, "reduce: bad op %d", op);
@@ -272,27 +313,30 @@ extern "C" int b200_reduce(int dt, const void* x, float* y, int64_t outer, int64
     }
     return check_launch("reduce(rows)");
   }
-  // column mode; split `red` across CTAs when there are too few columns to fill the GPU
-  const int64_t cols_blocks = ceil_div(inner, 256);
-  int64_t split = 1;
-  const int64_t want = (int64_t)num_sms() * 4;
-  if (cols_blocks * outer < want) split = std::min<int64_t>(ceil_div(want, cols_blocks * outer), ceil_div(red, 32));
-  if (split < 1) split = 1;
-  if (split > 65535) split = 65535;
-  const int64_t chunk = ceil_div(red, split);
-  split = ceil_div(red, chunk);
-  if (split > 1) {
-    fill_kernel<<<64, 256, 0, s>>>(y, outer * inner, op == B200_RED_MAX ? -INFINITY : 0.f);
-    int rc = check_launch("reduce(init)");
-    if (rc) return rc;
+  int64_t split, chunk;
+  reduce_plan(outer, red, inner, split, chunk);
+  // without room for the chunk partials, one chunk per column (slower, same result)
+  if (split > 1 && (!workspace || workspace_bytes < b200_reduce_workspace_bytes(outer, red, inner))) {
+    split = 1;
+    chunk = red;
   }
-  dim3 grid((unsigned)cols_blocks, (unsigned)outer, (unsigned)split);
+  float* part = split > 1 ? reinterpret_cast<float*>(workspace) : nullptr;
+  dim3 grid((unsigned)ceil_div(inner, 256), (unsigned)outer, (unsigned)split);
   switch (op) {
-    case B200_RED_SUM: reduce_cols_kernel<B200_RED_SUM><<<grid, 256, 0, s>>>(x, dt, y, outer, red, inner, chunk, split > 1); break;
-    case B200_RED_MEAN: reduce_cols_kernel<B200_RED_MEAN><<<grid, 256, 0, s>>>(x, dt, y, outer, red, inner, chunk, split > 1); break;
-    default: reduce_cols_kernel<B200_RED_MAX><<<grid, 256, 0, s>>>(x, dt, y, outer, red, inner, chunk, split > 1); break;
+    case B200_RED_SUM: reduce_cols_kernel<B200_RED_SUM><<<grid, 256, 0, s>>>(x, dt, y, part, outer, red, inner, chunk); break;
+    case B200_RED_MEAN: reduce_cols_kernel<B200_RED_MEAN><<<grid, 256, 0, s>>>(x, dt, y, part, outer, red, inner, chunk); break;
+    default: reduce_cols_kernel<B200_RED_MAX><<<grid, 256, 0, s>>>(x, dt, y, part, outer, red, inner, chunk); break;
   }
-  return check_launch("reduce(cols)");
+  int rc = check_launch("reduce(cols)");
+  if (rc || split == 1) return rc;
+  const int64_t n = outer * inner;
+  const unsigned g2 = (unsigned)ceil_div(n, 256);
+  switch (op) {
+    case B200_RED_SUM: reduce_splits_kernel<B200_RED_SUM><<<g2, 256, 0, s>>>(part, y, n, split, red); break;
+    case B200_RED_MEAN: reduce_splits_kernel<B200_RED_MEAN><<<g2, 256, 0, s>>>(part, y, n, split, red); break;
+    default: reduce_splits_kernel<B200_RED_MAX><<<g2, 256, 0, s>>>(part, y, n, split, red); break;
+  }
+  return check_launch("reduce(splits)");
 }
 
 extern "C" int b200_argmax(int dt, const void* x, int64_t* idx, int64_t outer, int64_t red, int64_t inner, void* stream) {
@@ -344,22 +388,33 @@ extern "C" int b200_layernorm_input_grad(const float* dy, const float* x, const 
   return check_launch("layernorm_input_grad");
 }
 
+extern "C" size_t b200_layernorm_param_grad_workspace_bytes(int64_t rows, int64_t cols) {
+  if (rows <= 0 || cols <= 0) return 0;
+  return (size_t)ceil_div(rows, (int64_t)LN_PG_ROWS) * 2 * (size_t)cols * sizeof(float);
+}
+
 extern "C" int b200_layernorm_param_grad(const float* dy, const float* x, float* dg, float* db, int64_t rows, int64_t cols,
-                                         float eps, void* stream) {
+                                         float eps, void* workspace, size_t workspace_bytes, void* stream) {
   B200_REQUIRE(dy && x, "layernorm_param_grad: null pointer");
   B200_REQUIRE(dg || db, "layernorm_param_grad: no output");
   B200_REQUIRE(rows >= 0 && cols >= 1, "layernorm_param_grad: bad sizes");
   B200_REQUIRE(cols <= 16384, "layernorm_param_grad: cols %lld > 16384", (long long)cols);
   cudaStream_t s = as_stream(stream);
-  if (dg) {
-    cudaMemsetAsync(dg, 0, cols * sizeof(float), s);
+  if (rows == 0) {
+    if (dg) cudaMemsetAsync(dg, 0, cols * sizeof(float), s);
+    if (db) cudaMemsetAsync(db, 0, cols * sizeof(float), s);
+    return check_launch("layernorm_param_grad(zero)");
   }
-  if (db) {
-    cudaMemsetAsync(db, 0, cols * sizeof(float), s);
-  }
-  if (rows == 0) return check_launch("layernorm_param_grad(zero)");
+  const size_t need = b200_layernorm_param_grad_workspace_bytes(rows, cols);
+  B200_REQUIRE(workspace && workspace_bytes >= need, "layernorm_param_grad: workspace %zu < %zu", workspace_bytes, need);
+  const int64_t G = ceil_div(rows, (int64_t)LN_PG_ROWS);
+  B200_REQUIRE(G <= 2147483647LL, "layernorm_param_grad: too many rows");
   const size_t smem = 2 * cols * sizeof(float);
   if (smem > 48 * 1024) cudaFuncSetAttribute(layernorm_param_grad_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-  layernorm_param_grad_kernel<<<(unsigned)ceil_div(rows, LN_PG_ROWS), 256, smem, s>>>(dy, x, dg, db, rows, cols, eps);
-  return check_launch("layernorm_param_grad");
+  float* part = reinterpret_cast<float*>(workspace);
+  layernorm_param_grad_kernel<<<(unsigned)G, 256, smem, s>>>(dy, x, part, rows, cols, eps);
+  int rc = check_launch("layernorm_param_grad");
+  if (rc) return rc;
+  ln_pg_colsum_kernel<<<(unsigned)ceil_div(2 * cols, (int64_t)256), 256, 0, s>>>(part, dg, db, G, cols);
+  return check_launch("layernorm_param_grad(colsum)");
 }

@@ -628,3 +628,42 @@ def test_layernorm_bwd_rows_fused_matches_oracle(R, C):
     np.testing.assert_allclose(to_np(dx), O.execute_op("LayerNormInputGrad", dy, x, g, eps=1e-5), rtol=1e-4, atol=1e-5)
     np.testing.assert_allclose(to_np(dg), O.execute_op("LayerNormGammaGrad", dy, x, eps=1e-5), rtol=1e-4, atol=1e-3)
     np.testing.assert_allclose(to_np(db), O.execute_op("LayerNormBetaGrad", dy), rtol=1e-4, atol=1e-3)
+
+
+@pytest.mark.parametrize("n,V,D", [(3000, 50, 96), (4096, 32000, 64), (2500, 1, 33)])
+def test_scatter_add_rows_deterministic_in_position_order(n, V, D):
+    """Row scatter-add sums each row's sources in position order: equal to a sequential
+    fp32 accumulation, and bit-identical from run to run (one giant bucket included)."""
+    from b200 import ops
+
+    r = rng(n + V)
+    base = r.standard_normal((V, D)).astype(np.float32)
+    ids = r.integers(0, V, (n, 1)).astype(np.int64)
+    if V > 1:
+        ids[: n // 2, 0] = 0  # half the positions share one row
+    upd = r.standard_normal((n, D)).astype(np.float32)
+    ref = base.copy()
+    for i in range(n):  # np.add.at order, fp32
+        ref[ids[i, 0]] += upd[i]
+    got1 = ops.op_tensor_scatter_add(T(base), T(ids), T(upd))
+    got2 = ops.op_tensor_scatter_add(T(base), T(ids), T(upd))
+    torch.cuda.synchronize()
+    assert torch.equal(got1, got2)
+    np.testing.assert_allclose(to_np(got1), ref, rtol=1e-5, atol=1e-4)
+
+
+def test_column_reduce_split_deterministic():
+    from b200 import ops
+
+    r = rng(31)
+    x = r.standard_normal((32768, 1024)).astype(np.float32)
+    X = T(x)
+    a = ops.op_reduce_sum(X, axis=0)
+    b = ops.op_reduce_sum(X, axis=0)
+    torch.cuda.synchronize()
+    assert torch.equal(a, b)
+    np.testing.assert_allclose(to_np(a), x.astype(np.float64).sum(0), rtol=1e-4, atol=1e-3)
+    m = ops.op_reduce_mean(X, axis=0)
+    np.testing.assert_allclose(to_np(m), x.astype(np.float64).mean(0), rtol=1e-4, atol=1e-5)
+    mx = ops.op_reduce_max(X, axis=0)
+    np.testing.assert_array_equal(to_np(mx), x.max(0))
