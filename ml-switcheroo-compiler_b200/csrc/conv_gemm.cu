@@ -66,61 +66,74 @@ __device__ __forceinline__ float x_tap(const float* __restrict__ x, const Dims& 
   return __ldg(x + ((((int64_t)n * d.C + t.c) * d.H + h) * d.W + w));
 }
 
+constexpr int NPB = 8;  // images (or tap rows / channels) one block walks through
+
 // x -> col bf16 [N, Kp, Pp]   (fwd operand: rows are taps, contiguous pixels)
-// grid (ceil(Pp / 256), Kp, N)
+// grid (ceil(Pp / 256), Kp, ceil(N / NPB))
 __global__ void __launch_bounds__(256) im2col_kp_kernel(const float* __restrict__ x, __nv_bfloat16* __restrict__ col, Dims d) {
-  const int p = blockIdx.x * 256 + threadIdx.x, k = blockIdx.y, n = blockIdx.z;
+  const int p = blockIdx.x * 256 + threadIdx.x, k = blockIdx.y;
   const int Pp = (int)d.Pp();
   if (p >= Pp) return;
-  float v = 0.f;
-  if (k < (int)d.K() && p < (int)d.P()) v = x_tap(x, d, n, tap_of(d, k), p);
-  col[((int64_t)n * d.Kp() + k) * Pp + p] = bf(v);
+  const bool in = k < (int)d.K() && p < (int)d.P();
+  const Tap t = tap_of(d, in ? k : 0);
+  const int n1 = min((int)d.N, (int)(blockIdx.z + 1) * NPB);
+  for (int n = blockIdx.z * NPB; n < n1; ++n)
+    col[((int64_t)n * d.Kp() + k) * Pp + p] = bf(in ? x_tap(x, d, n, t, p) : 0.f);
 }
 
 // x -> col bf16 [S, Kp, L]: split s holds pixels q = s * L + l, q = n * Pp + p (zero past
 // the data), so each split is a dense K-major weight-gradient operand
-// grid (ceil(L / 256), Kp, S)
+// grid (ceil(L / 256), ceil(Kp / NPB), S)
 __global__ void __launch_bounds__(256) im2col_kq_kernel(const float* __restrict__ x, __nv_bfloat16* __restrict__ col, Dims d,
                                                         int64_t L) {
-  const int l = blockIdx.x * 256 + threadIdx.x, k = blockIdx.y, sidx = blockIdx.z;
+  const int l = blockIdx.x * 256 + threadIdx.x, sidx = blockIdx.z;
   if (l >= L) return;
   const int64_t q = (int64_t)sidx * L + l;
   const int Pp = (int)d.Pp();
   const int n = (int)(q / Pp), p = (int)(q - (int64_t)n * Pp);
-  float v = 0.f;
-  if (n < (int)d.N && k < (int)d.K() && p < (int)d.P()) v = x_tap(x, d, n, tap_of(d, k), p);
-  col[((int64_t)sidx * d.Kp() + k) * L + l] = bf(v);
+  const bool pix = n < (int)d.N && p < (int)d.P();
+  const int k1 = min((int)d.Kp(), (int)(blockIdx.y + 1) * NPB);
+  for (int k = blockIdx.y * NPB; k < k1; ++k) {
+    float v = 0.f;
+    if (pix && k < (int)d.K()) v = x_tap(x, d, n, tap_of(d, k), p);
+    col[((int64_t)sidx * d.Kp() + k) * L + l] = bf(v);
+  }
 }
 
-// dy fp32 [N, O, P] -> bf16 [N, O, Pp]; grid (ceil(Pp / 256), O, N)
+// dy fp32 [N, O, P] -> bf16 [N, O, Pp]; grid (ceil(Pp / 256), O, ceil(N / NPB))
 __global__ void __launch_bounds__(256) pack_dy_nop_kernel(const float* __restrict__ dy, __nv_bfloat16* __restrict__ out, Dims d) {
-  const int p = blockIdx.x * 256 + threadIdx.x, o = blockIdx.y, n = blockIdx.z;
+  const int p = blockIdx.x * 256 + threadIdx.x, o = blockIdx.y;
   const int P = (int)d.P(), Pp = (int)d.Pp();
   if (p >= Pp) return;
-  const int64_t no = (int64_t)n * d.O + o;
-  out[no * Pp + p] = bf(p < P ? __ldg(dy + no * P + p) : 0.f);
+  const int n1 = min((int)d.N, (int)(blockIdx.z + 1) * NPB);
+  for (int n = blockIdx.z * NPB; n < n1; ++n) {
+    const int64_t no = (int64_t)n * d.O + o;
+    out[no * Pp + p] = bf(p < P ? __ldg(dy + no * P + p) : 0.f);
+  }
 }
 
 // dy fp32 [N, O, P] -> bf16 [S, O, L]: split s holds columns q = s * L + l, q = n * Pp + p
 // (zero past the data), so each split is a dense [O, L] K-major GEMM operand
-// grid (ceil(L / 256), O, S)
+// grid (ceil(L / 256), ceil(O / NPB), S)
 __global__ void __launch_bounds__(256) pack_dy_sol_kernel(const float* __restrict__ dy, __nv_bfloat16* __restrict__ out, Dims d,
                                                           int64_t L) {
-  const int l = blockIdx.x * 256 + threadIdx.x, o = blockIdx.y, sidx = blockIdx.z;
+  const int l = blockIdx.x * 256 + threadIdx.x, sidx = blockIdx.z;
   if (l >= L) return;
   const int64_t q = (int64_t)sidx * L + l;
   const int P = (int)d.P(), Pp = (int)d.Pp();
   const int n = (int)(q / Pp), p = (int)(q - (int64_t)n * Pp);
-  const float v = (n < (int)d.N && p < P) ? __ldg(dy + ((int64_t)n * d.O + o) * P + p) : 0.f;
-  out[((int64_t)sidx * d.O + o) * L + l] = bf(v);
+  const bool in = n < (int)d.N && p < P;
+  const int o1 = min((int)d.O, (int)(blockIdx.y + 1) * NPB);
+  for (int o = blockIdx.y * NPB; o < o1; ++o) {
+    const float v = in ? __ldg(dy + ((int64_t)n * d.O + o) * P + p) : 0.f;
+    out[((int64_t)sidx * d.O + o) * L + l] = bf(v);
+  }
 }
 
 // dxcol fp32 [N, Kp, P] -> dx [N, C, H, W]: every input pixel gathers the taps that read it
-// grid (ceil(H W / 256), C, N)
-__global__ void __launch_bounds__(256) col2im_kernel(const float* __restrict__ dxcol, float* __restrict__ dx, Dims d) {
-  const int hw = blockIdx.x * 256 + threadIdx.x, c = blockIdx.y, n = blockIdx.z;
+__device__ __forceinline__ void col2im_one(const float* __restrict__ dxcol, float* __restrict__ dx, const Dims& d, int hw, int c,
+                                           int n) {
   const int H = (int)d.H, W = (int)d.W;
-  if (hw >= H * W) return;
   const int h = hw / W, w = hw - h * W;
   const int KH = (int)d.KH, KW = (int)d.KW, sh = (int)d.sh, sw = (int)d.sw, OH = (int)d.OH, OW = (int)d.OW;
   const int P = OH * OW;
@@ -141,6 +154,14 @@ __global__ void __launch_bounds__(256) col2im_kernel(const float* __restrict__ d
     }
   }
   dx[(((int64_t)n * d.C + c) * H) * W + hw] = acc;
+}
+
+// grid (ceil(H W / 256), C, ceil(N / NPB))
+__global__ void __launch_bounds__(256) col2im_kernel(const float* __restrict__ dxcol, float* __restrict__ dx, Dims d) {
+  const int hw = blockIdx.x * 256 + threadIdx.x, c = blockIdx.y;
+  if (hw >= (int)(d.H * d.W)) return;
+  const int n1 = min((int)d.N, (int)(blockIdx.z + 1) * NPB);
+  for (int n = blockIdx.z * NPB; n < n1; ++n) col2im_one(dxcol, dx, d, hw, c, n);
 }
 
 // partials [S, O, Kp] -> dw [O, K] (sum over S in order, drop the K padding)
@@ -214,7 +235,8 @@ extern "C" int b200_conv2d_fwd_tc(const float* x, const float* w, float* y, int6
   pack_weight_kernel<<<grid_of(O * Kp), 256, 0, s>>>(w, wp, O, d.K(), Kp);
   if ((rc = check_launch("conv2d_fwd_tc(pack w)"))) return rc;
   B200_REQUIRE(Kp <= 65535 && N <= 65535, "conv2d_fwd_tc: too many taps or images");
-  im2col_kp_kernel<<<dim3((unsigned)ceil_div(Pp, (int64_t)256), (unsigned)Kp, (unsigned)N), 256, 0, s>>>(x, col, d);
+  im2col_kp_kernel<<<dim3((unsigned)ceil_div(Pp, (int64_t)256), (unsigned)Kp, (unsigned)ceil_div(N, (int64_t)NPB)), 256, 0, s>>>(
+      x, col, d);
   if ((rc = check_launch("conv2d_fwd_tc(im2col)"))) return rc;
   // Y_n [O, P] = Wp [O, Kp] (shared) . Xcol_n [Kp, Pp]
   return gemm_bf16_tcgen05(B200_F32, wp, col, y, N, O, P, Kp, 0, Kp, 1, Kp * Pp, Pp, 1, O * P, P, 1.f, nullptr,
@@ -240,13 +262,15 @@ extern "C" int b200_conv2d_dgrad_tc(const float* dy, const float* w, float* dx, 
   pack_weight_kernel<<<grid_of(O * Kp), 256, 0, s>>>(w, wp, O, d.K(), Kp);
   if ((rc = check_launch("conv2d_dgrad_tc(pack w)"))) return rc;
   B200_REQUIRE(O <= 65535 && N <= 65535 && C <= 65535, "conv2d_dgrad_tc: too many channels or images");
-  pack_dy_nop_kernel<<<dim3((unsigned)ceil_div(Pp, (int64_t)256), (unsigned)O, (unsigned)N), 256, 0, s>>>(dy, dyp, d);
+  pack_dy_nop_kernel<<<dim3((unsigned)ceil_div(Pp, (int64_t)256), (unsigned)O, (unsigned)ceil_div(N, (int64_t)NPB)), 256, 0, s>>>(
+      dy, dyp, d);
   if ((rc = check_launch("conv2d_dgrad_tc(pack dy)"))) return rc;
   // dXcol_n [Kp, P] = Wp^T [Kp, O] (shared, MN-major) . dY_n [O, Pp]
   rc = gemm_bf16_tcgen05(B200_F32, wp, dyp, dxcol, N, Kp, P, O, 0, 1, Kp, O * Pp, Pp, 1, Kp * P, P, 1.f, nullptr, B200_EPI_NONE,
                          nullptr, s);
   if (rc) return rc;
-  col2im_kernel<<<dim3((unsigned)ceil_div(H * W, (int64_t)256), (unsigned)C, (unsigned)N), 256, 0, s>>>(dxcol, dx, d);
+  col2im_kernel<<<dim3((unsigned)ceil_div(H * W, (int64_t)256), (unsigned)C, (unsigned)ceil_div(N, (int64_t)NPB)), 256, 0, s>>>(
+      dxcol, dx, d);
   return check_launch("conv2d_dgrad_tc(col2im)");
 }
 
@@ -274,9 +298,9 @@ extern "C" int b200_conv2d_wgrad_tc(const float* x, const float* dy, float* dw, 
   auto* part = reinterpret_cast<float*>(base);
   B200_REQUIRE(O <= 65535 && Kp <= 65535 && S <= 65535, "conv2d_wgrad_tc: too many channels or splits");
   const unsigned gx = (unsigned)ceil_div(L, (int64_t)256);
-  pack_dy_sol_kernel<<<dim3(gx, (unsigned)O, (unsigned)S), 256, 0, s>>>(dy, dyt, d, L);
+  pack_dy_sol_kernel<<<dim3(gx, (unsigned)ceil_div(O, (int64_t)NPB), (unsigned)S), 256, 0, s>>>(dy, dyt, d, L);
   if ((rc = check_launch("conv2d_wgrad_tc(pack dy)"))) return rc;
-  im2col_kq_kernel<<<dim3(gx, (unsigned)Kp, (unsigned)S), 256, 0, s>>>(x, col, d, L);
+  im2col_kq_kernel<<<dim3(gx, (unsigned)ceil_div(Kp, (int64_t)NPB), (unsigned)S), 256, 0, s>>>(x, col, d, L);
   if ((rc = check_launch("conv2d_wgrad_tc(im2col)"))) return rc;
   // partial_s [O, Kp] = dYt_s [O, L] . col_s^T   (col_s [Kp, L]: K-major B operand)
   rc = gemm_bf16_tcgen05(B200_F32, dyt, col, part, S, O, Kp, L, O * L, L, 1, Kp * L, 1, L, O * Kp, Kp, 1.f, nullptr,
