@@ -232,7 +232,7 @@ __device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
 // in L2). The TMEM accumulator is double-buffered (2 x BN columns), so the epilogue of
 // tile i (TMEM -> registers -> HBM) overlaps the MMAs of tile i+1, and the TMA/MMA
 // pipeline runs continuously across tile boundaries.
-template <int BN>
+template <int BN, int EPI>
 __global__ void __launch_bounds__(THREADS, 1) gemm_tc_kernel(const __grid_constant__ CUtensorMap mapA,
                                                              const __grid_constant__ CUtensorMap mapB,
                                                              const __grid_constant__ CUtensorMap mapC,
@@ -385,19 +385,36 @@ __global__ void __launch_bounds__(THREADS, 1) gemm_tc_kernel(const __grid_consta
         }
         const int64_t cbase = col0 + c * 32;
         if (cbase >= args.N) continue;  // warp-uniform
-        // pre = alpha * acc + bias; act = epi(pre); mask bit = pre > 0
+        // pre = alpha * acc + bias; act = epi(pre); mask bit = pre > 0. The activation is a
+        // template parameter and the other choices are uniform branches outside the element
+        // loops, so a chunk without them costs one multiply per element (a runtime-selected
+        // activation inside the loop is if-converted: tanh would run for every element).
         float v[32], act[32];
         uint32_t mbits = 0;
+        if (args.bias && cbase + 32 <= args.N) {
+#pragma unroll
+          for (int i = 0; i < 32; ++i) v[i] = fmaf(args.alpha, __uint_as_float(cur[i]), __ldg(args.bias + cbase + i));
+        } else if (args.bias) {
+#pragma unroll
+          for (int i = 0; i < 32; ++i)
+            v[i] = args.alpha * __uint_as_float(cur[i]) + (cbase + i < args.N ? __ldg(args.bias + cbase + i) : 0.f);
+        } else {
+#pragma unroll
+          for (int i = 0; i < 32; ++i) v[i] = args.alpha * __uint_as_float(cur[i]);
+        }
+        if (args.aux) {
+#pragma unroll
+          for (int i = 0; i < 32; ++i) mbits |= (v[i] > 0.f ? 1u : 0u) << i;
+        }
 #pragma unroll
         for (int i = 0; i < 32; ++i) {
-          const int64_t n = cbase + i;
-          const float pre = args.alpha * __uint_as_float(cur[i]) + ((args.bias && n < args.N) ? __ldg(args.bias + n) : 0.f);
-          mbits |= (pre > 0.f ? 1u : 0u) << i;
-          float a = pre;
-          if (args.epi == B200_EPI_RELU) a = pre > 0.f ? pre : 0.f;
-          else if (args.epi == B200_EPI_GELU) a = gelu_tanh(pre);
-          act[i] = a;
-          v[i] = args.C2 ? pre : a;
+          if constexpr (EPI == B200_EPI_RELU) act[i] = v[i] > 0.f ? v[i] : 0.f;
+          else if constexpr (EPI == B200_EPI_GELU) act[i] = gelu_tanh(v[i]);
+          else act[i] = v[i];
+        }
+        if (!args.C2) {
+#pragma unroll
+          for (int i = 0; i < 32; ++i) v[i] = act[i];
         }
         const int64_t zoff = (int64_t)zo * args.sC + (int64_t)zi * args.sC_in;
         if (args.store_mode != 0) {
@@ -575,7 +592,7 @@ static bool make_store_map(CUtensorMap* map, void* base, CUtensorMapDataType dt,
              CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
-template <int BN>
+template <int BN, int EPI>
 static int launch(const CUtensorMap& ma, const CUtensorMap& mb, const CUtensorMap& mc, const CUtensorMap& mc2,
                   const CUtensorMap& maux, const Args& a, int64_t batch, cudaStream_t s) {
   const size_t smem = (size_t)STAGES * (BM * BK * 2 + BN * BK * 2) + EPI_SMEM + 1024 + 256;
@@ -584,11 +601,11 @@ static int launch(const CUtensorMap& ma, const CUtensorMap& mb, const CUtensorMa
   int dev = 0;
   cudaGetDevice(&dev);
   if (dev < 0 || dev >= 64 || !attr_set[dev]) {
-    cudaFuncSetAttribute(gemm_tc_kernel<BN>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    cudaFuncSetAttribute(gemm_tc_kernel<BN, EPI>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
     if (dev >= 0 && dev < 64) attr_set[dev] = true;
   }
   const unsigned grid = (unsigned)std::max<int64_t>(1, std::min<int64_t>(tiles, num_sms()));
-  gemm_tc_kernel<BN><<<grid, THREADS, smem, s>>>(ma, mb, mc, mc2, maux, a);
+  gemm_tc_kernel<BN, EPI><<<grid, THREADS, smem, s>>>(ma, mb, mc, mc2, maux, a);
   return check_launch("gemm(bf16 tcgen05)");
 }
 
@@ -679,8 +696,13 @@ int gemm_bf16_tcgen05_b2(int c_dt, const void* A, const void* B, void* C, int64_
     if (ok && aux) ok = make_store_map(&maux, aux, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, N, M, b_in, b_out, ldc, sC_in, sC_out);
     if (ok) a.store_mode = 2;
   }
-  if (BN == 256) return launch<256>(ma, mb, mc, mc2, maux, a, batch, s);
-  return launch<128>(ma, mb, mc, mc2, maux, a, batch, s);
+#define B200_GEMM_LAUNCH(E)                                               \
+  return BN == 256 ? launch<256, E>(ma, mb, mc, mc2, maux, a, batch, s) \
+                   : launch<128, E>(ma, mb, mc, mc2, maux, a, batch, s)
+  if (epi == B200_EPI_RELU) B200_GEMM_LAUNCH(B200_EPI_RELU);
+  if (epi == B200_EPI_GELU) B200_GEMM_LAUNCH(B200_EPI_GELU);
+  B200_GEMM_LAUNCH(B200_EPI_NONE);
+#undef B200_GEMM_LAUNCH
 }
 
 int gemm_bf16_tcgen05(int c_dt, const void* A, const void* B, void* C, int64_t batch, int64_t M, int64_t N, int64_t K,
