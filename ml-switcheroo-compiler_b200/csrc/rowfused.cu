@@ -28,139 +28,6 @@ constexpr float K_GELU = 0.7978845608028654f;  // sqrt(2/pi)
 constexpr float C_GELU = 0.044715f;
 constexpr float LOG2E = 1.4426950408889634f;
 
-// tanh(u) = 1 - 2 / (exp(2u) + 1), exp through ex2.approx, reciprocal through rcp.approx:
-// absolute error ~1e-7, saturates to +-1 for large |u|.
-__device__ __forceinline__ float fast_tanh(float u) {
-  const float e = exp2f(2.f * LOG2E * u);
-  return fmaf(-2.f, __frcp_rn(e + 1.f), 1.f);
-}
-
-struct Red2 {
-  float a, b;
-};
-
-// Block reductions: shuffle within each warp, then warp 0 combines the NW partials and
-// broadcasts the result through shared memory (2 barriers; only one warp does the second
-// level). Each reduction site in a row owns a separate shared-memory region, so no third
-// barrier is needed to protect the result from the next reduction's partials: a region is
-// written again only after later barriers every reader has passed.
-template <int NW>
-__device__ __forceinline__ float bsum(float v, float* sh) {
-  v = warp_sum(v);
-  const int lane = threadIdx.x & 31, w = threadIdx.x >> 5;
-  if (lane == 0) sh[w] = v;
-  __syncthreads();
-  if (w == 0) {
-    float t = lane < NW ? sh[lane] : 0.f;
-    t = warp_sum(t);
-    if (lane == 0) sh[32] = t;
-  }
-  __syncthreads();
-  return sh[32];
-}
-template <int NW>
-__device__ __forceinline__ Red2 bsum2(float a, float b, float* sh) {
-  a = warp_sum(a);
-  b = warp_sum(b);
-  const int lane = threadIdx.x & 31, w = threadIdx.x >> 5;
-  if (lane == 0) {
-    sh[w] = a;
-    sh[32 + w] = b;
-  }
-  __syncthreads();
-  if (w == 0) {
-    float ta = lane < NW ? sh[lane] : 0.f, tb = lane < NW ? sh[32 + lane] : 0.f;
-    ta = warp_sum(ta);
-    tb = warp_sum(tb);
-    if (lane == 0) {
-      sh[64] = ta;
-      sh[65] = tb;
-    }
-  }
-  __syncthreads();
-  const Red2 r = {sh[64], sh[65]};
-  return r;
-}
-// max of 64-bit keys (shared by row-max + argmax): key = (order-preserving bits of the
-// value) << 32 | ~index, so the largest key is the largest value at the smallest index.
-__device__ __forceinline__ unsigned long long order_key(float v, int idx) {
-  const uint32_t u = __float_as_uint(v);
-  const uint32_t o = (u & 0x80000000u) ? ~u : (u | 0x80000000u);
-  return ((unsigned long long)o << 32) | (uint32_t)(~idx);
-}
-__device__ __forceinline__ float key_value(unsigned long long k) {
-  const uint32_t o = (uint32_t)(k >> 32);
-  const uint32_t u = (o & 0x80000000u) ? (o & 0x7fffffffu) : ~o;
-  return __uint_as_float(u);
-}
-__device__ __forceinline__ int key_index(unsigned long long k) { return (int)~(uint32_t)k; }
-__device__ __forceinline__ unsigned long long warp_maxkey(unsigned long long k) {
-#pragma unroll
-  for (int o = 16; o > 0; o >>= 1) {
-    const unsigned long long k2 = __shfl_xor_sync(0xffffffffu, k, o);
-    k = k2 > k ? k2 : k;
-  }
-  return k;
-}
-template <int NW>
-__device__ __forceinline__ unsigned long long bmaxkey(unsigned long long k, float* sh) {
-  unsigned long long* s64 = reinterpret_cast<unsigned long long*>(sh);
-  k = warp_maxkey(k);
-  const int lane = threadIdx.x & 31, w = threadIdx.x >> 5;
-  if (lane == 0) s64[w] = k;
-  __syncthreads();
-  if (w == 0) {
-    unsigned long long t = lane < NW ? s64[lane] : 0ull;
-    t = warp_maxkey(t);
-    if (lane == 0) s64[32] = t;
-  }
-  __syncthreads();
-  return s64[32];
-}
-// sum of a float and max of a 64-bit key in one block reduction
-template <int NW>
-__device__ __forceinline__ void bsum_maxkey(float& v, unsigned long long& k, float* sh) {
-  unsigned long long* s64 = reinterpret_cast<unsigned long long*>(sh);
-  v = warp_sum(v);
-  k = warp_maxkey(k);
-  const int lane = threadIdx.x & 31, w = threadIdx.x >> 5;
-  if (lane == 0) {
-    s64[w] = k;        // keys in sh[0 .. 2 NW)
-    sh[68 + w] = v;    // sums in sh[68 .. 68 + NW)
-  }
-  __syncthreads();
-  if (w == 0) {
-    unsigned long long t = lane < NW ? s64[lane] : 0ull;
-    float f = lane < NW ? sh[68 + lane] : 0.f;
-    t = warp_maxkey(t);
-    f = warp_sum(f);
-    if (lane == 0) {
-      s64[32] = t;
-      sh[66] = f;
-    }
-  }
-  __syncthreads();
-  k = s64[32];
-  v = sh[66];
-}
-
-template <int NW>
-__device__ __forceinline__ float bmax(float v, float* sh) {
-  v = warp_max(v);
-  const int lane = threadIdx.x & 31, w = threadIdx.x >> 5;
-  if (lane == 0) sh[w] = v;
-  __syncthreads();
-  if (w == 0) {
-    float t = lane < NW ? sh[lane] : -INFINITY;
-    t = warp_max(t);
-    if (lane == 0) sh[32] = t;
-  }
-  __syncthreads();
-  const float r = sh[32];
-  __syncthreads();
-  return r;
-}
-
 struct Params {
   const float *x, *a, *b, *gamma, *beta, *c;
   float *y, *dx;
@@ -168,7 +35,8 @@ struct Params {
   float* part;  // [4][grid][cols] partial column sums: da, db, dgamma, dbeta
   int64_t rows, cols;
   float eps;
-  int want_gb;  // accumulate dgamma / dbeta partials
+  int want_gb;    // accumulate dgamma / dbeta partials
+  int aligned16;  // every row and column-vector pointer is 16-byte aligned (vector loads / cp.async allowed)
 };
 
 // ---- packed fp32x2 arithmetic (sm_100a): two lanes of a row per instruction -------
@@ -196,6 +64,11 @@ __device__ __forceinline__ F2 add2(F2 a, F2 b) {
   asm("add.rn.f32x2 %0, %1, %2;" : "=l"(r.v) : "l"(a.v), "l"(b.v));
   return r;
 }
+__device__ __forceinline__ F2 sub2(F2 a, F2 b) {
+  F2 r;
+  asm("sub.rn.f32x2 %0, %1, %2;" : "=l"(r.v) : "l"(a.v), "l"(b.v));
+  return r;
+}
 __device__ __forceinline__ F2 sp(float a) { return pk(a, a); }
 __device__ __forceinline__ float rcp_approx(float x) {
   float r;
@@ -207,31 +80,6 @@ __device__ __forceinline__ float ex2_approx(float x) {
   asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(r) : "f"(x));
   return r;
 }
-// tanh(u) = 1 - 2 / (exp(2u) + 1) on a pair; `u2l` is 2*log2(e)*u
-__device__ __forceinline__ F2 tanh2_from_scaled(F2 u2l) {
-  float a, b;
-  upk(u2l, a, b);
-  a = rcp_approx(ex2_approx(a) + 1.f);
-  b = rcp_approx(ex2_approx(b) + 1.f);
-  return fma2(pk(a, b), sp(-2.f), sp(1.f));
-}
-
-template <int V>
-__device__ __forceinline__ void ldg_pairs(F2 (&r)[V / 2], const float* __restrict__ p, int c0, int64_t C, bool vec, float dflt) {
-  if (p && vec) {
-#pragma unroll
-    for (int i = 0; i < V; i += 4) {
-      float4 t = __ldg(reinterpret_cast<const float4*>(p + c0 + i));
-      r[i / 2] = pk(t.x, t.y);
-      r[i / 2 + 1] = pk(t.z, t.w);
-    }
-  } else {
-#pragma unroll
-    for (int i = 0; i < V; i += 2)
-      r[i / 2] = pk((p && c0 + i < C) ? p[c0 + i] : dflt, (p && c0 + i + 1 < C) ? p[c0 + i + 1] : dflt);
-  }
-}
-
 // cp.async (Ampere-style, per thread) into this thread's own shared-memory slot; the
 // issuing thread is also the only reader, so completion needs no block barrier.
 __device__ __forceinline__ void cp_async16(void* sdst, const void* gsrc) {
@@ -247,57 +95,168 @@ __device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commi
 template <int N>
 __device__ __forceinline__ void cp_async_wait() { asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory"); }
 
-// T threads, V consecutive columns per thread (cols <= T*V), V/2 packed pairs.
-// Registers hold this thread's slice of the column vectors (a, b, gamma, beta, loaded
-// once per CTA), the forward tanh t, one working row array w and the column
-// accumulators. x and c of the current and the next row sit in this thread's own
-// shared-memory slot, prefetched with cp.async one row ahead (double-buffered).
+// lanes 0-15 return sum(a), lanes 16-31 sum(b) over the warp (one shuffle tree for both)
+__device__ __forceinline__ float warp_pair_sum(float a, float b, int lane) {
+  const bool hi = lane >= 16;
+  float keep = hi ? b : a;
+  const float send = hi ? a : b;
+  keep += __shfl_xor_sync(0xffffffffu, send, 16);
+  keep += __shfl_xor_sync(0xffffffffu, keep, 8);
+  keep += __shfl_xor_sync(0xffffffffu, keep, 4);
+  keep += __shfl_xor_sync(0xffffffffu, keep, 2);
+  keep += __shfl_xor_sync(0xffffffffu, keep, 1);
+  return keep;
+}
+// order-preserving map of a float onto an unsigned key and back
+__device__ __forceinline__ uint32_t ord_key(float v) {
+  const uint32_t u = __float_as_uint(v);
+  return (u & 0x80000000u) ? ~u : (u | 0x80000000u);
+}
+__device__ __forceinline__ float ord_value(uint32_t o) { return __uint_as_float((o & 0x80000000u) ? (o & 0x7fffffffu) : ~o); }
+
+// Block reductions of one barrier each: every warp shuffles its partials down, lane 0 /
+// lane 16 post them to the site's shared region, and after the barrier every warp combines
+// the NW warp partials itself (same order in every warp, so every thread sees the same
+// bits). A site is written again only in the next row, after later barriers every reader
+// of its previous contents has passed.
+template <int NW>
+__device__ __forceinline__ float2 block_finish(const float* red, int lane) {
+  if (NW > 16) {
+    const float ra = lane < NW ? red[lane] : 0.f, rb = lane < NW ? red[32 + lane] : 0.f;
+    const float t = warp_pair_sum(ra, rb, lane);
+    return make_float2(__shfl_sync(0xffffffffu, t, 0), __shfl_sync(0xffffffffu, t, 16));
+  }
+  float t = (lane & 15) < NW ? red[(lane >> 4) * 32 + (lane & 15)] : 0.f;
+#pragma unroll
+  for (int o = 8; o > 0; o >>= 1) t += __shfl_xor_sync(0xffffffffu, t, o);
+  return make_float2(__shfl_sync(0xffffffffu, t, 0), __shfl_sync(0xffffffffu, t, 16));
+}
+template <int NW>
+__device__ __forceinline__ float2 block_pair_sum(float a, float b, float* red, int lane, int w) {
+  const float v = warp_pair_sum(a, b, lane);
+  if ((lane & 15) == 0) red[(lane >> 4) * 32 + w] = v;
+  __syncthreads();
+  return block_finish<NW>(red, lane);
+}
+// the same plus the maximum of an unsigned key (red[64 .. 64 + NW))
+template <int NW>
+__device__ __forceinline__ float2 block_pair_sum_max(float a, float b, uint32_t& m, float* red, int lane, int w) {
+  const float v = warp_pair_sum(a, b, lane);
+  const uint32_t wm = __reduce_max_sync(0xffffffffu, m);
+  uint32_t* ured = reinterpret_cast<uint32_t*>(red);
+  if ((lane & 15) == 0) red[(lane >> 4) * 32 + w] = v;
+  if (lane == 0) ured[64 + w] = wm;
+  __syncthreads();
+  m = __reduce_max_sync(0xffffffffu, lane < NW ? ured[64 + lane] : 0u);
+  return block_finish<NW>(red, lane);
+}
+template <int NW>
+__device__ __forceinline__ uint32_t block_max_key(uint32_t m, float* red, int lane, int w) {
+  uint32_t* ured = reinterpret_cast<uint32_t*>(red);
+  const uint32_t wm = __reduce_max_sync(0xffffffffu, m);
+  if (lane == 0) ured[64 + w] = wm;
+  __syncthreads();
+  return __reduce_max_sync(0xffffffffu, lane < NW ? ured[64 + lane] : 0u);
+}
+
+// V values of a column vector from column c0 on: past the row end 0, a null vector `if_null`
+template <int V>
+__device__ __forceinline__ void ldg_vals(float (&r)[V], const float* __restrict__ p, int c0, int64_t C, bool vec, float if_null) {
+  if (p && vec) {
+#pragma unroll
+    for (int i = 0; i < V; i += 4) {
+      const float4 t = __ldg(reinterpret_cast<const float4*>(p + c0 + i));
+      r[i] = t.x; r[i + 1] = t.y; r[i + 2] = t.z; r[i + 3] = t.w;
+    }
+  } else {
+#pragma unroll
+    for (int i = 0; i < V; ++i) r[i] = c0 + i < C ? (p ? p[c0 + i] : if_null) : 0.f;
+  }
+}
+
+// T threads, V consecutive columns per thread (cols <= T*V), V/2 packed pairs, one row per
+// CTA at a time. Registers hold this thread's slice of the column vectors (a, b,
+// gamma log2e, (beta - shift) log2e, loaded once per CTA), sigma(2u) of the current row,
+// one working row array w and the column accumulators. x and c of the current and the
+// next row sit in this thread's own shared-memory slot, prefetched with cp.async one row
+// ahead (double-buffered). Per row three block reductions of one barrier each:
+//   R1  sum g, sum g^2                       (LayerNorm statistics)
+//   R2  sum e, sum c e, max e                (e = exp(n - shift); sum c y = sum(c e) / sum e)
+//   R3  sum dn gamma, sum dn gamma g_hat     (LayerNormInputGrad)
+// plus the row max of n before R2 when the fixed softmax shift does not apply.
+// gelu_tanh(p) = 0.5 p (1 + tanh u) = p sigma(2u), u = k (p + c p^3). Columns past the
+// row end have a = b = 0, gamma = 0, beta' = -inf and zero-filled x, c, so they add exact
+// zeros to every row sum and never win a maximum; they are only kept out of the stores.
+// argmax(y): y is a monotone function of e, so only threads whose largest e rounds to the
+// row's largest y search their columns, and post the first match with a shared-memory
+// atomicMin (an order-independent minimum).
 template <int T, int V, bool GB, bool RAGGED>
 __global__ void __launch_bounds__(T, (V == 4 ? 1024 : 512) / T > 0 ? (V == 4 ? 1024 : 512) / T : 1) rowfused_kernel(const __grid_constant__ Params P) {
   constexpr int NW = T / 32;
   constexpr int H = V / 2;
-  __shared__ __align__(16) float sh[104];       // set-up reductions
-  __shared__ __align__(16) float shr[5][104];   // per-row reduction sites
+  __shared__ __align__(16) float sh[4][32];    // set-up reductions
+  __shared__ __align__(16) float red[4][96];   // per-row reduction sites
+  __shared__ int s_am;
   extern __shared__ __align__(16) float sm[];  // [2 stages][x, c][T][V] (a warp's slices are contiguous)
   const int64_t C = P.cols;
+  const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5;
   const int c0 = threadIdx.x * V;
   const bool full = c0 + V <= C;
-  const bool vec = full && ((C & 3) == 0);
+  const bool vec = full && ((C & 3) == 0) && P.aligned16;
   const bool any = c0 < C;
-  auto msk = [&](int i) -> F2 { return RAGGED ? pk(c0 + 2 * i < C ? 1.f : 0.f, c0 + 2 * i + 1 < C ? 1.f : 0.f) : sp(1.f); };
-  auto mul_mask = [&](F2 v, int i) -> F2 { return RAGGED ? mul2(v, msk(i)) : v; };
   const float invC = 1.f / (float)C;
-  const float KG2L = 2.f * K_GELU * LOG2E;
   const int64_t G = gridDim.x;
 
-  F2 a[H], b[H], ga[H], be[H];
-  ldg_pairs<V>(a, P.a, c0, C, vec, 0.f);
-  ldg_pairs<V>(b, P.b, c0, C, vec, 0.f);
-  ldg_pairs<V>(ga, P.gamma, c0, C, vec, 1.f);
-  ldg_pairs<V>(be, P.beta, c0, C, vec, 0.f);
-  // Softmax shift: for n = gamma * x_hat + beta with every gamma >= 0, each row max lies in
-  // [min beta, max gamma * sqrt(C) + max beta] (|x_hat| <= sqrt(C), max x_hat >= 0). When
-  // that interval is at most 80 wide, exp(n - S) with S its top never overflows and the
-  // largest term never underflows, so the per-row max reduction is not needed.
-  float shiftS = 0.f;
+  F2 a[H], b[H], gl[H], bl[H];
   bool use_shift;
   {
+    float av[V], bv[V], gv[V], ev[V];
+    ldg_vals<V>(av, P.a, c0, C, vec, 0.f);
+    ldg_vals<V>(bv, P.b, c0, C, vec, 0.f);
+    ldg_vals<V>(gv, P.gamma, c0, C, vec, 1.f);
+    ldg_vals<V>(ev, P.beta, c0, C, vec, 0.f);
+    // Softmax shift: for n = gamma * x_hat + beta with every gamma >= 0, each row max lies in
+    // [min beta, max gamma * sqrt(C) + max beta] (|x_hat| <= sqrt(C), max x_hat >= 0). When
+    // that interval is at most 80 wide, exp(n - S) with S its top never overflows and the
+    // largest term never underflows, so the per-row max reduction is not needed.
     float gmin = INFINITY, gmx = -INFINITY, bmn = INFINITY, bmx = -INFINITY;
 #pragma unroll
-    for (int i = 0; i < H; ++i) {
-      float g0, g1, b0, b1;
-      upk(ga[i], g0, g1);
-      upk(be[i], b0, b1);
-      if (c0 + 2 * i < C) { gmin = fminf(gmin, g0); gmx = fmaxf(gmx, g0); bmn = fminf(bmn, b0); bmx = fmaxf(bmx, b0); }
-      if (c0 + 2 * i + 1 < C) { gmin = fminf(gmin, g1); gmx = fmaxf(gmx, g1); bmn = fminf(bmn, b1); bmx = fmaxf(bmx, b1); }
+    for (int i = 0; i < V; ++i) {
+      if (!RAGGED || c0 + i < C) {
+        gmin = fminf(gmin, gv[i]); gmx = fmaxf(gmx, gv[i]);
+        bmn = fminf(bmn, ev[i]); bmx = fmaxf(bmx, ev[i]);
+      }
     }
-    gmin = -bmax<NW>(-gmin, sh);
-    gmx = bmax<NW>(gmx, sh);
-    bmn = -bmax<NW>(-bmn, sh);
-    bmx = bmax<NW>(bmx, sh);
-    shiftS = gmx * sqrtf((float)C) + bmx;
+    gmin = -warp_max(-gmin);
+    gmx = warp_max(gmx);
+    bmn = -warp_max(-bmn);
+    bmx = warp_max(bmx);
+    if (lane == 0) {
+      sh[0][wid] = gmin; sh[1][wid] = gmx; sh[2][wid] = bmn; sh[3][wid] = bmx;
+    }
+    if (threadIdx.x == 0) s_am = 0x7fffffff;
+    __syncthreads();
+    const int l = lane < NW ? lane : 0;
+    gmin = -warp_max(-sh[0][l]);
+    gmx = warp_max(sh[1][l]);
+    bmn = -warp_max(-sh[2][l]);
+    bmx = warp_max(sh[3][l]);
+    const float shiftS = gmx * sqrtf((float)C) + bmx;
     use_shift = gmin >= 0.f && (shiftS - bmn) <= 80.f && isfinite(shiftS);
+    const float sub = use_shift ? shiftS : 0.f;
+#pragma unroll
+    for (int i = 0; i < H; ++i) {
+      const bool ok0 = !RAGGED || c0 + 2 * i < C, ok1 = !RAGGED || c0 + 2 * i + 1 < C;
+      a[i] = pk(av[2 * i], av[2 * i + 1]);
+      b[i] = pk(bv[2 * i], bv[2 * i + 1]);
+      gl[i] = pk(gv[2 * i] * LOG2E, gv[2 * i + 1] * LOG2E);
+      bl[i] = pk(ok0 ? (ev[2 * i] - sub) * LOG2E : -INFINITY, ok1 ? (ev[2 * i + 1] - sub) * LOG2E : -INFINITY);
+    }
   }
+  constexpr float CS0 = -2.f * LOG2E * K_GELU;  // sigma(2u) = 1 / (1 + 2^(p (CS0 + CS1 p^2)))
+  constexpr float CS1 = -2.f * LOG2E * K_GELU * C_GELU;
+  constexpr float D0 = 2.f * K_GELU, D1 = 6.f * K_GELU * C_GELU;  // gelu' = s + p (D0 + D1 p^2) s (1 - s)
+
   F2 acc_da[H], acc_db[H], acc_dg[GB ? H : 1], acc_dbe[GB ? H : 1];
 #pragma unroll
   for (int i = 0; i < H; ++i) {
@@ -363,8 +322,8 @@ __global__ void __launch_bounds__(T, (V == 4 ? 1024 : 512) / T > 0 ? (V == 4 ? 1
     cp_async_wait<1>();
     const float* xs = sm + ((size_t)stage * 2 * T + threadIdx.x) * V;
     const float* cs = xs + (size_t)T * V;
-    F2 w[H], t[H];
-    // ---- forward: p = x a + b ; t = tanh(k p (1 + c p^2)) ; w = g = 0.5 p (1 + t)
+    F2 sg[H], w[H];
+    // ---- forward: p = x a + b ; s = sigma(2u) ; w = g = p s
     F2 s2 = sp(0.f), q2 = sp(0.f);
     {
       F2 x[H];
@@ -372,10 +331,12 @@ __global__ void __launch_bounds__(T, (V == 4 ? 1024 : 512) / T > 0 ? (V == 4 ? 1
 #pragma unroll
       for (int i = 0; i < H; ++i) {
         const F2 p = fma2(x[i], a[i], b[i]);
-        const F2 q = fma2(mul2(p, p), sp(C_GELU), sp(1.f));
-        t[i] = tanh2_from_scaled(mul2(mul2(p, q), sp(KG2L)));
-        const F2 hp = mul2(p, sp(0.5f));
-        w[i] = mul_mask(fma2(hp, t[i], hp), i);
+        const F2 u = mul2(p, fma2(mul2(p, p), sp(CS1), sp(CS0)));
+        float u0, u1, d0, d1;
+        upk(u, u0, u1);
+        upk(add2(pk(ex2_approx(u0), ex2_approx(u1)), sp(1.f)), d0, d1);
+        sg[i] = pk(rcp_approx(d0), rcp_approx(d1));
+        w[i] = mul2(p, sg[i]);
         s2 = add2(s2, w[i]);
         q2 = fma2(w[i], w[i], q2);
       }
@@ -383,174 +344,112 @@ __global__ void __launch_bounds__(T, (V == 4 ? 1024 : 512) / T > 0 ? (V == 4 ? 1
     float sa, sb, qa, qb;
     upk(s2, sa, sb);
     upk(q2, qa, qb);
-    const Red2 SG = bsum2<NW>(sa + sb, qa + qb, shr[0]);
-    const float mean = SG.a * invC;
-    const float rstd = rsqrtf(fmaxf(SG.b * invC - mean * mean, 0.f) + P.eps);
-    const F2 nmr = sp(-mean * rstd), rs = sp(rstd);
-    // w = n = LayerNorm(g); row max (skipped on the shift path) with its first index
-    float M;
-    int jn = 0;
+    const float2 SQ = block_pair_sum<NW>(sa + sb, qa + qb, red[0], lane, wid);
+    const float mean = SQ.x * invC;
+    const float rstd = rsqrtf(fmaxf(SQ.y * invC - mean * mean, 0.f) + P.eps);
+    const F2 rs = sp(rstd), nmr = sp(-mean * rstd);
+    // ---- z = (g_hat gamma + beta - shift) log2e ; e = 2^z ; sum e, sum c e, max e
 #pragma unroll
-    for (int i = 0; i < H; ++i) w[i] = fma2(fma2(w[i], rs, nmr), ga[i], be[i]);
-    if (!use_shift) {
-      unsigned long long mk = 0ull;
+    for (int i = 0; i < H; ++i) w[i] = fma2(fma2(w[i], rs, nmr), gl[i], bl[i]);
+    if (!use_shift) {  // per-row max of z
+      float mz = -INFINITY;
 #pragma unroll
       for (int i = 0; i < H; ++i) {
         float u0, u1;
         upk(w[i], u0, u1);
-        if (!RAGGED || c0 + 2 * i < C) {
-          const unsigned long long k0 = order_key(u0, c0 + 2 * i);
-          mk = k0 > mk ? k0 : mk;
-        }
-        if (!RAGGED || c0 + 2 * i + 1 < C) {
-          const unsigned long long k1 = order_key(u1, c0 + 2 * i + 1);
-          mk = k1 > mk ? k1 : mk;
-        }
+        mz = fmaxf(mz, fmaxf(u0, u1));
       }
-      mk = bmaxkey<NW>(mk, shr[1]);
-      M = key_value(mk);
-      jn = key_index(mk);  // first index of max(n)
-    } else {
-      M = shiftS;
-    }
-    // w = exp(n - M)
-    F2 se2 = sp(0.f);
-    {
-      const F2 ml = sp(-M * LOG2E), l2 = sp(LOG2E);
+      const F2 nz = sp(-ord_value(block_max_key<NW>(ord_key(mz), red[1], lane, wid)));
 #pragma unroll
-      for (int i = 0; i < H; ++i) {
-        float u0, u1;
-        upk(fma2(w[i], l2, ml), u0, u1);
-        w[i] = mul_mask(pk(ex2_approx(u0), ex2_approx(u1)), i);
-        se2 = add2(se2, w[i]);
-      }
+      for (int i = 0; i < H; ++i) w[i] = add2(w[i], nz);
     }
-    upk(se2, sa, sb);
-    const float inv = 1.f / bsum<NW>(sa + sb, shr[2]);
-    // w = y ; sum(c*y) ; argmax(y), first max wins
-    F2 cy2 = sp(0.f);
+    F2 se2 = sp(0.f), sce2 = sp(0.f);
+    float me = 0.f;
     {
       F2 c[H];
       lds_pairs(cs, c);
-      const F2 iv = sp(inv);
-#pragma unroll
-      for (int i = 0; i < H; ++i) {
-        w[i] = mul2(w[i], iv);
-        cy2 = fma2(c[i], w[i], cy2);
-      }
-    }
-    upk(cy2, sa, sb);
-    float cy;
-    int yj;
-    if (use_shift) {
-      // exact argmax of y: its key max travels with the sum of c*y
-      unsigned long long yk = 0ull;
 #pragma unroll
       for (int i = 0; i < H; ++i) {
         float u0, u1;
         upk(w[i], u0, u1);
-        if (!RAGGED || c0 + 2 * i < C) {
-          const unsigned long long k0 = order_key(u0, c0 + 2 * i);
-          yk = k0 > yk ? k0 : yk;
-        }
-        if (!RAGGED || c0 + 2 * i + 1 < C) {
-          const unsigned long long k1 = order_key(u1, c0 + 2 * i + 1);
-          yk = k1 > yk ? k1 : yk;
-        }
-      }
-      cy = sa + sb;
-      bsum_maxkey<NW>(cy, yk, shr[3]);
-      yj = key_index(yk);
-    } else {
-      // argmax(y) is argmax(n) unless rounding made some y beat y[jn]: one block-wide OR
-      if (jn >= c0 && jn < c0 + V) {
-#pragma unroll
-        for (int i = 0; i < H; ++i) {
-          float u0, u1;
-          upk(w[i], u0, u1);
-          if (c0 + 2 * i == jn) shr[3][70] = u0;
-          if (c0 + 2 * i + 1 == jn) shr[3][70] = u1;
-        }
-      }
-      cy = bsum<NW>(sa + sb, shr[3]);  // its barriers also publish shr[3][70] = y[jn]
-      yj = jn;
-      const float ymax = shr[3][70];
-      int tie = 0;
-#pragma unroll
-      for (int i = 0; i < H; ++i) {
-        float u0, u1;
-        upk(w[i], u0, u1);
-        const int j0 = c0 + 2 * i, j1 = j0 + 1;
-        if ((!RAGGED || j0 < C) && (j0 < jn ? u0 >= ymax : (j0 > jn && u0 > ymax))) tie = 1;
-        if ((!RAGGED || j1 < C) && (j1 < jn ? u1 >= ymax : (j1 > jn && u1 > ymax))) tie = 1;
-      }
-      if (__syncthreads_or(tie)) {
-        unsigned long long yk = 0ull;
-#pragma unroll
-        for (int i = 0; i < H; ++i) {
-          float u0, u1;
-          upk(w[i], u0, u1);
-          if (!RAGGED || c0 + 2 * i < C) {
-            const unsigned long long k0 = order_key(u0, c0 + 2 * i);
-            yk = k0 > yk ? k0 : yk;
-          }
-          if (!RAGGED || c0 + 2 * i + 1 < C) {
-            const unsigned long long k1 = order_key(u1, c0 + 2 * i + 1);
-            yk = k1 > yk ? k1 : yk;
-          }
-        }
-        yj = key_index(bmaxkey<NW>(yk, shr[1]));
+        u0 = ex2_approx(u0);
+        u1 = ex2_approx(u1);
+        me = fmaxf(me, fmaxf(u0, u1));
+        w[i] = pk(u0, u1);
+        se2 = add2(se2, w[i]);
+        sce2 = fma2(c[i], w[i], sce2);
       }
     }
-    if (P.am && threadIdx.x == 0) P.am[row] = yj;
-    store_row(P.y + row * C, w);
-    // ---- backward 1: w = dn = y (c - cy) ; s1 = sum dn gamma ; s2 = sum dn gamma g_hat
+    upk(se2, sa, sb);
+    upk(sce2, qa, qb);
+    uint32_t emax = __float_as_uint(me);  // e >= 0: the bit pattern orders like the value
+    const float2 E = block_pair_sum_max<NW>(sa + sb, qa + qb, emax, red[2], lane, wid);
+    const float inv = 1.f / E.x;
+    const float cy = E.y * inv;
+    if (P.am) {  // argmax(y): the first column whose y equals the row's largest y
+      const float ymax = __uint_as_float(emax) * inv;
+      if (me * inv == ymax) {
+        int first = 0x7fffffff;
+#pragma unroll
+        for (int i = H - 1; i >= 0; --i) {
+          float u0, u1;
+          upk(mul2(w[i], sp(inv)), u0, u1);
+          if (u1 == ymax) first = c0 + 2 * i + 1;
+          if (u0 == ymax) first = c0 + 2 * i;
+        }
+        atomicMin(&s_am, first);
+      }
+    }
+    // ---- y = e / sum e ; dn = y (c - cy) ; w = dn gamma log2e ; S1 = sum w, S2 = sum w g_hat
     F2 s12 = sp(0.f), s22 = sp(0.f);
     {
-      F2 c[H], x[H];
+      F2 c[H], x[H], y[H];
       lds_pairs(cs, c);
       lds_pairs(xs, x);
-      const F2 ncy = sp(-cy);
+      const F2 iv = sp(inv), ncy = sp(-cy);
 #pragma unroll
       for (int i = 0; i < H; ++i) {
-        w[i] = mul2(w[i], add2(c[i], ncy));
-        const F2 p = fma2(x[i], a[i], b[i]);
-        const F2 hp = mul2(p, sp(0.5f));
-        const F2 gh = mul_mask(fma2(fma2(hp, t[i], hp), rs, nmr), i);
-        const F2 dyg = mul2(w[i], ga[i]);
-        s12 = add2(s12, dyg);
-        s22 = fma2(dyg, gh, s22);
+        y[i] = mul2(w[i], iv);
+        const F2 dn = mul2(y[i], add2(c[i], ncy));
+        const F2 gh = fma2(mul2(fma2(x[i], a[i], b[i]), sg[i]), rs, nmr);
+        if (GB) {
+          acc_dg[GB ? i : 0] = fma2(dn, gh, acc_dg[GB ? i : 0]);
+          acc_dbe[GB ? i : 0] = add2(acc_dbe[GB ? i : 0], dn);
+        }
+        w[i] = mul2(dn, gl[i]);
+        s12 = add2(s12, w[i]);
+        s22 = fma2(w[i], gh, s22);
       }
+      store_row(P.y + row * C, y);
     }
     float s1a, s1b, s2a, s2b;
     upk(s12, s1a, s1b);
     upk(s22, s2a, s2b);
-    const Red2 S = bsum2<NW>(s1a + s1b, s2a + s2b, shr[4]);
-    // ---- backward 2: dg, gelu', dp ; dx = dp a ; da += dp x ; db += dp
+    const float2 S = block_pair_sum<NW>(s1a + s1b, s2a + s2b, red[3], lane, wid);
+    if (P.am && threadIdx.x == 0) {
+      const int j = s_am;
+      P.am[row] = j == 0x7fffffff ? 0 : j;  // no candidate: y is NaN throughout, argmax 0
+      s_am = 0x7fffffff;
+    }
+    // ---- dg = rstd/C (C dn gamma - S1 - g_hat S2), with g_hat = g rstd - mean rstd folded in:
+    //      dg = g A + (w kC + B) ; dp = dg gelu'(p) ; dx = dp a ; da += dp x ; db += dp
     {
+      const float kC = rstd * (1.f / LOG2E);
+      const float kS2 = -kC * invC * S.y;
+      const F2 fkC = sp(kC), fA = sp(rstd * kS2), fB = sp(fmaf(-mean * rstd, kS2, -kC * invC * S.x));
       F2 x[H], dx[H];
       lds_pairs(xs, x);
-      const F2 k1 = sp(rstd * invC), fC = sp((float)C), nS1 = sp(-S.a), nS2 = sp(-S.b);
 #pragma unroll
       for (int i = 0; i < H; ++i) {
         const F2 p = fma2(x[i], a[i], b[i]);
-        const F2 hp = mul2(p, sp(0.5f));
-        const F2 gh = mul_mask(fma2(fma2(hp, t[i], hp), rs, nmr), i);
-        // dg = rstd/C (C dn gamma - S1 - g_hat S2)
-        const F2 dg = mul2(k1, fma2(gh, nS2, fma2(fC, mul2(w[i], ga[i]), nS1)));
-        // gelu'(p) = 0.5 (1 + t) + 0.5 k p (1 - t^2) (1 + 3 c p^2)
-        const F2 A = fma2(t[i], sp(0.5f), sp(0.5f));
-        const F2 sech2 = fma2(t[i], mul2(t[i], sp(-1.f)), sp(1.f));
-        const F2 Bq = fma2(mul2(p, p), sp(3.f * C_GELU), sp(1.f));
-        const F2 gd = fma2(mul2(mul2(p, sp(0.5f * K_GELU)), sech2), Bq, A);
-        const F2 dp = mul_mask(mul2(dg, gd), i);
+        const F2 dg = fma2(mul2(p, sg[i]), fA, fma2(w[i], fkC, fB));
+        // gelu'(p) = s + r (1 - s) with r = p (D0 + D1 p^2) s
+        const F2 r = mul2(mul2(p, fma2(mul2(p, p), sp(D1), sp(D0))), sg[i]);
+        const F2 gd = sub2(add2(sg[i], r), mul2(r, sg[i]));
+        const F2 dp = mul2(dg, gd);
         dx[i] = mul2(dp, a[i]);
         acc_da[i] = fma2(dp, x[i], acc_da[i]);
         acc_db[i] = add2(acc_db[i], dp);
-        if (GB) {
-          acc_dg[i] = fma2(w[i], gh, acc_dg[i]);
-          acc_dbe[i] = add2(acc_dbe[i], w[i]);
-        }
       }
       store_row(P.dx + row * C, dx);
     }
@@ -571,18 +470,33 @@ __global__ void __launch_bounds__(T, (V == 4 ? 1024 : 512) / T > 0 ? (V == 4 ? 1
   }
 }
 
-// out[k][col] = sum_g part[k][g][col], g in increasing order (deterministic)
-__global__ void colsum_kernel(const float* __restrict__ part, float* __restrict__ o0, float* __restrict__ o1,
-                              float* __restrict__ o2, float* __restrict__ o3, int64_t G, int64_t C, int nk) {
-  const int64_t col = blockIdx.x * (int64_t)blockDim.x + threadIdx.x;
+// out[k][col] = sum_g part[k][g][col] in a fixed order (deterministic): warp w of a block
+// sums g = w, w + 8, w + 16, ... in increasing g for 32 adjacent columns, then the 8 warp
+// sums are added in warp order. 8 independent chains per column keep enough loads in flight.
+constexpr int CS_WARPS = 8;
+__global__ void __launch_bounds__(32 * CS_WARPS) colsum_kernel(const float* __restrict__ part, float* __restrict__ o0,
+                                                               float* __restrict__ o1, float* __restrict__ o2,
+                                                               float* __restrict__ o3, int64_t G, int64_t C, int nk) {
+  __shared__ float sh[CS_WARPS][33];
+  const int lane = threadIdx.x & 31, w = threadIdx.x >> 5;
+  const int64_t col = (int64_t)blockIdx.x * 32 + lane;
   const int k = blockIdx.y;
-  if (col >= C || k >= nk) return;
   float* out = k == 0 ? o0 : k == 1 ? o1 : k == 2 ? o2 : o3;
-  if (!out) return;
-  const float* p = part + (int64_t)k * G * C + col;
+  const bool live = col < C && k < nk && out != nullptr;
   float s = 0.f;
-  for (int64_t g = 0; g < G; ++g) s += p[g * C];
-  out[col] = s;
+  if (live) {
+    const float* p = part + (int64_t)k * G * C + col;
+#pragma unroll 4
+    for (int64_t g = w; g < G; g += CS_WARPS) s += __ldg(p + g * C);
+  }
+  sh[w][lane] = s;
+  __syncthreads();
+  if (w == 0 && live) {
+    float t = sh[0][lane];
+#pragma unroll
+    for (int i = 1; i < CS_WARPS; ++i) t += sh[i][lane];
+    out[col] = t;
+  }
 }
 
 template <int T, int V>
@@ -664,6 +578,8 @@ extern "C" int b200_rowfused_fwd_bwd(const float* x, const float* a, const float
   P.part = reinterpret_cast<float*>(workspace);
   P.rows = rows; P.cols = cols; P.eps = eps;
   P.want_gb = (dgamma || dbeta) ? 1 : 0;
+  auto al = [](const void* p) { return p == nullptr || (reinterpret_cast<uintptr_t>(p) & 15) == 0; };
+  P.aligned16 = al(x) && al(a) && al(b) && al(gamma) && al(beta) && al(cot) && al(y) && al(dx) ? 1 : 0;
   int T, V;
   shape_for(cols, T, V);
   const int64_t grid = grid_for(rows, cols);
@@ -683,7 +599,7 @@ extern "C" int b200_rowfused_fwd_bwd(const float* x, const float* a, const float
     rc = launch<1024, 16>(P, grid, s);
   }
   if (rc) return rc;
-  dim3 g2((unsigned)ceil_div(cols, 256), P.want_gb ? 4 : 2);
-  colsum_kernel<<<g2, 256, 0, s>>>(P.part, da, db, dgamma, dbeta, grid, cols, P.want_gb ? 4 : 2);
+  dim3 g2((unsigned)ceil_div(cols, 32), P.want_gb ? 4 : 2);
+  colsum_kernel<<<g2, 32 * CS_WARPS, 0, s>>>(P.part, da, db, dgamma, dbeta, grid, cols, P.want_gb ? 4 : 2);
   return check_launch("rowfused(colsum)");
 }

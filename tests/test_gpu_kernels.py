@@ -299,10 +299,14 @@ def test_logsoftmax_pick_fwd_bwd(R, V):
     np.testing.assert_allclose(to_np(dx), dx_ref, rtol=1e-4, atol=1e-6)
 
 
-@pytest.mark.parametrize("C,path", [(4096, "shift"), (4096, "general"), (1000, "general"), (77, "shift"), (6000, "general")])
-def test_rowfused_kernel_both_softmax_paths(C, path):
+@pytest.mark.parametrize("C,path,gb", [(4096, "shift", True), (4096, "general", True), (1000, "general", True),
+                                       (77, "shift", True), (6000, "general", True), (4096, "shift", False),
+                                       (4096, "general", False), (3000, "shift", False), (3000, "general", False),
+                                       (2056, "general", False), (1000, "shift", False)])
+def test_rowfused_kernel_both_softmax_paths(C, path, gb):
     """The fused row kernel against the oracle: gamma = 1 / beta = 0 takes the fixed-shift
-    softmax path, signed gamma / wide beta the per-row max path; dgamma/dbeta outputs on."""
+    softmax path, signed gamma / wide beta the per-row max path; with and without the
+    dgamma/dbeta accumulators, 4 / 8 columns per thread, whole and ragged rows."""
     from b200 import _lib as L
     from b200 import ops
     from oracle import evaluator as O
@@ -327,8 +331,9 @@ def test_rowfused_kernel_both_softmax_paths(C, path):
     k, c_ = np.sqrt(2 / np.pi), 0.044715
     t = np.tanh(k * (p + c_ * p**3))
     dp = dg * (0.5 * (1 + t) + 0.5 * p * (1 - t * t) * k * (1 + 3 * c_ * p * p))
-    refs = {"y": y, "dx": dp * a, "da": (dp * x).sum(0), "db": dp.sum(0),
-            "dgamma": O.execute_op("LayerNormGammaGrad", dn, g, eps=1e-5), "dbeta": dn.sum(0)}
+    refs = {"y": y, "dx": dp * a, "da": (dp * x).sum(0), "db": dp.sum(0)}
+    if gb:
+        refs.update({"dgamma": O.execute_op("LayerNormGammaGrad", dn, g, eps=1e-5), "dbeta": dn.sum(0)})
     dev = "cuda"
     out = {k_: torch.empty(R, C, device=dev) for k_ in ("y", "dx")}
     out.update({k_: torch.empty(C, device=dev) for k_ in ("da", "db", "dgamma", "dbeta")})
@@ -337,14 +342,58 @@ def test_rowfused_kernel_both_softmax_paths(C, path):
     ws = torch.empty(wsb, dtype=torch.uint8, device=dev)
     ins = [T(v) for v in (x, a, b, gamma, beta, cot)]
     L.call("b200_rowfused_fwd_bwd", *[v.data_ptr() for v in ins], out["y"].data_ptr(), am.data_ptr(), out["dx"].data_ptr(),
-           out["da"].data_ptr(), out["db"].data_ptr(), out["dgamma"].data_ptr(), out["dbeta"].data_ptr(), R, C, 1e-5,
-           ws.data_ptr(), wsb, ops.stream_ptr())
+           out["da"].data_ptr(), out["db"].data_ptr(), out["dgamma"].data_ptr() if gb else None,
+           out["dbeta"].data_ptr() if gb else None, R, C, 1e-5, ws.data_ptr(), wsb, ops.stream_ptr())
     for k_, ref in refs.items():
         got = to_np(out[k_])
         scale = float(np.abs(ref).max())
         np.testing.assert_allclose(got, ref, rtol=1e-4, atol=1e-4 * scale, err_msg=k_)
     ygot = to_np(out["y"])
     np.testing.assert_array_equal(to_np(am), np.argmax(ygot, axis=-1))
+
+
+@pytest.mark.parametrize("C", [4096, 3000])
+def test_rowfused_argmax_ties_and_misaligned_rows(C):
+    """argmax(y) takes the first of equal maxima: constant rows (every y equal -> 0), rows
+    with the same peak value planted at two columns, and the same inputs through pointers
+    offset by 4 bytes (scalar-load kernel) give identical results."""
+    from b200 import _lib as L
+    from b200 import ops
+
+    r = rng(21)
+    R = 64
+    x = r.standard_normal((R, C), dtype=np.float32)
+    x[0:4] = 0.25                            # constant rows
+    for i in range(4, 16):                   # equal peak at two columns
+        j1, j2 = sorted(r.choice(C, 2, replace=False))
+        x[i, j1] = x[i, j2] = 9.0
+    a, b = np.ones(C, np.float32), np.zeros(C, np.float32)
+    gamma, beta = np.ones(C, np.float32), np.zeros(C, np.float32)
+    cot = r.standard_normal((R, C), dtype=np.float32)
+
+    def run(offset):
+        def dev(v):
+            flat = torch.zeros(v.size + offset, dtype=torch.float32, device="cuda")
+            flat[offset:] = torch.from_numpy(np.ascontiguousarray(v).reshape(-1)).cuda()
+            return flat[offset:].view(v.shape)
+        ins = [dev(v) for v in (x, a, b, gamma, beta, cot)]
+        y, dx = dev(np.zeros((R, C), np.float32)), dev(np.zeros((R, C), np.float32))
+        da, db = torch.empty(C, device="cuda"), torch.empty(C, device="cuda")
+        am = torch.empty(R, dtype=torch.int64, device="cuda")
+        wsb = int(L.lib().b200_rowfused_workspace_bytes(R, C))
+        ws = torch.empty(wsb, dtype=torch.uint8, device="cuda")
+        L.call("b200_rowfused_fwd_bwd", *[v.data_ptr() for v in ins], y.data_ptr(), am.data_ptr(), dx.data_ptr(),
+               da.data_ptr(), db.data_ptr(), None, None, R, C, 1e-5, ws.data_ptr(), wsb, ops.stream_ptr())
+        torch.cuda.synchronize()
+        return to_np(y), to_np(am), to_np(dx), to_np(da), to_np(db)
+
+    y0, am0, dx0, da0, db0 = run(0)
+    np.testing.assert_array_equal(am0, np.argmax(y0, axis=-1))
+    assert (am0[0:4] == 0).all()
+    y1, am1, dx1, da1, db1 = run(1)
+    np.testing.assert_array_equal(am1, np.argmax(y1, axis=-1))
+    for got, ref in ((y1, y0), (dx1, dx0), (da1, da0), (db1, db0)):
+        np.testing.assert_allclose(got, ref, rtol=1e-4, atol=1e-4 * float(np.abs(ref).max()))
 
 
 @pytest.mark.parametrize("N,C,H,O,k,stride,padding", [(2, 3, 32, 64, 3, 1, "VALID"), (3, 64, 30, 64, 3, 2, "VALID"),
