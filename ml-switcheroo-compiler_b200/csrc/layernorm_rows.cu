@@ -306,15 +306,33 @@ __global__ void __launch_bounds__(WARPS * 32) ln_bwd_warp_kernel(const float* __
   }
 }
 
-__global__ void ln_colsum_kernel(const float* __restrict__ part, float* __restrict__ dg, float* __restrict__ db, int64_t G,
-                                 int64_t cols) {
-  const int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x;
-  if (i >= 2 * cols) return;
-  const int64_t which = i / cols, col = i % cols;
+// part[g][2][cols] -> (dgamma, dbeta): entry i of the 2 cols outputs is the sum over g in a
+// fixed order (deterministic): warp w of a block adds g = w, w + 8, ... in increasing g for
+// 32 adjacent entries, then the 8 warp sums are added in warp order.
+constexpr int LN_CS_WARPS = 8;
+__global__ void __launch_bounds__(32 * LN_CS_WARPS) ln_colsum_kernel(const float* __restrict__ part, float* __restrict__ dg,
+                                                             float* __restrict__ db, int64_t G, int64_t cols) {
+  __shared__ float sh[LN_CS_WARPS][33];
+  const int lane = threadIdx.x & 31, w = threadIdx.x >> 5;
+  const int64_t i = (int64_t)blockIdx.x * 32 + lane;
+  const bool live = i < 2 * cols;
   float acc = 0.f;
-  for (int64_t g = 0; g < G; ++g) acc += part[(g * 2 + which) * cols + col];
-  if (which == 0 && dg) dg[col] = acc;
-  if (which == 1 && db) db[col] = acc;
+  if (live) {
+#pragma unroll 4
+    for (int64_t g = w; g < G; g += LN_CS_WARPS) acc += __ldg(part + g * 2 * cols + i);
+  }
+  sh[w][lane] = acc;
+  __syncthreads();
+  if (w == 0 && live) {
+    float t = sh[0][lane];
+#pragma unroll
+    for (int k = 1; k < LN_CS_WARPS; ++k) t += sh[k][lane];
+    if (i < cols) {
+      if (dg) dg[i] = t;
+    } else if (db) {
+      db[i - cols] = t;
+    }
+  }
 }
 
 inline int64_t ln_bwd_grid(int64_t rows) {
@@ -444,6 +462,6 @@ extern "C" int b200_layernorm_bwd_rows(const float* dy, const float* x, const fl
   int rc = check_launch("layernorm_bwd_rows");
   if (rc) return rc;
   if (!dgamma && !dbeta) return B200_OK;
-  ln_colsum_kernel<<<(unsigned)ceil_div(2 * cols, (int64_t)256), 256, 0, s>>>(part, dgamma, dbeta, G, cols);
+  ln_colsum_kernel<<<(unsigned)ceil_div(2 * cols, (int64_t)32), 32 * LN_CS_WARPS, 0, s>>>(part, dgamma, dbeta, G, cols);
   return check_launch("layernorm_bwd_rows(colsum)");
 }
