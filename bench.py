@@ -476,9 +476,9 @@ def main() -> None:
     ap.add_argument("--impl", default="b200", choices=["b200", "reference"])
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline leg")
     ap.add_argument("--no-e2e", action="store_true")
-    # dram__bytes_read.sum + dram__bytes_write.sum of one rowfused_kernel launch at
+    # dram__bytes_read.sum + dram__bytes_write.sum of one rowfused2_kernel launch at
     # [8192, 4096] (ncu --set full capture summarised in profiles/rowfused_kernel_8192x4096.md)
-    ap.add_argument("--traffic", type=float, default=489089024.0, help="ncu dram bytes per launch of the dominant kernel")
+    ap.add_argument("--traffic", type=float, default=488077312.0, help="ncu dram bytes per launch of the dominant kernel")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3
