@@ -266,9 +266,13 @@ def run_gpu(args) -> None:
             sync([out[gid] for gid in grad_ids])
 
     stream = torch.cuda.current_stream()
-    for _ in range(args.warmup):
+    sync_launches = 0
+    for i in range(args.warmup):
         out = cg(dinputs)
+        n0 = _lib.launch_count()
         allreduce()
+        if i == args.warmup - 1:
+            sync_launches = int(_lib.launch_count() - n0)  # our own kernels in the gradient exchange
     torch.cuda.synchronize()
     if dist is not None:
         dist.barrier()
@@ -284,6 +288,7 @@ def run_gpu(args) -> None:
     if dist is not None:
         dist.barrier()
     ms = ev0.elapsed_time(ev1)
+    sync.check()  # a peer wait that gave up raises here
     t = torch.tensor([ms], device=dev)
     if dist is not None:
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
@@ -387,9 +392,10 @@ def run_gpu(args) -> None:
             "config": {"workload": spec["desc"], "graph": spec["dp_graphs"][world] if strong else spec["graph"], "dims": g.meta["dims"],
                        "parallelism": f"dp{world}" if world > 1 else "single",
                        "l2": "inputs larger than the 126 MB L2 (no flush needed)" if args.workload in ("rowfused", "bmm") else "L2 not flushed",
-                       "replay": "CUDA graph of the fused plan"},
-            "gpu_launches": int(launches_per_step * args.steps),
-            "launches_per_step": launches_per_step,
+                       "replay": "CUDA graph of the fused plan",
+                       "grad_exchange": (("peer-memory kernel + " if sync.peer is not None else "") + "NCCL buckets") if world > 1 else None},
+            "gpu_launches": int((launches_per_step + sync_launches) * args.steps),
+            "launches_per_step": launches_per_step + sync_launches,
             "plan_steps": int(n_capture),
             "plan": plan.describe(),
             "clocks": clk.summary(),

@@ -366,6 +366,28 @@ int b200_conv2d_wgrad_tc(const float* x, const float* dy, float* dw, int64_t N, 
                          int64_t KH, int64_t KW, int64_t OH, int64_t OW, int64_t sh, int64_t sw, int64_t pt, int64_t pl,
                          void* workspace, size_t workspace_bytes, void* stream);
 
+
+/* All-reduce of n fp32 values across `world` ranks through peer-mapped memory, for the
+ * buckets of small gradients that the reference exchanges with its AllReduce node
+ * (numpy/eager/distributed.py:205-225, all_reduce_ring :105). One kernel: this rank's
+ * values go into its slot of a symmetric buffer, a flag goes into every peer's signal
+ * pad, the kernel waits (at most spin_limit polls per flag) for every peer's flag, and
+ * then adds all ranks' slots in rank order (NVLink P2P loads), times `scale` (1 for a
+ * sum, 1/world for a mean). The result is identical on every rank.
+ *   slots_dev: device array of `world` pointers, rank q's symmetric buffer of >= 2 n floats
+ *   pads_dev:  device array of `world` pointers, rank q's signal pad of >= blocks * world
+ *              uint32, zero before the first call
+ *   epoch:     this rank's per-block call counters (`blocks` uint32, zero at start); every
+ *              rank must make the same calls with the same n and blocks
+ *   status:    device int, set to B200_ERR_TIMEOUT when a peer's flag did not arrive (the
+ *              values of that block are then left unchanged)
+ * b200_peer_allreduce_blocks gives the number of blocks for n values and a pad size. */
+int b200_peer_allreduce_blocks(int64_t n, int world, size_t pad_bytes);
+int b200_peer_allreduce_f32(float* data, int64_t n, const void* slots_dev, const void* pads_dev, int rank, int world,
+                            unsigned int* epoch, int* status, int64_t spin_limit, float scale, int blocks, void* stream);
+/* cudaMemsetAsync of a device range (clears a signal pad before its first use). */
+int b200_memset_async(void* p, int value, size_t bytes, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

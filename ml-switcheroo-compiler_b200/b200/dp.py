@@ -13,11 +13,15 @@ combined:
   the global mean is the average of the shard means.
 
 Small gradients are packed into buckets (contiguous device-to-device copies, no compute)
-so a step issues a few large collectives instead of one per parameter.
+so a step issues a few large collectives instead of one per parameter. On GPUs, fp32
+buckets up to ``peer_below`` bytes skip NCCL: ``PeerAllReduce`` adds the ranks' values
+with one kernel over peer-mapped memory (NVLink P2P loads), where a collective's fixed
+latency would dominate (the fused row graph's column gradients are 32 KB).
 """
 
 from __future__ import annotations
 
+import os
 from typing import Sequence
 
 import torch
@@ -32,21 +36,97 @@ def shard_rows(n: int, rank: int, world: int) -> slice:
     return slice(lo, lo + per + (1 if rank < rem else 0))
 
 
+class PeerAllReduce:
+    """All-reduce of small fp32 buffers through a symmetric buffer that every rank maps
+    (``b200_peer_allreduce_f32``): one kernel copies this rank's values into its slot,
+    flags every peer, waits for every peer's flag (bounded), and adds the ranks' slots in
+    rank order, so all ranks hold bit-identical sums.
+
+    Construction is collective (symmetric-memory rendezvous on ``group``). Every rank must
+    then make the same calls with the same sizes. A wait that gives up sets a status that
+    ``check()`` turns into ``TimeoutError``.
+    """
+
+    SPIN_LIMIT = 1 << 24  # polls per flag, each after a ~128 ns sleep: seconds, not forever
+
+    def __init__(self, group, max_numel: int, device: torch.device) -> None:
+        import torch.distributed as dist
+
+        # plain peer mappings only: no NVLink multicast object behind the buffer
+        os.environ.setdefault("TORCH_SYMM_MEM_DISABLE_MULTICAST", "1")
+        import torch.distributed._symmetric_memory as symm
+
+        from . import _lib as L
+        from . import ops
+
+        self.group, self.device = group, device
+        self.world, self.rank = dist.get_world_size(group), dist.get_rank(group)
+        self.max_numel = int(max_numel)
+        self.buf = symm.empty(2 * self.max_numel, dtype=torch.float32, device=device)
+        self.handle = symm.rendezvous(self.buf, group if group is not None else dist.group.WORLD)
+        self.pad_bytes = int(self.handle.signal_pad_size)
+        self.epoch = torch.zeros(64, dtype=torch.int32, device=device)
+        self.status = torch.zeros(1, dtype=torch.int32, device=device)
+        L.call("b200_memset_async", int(self.handle.signal_pad_ptrs[self.handle.rank]), 0, self.pad_bytes, ops.stream_ptr())
+        torch.cuda.synchronize(device)
+        dist.barrier(group)  # every pad is clear before any rank raises a flag
+
+    def __call__(self, flat: torch.Tensor, scale: float = 1.0) -> None:
+        from . import _lib as L
+        from . import ops
+
+        if flat.dtype != torch.float32 or not flat.is_contiguous() or flat.numel() > self.max_numel:
+            raise ValueError("PeerAllReduce takes contiguous fp32 buffers of at most max_numel values")
+        n = flat.numel()
+        blocks = int(L.lib().b200_peer_allreduce_blocks(n, self.world, self.pad_bytes))
+        L.call("b200_peer_allreduce_f32", flat.data_ptr(), n, int(self.handle.buffer_ptrs_dev),
+               int(self.handle.signal_pad_ptrs_dev), self.rank, self.world, self.epoch.data_ptr(),
+               self.status.data_ptr(), self.SPIN_LIMIT, float(scale), blocks, ops.stream_ptr())
+
+    def check(self) -> None:
+        """Raise TimeoutError if a wait for a peer gave up since construction."""
+        code = int(self.status.item())
+        if code:
+            raise TimeoutError(f"peer all-reduce: a peer's flag did not arrive (status {code})")
+
+
 class GradAllReduce:
     """In-place all-reduce of a list of gradient tensors across the process group."""
 
-    def __init__(self, op: str = "sum", group=None, bucket_bytes: int = 32 << 20, pack_below: int = 4 << 20) -> None:
+    def __init__(self, op: str = "sum", group=None, bucket_bytes: int = 32 << 20, pack_below: int = 4 << 20,
+                 peer_below: int = 1 << 20) -> None:
         if op not in ("sum", "mean"):
             raise ValueError(f"op must be 'sum' or 'mean', not {op!r}")
         self.op, self.group = op, group
         self.bucket_bytes, self.pack_below = bucket_bytes, pack_below
+        self.peer_below = peer_below if os.environ.get("B200_PEER_ALLREDUCE", "1") != "0" else 0
         self._flat: dict[tuple, torch.Tensor] = {}
+        self.peer: PeerAllReduce | None = None
+
+    def _peer_for(self, t: torch.Tensor) -> PeerAllReduce | None:
+        import torch.distributed as dist
+
+        if (not t.is_cuda or t.dtype != torch.float32 or not t.is_contiguous()
+                or t.numel() * 4 > self.peer_below or dist.get_backend(self.group) != "nccl"):
+            return None
+        if self.peer is None:
+            self.peer = PeerAllReduce(self.group, self.peer_below // 4, t.device)
+        return self.peer
+
+    def check(self) -> None:
+        """Raise if a peer-memory exchange gave up waiting for a peer."""
+        if self.peer is not None:
+            self.peer.check()
 
     def _reduce(self, t: torch.Tensor) -> None:
         import torch.distributed as dist
 
         world = dist.get_world_size(self.group)
         if world == 1:
+            return
+        peer = self._peer_for(t)
+        if peer is not None:
+            peer(t.reshape(-1), 1.0 / world if self.op == "mean" else 1.0)
             return
         if self.op == "mean" and dist.get_backend(self.group) == "nccl":
             dist.all_reduce(t, op=dist.ReduceOp.AVG, group=self.group)
