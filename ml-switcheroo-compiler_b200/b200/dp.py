@@ -42,8 +42,9 @@ class PeerAllReduce:
     flags every peer, waits for every peer's flag (bounded), and adds the ranks' slots in
     rank order, so all ranks hold bit-identical sums.
 
-    Construction is collective (symmetric-memory rendezvous on ``group``). Every rank must
-    then make the same calls with the same sizes. A wait that gives up sets a status that
+    Construction is collective (symmetric-memory rendezvous on ``group``) and must be
+    followed by one more collective on ``group`` before the first call, so that every pad
+    is clear. Every rank must then make the same calls with the same sizes. A wait that gives up sets a status that
     ``check()`` turns into ``TimeoutError``.
     """
 
@@ -69,7 +70,8 @@ class PeerAllReduce:
         self.status = torch.zeros(1, dtype=torch.int32, device=device)
         L.call("b200_memset_async", int(self.handle.signal_pad_ptrs[self.handle.rank]), 0, self.pad_bytes, ops.stream_ptr())
         torch.cuda.synchronize(device)
-        dist.barrier(group)  # every pad is clear before any rank raises a flag
+        # the first call must wait until every rank has cleared its pad: the caller follows
+        # construction with a collective on `group` (GradAllReduce agrees on success)
 
     def __call__(self, flat: torch.Tensor, scale: float = 1.0) -> None:
         from . import _lib as L
@@ -102,6 +104,7 @@ class GradAllReduce:
         self.peer_below = peer_below if os.environ.get("B200_PEER_ALLREDUCE", "1") != "0" else 0
         self._flat: dict[tuple, torch.Tensor] = {}
         self.peer: PeerAllReduce | None = None
+        self._peer_failed = False
 
     def _peer_for(self, t: torch.Tensor) -> PeerAllReduce | None:
         import torch.distributed as dist
@@ -109,8 +112,23 @@ class GradAllReduce:
         if (not t.is_cuda or t.dtype != torch.float32 or not t.is_contiguous()
                 or t.numel() * 4 > self.peer_below or dist.get_backend(self.group) != "nccl"):
             return None
-        if self.peer is None:
-            self.peer = PeerAllReduce(self.group, self.peer_below // 4, t.device)
+        if self.peer is None and not self._peer_failed:
+            # collective set-up; every rank reports success, and the peer path is used only
+            # when all ranks have it (otherwise every rank keeps NCCL for these buckets)
+            err = None
+            try:
+                peer = PeerAllReduce(self.group, self.peer_below // 4, t.device)
+            except Exception as e:  # noqa: BLE001 - reported below, ranks agree on the outcome
+                peer, err = None, e
+            ok = torch.tensor([0 if peer is None else 1], dtype=torch.int32, device=t.device)
+            dist.all_reduce(ok, op=dist.ReduceOp.MIN, group=self.group)
+            if int(ok.item()) == 1:
+                self.peer = peer
+            else:
+                self._peer_failed = True
+                import warnings
+
+                warnings.warn(f"peer-memory all-reduce unavailable on this group, NCCL only ({err!r})")
         return self.peer
 
     def check(self) -> None:
