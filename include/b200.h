@@ -388,6 +388,32 @@ int b200_peer_allreduce_f32(float* data, int64_t n, const void* slots_dev, const
 /* cudaMemsetAsync of a device range (clears a signal pad before its first use). */
 int b200_memset_async(void* p, int value, size_t bytes, void* stream);
 
+/* Optimizer update steps ApplyAdam (kind 0), ApplyAdagrad (1), ApplyFtrl (2), ApplyRMSProp
+ * (3), as the reference's numpy backend computes them (numpy/eager/optimizers_ops.py:11-103):
+ * its fixed hyperparameters, fp32, one IEEE rounding per operation in the same order, so the
+ * results are bit-identical to the reference's. `count` fp32 tensors in one launch per 128:
+ * host arrays of device pointers param[i], s1[i], s2[i] (the state arrays: Adam m, v;
+ * Adagrad accum, s2 unused and may be NULL; FTRL accum, linear; RMSProp ms, mom), grad[i],
+ * and the outputs, which may be the inputs themselves (in-place step); n[i] elements each.
+ * b200_optimizer_default_lr gives the numpy kernels' default lr of each kind. */
+double b200_optimizer_default_lr(int kind);
+int b200_apply_optimizer_f32(int kind, int count, const float* const* param, const float* const* s1, const float* const* s2,
+                             const float* const* grad, float* const* param_out, float* const* s1_out, float* const* s2_out,
+                             const int64_t* n, float lr, void* stream);
+
+/* b200_peer_allreduce_f32 followed, in the same kernel, by an optimizer step on the summed
+ * values (the reference's AllReduce node and then ApplyAdam / ApplyAdagrad / ApplyFtrl /
+ * ApplyRMSProp, numpy/eager/distributed.py:205-225 and numpy/eager/optimizers_ops.py:11-103):
+ * the n values are the gradients of `count` (<= 64) parameter tensors laid end to end,
+ * tensor j covering [offsets[j], offsets[j + 1]) with offsets[0] = 0, offsets[count] = n.
+ * Each summed element also updates param[j], s1[j] (and s2[j]; Adagrad has none) in
+ * place, bit-identically to b200_apply_optimizer_f32; `data` receives the summed values.
+ * offsets, param, s1, s2 are host arrays (device pointers). */
+int b200_peer_allreduce_apply_f32(float* data, int64_t n, const void* slots_dev, const void* pads_dev, int rank, int world,
+                                  unsigned int* epoch, int* status, int64_t spin_limit, float scale, int blocks, int kind,
+                                  int count, const int64_t* offsets, float* const* param, float* const* s1, float* const* s2,
+                                  float lr, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -73,7 +73,15 @@ class PeerAllReduce:
         # the first call must wait until every rank has cleared its pad: the caller follows
         # construction with a collective on `group` (GradAllReduce agrees on success)
 
-    def __call__(self, flat: torch.Tensor, scale: float = 1.0) -> None:
+    MAX_SEGMENTS = 64  # parameter tensors of one fused optimizer epilogue
+
+    def __call__(self, flat: torch.Tensor, scale: float = 1.0, step: "OptimizerStep | None" = None,
+                 indices: Sequence[int] = ()) -> None:
+        """Sum ``flat`` over the ranks (times ``scale``). With ``step``, the same kernel then
+        applies ``step``'s optimizer to its parameters ``indices``, whose gradients are laid
+        end to end in ``flat``."""
+        import ctypes as C
+
         from . import _lib as L
         from . import ops
 
@@ -81,9 +89,23 @@ class PeerAllReduce:
             raise ValueError("PeerAllReduce takes contiguous fp32 buffers of at most max_numel values")
         n = flat.numel()
         blocks = int(L.lib().b200_peer_allreduce_blocks(n, self.world, self.pad_bytes))
-        L.call("b200_peer_allreduce_f32", flat.data_ptr(), n, int(self.handle.buffer_ptrs_dev),
-               int(self.handle.signal_pad_ptrs_dev), self.rank, self.world, self.epoch.data_ptr(),
-               self.status.data_ptr(), self.SPIN_LIMIT, float(scale), blocks, ops.stream_ptr())
+        head = (flat.data_ptr(), n, int(self.handle.buffer_ptrs_dev), int(self.handle.signal_pad_ptrs_dev), self.rank,
+                self.world, self.epoch.data_ptr(), self.status.data_ptr(), self.SPIN_LIMIT, float(scale), blocks)
+        if step is None:
+            L.call("b200_peer_allreduce_f32", *head, ops.stream_ptr())
+            return
+        if not 1 <= len(indices) <= self.MAX_SEGMENTS:
+            raise ValueError(f"a fused optimizer epilogue takes 1..{self.MAX_SEGMENTS} tensors")
+        offs = [0]
+        for i in indices:
+            offs.append(offs[-1] + step.params[i].numel())
+        if offs[-1] != n:
+            raise ValueError("the gradients of `indices` must fill `flat` exactly")
+        P = C.c_void_p * len(indices)
+        s2 = P(*[step.states[i][1].data_ptr() for i in indices]) if step.nstates == 2 else None
+        L.call("b200_peer_allreduce_apply_f32", *head, step.kind, len(indices), (C.c_int64 * len(offs))(*offs),
+               P(*[step.params[i].data_ptr() for i in indices]), P(*[step.states[i][0].data_ptr() for i in indices]), s2,
+               float(step.lr), ops.stream_ptr())
 
     def check(self) -> None:
         """Raise TimeoutError if a wait for a peer gave up since construction."""
@@ -92,8 +114,42 @@ class PeerAllReduce:
             raise TimeoutError(f"peer all-reduce: a peer's flag did not arrive (status {code})")
 
 
+class OptimizerStep:
+    """Device optimizer for a list of fp32 parameter tensors, updated in place: ApplyAdam,
+    ApplyAdagrad, ApplyFtrl or ApplyRMSProp with the reference numpy backend's formulas
+    (``numpy/eager/optimizers_ops.py``), states starting at zero. ``GradAllReduce(grads,
+    step)`` applies it after the gradient exchange, fused into the peer-memory kernel for
+    the buckets that take that path."""
+
+    def __init__(self, op: str, params: Sequence[torch.Tensor], lr: float | None = None) -> None:
+        from . import _lib as L
+        from . import ops
+
+        if op not in ops._OPT_KIND:
+            raise ValueError(f"unknown optimizer op {op!r}")
+        for p in params:
+            if p.dtype != torch.float32 or not p.is_cuda or not p.is_contiguous():
+                raise ValueError("OptimizerStep updates contiguous fp32 CUDA tensors in place")
+        self.op, self.kind = op, ops._OPT_KIND[op]
+        self.lr = float(L.lib().b200_optimizer_default_lr(self.kind)) if lr is None else float(lr)
+        self.params = list(params)
+        self.nstates = 1 if op == "ApplyAdagrad" else 2
+        self.states = [tuple(torch.zeros_like(p) for _ in range(self.nstates)) for p in self.params]
+
+    def apply(self, indices: Sequence[int], grads: Sequence[torch.Tensor]) -> None:
+        """One launch: parameters ``indices`` take one step with ``grads`` (same order)."""
+        from . import ops
+
+        if not indices:
+            return
+        ps = [self.params[i] for i in indices]
+        sts = [self.states[i] for i in indices]
+        ops.apply_optimizer(self.op, ps, sts, list(grads), lr=self.lr, out=[(p,) + st for p, st in zip(ps, sts)])
+
+
 class GradAllReduce:
-    """In-place all-reduce of a list of gradient tensors across the process group."""
+    """In-place all-reduce of a list of gradient tensors across the process group, and,
+    when given an ``OptimizerStep`` over the matching parameters, the optimizer step."""
 
     def __init__(self, op: str = "sum", group=None, bucket_bytes: int = 32 << 20, pack_below: int = 4 << 20,
                  peer_below: int = 1 << 20) -> None:
@@ -173,10 +229,22 @@ class GradAllReduce:
             out.append(cur)
         return out
 
-    def __call__(self, grads: Sequence[torch.Tensor]) -> None:
+    def __call__(self, grads: Sequence[torch.Tensor], step: OptimizerStep | None = None) -> None:
+        import torch.distributed as dist
+
+        if step is not None and len(step.params) != len(grads):
+            raise ValueError("the optimizer step must cover the same tensors as the gradients")
+        world = dist.get_world_size(self.group)
         for b in self.buckets(grads):
             if len(b) == 1:
-                self._reduce(grads[b[0]])
+                g = grads[b[0]]
+                peer = self._peer_for(g) if world > 1 and step is not None else None
+                if peer is not None:  # exchange and step in one kernel
+                    peer(g.reshape(-1), 1.0 / world if self.op == "mean" else 1.0, step, b)
+                    continue
+                self._reduce(g)
+                if step is not None:
+                    step.apply(b, [g])
                 continue
             ts = [grads[i] for i in b]
             n = sum(t.numel() for t in ts)
@@ -189,8 +257,15 @@ class GradAllReduce:
             for t in ts:  # contiguous copies: device-to-device memcpy, no kernel
                 flat[off : off + t.numel()].copy_(t.reshape(-1))
                 off += t.numel()
-            self._reduce(flat)
+            peer = (self._peer_for(flat) if world > 1 and step is not None and len(b) <= PeerAllReduce.MAX_SEGMENTS
+                    else None)
+            if peer is not None:
+                peer(flat, 1.0 / world if self.op == "mean" else 1.0, step, b)
+            else:
+                self._reduce(flat)
             off = 0
             for t in ts:
                 t.reshape(-1).copy_(flat[off : off + t.numel()])
                 off += t.numel()
+            if step is not None and peer is None:
+                step.apply(b, ts)

@@ -1033,7 +1033,55 @@ def op_all_reduce(x, op_type="sum", **_):  # numpy/eager/distributed.py:205-225
     return x
 
 
+# ---- optimizer update steps ---------------------------------------------------------
+_OPT_KIND = {"ApplyAdam": 0, "ApplyAdagrad": 1, "ApplyFtrl": 2, "ApplyRMSProp": 3}
+
+
+def apply_optimizer(op: str, params, states, grads, lr=None, out=None):
+    """One launch per 128 tensors of ``op`` (ApplyAdam / ApplyAdagrad / ApplyFtrl /
+    ApplyRMSProp, the numpy backend's formulas, ``numpy/eager/optimizers_ops.py``).
+
+    ``params`` / ``grads`` are lists of fp32 tensors, ``states`` a list of per-tensor
+    tuples of state tensors (Adam: m, v; Adagrad: accum; FTRL: accum, linear; RMSProp: ms,
+    mom). Results go to ``out`` (per-tensor tuples of param, states; the inputs themselves
+    for an in-place step) or to new tensors. Returns the per-tensor result tuples."""
+    kind = _OPT_KIND[op]
+    if lr is None:
+        lr = float(L.lib().b200_optimizer_default_lr(kind))
+    nst = 1 if kind == 1 else 2
+    ps = [contiguous(cast(to_device(p), torch.float32)) for p in params]
+    gs = [contiguous(cast(to_device(g), torch.float32)) for g in grads]
+    ss = [[contiguous(cast(to_device(x), torch.float32)) for x in st] for st in states]
+    for p, g, st in zip(ps, gs, ss):
+        if len(st) != nst or g.shape != p.shape or any(x.shape != p.shape for x in st):
+            raise ValueError(f"{op}: param, states and grad must have one shape ({nst} state arrays)")
+    if out is None:
+        out = [tuple(torch.empty_like(p) for _ in range(1 + nst)) for p in ps]
+    n = len(ps)
+    P = C.c_void_p * n
+    ptr = lambda ts: P(*[t.data_ptr() for t in ts])  # noqa: E731
+    s2 = ptr([st[1] for st in ss]) if nst == 2 else None
+    s2o = ptr([o[2] for o in out]) if nst == 2 else None
+    sizes = (C.c_int64 * n)(*[p.numel() for p in ps])
+    L.call("b200_apply_optimizer_f32", kind, n, ptr(ps), ptr([st[0] for st in ss]), s2, ptr(gs), ptr([o[0] for o in out]),
+           ptr([o[1] for o in out]), s2o, sizes, float(lr), stream_ptr())
+    return out
+
+
+def _opt_op(op: str):
+    def run(param, *rest, lr=None, **_):
+        states, grad = rest[:-1], rest[-1]
+        return tuple(apply_optimizer(op, [param], [states], [grad], lr=lr)[0])
+
+    run.__name__ = "op_" + op
+    return run
+
+
 OPS: dict[str, Any] = {
+    "ApplyAdam": _opt_op("ApplyAdam"),  # numpy/eager/optimizers_ops.py:11-35
+    "ApplyAdagrad": _opt_op("ApplyAdagrad"),  # :38-59
+    "ApplyFtrl": _opt_op("ApplyFtrl"),  # :62-83
+    "ApplyRMSProp": _opt_op("ApplyRMSProp"),  # :86-103
     "Add": op_add,
     "Subtract": op_subtract,
     "Multiply": op_multiply,

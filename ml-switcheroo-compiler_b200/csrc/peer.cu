@@ -18,11 +18,25 @@
 #include <algorithm>
 
 #include "common.cuh"
+#include "optim_math.cuh"
 
 namespace b200 {
 namespace peer {
 
 constexpr int PT = 512;  // threads per block
+constexpr int MAXS = 64;  // parameter segments of a fused optimizer epilogue
+
+// Optional optimizer epilogue: the summed values are the gradients of `count` parameter
+// tensors laid end to end, segment j covering [off[j], off[j + 1]); each summed element
+// also updates its parameter and state elements in place.
+struct Segs {
+  int count, kind;
+  opt::Consts k;
+  int64_t off[MAXS + 1];
+  float* p[MAXS];
+  float* s1[MAXS];
+  float* s2[MAXS];
+};
 
 __device__ __forceinline__ void st_release_sys(uint32_t* p, uint32_t v) {
   asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
@@ -36,7 +50,8 @@ __device__ __forceinline__ uint32_t ld_acquire_sys(const uint32_t* p) {
 __global__ void __launch_bounds__(PT) peer_allreduce_kernel(float* __restrict__ data, int64_t n, int64_t chunk,
                                                             const uint64_t* __restrict__ slots, const uint64_t* __restrict__ pads,
                                                             int rank, int world, uint32_t* __restrict__ epoch,
-                                                            int* __restrict__ status, int64_t spin_limit, float scale) {
+                                                            int* __restrict__ status, int64_t spin_limit, float scale,
+                                                            const __grid_constant__ Segs S) {
   __shared__ int s_err;
   const int b = blockIdx.x, tid = threadIdx.x;
   const int64_t lo = (int64_t)b * chunk, hi = min(n, lo + chunk);
@@ -68,7 +83,25 @@ __global__ void __launch_bounds__(PT) peer_allreduce_kernel(float* __restrict__ 
     float s = 0.f;
 #pragma unroll 8
     for (int q = 0; q < world; ++q) s += reinterpret_cast<const float*>(slots[q])[off + i];
-    data[i] = s * scale;
+    const float g = s * scale;
+    data[i] = g;
+    if (S.count > 0) {  // the parameter segment of element i (binary search), then its update
+      int lo_s = 0, hi_s = S.count - 1;
+      while (lo_s < hi_s) {
+        const int mid = (lo_s + hi_s + 1) >> 1;
+        if (S.off[mid] <= i) lo_s = mid;
+        else hi_s = mid - 1;
+      }
+      const int64_t j = i - S.off[lo_s];
+      float* p = S.p[lo_s];
+      float* a = S.s1[lo_s];
+      float* b = S.s2[lo_s];
+      float po, ao, bo;
+      opt::update(S.kind, S.k, p[j], a[j], b ? b[j] : 0.f, g, po, ao, bo);
+      p[j] = po;
+      a[j] = ao;
+      if (b) b[j] = bo;
+    }
   }
   if (tid == 0) epoch[b] = e;
 }
@@ -85,9 +118,8 @@ extern "C" int b200_peer_allreduce_blocks(int64_t n, int world, size_t pad_bytes
   return (int)std::max<int64_t>(1, std::min<int64_t>(std::min<int64_t>(by_size, by_pad), 64));
 }
 
-extern "C" int b200_peer_allreduce_f32(float* data, int64_t n, const void* slots_dev, const void* pads_dev, int rank, int world,
-                                       unsigned int* epoch, int* status, int64_t spin_limit, float scale, int blocks,
-                                       void* stream) {
+static int peer_launch(float* data, int64_t n, const void* slots_dev, const void* pads_dev, int rank, int world, unsigned int* epoch,
+                       int* status, int64_t spin_limit, float scale, int blocks, const peer::Segs& S, void* stream) {
   B200_REQUIRE(data && slots_dev && pads_dev && epoch && status, "peer_allreduce: null pointer");
   B200_REQUIRE(n >= 0 && world >= 1 && world <= 64 && rank >= 0 && rank < world, "peer_allreduce: bad rank %d / world %d", rank,
                world);
@@ -97,8 +129,42 @@ extern "C" int b200_peer_allreduce_f32(float* data, int64_t n, const void* slots
   const int64_t chunk = ceil_div(n, (int64_t)blocks);
   peer::peer_allreduce_kernel<<<blocks, peer::PT, 0, as_stream(stream)>>>(
       data, n, chunk, reinterpret_cast<const uint64_t*>(slots_dev), reinterpret_cast<const uint64_t*>(pads_dev), rank, world,
-      reinterpret_cast<uint32_t*>(epoch), status, spin_limit, scale);
+      reinterpret_cast<uint32_t*>(epoch), status, spin_limit, scale, S);
   return check_launch("peer_allreduce");
+}
+
+extern "C" int b200_peer_allreduce_f32(float* data, int64_t n, const void* slots_dev, const void* pads_dev, int rank, int world,
+                                       unsigned int* epoch, int* status, int64_t spin_limit, float scale, int blocks,
+                                       void* stream) {
+  peer::Segs S;
+  S.count = 0;
+  return peer_launch(data, n, slots_dev, pads_dev, rank, world, epoch, status, spin_limit, scale, blocks, S, stream);
+}
+
+extern "C" int b200_peer_allreduce_apply_f32(float* data, int64_t n, const void* slots_dev, const void* pads_dev, int rank,
+                                             int world, unsigned int* epoch, int* status, int64_t spin_limit, float scale,
+                                             int blocks, int kind, int count, const int64_t* offsets, float* const* param,
+                                             float* const* s1, float* const* s2, float lr, void* stream) {
+  B200_REQUIRE(kind >= 0 && kind <= 3, "peer_allreduce_apply: kind %d not in [0, 3]", kind);
+  B200_REQUIRE(count >= 1 && count <= peer::MAXS, "peer_allreduce_apply: %d segments not in [1, %d]", count, peer::MAXS);
+  B200_REQUIRE(offsets && param && s1, "peer_allreduce_apply: null table");
+  B200_REQUIRE(offsets[0] == 0 && offsets[count] == n, "peer_allreduce_apply: segments must cover [0, n) exactly");
+  const bool two = kind != opt::ADAGRAD;
+  B200_REQUIRE(!two || s2, "peer_allreduce_apply: this optimizer has a second state array");
+  peer::Segs S;
+  S.count = count;
+  S.kind = kind;
+  S.k = opt::consts_for(kind, lr);
+  for (int j = 0; j < count; ++j) {
+    B200_REQUIRE(offsets[j + 1] >= offsets[j], "peer_allreduce_apply: offsets must not decrease");
+    B200_REQUIRE(param[j] && s1[j] && (!two || s2[j]), "peer_allreduce_apply: null pointer for segment %d", j);
+    S.off[j] = offsets[j];
+    S.p[j] = param[j];
+    S.s1[j] = s1[j];
+    S.s2[j] = two ? s2[j] : nullptr;
+  }
+  S.off[count] = offsets[count];
+  return peer_launch(data, n, slots_dev, pads_dev, rank, world, epoch, status, spin_limit, scale, blocks, S, stream);
 }
 
 extern "C" int b200_memset_async(void* p, int value, size_t bytes, void* stream) {

@@ -334,7 +334,56 @@ def _op_conv2d_bias_grad(d_out, **_):
     return np.sum(d_out, axis=(0, 2, 3))
 
 
+# ---- optimizer update steps (backends/numpy/eager/optimizers_ops.py) ----------------
+# The numpy backend's own registry wins over the generic one for these names
+# (numpy/eager/__init__.py:110-115), so its fixed hyperparameters apply: Adam with
+# beta1 0.9, beta2 0.999, eps 1e-8 and no bias correction; Adagrad eps 1e-10; RMSProp rho
+# 0.9, momentum 0, eps 1e-8; FTRL in its simplified numpy form. `lr` is a Python float,
+# so numpy computes in the arrays' fp32 with one rounding per operation.
+def _op_apply_adam(param, m, v, grad, lr=0.001, **_):
+    # numpy/eager/optimizers_ops.py:11-35
+    p, m_, v_, g = np.asarray(param), np.asarray(m), np.asarray(v), np.asarray(grad)
+    beta1, beta2, eps = 0.9, 0.999, 1e-8
+    m_new = m_ * beta1 + g * (1.0 - beta1)
+    v_new = v_ * beta2 + (g * g) * (1.0 - beta2)
+    p_new = p - float(lr) * (m_new / (np.sqrt(v_new) + eps))
+    return p_new, m_new, v_new
+
+
+def _op_apply_adagrad(param, accum, grad, lr=0.01, **_):
+    # numpy/eager/optimizers_ops.py:38-59
+    p, a, g = np.asarray(param), np.asarray(accum), np.asarray(grad)
+    a_new = a + g * g
+    p_new = p - float(lr) * (g / (np.sqrt(a_new) + 1e-10))
+    return p_new, a_new
+
+
+def _op_apply_ftrl(param, accum, linear, grad, lr=0.001, **_):
+    # numpy/eager/optimizers_ops.py:62-83
+    p, a, lin, g = np.asarray(param), np.asarray(accum), np.asarray(linear), np.asarray(grad)
+    lr = float(lr)
+    a_new = a + g * g
+    sigma = (np.sqrt(a_new) - np.sqrt(a)) / lr
+    l_new = lin - g + sigma * p
+    p_new = p - lr * g
+    return p_new, a_new, l_new
+
+
+def _op_apply_rmsprop(param, ms, mom, grad, lr=0.001, **_):
+    # numpy/eager/optimizers_ops.py:86-103
+    p, m, mo, g = np.asarray(param), np.asarray(ms), np.asarray(mom), np.asarray(grad)
+    rho, momentum, eps = 0.9, 0.0, 1e-8
+    m_new = m * rho + (g * g) * (1.0 - rho)
+    mo_new = mo * momentum + g / (np.sqrt(m_new) + eps)
+    p_new = p - float(lr) * mo_new
+    return p_new, m_new, mo_new
+
+
 OPS: dict[str, Any] = {
+    "ApplyAdam": _op_apply_adam,
+    "ApplyAdagrad": _op_apply_adagrad,
+    "ApplyFtrl": _op_apply_ftrl,
+    "ApplyRMSProp": _op_apply_rmsprop,
     "Matmul": _op_matmul,
     "BatchMatMul": _op_matmul,
     "Add": lambda a, b, **_: np.add(a, b),  # backends/numpy/eager/math_binary.py:9-20

@@ -14,6 +14,7 @@ import os
 import queue as queue_mod
 import socket
 
+import numpy as np
 import pytest
 import torch
 
@@ -65,6 +66,54 @@ def test_peer_allreduce_world1_and_emulated_pair(cuda, n, blocks):
     assert pad1[0::2].tolist() == [1] * blocks  # and its flags in the peer's pad
 
 
+@pytest.mark.parametrize("op", ["ApplyAdam", "ApplyAdagrad", "ApplyFtrl", "ApplyRMSProp"])
+def test_peer_allreduce_fused_optimizer_step_emulated_pair(cuda, op):
+    """Exchange plus optimizer epilogue in one kernel: two parameter tensors laid end to
+    end, the peer's gradients planted in its slot; the summed gradients and the updated
+    parameters / states equal the oracle's step on the summed gradients bit for bit."""
+    import ctypes as C
+
+    from b200 import _lib as L
+    from b200 import ops
+    from oracle import evaluator as O
+
+    rng = np.random.default_rng(9)
+    sizes = [1000, 3333]
+    n = sum(sizes)
+    nst = 1 if op == "ApplyAdagrad" else 2
+    host_p = [rng.standard_normal(k).astype(np.float32) for k in sizes]
+    host_s = [[np.abs(rng.standard_normal(k)).astype(np.float32) * np.float32(0.1) for _ in range(nst)] for k in sizes]
+    x = rng.standard_normal(n).astype(np.float32)
+    y = rng.standard_normal(n).astype(np.float32)
+    params = [torch.from_numpy(p).cuda() for p in host_p]
+    states = [[torch.from_numpy(v).cuda() for v in st] for st in host_s]
+    data = torch.from_numpy(x).cuda()
+    buf0, buf1 = torch.zeros(2 * n, device="cuda"), torch.zeros(2 * n, device="cuda")
+    buf1[n:] = torch.from_numpy(y).cuda()
+    pad0 = torch.zeros(2, dtype=torch.int32, device="cuda")
+    pad1 = torch.zeros(2, dtype=torch.int32, device="cuda")
+    pad0[1] = 1
+    epoch = torch.zeros(64, dtype=torch.int32, device="cuda")
+    status = torch.zeros(1, dtype=torch.int32, device="cuda")
+    P = C.c_void_p * 2
+    offs = (C.c_int64 * 3)(0, sizes[0], n)
+    s2 = P(*[st[1].data_ptr() for st in states]) if nst == 2 else None
+    L.call("b200_peer_allreduce_apply_f32", data.data_ptr(), n, _ptrs([buf0, buf1]).data_ptr(), _ptrs([pad0, pad1]).data_ptr(),
+           0, 2, epoch.data_ptr(), status.data_ptr(), 1 << 20, 1.0, 1, ops._OPT_KIND[op], 2, offs,
+           P(*[q.data_ptr() for q in params]), P(*[st[0].data_ptr() for st in states]), s2, 0.01, ops.stream_ptr())
+    torch.cuda.synchronize()
+    assert int(status.item()) == 0
+    g = x + y
+    np.testing.assert_array_equal(data.cpu().numpy(), g)
+    lo = 0
+    for k, size in enumerate(sizes):
+        ref = O.execute_op(op, host_p[k], *host_s[k], g[lo : lo + size], lr=0.01)
+        got = [params[k]] + list(states[k])
+        for r, t in zip(ref, got):
+            np.testing.assert_array_equal(t.cpu().numpy(), r)
+        lo += size
+
+
 def test_peer_allreduce_wait_gives_up(cuda):
     n = 4096
     x = torch.arange(n, dtype=torch.float32, device="cuda")
@@ -93,6 +142,7 @@ def _rank_main(rank: int, world: int, port: int, q) -> None:
 
     here = os.path.dirname(os.path.abspath(__file__))
     sys.path.insert(0, os.path.join(os.path.dirname(here), "ml-switcheroo-compiler_b200"))
+    sys.path.insert(0, os.path.dirname(here))
     import torch.distributed as dist
 
     from b200.dp import GradAllReduce
@@ -116,8 +166,25 @@ def _rank_main(rank: int, world: int, port: int, q) -> None:
                 dist.all_reduce(t, op=dist.ReduceOp.SUM)
                 t.div_(world)
             ok.append(all(torch.allclose(a, b, rtol=1e-6, atol=1e-6) for a, b in zip(mine, nccl)))
+        # the exchange with a fused Adam step: every rank ends with the same parameters,
+        # equal to one step on the mean gradient
+        from b200.dp import OptimizerStep
+        from oracle import evaluator as O
+
+        params = [torch.full((4096,), 0.5, device="cuda"), torch.linspace(-1, 1, 15, device="cuda").reshape(3, 5)]
+        gs = [torch.randn(4096, generator=g).cuda(), torch.randn(3, 5, generator=g).cuda()]
+        mean = [t.clone() for t in gs]
+        for t in mean:
+            dist.all_reduce(t, op=dist.ReduceOp.SUM)
+            t.div_(world)
+        step = OptimizerStep("ApplyAdam", params, lr=0.01)
+        p0 = [t.cpu().numpy() for t in params]
+        sync(gs, step)
         sync.check()
-        q.put((rank, ok, sync.peer is not None, [t.cpu() for t in mine]))
+        for pr, p_init, gm in zip(params, p0, mean):
+            ref = O.execute_op("ApplyAdam", p_init, np.zeros_like(p_init), np.zeros_like(p_init), gm.cpu().numpy(), lr=0.01)
+            ok.append(bool(np.allclose(pr.cpu().numpy(), ref[0], rtol=1e-6, atol=1e-7)))
+        q.put((rank, ok, sync.peer is not None, [t.cpu() for t in mine] + [t.cpu() for t in params]))
         torch.cuda.synchronize()
         dist.barrier()
     finally:

@@ -75,3 +75,34 @@ def test_oracle_cycle_detected():
 def test_argmax_first_max_wins():
     x = np.array([[1.0, 3.0, 3.0, 0.0], [2.0, 2.0, 2.0, 2.0]], np.float32)
     np.testing.assert_array_equal(O.execute_op("Argmax", x, axis=-1), [1, 0])
+
+
+def _optim_cases():
+    import os
+
+    z = np.load(os.path.join(os.path.dirname(__file__), "golden", "ops", "optim.npz"))
+    ops = sorted({k.split("/")[0] for k in z.files})
+    for op in ops:
+        k = 0
+        while f"{op}/{k}/in0" in z.files:
+            ins = [z[f"{op}/{k}/in{j}"] for j in range(4) if f"{op}/{k}/in{j}" in z.files]
+            outs = [z[f"{op}/{k}/out{j}"] for j in range(3) if f"{op}/{k}/out{j}" in z.files]
+            kw = {"lr": float(z[f"{op}/{k}/lr"])} if f"{op}/{k}/lr" in z.files else {}
+            yield op, k, ins, outs, kw
+            k += 1
+
+
+def test_oracle_optimizer_steps_match_reference_bit_exact():
+    """ApplyAdam / Adagrad / Ftrl / RMSProp restatements against the reference numpy
+    backend's own outputs (tests/golden/make_optim_golden.py): bit-identical."""
+    from oracle import evaluator as O
+
+    seen = set()
+    for op, k, ins, outs, kw in _optim_cases():
+        res = O.execute_op(op, *ins, **kw)
+        assert len(res) == len(outs)
+        for r, ref in zip(res, outs):
+            assert r.dtype == np.float32
+            np.testing.assert_array_equal(r, ref, err_msg=f"{op} case {k}")
+        seen.add(op)
+    assert seen == {"ApplyAdam", "ApplyAdagrad", "ApplyFtrl", "ApplyRMSProp"}
