@@ -98,7 +98,8 @@ def test_peer_allreduce_fused_optimizer_step_emulated_pair(cuda, op):
     P = C.c_void_p * 2
     offs = (C.c_int64 * 3)(0, sizes[0], n)
     s2 = P(*[st[1].data_ptr() for st in states]) if nst == 2 else None
-    L.call("b200_peer_allreduce_apply_f32", data.data_ptr(), n, _ptrs([buf0, buf1]).data_ptr(), _ptrs([pad0, pad1]).data_ptr(),
+    slot_tab, pad_tab = _ptrs([buf0, buf1]), _ptrs([pad0, pad1])  # alive until the kernel has run
+    L.call("b200_peer_allreduce_apply_f32", data.data_ptr(), n, slot_tab.data_ptr(), pad_tab.data_ptr(),
            0, 2, epoch.data_ptr(), status.data_ptr(), 1 << 20, 1.0, 1, ops._OPT_KIND[op], 2, offs,
            P(*[q.data_ptr() for q in params]), P(*[st[0].data_ptr() for st in states]), s2, 0.01, ops.stream_ptr())
     torch.cuda.synchronize()
