@@ -512,6 +512,50 @@ def run_optimizer_micro(args) -> None:
                       "peak_source": pk["source"]}), flush=True)
 
 
+def run_weights_micro(args) -> None:
+    """Weight I/O microbenchmark: the pre-LN transformer workload's parameters (116.4 M fp32,
+    466 MB) saved from HBM to a safetensors file in the reference's layout and loaded back
+    into HBM (file in the page cache after the first pass), wall-clock around each call
+    with the device synchronised. Host-side file I/O plus one PCIe copy per direction."""
+    import os
+    import tempfile
+    import time
+
+    import torch
+
+    from b200 import graph as G
+    from b200 import weights as W
+    from b200.workloads import make_inputs
+
+    torch.cuda.set_device(0)
+    g = G.load("transformer_full")
+    arrays = make_inputs(g.meta["workload"], g.meta["dims"], seed=0)
+    names = [k[2:] for k in g.output_names if k.startswith("d_") and k[2:] in arrays]
+    w = {r: torch.from_numpy(np.ascontiguousarray(arrays[r], dtype=np.float32)).cuda() for r in names}
+    nbytes = sum(t.numel() * 4 for t in w.values())
+    path = os.path.join(tempfile.gettempdir(), "b200_bench_weights.safetensors")
+    save_s, load_s = [], []
+    try:
+        for i in range(max(2, args.steps // 5) + 1):
+            torch.cuda.synchronize()
+            t0 = time.perf_counter()
+            W.save_safetensors(w, path)
+            t1 = time.perf_counter()
+            back = W.load_safetensors(path)
+            torch.cuda.synchronize()
+            t2 = time.perf_counter()
+            if i:  # first pass warms the page cache and the pinned allocator
+                save_s.append(t1 - t0)
+                load_s.append(t2 - t1)
+        ok = all(torch.equal(back[k], w[k]) for k in w)
+    finally:
+        if os.path.exists(path):
+            os.remove(path)
+    print(json.dumps({"microbench": "weights_safetensors", "tensors": len(w), "bytes": nbytes, "roundtrip_exact": ok,
+                      "save": {"s": round(min(save_s), 4), "GB/s": round(nbytes / min(save_s) / 1e9, 2)},
+                      "load": {"s": round(min(load_s), 4), "GB/s": round(nbytes / min(load_s) / 1e9, 2)}}), flush=True)
+
+
 def run_reference(args) -> None:
     rank = env_int("RANK", 0)
     if rank != 0:
@@ -540,7 +584,7 @@ def main() -> None:
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=20)
     ap.add_argument("--warmup", type=int, default=5)
-    ap.add_argument("--workload", default="rowfused", choices=sorted(WORKLOADS) + ["gemm", "adam"])
+    ap.add_argument("--workload", default="rowfused", choices=sorted(WORKLOADS) + ["gemm", "adam", "weights"])
     ap.add_argument("--impl", default="b200", choices=["b200", "reference"])
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline leg")
     ap.add_argument("--no-e2e", action="store_true")
@@ -554,6 +598,8 @@ def main() -> None:
         run_gemm_micro(args)
     elif args.workload == "adam":
         run_optimizer_micro(args)
+    elif args.workload == "weights":
+        run_weights_micro(args)
     elif args.impl == "reference":
         run_reference(args)
     else:

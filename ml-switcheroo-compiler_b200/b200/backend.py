@@ -61,6 +61,28 @@ class B200Backend:
     def get_module(cls) -> Any:
         return ops
 
+    # ---- weight I/O hooks of the reference's format classes -------------------------
+    @classmethod
+    def from_buffer(cls, buffer: bytes, dtype: str, shape: Any) -> Any:
+        """serialization/formats/safetensors.py:118-129: one tensor's bytes -> HBM."""
+        from . import weights
+
+        return weights.from_buffer(buffer, dtype, shape)
+
+    @classmethod
+    def load_npz(cls, filepath: str) -> Any:
+        """serialization/formats/npz.py:84-93: the archive's arrays -> HBM."""
+        from . import weights
+
+        return weights.load_npz(filepath)
+
+    @classmethod
+    def save_npz(cls, weights_np: Any, filepath: str) -> None:
+        """serialization/formats/npz.py:105-108: device tensors -> the reference's npz layout."""
+        from . import weights
+
+        weights.save_npz(weights_np, filepath)
+
     # ---- whole-graph hooks -----------------------------------------------------------
     @classmethod
     def _runner(cls, graph: Any) -> GraphRunner:
