@@ -187,6 +187,23 @@ class GradAllReduce:
                 warnings.warn(f"peer-memory all-reduce unavailable on this group, NCCL only ({err!r})")
         return self.peer
 
+    def graph_safe(self, grads: Sequence[torch.Tensor]) -> bool:
+        """True when every bucket of ``grads`` goes through the peer-memory kernel (set up
+        by an earlier call): no NCCL call and no host synchronisation, so the exchange can
+        be captured in a CUDA graph and replayed (its call counters live on the device)."""
+        import torch.distributed as dist
+
+        if dist.get_world_size(self.group) == 1:
+            return True
+        if self.peer is None:
+            return False
+        for b in self.buckets(grads):
+            t = grads[b[0]]
+            n = sum(grads[i].numel() for i in b)
+            if t.dtype != torch.float32 or not t.is_cuda or n > self.peer.max_numel:
+                return False
+        return True
+
     def check(self) -> None:
         """Raise if a peer-memory exchange gave up waiting for a peer."""
         if self.peer is not None:

@@ -52,15 +52,21 @@ def _device() -> torch.device:
     return ops.device()
 
 
+def _c_order(a: np.ndarray) -> np.ndarray:
+    """C-contiguous, keeping 0-d arrays 0-d (np.ascontiguousarray returns at least 1-d)."""
+    a = np.asarray(a)
+    return a if a.flags.c_contiguous else a.copy(order="C")
+
+
 def _as_tensor(v: Any) -> torch.Tensor:
     if isinstance(v, torch.Tensor):
         return v
-    return torch.from_numpy(np.ascontiguousarray(v))
+    return torch.from_numpy(_c_order(v))
 
 
-def _host_bytes(tensors: list[torch.Tensor]) -> list[bytes]:
-    """Raw little-endian bytes of each tensor (device tensors: one copy each into pinned
-    memory, one synchronisation for all)."""
+def _host_views(tensors: list[torch.Tensor]) -> list[memoryview]:
+    """Raw little-endian bytes of each tensor as memoryviews of host memory (device
+    tensors: one copy each into pinned memory, one synchronisation for all)."""
     hosts = []
     for t in tensors:
         t = t.contiguous()
@@ -72,52 +78,65 @@ def _host_bytes(tensors: list[torch.Tensor]) -> list[bytes]:
             hosts.append(t)
     if any(t.is_cuda for t in tensors):
         torch.cuda.synchronize()
-    return [h.reshape(-1).view(torch.uint8).numpy().tobytes() for h in hosts]
+    return [memoryview(h.reshape(-1).view(torch.uint8).numpy()) for h in hosts]
+
+
 
 
 # ---- safetensors ----------------------------------------------------------------------
-def safetensors_bytes(weights: Mapping[str, Any]) -> bytes:
-    """The file contents the reference's saver writes for ``weights`` (safetensors.py:130-185)."""
+def _safetensors_parts(weights: Mapping[str, Any]) -> tuple[bytes, list[memoryview]]:
+    """Length prefix + padded header, and the tensors' bytes in file order
+    (safetensors.py:130-185)."""
     items = [(str(k), _as_tensor(v)) for k, v in weights.items()]
-    blobs = _host_bytes([t for _, t in items])
+    for k, t in items:
+        if t.dtype not in _ST_OF_TORCH:
+            raise TypeError(f"safetensors: unsupported dtype {t.dtype} for {k!r}")
+    blobs = _host_views([t for _, t in items])
     header: dict[str, Any] = {}
     offset = 0
     for (k, t), b in zip(items, blobs):
-        if t.dtype not in _ST_OF_TORCH:
-            raise TypeError(f"safetensors: unsupported dtype {t.dtype} for {k!r}")
-        header[k] = {"dtype": _ST_OF_TORCH[t.dtype], "shape": list(t.shape), "data_offsets": [offset, offset + len(b)]}
-        offset += len(b)
+        header[k] = {"dtype": _ST_OF_TORCH[t.dtype], "shape": list(t.shape), "data_offsets": [offset, offset + b.nbytes]}
+        offset += b.nbytes
     hb = json.dumps(header, separators=(",", ":")).encode("utf-8")
     hb += b" " * ((8 - len(hb) % 8) % 8)
-    return struct.pack("<Q", len(hb)) + hb + b"".join(blobs)
+    return struct.pack("<Q", len(hb)) + hb, blobs
+
+
+def safetensors_bytes(weights: Mapping[str, Any]) -> bytes:
+    """The file contents the reference's saver writes for ``weights``."""
+    head, blobs = _safetensors_parts(weights)
+    return head + b"".join(blobs)
 
 
 def save_safetensors(weights: Mapping[str, Any], path: str) -> None:
+    head, blobs = _safetensors_parts(weights)
     with open(path, "wb") as f:
-        f.write(safetensors_bytes(weights))
-
-
-def _parse_safetensors_header(raw: bytes) -> tuple[dict, int]:
-    if len(raw) < 8:
-        return {}, 0
-    (hlen,) = struct.unpack("<Q", raw[:8])
-    return json.loads(raw[8 : 8 + hlen].decode("utf-8")), 8 + hlen
+        f.write(head)
+        for b in blobs:  # straight from the pinned copies, no intermediate join
+            f.write(b)
 
 
 def load_safetensors(path: str, device: torch.device | None = None) -> dict[str, torch.Tensor]:
     """All tensors of a safetensors file on the device: the data section goes to HBM in one
     copy; each tensor is a view of it (or a copy, where its offset does not fit its dtype's
     alignment)."""
+    import os
+
     with open(path, "rb") as f:
-        raw = f.read()
-    header, start = _parse_safetensors_header(raw)
-    entries = [(k, v) for k, v in header.items() if k != "__metadata__"]
-    if not entries:
-        return {}
+        pre = f.read(8)
+        if len(pre) < 8:
+            return {}
+        (hlen,) = struct.unpack("<Q", pre)
+        header = json.loads(f.read(hlen).decode("utf-8"))
+        entries = [(k, v) for k, v in header.items() if k != "__metadata__"]
+        if not entries:
+            return {}
+        size = os.fstat(f.fileno()).st_size - 8 - hlen
+        pinned = torch.empty(size, dtype=torch.uint8, pin_memory=True)
+        got = f.readinto(memoryview(pinned.numpy()))  # the data section straight into pinned memory
+        if got != size:
+            raise OSError(f"{path}: short read ({got} of {size} bytes)")
     dev = device or _device()
-    data = np.frombuffer(raw, dtype=np.uint8, offset=start)
-    pinned = torch.empty(data.size, dtype=torch.uint8, pin_memory=True)
-    pinned.numpy()[:] = data
     blob = pinned.to(dev, non_blocking=True)
     out = {}
     for k, v in entries:
@@ -148,7 +167,7 @@ def npy_bytes(tensor: Any) -> bytes:
     shape_str = f"({shape[0]},)" if len(shape) == 1 else str(shape)
     d = "{'descr': '" + _DESCR_OF_TORCH[t.dtype] + "', 'fortran_order': False, 'shape': " + shape_str + ", }"
     d += " " * (16 - (len(d) + 10) % 16) + "\n"
-    return b"\x93NUMPY" + struct.pack("<BBH", 1, 0, len(d)) + d.encode("ascii") + _host_bytes([t])[0]
+    return b"\x93NUMPY" + struct.pack("<BBH", 1, 0, len(d)) + d.encode("ascii") + bytes(_host_views([t])[0])
 
 
 def save_npz(weights: Mapping[str, Any], path: str) -> None:
@@ -166,6 +185,6 @@ def load_npz(path: str, device: torch.device | None = None) -> dict[str, torch.T
         for name in zf.namelist():
             arr = np.lib.format.read_array(io.BytesIO(zf.read(name)), allow_pickle=False)
             key = name[:-4] if name.endswith(".npy") else name
-            host = torch.from_numpy(np.ascontiguousarray(arr))
+            host = torch.from_numpy(_c_order(arr))
             out[key] = host.pin_memory().to(dev, non_blocking=True) if host.numel() else host.to(dev)
     return out

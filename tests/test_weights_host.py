@@ -40,3 +40,12 @@ def test_npz_entries_match_reference_bytes(tmp_path):
     for n in ref.namelist():
         assert mine.read(n) == ref.read(n)
         assert mine.getinfo(n).compress_type == zipfile.ZIP_STORED
+
+
+def test_writers_take_numpy_arrays_and_keep_0d_shapes():
+    from b200 import weights as W
+
+    w = _arrays()
+    with open(os.path.join(OPS, "weights.safetensors"), "rb") as f:
+        assert W.safetensors_bytes(w) == f.read()  # numpy inputs, 0-d "scale" included
+    assert W.npy_bytes(w["scale"]) == zipfile.ZipFile(os.path.join(OPS, "weights.npz")).read("scale.npy")
