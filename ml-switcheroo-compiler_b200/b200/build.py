@@ -1,5 +1,5 @@
 """Build libb200.so in-tree: every ``csrc/*.cu`` compiled for sm_100a and linked into one
-shared library next to this file (so it travels with the source tree to the GPU box).
+shared library next to this file (in-tree, so it is found wherever the source tree is copied).
 
     python -m b200.build            (from ml-switcheroo-compiler_b200/)
 """

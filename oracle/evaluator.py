@@ -2,7 +2,7 @@
 graph interpreter and of the numpy-backend op kernels on the fwd+bwd hot path.
 
 Only ``tests/``, ``__graft_entry__.smoke()`` and ``bench.py``'s CPU-baseline leg may
-import this module, and only as the checker or as the timed CPU reference. The
+import this module, and only to check results or as the timed CPU reference. The
 ``b200`` backend never calls it.
 
 Interpreter: ``evaluate`` follows ``interpreter/evaluator.py:272-305`` (env = inputs,
