@@ -357,8 +357,7 @@ def run_gpu(args) -> None:
         fn = B200Backend.compile_graph(g)
 
         def e2e_step():
-            dv = {k: v.to(dev, non_blocking=True) for k, v in host.items()}
-            o = fn(dv)
+            o = fn(host)  # pinned host inputs: copied by the call straight into its static buffers
             if dist is not None:
                 sync([o[gid] for gid in grad_ids])
             for k in res_ids:

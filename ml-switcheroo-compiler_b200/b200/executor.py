@@ -214,6 +214,17 @@ class CompiledGraph:
         self.sig = _signature(d)
 
     def __call__(self, inputs: dict[str, Any]) -> dict[str, Any]:
+        if self.static_in is not None and self.sig == _signature(inputs):
+            # the captured signature: host tensors (pinned: asynchronous H2D) and device
+            # tensors go straight into the static buffers, with no intermediate copy
+            for k, v in inputs.items():
+                dst = self.static_in[k]
+                if isinstance(dst, torch.Tensor) and v is not dst:
+                    dst.copy_(v, non_blocking=True)
+            if self.cuda_graph is not None:
+                self.cuda_graph.replay()
+                return self.static_out
+            return self.runner.plan_for(self.static_in).run(self.static_in)
         d = self.runner.device_inputs(inputs)
         if self.sig != _signature(d):
             self._capture(d)
