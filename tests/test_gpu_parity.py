@@ -22,7 +22,7 @@ BF16 = {"bmm", "cnn", "transformer"}
 
 
 @pytest.mark.gpu
-@pytest.mark.parametrize("mode", ["pernode", "graph", "compiled"])
+@pytest.mark.parametrize("mode", ["pernode", "graph", "compiled", "compiled_host"])
 @pytest.mark.parametrize("case", CASES)
 def test_graph_parity(cuda, case, mode):
     got, ref, g = run_case(case, mode)
