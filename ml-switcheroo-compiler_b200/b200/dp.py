@@ -48,7 +48,7 @@ class PeerAllReduce:
     ``check()`` turns into ``TimeoutError``.
     """
 
-    SPIN_LIMIT = 1 << 24  # polls per flag, each after a ~128 ns sleep: seconds, not forever
+    SPIN_LIMIT = 1 << 24  # polls per flag (backing off to ~256 ns sleeps): seconds, not forever
 
     def __init__(self, group, max_numel: int, device: torch.device) -> None:
         import torch.distributed as dist

@@ -41,11 +41,12 @@ struct Segs {
 __device__ __forceinline__ void st_release_sys(uint32_t* p, uint32_t v) {
   asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
 }
-__device__ __forceinline__ uint32_t ld_acquire_sys(const uint32_t* p) {
+__device__ __forceinline__ uint32_t ld_relaxed_sys(const uint32_t* p) {
   uint32_t v;
-  asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  asm volatile("ld.relaxed.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
   return v;
 }
+__device__ __forceinline__ void fence_acq_rel_sys() { asm volatile("fence.acq_rel.sys;" ::: "memory"); }
 
 __global__ void __launch_bounds__(PT) peer_allreduce_kernel(float* __restrict__ data, int64_t n, int64_t chunk,
                                                             const uint64_t* __restrict__ slots, const uint64_t* __restrict__ pads,
@@ -60,7 +61,10 @@ __global__ void __launch_bounds__(PT) peer_allreduce_kernel(float* __restrict__ 
   float* mine = reinterpret_cast<float*>(slots[rank]) + off;
   if (tid == 0) s_err = 0;
   for (int64_t i = lo + tid; i < hi; i += PT) mine[i] = data[i];
-  __threadfence_system();
+  // The block's slot writes are ordered before the flag by the barrier and the flag's
+  // system-scope release (release is cumulative over what the releasing thread has
+  // synchronised with); likewise one acquire fence after the last poll, then the barrier,
+  // orders the peers' slot writes before every thread's reads.
   __syncthreads();
   if (tid < world && tid != rank) {
     // tell peer `tid` that this rank's chunk b of call e is in place ...
@@ -68,14 +72,15 @@ __global__ void __launch_bounds__(PT) peer_allreduce_kernel(float* __restrict__ 
     // ... and wait until peer `tid` has said the same to this rank
     const uint32_t* f = reinterpret_cast<const uint32_t*>(pads[rank]) + (size_t)b * world + tid;
     int64_t it = 0;
-    while ((int32_t)(ld_acquire_sys(f) - e) < 0) {
+    while ((int32_t)(ld_relaxed_sys(f) - e) < 0) {
       if (++it > spin_limit) {
         s_err = 1;
         atomicExch(status, B200_ERR_TIMEOUT);
         break;
       }
-      __nanosleep(128);
+      if (it > 32) __nanosleep(it > 4096 ? 256 : 32);
     }
+    fence_acq_rel_sys();
   }
   __syncthreads();
   if (s_err) return;

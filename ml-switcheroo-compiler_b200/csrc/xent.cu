@@ -9,6 +9,8 @@
 // (advanced_indexing.py:309-326), ReduceSum/Exp/Multiply/Subtract of the LogSoftmax VJP.
 // One CTA per row: an online max/sum-exp pass, then one write pass (the row is re-read
 // from L2). Out-of-range labels set the device error flag.
+#include <algorithm>
+
 #include "common.cuh"
 
 namespace b200 {
@@ -69,71 +71,112 @@ __global__ void __launch_bounds__(XE_T) xent_kernel(const T* __restrict__ x, con
 // written in fp32 and/or bf16 (bf16 when it only feeds the output-projection GEMMs).
 constexpr int XR_T = 512;
 
+__device__ __forceinline__ void xr_cp_async16(void* sdst, const void* gsrc) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"((uint32_t)__cvta_generic_to_shared(sdst)), "l"(gsrc) : "memory");
+}
+__device__ __forceinline__ void xr_cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+__device__ __forceinline__ void xr_cp_async_wait_all() { asm volatile("cp.async.wait_group 0;" ::: "memory"); }
+
+// Persistent over rows (one CTA per SM): while a row is reduced and its gradient written
+// from registers, the CTA's next row streams into shared memory with cp.async, so HBM
+// reads overlap the math and the stores. Thread t copies and later reads only its own
+// float4 slots, so the staging buffer needs no barrier.
 template <int VPT>
-__global__ void __launch_bounds__(XR_T) xent_reg_kernel(const float* __restrict__ x, const int64_t* __restrict__ label,
-                                                        const float* __restrict__ d, float* __restrict__ picked,
-                                                        float* __restrict__ dx, __nv_bfloat16* __restrict__ dxb, int64_t V) {
+__global__ void __launch_bounds__(XR_T, 1) xent_reg_kernel(const float* __restrict__ x, const int64_t* __restrict__ label,
+                                                           const float* __restrict__ d, float* __restrict__ picked,
+                                                           float* __restrict__ dx, __nv_bfloat16* __restrict__ dxb, int64_t V,
+                                                           int64_t rows) {
   __shared__ float red[32];
+  extern __shared__ float4 stage[];  // [NC][XR_T]: the next row
   constexpr int NC = VPT / 4;
-  const int64_t r = blockIdx.x;
-  const float* xr = x + r * V;
-  float v[NC][4];
-  float m = -INFINITY;
+  const int64_t G = gridDim.x;
+  auto prefetch = [&](int64_t r) {
+    if (r < rows) {
+      const float* xr = x + r * V;
 #pragma unroll
-  for (int c = 0; c < NC; ++c) {
-    const int64_t col = ((int64_t)c * XR_T + threadIdx.x) * 4;
-    if (col < V) {
-      const float4 t = __ldcs(reinterpret_cast<const float4*>(xr + col));
-      v[c][0] = t.x; v[c][1] = t.y; v[c][2] = t.z; v[c][3] = t.w;
-    } else {
-      v[c][0] = v[c][1] = v[c][2] = v[c][3] = -INFINITY;
+      for (int c = 0; c < NC; ++c) {
+        const int64_t col = ((int64_t)c * XR_T + threadIdx.x) * 4;
+        if (col < V) xr_cp_async16(&stage[c * XR_T + threadIdx.x], xr + col);
+      }
     }
+    xr_cp_async_commit();
+  };
+  prefetch(blockIdx.x);
+  for (int64_t r = blockIdx.x; r < rows; r += G) {
+    xr_cp_async_wait_all();
+    float v[NC][4];
+    float m = -INFINITY;
 #pragma unroll
-    for (int k = 0; k < 4; ++k) m = fmaxf(m, v[c][k]);
-  }
-  const float M = block_max(m, red);
-  int64_t lab = label[r];
-  if (lab < 0) lab += V;
-  const bool ok = lab >= 0 && lab < V;
-  float xl = 0.f, s = 0.f;
+    for (int c = 0; c < NC; ++c) {
+      const int64_t col = ((int64_t)c * XR_T + threadIdx.x) * 4;
+      if (col < V) {
+        const float4 t = stage[c * XR_T + threadIdx.x];
+        v[c][0] = t.x; v[c][1] = t.y; v[c][2] = t.z; v[c][3] = t.w;
+      } else {
+        v[c][0] = v[c][1] = v[c][2] = v[c][3] = -INFINITY;
+      }
 #pragma unroll
-  for (int c = 0; c < NC; ++c) {
-    const int64_t col = ((int64_t)c * XR_T + threadIdx.x) * 4;
+      for (int k = 0; k < 4; ++k) m = fmaxf(m, v[c][k]);
+    }
+    prefetch(r + G);  // this thread's slots are in registers now
+    const float M = block_max(m, red);
+    int64_t lab = label[r];
+    if (lab < 0) lab += V;
+    const bool ok = lab >= 0 && lab < V;
+    float xl = 0.f, s = 0.f;
 #pragma unroll
-    for (int k = 0; k < 4; ++k) {
-      if (col + k == lab) xl = v[c][k];
-      const float e = (v[c][k] == -INFINITY) ? 0.f : expf(v[c][k] - M);
-      v[c][k] = e;
-      s += e;
+    for (int c = 0; c < NC; ++c) {
+      const int64_t col = ((int64_t)c * XR_T + threadIdx.x) * 4;
+#pragma unroll
+      for (int k = 0; k < 4; ++k) {
+        if (col + k == lab) xl = v[c][k];
+        const float e = (v[c][k] == -INFINITY) ? 0.f : expf(v[c][k] - M);
+        v[c][k] = e;
+        s += e;
+      }
+    }
+    const float S = block_sum(s, red);
+    const float lse = M + logf(S);
+    // the label's logit: exactly one thread holds it
+    const bool holder = ok && ((lab >> 2) % XR_T) == threadIdx.x;
+    if (holder && picked) picked[r] = xl - lse;
+    if (threadIdx.x == 0 && !ok) {
+      raise_device_error(B200_ERR_ARG);
+      if (picked) picked[r] = 0.f;
+    }
+    if (!dx && !dxb) continue;
+    const float dr = d[r], inv = 1.f / S;
+#pragma unroll
+    for (int c = 0; c < NC; ++c) {
+      const int64_t col = ((int64_t)c * XR_T + threadIdx.x) * 4;
+      if (col >= V) continue;
+      float o[4];
+#pragma unroll
+      for (int k = 0; k < 4; ++k) o[k] = dr * ((col + k == lab ? 1.f : 0.f) - v[c][k] * inv);
+      if (dx) __stcs(reinterpret_cast<float4*>(dx + r * V + col), make_float4(o[0], o[1], o[2], o[3]));
+      if (dxb) {
+        __nv_bfloat162 lo = __floats2bfloat162_rn(o[0], o[1]), hi = __floats2bfloat162_rn(o[2], o[3]);
+        uint2 u;
+        u.x = *reinterpret_cast<uint32_t*>(&lo);
+        u.y = *reinterpret_cast<uint32_t*>(&hi);
+        __stcs(reinterpret_cast<uint2*>(dxb + r * V + col), u);
+      }
     }
   }
-  const float S = block_sum(s, red);
-  const float lse = M + logf(S);
-  // the label's logit: exactly one thread holds it
-  const bool holder = ok && ((lab >> 2) % XR_T) == threadIdx.x;
-  if (holder && picked) picked[r] = xl - lse;
-  if (threadIdx.x == 0 && !ok) {
-    raise_device_error(B200_ERR_ARG);
-    if (picked) picked[r] = 0.f;
+  xr_cp_async_wait_all();
+}
+
+template <int VPT>
+void launch_xent_reg(const float* x, const int64_t* label, const float* d, float* picked, float* dx, __nv_bfloat16* dxb,
+                     int64_t V, int64_t rows, cudaStream_t s) {
+  const size_t smem = (size_t)VPT * XR_T * sizeof(float);
+  static bool attr = false;
+  if (!attr && smem > 48 * 1024) {
+    cudaFuncSetAttribute(xent_reg_kernel<VPT>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    attr = true;
   }
-  if (!dx && !dxb) return;
-  const float dr = d[r], inv = 1.f / S;
-#pragma unroll
-  for (int c = 0; c < NC; ++c) {
-    const int64_t col = ((int64_t)c * XR_T + threadIdx.x) * 4;
-    if (col >= V) continue;
-    float o[4];
-#pragma unroll
-    for (int k = 0; k < 4; ++k) o[k] = dr * ((col + k == lab ? 1.f : 0.f) - v[c][k] * inv);
-    if (dx) __stcs(reinterpret_cast<float4*>(dx + r * V + col), make_float4(o[0], o[1], o[2], o[3]));
-    if (dxb) {
-      __nv_bfloat162 lo = __floats2bfloat162_rn(o[0], o[1]), hi = __floats2bfloat162_rn(o[2], o[3]);
-      uint2 u;
-      u.x = *reinterpret_cast<uint32_t*>(&lo);
-      u.y = *reinterpret_cast<uint32_t*>(&hi);
-      *reinterpret_cast<uint2*>(dxb + r * V + col) = u;
-    }
-  }
+  const int64_t grid = std::min<int64_t>(rows, (int64_t)num_sms());
+  xent_reg_kernel<VPT><<<(unsigned)grid, XR_T, smem, s>>>(x, label, d, picked, dx, dxb, V, rows);
 }
 
 }  // namespace b200
@@ -154,11 +197,11 @@ extern "C" int b200_logsoftmax_pick(int x_dtype, const void* x, const int64_t* l
     const int vpt = (int)ceil_div(ceil_div(cols, (int64_t)XR_T), (int64_t)4) * 4;
     auto* db = reinterpret_cast<__nv_bfloat16*>(dx_bf16);
     const float* xf = (const float*)x;
-    if (vpt <= 4) xent_reg_kernel<4><<<(unsigned)rows, XR_T, 0, s>>>(xf, label, d, picked, dx, db, cols);
-    else if (vpt <= 8) xent_reg_kernel<8><<<(unsigned)rows, XR_T, 0, s>>>(xf, label, d, picked, dx, db, cols);
-    else if (vpt <= 16) xent_reg_kernel<16><<<(unsigned)rows, XR_T, 0, s>>>(xf, label, d, picked, dx, db, cols);
-    else if (vpt <= 32) xent_reg_kernel<32><<<(unsigned)rows, XR_T, 0, s>>>(xf, label, d, picked, dx, db, cols);
-    else xent_reg_kernel<64><<<(unsigned)rows, XR_T, 0, s>>>(xf, label, d, picked, dx, db, cols);
+    if (vpt <= 4) launch_xent_reg<4>(xf, label, d, picked, dx, db, cols, rows, s);
+    else if (vpt <= 8) launch_xent_reg<8>(xf, label, d, picked, dx, db, cols, rows, s);
+    else if (vpt <= 16) launch_xent_reg<16>(xf, label, d, picked, dx, db, cols, rows, s);
+    else if (vpt <= 32) launch_xent_reg<32>(xf, label, d, picked, dx, db, cols, rows, s);
+    else launch_xent_reg<64>(xf, label, d, picked, dx, db, cols, rows, s);
     return check_launch("logsoftmax_pick(rows in registers)");
   }
   B200_REQUIRE(!dx_bf16, "logsoftmax_pick: bf16 dx needs fp32 logits with cols %% 4 == 0");
