@@ -369,22 +369,21 @@ int b200_conv2d_wgrad_tc(const float* x, const float* dy, float* dw, int64_t N, 
 
 /* All-reduce of n fp32 values across `world` ranks through peer-mapped memory, for the
  * buckets of small gradients that the reference exchanges with its AllReduce node
- * (numpy/eager/distributed.py:205-225, all_reduce_ring :105). One kernel: this rank's
- * values go into its slot of a symmetric buffer, a flag goes into every peer's signal
- * pad, the kernel waits (at most spin_limit polls per flag) for every peer's flag, and
- * then adds all ranks' slots in rank order (NVLink P2P loads), times `scale` (1 for a
- * sum, 1/world for a mean). The result is identical on every rank.
- *   slots_dev: device array of `world` pointers, rank q's symmetric buffer of >= 2 n floats
- *   pads_dev:  device array of `world` pointers, rank q's signal pad of >= blocks * world
- *              uint32, zero before the first call
- *   epoch:     this rank's per-block call counters (`blocks` uint32, zero at start); every
- *              rank must make the same calls with the same n and blocks
- *   status:    device int, set to B200_ERR_TIMEOUT when a peer's flag did not arrive (the
- *              values of that block are then left unchanged)
- * b200_peer_allreduce_blocks gives the number of blocks for n values and a pad size. */
-int b200_peer_allreduce_blocks(int64_t n, int world, size_t pad_bytes);
-int b200_peer_allreduce_f32(float* data, int64_t n, const void* slots_dev, const void* pads_dev, int rank, int world,
-                            unsigned int* epoch, int* status, int64_t spin_limit, float scale, int blocks, void* stream);
+ * (numpy/eager/distributed.py:205-225, all_reduce_ring :105). One kernel: every value
+ * travels with its call number in one 64-bit word (call << 32 | value bits), pushed into
+ * every peer's receive area over NVLink; each rank polls its own area (at most spin_limit
+ * polls per thread) and adds all ranks' values in rank order, times `scale` (1 for a sum,
+ * 1/world for a mean). The result is identical on every rank.
+ *   bufs_dev: device array of `world` pointers, rank q's receive area of
+ *             2 * world * capacity 64-bit words, zero before the first call
+ *   epoch:    this rank's per-block call counters (64 uint32, zero at start); every rank
+ *             must make the same calls with the same n
+ *   status:   device int, set to B200_ERR_TIMEOUT when a peer's words did not arrive (the
+ *             values of that block are then left unchanged)
+ * n <= capacity and n <= 64 * 4096. b200_peer_allreduce_blocks gives the blocks for n. */
+int b200_peer_allreduce_blocks(int64_t n);
+int b200_peer_allreduce_f32(float* data, int64_t n, const void* bufs_dev, int64_t capacity, int rank, int world,
+                            unsigned int* epoch, int* status, int64_t spin_limit, float scale, void* stream);
 /* cudaMemsetAsync of a device range (clears a signal pad before its first use). */
 int b200_memset_async(void* p, int value, size_t bytes, void* stream);
 
@@ -409,10 +408,10 @@ int b200_apply_optimizer_f32(int kind, int count, const float* const* param, con
  * Each summed element also updates param[j], s1[j] (and s2[j]; Adagrad has none) in
  * place, bit-identically to b200_apply_optimizer_f32; `data` receives the summed values.
  * offsets, param, s1, s2 are host arrays (device pointers). */
-int b200_peer_allreduce_apply_f32(float* data, int64_t n, const void* slots_dev, const void* pads_dev, int rank, int world,
-                                  unsigned int* epoch, int* status, int64_t spin_limit, float scale, int blocks, int kind,
-                                  int count, const int64_t* offsets, float* const* param, float* const* s1, float* const* s2,
-                                  float lr, void* stream);
+int b200_peer_allreduce_apply_f32(float* data, int64_t n, const void* bufs_dev, int64_t capacity, int rank, int world,
+                                  unsigned int* epoch, int* status, int64_t spin_limit, float scale, int kind, int count,
+                                  const int64_t* offsets, float* const* param, float* const* s1, float* const* s2, float lr,
+                                  void* stream);
 
 #ifdef __cplusplus
 }

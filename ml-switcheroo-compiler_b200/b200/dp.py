@@ -37,18 +37,19 @@ def shard_rows(n: int, rank: int, world: int) -> slice:
 
 
 class PeerAllReduce:
-    """All-reduce of small fp32 buffers through a symmetric buffer that every rank maps
-    (``b200_peer_allreduce_f32``): one kernel copies this rank's values into its slot,
-    flags every peer, waits for every peer's flag (bounded), and adds the ranks' slots in
-    rank order, so all ranks hold bit-identical sums.
+    """All-reduce of small fp32 buffers through peer-mapped memory
+    (``b200_peer_allreduce_f32``): one kernel pushes each value, tagged with its call
+    number in one 64-bit word, into every peer's receive area, then adds the words it
+    receives in rank order, so all ranks hold bit-identical sums.
 
     Construction is collective (symmetric-memory rendezvous on ``group``) and must be
-    followed by one more collective on ``group`` before the first call, so that every pad
-    is clear. Every rank must then make the same calls with the same sizes. A wait that gives up sets a status that
-    ``check()`` turns into ``TimeoutError``.
+    followed by one more collective on ``group`` before the first call, so that every
+    receive area is clear. Every rank must then make the same calls with the same sizes. A
+    wait that gives up sets a status that ``check()`` turns into ``TimeoutError``.
     """
 
-    SPIN_LIMIT = 1 << 24  # polls per flag (backing off to ~256 ns sleeps): seconds, not forever
+    SPIN_LIMIT = 1 << 24  # polls per thread (backing off to ~256 ns sleeps): seconds, not forever
+    MAX_NUMEL = 64 * 4096  # values per call (64 blocks of 4096)
 
     def __init__(self, group, max_numel: int, device: torch.device) -> None:
         import torch.distributed as dist
@@ -62,15 +63,15 @@ class PeerAllReduce:
 
         self.group, self.device = group, device
         self.world, self.rank = dist.get_world_size(group), dist.get_rank(group)
-        self.max_numel = int(max_numel)
-        self.buf = symm.empty(2 * self.max_numel, dtype=torch.float32, device=device)
+        self.max_numel = min(int(max_numel), self.MAX_NUMEL)
+        # receive area: [2 halves][world sources][max_numel] 64-bit words
+        self.buf = symm.empty(2 * self.world * self.max_numel, dtype=torch.int64, device=device)
         self.handle = symm.rendezvous(self.buf, group if group is not None else dist.group.WORLD)
-        self.pad_bytes = int(self.handle.signal_pad_size)
         self.epoch = torch.zeros(64, dtype=torch.int32, device=device)
         self.status = torch.zeros(1, dtype=torch.int32, device=device)
-        L.call("b200_memset_async", int(self.handle.signal_pad_ptrs[self.handle.rank]), 0, self.pad_bytes, ops.stream_ptr())
+        L.call("b200_memset_async", self.buf.data_ptr(), 0, self.buf.numel() * 8, ops.stream_ptr())
         torch.cuda.synchronize(device)
-        # the first call must wait until every rank has cleared its pad: the caller follows
+        # the first call must wait until every rank has cleared its area: the caller follows
         # construction with a collective on `group` (GradAllReduce agrees on success)
 
     MAX_SEGMENTS = 64  # parameter tensors of one fused optimizer epilogue
@@ -88,9 +89,8 @@ class PeerAllReduce:
         if flat.dtype != torch.float32 or not flat.is_contiguous() or flat.numel() > self.max_numel:
             raise ValueError("PeerAllReduce takes contiguous fp32 buffers of at most max_numel values")
         n = flat.numel()
-        blocks = int(L.lib().b200_peer_allreduce_blocks(n, self.world, self.pad_bytes))
-        head = (flat.data_ptr(), n, int(self.handle.buffer_ptrs_dev), int(self.handle.signal_pad_ptrs_dev), self.rank,
-                self.world, self.epoch.data_ptr(), self.status.data_ptr(), self.SPIN_LIMIT, float(scale), blocks)
+        head = (flat.data_ptr(), n, int(self.handle.buffer_ptrs_dev), self.max_numel, self.rank, self.world,
+                self.epoch.data_ptr(), self.status.data_ptr(), self.SPIN_LIMIT, float(scale))
         if step is None:
             L.call("b200_peer_allreduce_f32", *head, ops.stream_ptr())
             return
@@ -111,7 +111,7 @@ class PeerAllReduce:
         """Raise TimeoutError if a wait for a peer gave up since construction."""
         code = int(self.status.item())
         if code:
-            raise TimeoutError(f"peer all-reduce: a peer's flag did not arrive (status {code})")
+            raise TimeoutError(f"peer all-reduce: a peer's values did not arrive (status {code})")
 
 
 class OptimizerStep:

@@ -2,9 +2,10 @@
 
 On one GPU every case is a single kernel launch that waits on no other kernel:
 * world 1: the values come back times ``scale``;
-* an emulated world-2 exchange: the peer's slot and its flag are written beforehand, so
-  the kernel finds them and adds the two ranks' values in rank order;
-* the bounded wait: a flag that nothing sets makes the kernel give up, report
+* an emulated world-2 exchange: the peer's words (value + call number) are written into
+  this rank's receive area beforehand, so the kernel finds them and adds the two ranks'
+  values in rank order (also with the fused optimizer epilogue);
+* the bounded wait: words that never arrive make the kernel give up, report
   B200_ERR_TIMEOUT through the status word and leave the values unchanged.
 With two or more GPUs, ``GradAllReduce`` over NCCL process groups (peer kernel for the
 small fp32 bucket) is checked against NCCL's own all-reduce.
@@ -25,51 +26,56 @@ def _ptrs(ts):
     return torch.tensor([t.data_ptr() for t in ts], dtype=torch.int64, device="cuda")
 
 
-def _run(data, slots, pads, rank, world, epoch, status, spin, scale, blocks):
+def _words(values: torch.Tensor, call: int) -> torch.Tensor:
+    """The 64-bit words a rank pushes: call number in the high half, value bits in the low."""
+    return (values.contiguous().view(torch.int32).to(torch.int64) & 0xFFFFFFFF) | (call << 32)
+
+
+def _area(world, cap):
+    return torch.zeros(2 * world * cap, dtype=torch.int64, device="cuda")
+
+
+def _run(data, bufs, cap, rank, world, epoch, status, spin, scale):
     from b200 import _lib as L
     from b200 import ops
 
-    sd, pd = _ptrs(slots), _ptrs(pads)
-    L.call("b200_peer_allreduce_f32", data.data_ptr(), data.numel(), sd.data_ptr(), pd.data_ptr(), rank, world,
-           epoch.data_ptr(), status.data_ptr(), spin, scale, blocks, ops.stream_ptr())
+    tab = _ptrs(bufs)  # alive until the kernel has run
+    L.call("b200_peer_allreduce_f32", data.data_ptr(), data.numel(), tab.data_ptr(), cap, rank, world, epoch.data_ptr(),
+           status.data_ptr(), spin, scale, ops.stream_ptr())
     torch.cuda.synchronize()
 
 
-@pytest.mark.parametrize("n,blocks", [(1, 1), (8192, 1), (100000, 4)])
-def test_peer_allreduce_world1_and_emulated_pair(cuda, n, blocks):
+@pytest.mark.parametrize("n", [1, 8192, 100000])
+def test_peer_allreduce_world1_and_emulated_pair(cuda, n):
+    from b200 import _lib as L
+
+    blocks = int(L.lib().b200_peer_allreduce_blocks(n))
     g = torch.Generator().manual_seed(n)
     x = torch.randn(n, generator=g).cuda()
-    # world 1
-    buf = torch.zeros(2 * n, device="cuda")
-    pad = torch.zeros(64, dtype=torch.int32, device="cuda")
     epoch = torch.zeros(64, dtype=torch.int32, device="cuda")
     status = torch.zeros(1, dtype=torch.int32, device="cuda")
+    # world 1
     d = x.clone()
-    _run(d, [buf], [pad], 0, 1, epoch, status, 1000, 0.5, blocks)
+    _run(d, [_area(1, n)], n, 0, 1, epoch, status, 1000, 0.5)
     assert int(status.item()) == 0
     assert torch.equal(d, x * 0.5)
     assert epoch[:blocks].tolist() == [1] * blocks
-    # world 2, this rank 0; rank 1's values for call 1 already in its slot (half 1) and its
-    # flags raised in rank 0's pad
+    # world 2, this rank 0, call 1 (half 1): rank 1's words already in this rank's area
     y = torch.randn(n, generator=g).cuda()
-    buf0, buf1 = torch.zeros(2 * n, device="cuda"), torch.zeros(2 * n, device="cuda")
-    buf1[n:] = y
-    pad0 = torch.zeros(2 * blocks, dtype=torch.int32, device="cuda")
-    pad1 = torch.zeros(2 * blocks, dtype=torch.int32, device="cuda")
-    pad0[1::2] = 1  # slot b * world + 1: peer 1, call 1
+    a0, a1 = _area(2, n), _area(2, n)
+    a0[(1 * 2 + 1) * n : (1 * 2 + 2) * n] = _words(y, 1)
     epoch.zero_()
     d = x.clone()
-    _run(d, [buf0, buf1], [pad0, pad1], 0, 2, epoch, status, 1 << 20, 1.0, blocks)
+    _run(d, [a0, a1], n, 0, 2, epoch, status, 1 << 20, 1.0)
     assert int(status.item()) == 0
     assert torch.equal(d, x + y)  # rank order: rank 0's value first
-    assert torch.equal(buf0[n:], x)  # this rank's values landed in its slot
-    assert pad1[0::2].tolist() == [1] * blocks  # and its flags in the peer's pad
+    assert torch.equal(a1[(1 * 2 + 0) * n : (1 * 2 + 1) * n], _words(x, 1))  # this rank's words reached the peer
 
 
 @pytest.mark.parametrize("op", ["ApplyAdam", "ApplyAdagrad", "ApplyFtrl", "ApplyRMSProp"])
 def test_peer_allreduce_fused_optimizer_step_emulated_pair(cuda, op):
     """Exchange plus optimizer epilogue in one kernel: two parameter tensors laid end to
-    end, the peer's gradients planted in its slot; the summed gradients and the updated
+    end, the peer's words planted in this rank's area; the summed gradients and the updated
     parameters / states equal the oracle's step on the summed gradients bit for bit."""
     import ctypes as C
 
@@ -88,20 +94,17 @@ def test_peer_allreduce_fused_optimizer_step_emulated_pair(cuda, op):
     params = [torch.from_numpy(p).cuda() for p in host_p]
     states = [[torch.from_numpy(v).cuda() for v in st] for st in host_s]
     data = torch.from_numpy(x).cuda()
-    buf0, buf1 = torch.zeros(2 * n, device="cuda"), torch.zeros(2 * n, device="cuda")
-    buf1[n:] = torch.from_numpy(y).cuda()
-    pad0 = torch.zeros(2, dtype=torch.int32, device="cuda")
-    pad1 = torch.zeros(2, dtype=torch.int32, device="cuda")
-    pad0[1] = 1
+    a0, a1 = _area(2, n), _area(2, n)
+    a0[3 * n : 4 * n] = _words(torch.from_numpy(y).cuda(), 1)
     epoch = torch.zeros(64, dtype=torch.int32, device="cuda")
     status = torch.zeros(1, dtype=torch.int32, device="cuda")
     P = C.c_void_p * 2
     offs = (C.c_int64 * 3)(0, sizes[0], n)
     s2 = P(*[st[1].data_ptr() for st in states]) if nst == 2 else None
-    slot_tab, pad_tab = _ptrs([buf0, buf1]), _ptrs([pad0, pad1])  # alive until the kernel has run
-    L.call("b200_peer_allreduce_apply_f32", data.data_ptr(), n, slot_tab.data_ptr(), pad_tab.data_ptr(),
-           0, 2, epoch.data_ptr(), status.data_ptr(), 1 << 20, 1.0, 1, ops._OPT_KIND[op], 2, offs,
-           P(*[q.data_ptr() for q in params]), P(*[st[0].data_ptr() for st in states]), s2, 0.01, ops.stream_ptr())
+    tab = _ptrs([a0, a1])  # alive until the kernel has run
+    L.call("b200_peer_allreduce_apply_f32", data.data_ptr(), n, tab.data_ptr(), n, 0, 2, epoch.data_ptr(), status.data_ptr(),
+           1 << 20, 1.0, ops._OPT_KIND[op], 2, offs, P(*[q.data_ptr() for q in params]),
+           P(*[st[0].data_ptr() for st in states]), s2, 0.01, ops.stream_ptr())
     torch.cuda.synchronize()
     assert int(status.item()) == 0
     g = x + y
@@ -118,12 +121,10 @@ def test_peer_allreduce_fused_optimizer_step_emulated_pair(cuda, op):
 def test_peer_allreduce_wait_gives_up(cuda):
     n = 4096
     x = torch.arange(n, dtype=torch.float32, device="cuda")
-    bufs = [torch.zeros(2 * n, device="cuda") for _ in range(2)]
-    pads = [torch.zeros(2, dtype=torch.int32, device="cuda") for _ in range(2)]
     epoch = torch.zeros(64, dtype=torch.int32, device="cuda")
     status = torch.zeros(1, dtype=torch.int32, device="cuda")
     d = x.clone()
-    _run(d, bufs, pads, 0, 2, epoch, status, 2000, 1.0, 1)  # nobody raises rank 1's flag
+    _run(d, [_area(2, n), _area(2, n)], n, 0, 2, epoch, status, 2000, 1.0)  # rank 1 never sends
     assert int(status.item()) == 4  # B200_ERR_TIMEOUT
     assert torch.equal(d, x)
     assert int(epoch[0].item()) == 0
