@@ -384,6 +384,15 @@ int b200_conv2d_wgrad_tc(const float* x, const float* dy, float* dw, int64_t N, 
 int b200_peer_allreduce_blocks(int64_t n);
 int b200_peer_allreduce_f32(float* data, int64_t n, const void* bufs_dev, int64_t capacity, int rank, int world,
                             unsigned int* epoch, int* status, int64_t spin_limit, float scale, void* stream);
+/* The same exchange over `count` (<= 64) fp32 tensors laid end to end, without packing
+ * them into one buffer: tensors[j] holds values [offsets[j], offsets[j + 1]) and receives
+ * their sums in place (offsets[0] = 0, offsets[count] = total <= capacity). kind >= 0 adds
+ * the optimizer epilogue of b200_peer_allreduce_apply_f32 on param / s1 / s2; kind -1 is
+ * the plain sum. Host arrays of device pointers. */
+int b200_peer_allreduce_tensors_f32(int count, const int64_t* offsets, float* const* tensors, const void* bufs_dev,
+                                    int64_t capacity, int rank, int world, unsigned int* epoch, int* status, int64_t spin_limit,
+                                    float scale, int kind, float* const* param, float* const* s1, float* const* s2, float lr,
+                                    void* stream);
 /* cudaMemsetAsync of a device range (clears a signal pad before its first use). */
 int b200_memset_async(void* p, int value, size_t bytes, void* stream);
 

@@ -101,6 +101,8 @@ SIGNATURES = {
     "b200_peer_allreduce_blocks": ([_I64], C.c_int),
     "b200_peer_allreduce_f32": ([_P, _I64, _P, _I64, C.c_int, C.c_int, _P, _P, _I64, _F32, _P], C.c_int),
     "b200_memset_async": ([_P, C.c_int, C.c_size_t, _P], C.c_int),
+    "b200_peer_allreduce_tensors_f32": ([C.c_int, _P, _P, _P, _I64, C.c_int, C.c_int, _P, _P, _I64, _F32, C.c_int, _P, _P, _P,
+                                         _F32, _P], C.c_int),
     "b200_optimizer_default_lr": ([C.c_int], C.c_double),
     "b200_apply_optimizer_f32": ([C.c_int, C.c_int, _P, _P, _P, _P, _P, _P, _P, _P, _F32, _P], C.c_int),
     "b200_peer_allreduce_apply_f32": ([_P, _I64, _P, _I64, C.c_int, C.c_int, _P, _P, _I64, _F32, C.c_int, C.c_int, _P, _P,

@@ -107,6 +107,39 @@ class PeerAllReduce:
                P(*[step.params[i].data_ptr() for i in indices]), P(*[step.states[i][0].data_ptr() for i in indices]), s2,
                float(step.lr), ops.stream_ptr())
 
+    def tensors(self, ts: Sequence[torch.Tensor], scale: float = 1.0, step: "OptimizerStep | None" = None,
+                indices: Sequence[int] = ()) -> None:
+        """Sum each of the contiguous fp32 tensors ``ts`` over the ranks in place (times
+        ``scale``) in one kernel, without packing them into one buffer. With ``step``, the
+        same kernel applies ``step``'s optimizer to its parameters ``indices`` (one per
+        tensor, in order)."""
+        import ctypes as C
+
+        from . import _lib as L
+        from . import ops
+
+        if not 1 <= len(ts) <= self.MAX_SEGMENTS:
+            raise ValueError(f"PeerAllReduce.tensors takes 1..{self.MAX_SEGMENTS} tensors")
+        offs = [0]
+        for t in ts:
+            if t.dtype != torch.float32 or not t.is_contiguous():
+                raise ValueError("PeerAllReduce.tensors takes contiguous fp32 tensors")
+            offs.append(offs[-1] + t.numel())
+        if offs[-1] > self.max_numel:
+            raise ValueError("PeerAllReduce.tensors: more values than the receive capacity")
+        P = C.c_void_p * len(ts)
+        kind, par, st1, st2, lr = -1, None, None, None, 0.0
+        if step is not None:
+            if len(indices) != len(ts):
+                raise ValueError("one parameter index per tensor")
+            kind, lr = step.kind, float(step.lr)
+            par = P(*[step.params[i].data_ptr() for i in indices])
+            st1 = P(*[step.states[i][0].data_ptr() for i in indices])
+            st2 = P(*[step.states[i][1].data_ptr() for i in indices]) if step.nstates == 2 else None
+        L.call("b200_peer_allreduce_tensors_f32", len(ts), (C.c_int64 * len(offs))(*offs), P(*[t.data_ptr() for t in ts]),
+               int(self.handle.buffer_ptrs_dev), self.max_numel, self.rank, self.world, self.epoch.data_ptr(),
+               self.status.data_ptr(), self.SPIN_LIMIT, float(scale), kind, par, st1, st2, lr, ops.stream_ptr())
+
     def check(self) -> None:
         """Raise TimeoutError if a wait for a peer gave up since construction."""
         code = int(self.status.item())
@@ -162,11 +195,14 @@ class GradAllReduce:
         self.peer: PeerAllReduce | None = None
         self._peer_failed = False
 
-    def _peer_for(self, t: torch.Tensor) -> PeerAllReduce | None:
+    def _peer_for(self, t: torch.Tensor, numel: int | None = None) -> PeerAllReduce | None:
+        """The peer-memory path for ``numel`` (default ``t.numel()``) contiguous fp32 values
+        on ``t``'s device, set up on first use, or None where it does not apply."""
         import torch.distributed as dist
 
+        numel = t.numel() if numel is None else numel
         if (not t.is_cuda or t.dtype != torch.float32 or not t.is_contiguous()
-                or t.numel() * 4 > self.peer_below or dist.get_backend(self.group) != "nccl"):
+                or numel * 4 > self.peer_below or dist.get_backend(self.group) != "nccl"):
             return None
         if self.peer is None and not self._peer_failed:
             # collective set-up; every rank reports success, and the peer path is used only
@@ -265,6 +301,12 @@ class GradAllReduce:
                 continue
             ts = [grads[i] for i in b]
             n = sum(t.numel() for t in ts)
+            if (world > 1 and len(b) <= PeerAllReduce.MAX_SEGMENTS and ts[0].dtype == torch.float32
+                    and all(t.is_contiguous() for t in ts)):
+                peer = self._peer_for(ts[0], n)
+                if peer is not None:  # one kernel over the tensors themselves: no packing copies
+                    peer.tensors(ts, 1.0 / world if self.op == "mean" else 1.0, step, b if step is not None else ())
+                    continue
             key = (ts[0].dtype, str(ts[0].device), n)
             flat = self._flat.get(key)
             if flat is None:

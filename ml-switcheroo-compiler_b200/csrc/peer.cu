@@ -30,17 +30,32 @@ constexpr int PT = 512;  // threads per block
 constexpr int MAXS = 64;  // parameter segments of a fused optimizer epilogue
 constexpr int MAXB = 64;  // blocks (call counters) per launch
 
-// Optional optimizer epilogue: the summed values are the gradients of `count` parameter
-// tensors laid end to end, segment j covering [off[j], off[j + 1]); each summed element
-// also updates its parameter and state elements in place.
+// Segments: the values are `count` tensors laid end to end, segment j covering
+// [off[j], off[j + 1]); they are read from and written back to those tensors (`direct`),
+// and / or, with an optimizer, they are the gradients of the parameters p[j] and each
+// summed element also updates its parameter and state elements in place.
 struct Segs {
-  int count, kind;
+  int count;   // segments; 0: one flat buffer and no optimizer
+  int kind;    // optimizer kind, -1 for none
+  int direct;  // the values live in the segments' own tensors d[j], not in one flat buffer
   opt::Consts k;
   int64_t off[MAXS + 1];
+  float* d[MAXS];
   float* p[MAXS];
   float* s1[MAXS];
   float* s2[MAXS];
 };
+
+// the segment holding element i: the last j with off[j] <= i
+__device__ __forceinline__ int seg_of(const Segs& S, int64_t i) {
+  int lo = 0, hi = S.count - 1;
+  while (lo < hi) {
+    const int mid = (lo + hi + 1) >> 1;
+    if (S.off[mid] <= i) lo = mid;
+    else hi = mid - 1;
+  }
+  return lo;
+}
 
 constexpr int EPT = 8;  // values per thread: a block covers PT * EPT values
 
@@ -68,7 +83,16 @@ __global__ void __launch_bounds__(PT) peer_allreduce_kernel(float* __restrict__ 
 #pragma unroll
   for (int k = 0; k < EPT; ++k) {
     const int64_t i = lo + (int64_t)k * PT + tid;
-    mine[k] = i < n ? data[i] : 0.f;
+    if (i < n) {
+      if (S.direct) {
+        const int j = seg_of(S, i);
+        mine[k] = S.d[j][i - S.off[j]];
+      } else {
+        mine[k] = data[i];
+      }
+    } else {
+      mine[k] = 0.f;
+    }
     if (i < n) {
       const uint64_t w = ((uint64_t)e << 32) | (uint64_t)__float_as_uint(mine[k]);
       for (int q = 0; q < world; ++q)
@@ -118,23 +142,19 @@ __global__ void __launch_bounds__(PT) peer_allreduce_kernel(float* __restrict__ 
     const int64_t i = lo + (int64_t)k * PT + tid;
     if (i >= n) continue;
     const float g = sum[k] * scale;
-    data[i] = g;
-    if (S.count > 0) {  // the parameter segment of element i (binary search), then its update
-      int lo_s = 0, hi_s = S.count - 1;
-      while (lo_s < hi_s) {
-        const int mid = (lo_s + hi_s + 1) >> 1;
-        if (S.off[mid] <= i) lo_s = mid;
-        else hi_s = mid - 1;
-      }
-      const int64_t j = i - S.off[lo_s];
-      float* p = S.p[lo_s];
-      float* a = S.s1[lo_s];
-      float* bb = S.s2[lo_s];
+    const int j = S.count > 0 ? seg_of(S, i) : 0;
+    const int64_t jj = S.count > 0 ? i - S.off[j] : i;
+    if (S.direct) S.d[j][jj] = g;
+    else data[i] = g;
+    if (S.kind >= 0) {  // optimizer step on element jj of parameter tensor j
+      float* p = S.p[j];
+      float* a = S.s1[j];
+      float* bb = S.s2[j];
       float po, ao, bo;
-      opt::update(S.kind, S.k, p[j], a[j], bb ? bb[j] : 0.f, g, po, ao, bo);
-      p[j] = po;
-      a[j] = ao;
-      if (bb) bb[j] = bo;
+      opt::update(S.kind, S.k, p[jj], a[jj], bb ? bb[jj] : 0.f, g, po, ao, bo);
+      p[jj] = po;
+      a[jj] = ao;
+      if (bb) bb[jj] = bo;
     }
   }
   if (tid == 0) epoch[b] = e;
@@ -151,7 +171,7 @@ extern "C" int b200_peer_allreduce_blocks(int64_t n) {
 
 static int peer_launch(float* data, int64_t n, const void* bufs_dev, int64_t capacity, int rank, int world, unsigned int* epoch,
                        int* status, int64_t spin_limit, float scale, const peer::Segs& S, void* stream) {
-  B200_REQUIRE(data && bufs_dev && epoch && status, "peer_allreduce: null pointer");
+  B200_REQUIRE((data || S.direct) && bufs_dev && epoch && status, "peer_allreduce: null pointer");
   B200_REQUIRE(n >= 0 && world >= 1 && world <= 64 && rank >= 0 && rank < world, "peer_allreduce: bad rank %d / world %d", rank,
                world);
   B200_REQUIRE(n <= capacity, "peer_allreduce: %lld values above the receive capacity %lld", (long long)n, (long long)capacity);
@@ -169,6 +189,8 @@ extern "C" int b200_peer_allreduce_f32(float* data, int64_t n, const void* bufs_
                                        unsigned int* epoch, int* status, int64_t spin_limit, float scale, void* stream) {
   peer::Segs S;
   S.count = 0;
+  S.kind = -1;
+  S.direct = 0;
   return peer_launch(data, n, bufs_dev, capacity, rank, world, epoch, status, spin_limit, scale, S, stream);
 }
 
@@ -185,6 +207,7 @@ extern "C" int b200_peer_allreduce_apply_f32(float* data, int64_t n, const void*
   peer::Segs S;
   S.count = count;
   S.kind = kind;
+  S.direct = 0;
   S.k = opt::consts_for(kind, lr);
   for (int j = 0; j < count; ++j) {
     B200_REQUIRE(offsets[j + 1] >= offsets[j], "peer_allreduce_apply: offsets must not decrease");
@@ -196,6 +219,38 @@ extern "C" int b200_peer_allreduce_apply_f32(float* data, int64_t n, const void*
   }
   S.off[count] = offsets[count];
   return peer_launch(data, n, bufs_dev, capacity, rank, world, epoch, status, spin_limit, scale, S, stream);
+}
+
+// The same exchange over `count` (<= 64) tensors laid end to end without packing them:
+// values are read from and the sums written back to tensors[j], which covers
+// [offsets[j], offsets[j + 1]). kind >= 0 adds the optimizer epilogue on param / s1 / s2
+// (as b200_peer_allreduce_apply_f32); kind -1 is the plain sum.
+extern "C" int b200_peer_allreduce_tensors_f32(int count, const int64_t* offsets, float* const* tensors, const void* bufs_dev,
+                                               int64_t capacity, int rank, int world, unsigned int* epoch, int* status,
+                                               int64_t spin_limit, float scale, int kind, float* const* param,
+                                               float* const* s1, float* const* s2, float lr, void* stream) {
+  B200_REQUIRE(count >= 1 && count <= peer::MAXS, "peer_allreduce_tensors: %d tensors not in [1, %d]", count, peer::MAXS);
+  B200_REQUIRE(offsets && tensors && offsets[0] == 0, "peer_allreduce_tensors: null table or offsets[0] != 0");
+  B200_REQUIRE(kind >= -1 && kind <= 3, "peer_allreduce_tensors: kind %d not in [-1, 3]", kind);
+  const bool opt_on = kind >= 0, two = kind >= 0 && kind != opt::ADAGRAD;
+  B200_REQUIRE(!opt_on || (param && s1 && (!two || s2)), "peer_allreduce_tensors: optimizer tables missing");
+  peer::Segs S;
+  S.count = count;
+  S.kind = kind;
+  S.direct = 1;
+  S.k = opt::consts_for(opt_on ? kind : 0, lr);
+  for (int j = 0; j < count; ++j) {
+    B200_REQUIRE(offsets[j + 1] >= offsets[j], "peer_allreduce_tensors: offsets must not decrease");
+    B200_REQUIRE(offsets[j + 1] == offsets[j] || tensors[j], "peer_allreduce_tensors: null tensor %d", j);
+    B200_REQUIRE(!opt_on || (param[j] && s1[j] && (!two || s2[j])), "peer_allreduce_tensors: null pointer for tensor %d", j);
+    S.off[j] = offsets[j];
+    S.d[j] = tensors[j];
+    S.p[j] = opt_on ? param[j] : nullptr;
+    S.s1[j] = opt_on ? s1[j] : nullptr;
+    S.s2[j] = two ? s2[j] : nullptr;
+  }
+  S.off[count] = offsets[count];
+  return peer_launch(nullptr, offsets[count], bufs_dev, capacity, rank, world, epoch, status, spin_limit, scale, S, stream);
 }
 
 extern "C" int b200_memset_async(void* p, int value, size_t bytes, void* stream) {

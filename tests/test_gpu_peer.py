@@ -118,6 +118,54 @@ def test_peer_allreduce_fused_optimizer_step_emulated_pair(cuda, op):
         lo += size
 
 
+@pytest.mark.parametrize("with_step", [False, True])
+def test_peer_allreduce_tensors_in_place_emulated_pair(cuda, with_step):
+    """The exchange over two tensors without packing (values read from and sums written
+    back to the tensors themselves), optionally with the Adam epilogue; the peer's words
+    planted in this rank's area as in the flat case."""
+    import ctypes as C
+
+    from b200 import _lib as L
+    from b200 import ops
+    from oracle import evaluator as O
+
+    rng = np.random.default_rng(11)
+    sizes = [1000, 3333]
+    n = sum(sizes)
+    xs = [rng.standard_normal(k).astype(np.float32) for k in sizes]
+    y = rng.standard_normal(n).astype(np.float32)
+    ts = [torch.from_numpy(x).cuda() for x in xs]
+    a0, a1 = _area(2, n), _area(2, n)
+    a0[3 * n : 4 * n] = _words(torch.from_numpy(y).cuda(), 1)
+    epoch = torch.zeros(64, dtype=torch.int32, device="cuda")
+    status = torch.zeros(1, dtype=torch.int32, device="cuda")
+    P = C.c_void_p * 2
+    offs = (C.c_int64 * 3)(0, sizes[0], n)
+    host_p = [rng.standard_normal(k).astype(np.float32) for k in sizes]
+    params = [torch.from_numpy(q).cuda() for q in host_p]
+    ms = [torch.zeros(k, device="cuda") for k in sizes]
+    vs = [torch.zeros(k, device="cuda") for k in sizes]
+    tab = _ptrs([a0, a1])  # alive until the kernel has run
+    L.call("b200_peer_allreduce_tensors_f32", 2, offs, P(*[t.data_ptr() for t in ts]), tab.data_ptr(), n, 0, 2,
+           epoch.data_ptr(), status.data_ptr(), 1 << 20, 0.5, ops._OPT_KIND["ApplyAdam"] if with_step else -1,
+           P(*[q.data_ptr() for q in params]) if with_step else None, P(*[m.data_ptr() for m in ms]) if with_step else None,
+           P(*[v.data_ptr() for v in vs]) if with_step else None, 0.01, ops.stream_ptr())
+    torch.cuda.synchronize()
+    assert int(status.item()) == 0
+    lo = 0
+    for k, size in enumerate(sizes):
+        g = (xs[k] + y[lo : lo + size]) * np.float32(0.5)
+        np.testing.assert_array_equal(ts[k].cpu().numpy(), g)
+        if with_step:
+            ref = O.execute_op("ApplyAdam", host_p[k], np.zeros(size, np.float32), np.zeros(size, np.float32), g, lr=0.01)
+            for r, t in zip(ref, (params[k], ms[k], vs[k])):
+                np.testing.assert_array_equal(t.cpu().numpy(), r)
+        else:
+            np.testing.assert_array_equal(params[k].cpu().numpy(), host_p[k])
+        lo += size
+    assert torch.equal(a1[2 * n : 3 * n], _words(torch.from_numpy(np.concatenate(xs)).cuda(), 1))
+
+
 def test_peer_allreduce_wait_gives_up(cuda):
     n = 4096
     x = torch.arange(n, dtype=torch.float32, device="cuda")
