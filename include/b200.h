@@ -36,6 +36,7 @@ extern "C" {
 #define B200_I64 2
 #define B200_BOOL 3 /* one byte, 0/1 */
 #define B200_I32 4
+#define B200_F64 5
 
 int b200_abi_version(void);
 const char* b200_last_error(void);
@@ -279,10 +280,42 @@ int b200_rowfused_fwd_bwd(const float* x, const float* a, const float* b, const 
  * B200_ERR_ARG (use b200_rowfused_fwd_bwd then). The first call on each device looks up
  * the array's device address (set-up, no allocation); make that first call before any
  * stream capture. Nothing must be zeroed beforehand. Calls that overlap on the GPU share
- * the array and race: serialise them. Outputs as b200_rowfused_fwd_bwd. */
+ * the array and race: serialise them. The cached address does not survive a
+ * cudaDeviceReset of that device: do not call this entry point again after one in the
+ * same process. Outputs as b200_rowfused_fwd_bwd. */
 int b200_rowfused_fwd_bwd_noalloc(const float* x, const float* a, const float* b, const float* gamma, const float* beta,
                                   const float* cot, float* y, int64_t* am, float* dx, float* da, float* db, float* dgamma,
                                   float* dbeta, int64_t rows, int64_t cols, float eps, void* stream);
+
+/* Gather (numpy/eager/indexing.py:312-332: np.take_along_axis(tensor, index, axis=dim))
+ * and TakeAlongAxis on any axis (numpy/eager/advanced_indexing.py:163-177): over the
+ * output index space `shape` (ndim <= B200_GATHER_MAX_DIM, the broadcast of the tensor's
+ * and the indices' shapes outside `axis`), y[i] = x[i with i[axis] replaced by idx[i]].
+ * x_strides / idx_strides are element strides per output axis (0 = broadcast); the x
+ * entry at `axis` is the stride along the gathered axis of length axis_len. Elements are
+ * copied as raw elem_bytes (1, 2, 4 or 8) values, so every dtype keeps its bits. Negative
+ * indices count from the end; an index outside [-axis_len, axis_len) sets the device
+ * error flag (b200_check_device_error) and writes zero. y is dense row-major. */
+#define B200_GATHER_MAX_DIM 8
+int b200_gather_axis(int elem_bytes, const void* x, const int64_t* x_strides, const int64_t* idx, const int64_t* idx_strides,
+                     void* y, const int64_t* shape, int ndim, int axis, int64_t axis_len, void* stream);
+
+/* Element copy between two strided views of one index space `shape` (ndim <=
+ * B200_GATHER_MAX_DIM; element strides, src strides may be 0 to broadcast): the value
+ * write of the interpreter's IndexPut / SetItem node (interpreter/evaluator.py:488-508,
+ * `arr[key] = val` after the Clone of the base), with dst a view of the cloned base.
+ * Raw elem_bytes (1, 2, 4 or 8) values. The views must not overlap. */
+int b200_copy_strided(int elem_bytes, const void* src, const int64_t* src_strides, void* dst, const int64_t* dst_strides,
+                      const int64_t* shape, int ndim, void* stream);
+
+/* OneHot (numpy/eager/math_advanced/math_general.py:710-736): y = eye(depth)[idx] *
+ * (on - off) + off, cast to out_dtype (B200_F32, B200_F64, B200_I64, B200_I32, B200_BOOL),
+ * laid out [outer, depth, inner] where idx is [outer, inner] (the class axis moved to
+ * position `axis` of the indices' shape). The arithmetic matches numpy's: fp32 outputs
+ * round (on - off) and off to fp32 and compute in fp32; the others compute in fp64 and
+ * then convert (truncation for integers, != 0 for bool). Index rules as b200_gather_axis. */
+int b200_one_hot(const int64_t* idx, void* y, int out_dtype, int64_t outer, int64_t depth, int64_t inner, double on_value,
+                 double off_value, void* stream);
 
 /* ReLU-with-bias backward in one pass: gp = g * mask (Multiply(cot, Greater(pre, 0)),
  * the Relu VJP of transforms/autodiff_rules/vjp_rules.yaml:25-27 evaluated by
@@ -378,8 +411,18 @@ int b200_conv2d_wgrad_tc(const float* x, const float* dy, float* dw, int64_t N, 
  *             2 * world * capacity 64-bit words, zero before the first call
  *   epoch:    this rank's per-block call counters (64 uint32, zero at start); every rank
  *             must make the same calls with the same n
- *   status:   device int, set to B200_ERR_TIMEOUT when a peer's words did not arrive (the
- *             values of that block are then left unchanged)
+ *   status:   device int, set to B200_ERR_TIMEOUT when a peer's words did not arrive. The
+ *             values of that block are left unchanged on this rank, but peers that
+ *             received this rank's words did complete the call, so the ranks no longer
+ *             agree on call numbers. A timeout is therefore fatal: while status is non-zero
+ *             every later call returns at once (no values sent, summed or updated), so the
+ *             peers time out too and no rank ever adds a stale word. Re-opening the
+ *             exchange needs a collective reset: receive areas cleared, epoch and status
+ *             zeroed on every rank. With the optimizer epilogue, parameters may differ
+ *             across ranks after a timeout.
+ * Every call of one rank must be issued on one stream, in call order (CUDA graph replays
+ * included): the double-buffer argument above relies on call e - 2 having finished before
+ * call e starts on this rank.
  * n <= capacity and n <= 64 * 4096. b200_peer_allreduce_blocks gives the blocks for n. */
 int b200_peer_allreduce_blocks(int64_t n);
 int b200_peer_allreduce_f32(float* data, int64_t n, const void* bufs_dev, int64_t capacity, int rank, int world,

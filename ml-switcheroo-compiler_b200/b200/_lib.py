@@ -16,7 +16,8 @@ from .errors import BackendNotSupportedError, UnimplementedMathError
 PKG = os.path.dirname(os.path.abspath(__file__))
 LIB_PATH = os.path.join(PKG, "libb200.so")
 
-F32, BF16, I64, BOOL, I32 = 0, 1, 2, 3, 4
+F32, BF16, I64, BOOL, I32, F64 = 0, 1, 2, 3, 4, 5
+GATHER_MAX_DIM = 8
 OK, ERR_ARG, ERR_DTYPE, ERR_CUDA, ERR_TIMEOUT, ERR_UNSUPPORTED = 0, 1, 2, 3, 4, 5
 
 EW_MAX_IN, EW_MAX_OUT, EW_MAX_DIM, EW_MAX_INS, EW_MAX_REG = 8, 4, 6, 48, 16
@@ -87,6 +88,9 @@ SIGNATURES = {
     "b200_take_along_last": ([_P, _P, _P, _I64, _I64, _I64, _P], C.c_int),
     "b200_scatter_add_last": ([_P, _P, _P, _P, _I64, _I64, _I64, _P], C.c_int),
     "b200_take_rows": ([_I32, _P, _P, _P, _I64, _I64, _I64, _P], C.c_int),
+    "b200_gather_axis": ([_I32, _P, C.POINTER(_I64), _P, C.POINTER(_I64), _P, C.POINTER(_I64), _I32, _I32, _I64, _P], C.c_int),
+    "b200_copy_strided": ([_I32, _P, C.POINTER(_I64), _P, C.POINTER(_I64), C.POINTER(_I64), _I32, _P], C.c_int),
+    "b200_one_hot": ([_P, _P, _I32, _I64, _I64, _I64, C.c_double, C.c_double, _P], C.c_int),
     "b200_scatter_add_rows": ([_P, _P, _P, _I64, _I64, _I64, _I32, _P, C.c_size_t, _P], C.c_int),
     "b200_scatter_add_rows_workspace_bytes": ([_I64, _I64], C.c_size_t),
     "b200_gemm": (

@@ -18,21 +18,28 @@ Unknown ops raise ``UnimplementedMathError``; there is no CPU fallback.
 
 from __future__ import annotations
 
-import weakref
+from collections import OrderedDict
 from typing import Any, Callable, Mapping
 
 import torch
 
 from . import ops
 from .executor import CompiledGraph, GraphRunner
+from .graph import coerce, content_key
 
 
 class B200Backend:
     """Backend plugin for NVIDIA B200 (sm_100a)."""
 
     name = "b200"
-    _runners: "weakref.WeakKeyDictionary[Any, GraphRunner]" = weakref.WeakKeyDictionary()
-    _runners_by_id: dict[int, GraphRunner] = {}
+    # runners (one plan per input signature each) keyed by the graph's content: node ids,
+    # op types, inputs, attributes, shape metadata, graph inputs / outputs. The reference
+    # builds a new LogicalGraph object per backward() call and its graphs are unhashable,
+    # so identity keys would miss every time and could alias a dead graph's plan to a new
+    # graph that reuses its address; content keys do neither. Least recently used first
+    # out beyond MAX_RUNNERS.
+    MAX_RUNNERS = 16
+    _runners: "OrderedDict[str, GraphRunner]" = OrderedDict()
 
     # ---- per-op path -------------------------------------------------------------
     @classmethod
@@ -86,28 +93,43 @@ class B200Backend:
     # ---- whole-graph hooks -----------------------------------------------------------
     @classmethod
     def _runner(cls, graph: Any) -> GraphRunner:
-        try:
-            r = cls._runners.get(graph)
-        except TypeError:
-            r = cls._runners_by_id.get(id(graph))
+        g = coerce(graph)
+        key = content_key(g)
+        r = cls._runners.get(key)
         if r is None:
-            r = GraphRunner(graph)
-            try:
-                cls._runners[graph] = r
-            except TypeError:
-                cls._runners_by_id[id(graph)] = r
+            r = GraphRunner(g)
+            cls._runners[key] = r
+            while len(cls._runners) > cls.MAX_RUNNERS:
+                cls._runners.popitem(last=False)
+        else:
+            cls._runners.move_to_end(key)
         return r
 
     @classmethod
     def execute_graph(cls, graph: Any, inputs: Mapping[str, Any]) -> dict[str, Any]:
-        """Run a whole fwd+bwd graph: fused kernels, dead nodes pruned."""
+        """Run a whole fwd+bwd graph: fused kernels, dead nodes pruned. The returned
+        tensors are fresh per call (the caller owns them)."""
         return cls._runner(graph)(dict(inputs))
 
     @classmethod
-    def compile_graph(cls, graph: Any) -> Callable[[Mapping[str, Any]], Mapping[str, Any]]:
-        """A replayable executable (static buffers + one CUDA graph per input signature)."""
+    def compile_graph(cls, graph: Any, alias_outputs: bool = False) -> Callable[[Mapping[str, Any]], Mapping[str, Any]]:
+        """A replayable executable: static input buffers plus one captured CUDA graph per
+        input signature. Host inputs (pinned: asynchronous) are copied straight into the
+        static buffers.
+
+        Each call returns fresh output tensors (device copies of the graph's static
+        outputs), so results held from an earlier call are never overwritten, as with
+        ``execute_graph``. ``alias_outputs=True`` skips that copy: every call then returns
+        the same static output tensors, which the next call overwrites in place."""
         cg = CompiledGraph(graph)
-        return lambda inputs: cg(dict(inputs))
+        if alias_outputs:
+            return lambda inputs: cg(dict(inputs))
+
+        def run(inputs: Mapping[str, Any]) -> dict[str, Any]:
+            out = cg(dict(inputs))
+            return {k: (ops.copy(v) if isinstance(v, torch.Tensor) else v) for k, v in out.items()}
+
+        return run
 
 
 def register() -> type[B200Backend]:

@@ -44,8 +44,15 @@ class PeerAllReduce:
 
     Construction is collective (symmetric-memory rendezvous on ``group``) and must be
     followed by one more collective on ``group`` before the first call, so that every
-    receive area is clear. Every rank must then make the same calls with the same sizes. A
-    wait that gives up sets a status that ``check()`` turns into ``TimeoutError``.
+    receive area is clear. Every rank must then make the same calls with the same sizes,
+    and issue all of them on one stream in call order (CUDA graph replays included): the
+    receive area is double-buffered by call parity, which is safe only while call e - 2 of
+    a rank has finished before its call e starts.
+
+    A wait that gives up sets a status word, and from then on every call on that rank
+    returns at once without sending, summing or updating anything; its peers' next waits
+    then give up too. ``check()`` turns the status into ``TimeoutError``; ``reset()``
+    (collective) clears the receive areas, call counters and status on every rank.
     """
 
     SPIN_LIMIT = 1 << 24  # polls per thread (backing off to ~256 ns sleeps): seconds, not forever
@@ -98,9 +105,12 @@ class PeerAllReduce:
             raise ValueError(f"a fused optimizer epilogue takes 1..{self.MAX_SEGMENTS} tensors")
         offs = [0]
         for i in indices:
+            step.check_matches(i)
             offs.append(offs[-1] + step.params[i].numel())
         if offs[-1] != n:
             raise ValueError("the gradients of `indices` must fill `flat` exactly")
+        if any(step.params[i].device != flat.device for i in indices):
+            raise ValueError("parameters and gradients must be on the same device")
         P = C.c_void_p * len(indices)
         s2 = P(*[step.states[i][1].data_ptr() for i in indices]) if step.nstates == 2 else None
         L.call("b200_peer_allreduce_apply_f32", *head, step.kind, len(indices), (C.c_int64 * len(offs))(*offs),
@@ -132,6 +142,8 @@ class PeerAllReduce:
         if step is not None:
             if len(indices) != len(ts):
                 raise ValueError("one parameter index per tensor")
+            for t, i in zip(ts, indices):
+                step.check_matches(i, t)
             kind, lr = step.kind, float(step.lr)
             par = P(*[step.params[i].data_ptr() for i in indices])
             st1 = P(*[step.states[i][0].data_ptr() for i in indices])
@@ -140,11 +152,33 @@ class PeerAllReduce:
                int(self.handle.buffer_ptrs_dev), self.max_numel, self.rank, self.world, self.epoch.data_ptr(),
                self.status.data_ptr(), self.SPIN_LIMIT, float(scale), kind, par, st1, st2, lr, ops.stream_ptr())
 
+    def failed(self) -> bool:
+        """True if a wait for a peer gave up on this rank since construction or the last
+        ``reset()`` (reads the device status word: synchronises with the stream)."""
+        return int(self.status.item()) != 0
+
     def check(self) -> None:
-        """Raise TimeoutError if a wait for a peer gave up since construction."""
+        """Raise TimeoutError if a wait for a peer gave up on this rank."""
         code = int(self.status.item())
         if code:
-            raise TimeoutError(f"peer all-reduce: a peer's values did not arrive (status {code})")
+            raise TimeoutError(f"peer all-reduce: a peer's values did not arrive (status {code}); the exchange is "
+                               "stopped on this rank until a collective reset()")
+
+    def reset(self) -> None:
+        """Collective: clear this rank's receive area, call counters and status, then wait
+        for every rank to have done the same, so the next call starts from call 1 on all
+        ranks. Every rank of the group must call it, with no exchange in flight."""
+        import torch.distributed as dist
+
+        from . import _lib as L
+        from . import ops
+
+        torch.cuda.synchronize(self.device)
+        L.call("b200_memset_async", self.buf.data_ptr(), 0, self.buf.numel() * 8, ops.stream_ptr())
+        self.epoch.zero_()
+        self.status.zero_()
+        torch.cuda.synchronize(self.device)
+        dist.barrier(group=self.group)
 
 
 class OptimizerStep:
@@ -168,6 +202,17 @@ class OptimizerStep:
         self.params = list(params)
         self.nstates = 1 if op == "ApplyAdagrad" else 2
         self.states = [tuple(torch.zeros_like(p) for _ in range(self.nstates)) for p in self.params]
+
+    def check_matches(self, i: int, grad: torch.Tensor | None = None) -> None:
+        """Raise ValueError unless parameter ``i``, its state arrays and (when given)
+        ``grad`` have the same number of elements and device: the kernels index all of them
+        with the gradient's offsets and cannot check their extents."""
+        p = self.params[i]
+        ts = [p, *self.states[i]] + ([grad] if grad is not None else [])
+        for t in ts:
+            if t.numel() != p.numel() or t.device != p.device:
+                raise ValueError(f"optimizer tensor {i}: parameter {tuple(p.shape)} on {p.device}, but a state or "
+                                 f"gradient has {t.numel()} elements on {t.device}")
 
     def apply(self, indices: Sequence[int], grads: Sequence[torch.Tensor]) -> None:
         """One launch: parameters ``indices`` take one step with ``grads`` (same order)."""
@@ -241,9 +286,25 @@ class GradAllReduce:
         return True
 
     def check(self) -> None:
-        """Raise if a peer-memory exchange gave up waiting for a peer."""
-        if self.peer is not None:
-            self.peer.check()
+        """Collective: raise TimeoutError if a peer-memory exchange gave up waiting on any
+        rank. The ranks agree on the outcome (one small all-reduce), and after a failure
+        every rank drops the peer path and exchanges through NCCL from then on, so no rank
+        keeps using an exchange whose call numbers have diverged. Parameters updated by a
+        fused optimizer epilogue may differ across ranks after a failure: re-broadcast them
+        before continuing. Call it on every rank at the same point (for instance once per
+        step or every few steps)."""
+        import torch.distributed as dist
+
+        if self.peer is None:
+            return
+        bad = torch.tensor([1 if self.peer.failed() else 0], dtype=torch.int32, device=self.peer.device)
+        if dist.get_world_size(self.group) > 1:
+            dist.all_reduce(bad, op=dist.ReduceOp.MAX, group=self.group)
+        if int(bad.item()):
+            self.peer, self._peer_failed = None, True
+            raise TimeoutError("peer all-reduce: a wait for a peer gave up on some rank; the peer path is off and "
+                               "later exchanges use NCCL. Parameters stepped by the fused optimizer may differ "
+                               "across ranks: re-broadcast them.")
 
     def _reduce(self, t: torch.Tensor) -> None:
         import torch.distributed as dist
@@ -285,8 +346,11 @@ class GradAllReduce:
     def __call__(self, grads: Sequence[torch.Tensor], step: OptimizerStep | None = None) -> None:
         import torch.distributed as dist
 
-        if step is not None and len(step.params) != len(grads):
-            raise ValueError("the optimizer step must cover the same tensors as the gradients")
+        if step is not None:
+            if len(step.params) != len(grads):
+                raise ValueError("the optimizer step must cover the same tensors as the gradients")
+            for i, g in enumerate(grads):
+                step.check_matches(i, g)
         world = dist.get_world_size(self.group)
         for b in self.buckets(grads):
             if len(b) == 1:

@@ -30,6 +30,8 @@ ALIASES = ops.ALIASES
 def node_kwargs(node: Node, target: str) -> dict[str, Any]:
     """Attribute -> kwargs rules of ``_prepare_node_kwargs`` (evaluator.py:793-832)."""
     kw = {k: v for k, v in node.attributes.items() if k not in ("var_name", "is_parameter", "param_name")}
+    if target == "Checkpoint":
+        return {}
     conv_like = {"Conv", "Conv1D", "Conv2D", "Conv3D", "ConvTranspose", "ConvTranspose2D", "MaxPool2D", "AvgPool2D", "StridedSlice"}
     if "strides" in kw and target not in conv_like:
         kw.pop("strides")
@@ -81,17 +83,82 @@ def node_step(node: Node) -> Step:
             env[nid] = env[ins[0]] if ins else None
 
         return Step([nid], ins, run_id, "Identity")
+    if op == "Recompute":
+        # _evaluate_recompute_node (evaluator.py:720-735): the original op with its attributes
+        orig = ALIASES.get(str(node.attributes.get("original_op", op)), str(node.attributes.get("original_op", op)))
+        oa = node.attributes.get("original_attrs", {})
+        resolved = Node(nid, orig, list(node.inputs), dict(oa) if isinstance(oa, dict) else {}, node.shape_metadata)
+        st = node_step(resolved)
+        st.label = f"Recompute({st.label})"
+        return st
     target = ALIASES.get(op, op)
+    ins = list(node.inputs)
+    if target in ("Slice", "GetItem", "IndexPut", "SetItem"):
+        return _indexing_step(node, target)
+    if target == "Checkpoint":
+        return _checkpoint_step(node)
     fn = ops.OPS.get(target)
     if fn is None:
         raise UnimplementedMathError(f"Operation {op} is not implemented in the b200 backend.")
     kwargs = node_kwargs(node, target)
-    ins = list(node.inputs)
 
     def run_op(env: dict) -> None:
         env[nid] = fn(*[env[i] for i in ins], **kwargs)
 
     return Step([nid], ins, run_op, target)
+
+
+def _indexing_step(node: Node, target: str) -> Step:
+    """Slice / GetItem / IndexPut / SetItem (evaluator.py:428-508) on device values."""
+    from . import indexing
+
+    nid, ins = node.id, list(node.inputs)
+    kwargs = node_kwargs(node, target)
+    cache: dict = {}  # device index arrays of the key, uploaded on the first (eager) run
+    if target == "Slice":
+
+        def run(env: dict) -> None:
+            env[nid] = indexing.slice_node(env[ins[0]], kwargs, cache)
+
+    elif target == "GetItem":
+        key = indexing.parse_key(kwargs.get("key"))
+
+        def run(env: dict) -> None:
+            env[nid] = indexing.get_item(env[ins[0]], key, cache)
+
+    else:
+        key = indexing.parse_key(kwargs.get("key", kwargs.get("index", 0)))
+
+        def run(env: dict) -> None:
+            env[nid] = indexing.index_put(env[ins[0]], key, env[ins[1]])
+
+    return Step([nid], ins, run, target)
+
+
+def _subgraph_of(node: Node) -> Any:
+    sg = None
+    subs = getattr(node, "subgraphs", None) or {}
+    if isinstance(subs, dict):
+        sg = subs.get("body") or subs.get("subgraph")
+    return sg if sg is not None else node.attributes.get("subgraph")
+
+
+def _checkpoint_step(node: Node) -> Step:
+    """_handle_checkpoint (evaluator.py:511-545): the node's forward subgraph evaluated on
+    its inputs by a nested plan (fused like any graph); one output, or a tuple."""
+    raw = _subgraph_of(node)
+    if raw is None or not hasattr(raw, "inputs") and not (isinstance(raw, dict) and "inputs" in raw):
+        raise AttributeError("Checkpoint node is missing a valid subgraph")
+    sub = coerce(raw)
+    runner = GraphRunner(sub)
+    nid, ins = node.id, list(node.inputs)
+    sg_in = list(sub.inputs)
+
+    def run(env: dict) -> None:
+        res = runner(dict(zip(sg_in, [env[i] for i in ins])))
+        env[nid] = res[sub.outputs[0]] if len(sub.outputs) == 1 else tuple(res[o] for o in sub.outputs)
+
+    return Step([nid], ins, run, "Checkpoint")
 
 
 class Plan:

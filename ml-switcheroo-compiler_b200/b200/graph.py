@@ -27,6 +27,7 @@ class Node:
     attributes: dict[str, Any] = field(default_factory=dict)
     shape_metadata: tuple | None = None
     const_dtype: str | None = None
+    subgraphs: dict[str, Any] = field(default_factory=dict)
 
 
 @dataclass
@@ -69,12 +70,44 @@ class Graph:
         return order
 
 
+def _canon(v: Any) -> Any:
+    """A deterministic, hashable form of an attribute value (arrays by dtype, shape, bytes)."""
+    if isinstance(v, dict):
+        return ("d", tuple(sorted((str(k), _canon(x)) for k, x in v.items())))
+    if isinstance(v, (list, tuple)):
+        return ("l", tuple(_canon(x) for x in v))
+    if hasattr(v, "tobytes") and hasattr(v, "dtype") and hasattr(v, "shape"):
+        return ("a", str(v.dtype), tuple(v.shape), v.tobytes())
+    if isinstance(v, (str, int, float, bool)) or v is None:
+        return (type(v).__name__, v)
+    if hasattr(v, "model_dump"):  # pydantic attribute / subgraph objects
+        return ("m", type(v).__name__, _canon(v.model_dump()))
+    return ("r", type(v).__name__, repr(v))
+
+
+def content_key(g: Graph) -> str:
+    """Digest of everything execution depends on: every node's id, op type, inputs,
+    attributes and shape metadata, and the graph's inputs, outputs and initializer names.
+    Two graphs with the same key run the same plan."""
+    import hashlib
+
+    h = hashlib.sha256()
+    h.update(repr((tuple(g.inputs), tuple(g.outputs), tuple(sorted(g.initializers)))).encode())
+    for nid in sorted(g.nodes):
+        n = g.nodes[nid]
+        h.update(repr((n.id, n.op_type, tuple(n.inputs), _canon(n.attributes), n.shape_metadata, n.const_dtype,
+                       _canon(n.subgraphs))).encode())
+    for k in sorted(g.initializers):
+        h.update(repr(_canon(g.initializers[k])).encode())
+    return h.hexdigest()
+
+
 def from_json(doc: dict) -> Graph:
     nodes = {}
     for n in doc["nodes"]:
         sm = n.get("shape_metadata")
         nodes[n["id"]] = Node(n["id"], n["op_type"], list(n["inputs"]), dict(n.get("attributes") or {}),
-                              tuple(sm) if sm is not None else None, n.get("const_dtype"))
+                              tuple(sm) if sm is not None else None, n.get("const_dtype"), dict(n.get("subgraphs") or {}))
     return Graph(doc.get("name", "graph"), nodes, list(doc["inputs"]), list(doc["outputs"]), {},
                  dict(doc.get("roles", {})), dict(doc.get("output_names", {})),
                  {k: doc[k] for k in ("workload", "dims") if k in doc})
@@ -104,7 +137,9 @@ def coerce(graph: Any) -> Graph:
             import numpy as np
 
             cd = str(np.asarray(attrs.get("value")).dtype)
-        nodes[n.id] = Node(n.id, n.op_type, list(n.inputs), attrs, tuple(sm) if sm is not None else None, cd)
+        subs = getattr(n, "subgraphs", None)
+        nodes[n.id] = Node(n.id, n.op_type, list(n.inputs), attrs, tuple(sm) if sm is not None else None, cd,
+                           dict(subs) if isinstance(subs, dict) else {})
     outs = graph.outputs if isinstance(graph.outputs, list) else [graph.outputs]
     return Graph(getattr(graph, "name", "graph"), nodes, list(graph.inputs), list(outs),
                  dict(getattr(graph, "initializers", None) or {}))

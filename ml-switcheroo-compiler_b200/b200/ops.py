@@ -23,7 +23,8 @@ import torch
 from . import _lib as L
 from .errors import BackendNotSupportedError, UnimplementedMathError
 
-_TORCH2CODE = {torch.float32: L.F32, torch.bfloat16: L.BF16, torch.int64: L.I64, torch.bool: L.BOOL, torch.int32: L.I32}
+_TORCH2CODE = {torch.float32: L.F32, torch.bfloat16: L.BF16, torch.int64: L.I64, torch.bool: L.BOOL, torch.int32: L.I32,
+               torch.float64: L.F64}
 _FLOATS = (torch.float32, torch.bfloat16)
 
 
@@ -592,19 +593,121 @@ def op_layer_norm_beta_grad(dy, axis=-1, **_):  # numpy/eager/nn_ops.py:300-318
 # ----------------------------------------------------------------------------------
 
 
-def op_take_along_axis(x, indices, axis=-1, **_):  # numpy/eager/advanced_indexing.py:163-177
-    if not _last_axis(x, axis) or x.dim() != indices.dim():
-        raise UnimplementedMathError("TakeAlongAxis on a non-last axis")
-    xc = contiguous(cast(x, torch.float32))
-    cols = xc.shape[-1]
-    rows = xc.numel() // cols
-    k = indices.shape[-1]
-    if tuple(indices.shape[:-1]) != tuple(xc.shape[:-1]):
-        raise UnimplementedMathError("TakeAlongAxis with broadcast leading dims")
-    ic = contiguous(indices.to(torch.int64) if indices.dtype != torch.int64 else indices)
-    y = torch.empty(tuple(xc.shape[:-1]) + (k,), dtype=torch.float32, device=device())
-    L.call("b200_take_along_last", xc.data_ptr(), ic.data_ptr(), y.data_ptr(), rows, cols, k, stream_ptr())
+def _int_indices(indices: Any) -> torch.Tensor:
+    """Indices as an int64 CUDA tensor (numpy accepts any integer dtype; floats raise)."""
+    t = indices if isinstance(indices, torch.Tensor) else to_device(indices)
+    if t.dtype == torch.int64:
+        return t
+    if t.dtype in (torch.int32, torch.int16, torch.int8, torch.uint8):
+        return cast(t, torch.int64) if t.dtype == torch.int32 else cast(t.to(torch.int32), torch.int64)
+    raise IndexError("arrays used as indices must be of integer type")
+
+
+def gather_along_axis(x: torch.Tensor, indices: Any, axis: Any) -> torch.Tensor:
+    """np.take_along_axis(x, indices, axis): the other axes of x and indices broadcast;
+    axis=None gathers from x flattened (1-d indices). Any dtype, bits copied unchanged."""
+    idx = _int_indices(indices)
+    if axis is None:
+        if idx.dim() != 1:
+            raise ValueError("when axis=None, `indices` must have a single dimension.")
+        x = contiguous(x).reshape(-1)
+        axis = 0
+    nd = x.dim()
+    if nd == 0 or idx.dim() != nd:
+        raise ValueError("`indices` and `arr` must have the same number of dimensions")
+    ax = int(axis)
+    if not -nd <= ax < nd:
+        raise ValueError(f"axis {ax} is out of bounds for array of dimension {nd}")
+    ax %= nd
+    if nd > L.GATHER_MAX_DIM:
+        raise UnimplementedMathError(f"Gather over {nd} dimensions (at most {L.GATHER_MAX_DIM})")
+    shape = []
+    for d in range(nd):
+        if d == ax:
+            shape.append(idx.shape[d])
+        else:
+            shape.append(tuple(torch.broadcast_shapes((x.shape[d],), (idx.shape[d],)))[0])
+    xs = [x.stride(d) if (d == ax or x.shape[d] == shape[d]) else 0 for d in range(nd)]
+    is_ = [idx.stride(d) if idx.shape[d] == shape[d] else 0 for d in range(nd)]
+    y = torch.empty(tuple(shape), dtype=x.dtype, device=device())
+    import ctypes as C
+
+    A = C.c_int64 * nd
+    L.call("b200_gather_axis", x.element_size(), x.data_ptr(), A(*xs), idx.data_ptr(), A(*is_), y.data_ptr(), A(*shape), nd,
+           ax, int(x.shape[ax]), stream_ptr())
     return y
+
+
+def op_take_along_axis(x, indices, axis=-1, **_):  # numpy/eager/advanced_indexing.py:163-177
+    y = gather_along_axis(x, indices, axis)
+    # bf16 graph values stand for the reference's fp32 values: the gathered result is fp32
+    return cast(y, torch.float32) if y.dtype == torch.bfloat16 else y
+
+
+def op_gather(*args, **kwargs):  # numpy/eager/indexing.py:312-332
+    """Gather(tensor, dim, index) = np.take_along_axis(tensor, index, axis=dim), arguments
+    positional in that order or as the keywords tensor / dim / index."""
+    t = args[0] if len(args) > 0 else kwargs.get("tensor")
+    dim = args[1] if len(args) > 1 else kwargs.get("dim")
+    index = args[2] if len(args) > 2 else kwargs.get("index")
+    if isinstance(dim, torch.Tensor):
+        dim = int(dim.item())
+    elif dim is not None:
+        dim = int(dim)
+    return op_take_along_axis(t, index, axis=dim)
+
+
+_ONEHOT_DTYPES = {"float32": torch.float32, "float64": torch.float64, "float": torch.float64, "double": torch.float64,
+                  "int64": torch.int64, "int": torch.int64, "int32": torch.int32, "bool": torch.bool}
+
+
+def _one_hot_dtype(dtype: Any) -> torch.dtype:
+    if dtype is None or dtype is float:
+        return torch.float64
+    if dtype is int:
+        return torch.int64
+    if dtype is bool:
+        return torch.bool
+    name = getattr(dtype, "__name__", None) if isinstance(dtype, type) else None
+    key = str(name or dtype).replace("np.", "").replace("numpy.", "").replace("torch.", "").replace("<class '", "").rstrip("'>")
+    if key not in _ONEHOT_DTYPES:
+        raise UnimplementedMathError(f"OneHot to dtype {dtype!r} has no b200 kernel")
+    return _ONEHOT_DTYPES[key]
+
+
+def op_one_hot(*args, **kwargs):  # numpy/eager/math_advanced/math_general.py:710-736
+    """OneHot(indices, depth, on_value=1, off_value=0, axis=-1, dtype=float):
+    eye(depth)[indices] * (on - off) + off, the class axis moved to ``axis``. A float64
+    result (the default dtype) is computed in fp64 and stored as fp32, the backend's
+    floating-point type (host float64 arrays are uploaded as fp32 too)."""
+    indices = args[0] if args else None
+    depth = args[1] if len(args) > 1 else kwargs.get("depth")
+    if indices is None or depth is None:
+        return None
+    on_value = float(kwargs.get("on_value", 1))
+    off_value = float(kwargs.get("off_value", 0))
+    axis = kwargs.get("axis", -1)
+    want = _one_hot_dtype(kwargs.get("dtype", float))
+    depth = int(depth.item()) if isinstance(depth, torch.Tensor) else int(depth)
+    if depth < 0:
+        raise ValueError("negative dimensions are not allowed")
+    idx = contiguous(_int_indices(indices))
+    nd = idx.dim() + 1
+    pos = int(axis)
+    if not -nd <= pos < nd:
+        raise ValueError(f"destination {pos} is out of bounds for array of dimension {nd}")
+    pos %= nd
+    outer = 1
+    for d in idx.shape[:pos]:
+        outer *= int(d)
+    inner = 1
+    for d in idx.shape[pos:]:
+        inner *= int(d)
+    shape = tuple(idx.shape[:pos]) + (depth,) + tuple(idx.shape[pos:])
+    kdt = torch.float64 if want == torch.float64 else want
+    y = torch.empty(shape, dtype=kdt, device=device())
+    L.call("b200_one_hot", idx.data_ptr(), y.data_ptr(), code(y), outer, depth, inner, on_value, off_value, stream_ptr())
+    return cast(y, torch.float32) if kdt == torch.float64 else y
 
 
 def op_scatter_add(inp, index, src, dim=0, **_):  # numpy/eager/advanced_indexing.py:309-326
@@ -1126,6 +1229,8 @@ OPS: dict[str, Any] = {
     "LayerNormGammaGrad": op_layer_norm_gamma_grad,
     "LayerNormBetaGrad": op_layer_norm_beta_grad,
     "TakeAlongAxis": op_take_along_axis,
+    "Gather": op_gather,
+    "OneHot": op_one_hot,
     "ScatterAdd": op_scatter_add,
     "Take": op_take,
     "TensorScatterAdd": op_tensor_scatter_add,
@@ -1137,7 +1242,12 @@ OPS: dict[str, Any] = {
     "Conv2DBiasGrad": op_conv2d_bias_grad,
     "AllReduce": op_all_reduce,
     "NcclAllReduce": op_all_reduce,
+    "Clone": lambda x, *_, **__: copy(x) if isinstance(x, torch.Tensor) else x,  # numpy/eager/__init__.py:128-145
 }
+
+from . import fused_nodes as _fused_nodes  # noqa: E402  (fusion-pass node types, registered into OPS)
+
+_fused_nodes.register(OPS)
 
 # reference aliases (interpreter/evaluator.py:771-791)
 ALIASES = {"Sub": "Subtract", "Mul": "Multiply", "Div": "TrueDivide", "Neg": "Negative", "Pow": "Power", "MatMul": "Matmul",

@@ -36,6 +36,7 @@ __device__ __forceinline__ float load_as_f32(const void* p, int64_t i, int dtype
     case B200_I64: return (float)reinterpret_cast<const long long*>(p)[i];
     case B200_BOOL: return reinterpret_cast<const uint8_t*>(p)[i] ? 1.0f : 0.0f;
     case B200_I32: return (float)reinterpret_cast<const int*>(p)[i];
+    case B200_F64: return (float)reinterpret_cast<const double*>(p)[i];
   }
   return 0.0f;
 }
@@ -47,6 +48,7 @@ __device__ __forceinline__ void store_from_f32(void* p, int64_t i, int dtype, fl
     case B200_I64: reinterpret_cast<long long*>(p)[i] = (long long)v; break;
     case B200_BOOL: reinterpret_cast<uint8_t*>(p)[i] = (v != 0.0f) ? 1 : 0; break;
     case B200_I32: reinterpret_cast<int*>(p)[i] = (int)v; break;
+    case B200_F64: reinterpret_cast<double*>(p)[i] = (double)v; break;
   }
 }
 

@@ -18,6 +18,16 @@
 // area is cleared once at set-up and never again. A wait gives up after `spin_limit` polls
 // per thread: the block records B200_ERR_TIMEOUT in `status`, leaves its values
 // unchanged and does not advance its call number.
+//
+// A timeout is fatal for the exchange. After one, the ranks disagree on call numbers (a
+// peer that received this rank's words did advance), so a later call could find a peer's
+// words of the previous call under the number it expects and add stale values. Every
+// block therefore reads `status` first and returns without sending, summing or advancing
+// when it is non-zero: a rank that timed out stops exchanging, and its peers' next waits
+// time out in turn, so every rank ends with the status set and no rank sums stale words.
+// Only a collective reset (receive areas cleared, call numbers and status zeroed on every
+// rank) re-opens the exchange. With the optimizer epilogue, parameters may differ across
+// ranks after a timeout: the blocks that completed on one rank updated them.
 #include <algorithm>
 
 #include "common.cuh"
@@ -72,12 +82,12 @@ __global__ void __launch_bounds__(PT) peer_allreduce_kernel(float* __restrict__ 
                                                             int64_t cap, int rank, int world, uint32_t* __restrict__ epoch,
                                                             int* __restrict__ status, int64_t spin_limit, float scale,
                                                             const __grid_constant__ Segs S) {
-  __shared__ int s_err;
   const int b = blockIdx.x, tid = threadIdx.x;
+  // fail-stop: a rank whose exchange timed out before sends, sums and advances nothing
+  if (*reinterpret_cast<volatile const int*>(status) != 0) return;
   const int64_t lo = (int64_t)b * PT * EPT;
   const uint32_t e = epoch[b] + 1u;
   const int64_t half = (int64_t)(e & 1u) * world;
-  if (tid == 0) s_err = 0;
   float mine[EPT];
   // push this rank's values into every peer's receive area
 #pragma unroll
@@ -131,12 +141,9 @@ __global__ void __launch_bounds__(PT) peer_allreduce_kernel(float* __restrict__ 
     }
     sum[k] = acc;
   }
-  if (err) {
-    s_err = 1;
-    atomicExch(status, B200_ERR_TIMEOUT);
-  }
-  __syncthreads();
-  if (s_err) return;
+  if (err) atomicExch(status, B200_ERR_TIMEOUT);
+  // every thread of the block learns whether any wait gave up (one barrier, no shared flag)
+  if (__syncthreads_or(err ? 1 : 0)) return;
 #pragma unroll
   for (int k = 0; k < EPT; ++k) {
     const int64_t i = lo + (int64_t)k * PT + tid;

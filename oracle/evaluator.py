@@ -105,12 +105,26 @@ def _kwargs(node: dict, target: str) -> dict:
 # ----------------------------------------------------------------------------------
 
 
+# When set (``evaluate(..., blas_layout=True)``), fp32 contractions run on dense operands
+# through a batched CPU BLAS (torch.matmul on host tensors). numpy hands strided batch
+# views (attention's head split and its transposes) to a plain C loop instead of BLAS,
+# which is two orders of magnitude slower at the benchmark sizes. The arithmetic is the
+# same fp32 matmul with fp32 accumulation; only the summation order inside BLAS differs,
+# so this mode is for the size-scaled parity tests, which compare with a tolerance, not
+# for the bit-exact pins against the reference's fixtures.
+_BLAS_LAYOUT = False
+
+
 def _op_matmul(a, b, transpose_a=False, transpose_b=False, **_):
     # backends/eager/core_math_ops/math_matrix.py:21-44
     if transpose_a:
         a = np.swapaxes(a, -1, -2)
     if transpose_b:
         b = np.swapaxes(b, -1, -2)
+    if _BLAS_LAYOUT and a.dtype == np.float32 and b.dtype == np.float32 and a.ndim >= 2 and b.ndim >= 2:
+        import torch
+
+        return torch.matmul(torch.from_numpy(np.ascontiguousarray(a)), torch.from_numpy(np.ascontiguousarray(b))).numpy()
     return np.matmul(a, b)
 
 
@@ -379,6 +393,146 @@ def _op_apply_rmsprop(param, ms, mom, grad, lr=0.001, **_):
     return p_new, m_new, mo_new
 
 
+def _op_gather(*args, **kwargs):
+    # backends/numpy/eager/indexing.py:312-332: take_along_axis(tensor, index, axis=dim),
+    # arguments (tensor, dim, index) positionally or as keywords
+    t = args[0] if len(args) > 0 else kwargs.get("tensor")
+    dim = args[1] if len(args) > 1 else kwargs.get("dim")
+    index = args[2] if len(args) > 2 else kwargs.get("index")
+    dim = None if dim is None else int(np.asarray(dim).item())
+    return np.take_along_axis(np.asarray(t), np.asarray(index), axis=dim)
+
+
+def _op_one_hot(*args, **kwargs):
+    # backends/numpy/eager/math_advanced/math_general.py:710-736
+    indices = args[0] if args else None
+    depth = args[1] if len(args) > 1 else kwargs.get("depth")
+    if indices is None or depth is None:
+        return None
+    on_value = float(kwargs.get("on_value", 1))
+    off_value = float(kwargs.get("off_value", 0))
+    axis = kwargs.get("axis", -1)
+    dtype = kwargs.get("dtype", float)
+    out = np.eye(int(np.asarray(depth).item()), dtype=dtype)[indices]
+    if axis != -1:
+        out = np.moveaxis(out, -1, axis)
+    out = out * (on_value - off_value) + off_value
+    return out.astype(dtype)
+
+
+# --- node types of the reference's fusion passes (no reference kernel exists; their
+# meaning is the computation the pass folded into them) -----------------------------
+_C_FUNCS = {"fmaxf": np.fmax, "fminf": np.fmin, "expf": np.exp, "logf": np.log, "sqrtf": np.sqrt, "tanhf": np.tanh,
+            "fabsf": np.abs}
+
+
+def _scalar_expr(expr: str, inputs):
+    """Evaluate a FusedElementwise ``scalar_expr`` (transforms/passes/operator_fusion.py:
+    619-715: a C float expression over in0..inN) in float32, left to right like C."""
+    import ast
+    import re
+
+    text = re.sub(r"(\d+\.\d*|\.\d+|\d+)([eE][+-]?\d+)?[fF]\b", lambda m: m.group(1) + (m.group(2) or ""), expr)
+    tree = ast.parse(text, mode="eval").body
+    f32 = np.float32
+
+    def ev(n):
+        if isinstance(n, ast.BinOp):
+            a, b = ev(n.left), ev(n.right)
+            op = {ast.Add: np.add, ast.Sub: np.subtract, ast.Mult: np.multiply, ast.Div: np.true_divide}[type(n.op)]
+            return op(a, b, dtype=f32)
+        if isinstance(n, ast.UnaryOp):
+            v = ev(n.operand)
+            return np.negative(v, dtype=f32) if isinstance(n.op, ast.USub) else v
+        if isinstance(n, ast.Constant):
+            return f32(n.value)
+        if isinstance(n, ast.Name):
+            k = int(re.fullmatch(r"in_?(\d+)", n.id).group(1))
+            return np.asarray(inputs[k]).astype(f32)
+        if isinstance(n, ast.Call):
+            return _C_FUNCS[n.func.id](*[ev(a) for a in n.args], dtype=f32)
+        raise ValueError(f"scalar_expr: unsupported {ast.dump(n)}")
+
+    return np.asarray(ev(tree), dtype=f32)
+
+
+def _op_fused_elementwise(*inputs, scalar_expr="0.0f", **_):
+    # transforms/passes/operator_fusion.py:673-715
+    shape = np.broadcast_shapes(*[np.shape(x) for x in inputs]) if inputs else ()
+    return np.broadcast_to(_scalar_expr(str(scalar_expr), inputs), shape).copy()
+
+
+def _silu(x, **_):
+    return x * (1.0 / (1.0 + np.exp(-x)))
+
+
+_FUSION_ELEMS = ("Add", "Sub", "Mul", "Div", "TrueDivide", "Relu", "Sigmoid", "Neg", "Abs", "Exp", "Log", "Sqrt", "Gelu", "Silu",
+                 "Tanh", "Pow", "Maximum", "Minimum")  # operator_fusion.py:596-615
+_FUSION_ACTS = ("Relu", "Gelu", "Silu", "Sigmoid", "Tanh")  # operator_fusion.py:918
+
+
+def _named(op):
+    op = _ALIASES.get(op, op)
+    if op == "Silu":
+        return _silu
+    return OPS[op]
+
+
+def _elem_act(elem, act):
+    # operator_fusion.py:906-945 (attributes fused_ops = [elem, act]); the YAML rule
+    # ElementwiseFusion (fusion_patterns/ElementwiseFusion.yaml) builds AddRelu the same way
+    def run(*inputs, fused_ops=None, **_):
+        e, a = (list(fused_ops) if fused_ops else [elem, act])
+        return _named(a)(_named(e)(*inputs))
+
+    return run
+
+
+def _conv_bias_act(act):
+    # operator_fusion.py:851-890: act(Conv2D(x, w) + bias) with the conv's attributes;
+    # the declarative rule (attribute fused_pattern) is the activation root alone
+    def run(*inputs, activation=None, has_bias=True, fused_pattern=None, **kw):
+        if fused_pattern is not None:
+            return _named(act)(*inputs)
+        x, w, b = inputs
+        ck = {k: v for k, v in kw.items() if k in ("stride", "padding", "groups", "dilation")}
+        return _named(activation or act)(np.add(_op_conv2d(x, w, **ck), b))
+
+    return run
+
+
+def _horizontal(*inputs, fused_ops=(), **_):
+    # operator_fusion.py:992-1071: the siblings' ops on the shared inputs (their
+    # attributes are not kept by the pass)
+    return tuple(_named(op)(*inputs) for op in fused_ops)
+
+
+_DECLARATIVE_ROOT = {  # transforms/fusion_patterns.yaml: rule name -> targets[-1]
+    "ScaledDotProductAttention": "Matmul", "ConvBNActivation": "Relu", "LayerNorm": "Add", "MatMulBiasGelu": "Gelu",
+    "Conv2DBatchNormFusion": "BatchNorm", "Conv2DBiasActivationFusion": "Relu", "DotGeluFusion": "Gelu",
+    "DotReluFusion": "Relu", "FMAFusion": "Add", "MultiHeadAttentionFusion": "Matmul"}
+
+
+def _declarative(default_root):
+    # operator_fusion.py:464-482: the root node cloned under the fused name
+    def run(*inputs, fused_pattern=None, **kw):
+        root = _DECLARATIVE_ROOT.get(str(fused_pattern), default_root) if fused_pattern is not None else default_root
+        return _named(root)(*inputs, **kw)
+
+    return run
+
+
+def _fused_layer_norm(x, eps, scale=None, shift=None, **_):
+    # fusion_patterns/LayerNormFusion.yaml: (x - mean) / sqrt(var + eps) [* scale + shift]
+    e = float(np.asarray(eps).item())
+    mean = np.mean(x, axis=-1, keepdims=True)
+    var = np.mean((x - mean) * (x - mean), axis=-1, keepdims=True)
+    y = (x - mean) / np.sqrt(var + e)
+    if scale is not None:
+        y = y * scale + shift
+    return y
+
+
 OPS: dict[str, Any] = {
     "ApplyAdam": _op_apply_adam,
     "ApplyAdagrad": _op_apply_adagrad,
@@ -420,11 +574,42 @@ OPS: dict[str, Any] = {
     "TensorScatterAdd": _op_tensor_scatter_add,
     "Take": _op_take,
     "ZerosLike": lambda a, **_: np.zeros_like(a),  # np fallback
+    "Gather": _op_gather,
+    "OneHot": _op_one_hot,
+    "Clone": lambda a, *_, **__: np.copy(a),  # backends/numpy/eager/__init__.py:128-145
+    "Maximum": lambda a, b, **_: np.maximum(a, b),
+    "Minimum": lambda a, b, **_: np.minimum(a, b),
+    "Abs": lambda a, **_: np.abs(a),
+    "Sigmoid": lambda a, **_: 1.0 / (1.0 + np.exp(-a)),
     "Conv2D": _op_conv2d,
     "Conv2DInputGrad": _op_conv2d_input_grad,
     "Conv2DWeightGrad": _op_conv2d_weight_grad,
     "Conv2DBiasGrad": _op_conv2d_bias_grad,
 }
+
+
+OPS["FusedElementwise"] = _op_fused_elementwise
+for _e in _FUSION_ELEMS:
+    for _a in _FUSION_ACTS:
+        OPS.setdefault(f"{_e}{_a}", _elem_act(_e, _a))
+for _c in ("Conv2D", "Conv"):
+    for _a in _FUSION_ACTS:
+        OPS[f"Fused{_c}Bias{_a}"] = _conv_bias_act(_a)
+OPS["HorizontalFusedOps"] = _horizontal
+OPS["TupleGetItem"] = lambda t, index=0, **_: t[int(index)]
+for _n, _r in (("FusedAttention", "Matmul"), ("FusedConv2D", "Relu"), ("FusedLinearGELU", "Gelu"), ("FusedLinearGelu", "Gelu"),
+               ("FusedLinearRelu", "Relu"), ("ScaledDotProductAttention", "Matmul")):
+    OPS[_n] = _declarative(_r)
+OPS["FusedLayerNorm"] = lambda *a, fused_pattern=None, **k: (_declarative("Add")(*a, fused_pattern=fused_pattern, **k)
+                                                             if fused_pattern else _fused_layer_norm(*a, **k))
+OPS["FusedMultiplyAdd"] = lambda *a, fused_pattern=None, **k: (_declarative("Add")(*a, fused_pattern=fused_pattern, **k)
+                                                               if fused_pattern else np.add(np.multiply(a[0], a[1]), a[2]))
+OPS["FusedLayerNormAffine"] = lambda x, scale, shift, eps, **_: _fused_layer_norm(x, eps, scale, shift)
+OPS["FusedLogExp"] = lambda x, **_: np.exp(np.log(x))
+OPS["DotGelu"] = lambda a, b, **_: _op_gelu(np.dot(a, b))
+OPS["DotRelu"] = lambda a, b, **_: _op_relu(np.dot(a, b))
+OPS["Linear"] = lambda x, w, b, **_: np.add(np.matmul(x, w), b)
+OPS["Dot"] = lambda a, b, **_: np.dot(a, b)  # backends/eager/core_math_ops/math_matrix.py:66-82
 
 
 CONTRACTIONS = ("Matmul", "BatchMatMul", "Conv2D", "Conv2DInputGrad", "Conv2DWeightGrad")
@@ -454,8 +639,19 @@ def execute_op(op: str, *args, contraction_rounding: str | None = None, **kwargs
     return fn(*args, **kwargs)
 
 
-def evaluate(graph: dict, inputs: dict[str, np.ndarray], contraction_rounding: str | None = None) -> dict[str, Any]:
-    """``evaluate_graph`` (evaluator.py:272-305): every node, in dependency order."""
+def evaluate(graph: dict, inputs: dict[str, np.ndarray], contraction_rounding: str | None = None,
+             blas_layout: bool = False) -> dict[str, Any]:
+    """``evaluate_graph`` (evaluator.py:272-305): every node, in dependency order.
+    ``blas_layout=True`` passes dense operands to np.matmul (see ``_BLAS_LAYOUT``)."""
+    global _BLAS_LAYOUT
+    prev, _BLAS_LAYOUT = _BLAS_LAYOUT, bool(blas_layout)
+    try:
+        return _evaluate(graph, inputs, contraction_rounding)
+    finally:
+        _BLAS_LAYOUT = prev
+
+
+def _evaluate(graph: dict, inputs: dict[str, np.ndarray], contraction_rounding: str | None) -> dict[str, Any]:
     env: dict[str, Any] = dict(inputs)
     for node in topo_order(graph):
         op, nid = node["op_type"], node["id"]
@@ -470,9 +666,15 @@ def evaluate(graph: dict, inputs: dict[str, np.ndarray], contraction_rounding: s
             env[nid] = vals[0] if vals else None
         elif op == "Constant":
             env[nid] = np.array(node["attributes"]["value"], dtype=node.get("const_dtype"))
+        elif op == "Recompute":
+            # _evaluate_recompute_node (evaluator.py:720-735)
+            attrs = node.get("attributes") or {}
+            orig = _ALIASES.get(str(attrs.get("original_op", op)), str(attrs.get("original_op", op)))
+            res_node = {"id": nid, "op_type": orig, "inputs": node["inputs"], "attributes": dict(attrs.get("original_attrs") or {})}
+            env[nid] = _dispatch(res_node, orig, vals, contraction_rounding)
         else:
             target = _ALIASES.get(op, op)
-            env[nid] = execute_op(target, *vals, contraction_rounding=contraction_rounding, **_kwargs(node, target))
+            env[nid] = _dispatch(node, target, vals, contraction_rounding)
     out = {}
     for oid in graph["outputs"]:
         if oid not in env:
@@ -481,8 +683,69 @@ def evaluate(graph: dict, inputs: dict[str, np.ndarray], contraction_rounding: s
     return out
 
 
-def evaluate_roles(graph: dict, role_inputs: dict[str, np.ndarray], contraction_rounding: str | None = None) -> dict[str, Any]:
+def _parse_key(text):
+    """_parse_slice_string (evaluator.py:308-425): the index key an attribute string denotes."""
+    import ast
+    import builtins
+
+    def node(n):
+        if isinstance(n, ast.Tuple):
+            return tuple(node(e) for e in n.elts)
+        if isinstance(n, ast.List):
+            return [node(e) for e in n.elts]
+        if isinstance(n, ast.Constant):
+            return n.value.decode("utf-8", errors="replace") if isinstance(n.value, bytes) else n.value
+        if isinstance(n, ast.Name):
+            return {"None": None, "Ellipsis": Ellipsis, "False": False, "True": True}.get(n.id)
+        if isinstance(n, ast.UnaryOp):
+            if isinstance(n.op, ast.USub) and isinstance(n.operand, ast.Constant) and isinstance(n.operand.value, (int, float)):
+                return -n.operand.value
+            return None
+        if isinstance(n, ast.Call) and isinstance(n.func, ast.Name):
+            if n.func.id == "slice":
+                return builtins.slice(*[v if isinstance((v := node(a)), (int, float, str)) else None for a in n.args])
+            if n.func.id == "array":
+                return node(n.args[0])
+            return None
+        raise ValueError(f"Unsupported slice expression node: {type(n)}")
+
+    return node(ast.parse(str(text), mode="eval").body)
+
+
+def _dispatch(node, target, vals, contraction_rounding):
+    """_dispatch_op (evaluator.py:570-593): the interpreter's own indexing / checkpoint
+    handlers, else the op kernel."""
+    import builtins
+
+    kw = _kwargs(node, target)
+    if target == "Slice":  # _handle_slice, evaluator.py:428-463
+        arr = np.asarray(vals[0])
+        if "slices" in kw:
+            return arr[_parse_key(kw["slices"])]
+        dim = int(kw.get("dim", 0) or 0)
+        sl = [builtins.slice(None)] * arr.ndim
+        sl[dim] = builtins.slice(kw.get("start"), kw.get("end"), kw.get("step", 1))
+        return arr[tuple(sl)]
+    if target == "GetItem":  # _handle_getitem, :466-485
+        return np.asarray(vals[0])[_parse_key(kw.get("key"))]
+    if target in ("IndexPut", "SetItem"):  # _handle_index_put, :488-508
+        arr = np.copy(vals[0])
+        arr[_parse_key(kw.get("key", kw.get("index", 0)))] = vals[1]
+        return arr
+    if target == "Checkpoint":  # _handle_checkpoint, :511-545
+        subs = node.get("subgraphs") or {}
+        sg = subs.get("body") or subs.get("subgraph") or (node.get("attributes") or {}).get("subgraph")
+        if not isinstance(sg, dict) or "inputs" not in sg or "outputs" not in sg:
+            raise AttributeError("Checkpoint node is missing a valid subgraph")
+        res = _evaluate(sg, dict(zip(sg["inputs"], vals)), contraction_rounding)
+        outs = list(sg["outputs"]) if isinstance(sg["outputs"], list) else [sg["outputs"]]
+        return res[outs[0]] if len(outs) == 1 else tuple(res[o] for o in outs)
+    return execute_op(target, *vals, contraction_rounding=contraction_rounding, **kw)
+
+
+def evaluate_roles(graph: dict, role_inputs: dict[str, np.ndarray], contraction_rounding: str | None = None,
+                   blas_layout: bool = False) -> dict[str, Any]:
     """Evaluate with inputs keyed by workload role; outputs keyed by output name."""
     inputs = {nid: role_inputs[r] for r, nid in graph["roles"].items()}
-    res = evaluate(graph, inputs, contraction_rounding=contraction_rounding)
+    res = evaluate(graph, inputs, contraction_rounding=contraction_rounding, blas_layout=blas_layout)
     return {name: res[nid] for name, nid in graph["output_names"].items()}

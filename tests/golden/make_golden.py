@@ -1,7 +1,8 @@
 """Generate the workload graphs and golden vectors from the REFERENCE itself.
 
 Test infrastructure: this script is the only committed code that imports the
-reference (``ml_switcheroo_compiler``), read-only, from ``/root/reference/src``,
+reference (``ml_switcheroo_compiler``), read-only, from the source tree named by ``--reference-src`` or
+``$ML_SWITCHEROO_REFERENCE_SRC``,
 with the usage-derived ``ml_switcheroo_ir`` stand-in under ``oracle/standin``.
 It is run here (CPU container) and its outputs are committed:
 
@@ -20,7 +21,7 @@ registered through the reference's own public plugin API ``register_vjp``
 before the YAML rules, ``vjp_registry.py:126``). The reference source is not edited.
 Every corrected rule emits only ops that the reference numpy backend evaluates.
 
-Usage:  python tests/golden/make_golden.py [--graphs] [--goldens] [--only NAME]
+Usage:  python tests/golden/make_golden.py --reference-src PATH [--graphs] [--goldens] [--only NAME]
 """
 
 from __future__ import annotations
@@ -35,9 +36,10 @@ import numpy as np
 
 HERE = os.path.dirname(os.path.abspath(__file__))
 REPO = os.path.dirname(os.path.dirname(HERE))
-REF_SRC = "/root/reference/src"
-sys.path.insert(0, os.path.join(REPO, "oracle", "standin"))
-sys.path.insert(0, REF_SRC)
+sys.path.insert(0, HERE)
+from refpath import add_reference_to_path  # noqa: E402
+
+REF_SRC = add_reference_to_path()
 sys.path.insert(0, os.path.join(REPO, "ml-switcheroo-compiler_b200"))
 
 from b200.workloads import GOLDEN_CASES, GRAPH_CASES, WORKLOADS, make_inputs  # noqa: E402

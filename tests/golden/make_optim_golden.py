@@ -1,7 +1,7 @@
 """Generate golden vectors for the optimizer update ops from the REFERENCE itself.
 
-Test infrastructure: imports the reference (``ml_switcheroo_compiler``) read-only from
-``/root/reference/src`` with the usage-derived ``ml_switcheroo_ir`` stand-in under
+Test infrastructure: imports the reference (``ml_switcheroo_compiler``) read-only from the
+source tree named by ``--reference-src`` or ``$ML_SWITCHEROO_REFERENCE_SRC``, with the usage-derived ``ml_switcheroo_ir`` stand-in under
 ``oracle/standin``, runs the numpy backend's ``execute_op`` (``backends/numpy/generator.py:134``
 -> ``numpy/eager/__init__.py:90-125``, which resolves ``ApplyAdam`` / ``ApplyAdagrad`` /
 ``ApplyFtrl`` / ``ApplyRMSProp`` to ``numpy/eager/optimizers_ops.py``) on seeded fp32
@@ -13,7 +13,7 @@ inputs, and writes ``tests/golden/ops/optim.npz``:
 
 Cases cover the default learning rate and another one, zero accumulators (the first
 step), negative and zero gradients, and a ragged length. Usage:
-``python tests/golden/make_optim_golden.py``.
+``python tests/golden/make_optim_golden.py --reference-src PATH``.
 """
 
 from __future__ import annotations
@@ -25,8 +25,10 @@ import numpy as np
 
 HERE = os.path.dirname(os.path.abspath(__file__))
 REPO = os.path.dirname(os.path.dirname(HERE))
-sys.path.insert(0, os.path.join(REPO, "oracle", "standin"))
-sys.path.insert(0, "/root/reference/src")
+sys.path.insert(0, HERE)
+from refpath import add_reference_to_path  # noqa: E402
+
+add_reference_to_path()
 
 from ml_switcheroo_compiler.backends.registry import BackendRegistry  # noqa: E402
 

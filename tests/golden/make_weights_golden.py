@@ -1,8 +1,8 @@
 """Generate weight-file fixtures with the REFERENCE's own savers.
 
-Test infrastructure: imports the reference (``ml_switcheroo_compiler``) read-only from
-``/root/reference/src`` with the ``ml_switcheroo_ir`` stand-in under ``oracle/standin``,
-activates its numpy backend and writes, for one seeded weights dictionary (several dtypes,
+Test infrastructure: imports the reference (``ml_switcheroo_compiler``) read-only from the
+source tree named by ``--reference-src`` or ``$ML_SWITCHEROO_REFERENCE_SRC``, with the
+``ml_switcheroo_ir`` stand-in under ``oracle/standin``, activates its numpy backend and writes, for one seeded weights dictionary (several dtypes,
 0-d / 1-d / n-d shapes):
 
 * ``tests/golden/ops/weights.safetensors`` with ``SafetensorsWeightFormat().save``
@@ -10,7 +10,7 @@ activates its numpy backend and writes, for one seeded weights dictionary (sever
 * ``tests/golden/ops/weights.npz`` with ``NpzWeightFormat().save`` (``npz.py:95-115``);
 * ``tests/golden/ops/weights_arrays.npz``, the same arrays through numpy, for comparison.
 
-Usage: ``python tests/golden/make_weights_golden.py``.
+Usage: ``python tests/golden/make_weights_golden.py --reference-src PATH``.
 """
 
 from __future__ import annotations
@@ -22,8 +22,10 @@ import numpy as np
 
 HERE = os.path.dirname(os.path.abspath(__file__))
 REPO = os.path.dirname(os.path.dirname(HERE))
-sys.path.insert(0, os.path.join(REPO, "oracle", "standin"))
-sys.path.insert(0, "/root/reference/src")
+sys.path.insert(0, HERE)
+from refpath import add_reference_to_path  # noqa: E402
+
+add_reference_to_path()
 
 from ml_switcheroo_compiler.core.config import config  # noqa: E402
 from ml_switcheroo_compiler.serialization.formats.npz import NpzWeightFormat  # noqa: E402

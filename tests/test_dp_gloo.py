@@ -114,3 +114,93 @@ def test_two_rank_gloo_gradient_exchange():
         assert c == [1.5, 3.0]
         for k, v in grads.items():
             np.testing.assert_allclose(v, full[k], rtol=1e-5, atol=1e-6 * float(np.abs(full[k]).max()), err_msg=k)
+
+
+def _bare_step(params, nstates=2):
+    """An OptimizerStep over host tensors, built without its CUDA-only constructor: only
+    the shape checks are exercised, no kernel runs."""
+    from b200.dp import OptimizerStep
+
+    st = OptimizerStep.__new__(OptimizerStep)
+    st.op, st.kind, st.lr, st.nstates = "ApplyAdam", 0, 1e-3, nstates
+    st.params = list(params)
+    st.states = [tuple(torch.zeros_like(p) for _ in range(nstates)) for p in st.params]
+    return st
+
+
+def test_optimizer_step_rejects_mismatched_tensors():
+    """A parameter, state or gradient whose element count differs from its partner's is
+    rejected on the host before any exchange or kernel: the kernels index them all with the
+    gradient's offsets and would write past the end of the smaller one."""
+    from b200.dp import GradAllReduce
+
+    step = _bare_step([torch.zeros(8), torch.zeros(3, 5)])
+    step.check_matches(0, torch.zeros(8))
+    with pytest.raises(ValueError):
+        step.check_matches(1, torch.zeros(16))
+    with pytest.raises(ValueError):
+        GradAllReduce("sum")([torch.zeros(8), torch.zeros(16)], step)  # raises before any collective
+    bad_state = _bare_step([torch.zeros(8)])
+    bad_state.states[0] = (torch.zeros(8), torch.zeros(7))
+    with pytest.raises(ValueError):
+        bad_state.check_matches(0, torch.zeros(8))
+
+
+class _FakePeer:
+    """Stands in for PeerAllReduce: only its failure status is read by check()."""
+
+    def __init__(self, failed: bool) -> None:
+        self._failed = failed
+        self.device = torch.device("cpu")
+
+    def failed(self) -> bool:
+        return self._failed
+
+
+def _check_rank_main(rank: int, world: int, port: int, q) -> None:
+    import datetime
+    import sys
+
+    here = os.path.dirname(os.path.abspath(__file__))
+    root = os.path.dirname(here)
+    for p in (here, root, os.path.join(root, "ml-switcheroo-compiler_b200")):
+        if p not in sys.path:
+            sys.path.insert(0, p)
+    import torch.distributed as dist
+
+    from b200.dp import GradAllReduce
+
+    dist.init_process_group("gloo", init_method=f"tcp://127.0.0.1:{port}", rank=rank, world_size=world,
+                            timeout=datetime.timedelta(seconds=60))
+    try:
+        sync = GradAllReduce("sum")
+        sync.peer = _FakePeer(failed=(rank == 1))  # only rank 1's wait gave up
+        raised = False
+        try:
+            sync.check()
+        except TimeoutError:
+            raised = True
+        # after the failure every rank exchanges through the collective library
+        t = torch.tensor([float(rank + 1)])
+        sync([t])
+        q.put((rank, raised, sync.peer is None, sync._peer_failed, t.item()))
+    finally:
+        dist.destroy_process_group()
+
+
+def test_peer_timeout_is_agreed_and_fatal_on_every_rank():
+    """A timeout seen by one rank makes check() raise on every rank, and every rank drops
+    the peer path, so no rank keeps exchanging with diverged call numbers."""
+    world, port = 2, _free_port()
+    ctx = mp.get_context("spawn")
+    q = ctx.SimpleQueue()
+    procs = [ctx.Process(target=_check_rank_main, args=(r, world, port, q)) for r in range(world)]
+    for p in procs:
+        p.start()
+    results = [q.get() for _ in range(world)]
+    for p in procs:
+        p.join(timeout=120)
+        assert p.exitcode == 0
+    for rank, raised, dropped, failed, val in results:
+        assert raised and dropped and failed, rank
+        assert val == 3.0

@@ -16,8 +16,13 @@ import pytest
 
 from gpu_helpers import assert_close, run_case, to_np
 
-CASES = ["mlp_small", "mlp_ragged", "rowfused_small", "rowfused_ragged", "bmm_small", "cnn_small", "transformer_small"]
-RTOL = {"mlp": 1e-4, "rowfused": 1e-4, "bmm": 2e-2, "cnn": 2e-2, "transformer": 2e-2}
+CASES = ["mlp_small", "mlp_ragged", "rowfused_small", "rowfused_ragged", "bmm_small", "cnn_small", "transformer_small",
+         # node types outside the workloads: the reference's fusion-pass outputs (golden = the
+         # reference's evaluation of the graph before fusion) and the interpreter's indexing /
+         # Recompute / Checkpoint nodes plus Gather and OneHot (tests/golden/make_node_golden.py)
+         "nodes_fused_ew", "nodes_fused_act", "nodes_fused_conv", "nodes_fused_horizontal", "nodes_fused_full",
+         "nodes_indexing"]
+RTOL = {"mlp": 1e-4, "rowfused": 1e-4, "bmm": 2e-2, "cnn": 2e-2, "transformer": 2e-2, "nodes": 1e-4}
 BF16 = {"bmm", "cnn", "transformer"}
 
 

@@ -178,6 +178,37 @@ def test_peer_allreduce_wait_gives_up(cuda):
     assert int(epoch[0].item()) == 0
 
 
+def test_peer_allreduce_after_timeout_refuses_stale_words(cuda):
+    """A timeout is fatal: after one, the peer's words of the call that timed out are
+    planted under the call number this rank expects next (what a peer that did complete
+    that call leaves behind). The next call must not add them: it returns at once with the
+    values unchanged, the status still set and the call counter not advanced."""
+    n = 4096
+    x = torch.arange(n, dtype=torch.float32, device="cuda")
+    epoch = torch.zeros(64, dtype=torch.int32, device="cuda")
+    status = torch.zeros(1, dtype=torch.int32, device="cuda")
+    a0, a1 = _area(2, n), _area(2, n)
+    d = x.clone()
+    _run(d, [a0, a1], n, 0, 2, epoch, status, 2000, 1.0)  # rank 1 never sends: times out
+    assert int(status.item()) == 4 and torch.equal(d, x) and int(epoch[0].item()) == 0
+    stale = torch.full((n,), 7.0, device="cuda")
+    a0[(1 * 2 + 1) * n : (1 * 2 + 2) * n] = _words(stale, 1)  # peer's words of call 1, half 1
+    a1.zero_()
+    _run(d, [a0, a1], n, 0, 2, epoch, status, 1 << 20, 1.0)
+    assert torch.equal(d, x), "a call after a timeout added a stale peer word"
+    assert int(status.item()) == 4
+    assert int(epoch[0].item()) == 0
+    assert int(a1.abs().sum().item()) == 0, "a call after a timeout still sent words"
+    # a collective reset (areas, counters and status cleared) re-opens the exchange
+    status.zero_()
+    a0.zero_()
+    y = torch.randn(n, device="cuda")
+    a0[(1 * 2 + 1) * n : (1 * 2 + 2) * n] = _words(y, 1)
+    _run(d, [a0, a1], n, 0, 2, epoch, status, 1 << 20, 1.0)
+    assert int(status.item()) == 0
+    assert torch.equal(d, x + y)
+
+
 def _free_port() -> int:
     s = socket.socket()
     s.bind(("127.0.0.1", 0))

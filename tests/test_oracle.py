@@ -32,7 +32,8 @@ def test_oracle_matches_reference_golden(case):
         if ref.dtype.kind in "iub":
             np.testing.assert_array_equal(v, ref)
         else:
-            # bit-identical except conv (summation order of the per-tap einsum differs)
+            # bit-identical except conv (summation order of the per-tap einsum differs) and
+            # FusedElementwise (float32 C-expression arithmetic against the unfused numpy ops)
             tol = 1e-6 * max(1.0, float(np.abs(ref).max()))
             assert float(np.abs(v.astype(np.float64) - ref).max()) <= tol, k
 
