@@ -2,26 +2,31 @@
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--workload NAME] [--impl b200|reference]
 
-A step is one evaluation of the workload's fwd+bwd LogicalGraph (the graph the
-reference's tracer + AD produced, stored under tests/golden/graphs) on one batch of
-seeded synthetic inputs. Default workload: the fused bandwidth-bound row graph
-(x[8192,4096]: affine -> GELU -> LayerNorm -> softmax + argmax, fwd+bwd w.r.t. x, a, b).
+A step is one evaluation of a workload's fwd+bwd LogicalGraph (the graph the reference's
+tracer + AD produced, stored under tests/golden/graphs) on one batch of seeded synthetic
+inputs. The headline workload (default) is the pre-LN transformer encoder stack (4 x
+d 1024, 16 heads, FFN 4096, seq 512, vocab 32000, global batch 64): the configuration
+with a data-parallel split and a multi-GPU target. The other four workloads (fused
+bandwidth-bound row graph, MLP, batched contraction, small CNN) are timed in the same run
+and reported in the line's ``configs`` block.
 
-Multi-GPU (torchrun, one process per GPU, NCCL): weak scaling - every rank runs one full
-batch per step and the replicated-parameter gradients are summed with NCCL AllReduce.
-``value`` = batches processed by all ranks / max-over-ranks device time.
+Multi-GPU (torchrun, one process per GPU, NCCL): workloads with per-rank graphs split the
+global batch over the ranks (strong scaling: transformer, CNN, batched contraction); the
+others run one full batch per rank (weak scaling). Replicated-parameter gradients are
+all-reduced. ``value`` = global batches processed by all ranks / max-over-ranks device
+time.
 
 ``--impl reference`` times the reference algorithm on the host CPU: the numpy
-restatement of the reference's evaluate_graph + numpy kernels (pinned bit-exact to the
-reference's own evaluation by tests/test_oracle.py), on a bounded row sample spread over
-all host cores, scaled to a full step.
+restatement of the reference's evaluate_graph + numpy kernels (pinned to the reference's
+own evaluation by tests/test_oracle.py), on bounded samples of the same workload, scaled
+to a full step. Only the evaluation is timed.
 """
 
 from __future__ import annotations
 
 import argparse
+import gc
 import json
-import math
 import os
 import statistics
 import subprocess
@@ -37,32 +42,25 @@ for _p in (ROOT, PKG):
 
 import numpy as np  # noqa: E402
 
-# workload -> (graph case at per-rank batch, metric config, dtype, dominant kernel, params)
+# workload -> graph at the global batch, per-rank graphs for a batch split, dtype, the
+# replicated parameters whose gradients are exchanged, and the CPU sample
 WORKLOADS = {
-    "rowfused": {
-        "graph": "rowfused_full",
-        "dtype": "f32",
-        "params": ["a", "b"],
-        "reduce": "sum",
-        "desc": "fused bandwidth-bound graph x[8192,4096]: gelu_tanh(x*a+b) -> LayerNorm -> softmax + argmax, fwd+bwd wrt x,a,b",
-    },
-    "bmm": {
-        "graph": "bmm_full",
-        "dtype": "bf16",
-        "params": ["bias"],
-        "bf16_inputs": ["A", "B"],
-        "reduce": "sum",
-        "desc": "batched contraction A,B[16,2048,2048] bf16: relu(A@B+bias) fwd+bwd (dA, dB, dbias)",
-    },
-    "mlp": {"graph": "mlp_full", "dtype": "f32", "params": ["W1", "b1", "W2", "b2"], "reduce": "mean",
-            "desc": "2-layer MLP x[64,784] 784->256->10 softmax CE fwd+bwd"},
-    "cnn": {"graph": "cnn_full", "dtype": "bf16", "params": ["w1", "w2", "w3", "Wl", "bl"], "reduce": "mean",
-            "dp_graphs": {2: "cnn_n256", 4: "cnn_n128", 8: "cnn_n64"},
-            "desc": "small CNN [512,3,32,32] 3 conv3x3 + GAP + linear, softmax CE fwd+bwd"},
     "transformer": {"graph": "transformer_full", "dtype": "bf16", "params": "all", "reduce": "mean",
                     "dp_graphs": {2: "transformer_b32", 4: "transformer_b16", 8: "transformer_b8"},
+                    "cpu_sample": ("transformer_b1", 64),
                     "desc": "pre-LN transformer encoder 4x(d1024,h16,ffn4096) seq 512, global batch 64, next-token CE fwd+bwd"},
+    "rowfused": {"graph": "rowfused_full", "dtype": "f32", "params": ["a", "b"], "reduce": "sum",
+                 "desc": "fused bandwidth-bound graph x[8192,4096]: gelu_tanh(x*a+b) -> LayerNorm -> softmax + argmax, fwd+bwd wrt x,a,b"},
+    "mlp": {"graph": "mlp_full", "dtype": "f32", "params": ["W1", "b1", "W2", "b2"], "reduce": "mean",
+            "desc": "2-layer MLP x[64,784] 784->256->10 softmax CE fwd+bwd"},
+    "bmm": {"graph": "bmm_full", "dtype": "bf16", "params": ["bias"], "bf16_inputs": ["A", "B"], "reduce": "sum",
+            "dp_graphs": {2: "bmm_z8", 4: "bmm_z4", 8: "bmm_z2"},
+            "desc": "batched contraction A,B[16,2048,2048] bf16: relu(A@B+bias) fwd+bwd (dA, dB, dbias)"},
+    "cnn": {"graph": "cnn_full", "dtype": "bf16", "params": ["w1", "w2", "w3", "Wl", "bl"], "reduce": "mean",
+            "dp_graphs": {2: "cnn_n256", 4: "cnn_n128", 8: "cnn_n64"},
+            "desc": "small CNN [512,3,32,32] 3 conv3x3 (VALID) + GAP + linear, softmax CE fwd+bwd"},
 }
+CONFIG_ORDER = ["transformer", "rowfused", "mlp", "bmm", "cnn"]
 
 
 def env_int(name: str, default: int) -> int:
@@ -77,7 +75,7 @@ def peaks() -> dict:
     if os.path.exists(p):
         d = json.load(open(p))
         return {"hbm_gbs": d["hbm_gbs"], "bf16_tflops": d["bf16_tflops"],
-                "bf16_tflops_sustained": d.get("bf16_tflops_sustained"), "source": "measured"}
+                "bf16_tflops_sustained": d.get("bf16_tflops_sustained") or d["bf16_tflops"], "source": "measured"}
     return {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0, "source": "fallback"}
 
 
@@ -136,17 +134,25 @@ class ClockSampler:
 
 
 # ----------------------------------------------------------------------------------
-# CPU reference arm (the oracle port of the reference's numpy evaluation)
+# CPU reference (the oracle port of the reference's numpy evaluation)
 # ----------------------------------------------------------------------------------
-def _cpu_eval_rows(args):
-    case, lo, hi = args
-    from b200.workloads import make_inputs  # noqa: F401  (inputs are re-drawn per worker)
+_ROW_STATE: dict = {}
+
+
+def _row_worker_init(case: str, lo: int, hi: int) -> None:
+    """Pool initializer: import, load the graph and draw this worker's rows (untimed)."""
     from oracle import evaluator as O
 
-    g = O.load_graph(case)
-    arr = _row_slice_inputs(g, lo, hi)
+    _ROW_STATE["g"] = O.load_graph(case)
+    _ROW_STATE["arrays"] = _row_slice_inputs(_ROW_STATE["g"], lo, hi)
+
+
+def _row_worker_eval(_) -> float:
+    """One evaluation of this worker's rows; returns its duration."""
+    from oracle import evaluator as O
+
     t0 = time.perf_counter()
-    O.evaluate_roles(g, arr)
+    O.evaluate_roles(_ROW_STATE["g"], _ROW_STATE["arrays"])
     return time.perf_counter() - t0
 
 
@@ -160,42 +166,98 @@ def _row_slice_inputs(g, lo, hi):
             "cotangent": rng.standard_normal((n, C), dtype=f32)}
 
 
-def cpu_reference(workload: str, budget_s: float = 20.0) -> dict:
-    """Time the CPU reference on a bounded sample; returns steps/s for a full step."""
-    import multiprocessing as mp
+class CpuReference:
+    """Timed CPU evaluations of a workload by the oracle. Everything but the evaluation
+    (process start, imports, graph loading, input generation, one warm-up evaluation)
+    happens in ``prepare``; ``sample()`` times one evaluation and returns the full-step
+    time it stands for."""
 
-    spec = WORKLOADS[workload]
-    cores = os.cpu_count() or 1
-    if workload != "rowfused":
-        # whole-graph sample on one core (BLAS may use more): the full batch / a slice of it
-        from b200 import graph as G
-        from b200.workloads import make_inputs
+    def __init__(self, workload: str) -> None:
+        self.workload = workload
+        self.spec = WORKLOADS[workload]
+        self.cores = os.cpu_count() or 1
+        self.pool = None
+
+    def prepare(self, budget_s: float = 20.0) -> None:
         from oracle import evaluator as O
 
-        g = O.load_graph(spec["graph"])
-        gg = G.load(spec["graph"])
-        arr = make_inputs(gg.meta["workload"], gg.meta["dims"], seed=0)
+        if self.workload == "rowfused":
+            import multiprocessing as mp
+
+            R = 8192
+            self.R = R
+            # one worker per core, each evaluating its own contiguous rows (rows are independent)
+            g = O.load_graph("rowfused_full")
+            probe_in = _row_slice_inputs(g, 0, 16)
+            O.evaluate_roles(g, probe_in)
+            t0 = time.perf_counter()
+            O.evaluate_roles(g, probe_in)
+            per_row = max((time.perf_counter() - t0) / 16, 1e-5)
+            rows_total = int(min(R, max(self.cores * 8, budget_s * self.cores / per_row / 2)))
+            self.rows = rows_total
+            chunk = max(8, -(-rows_total // self.cores))
+            self.shards = [(lo, min(rows_total, lo + chunk)) for lo in range(0, rows_total, chunk)]
+            ctx = mp.get_context("spawn")
+            self.pool = [ctx.Pool(1, initializer=_row_worker_init, initargs=("rowfused_full", lo, hi)) for lo, hi in self.shards]
+            self._map()  # warm-up evaluation in every worker (untimed)
+            self.desc = f"{rows_total} of {R} rows in {len(self.shards)} processes (one evaluation each), scaled to {R} rows"
+            self.used_cores = len(self.shards)
+            return
+        case, scale = self.spec.get("cpu_sample", (self.spec["graph"], 1))
+        self.scale = scale
+        self.g = O.load_graph(case)
+        from b200.workloads import make_inputs
+
+        self.arrays = make_inputs(self.g["workload"], self.g["dims"], seed=0)
+        self._eval()  # warm-up evaluation (untimed)
+        # fp32 numpy on the operands' own layouts, as the reference evaluates these graphs
+        # (its numpy Cast to bfloat16 is fp32, numpy/eager/variable_ops.py:42-43)
+        self.desc = (f"one fwd+bwd evaluation of {case}" + (f" (1/{scale} of the global batch), scaled x{scale}" if scale > 1 else "")
+                     + f"; fp32 numpy as the reference runs it, BLAS threads = {self.cores}")
+        self.used_cores = self.cores
+
+    def _eval(self) -> None:
+        from oracle import evaluator as O
+
+        O.evaluate_roles(self.g, self.arrays)
+
+    def _map(self) -> float:
+        rs = [p.apply_async(_row_worker_eval, (0,)) for p in self.pool]
+        return max(r.get() for r in rs)
+
+    def sample(self) -> float:
+        """Seconds of one full step, from one timed evaluation of the sample."""
+        if self.workload == "rowfused":
+            t0 = time.perf_counter()
+            self._map()
+            return (time.perf_counter() - t0) * self.R / self.rows
         t0 = time.perf_counter()
-        O.evaluate_roles(g, arr)
-        dt = time.perf_counter() - t0
-        return {"value": 1.0 / dt, "unit": "steps/s", "cores": cores, "kind": "port",
-                "sample": f"one full step of {spec['graph']} (numpy, BLAS threads={cores})"}
-    # rowfused: rows are independent -> shard a row sample over all cores
-    R = 8192
-    probe = _cpu_eval_rows(("rowfused_full", 0, 16))  # warm-up + per-row cost estimate
-    per_row = max(probe / 16, 1e-5)
-    rows_total = int(min(R, max(cores * 8, budget_s * cores / per_row / 2)))
-    chunk = max(8, rows_total // cores)
-    tasks = [("rowfused_full", lo, min(rows_total, lo + chunk)) for lo in range(0, rows_total, chunk)]
-    ctx = mp.get_context("spawn")
-    t0 = time.perf_counter()
-    with ctx.Pool(min(cores, len(tasks))) as pool:
-        pool.map(_cpu_eval_rows, tasks)
-    wall = time.perf_counter() - t0
-    rows_done = sum(hi - lo for _, lo, hi in tasks)
-    step_s = wall * R / rows_done
-    return {"value": 1.0 / step_s, "unit": "steps/s", "cores": min(cores, len(tasks)), "kind": "port",
-            "sample": f"{rows_done} of {R} rows (row-sharded over {min(cores, len(tasks))} processes), wall {wall:.2f}s, scaled to 8192 rows"}
+        self._eval()
+        return (time.perf_counter() - t0) * self.scale
+
+    def close(self) -> None:
+        for p in self.pool or []:
+            p.terminate()
+
+    def baseline(self, value: float, samples: int) -> dict:
+        return {"value": value, "unit": "steps/s", "cores": self.used_cores, "kind": "port",
+                "sample": f"{self.desc}; {samples} timed sample(s)"}
+
+
+def cpu_baseline(workload: str, max_samples: int = 3, budget_s: float = 45.0) -> dict:
+    """The oracle on the host cores, beside the GPU number: at most ``max_samples`` timed
+    evaluations, stopped once ``budget_s`` seconds of them have run."""
+    ref = CpuReference(workload)
+    try:
+        ref.prepare()
+        times, t_start = [], time.perf_counter()
+        while len(times) < max_samples:
+            times.append(ref.sample())
+            if time.perf_counter() - t_start > budget_s:
+                break
+        return ref.baseline(1.0 / statistics.median(times), len(times))
+    finally:
+        ref.close()
 
 
 # ----------------------------------------------------------------------------------
@@ -206,161 +268,214 @@ def algorithmic_bytes_rowfused(R: int, C: int) -> int:
     return 4 * R * C * 4 + R * 8 + 2 * C * 4 + 4 * C * 4
 
 
-def run_gpu(args) -> None:
+def cnn_flops(N: int) -> float:
+    """Conv FLOPs of one fwd+bwd step of the small CNN (VALID padding, the shapes the
+    reference's tracer infers): forward and weight gradient of the three convs, input
+    gradient of the last two (the first conv's is dead)."""
+    f1 = 2.0 * 64 * 30 * 30 * 3 * 9
+    f2 = 2.0 * 64 * 14 * 14 * 64 * 9
+    f3 = 2.0 * 128 * 6 * 6 * 64 * 9
+    return N * (2 * (f1 + f2 + f3) + f2 + f3)
+
+
+class GemmTimer:
+    """CUDA events around every bf16 tcgen05 GEMM launch of one eager plan run, on the
+    launching stream: algorithmic FLOPs (2 M N K per batch matrix) / event time."""
+
+    NAMES = ("b200_gemm", "b200_gemm_batched2")
+
+    def __init__(self) -> None:
+        self.recs: list = []
+
+    def run(self, plan, inputs) -> dict:
+        import torch
+
+        from b200 import _lib as L
+
+        orig = L.call
+
+        def call(name, *a):
+            if name in self.NAMES and a[0] == L.BF16:
+                e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+                e0.record()
+                orig(name, *a)
+                e1.record()
+                fl = 2.0 * a[5] * a[6] * a[7] * a[8] * (a[9] if name == "b200_gemm_batched2" else 1)
+                self.recs.append((fl, e0, e1))
+            else:
+                orig(name, *a)
+
+        L.call = call
+        try:
+            plan.run(dict(inputs))
+            torch.cuda.synchronize()
+        finally:
+            L.call = orig
+        fl = sum(r[0] for r in self.recs)
+        ms = sum(r[1].elapsed_time(r[2]) for r in self.recs)
+        return {"launches": len(self.recs), "flops": fl, "ms": ms}
+
+
+def _sync_fn(dist, sync, grads):
+    if dist is None:
+        return lambda out: None
+    return lambda out: sync([out[g] for g in grads])
+
+
+def measure(name: str, args, world: int, rank: int, dist, dev, headline: bool) -> dict:
+    """Time one workload: CUDA-graph replays of its fused plan on resident inputs (plus the
+    gradient exchange at N > 1), then the same steps end to end through the public
+    ``compile_graph`` call with pinned host inputs and every output copied back."""
     import torch
 
-    rank, world = env_int("RANK", 0), env_int("WORLD_SIZE", 1)
-    local = env_int("LOCAL_RANK", 0)
-    torch.cuda.set_device(local)
-    dist = None
-    if world > 1:
-        import datetime
-
-        import torch.distributed as dist
-
-        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=torch.device("cuda", local))
     from b200 import _lib
     from b200 import graph as G
     from b200 import ops
     from b200.backend import B200Backend
+    from b200.dp import GradAllReduce
     from b200.executor import CompiledGraph
     from b200.workloads import make_inputs
 
-    spec = WORKLOADS[args.workload]
+    spec = WORKLOADS[name]
     ops.Config.matmul_dtype = "bf16" if spec["dtype"] == "bf16" else "f32"
     ops.Config.conv_dtype = ops.Config.matmul_dtype
-    # strong scaling (fixed global batch split over ranks) where a per-rank graph exists,
-    # weak scaling (one full batch per rank) otherwise
     strong = world > 1 and world in spec.get("dp_graphs", {})
-    g = G.load(spec["dp_graphs"][world] if strong else spec["graph"])
+    gname = spec["dp_graphs"][world] if strong else spec["graph"]
+    g = G.load(gname)
     arrays = make_inputs(g.meta["workload"], g.meta["dims"], seed=rank)  # each rank: its own shard
     params = [k[2:] for k in g.output_names if k.startswith("d_")] if spec["params"] == "all" else spec["params"]
     grad_ids = [g.output_names["d_" + r] for r in params]
-    scale_grads = strong and spec.get("reduce") == "mean"
+    sync = GradAllReduce("mean" if (strong and spec["reduce"] == "mean") else "sum")
+    allreduce = _sync_fn(dist, sync, grad_ids)
 
-    dev = torch.device("cuda", local)
-    # bf16 workloads feed their bf16 operands as bf16 tensors (the values are bf16-exact)
     bf16_roles = set(spec.get("bf16_inputs", []))
     dinputs = {nid: torch.from_numpy(np.ascontiguousarray(arrays[r])).to(dev) for r, nid in g.roles.items()}
     for r in bf16_roles:
         dinputs[g.roles[r]] = dinputs[g.roles[r]].to(torch.bfloat16)
-    cg = CompiledGraph(g)
-    out = cg(dinputs)  # plan + capture
-    torch.cuda.synchronize()
-    dinputs = cg.static_in  # inputs resident in the graph's static buffers from here on
-    plan = cg.runner.plan_for(cg.static_in)
-    n_before = _lib.launch_count()
-    plan.run(dict(cg.static_in))  # one eager run of the fused plan: count its kernels
-    torch.cuda.synchronize()
-    launches_per_step = int(_lib.launch_count() - n_before)
-    n_capture = len(plan.steps)
-
-    from b200.dp import GradAllReduce
-
-    sync = GradAllReduce("mean" if scale_grads else "sum")
-
-    def allreduce():
-        if dist is not None:
-            # data-parallel gradient exchange over NCCL (NVLink); a mean loss over the global
-            # batch is the average of the per-shard means
-            sync([out[gid] for gid in grad_ids])
-
     stream = torch.cuda.current_stream()
+    overlap = dist is not None and strong and not args.no_overlap
+    exchange = ov = cg = None
+    if overlap:
+        # gradient buckets all-reduced on a side stream while the backward computes
+        from b200.dp import OverlappedStep
+
+        ov = OverlappedStep(g, dinputs, grad_ids, sync)
+        static_in, plan = ov.static_in, ov.plan
+    else:
+        cg = CompiledGraph(g)
+        out = cg(dinputs)  # plan + capture
+        torch.cuda.synchronize()
+        static_in = cg.static_in  # resident in the graph's static buffers from here on
+        plan = cg.runner.plan_for(cg.static_in)
+    n0 = _lib.launch_count()
+    plan.run(dict(static_in))  # one eager run of the plan: count its kernels
+    torch.cuda.synchronize()
+    launches_per_step = int(_lib.launch_count() - n0)
+
     sync_launches = 0
     for i in range(args.warmup):
-        out = cg(dinputs)
-        n0 = _lib.launch_count()
-        allreduce()
+        if ov is not None:
+            n1 = _lib.launch_count()
+            ov()
+            if i == args.warmup - 1:
+                sync_launches = max(0, int(_lib.launch_count() - n1))  # exchange kernels (graph replays do not count)
+            continue
+        out = cg(static_in)
+        n1 = _lib.launch_count()
+        allreduce(out)
         if i == args.warmup - 1:
-            sync_launches = int(_lib.launch_count() - n0)  # our own kernels in the gradient exchange
+            sync_launches = int(_lib.launch_count() - n1)
     torch.cuda.synchronize()
-    # an exchange that only uses the peer-memory kernel replays as one CUDA graph per step
-    exchange = None
-    if dist is not None and sync.graph_safe([out[gid] for gid in grad_ids]):
+    if cg is not None and dist is not None and sync.graph_safe([out[gid] for gid in grad_ids]):
         exchange = torch.cuda.CUDAGraph()
         with torch.cuda.graph(exchange):
-            allreduce()
+            allreduce(out)
         torch.cuda.synchronize()
     if dist is not None:
         dist.barrier()
     torch.cuda.synchronize()
     ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    with ClockSampler(local) as clk:
+    with ClockSampler(env_int("LOCAL_RANK", 0)) as clk:
         ev0.record(stream)
         for _ in range(args.steps):
-            out = cg(dinputs)
+            if ov is not None:
+                ov()
+                continue
+            out = cg(static_in)
             if exchange is not None:
                 exchange.replay()
             else:
-                allreduce()
+                allreduce(out)
         ev1.record(stream)
         torch.cuda.synchronize()
     if dist is not None:
         dist.barrier()
     ms = ev0.elapsed_time(ev1)
-    sync.check()  # a peer wait that gave up raises here
+    sync.check()  # collective: a peer wait that gave up raises here on every rank
     t = torch.tensor([ms], device=dev)
     if dist is not None:
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
     ms_max = float(t.item())
+    ms_step = ms_max / args.steps
     value = (1 if strong else world) * args.steps / (ms_max / 1000.0)
+    res = {"value": round(value, 3), "unit": "steps/s", "ms_per_step": round(ms_step, 4),
+           "scaling": "strong" if strong else "weak", "graph": gname, "dims": g.meta["dims"],
+           "launches_per_step": launches_per_step + sync_launches, "gpu_launches": (launches_per_step + sync_launches) * args.steps,
+           "plan_steps": len(plan.steps), "clocks": clk.summary(),
+           "grad_exchange": ((("overlapped with the backward: " + json.dumps(ov.describe())) if ov is not None else "after the step")
+                             + "; " + (("peer-memory kernel" + (", CUDA graph" if exchange is not None else " + NCCL buckets"))
+                                       if sync.peer is not None else "NCCL buckets")) if world > 1 else None}
+    if headline:
+        res["plan"] = plan.describe()
 
-    # dominant kernel alone, CUDA events on its stream (roofline)
+    # roofline of the dominant kernel
+    pk = peaks()
     roof = None
-    if args.workload == "rowfused":
+    if name in ("transformer", "bmm"):
+        gt = GemmTimer().run(plan, static_in)
+        ach = gt["flops"] / (gt["ms"] / 1000.0) / 1e12
+        peak = pk["bf16_tflops_sustained"]
+        roof = {"bound": "tensor", "kernel": "gemm_tc_kernel (tcgen05, every bf16 GEMM launch of one step)", "achieved": round(ach, 1),
+                "peak": peak, "peak_kind": "sustained (GEMMs timed inside a long step)", "unit": "TFLOP/s",
+                "frac": round(ach / peak, 4), "peak_source": pk["source"], "launches": gt["launches"],
+                "algorithmic_flops": gt["flops"], "kernel_ms": round(gt["ms"], 4), "traffic": None,
+                "step_tflops": round(gt["flops"] / (ms_step / 1000.0) / 1e12, 1)}
+    elif name == "rowfused":
         R, C = g.meta["dims"]["R"], g.meta["dims"]["C"]
-        xs = [dinputs[g.roles[k]] for k in ("x", "a", "b", "gamma", "beta", "cotangent")]
-        y = torch.empty(R, C, device=dev)
-        dx = torch.empty(R, C, device=dev)
-        am = torch.empty(R, dtype=torch.int64, device=dev)
-        da, db = torch.empty(C, device=dev), torch.empty(C, device=dev)
-        wsb = int(_lib.lib().b200_rowfused_workspace_bytes(R, C))
-        ws = torch.empty(wsb, dtype=torch.uint8, device=dev)
-        s = ops.stream_ptr()
-
-        def launch():
-            _lib.call("b200_rowfused_fwd_bwd", *[x.data_ptr() for x in xs], y.data_ptr(), am.data_ptr(), dx.data_ptr(),
-                      da.data_ptr(), db.data_ptr(), None, None, R, C, 1e-5, ws.data_ptr(), wsb, s)
-
-        for _ in range(3):
-            launch()
-        torch.cuda.synchronize()
-        evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(max(5, args.steps))]
-        for a, b in evs:
-            a.record(stream)
-            launch()
-            b.record(stream)
-        torch.cuda.synchronize()
-        kms = statistics.mean(a.elapsed_time(b) for a, b in evs)
-        pk = peaks()
         bytes_ = algorithmic_bytes_rowfused(R, C)
-        ach = bytes_ / (kms / 1000.0) / 1e9
-        roof = {"bound": "hbm", "kernel": "rowfused_fwd_bwd (+colsum)", "achieved": round(ach, 1), "peak": pk["hbm_gbs"],
-                "unit": "GB/s", "frac": round(ach / pk["hbm_gbs"], 4), "peak_source": pk["source"],
-                "algorithmic_bytes": bytes_, "kernel_ms": round(kms, 4), "traffic": args.traffic}
+        ach = bytes_ / (ms_step / 1000.0) / 1e9
+        roof = {"bound": "hbm", "kernel": "rowfused (fused row kernel + column-sum kernel: the whole replayed step)",
+                "achieved": round(ach, 1), "peak": pk["hbm_gbs"], "unit": "GB/s", "frac": round(ach / pk["hbm_gbs"], 4),
+                "peak_source": pk["source"], "algorithmic_bytes": bytes_, "kernel_ms": round(ms_step, 4), "traffic": args.traffic}
+    elif name == "cnn":
+        fl = cnn_flops(g.meta["dims"]["N"])
+        ach = fl / (ms_step / 1000.0) / 1e12
+        roof = {"bound": "tensor", "kernel": "whole step (conv FLOPs / step time)", "achieved": round(ach, 2),
+                "peak": pk["bf16_tflops_sustained"], "unit": "TFLOP/s", "frac": round(ach / pk["bf16_tflops_sustained"], 4),
+                "peak_source": pk["source"], "algorithmic_flops": fl, "traffic": None}
+    res["roofline"] = roof
 
-    # end-to-end through the public API with host buffers
-    e2e = None
+    # end to end through the public API: pinned host inputs in, every output back to pinned host
     if not args.no_e2e:
         host = {nid: torch.from_numpy(np.ascontiguousarray(arrays[r])) for r, nid in g.roles.items()}
         for r in bf16_roles:
             host[g.roles[r]] = host[g.roles[r]].to(torch.bfloat16)
         host = {k: v.pin_memory() for k, v in host.items()}
-        res_ids = [g.output_names[k] for k in g.output_names if k.startswith("d_") and k[2:] in params]
-        if "argmax" in g.output_names:
-            res_ids.append(g.output_names["argmax"])
-        if "loss" in g.output_names:
-            res_ids.append(g.output_names["loss"])
-        host_out = {k: torch.empty(out[k].shape, dtype=out[k].dtype).pin_memory() for k in res_ids}
+        out_ids = list(dict.fromkeys(g.output_names.values()))
+        ref_out = ov.static_out if ov is not None else out
+        host_out = {k: torch.empty(ref_out[k].shape, dtype=ref_out[k].dtype).pin_memory() for k in out_ids}
         h2d = sum(v.numel() * v.element_size() for v in host.values())
         d2h = sum(v.numel() * v.element_size() for v in host_out.values())
+        del cg, ov, plan, ref_out
+        out = None
+        gc.collect()
+        torch.cuda.empty_cache()
         fn = B200Backend.compile_graph(g)
 
         def e2e_step():
-            o = fn(host)  # pinned host inputs: copied by the call straight into its static buffers
-            if dist is not None:
-                sync([o[gid] for gid in grad_ids])
-            for k in res_ids:
+            o = fn(host)  # pinned host inputs copied by the call straight into its static buffers
+            allreduce(o)
+            for k in out_ids:
                 host_out[k].copy_(o[k], non_blocking=True)
 
         for _ in range(max(2, args.warmup)):
@@ -377,48 +492,107 @@ def run_gpu(args) -> None:
         et = torch.tensor([a.elapsed_time(b)], device=dev)
         if dist is not None:
             dist.all_reduce(et, op=dist.ReduceOp.MAX)
-        e2e = {"value": round((1 if strong else world) * args.steps / (float(et.item()) / 1000.0), 3), "unit": "steps/s",
-               "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h}
+        res["e2e"] = {"value": round((1 if strong else world) * args.steps / (float(et.item()) / 1000.0), 3), "unit": "steps/s",
+                      "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
+                      "outputs_copied": f"all {len(out_ids)} graph outputs"}
+        del fn
+    gc.collect()
+    torch.cuda.empty_cache()
+    return res
 
+
+def run_gpu(args) -> None:
+    import torch
+
+    rank, world = env_int("RANK", 0), env_int("WORLD_SIZE", 1)
+    local = env_int("LOCAL_RANK", 0)
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    dist = None
+    if world > 1:
+        import datetime
+
+        import torch.distributed as dist
+
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=dev)
+    from b200 import _lib
+
+    _lib.load()
+    head = args.workload
+    others = [] if args.only else [w for w in CONFIG_ORDER if w != head]
+    results = {head: measure(head, args, world, rank, dist, dev, headline=True)}
+    for w in others:
+        results[w] = measure(w, args, world, rank, dist, dev, headline=False)
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu:
-        cpu = cpu_reference(args.workload)
-
+        cpu = cpu_baseline(head)
     if rank == 0:
+        h = results[head]
+        spec = WORKLOADS[head]
         line = {
             "metric": "fwd+bwd graph steps/sec",
-            "value": round(value, 3),
+            "value": h["value"],
             "unit": "steps/s",
             "n_gpus": world,
             "steps": args.steps,
             "warmup": args.warmup,
-            "ms_per_step": round(ms_max / args.steps, 4),
+            "ms_per_step": h["ms_per_step"],
             "higher_is_better": True,
-            "scaling": "strong" if strong else "weak",
+            "scaling": h["scaling"],
             "vs_baseline": None,
             "dtype": spec["dtype"],
             "data": "synthetic (seeded numpy, per-rank seed)",
-            "config": {"workload": spec["desc"], "graph": spec["dp_graphs"][world] if strong else spec["graph"], "dims": g.meta["dims"],
+            "config": {"workload": spec["desc"], "graph": h["graph"], "dims": h["dims"],
                        "parallelism": f"dp{world}" if world > 1 else "single",
-                       "l2": "inputs larger than the 126 MB L2 (no flush needed)" if args.workload in ("rowfused", "bmm") else "L2 not flushed",
-                       "replay": "CUDA graph of the fused plan",
-                       "grad_exchange": ((("peer-memory kernel" + (", CUDA graph" if exchange is not None else " + NCCL buckets"))
-                                          if sync.peer is not None else "NCCL buckets") if world > 1 else None)},
-            "gpu_launches": int((launches_per_step + sync_launches) * args.steps),
-            "launches_per_step": launches_per_step + sync_launches,
-            "plan_steps": int(n_capture),
-            "plan": plan.describe(),
-            "clocks": clk.summary(),
-            "roofline": roof,
+                       "l2": "inputs and the step's working set larger than the 126 MB L2 (no flush needed)",
+                       "replay": "CUDA graph of the fused plan", "grad_exchange": h["grad_exchange"]},
+            "gpu_launches": sum(r["gpu_launches"] for r in results.values()),
+            "launches_per_step": h["launches_per_step"],
+            "plan_steps": h["plan_steps"],
+            "plan": h.get("plan"),
+            "clocks": h["clocks"],
+            "roofline": h["roofline"],
             "cpu_baseline": cpu,
-            "e2e": e2e,
+            "e2e": h.get("e2e"),
+            "configs": {w: {k: v for k, v in r.items() if k not in ("plan",)} for w, r in results.items() if w != head},
         }
         print(json.dumps(line), flush=True)
-    cg.cuda_graph = None
-    exchange = None
     if dist is not None:
         dist.barrier()
         dist.destroy_process_group()
+
+
+def run_reference(args) -> None:
+    """The reference algorithm on the host CPU (the oracle port), for the same workload,
+    metric and unit as the GPU arm: one untimed warm-up evaluation, then timed samples
+    (at most --steps, stopped once ~90 s of samples have run); only evaluations are timed."""
+    rank = env_int("RANK", 0)
+    if rank != 0:
+        return
+    spec = WORKLOADS[args.workload]
+    ref = CpuReference(args.workload)
+    try:
+        ref.prepare()
+        times: list[float] = []
+        spent = 0.0
+        while len(times) < max(1, args.steps):
+            t0 = time.perf_counter()
+            times.append(ref.sample())
+            spent += time.perf_counter() - t0
+            if spent > 90.0:
+                break
+    finally:
+        ref.close()
+    v = 1.0 / statistics.median(times)
+    line = {"impl": "reference", "metric": "fwd+bwd graph steps/sec", "value": v, "unit": "steps/s",
+            "n_gpus": env_int("WORLD_SIZE", 1), "steps": len(times), "warmup": 1,
+            "ms_per_step": 1000.0 / v, "higher_is_better": True, "scaling": "weak",
+            "vs_baseline": None, "dtype": spec["dtype"], "data": "synthetic (seeded numpy)",
+            "config": {"workload": spec["desc"], "graph": spec["graph"]},
+            "timed_region_s": round(spent, 2),
+            "cpu_baseline": ref.baseline(v, len(times)),
+            "e2e": {"value": v, "unit": "steps/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+    print(json.dumps(line), flush=True)
 
 
 def run_gemm_micro(args) -> None:
@@ -567,41 +741,21 @@ def run_weights_micro(args) -> None:
                       "load": {"s": round(min(load_s), 4), "GB/s": round(nbytes / min(load_s) / 1e9, 2)}}), flush=True)
 
 
-def run_reference(args) -> None:
-    rank = env_int("RANK", 0)
-    if rank != 0:
-        return
-    spec = WORKLOADS[args.workload]
-    vals = []
-    info = None
-    for _ in range(max(1, args.warmup if args.workload != "rowfused" else 0)):
-        pass
-    for _ in range(max(1, min(args.steps, 3))):
-        info = cpu_reference(args.workload, budget_s=8.0)
-        vals.append(info["value"])
-    v = statistics.median(vals)
-    info["value"] = v
-    line = {"impl": "reference", "metric": "fwd+bwd graph steps/sec", "value": v, "unit": "steps/s",
-            "n_gpus": env_int("WORLD_SIZE", 1), "steps": args.steps, "warmup": args.warmup,
-            "ms_per_step": 1000.0 / v if v else None, "higher_is_better": True, "scaling": "weak",
-            "vs_baseline": None, "dtype": spec["dtype"], "data": "synthetic (seeded numpy)",
-            "config": {"workload": spec["desc"], "graph": spec["graph"]},
-            "cpu_baseline": info, "e2e": {"value": v, "unit": "steps/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
-    print(json.dumps(line), flush=True)
-
 
 def main() -> None:
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=20)
     ap.add_argument("--warmup", type=int, default=5)
-    ap.add_argument("--workload", default="rowfused", choices=sorted(WORKLOADS) + ["gemm", "adam", "weights"])
+    ap.add_argument("--workload", default="transformer", choices=sorted(WORKLOADS) + ["gemm", "adam", "weights"])
+    ap.add_argument("--only", action="store_true", help="time the --workload alone (no configs block)")
     ap.add_argument("--impl", default="b200", choices=["b200", "reference"])
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline leg")
     ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--no-overlap", action="store_true", help="all-reduce after the step instead of during the backward")
     # dram__bytes_read.sum + dram__bytes_write.sum of one rowfused2_kernel launch at
-    # [8192, 4096] (ncu --set full capture summarised in profiles/rowfused_kernel_8192x4096.md)
-    ap.add_argument("--traffic", type=float, default=488077312.0, help="ncu dram bytes per launch of the dominant kernel")
+    # [8192, 4096] (ncu capture summarised in profiles/rowfused_kernel_8192x4096.md)
+    ap.add_argument("--traffic", type=float, default=488077312.0, help="ncu dram bytes per launch of the row kernel")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3

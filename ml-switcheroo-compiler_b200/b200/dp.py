@@ -392,3 +392,108 @@ class GradAllReduce:
                 off += t.numel()
             if step is not None and peer is None:
                 step.apply(b, ts)
+
+
+class OverlappedStep:
+    """One data-parallel fwd+bwd step with the gradient all-reduce overlapped with the
+    backward pass.
+
+    The reference puts its ``AllReduce`` nodes after the whole backward
+    (``transforms/passes/spmd.py:636``); here each gradient is exchanged as soon as the
+    step that writes it (and every step that reads it) has run. The fused plan is captured
+    as a few CUDA graphs, split where a bucket of gradients becomes final: gradients are
+    grouped in the order the backward finishes them, ``bucket_bytes`` or more per bucket.
+    A replay runs the segments on the current (compute) stream; after each one an event
+    releases that segment's buckets to a communication stream, which all-reduces them with
+    ``GradAllReduce`` (NCCL, or the peer-memory kernel for small fp32 buckets) while the
+    next segment computes. The compute stream waits for the communication stream at the
+    end, so the returned gradients are the all-reduced ones.
+
+    The segments share one CUDA graph memory pool and always replay in capture order, so
+    memory one segment frees can be reused by a later one exactly as inside one graph.
+    Gradients are graph outputs and are never freed, so the communication stream can read
+    and write them while later segments run."""
+
+    def __init__(self, graph, inputs: dict, grad_ids: Sequence[str], sync: "GradAllReduce",
+                 bucket_bytes: int = 48 << 20, max_segments: int = 8) -> None:
+        from . import ops
+        from .executor import GraphRunner
+
+        self.runner = GraphRunner(graph)
+        self.sync = sync
+        self.static_in = {k: (ops.copy(v) if isinstance(v, torch.Tensor) else v) for k, v in inputs.items()}
+        plan = self.runner.plan_for(self.static_in)
+        self.plan = plan
+        last = plan.last_use()
+        n = len(plan.steps)
+        ready = sorted((last.get(gid, n - 1), k, gid) for k, gid in enumerate(grad_ids))
+        # warm-up run (eager, side stream): allocations settle, output shapes known
+        side = torch.cuda.Stream()
+        side.wait_stream(torch.cuda.current_stream())
+        with torch.cuda.stream(side):
+            out = plan.run(dict(self.static_in))
+        torch.cuda.current_stream().wait_stream(side)
+        torch.cuda.synchronize()
+        sizes = {gid: out[gid].numel() * out[gid].element_size() for gid in grad_ids}
+        del out
+        # buckets in finishing order; a bucket is released after its last gradient's step
+        buckets: list[tuple[int, list[str]]] = []
+        cur: list[str] = []
+        acc = 0
+        for pos, _, gid in ready:
+            cur.append(gid)
+            acc += sizes[gid]
+            if acc >= bucket_bytes:
+                buckets.append((pos, cur))
+                cur, acc = [], 0
+        if cur:
+            buckets.append((ready[-1][0], cur))
+        # at most max_segments segments: merge the earliest buckets when there are more
+        while len(buckets) > max_segments:
+            (p0, b0), (p1, b1) = buckets[0], buckets[1]
+            buckets[0:2] = [(max(p0, p1), b0 + b1)]
+        self.buckets = buckets
+        cuts = sorted({p + 1 for p, _ in buckets} | {n})
+        self.bounds = list(zip([0] + cuts[:-1], cuts))
+        self.release = {}  # segment index -> bucket lists released after it
+        for p, b in buckets:
+            seg = next(i for i, (lo, hi) in enumerate(self.bounds) if lo <= p < hi)
+            self.release.setdefault(seg, []).append(b)
+        # capture the segments into graphs sharing one memory pool
+        pool = torch.cuda.graph_pool_handle()
+        self.graphs: list[torch.cuda.CUDAGraph] = []
+        env = plan.begin(self.static_in)
+        try:
+            for lo, hi in self.bounds:
+                cg = torch.cuda.CUDAGraph()
+                with torch.cuda.graph(cg, pool=pool):
+                    plan.run_steps(env, lo, hi)
+                self.graphs.append(cg)
+        finally:
+            self.static_out = plan.finish(env)
+        self.comm = torch.cuda.Stream()
+        self.events = [torch.cuda.Event() for _ in self.bounds]
+
+    def __call__(self, inputs: dict | None = None) -> dict:
+        """Replay one step (inputs, when given, are copied into the static buffers first)
+        and return the graph's outputs with the gradients all-reduced."""
+        if inputs:
+            for k, v in inputs.items():
+                dst = self.static_in[k]
+                if isinstance(dst, torch.Tensor) and v is not dst:
+                    dst.copy_(v, non_blocking=True)
+        compute = torch.cuda.current_stream()
+        for i, g in enumerate(self.graphs):
+            g.replay()
+            if i in self.release:
+                self.events[i].record(compute)
+                self.comm.wait_event(self.events[i])
+                with torch.cuda.stream(self.comm):
+                    for b in self.release[i]:
+                        self.sync([self.static_out[gid] for gid in b])
+        compute.wait_stream(self.comm)
+        return self.static_out
+
+    def describe(self) -> dict:
+        return {"segments": len(self.graphs), "buckets": [len(b) for _, b in self.buckets],
+                "released_after_steps": [p for p, _ in self.buckets]}

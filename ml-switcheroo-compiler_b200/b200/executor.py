@@ -192,26 +192,47 @@ class Plan:
             if v not in outs and v not in self.input_ids:
                 self.free_after[i].append(v)
 
-    def run(self, inputs: dict[str, Any]) -> dict[str, Any]:
+    def begin(self, inputs: dict[str, Any]) -> dict[str, Any]:
+        """The environment of one run: initializers and inputs (missing inputs raise)."""
         env: dict[str, Any] = dict(self.graph.initializers)
         env.update(inputs)
         for i in self.input_ids:
             if i not in env:
                 raise ValueError(f"Missing input value for node '{i}'")  # environment.py:33-48
         ops.clear_cast_cache()
-        try:
-            for st, dead in zip(self.steps, self.free_after):
-                st.fn(env)
-                for v in dead:
-                    env.pop(v, None)
-        finally:
-            ops.clear_cast_cache()
+        return env
+
+    def run_steps(self, env: dict[str, Any], lo: int, hi: int) -> None:
+        """Steps [lo, hi) of a run begun with ``begin``; values die after their last use."""
+        for st, dead in zip(self.steps[lo:hi], self.free_after[lo:hi]):
+            st.fn(env)
+            for v in dead:
+                env.pop(v, None)
+
+    def finish(self, env: dict[str, Any]) -> dict[str, Any]:
+        ops.clear_cast_cache()
         res = {}
         for oid in self.graph.outputs:
             if oid not in env:
                 raise RuntimeError(f"Output node '{oid}' was never evaluated.")  # evaluator.py:301-303
             res[oid] = env[oid]
         return res
+
+    def run(self, inputs: dict[str, Any]) -> dict[str, Any]:
+        env = self.begin(inputs)
+        try:
+            self.run_steps(env, 0, len(self.steps))
+        finally:
+            ops.clear_cast_cache()
+        return self.finish(env)
+
+    def last_use(self) -> dict[str, int]:
+        """Index of the last step that produces or reads each value."""
+        last: dict[str, int] = {}
+        for i, st in enumerate(self.steps):
+            for v in list(st.outputs) + list(st.inputs):
+                last[v] = i
+        return last
 
     def describe(self) -> list[str]:
         return [s.label for s in self.steps]

@@ -92,6 +92,8 @@ GRAPH_CASES: dict[str, tuple[str, dict]] = {
     "transformer_b32": ("transformer", dict(WORKLOADS["transformer"]["full"], B=32)),
     "transformer_b16": ("transformer", dict(WORKLOADS["transformer"]["full"], B=16)),
     "transformer_b8": ("transformer", dict(WORKLOADS["transformer"]["full"], B=8)),
+    # one sequence at full width: the bounded CPU sample of the transformer step
+    "transformer_b1": ("transformer", dict(WORKLOADS["transformer"]["full"], B=1)),
 }
 
 # Small cases with reference-evaluated golden outputs.

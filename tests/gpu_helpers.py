@@ -25,15 +25,37 @@ def to_np(v):
     return np.asarray(v)
 
 
-def assert_close(name, got, ref, rtol, atol_scale=None):
+def rms(a) -> float:
+    a = np.asarray(a, dtype=np.float64)
+    return float(np.sqrt(np.mean(a * a))) if a.size else 0.0
+
+
+def assert_close(name, got, ref, rtol, floor=0.0):
+    """Elementwise: |got - ref| <= rtol * |ref| + atol for every element, with the
+    absolute floor atol = rtol * max(rms(ref), floor).
+
+    Why a floor at all: an entry much smaller than its output's typical magnitude is a sum
+    whose terms cancelled, so its absolute rounding error is set by the size of those
+    terms, which is the output's RMS, not by the entry itself. The floor bounds that error
+    at rtol of the RMS. ``floor`` (default 0) covers outputs that are zero in exact
+    arithmetic (pure rounding noise, RMS included): the caller derives it from a related
+    output. Integer / bool outputs (argmax, labels, gathers) must be bit-exact."""
     got = to_np(got)
+    ref = np.asarray(ref)
     assert got.shape == ref.shape, (name, got.shape, ref.shape)
     if ref.dtype.kind in "iub":
         np.testing.assert_array_equal(got, ref, err_msg=name)
         return
-    scale = float(np.abs(ref).max()) if ref.size else 1.0
-    atol = rtol * max(scale, 1e-30) if atol_scale is None else atol_scale
-    np.testing.assert_allclose(got.astype(np.float64), ref.astype(np.float64), rtol=rtol, atol=atol, err_msg=name)
+    g64, r64 = got.astype(np.float64), ref.astype(np.float64)
+    atol = rtol * max(rms(r64), float(floor), 1e-30)
+    err = np.abs(g64 - r64)
+    lim = atol + rtol * np.abs(r64)
+    bad = ~(err <= lim)
+    if bad.any():
+        k = int(np.argmax(np.where(bad, err / lim, 0)))
+        raise AssertionError(f"{name}: {int(bad.sum())} of {ref.size} elements outside rtol {rtol} (atol {atol:.3g}); "
+                             f"worst at flat index {k}: got {g64.flat[k]:.6g}, ref {r64.flat[k]:.6g}, "
+                             f"|diff| / limit = {float(err.flat[k] / lim.flat[k]):.3g}")
 
 
 def run_case(case: str, mode: str = "graph"):

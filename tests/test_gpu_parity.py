@@ -1,14 +1,18 @@
 """Whole-graph parity: every golden case (fwd+bwd graph traced and differentiated by the
 reference, evaluated by the reference numpy backend) run on the b200 backend.
 
-Tolerances (written per workload):
-* fp32 workloads (mlp, rowfused): rtol 1e-4 of each output's max magnitude against the
-  reference golden vectors; integer outputs (argmax) bit-exact.
-* bf16-math workloads (bmm, cnn, transformer): rtol 2e-2 of max magnitude against the
-  oracle evaluated under the same bf16 operand-rounding policy (contraction operands
-  rounded to bf16, fp32 accumulation); against the pure-fp32 reference golden the
-  norm-wise relative error must stay within 0.1 (bf16 rounding alone gives up to 0.057
-  on the cancellation-heavy first-conv weight gradient at batch 4).
+Tolerances (written per workload; elementwise, ``gpu_helpers.assert_close``):
+* fp32 workloads (mlp, rowfused, the node-type cases): rtol 1e-4 per element, absolute
+  floor 1e-4 x the output's RMS, against the reference golden vectors; integer outputs
+  (argmax) bit-exact.
+* bf16-math workloads (bmm, cnn, transformer): rtol 2e-2 per element, absolute floor
+  2e-2 x the output's RMS, against the oracle evaluated under the same bf16
+  operand-rounding policy (contraction operands rounded to bf16, fp32 accumulation).
+  Outputs that are zero in exact arithmetic (the attention key-bias gradients: softmax
+  is invariant to a per-row shift) are rounding noise, so their floor is 1e-3 of the
+  largest output instead. Against the pure-fp32 reference golden the norm-wise relative
+  error must stay within 0.1 (bf16 rounding alone gives up to 0.057 on the
+  cancellation-heavy first-conv weight gradient at batch 4).
 """
 
 import numpy as np
@@ -24,6 +28,12 @@ CASES = ["mlp_small", "mlp_ragged", "rowfused_small", "rowfused_ragged", "bmm_sm
          "nodes_indexing"]
 RTOL = {"mlp": 1e-4, "rowfused": 1e-4, "bmm": 2e-2, "cnn": 2e-2, "transformer": 2e-2, "nodes": 1e-4}
 BF16 = {"bmm", "cnn", "transformer"}
+
+
+def _exact_zero(name: str) -> bool:
+    """Gradients that vanish in exact arithmetic: the attention key bias (softmax over the
+    key axis is invariant to adding the same q.bk to every score of a row)."""
+    return name.startswith("d_") and name.endswith("_bk")
 
 
 @pytest.mark.gpu
@@ -54,8 +64,7 @@ def test_graph_parity(cuda, case, mode):
         floor = 1e-3 * max(float(np.abs(np.asarray(v)).max()) for v in emu.values() if np.asarray(v).size)
         for name, r in ref.items():
             e = np.asarray(emu[name], dtype=np.float32)
-            atol = rtol * max(float(np.abs(e).max()) if e.size else 0.0, floor)
-            assert_close(f"{case}:{name}(bf16 policy)", got[name], e, rtol, atol_scale=atol)
+            assert_close(f"{case}:{name}(bf16 policy)", got[name], e, rtol, floor=floor if _exact_zero(name) else 0.0)
             v = to_np(got[name]).astype(np.float64)
             nrel = np.linalg.norm(v - r) / max(np.linalg.norm(r), floor * np.sqrt(r.size), 1e-30)
             assert nrel <= 0.1, (name, nrel)
