@@ -202,10 +202,15 @@ class Plan:
         ops.clear_cast_cache()
         return env
 
-    def run_steps(self, env: dict[str, Any], lo: int, hi: int) -> None:
-        """Steps [lo, hi) of a run begun with ``begin``; values die after their last use."""
+    def run_steps(self, env: dict[str, Any], lo: int, hi: int, capture: dict | None = None) -> None:
+        """Steps [lo, hi) of a run begun with ``begin``; values die after their last use.
+        ``capture`` (id -> None) receives the values of those ids as they are produced."""
         for st, dead in zip(self.steps[lo:hi], self.free_after[lo:hi]):
             st.fn(env)
+            if capture is not None:
+                for o in st.outputs:
+                    if o in capture and o in env:
+                        capture[o] = env[o]
             for v in dead:
                 env.pop(v, None)
 
@@ -218,10 +223,10 @@ class Plan:
             res[oid] = env[oid]
         return res
 
-    def run(self, inputs: dict[str, Any]) -> dict[str, Any]:
+    def run(self, inputs: dict[str, Any], capture: dict | None = None) -> dict[str, Any]:
         env = self.begin(inputs)
         try:
-            self.run_steps(env, 0, len(self.steps))
+            self.run_steps(env, 0, len(self.steps), capture)
         finally:
             ops.clear_cast_cache()
         return self.finish(env)

@@ -199,7 +199,7 @@ def run_dag(dag: ExprDag, root: int, inputs: list[Any], shape: tuple) -> torch.T
         if prog is not None:
             p = ops.Prog()
             p.inputs = [inputs[k] for k in used_inputs]
-            p.ins, p.nreg = prog
+            p.ins, p.nreg = prog[0], prog[1]
             return p.run([(prog[2], torch.float32)], shape)[0]
     # one kernel per node
     vals: dict[int, Any] = {}

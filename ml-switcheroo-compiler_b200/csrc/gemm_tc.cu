@@ -11,6 +11,7 @@
 // Every mbarrier wait is bounded by a wall-clock limit: on expiry the thread records
 // B200_ERR_TIMEOUT in the device error flag and the CTA winds down (TMEM is freed).
 #include <cuda.h>
+#include <stdlib.h>
 #include <string.h>
 #include <cudaTypedefs.h>
 
@@ -27,7 +28,7 @@ namespace tc {
 // main loop is short, K <= 128); 2 = the 32 x 32 chunk is staged in a swizzled 4 KB
 // shared-memory buffer per warp and leaves through a TMA bulk-tensor store; 1 = staged
 // the same way, then written back as whole row segments (when no store map fits).
-constexpr int BM = 128, BK = 64, STAGES = 4, EPI_WARPS = B200_GEMM_EPI_WARPS, THREADS = 64 + 32 * EPI_WARPS;
+constexpr int BM = 128, BK = 64, STAGES = 4, STAGES_PAIR = 6, EPI_WARPS = B200_GEMM_EPI_WARPS, THREADS = 64 + 32 * EPI_WARPS;
 constexpr uint32_t EPI_BUF = 4096;  // per epilogue warp
 constexpr uint32_t EPI_SMEM = EPI_WARPS * EPI_BUF;  // after the operand ring
 static_assert(EPI_WARPS == 4 || EPI_WARPS == 8, "4 or 8 epilogue warps (the staging buffers must fit)");
@@ -227,55 +228,113 @@ __device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
   asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
 }
 
-// Persistent kernel: gridDim.x CTAs (one per SM) walk the output tiles in a static
+// ---- CTA pairs (tcgen05 cta_group::2) ----
+// In a cluster of two CTAs, bit 24 of a shared-memory address selects the CTA; clearing
+// it names the same offset in CTA 0, the pair's leader, which owns the barriers the MMA
+// waits on.
+constexpr uint32_t LEADER_MASK = 0xFEFFFFFFu;
+
+__device__ __forceinline__ uint32_t cluster_rank() {
+  uint32_t r;
+  asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+  return r;
+}
+// every thread of both CTAs (not warp-aligned: lanes may arrive separately)
+__device__ __forceinline__ void cluster_sync_all() {
+  asm volatile("barrier.cluster.arrive.release;\n barrier.cluster.wait.acquire;" ::: "memory");
+}
+// TMA load into this CTA's shared memory whose completed bytes count on the leader's barrier
+__device__ __forceinline__ void tma_load_4d_pair(void* dst, const CUtensorMap* map, uint64_t* bar, int c0, int c1, int c2,
+                                                 int c3) {
+  asm volatile(
+      "cp.async.bulk.tensor.4d.cta_group::2.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3, %4, %5}], "
+      "[%6];" ::"r"(smem_u32(dst)),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(c0), "r"(c1), "r"(c2), "r"(c3), "r"(smem_u32(bar) & LEADER_MASK)
+      : "memory");
+}
+__device__ __forceinline__ void mma_bf16_pair(uint32_t tmem_d, uint64_t adesc, uint64_t bdesc, uint32_t idesc, uint32_t acc) {
+  asm volatile(
+      "{\n .reg .pred p;\n setp.ne.b32 p, %4, 0;\n tcgen05.mma.cta_group::2.kind::f16 [%0], %1, %2, %3, p;\n}\n" ::"r"(tmem_d),
+      "l"(adesc), "l"(bdesc), "r"(idesc), "r"(acc));
+}
+// arrive once on the barrier at this offset in both CTAs when the issued MMAs complete
+__device__ __forceinline__ void mma_commit_pair(uint64_t* bar) {
+  asm volatile("tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.multicast::cluster.b64 [%0], %1;" ::"r"(
+                   smem_u32(bar)),
+               "h"((uint16_t)3)
+               : "memory");
+}
+// arrive on the leader's copy of `bar` (a no-op remap in the leader itself)
+__device__ __forceinline__ void mbar_arrive_leader(uint64_t* bar) {
+  asm volatile("mbarrier.arrive.shared::cluster.b64 _, [%0];" ::"r"(smem_u32(bar) & LEADER_MASK) : "memory");
+}
+
+// Persistent kernel: the CTAs (one per SM) walk the output tiles in a static
 // round-robin order (n fastest, then m, then batch: concurrent CTAs share operand panels
 // in L2). The TMEM accumulator is double-buffered (2 x BN columns), so the epilogue of
 // tile i (TMEM -> registers -> HBM) overlaps the MMAs of tile i+1, and the TMA/MMA
 // pipeline runs continuously across tile boundaries.
-template <int BN, int EPI>
-__global__ void __launch_bounds__(THREADS, 1) gemm_tc_kernel(const __grid_constant__ CUtensorMap mapA,
-                                                             const __grid_constant__ CUtensorMap mapB,
-                                                             const __grid_constant__ CUtensorMap mapC,
-                                                             const __grid_constant__ CUtensorMap mapC2,
-                                                             const __grid_constant__ CUtensorMap mapAux,
-                                                             const __grid_constant__ Args args) {
-  constexpr uint32_t A_BYTES = BM * BK * 2;  // 16 KB
-  constexpr uint32_t B_BYTES = BN * BK * 2;
+//
+// PAIR: two CTAs of a cluster compute one 256 x BN tile with tcgen05 cta_group::2. Each
+// CTA loads its 128 rows of A and half of B's BN columns into its own shared memory; the
+// pair's MMA (issued by the leader, CTA 0) reads A and B from both, and writes each CTA's
+// 128 x BN accumulator into that CTA's TMEM. Per SM that halves the B operand's
+// shared-memory traffic (TMA writes + MMA reads), which bounds the single-CTA kernel on
+// 128 x 256 tiles. Both CTAs' loads complete on the leader's stage barrier (it expects
+// the bytes of both); the leader's commits arrive on both CTAs' barriers; the epilogue
+// warps of both CTAs release an accumulator on the leader's barrier.
+template <int BN, int EPI, bool PAIR>
+__device__ __forceinline__ void gemm_body(const CUtensorMap& mapA, const CUtensorMap& mapB, const CUtensorMap& mapC,
+                                          const CUtensorMap& mapC2, const CUtensorMap& mapAux, const Args& args) {
+  constexpr int STG = PAIR ? STAGES_PAIR : STAGES;
+  constexpr uint32_t A_BYTES = BM * BK * 2;                    // 16 KB
+  constexpr uint32_t B_BYTES = (PAIR ? BN / 2 : BN) * BK * 2;  // this CTA's share of B
+  constexpr int TM = PAIR ? 2 * BM : BM;                       // output rows per tile
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* sA = smem;
-  uint8_t* sB = smem + STAGES * A_BYTES;
-  uint8_t* sEpi = sB + STAGES * B_BYTES;  // EPI_SMEM bytes, 1024-aligned
+  uint8_t* sB = smem + STG * A_BYTES;
+  uint8_t* sEpi = sB + STG * B_BYTES;  // EPI_SMEM bytes, 1024-aligned
   uint64_t* full_bar = reinterpret_cast<uint64_t*>(sEpi + EPI_SMEM);
-  uint64_t* empty_bar = full_bar + STAGES;
+  uint64_t* empty_bar = full_bar + STG;
   uint64_t* acc_full = empty_bar + STAGES;  // [2]
   uint64_t* acc_empty = acc_full + 2;       // [2]
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(acc_empty + 2);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const uint32_t rank = PAIR ? cluster_rank() : 0u;        // CTA within the pair
+  const int unit = PAIR ? (int)(blockIdx.x >> 1) : (int)blockIdx.x;  // tile walker
+  const int units = PAIR ? (int)(gridDim.x >> 1) : (int)gridDim.x;
   const int num_kb = (int)((args.K + BK - 1) / BK);
   const int tiles_n = (int)((args.N + BN - 1) / BN);
-  const int tiles_m = (int)((args.M + BM - 1) / BM);
+  const int tiles_m = (int)((args.M + TM - 1) / TM);
   const int tiles_mn = tiles_n * tiles_m;
   const int total = tiles_mn * args.batch;
 
   if (threadIdx.x == 0) {
-    for (int s = 0; s < STAGES; ++s) {
-      mbar_init(&full_bar[s], 1);
-      mbar_init(&empty_bar[s], 1);
+    for (int s = 0; s < STG; ++s) {
+      mbar_init(&full_bar[s], 1);   // the (leader's) producer arrival + the loads' bytes
+      mbar_init(&empty_bar[s], 1);  // one MMA commit
     }
     for (int b = 0; b < 2; ++b) {
       mbar_init(&acc_full[b], 1);
-      mbar_init(&acc_empty[b], EPI_WARPS);  // one arrive per epilogue warp
+      mbar_init(&acc_empty[b], (PAIR ? 2 : 1) * EPI_WARPS);  // one arrive per epilogue warp (of both CTAs)
     }
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
   }
   if (warp == 1) {
-    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tmem_slot)), "r"(2 * BN));
-    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
+    if constexpr (PAIR) {
+      asm volatile("tcgen05.alloc.cta_group::2.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tmem_slot)), "r"(2 * BN));
+      asm volatile("tcgen05.relinquish_alloc_permit.cta_group::2.sync.aligned;");
+    } else {
+      asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tmem_slot)), "r"(2 * BN));
+      asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
+    }
   }
   tc_fence_before();
-  __syncthreads();
+  // both CTAs' barriers are initialised before either CTA's loads or commits can reach them
+  if constexpr (PAIR) cluster_sync_all();
+  else __syncthreads();
   tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
 
@@ -284,54 +343,65 @@ __global__ void __launch_bounds__(THREADS, 1) gemm_tc_kernel(const __grid_consta
       // ---------------- TMA producer ----------------
       uint32_t it = 0;
       bool ok = true;
-      for (int tile = blockIdx.x; tile < total && ok; tile += gridDim.x) {
+      for (int tile = unit; tile < total && ok; tile += units) {
         const int z = tile / tiles_mn, r = tile % tiles_mn;
         const int m_tile = r / tiles_n, n_tile = r % tiles_n;
+        const int m0 = m_tile * TM + (int)rank * BM;                       // this CTA's A rows
+        const int n0 = n_tile * BN + (PAIR ? (int)rank * (BN / 2) : 0);   // this CTA's B columns
         for (int kb = 0; kb < num_kb; ++kb, ++it) {
-          const int s = it % STAGES;
-          const uint32_t round = it / STAGES;
+          const int s = it % STG;
+          const uint32_t round = it / STG;
           if (!mbar_wait(&empty_bar[s], (round & 1) ^ 1)) {
             ok = false;
             break;
           }
-          mbar_expect_tx(&full_bar[s], A_BYTES + B_BYTES);
+          if (rank == 0) mbar_expect_tx(&full_bar[s], (PAIR ? 2u : 1u) * (A_BYTES + B_BYTES));
           const int k0 = kb * BK;
           uint8_t* a_dst = sA + s * A_BYTES;
           uint8_t* b_dst = sB + s * B_BYTES;
           const int zo = z / args.b_in, zi = z % args.b_in;
           const int ai = args.a_bc_in ? 0 : zi, ao = args.a_bc_out ? 0 : zo;
           const int bi = args.b_bc_in ? 0 : zi, bo = args.b_bc_out ? 0 : zo;
+          auto load = [&](void* dst, const CUtensorMap* map, int c0, int c1, int c2, int c3) {
+            if constexpr (PAIR) tma_load_4d_pair(dst, map, &full_bar[s], c0, c1, c2, c3);
+            else tma_load_4d(dst, map, &full_bar[s], c0, c1, c2, c3);
+          };
           if (!args.a_mn) {
-            tma_load_4d(a_dst, &mapA, &full_bar[s], k0, m_tile * BM, ai, ao);
+            load(a_dst, &mapA, k0, m0, ai, ao);
           } else {
-            tma_load_4d(a_dst, &mapA, &full_bar[s], m_tile * BM, k0, ai, ao);
-            tma_load_4d(a_dst + 8192, &mapA, &full_bar[s], m_tile * BM + 64, k0, ai, ao);
+            load(a_dst, &mapA, m0, k0, ai, ao);
+            load(a_dst + 8192, &mapA, m0 + 64, k0, ai, ao);
           }
           if (!args.b_mn) {
-            tma_load_4d(b_dst, &mapB, &full_bar[s], k0, n_tile * BN, bi, bo);
+            load(b_dst, &mapB, k0, n0, bi, bo);
           } else {
 #pragma unroll
-            for (int j = 0; j < BN / 64; ++j) tma_load_4d(b_dst + j * 8192, &mapB, &full_bar[s], n_tile * BN + 64 * j, k0, bi, bo);
+            for (int j = 0; j < (PAIR ? BN / 2 : BN) / 64; ++j) load(b_dst + j * 8192, &mapB, n0 + 64 * j, k0, bi, bo);
           }
         }
       }
+      if constexpr (PAIR) {
+        // producer tail: wait until the MMAs released every stage this CTA filled, so no
+        // commit from the leader can arrive on this CTA's barriers after it has exited
+        for (int i = 0; i < STG && ok; ++i, ++it) ok = mbar_wait(&empty_bar[it % STG], ((it / STG) & 1) ^ 1, 64);
+      }
     }
   } else if (warp == 1) {
-    if (lane == 0) {
-      // ---------------- MMA issuer ----------------
+    if (lane == 0 && rank == 0) {
+      // ---------------- MMA issuer (the leader, for a pair) ----------------
       const uint32_t idesc = (1u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)args.a_mn << 15) | ((uint32_t)args.b_mn << 16) |
-                             ((uint32_t)(BN >> 3) << 17) | ((uint32_t)(BM >> 4) << 24);
+                             ((uint32_t)(BN >> 3) << 17) | ((uint32_t)(TM >> 4) << 24);
       uint32_t it = 0, local = 0;
       bool ok = true;
-      for (int tile = blockIdx.x; tile < total && ok; tile += gridDim.x, ++local) {
+      for (int tile = unit; tile < total && ok; tile += units, ++local) {
         const int b = local & 1;
         const uint32_t use = local >> 1;
         if (!mbar_wait(&acc_empty[b], (use & 1) ^ 1)) break;
         tc_fence_after();
         const uint32_t d_tmem = tmem_base + (uint32_t)(b * BN);
         for (int kb = 0; kb < num_kb; ++kb, ++it) {
-          const int s = it % STAGES;
-          const uint32_t round = it / STAGES;
+          const int s = it % STG;
+          const uint32_t round = it / STG;
           if (!mbar_wait(&full_bar[s], round & 1)) {
             ok = false;
             break;
@@ -345,11 +415,18 @@ __global__ void __launch_bounds__(THREADS, 1) gemm_tc_kernel(const __grid_consta
             // MN-major: +2048 B per K step (two 8-row groups of 1024 B).
             const uint64_t ad = args.a_mn ? smem_desc(a_base + k * 2048, 8192, 1024) : smem_desc(a_base + k * 32, 16, 1024);
             const uint64_t bd = args.b_mn ? smem_desc(b_base + k * 2048, 8192, 1024) : smem_desc(b_base + k * 32, 16, 1024);
-            mma_bf16(d_tmem, ad, bd, idesc, (kb > 0 || k > 0) ? 1u : 0u);
+            if constexpr (PAIR) mma_bf16_pair(d_tmem, ad, bd, idesc, (kb > 0 || k > 0) ? 1u : 0u);
+            else mma_bf16(d_tmem, ad, bd, idesc, (kb > 0 || k > 0) ? 1u : 0u);
           }
-          mma_commit(&empty_bar[s]);  // stage s free once these MMAs have read it
+          // stage s free once these MMAs have read it (in both CTAs of a pair)
+          if constexpr (PAIR) mma_commit_pair(&empty_bar[s]);
+          else mma_commit(&empty_bar[s]);
         }
-        if (ok) mma_commit(&acc_full[b]);  // accumulator b complete (also fires when num_kb == 0)
+        // accumulator b complete (also fires when num_kb == 0)
+        if (ok) {
+          if constexpr (PAIR) mma_commit_pair(&acc_full[b]);
+          else mma_commit(&acc_full[b]);
+        }
       }
     }
   } else {
@@ -362,14 +439,14 @@ __global__ void __launch_bounds__(THREADS, 1) gemm_tc_kernel(const __grid_consta
     const int half = (warp - 2) >> 2;
     constexpr int CH = BN / 32 / NHALF;  // chunks per warp per tile
     uint32_t local = 0;
-    for (int tile = blockIdx.x; tile < total; tile += gridDim.x, ++local) {
+    for (int tile = unit; tile < total; tile += units, ++local) {
       const int z = tile / tiles_mn, r = tile % tiles_mn;
       const int m_tile = r / tiles_n, n_tile = r % tiles_n;
       const int b = local & 1;
       const uint32_t use = local >> 1;
       if (!mbar_wait(&acc_full[b], use & 1)) break;
       tc_fence_after();
-      const int64_t row = (int64_t)m_tile * BM + q * 32 + lane;
+      const int64_t row = (int64_t)m_tile * TM + (int64_t)rank * BM + q * 32 + lane;
       const int64_t col0 = (int64_t)n_tile * BN + half * (BN / NHALF);
       const int zo = z / args.b_in, zi = z % args.b_in;
       const uint32_t tbase = tmem_base + ((uint32_t)(q * 32) << 16) + (uint32_t)(b * BN + half * (BN / NHALF));
@@ -418,7 +495,7 @@ __global__ void __launch_bounds__(THREADS, 1) gemm_tc_kernel(const __grid_consta
         }
         const int64_t zoff = (int64_t)zo * args.sC + (int64_t)zi * args.sC_in;
         if (args.store_mode != 0) {
-          const int row0 = (int)(m_tile * BM + q * 32);
+          const int row0 = (int)(m_tile * TM + (int)rank * BM + q * 32);
           if (row0 >= args.M) continue;  // warp-uniform: none of this warp's rows exist
           const int rows_in = (int)min((int64_t)32, args.M - row0);
           const int64_t cols_in = min((int64_t)32, args.N - cbase);
@@ -518,16 +595,42 @@ __global__ void __launch_bounds__(THREADS, 1) gemm_tc_kernel(const __grid_consta
       // accumulator b may be overwritten once every epilogue warp has read it
       tc_fence_before();
       __syncwarp();
-      if (lane == 0) mbar_arrive(&acc_empty[b]);
+      if (lane == 0) {
+        if constexpr (PAIR) mbar_arrive_leader(&acc_empty[b]);
+        else mbar_arrive(&acc_empty[b]);
+      }
     }
   }
   if (args.store_mode == 2 && warp >= 2 && lane == 0) bulk_wait0();  // this warp's bulk stores are complete
   tc_fence_before();
-  __syncthreads();
+  // a pair's TMEM is written by the leader's MMAs and read by both epilogues: free it only
+  // after both CTAs are done
+  if constexpr (PAIR) cluster_sync_all();
+  else __syncthreads();
   if (warp == 1) {
     tc_fence_after();
-    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem_base), "r"(2 * BN));
+    if constexpr (PAIR) asm volatile("tcgen05.dealloc.cta_group::2.sync.aligned.b32 %0, %1;" ::"r"(tmem_base), "r"(2 * BN));
+    else asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem_base), "r"(2 * BN));
   }
+}
+
+template <int BN, int EPI>
+__global__ void __launch_bounds__(THREADS, 1) gemm_tc_kernel(const __grid_constant__ CUtensorMap mapA,
+                                                             const __grid_constant__ CUtensorMap mapB,
+                                                             const __grid_constant__ CUtensorMap mapC,
+                                                             const __grid_constant__ CUtensorMap mapC2,
+                                                             const __grid_constant__ CUtensorMap mapAux,
+                                                             const __grid_constant__ Args args) {
+  gemm_body<BN, EPI, false>(mapA, mapB, mapC, mapC2, mapAux, args);
+}
+
+// the CTA-pair kernel: clusters of two CTAs along x (CTAs 2p and 2p + 1 form pair p)
+template <int BN, int EPI>
+__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(THREADS, 1)
+    gemm_tc2_kernel(const __grid_constant__ CUtensorMap mapA, const __grid_constant__ CUtensorMap mapB,
+                    const __grid_constant__ CUtensorMap mapC, const __grid_constant__ CUtensorMap mapC2,
+                    const __grid_constant__ CUtensorMap mapAux, const __grid_constant__ Args args) {
+  gemm_body<BN, EPI, true>(mapA, mapB, mapC, mapC2, mapAux, args);
 }
 
 // ---------------------------------------------------------------------------------
@@ -592,21 +695,67 @@ static bool make_store_map(CUtensorMap* map, void* base, CUtensorMapDataType dt,
              CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
-template <int BN, int EPI>
+template <int BN, int EPI, bool PAIR>
 static int launch(const CUtensorMap& ma, const CUtensorMap& mb, const CUtensorMap& mc, const CUtensorMap& mc2,
                   const CUtensorMap& maux, const Args& a, int64_t batch, cudaStream_t s) {
-  const size_t smem = (size_t)STAGES * (BM * BK * 2 + BN * BK * 2) + EPI_SMEM + 1024 + 256;
-  const int64_t tiles = ceil_div(a.N, BN) * ceil_div(a.M, BM) * batch;  // batch = b_out * b_in
+  constexpr int STG = PAIR ? STAGES_PAIR : STAGES;
+  constexpr int BNC = PAIR ? BN / 2 : BN;  // B columns one CTA loads
+  const size_t smem = (size_t)STG * (BM * BK * 2 + BNC * BK * 2) + EPI_SMEM + 1024 + 256;
+  const int64_t tiles = ceil_div(a.N, BN) * ceil_div(a.M, PAIR ? 2 * BM : BM) * batch;  // batch = b_out * b_in
   static bool attr_set[64] = {false};
   int dev = 0;
   cudaGetDevice(&dev);
   if (dev < 0 || dev >= 64 || !attr_set[dev]) {
-    cudaFuncSetAttribute(gemm_tc_kernel<BN, EPI>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    if constexpr (PAIR) cudaFuncSetAttribute(gemm_tc2_kernel<BN, EPI>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    else cudaFuncSetAttribute(gemm_tc_kernel<BN, EPI>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
     if (dev >= 0 && dev < 64) attr_set[dev] = true;
   }
-  const unsigned grid = (unsigned)std::max<int64_t>(1, std::min<int64_t>(tiles, num_sms()));
-  gemm_tc_kernel<BN, EPI><<<grid, THREADS, smem, s>>>(ma, mb, mc, mc2, maux, a);
-  return check_launch("gemm(bf16 tcgen05)");
+  if constexpr (PAIR) {
+    // as many CTA pairs as can be resident at once (at most one per two SMs; a pair needs
+    // two SMs of one GPC), each walking its share of the tiles
+    static int max_pairs[64] = {0};
+    int cap = num_sms() / 2;
+    if (dev >= 0 && dev < 64) {
+      if (!max_pairs[dev]) {
+        cudaLaunchConfig_t cfg = {};
+        cfg.gridDim = dim3((unsigned)(2 * cap), 1, 1);
+        cfg.blockDim = dim3(THREADS, 1, 1);
+        cfg.dynamicSmemBytes = smem;
+        cudaLaunchAttribute attr;
+        attr.id = cudaLaunchAttributeClusterDimension;
+        attr.val.clusterDim.x = 2;
+        attr.val.clusterDim.y = 1;
+        attr.val.clusterDim.z = 1;
+        cfg.attrs = &attr;
+        cfg.numAttrs = 1;
+        int n = 0;
+        if (cudaOccupancyMaxActiveClusters(&n, gemm_tc2_kernel<BN, EPI>, &cfg) != cudaSuccess || n <= 0) {
+          cudaGetLastError();  // clear: fall back to one pair per two SMs
+          n = cap;
+        }
+        max_pairs[dev] = std::min(n, cap);
+      }
+      cap = max_pairs[dev];
+    }
+    const int64_t pairs = std::max<int64_t>(1, std::min<int64_t>(tiles, cap));
+    gemm_tc2_kernel<BN, EPI><<<(unsigned)(2 * pairs), THREADS, smem, s>>>(ma, mb, mc, mc2, maux, a);
+    return check_launch("gemm(bf16 tcgen05, CTA pairs)");
+  } else {
+    const unsigned grid = (unsigned)std::max<int64_t>(1, std::min<int64_t>(tiles, num_sms()));
+    gemm_tc_kernel<BN, EPI><<<grid, THREADS, smem, s>>>(ma, mb, mc, mc2, maux, a);
+    return check_launch("gemm(bf16 tcgen05)");
+  }
+}
+
+// CTA pairs for large GEMMs: 256 x 256 tiles, both M and N at least one full pair tile.
+// B200_GEMM_PAIR=0 in the environment selects the single-CTA kernel everywhere.
+static bool use_pairs(int64_t M, int64_t N) {
+  static int env = -1;
+  if (env < 0) {
+    const char* e = getenv("B200_GEMM_PAIR");
+    env = (e && e[0] == '0') ? 0 : 1;
+  }
+  return env == 1 && N > 128 && M >= 256;
 }
 
 }  // namespace tc
@@ -657,7 +806,9 @@ int gemm_bf16_tcgen05_b2(int c_dt, const void* A, const void* B, void* C, int64_
   if (!a_mn) rc = make_map(&ma, A, K, M, aIn, aOut, lda * 2, sAi, sAo, 64, 128);
   else rc = make_map(&ma, A, M, K, aIn, aOut, lda * 2, sAi, sAo, 64, 64);
   if (rc) return rc;
-  if (!b_mn) rc = make_map(&mb, B, K, N, bIn, bOut, ldb * 2, sBi, sBo, 64, BN);
+  const bool pair = BN == 256 && use_pairs(M, N);
+  // K-major B: a CTA of a pair loads BN / 2 of the tile's columns
+  if (!b_mn) rc = make_map(&mb, B, K, N, bIn, bOut, ldb * 2, sBi, sBo, 64, pair ? BN / 2 : BN);
   else rc = make_map(&mb, B, N, K, bIn, bOut, ldb * 2, sBi, sBo, 64, 64);
   if (rc) return rc;
   Args a;
@@ -696,9 +847,10 @@ int gemm_bf16_tcgen05_b2(int c_dt, const void* A, const void* B, void* C, int64_
     if (ok && aux) ok = make_store_map(&maux, aux, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, N, M, b_in, b_out, ldc, sC_in, sC_out);
     if (ok) a.store_mode = 2;
   }
-#define B200_GEMM_LAUNCH(E)                                               \
-  return BN == 256 ? launch<256, E>(ma, mb, mc, mc2, maux, a, batch, s) \
-                   : launch<128, E>(ma, mb, mc, mc2, maux, a, batch, s)
+#define B200_GEMM_LAUNCH(E)                                                          \
+  return pair ? launch<256, E, true>(ma, mb, mc, mc2, maux, a, batch, s)           \
+              : (BN == 256 ? launch<256, E, false>(ma, mb, mc, mc2, maux, a, batch, s) \
+                           : launch<128, E, false>(ma, mb, mc, mc2, maux, a, batch, s))
   if (epi == B200_EPI_RELU) B200_GEMM_LAUNCH(B200_EPI_RELU);
   if (epi == B200_EPI_GELU) B200_GEMM_LAUNCH(B200_EPI_GELU);
   B200_GEMM_LAUNCH(B200_EPI_NONE);

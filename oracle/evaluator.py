@@ -640,18 +640,42 @@ def execute_op(op: str, *args, contraction_rounding: str | None = None, **kwargs
 
 
 def evaluate(graph: dict, inputs: dict[str, np.ndarray], contraction_rounding: str | None = None,
-             blas_layout: bool = False) -> dict[str, Any]:
+             blas_layout: bool = False, decisions: dict | None = None, decision_report: list | None = None) -> dict[str, Any]:
     """``evaluate_graph`` (evaluator.py:272-305): every node, in dependency order.
-    ``blas_layout=True`` passes dense operands to np.matmul (see ``_BLAS_LAYOUT``)."""
+    ``blas_layout=True`` passes dense operands to np.matmul (see ``_BLAS_LAYOUT``).
+
+    ``decisions`` (node id -> boolean array) replays another implementation's values for
+    ``Greater`` nodes, the ReLU VJP's masks: a pre-activation within rounding of zero may be
+    classified either way by two correct fp32 evaluations, and each such flip moves a
+    whole row of a weight gradient by one discrete term. Every replayed mask is checked
+    against this evaluation's own first: ``decision_report`` receives, per node, the
+    number of elements where the two differ and the largest |x| / rms(x) among them (the
+    comparison operand's magnitude there), so a caller can require that they differ only
+    at the decision boundary."""
     global _BLAS_LAYOUT
     prev, _BLAS_LAYOUT = _BLAS_LAYOUT, bool(blas_layout)
     try:
-        return _evaluate(graph, inputs, contraction_rounding)
+        return _evaluate(graph, inputs, contraction_rounding, decisions, decision_report)
     finally:
         _BLAS_LAYOUT = prev
 
 
-def _evaluate(graph: dict, inputs: dict[str, np.ndarray], contraction_rounding: str | None) -> dict[str, Any]:
+def _replay_decision(nid, own, given, x, report) -> np.ndarray:
+    given = np.asarray(given).astype(bool).reshape(np.shape(own))
+    diff = given != np.asarray(own)
+    n = int(diff.sum())
+    worst = 0.0
+    if n:
+        xa = np.abs(np.broadcast_to(np.asarray(x, dtype=np.float64), np.shape(own)))
+        scale = float(np.sqrt(np.mean(xa * xa))) or 1.0
+        worst = float(xa[diff].max() / scale)
+    if report is not None:
+        report.append((nid, n, worst))
+    return given
+
+
+def _evaluate(graph: dict, inputs: dict[str, np.ndarray], contraction_rounding: str | None, decisions: dict | None = None,
+              decision_report: list | None = None) -> dict[str, Any]:
     env: dict[str, Any] = dict(inputs)
     for node in topo_order(graph):
         op, nid = node["op_type"], node["id"]
@@ -675,6 +699,8 @@ def _evaluate(graph: dict, inputs: dict[str, np.ndarray], contraction_rounding: 
         else:
             target = _ALIASES.get(op, op)
             env[nid] = _dispatch(node, target, vals, contraction_rounding)
+            if decisions is not None and nid in decisions and target == "Greater":
+                env[nid] = _replay_decision(nid, env[nid], decisions[nid], vals[0], decision_report)
     out = {}
     for oid in graph["outputs"]:
         if oid not in env:
@@ -744,8 +770,9 @@ def _dispatch(node, target, vals, contraction_rounding):
 
 
 def evaluate_roles(graph: dict, role_inputs: dict[str, np.ndarray], contraction_rounding: str | None = None,
-                   blas_layout: bool = False) -> dict[str, Any]:
+                   blas_layout: bool = False, decisions: dict | None = None, decision_report: list | None = None) -> dict[str, Any]:
     """Evaluate with inputs keyed by workload role; outputs keyed by output name."""
     inputs = {nid: role_inputs[r] for r, nid in graph["roles"].items()}
-    res = evaluate(graph, inputs, contraction_rounding=contraction_rounding, blas_layout=blas_layout)
+    res = evaluate(graph, inputs, contraction_rounding=contraction_rounding, blas_layout=blas_layout, decisions=decisions,
+                   decision_report=decision_report)
     return {name: res[nid] for name, nid in graph["output_names"].items()}

@@ -134,14 +134,18 @@ def test_reference_pullback_graph_through_execute_and_compile(cuda, case):
     res2 = B200Backend.execute_graph(_standin_graph(doc["graph"]), inputs)
     assert len(B200Backend._runners) == n_runners
     for k in outs:
-        assert torch.equal(res2[k], res[k]), k
+        if isinstance(res[k], torch.Tensor):
+            assert torch.equal(res2[k], res[k]), k
+        else:
+            assert res2[k] == res[k], k
     # compile_graph: fresh outputs per call (a result held from call 1 is not overwritten)
     fn = B200Backend.compile_graph(lg)
     first = fn(inputs)
-    kept = {k: v.clone() for k, v in first.items()}
+    kept = {k: (v.clone() if isinstance(v, torch.Tensor) else v) for k, v in first.items()}
     scaled = {k: (v * 2 if v.is_floating_point() and k == sorted(inputs)[0] else v) for k, v in inputs.items()}
     fn(scaled)
     second = fn(inputs)
     for k, r in outs.items():
         _check(f"{case}:compile_graph:{k}", second[k], r)
-        assert torch.equal(first[k], kept[k]), f"{k}: a later call overwrote an earlier call's output"
+        if isinstance(first[k], torch.Tensor):
+            assert torch.equal(first[k], kept[k]), f"{k}: a later call overwrote an earlier call's output"

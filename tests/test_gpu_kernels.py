@@ -189,6 +189,29 @@ def test_gemm_bf16_tcgen05_layouts(ta, tb, shape):
     np.testing.assert_allclose(got, ref, rtol=1e-4, atol=1e-3 * np.sqrt(K))
 
 
+@pytest.mark.parametrize("Z,M,N,K,ta,tb", [(2, 2048, 2048, 2048, False, False), (1, 1000, 1000, 320, True, False),
+                                            (3, 512, 768, 64, False, True), (1, 4088, 1024, 1024, False, False)])
+def test_gemm_bf16_cta_pairs_many_tiles(Z, M, N, K, ta, tb):
+    """The CTA-pair kernel (256 x 256 tiles, M >= 256, N > 128) over many tiles per pair, a
+    long K (the stage ring and both accumulators wrap many times), a single K block (direct
+    stores), ragged M and N, and transposed operands; sampled rows against float64."""
+    from b200 import ops
+
+    r = rng(M + N + K + Z)
+    a = _bf16(r.standard_normal((Z, K, M) if ta else (Z, M, K), dtype=np.float32) * 0.05)
+    b = _bf16(r.standard_normal((Z, N, K) if tb else (Z, K, N), dtype=np.float32) * 0.05)
+    A, B = T(a).to(torch.bfloat16), T(b).to(torch.bfloat16)
+    A = A.transpose(-1, -2) if ta else A
+    B = B.transpose(-1, -2) if tb else B
+    an = np.swapaxes(a, -1, -2) if ta else a
+    bn = np.swapaxes(b, -1, -2) if tb else b
+    got = to_np(ops.gemm(A, B, ab_dtype=torch.bfloat16))
+    rows = np.unique(np.concatenate([r.choice(M, 24, replace=False), [0, 127, 128, 255, 256, M - 1]]))
+    for z in range(Z):
+        ref = an[z, rows].astype(np.float64) @ bn[z].astype(np.float64)
+        np.testing.assert_allclose(got[z, rows], ref, rtol=1e-4, atol=1e-4 * np.sqrt(K))
+
+
 def test_gemm_bf16_batched_bias_relu_mask_bf16_out():
     from b200 import _lib as L
     from b200 import ops

@@ -1,6 +1,11 @@
 """Whole-graph parity: every golden case (fwd+bwd graph traced and differentiated by the
 reference, evaluated by the reference numpy backend) run on the b200 backend.
 
+ReLU decisions: a pre-activation within rounding of zero may be classified either way by
+two correct evaluations, and each flip moves a whole weight-gradient row by a discrete
+term. For the bf16 comparison the backend's own masks are replayed into the oracle, which
+checks that they differ from its own only where |pre-activation| <= 1e-2 x its RMS.
+
 Tolerances (written per workload; elementwise, ``gpu_helpers.assert_close``):
 * fp32 workloads (mlp, rowfused, the node-type cases): rtol 1e-4 per element, absolute
   floor 1e-4 x the output's RMS, against the reference golden vectors; integer outputs
@@ -17,8 +22,9 @@ Tolerances (written per workload; elementwise, ``gpu_helpers.assert_close``):
 
 import numpy as np
 import pytest
+import torch
 
-from gpu_helpers import assert_close, run_case, to_np
+from gpu_helpers import assert_close, check_decisions, gpu_decisions, run_case, to_np
 
 CASES = ["mlp_small", "mlp_ragged", "rowfused_small", "rowfused_ragged", "bmm_small", "cnn_small", "transformer_small",
          # node types outside the workloads: the reference's fusion-pass outputs (golden = the
@@ -58,7 +64,13 @@ def test_graph_parity(cuda, case, mode):
         from oracle import evaluator as O
 
         ins, _ = load_golden(case)
-        emu = O.evaluate_roles(O.load_graph(case), ins, contraction_rounding="bf16")
+        # the backend's ReLU decisions replayed into the oracle (checked to differ from the
+        # oracle's own only at |pre-activation| ~ 0); every other value is the oracle's own
+        dev_in = {nid: torch.from_numpy(np.ascontiguousarray(ins[r])).cuda() for r, nid in g.roles.items()}
+        rep: list = []
+        emu = O.evaluate_roles(O.load_graph(case), ins, contraction_rounding="bf16", decisions=gpu_decisions(g, dev_in),
+                               decision_report=rep)
+        check_decisions(rep)
         # outputs that are zero in exact arithmetic (e.g. the key-bias gradient of softmax
         # attention) are compared against an absolute floor: 1e-3 of the largest output
         floor = 1e-3 * max(float(np.abs(np.asarray(v)).max()) for v in emu.values() if np.asarray(v).size)
