@@ -368,8 +368,14 @@ def measure(name: str, args, world: int, rank: int, dist, dev, headline: bool) -
         static_in = cg.static_in  # resident in the graph's static buffers from here on
         plan = cg.runner.plan_for(cg.static_in)
     n0 = _lib.launch_count()
+    if args.profile and headline:
+        # the profiler range (ncu --profile-from-start off) covers exactly this one eager step
+        torch.cuda.synchronize()
+        torch.cuda.profiler.start()
     plan.run(dict(static_in))  # one eager run of the plan: count its kernels
     torch.cuda.synchronize()
+    if args.profile and headline:
+        torch.cuda.profiler.stop()
     launches_per_step = int(_lib.launch_count() - n0)
 
     sync_launches = 0
@@ -753,6 +759,8 @@ def main() -> None:
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline leg")
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-overlap", action="store_true", help="all-reduce after the step instead of during the backward")
+    ap.add_argument("--profile", action="store_true",
+                    help="bracket one eager step of the headline plan with cudaProfilerStart/Stop (ncu --profile-from-start off)")
     # dram__bytes_read.sum + dram__bytes_write.sum of one rowfused2_kernel launch at
     # [8192, 4096] (ncu capture summarised in profiles/rowfused_kernel_8192x4096.md)
     ap.add_argument("--traffic", type=float, default=488077312.0, help="ncu dram bytes per launch of the row kernel")

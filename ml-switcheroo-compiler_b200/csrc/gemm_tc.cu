@@ -297,7 +297,7 @@ __device__ __forceinline__ void gemm_body(const CUtensorMap& mapA, const CUtenso
   uint8_t* sEpi = sB + STG * B_BYTES;  // EPI_SMEM bytes, 1024-aligned
   uint64_t* full_bar = reinterpret_cast<uint64_t*>(sEpi + EPI_SMEM);
   uint64_t* empty_bar = full_bar + STG;
-  uint64_t* acc_full = empty_bar + STAGES;  // [2]
+  uint64_t* acc_full = empty_bar + STG;  // [2]
   uint64_t* acc_empty = acc_full + 2;       // [2]
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(acc_empty + 2);
 
