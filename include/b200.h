@@ -300,6 +300,28 @@ int b200_rowfused_fwd_bwd_noalloc(const float* x, const float* a, const float* b
 int b200_gather_axis(int elem_bytes, const void* x, const int64_t* x_strides, const int64_t* idx, const int64_t* idx_strides,
                      void* y, const int64_t* shape, int ndim, int axis, int64_t axis_len, void* stream);
 
+/* Attention score rows with the softmax (or its VJP) in the GEMM epilogue, for rows of
+ * N <= 512 columns and K <= 128 (the scores Q.K^T and dO.V^T of multi-head attention):
+ *   b200_gemm_softmax_rows:     y  = softmax(scale * A.B) over the last axis
+ *   b200_gemm_softmax_bwd_rows: dx = scale * y * (G - rowsum(G * y)),  G = A.B
+ * replacing the Matmul (eager/core_math_ops/math_matrix.py:21-64), the Multiply by the
+ * scale and the Softmax (numpy/eager/math_advanced/math_signal.py:450-467), or the Softmax
+ * VJP chain the AD pass emits (numpy/eager/math_binary.py:9-51,
+ * eager/core_math_ops/math_reduction.py:37), without writing G or the scores to HBM.
+ * bf16 operands, both K-major (csA = 1, rsB = 1), two batch levels as b200_gemm_batched2;
+ * scale a device fp32 scalar (NULL: 1). Outputs y / dx fp32 and / or bf16 (either may be
+ * NULL, not both), [b_out, b_in, M, N] with element strides (s_out, s_in, ld); the backward
+ * reads y (fp32 or bf16 per y_dtype) with the same strides. B200_ERR_UNSUPPORTED for other
+ * layouts or sizes. */
+int b200_gemm_softmax_rows(const void* A, const void* B, int64_t b_out, int64_t b_in, int64_t M, int64_t N, int64_t K,
+                           int64_t sA_out, int64_t sA_in, int64_t rsA, int64_t csA, int64_t sB_out, int64_t sB_in, int64_t rsB,
+                           int64_t csB, const float* scale, float* y, void* y_bf16, int64_t sY_out, int64_t sY_in, int64_t ldy,
+                           void* stream);
+int b200_gemm_softmax_bwd_rows(const void* A, const void* B, int64_t b_out, int64_t b_in, int64_t M, int64_t N, int64_t K,
+                               int64_t sA_out, int64_t sA_in, int64_t rsA, int64_t csA, int64_t sB_out, int64_t sB_in, int64_t rsB,
+                               int64_t csB, const float* scale, int y_dtype, const void* y, float* dx, void* dx_bf16,
+                               int64_t s_out, int64_t s_in, int64_t ld, void* stream);
+
 /* Element copy between two strided views of one index space `shape` (ndim <=
  * B200_GATHER_MAX_DIM; element strides, src strides may be 0 to broadcast): the value
  * write of the interpreter's IndexPut / SetItem node (interpreter/evaluator.py:488-508,

@@ -91,6 +91,8 @@ SIGNATURES = {
     "b200_gather_axis": ([_I32, _P, C.POINTER(_I64), _P, C.POINTER(_I64), _P, C.POINTER(_I64), _I32, _I32, _I64, _P], C.c_int),
     "b200_copy_strided": ([_I32, _P, C.POINTER(_I64), _P, C.POINTER(_I64), C.POINTER(_I64), _I32, _P], C.c_int),
     "b200_one_hot": ([_P, _P, _I32, _I64, _I64, _I64, C.c_double, C.c_double, _P], C.c_int),
+    "b200_gemm_softmax_rows": ([_P, _P] + [_I64] * 13 + [_P, _P, _P, _I64, _I64, _I64, _P], C.c_int),
+    "b200_gemm_softmax_bwd_rows": ([_P, _P] + [_I64] * 13 + [_P, _I32, _P, _P, _P, _I64, _I64, _I64, _P], C.c_int),
     "b200_scatter_add_rows": ([_P, _P, _P, _I64, _I64, _I64, _I32, _P, C.c_size_t, _P], C.c_int),
     "b200_scatter_add_rows_workspace_bytes": ([_I64, _I64], C.c_size_t),
     "b200_gemm": (

@@ -959,6 +959,98 @@ def softmax_bwd_step(m: Match, meta: dict[str, Meta]) -> Step:
 
 
 # ----------------------------------------------------------------------------------
+# patterns: attention score rows. A Matmul whose only consumer is a (scaled) Softmax, or
+# the softmax VJP, runs as one tcgen05 kernel with the row reduction in its epilogue, so
+# the fp32 scores (or their gradient) never go to HBM.
+# ----------------------------------------------------------------------------------
+ATTN_MAX_N, ATTN_MAX_K = 512, 128
+
+
+def _attn_matmul(g: Graph, live: dict[str, Node], meta: dict[str, Meta], users: dict[str, list[str]], outputs: set[str],
+                 vid: str, allowed: set[str]) -> Node | None:
+    """The Matmul producing ``vid`` when it qualifies: bf16 GEMM policy, rows of at most
+    512 columns, K <= 128, and every consumer of ``vid`` inside ``allowed``."""
+    mm = live.get(vid)
+    if mm is None or _op_name(mm) not in ("Matmul", "BatchMatMul") or len(mm.inputs) != 2 or vid in outputs:
+        return None
+    if ops.Config.matmul_dtype != "bf16" or any(u not in allowed for u in users.get(vid, [])):
+        return None
+    mo, ma = meta.get(vid), meta.get(mm.inputs[0])
+    if mo is None or ma is None or mo.scalar or ma.scalar or len(mo.shape) < 2 or len(ma.shape) < 2:
+        return None
+    kw = node_kwargs(mm, "Matmul")
+    K = ma.shape[-2] if kw.get("transpose_a") else ma.shape[-1]
+    if mo.shape[-1] > ATTN_MAX_N or K > ATTN_MAX_K:
+        return None
+    return mm
+
+
+def _mm_operands(mm: Node, env: dict) -> tuple[torch.Tensor, torch.Tensor]:
+    kw = node_kwargs(mm, "Matmul")
+    a, b = env[mm.inputs[0]], env[mm.inputs[1]]
+    if kw.get("transpose_a"):
+        a = a.transpose(-1, -2)
+    if kw.get("transpose_b"):
+        b = b.transpose(-1, -2)
+    return a, b
+
+
+def find_attn_softmax(g: Graph, live: dict[str, Node], meta: dict[str, Meta], users: dict[str, list[str]],
+                      outputs: set[str]) -> list[Match]:
+    found = []
+    for m in find_softmax(g, live, meta, users, outputs):
+        if m.bind["log"] == "True":
+            continue
+        mm = _attn_matmul(g, live, meta, users, outputs, m.bind["x"], set(m.covered))
+        if mm is None:
+            continue
+        bind = dict(m.bind)
+        bind["mm"] = mm.id
+        found.append(Match("attn_softmax", bind, set(m.covered) | {mm.id}, {"y": bind["y"]}))
+    return found
+
+
+def attn_softmax_step(m: Match) -> Step:
+    b = m.bind
+    mm_id = b["mm"]
+    f32, bf = b["f32"] == "True", b["bf16"] == "True"
+    ins = list(dict.fromkeys(m.extra_inputs + ([b["scale"]] if b["scale"] else [])))
+
+    def run(env: dict) -> None:
+        a, bb = _mm_operands(m.mm_node, env)
+        y, yb = ops.gemm_softmax_rows(a, bb, env[b["scale"]] if b["scale"] else None, f32, bf)
+        _publish(env, b["y"], y, yb)
+
+    return Step([b["y"]], ins, run, ("scaled_" if b["scale"] else "") + "scores_softmax" + ("[bf16]" if bf and not f32 else ""))
+
+
+def find_attn_softmax_bwd(g: Graph, live: dict[str, Node], meta: dict[str, Meta], users: dict[str, list[str]],
+                          outputs: set[str]) -> list[Match]:
+    found = []
+    for m in find_softmax_bwd(g, live, meta, users, outputs):
+        mm = _attn_matmul(g, live, meta, users, outputs, m.bind["g"], set(m.covered))
+        if mm is None:
+            continue
+        bind = dict(m.bind)
+        bind["mm"] = mm.id
+        found.append(Match("attn_softmax_bwd", bind, set(m.covered) | {mm.id}, {"dx": bind["outv"]}))
+    return found
+
+
+def attn_softmax_bwd_step(m: Match) -> Step:
+    b = m.bind
+    f32, bf = b["f32"] == "True", b["bf16"] == "True"
+    ins = list(dict.fromkeys(m.extra_inputs + [b["y"]] + ([b["scale"]] if b["scale"] else [])))
+
+    def run(env: dict) -> None:
+        a, bb = _mm_operands(m.mm_node, env)
+        dx, dxb = ops.gemm_softmax_bwd_rows(a, bb, env[b["y"]], env[b["scale"]] if b["scale"] else None, f32, bf)
+        _publish(env, b["outv"], dx, dxb)
+
+    return Step([b["outv"]], ins, run, "scores_softmax_bwd" + ("_scaled" if b["scale"] else "") + ("[bf16]" if bf and not f32 else ""))
+
+
+# ----------------------------------------------------------------------------------
 # elementwise clustering (subsystem 1)
 # ----------------------------------------------------------------------------------
 EW_UNARY = {"Negative": "NEG", "Exp": "EXP", "Log": "LOG", "Tanh": "TANH", "Sqrt": "SQRT", "Relu": "RELU", "Gelu": "GELU",
@@ -1228,6 +1320,16 @@ def plan_steps(graph: Graph, nodes: list[Node], sample: dict[str, Any]) -> list[
         eps = float(graph.nodes[m.bind["n"]].attributes.get("eps", graph.nodes[m.bind["n"]].attributes.get("epsilon", 1e-5)))
         groups.append((sorted(m.covered), rowfused_step(m, meta, eps)))
         taken |= m.covered
+
+    # attention score rows: GEMM + (scaled) softmax, GEMM + softmax VJP
+    for finder, stepper in ((find_attn_softmax, attn_softmax_step), (find_attn_softmax_bwd, attn_softmax_bwd_step)):
+        for m in finder(graph, live, meta, users, outputs):
+            if m.covered & taken:
+                continue
+            m.mm_node = graph.nodes[m.bind["mm"]]
+            m.extra_inputs = list(m.mm_node.inputs)
+            groups.append((sorted(m.covered), stepper(m)))
+            taken |= m.covered
 
     for m in find_gemm_epilogue(graph, live, meta, users, outputs):
         if m.covered & taken:

@@ -902,6 +902,86 @@ def gemm(a: torch.Tensor, b: torch.Tensor, *, bias: torch.Tensor | None = None, 
     return (C_, mask) if want_mask else C_
 
 
+def _batch2(A: torch.Tensor, B: torch.Tensor, C: torch.Tensor, batch_shape: tuple) -> list | None:
+    """The batch dims of A, B (broadcast) and C coalesced into at most two levels:
+    [(b_out, sA_out, sB_out, sC_out), (b_in, sA_in, sB_in, sC_in)], or None."""
+    nb = len(batch_shape)
+    M, K = A.shape[-2], A.shape[-1]
+    N = B.shape[-1]
+    sa = list(A.expand(*batch_shape, M, K).stride()[:nb]) if A.dim() > 2 else [0] * nb
+    sb = list(B.expand(*batch_shape, K, N).stride()[:nb]) if B.dim() > 2 else [0] * nb
+    sc = list(C.stride()[:nb])
+    dims = [(sz, x, y, z) for sz, x, y, z in zip(batch_shape, sa, sb, sc) if sz != 1]
+    merged: list[list[int]] = []
+    for sz, x, y, z in dims:
+        if merged and merged[-1][1] == x * sz and merged[-1][2] == y * sz and merged[-1][3] == z * sz:
+            merged[-1] = [merged[-1][0] * sz, x, y, z]
+        else:
+            merged.append([sz, x, y, z])
+    if len(merged) > 2:
+        return None
+    while len(merged) < 2:
+        merged.insert(0, [1, 0, 0, 0])
+    return merged
+
+
+def gemm_softmax_rows(a: torch.Tensor, b: torch.Tensor, scale: torch.Tensor | None, f32: bool, bf16: bool):
+    """softmax(scale * a.b) over the last axis, with the scores kept on chip (one tcgen05
+    kernel: the GEMM's 128 x N accumulator in TMEM, the row softmax in its epilogue).
+    Returns (y fp32 or None, y bf16 or None). Falls back to the GEMM + the row-softmax
+    kernel when the operands' layout or sizes are outside the fused kernel."""
+    A, B = _gemm_operand(a, torch.bfloat16), _gemm_operand(b, torch.bfloat16)
+    M, K, N = a.shape[-2], a.shape[-1], b.shape[-1]
+    batch_shape = _bshape([a.shape[:-2], b.shape[:-2]])
+    shape = (*batch_shape, M, N)
+    y = torch.empty(shape, dtype=torch.float32, device=device()) if f32 else None
+    yb = torch.empty(shape, dtype=torch.bfloat16, device=device()) if bf16 else None
+    sc = contiguous(cast(scale, torch.float32)) if scale is not None else None
+    ref = y if y is not None else yb
+    lv = _batch2(A, B, ref, batch_shape) if (A is not None and B is not None) else None
+    if lv is not None and N <= 512 and K <= 128:
+        (bo, sao, sbo, sco), (bi, sai, sbi, sci) = lv
+        try:
+            L.call("b200_gemm_softmax_rows", A.data_ptr(), B.data_ptr(), bo, bi, M, N, K, sao, sai, A.stride(-2), A.stride(-1),
+                   sbo, sbi, B.stride(-2), B.stride(-1), _ptr(sc), _ptr(y), _ptr(yb), sco, sci, N, stream_ptr())
+            return y, yb
+        except UnimplementedMathError:
+            pass
+    x = gemm(a, b, ab_dtype=torch.bfloat16)
+    xc = contiguous(x)
+    L.call("b200_softmax_rows", xc.data_ptr(), _ptr(sc), _ptr(y), _ptr(yb), xc.numel() // N, N, 0, stream_ptr())
+    return y, yb
+
+
+def gemm_softmax_bwd_rows(a: torch.Tensor, b: torch.Tensor, y: torch.Tensor, scale: torch.Tensor | None, f32: bool, bf16: bool):
+    """scale * y * (G - rowsum(G * y)) with G = a.b kept on chip (the softmax VJP in the
+    epilogue of the tcgen05 GEMM that makes G). Returns (dx fp32 or None, dx bf16 or None);
+    falls back to the GEMM + the softmax-VJP kernel outside the fused kernel's range."""
+    A, B = _gemm_operand(a, torch.bfloat16), _gemm_operand(b, torch.bfloat16)
+    M, K, N = a.shape[-2], a.shape[-1], b.shape[-1]
+    batch_shape = _bshape([a.shape[:-2], b.shape[:-2]])
+    shape = (*batch_shape, M, N)
+    dx = torch.empty(shape, dtype=torch.float32, device=device()) if f32 else None
+    dxb = torch.empty(shape, dtype=torch.bfloat16, device=device()) if bf16 else None
+    sc = contiguous(cast(scale, torch.float32)) if scale is not None else None
+    yc = contiguous(y) if y.dtype in (torch.float32, torch.bfloat16) else contiguous(cast(y, torch.float32))
+    ref = dx if dx is not None else dxb
+    lv = _batch2(A, B, ref, batch_shape) if (A is not None and B is not None) else None
+    if lv is not None and N <= 512 and K <= 128 and tuple(yc.shape) == tuple(shape):
+        (bo, sao, sbo, sco), (bi, sai, sbi, sci) = lv
+        try:
+            L.call("b200_gemm_softmax_bwd_rows", A.data_ptr(), B.data_ptr(), bo, bi, M, N, K, sao, sai, A.stride(-2),
+                   A.stride(-1), sbo, sbi, B.stride(-2), B.stride(-1), _ptr(sc), code(yc), yc.data_ptr(), _ptr(dx), _ptr(dxb),
+                   sco, sci, N, stream_ptr())
+            return dx, dxb
+        except UnimplementedMathError:
+            pass
+    g = contiguous(gemm(a, b, ab_dtype=torch.bfloat16))
+    yf = contiguous(cast(yc, torch.float32))
+    L.call("b200_softmax_bwd_rows", yf.data_ptr(), g.data_ptr(), _ptr(sc), _ptr(dx), _ptr(dxb), g.numel() // N, N, stream_ptr())
+    return dx, dxb
+
+
 _SMS: dict[int, int] = {}
 
 

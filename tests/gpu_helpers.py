@@ -32,7 +32,25 @@ def rms(a) -> float:
     return float(np.sqrt(np.mean(nz * nz))) if nz.size else 0.0
 
 
-def close_report(name, got, ref, rtol, floor=0.0) -> str | None:
+BF16_SIGMAS = 6.0  # the bf16-noise part of the floor, in units of that output's bf16 rounding effect
+
+
+def bf16_noise_floor(ref_bf16, ref_fp32) -> float:
+    """The absolute floor of one output of a bf16-math graph: BF16_SIGMAS x the RMS of the
+    difference bf16 operand rounding itself makes to that output (the oracle evaluated
+    with and without rounding every contraction operand to bf16).
+
+    Why: two correct bf16 evaluations (this backend and the oracle's bf16 emulation)
+    differ only in fp32 summation order, but a difference of one fp32 ulp before a bf16
+    rounding can move the rounded operand by a whole bf16 ulp, and through a deep network
+    such flips compound until the two evaluations differ like two independent roundings:
+    by about the size of the rounding's own effect. An element further from the oracle
+    than BF16_SIGMAS times that (a 6-sigma tail for Gaussian noise) is not rounding."""
+    a = np.asarray(ref_bf16, dtype=np.float64) - np.asarray(ref_fp32, dtype=np.float64)
+    return BF16_SIGMAS * float(np.sqrt(np.mean(a * a))) if a.size else 0.0
+
+
+def close_report(name, got, ref, rtol, floor=0.0, atol_floor=0.0) -> str | None:
     """None when ``got`` matches ``ref`` elementwise, else a one-line description:
     |got - ref| <= rtol * |ref| + atol for every element, with the absolute floor
     atol = rtol * max(rms(ref), floor), rms over ref's non-zero entries.
@@ -43,7 +61,8 @@ def close_report(name, got, ref, rtol, floor=0.0) -> str | None:
     entry itself. The floor bounds that error at rtol of the RMS. Entries that are exactly
     zero in the reference (embedding rows of tokens absent from the batch) do not set the
     scale. ``floor`` covers outputs that are zero in exact arithmetic (pure rounding
-    noise): the caller derives it from a related output. Integer / bool outputs (argmax,
+    noise): the caller derives it from a related output. ``atol_floor`` is an absolute
+    floor in the output's units (``bf16_noise_floor``). Integer / bool outputs (argmax,
     labels, gathers) must be bit-exact."""
     got = to_np(got)
     ref = np.asarray(ref)
@@ -54,7 +73,7 @@ def close_report(name, got, ref, rtol, floor=0.0) -> str | None:
         return None if n == 0 else f"{name}: {n} of {ref.size} integer elements differ"
     g64, r64 = got.astype(np.float64), ref.astype(np.float64)
     scale = rms(r64)
-    atol = rtol * max(scale, float(floor), 1e-30)
+    atol = max(rtol * max(scale, float(floor), 1e-30), float(atol_floor))
     err = np.abs(g64 - r64)
     lim = atol + rtol * np.abs(r64)
     bad = ~(err <= lim)
@@ -66,9 +85,9 @@ def close_report(name, got, ref, rtol, floor=0.0) -> str | None:
             f"{float(err.flat[k] / lim.flat[k]):.3g}; max |diff| / rms = {float(err.max() / max(scale, 1e-30)):.3g}")
 
 
-def assert_close(name, got, ref, rtol, floor=0.0):
+def assert_close(name, got, ref, rtol, floor=0.0, atol_floor=0.0):
     """``close_report`` as an assertion."""
-    msg = close_report(name, got, ref, rtol, floor)
+    msg = close_report(name, got, ref, rtol, floor, atol_floor)
     if msg:
         raise AssertionError(msg)
 

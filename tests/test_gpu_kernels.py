@@ -739,3 +739,40 @@ def test_column_reduce_split_deterministic():
     np.testing.assert_allclose(to_np(m), x.astype(np.float64).mean(0), rtol=1e-4, atol=1e-5)
     mx = ops.op_reduce_max(X, axis=0)
     np.testing.assert_array_equal(to_np(mx), x.max(0))
+
+
+@pytest.mark.parametrize("B_,H,S,hd", [(2, 4, 512, 64), (1, 3, 200, 64), (2, 2, 32, 16), (1, 2, 384, 128)])
+def test_attention_rows_fused_softmax_and_vjp(B_, H, S, hd):
+    """Scores GEMM with the softmax in its epilogue (and dO.V^T with the softmax VJP), on
+    the head-split views attention uses ([B*S, H*hd] read as [B, H, S, hd] without copies):
+    against float64 on the same bf16 operands. Ragged rows / columns (S = 200), a head dim
+    of 16 and of 128, and both dtypes of the saved softmax output in the backward."""
+    from b200 import ops
+
+    r = rng(B_ * 1000 + S + hd)
+    q = _bf16(r.standard_normal((B_ * S, H * hd), dtype=np.float32))
+    k = _bf16(r.standard_normal((B_ * S, H * hd), dtype=np.float32))
+    Q = T(q).to(torch.bfloat16).view(B_, S, H, hd).permute(0, 2, 1, 3)   # [B, H, S, hd]
+    KT = T(k).to(torch.bfloat16).view(B_, S, H, hd).permute(0, 2, 3, 1)  # [B, H, hd, S]
+    scale = np.float32(1.0 / np.sqrt(hd))
+    qn = q.reshape(B_, S, H, hd).transpose(0, 2, 1, 3).astype(np.float64)
+    kn = k.reshape(B_, S, H, hd).transpose(0, 2, 3, 1).astype(np.float64)
+    z = np.matmul(qn, kn) * np.float64(scale)
+    e = np.exp(z - z.max(-1, keepdims=True))
+    yref = e / e.sum(-1, keepdims=True)
+    y, yb = ops.gemm_softmax_rows(Q, KT, T(np.array(scale)), True, True)
+    np.testing.assert_allclose(to_np(y), yref, rtol=1e-4, atol=1e-6)
+    np.testing.assert_allclose(to_np(yb.float()), yref, rtol=1e-2, atol=1e-4)
+    # backward: G = dO.V^T, dx = scale * y * (G - rowsum(G y))
+    do = _bf16(r.standard_normal((B_ * S, H * hd), dtype=np.float32))
+    v = _bf16(r.standard_normal((B_ * S, H * hd), dtype=np.float32))
+    DO = T(do).to(torch.bfloat16).view(B_, S, H, hd).permute(0, 2, 1, 3)
+    VT = T(v).to(torch.bfloat16).view(B_, S, H, hd).permute(0, 2, 3, 1)
+    G = np.matmul(do.reshape(B_, S, H, hd).transpose(0, 2, 1, 3).astype(np.float64),
+                  v.reshape(B_, S, H, hd).transpose(0, 2, 3, 1).astype(np.float64))
+    for ysaved in (y, yb):
+        yv = to_np(ysaved.float()).astype(np.float64)
+        dref = np.float64(scale) * yv * (G - (G * yv).sum(-1, keepdims=True))
+        dx, dxb = ops.gemm_softmax_bwd_rows(DO, VT, ysaved, T(np.array(scale)), True, True)
+        np.testing.assert_allclose(to_np(dx), dref, rtol=1e-4, atol=1e-5)
+        np.testing.assert_allclose(to_np(dxb.float()), dref, rtol=1e-2, atol=1e-3)
