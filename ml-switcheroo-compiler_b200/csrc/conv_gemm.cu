@@ -66,67 +66,106 @@ __device__ __forceinline__ float x_tap(const float* __restrict__ x, const Dims& 
   return __ldg(x + ((((int64_t)n * d.C + t.c) * d.H + h) * d.W + w));
 }
 
-constexpr int NPB = 8;  // images (or tap rows / channels) one block walks through
+constexpr int NPB = 8;  // images (or channels) one col2im block walks through
+
+__device__ __forceinline__ uint4 pack8(const float (&v)[8]) {
+  __nv_bfloat162 a = __floats2bfloat162_rn(v[0], v[1]), b = __floats2bfloat162_rn(v[2], v[3]);
+  __nv_bfloat162 c = __floats2bfloat162_rn(v[4], v[5]), e = __floats2bfloat162_rn(v[6], v[7]);
+  return make_uint4(*reinterpret_cast<uint32_t*>(&a), *reinterpret_cast<uint32_t*>(&b), *reinterpret_cast<uint32_t*>(&c),
+                    *reinterpret_cast<uint32_t*>(&e));
+}
+
+// The staging kernels below walk their output as one flat array of 8-element groups:
+// every group lies inside one row (Pp and L are multiples of 8), is decoded once, and
+// leaves as one 16-byte store; a grid-stride loop covers the groups.
 
 // x -> col bf16 [N, Kp, Pp]   (fwd operand: rows are taps, contiguous pixels)
-// grid (ceil(Pp / 256), Kp, ceil(N / NPB))
 __global__ void __launch_bounds__(256) im2col_kp_kernel(const float* __restrict__ x, __nv_bfloat16* __restrict__ col, Dims d) {
-  const int p = blockIdx.x * 256 + threadIdx.x, k = blockIdx.y;
-  const int Pp = (int)d.Pp();
-  if (p >= Pp) return;
-  const bool in = k < (int)d.K() && p < (int)d.P();
-  const Tap t = tap_of(d, in ? k : 0);
-  const int n1 = min((int)d.N, (int)(blockIdx.z + 1) * NPB);
-  for (int n = blockIdx.z * NPB; n < n1; ++n)
-    col[((int64_t)n * d.Kp() + k) * Pp + p] = bf(in ? x_tap(x, d, n, t, p) : 0.f);
+  const int64_t Kp = d.Kp(), Pp = d.Pp(), P = d.P(), K = d.K();
+  const int64_t groups = d.N * Kp * Pp / 8;
+  for (int64_t g = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; g < groups; g += (int64_t)gridDim.x * blockDim.x) {
+    const int64_t e = g * 8;
+    const int p0 = (int)(e % Pp);
+    const int64_t nk = e / Pp;
+    const int k = (int)(nk % Kp), n = (int)(nk / Kp);
+    float v[8];
+    if (k < K) {
+      const Tap t = tap_of(d, k);
+#pragma unroll
+      for (int i = 0; i < 8; ++i) v[i] = (p0 + i < P) ? x_tap(x, d, n, t, p0 + i) : 0.f;
+    } else {
+#pragma unroll
+      for (int i = 0; i < 8; ++i) v[i] = 0.f;
+    }
+    *reinterpret_cast<uint4*>(col + e) = pack8(v);
+  }
 }
 
 // x -> col bf16 [S, Kp, L]: split s holds pixels q = s * L + l, q = n * Pp + p (zero past
 // the data), so each split is a dense K-major weight-gradient operand
-// grid (ceil(L / 256), ceil(Kp / NPB), S)
 __global__ void __launch_bounds__(256) im2col_kq_kernel(const float* __restrict__ x, __nv_bfloat16* __restrict__ col, Dims d,
-                                                        int64_t L) {
-  const int l = blockIdx.x * 256 + threadIdx.x, sidx = blockIdx.z;
-  if (l >= L) return;
-  const int64_t q = (int64_t)sidx * L + l;
-  const int Pp = (int)d.Pp();
-  const int n = (int)(q / Pp), p = (int)(q - (int64_t)n * Pp);
-  const bool pix = n < (int)d.N && p < (int)d.P();
-  const int k1 = min((int)d.Kp(), (int)(blockIdx.y + 1) * NPB);
-  for (int k = blockIdx.y * NPB; k < k1; ++k) {
-    float v = 0.f;
-    if (pix && k < (int)d.K()) v = x_tap(x, d, n, tap_of(d, k), p);
-    col[((int64_t)sidx * d.Kp() + k) * L + l] = bf(v);
+                                                        int64_t L, int64_t S) {
+  const int64_t Kp = d.Kp(), Pp = d.Pp(), P = d.P(), K = d.K();
+  const int64_t groups = S * Kp * L / 8;
+  for (int64_t g = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; g < groups; g += (int64_t)gridDim.x * blockDim.x) {
+    const int64_t e = g * 8;
+    const int64_t l0 = e % L, sk = e / L;
+    const int k = (int)(sk % Kp);
+    const int64_t sidx = sk / Kp;
+    const int64_t q0 = sidx * L + l0;  // 8 consecutive pixels of one image (Pp % 8 == 0)
+    const int n = (int)(q0 / Pp), p0 = (int)(q0 - (int64_t)n * Pp);
+    float v[8];
+    if (k < K && n < d.N) {
+      const Tap t = tap_of(d, k);
+#pragma unroll
+      for (int i = 0; i < 8; ++i) v[i] = (p0 + i < P) ? x_tap(x, d, n, t, p0 + i) : 0.f;
+    } else {
+#pragma unroll
+      for (int i = 0; i < 8; ++i) v[i] = 0.f;
+    }
+    *reinterpret_cast<uint4*>(col + e) = pack8(v);
   }
 }
 
-// dy fp32 [N, O, P] -> bf16 [N, O, Pp]; grid (ceil(Pp / 256), O, ceil(N / NPB))
+// dy fp32 [N, O, P] -> bf16 [N, O, Pp]
 __global__ void __launch_bounds__(256) pack_dy_nop_kernel(const float* __restrict__ dy, __nv_bfloat16* __restrict__ out, Dims d) {
-  const int p = blockIdx.x * 256 + threadIdx.x, o = blockIdx.y;
-  const int P = (int)d.P(), Pp = (int)d.Pp();
-  if (p >= Pp) return;
-  const int n1 = min((int)d.N, (int)(blockIdx.z + 1) * NPB);
-  for (int n = blockIdx.z * NPB; n < n1; ++n) {
-    const int64_t no = (int64_t)n * d.O + o;
-    out[no * Pp + p] = bf(p < P ? __ldg(dy + no * P + p) : 0.f);
+  const int64_t P = d.P(), Pp = d.Pp();
+  const int64_t groups = d.N * d.O * Pp / 8;
+  for (int64_t g = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; g < groups; g += (int64_t)gridDim.x * blockDim.x) {
+    const int64_t e = g * 8;
+    const int64_t no = e / Pp;
+    const int p0 = (int)(e - no * Pp);
+    const float* src = dy + no * P;
+    float v[8];
+#pragma unroll
+    for (int i = 0; i < 8; ++i) v[i] = (p0 + i < P) ? __ldg(src + p0 + i) : 0.f;
+    *reinterpret_cast<uint4*>(out + e) = pack8(v);
   }
 }
 
 // dy fp32 [N, O, P] -> bf16 [S, O, L]: split s holds columns q = s * L + l, q = n * Pp + p
 // (zero past the data), so each split is a dense [O, L] K-major GEMM operand
-// grid (ceil(L / 256), ceil(O / NPB), S)
 __global__ void __launch_bounds__(256) pack_dy_sol_kernel(const float* __restrict__ dy, __nv_bfloat16* __restrict__ out, Dims d,
-                                                          int64_t L) {
-  const int l = blockIdx.x * 256 + threadIdx.x, sidx = blockIdx.z;
-  if (l >= L) return;
-  const int64_t q = (int64_t)sidx * L + l;
-  const int P = (int)d.P(), Pp = (int)d.Pp();
-  const int n = (int)(q / Pp), p = (int)(q - (int64_t)n * Pp);
-  const bool in = n < (int)d.N && p < P;
-  const int o1 = min((int)d.O, (int)(blockIdx.y + 1) * NPB);
-  for (int o = blockIdx.y * NPB; o < o1; ++o) {
-    const float v = in ? __ldg(dy + ((int64_t)n * d.O + o) * P + p) : 0.f;
-    out[((int64_t)sidx * d.O + o) * L + l] = bf(v);
+                                                          int64_t L, int64_t S) {
+  const int64_t P = d.P(), Pp = d.Pp(), O = d.O;
+  const int64_t groups = S * O * L / 8;
+  for (int64_t g = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; g < groups; g += (int64_t)gridDim.x * blockDim.x) {
+    const int64_t e = g * 8;
+    const int64_t l0 = e % L, so = e / L;
+    const int64_t o = so % O, sidx = so / O;
+    const int64_t q0 = sidx * L + l0;
+    const int64_t n = q0 / Pp;
+    const int p0 = (int)(q0 - n * Pp);
+    float v[8];
+    if (n < d.N) {
+      const float* src = dy + (n * O + o) * P;
+#pragma unroll
+      for (int i = 0; i < 8; ++i) v[i] = (p0 + i < P) ? __ldg(src + p0 + i) : 0.f;
+    } else {
+#pragma unroll
+      for (int i = 0; i < 8; ++i) v[i] = 0.f;
+    }
+    *reinterpret_cast<uint4*>(out + e) = pack8(v);
   }
 }
 
@@ -234,9 +273,7 @@ extern "C" int b200_conv2d_fwd_tc(const float* x, const float* w, float* y, int6
   auto* col = reinterpret_cast<__nv_bfloat16*>(reinterpret_cast<uint8_t*>(ws) + al256((size_t)O * Kp * 2));
   pack_weight_kernel<<<grid_of(O * Kp), 256, 0, s>>>(w, wp, O, d.K(), Kp);
   if ((rc = check_launch("conv2d_fwd_tc(pack w)"))) return rc;
-  B200_REQUIRE(Kp <= 65535 && N <= 65535, "conv2d_fwd_tc: too many taps or images");
-  im2col_kp_kernel<<<dim3((unsigned)ceil_div(Pp, (int64_t)256), (unsigned)Kp, (unsigned)ceil_div(N, (int64_t)NPB)), 256, 0, s>>>(
-      x, col, d);
+  im2col_kp_kernel<<<grid_of(N * Kp * Pp / 8), 256, 0, s>>>(x, col, d);
   if ((rc = check_launch("conv2d_fwd_tc(im2col)"))) return rc;
   // Y_n [O, P] = Wp [O, Kp] (shared) . Xcol_n [Kp, Pp]
   return gemm_bf16_tcgen05(B200_F32, wp, col, y, N, O, P, Kp, 0, Kp, 1, Kp * Pp, Pp, 1, O * P, P, 1.f, nullptr,
@@ -262,8 +299,7 @@ extern "C" int b200_conv2d_dgrad_tc(const float* dy, const float* w, float* dx, 
   pack_weight_kernel<<<grid_of(O * Kp), 256, 0, s>>>(w, wp, O, d.K(), Kp);
   if ((rc = check_launch("conv2d_dgrad_tc(pack w)"))) return rc;
   B200_REQUIRE(O <= 65535 && N <= 65535 && C <= 65535, "conv2d_dgrad_tc: too many channels or images");
-  pack_dy_nop_kernel<<<dim3((unsigned)ceil_div(Pp, (int64_t)256), (unsigned)O, (unsigned)ceil_div(N, (int64_t)NPB)), 256, 0, s>>>(
-      dy, dyp, d);
+  pack_dy_nop_kernel<<<grid_of(N * O * Pp / 8), 256, 0, s>>>(dy, dyp, d);
   if ((rc = check_launch("conv2d_dgrad_tc(pack dy)"))) return rc;
   // dXcol_n [Kp, P] = Wp^T [Kp, O] (shared, MN-major) . dY_n [O, Pp]
   rc = gemm_bf16_tcgen05(B200_F32, wp, dyp, dxcol, N, Kp, P, O, 0, 1, Kp, O * Pp, Pp, 1, Kp * P, P, 1.f, nullptr, B200_EPI_NONE,
@@ -296,11 +332,9 @@ extern "C" int b200_conv2d_wgrad_tc(const float* x, const float* dy, float* dw, 
   auto* col = reinterpret_cast<__nv_bfloat16*>(base);
   base += al256((size_t)S * Kp * L * 2);
   auto* part = reinterpret_cast<float*>(base);
-  B200_REQUIRE(O <= 65535 && Kp <= 65535 && S <= 65535, "conv2d_wgrad_tc: too many channels or splits");
-  const unsigned gx = (unsigned)ceil_div(L, (int64_t)256);
-  pack_dy_sol_kernel<<<dim3(gx, (unsigned)ceil_div(O, (int64_t)NPB), (unsigned)S), 256, 0, s>>>(dy, dyt, d, L);
+  pack_dy_sol_kernel<<<grid_of(S * O * L / 8), 256, 0, s>>>(dy, dyt, d, L, S);
   if ((rc = check_launch("conv2d_wgrad_tc(pack dy)"))) return rc;
-  im2col_kq_kernel<<<dim3(gx, (unsigned)ceil_div(Kp, (int64_t)NPB), (unsigned)S), 256, 0, s>>>(x, col, d, L);
+  im2col_kq_kernel<<<grid_of(S * Kp * L / 8), 256, 0, s>>>(x, col, d, L, S);
   if ((rc = check_launch("conv2d_wgrad_tc(im2col)"))) return rc;
   // partial_s [O, Kp] = dYt_s [O, L] . col_s^T   (col_s [Kp, L]: K-major B operand)
   rc = gemm_bf16_tcgen05(B200_F32, dyt, col, part, S, O, Kp, L, O * L, L, 1, Kp * L, 1, L, O * Kp, Kp, 1.f, nullptr,
