@@ -32,22 +32,52 @@ def rms(a) -> float:
     return float(np.sqrt(np.mean(nz * nz))) if nz.size else 0.0
 
 
-BF16_SIGMAS = 6.0  # the bf16-noise part of the floor, in units of that output's bf16 rounding effect
+BF16_REALIZATIONS = 2.0  # the GPU's bf16 rounding and the oracle's emulation of it
 
 
-def bf16_noise_floor(ref_bf16, ref_fp32) -> float:
-    """The absolute floor of one output of a bf16-math graph: BF16_SIGMAS x the RMS of the
-    difference bf16 operand rounding itself makes to that output (the oracle evaluated
-    with and without rounding every contraction operand to bf16).
-
-    Why: two correct bf16 evaluations (this backend and the oracle's bf16 emulation)
-    differ only in fp32 summation order, but a difference of one fp32 ulp before a bf16
-    rounding can move the rounded operand by a whole bf16 ulp, and through a deep network
-    such flips compound until the two evaluations differ like two independent roundings:
-    by about the size of the rounding's own effect. An element further from the oracle
-    than BF16_SIGMAS times that (a 6-sigma tail for Gaussian noise) is not rounding."""
+def bf16_noise(ref_bf16, ref_fp32) -> tuple[float, float]:
+    """(largest |difference|, RMS difference) that bf16 operand rounding itself makes to one
+    output of a bf16-math graph: the oracle evaluated with and without rounding every
+    contraction operand to bf16 (fp32 accumulation both times)."""
     a = np.asarray(ref_bf16, dtype=np.float64) - np.asarray(ref_fp32, dtype=np.float64)
-    return BF16_SIGMAS * float(np.sqrt(np.mean(a * a))) if a.size else 0.0
+    if not a.size:
+        return 0.0, 0.0
+    return float(np.abs(a).max()), float(np.sqrt(np.mean(a * a)))
+
+
+def bf16_report(name, got, ref_bf16, ref_fp32, rtol, floor=0.0) -> str | None:
+    """None when ``got`` (the backend under the bf16 policy) is as close to the oracle's
+    bf16 emulation ``ref_bf16`` as a second bf16 evaluation can be, else a description.
+
+    Two correct bf16 evaluations (this backend and the oracle's emulation) differ only in
+    fp32 summation order before each rounding, but a difference of one fp32 ulp there can
+    move a rounded operand by a whole bf16 ulp. A difference d before a rounding thus
+    becomes about sqrt(d x ulp) after it, and through a deep graph the two evaluations
+    drift apart until they differ like two independent roundings (measured on the
+    transformer step: the ratio RMS(backend - emulation) / RMS(emulation - fp32) grows
+    0.005, 0.04, 0.18, 0.43, 0.67, ... through the first layer's GEMMs and settles near 1).
+    Rounding noise in a gradient is also heavy-tailed: its largest element is tens of times
+    its RMS. So each evaluation is held to the rounding's own size, measured on the oracle:
+    if both lie within M = max |emulation - fp32| of the exact result, they lie within 2M of
+    each other (and within 2 x RMS(emulation - fp32) in RMS):
+
+    * elementwise |got - ref_bf16| <= rtol * |ref_bf16| + atol, atol = the larger of
+      rtol * rms(ref_bf16) (``close_report``'s floor) and 2M;
+    * RMS(got - ref_bf16) <= 2 x RMS(ref_bf16 - ref_fp32) + 1e-5 x rms(ref_bf16), so a
+      systematic error cannot hide under the tails' allowance.
+    """
+    big, spread = bf16_noise(ref_bf16, ref_fp32)
+    msg = close_report(name, got, ref_bf16, rtol, floor=floor, atol_floor=BF16_REALIZATIONS * big)
+    if msg:
+        return msg
+    g = to_np(got).astype(np.float64)
+    e = np.asarray(ref_bf16, dtype=np.float64)
+    d = float(np.sqrt(np.mean((g - e) ** 2))) if e.size else 0.0
+    lim = BF16_REALIZATIONS * spread + 1e-5 * rms(e)
+    if d > lim:
+        return (f"{name}: RMS(got - oracle) {d:.3g} above {BF16_REALIZATIONS:g} x RMS of the bf16 rounding's own effect "
+                f"({spread:.3g}) + 1e-5 x rms")
+    return None
 
 
 def close_report(name, got, ref, rtol, floor=0.0, atol_floor=0.0) -> str | None:
@@ -62,7 +92,7 @@ def close_report(name, got, ref, rtol, floor=0.0, atol_floor=0.0) -> str | None:
     zero in the reference (embedding rows of tokens absent from the batch) do not set the
     scale. ``floor`` covers outputs that are zero in exact arithmetic (pure rounding
     noise): the caller derives it from a related output. ``atol_floor`` is an absolute
-    floor in the output's units (``bf16_noise_floor``). Integer / bool outputs (argmax,
+    floor in the output's units (``bf16_report``). Integer / bool outputs (argmax,
     labels, gathers) must be bit-exact."""
     got = to_np(got)
     ref = np.asarray(ref)
@@ -122,18 +152,24 @@ def run_case(case: str, mode: str = "graph"):
 
 
 def gpu_decisions(g, inputs) -> dict:
-    """The backend's own ReLU VJP masks (every ``Greater`` node of the graph), from an
-    unfused run of the same graph on the same inputs: node id -> bool array. The fused
-    kernels compute these comparisons from the same pre-activation arithmetic (a GEMM's
-    fp32 accumulator plus the bias, rounded once), so they decide the same way."""
+    """The backend's own ReLU VJP masks (every ``Greater`` node of the graph): node id ->
+    bool array. Each mask is taken from the fused plan the backend runs, where the kernel
+    that produces it (a GEMM or convolution epilogue, a fused elementwise step) publishes
+    it; a mask that stays inside a fused kernel is taken from an unfused run of the same
+    graph on the same inputs instead."""
     from b200.executor import GraphRunner
 
     ids = {n.id: None for n in g.nodes.values() if n.op_type == "Greater"}
     if not ids:
         return {}
-    r = GraphRunner(g, fuse=False)
-    d = r.device_inputs(inputs)
-    r.plan_for(d).run(d, capture=ids)
+    for fuse in (True, False):
+        want = {k: None for k, v in ids.items() if v is None}
+        if not want:
+            break
+        r = GraphRunner(g, fuse=fuse)
+        d = r.device_inputs(inputs)
+        r.plan_for(d).run(d, capture=want)
+        ids.update({k: v for k, v in want.items() if v is not None})
     return {k: to_np(v).astype(bool) for k, v in ids.items() if v is not None}
 
 
