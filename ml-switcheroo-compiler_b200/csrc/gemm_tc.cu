@@ -32,60 +32,6 @@ constexpr int BM = 128, BK = 64, STAGES = 4, STAGES_PAIR = 6, EPI_WARPS = B200_G
 constexpr uint32_t EPI_BUF = 4096;  // per epilogue warp
 constexpr uint32_t EPI_SMEM = EPI_WARPS * EPI_BUF;  // after the operand ring
 static_assert(EPI_WARPS == 4 || EPI_WARPS == 8, "4 or 8 epilogue warps (the staging buffers must fit)");
-// Stage a 32 x 32 chunk (lane = row, `w` = the row's 32 elements packed into 32-bit words)
-// into a swizzled buffer: ESZ-byte elements, rows of 32 * ESZ bytes, 16-byte pieces XORed
-// by the row index (the 128B / 64B / 32B TMA swizzle patterns), so both the row-per-lane
-// writes and the row-contiguous reads are free of bank conflicts.
-template <int ESZ>
-__device__ __forceinline__ void stage_chunk(uint32_t buf, int lane, const uint32_t (&w)[8 * ESZ]) {
-  constexpr int PIECES = 2 * ESZ;  // 16-byte pieces per row
-  const uint32_t rb = buf + (uint32_t)lane * (32u * ESZ);
-  const uint32_t sw = ESZ == 4 ? (uint32_t)(lane & 7) : (ESZ == 2 ? (uint32_t)((lane >> 1) & 3) : (uint32_t)((lane >> 2) & 1));
-#pragma unroll
-  for (int j = 0; j < PIECES; ++j)
-    st_shared_v4(rb + (((uint32_t)j ^ sw) << 4), w[4 * j], w[4 * j + 1], w[4 * j + 2], w[4 * j + 3]);
-}
-
-// store `n` (<= 16) bytes of a 16-byte piece at dst: one vector store when whole and aligned
-__device__ __forceinline__ void put_piece(uint8_t* dst, uint4 u, int64_t n) {
-  if (n >= 16 && (reinterpret_cast<uintptr_t>(dst) & 15) == 0) {
-    *reinterpret_cast<uint4*>(dst) = u;
-    return;
-  }
-  const uint32_t w[4] = {u.x, u.y, u.z, u.w};
-  if ((reinterpret_cast<uintptr_t>(dst) & 3) == 0) {
-#pragma unroll
-    for (int k = 0; k < 4; ++k)
-      if (4 * k + 4 <= n) reinterpret_cast<uint32_t*>(dst)[k] = w[k];
-      else {
-        for (int b = 4 * k; b < n && b < 4 * k + 4; ++b) dst[b] = (uint8_t)(w[k] >> (8 * (b & 3)));
-        break;
-      }
-    return;
-  }
-  for (int b = 0; b < 16 && b < n; ++b) dst[b] = (uint8_t)(w[b >> 2] >> (8 * (b & 3)));
-}
-
-// Write the staged chunk back row-contiguously: every warp store instruction covers
-// 512 / 32 / ... whole row segments. `base` = element (row0, cbase) of the output,
-// `ld` = row stride in elements, `rows` / `cols` = how much of the chunk is inside.
-template <int ESZ>
-__device__ __forceinline__ void write_chunk(uint32_t buf, int lane, uint8_t* base, int64_t ld, int rows, int64_t cols) {
-  constexpr int PIECES = 2 * ESZ;         // 16-byte pieces per row
-  constexpr int ROWS_PER = 32 / PIECES;   // rows one instruction covers
-  const int j = lane % PIECES;
-#pragma unroll
-  for (int i = 0; i < PIECES; ++i) {
-    const int rr = i * ROWS_PER + lane / PIECES;
-    if (rr >= rows) continue;
-    const uint32_t sw = ESZ == 4 ? (uint32_t)(rr & 7) : (ESZ == 2 ? (uint32_t)((rr >> 1) & 3) : (uint32_t)((rr >> 2) & 1));
-    const uint4 u = ld_shared_v4(buf + (uint32_t)rr * (32u * ESZ) + (((uint32_t)j ^ sw) << 4));
-    const int64_t left = (cols - (int64_t)j * (16 / ESZ)) * ESZ;  // bytes of this piece inside the row
-    if (left <= 0) continue;
-    put_piece(base + ((int64_t)rr * ld + (int64_t)j * (16 / ESZ)) * ESZ, u, left);
-  }
-}
-
 struct Args {
   void* C;
   void* C2;  // optional bf16 copy of the activation; C then receives the pre-activation
@@ -508,28 +454,6 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(THREADS, 1)
 // ---------------------------------------------------------------------------------
 // host side
 // ---------------------------------------------------------------------------------
-// Store map for C / C2 / mask (store mode 2): dims (N, M, b_in, b_out), byte strides
-// (ldc, sC_in, sC_out) * esize, box 32 x 32 (one epilogue warp's chunk), swizzle matching
-// the staged rows (128 B fp32, 64 B bf16, 32 B mask rows). False when TMA cannot address it.
-static bool make_store_map(CUtensorMap* map, void* base, CUtensorMapDataType dt, uint32_t esize, int64_t N, int64_t M,
-                           int64_t b_in, int64_t b_out, int64_t ldc, int64_t sC_in, int64_t sC_out) {
-  auto enc = get_encode();
-  if (!enc || !base || (reinterpret_cast<uintptr_t>(base) & 15)) return false;
-  const uint64_t rowb = (uint64_t)ldc * esize;
-  const uint64_t s2 = b_in > 1 ? (uint64_t)sC_in * esize : rowb * (uint64_t)M;
-  const uint64_t s3 = b_out > 1 ? (uint64_t)sC_out * esize : s2 * (uint64_t)b_in;
-  if (rowb % 16 || s2 % 16 || s3 % 16 || rowb == 0 || s2 == 0 || s3 == 0) return false;
-  if (rowb >= (1ull << 40) || s2 >= (1ull << 40) || s3 >= (1ull << 40)) return false;
-  cuuint64_t dims[4] = {(cuuint64_t)N, (cuuint64_t)M, (cuuint64_t)b_in, (cuuint64_t)b_out};
-  cuuint64_t strides[3] = {rowb, s2, s3};
-  cuuint32_t box[4] = {32, 32, 1, 1};
-  cuuint32_t estr[4] = {1, 1, 1, 1};
-  const CUtensorMapSwizzle sw =
-      esize == 4 ? CU_TENSOR_MAP_SWIZZLE_128B : (esize == 2 ? CU_TENSOR_MAP_SWIZZLE_64B : CU_TENSOR_MAP_SWIZZLE_32B);
-  return enc(map, dt, 4, base, dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, sw, CU_TENSOR_MAP_L2_PROMOTION_NONE,
-             CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
-}
-
 template <int BN, int EPI, bool PAIR>
 static int launch(const CUtensorMap& ma, const CUtensorMap& mb, const CUtensorMap& mc, const CUtensorMap& mc2,
                   const CUtensorMap& maux, const Args& a, int64_t batch, cudaStream_t s) {
