@@ -380,6 +380,105 @@ def gemm_epilogue_step(m: Match) -> Step:
     return Step(list(o.values()), ins, run, label)
 
 
+# ----------------------------------------------------------------------------------
+# patterns: convolution epilogues (bf16 implicit-GEMM convolutions)
+#   Relu(Conv2D(x, w)) -> one kernel writing relu(.) only. The pre-activation's other
+#   readers are the ReLU VJP's Greater(pre, 0) masks, and Greater(relu(pre), 0) is the
+#   same mask elementwise, so the ReLU output stands in for the pre-activation there.
+#   Multiply(Conv2DInputGrad(dy, w), Greater(pre, 0)) -> the input-gradient kernel
+#   multiplies by (pre > 0) in its epilogue.
+# ----------------------------------------------------------------------------------
+def _is_zero_mask(g: Graph, n: Node | None, of: str) -> bool:
+    return n is not None and _op_name(n) == "Greater" and len(n.inputs) == 2 and n.inputs[0] == of and \
+        _const_value(g, n.inputs[1]) == 0.0
+
+
+def _conv_attrs(n: Node) -> dict:
+    return {k: n.attributes[k] for k in ("stride", "strides", "padding", "groups", "dilation", "dilations", "target_shape")
+            if k in n.attributes}
+
+
+def _conv_ok(kind: int, n: Node, meta: dict[str, Meta]) -> bool:
+    a = n.attributes
+    if int(a.get("groups", 1) or 1) != 1 or ops._stride2(a.get("dilations", a.get("dilation", 1)) or 1) != (1, 1):
+        return False
+    stride = a.get("strides", a.get("stride", (1, 1)))
+    padding = a.get("padding", "SAME")
+    mi = [meta.get(i) for i in n.inputs[:2]]
+    mo = meta.get(n.id)
+    if any(m is None or m.scalar or m.dtype != torch.float32 for m in mi) or mo is None or mo.scalar:
+        return False
+    if kind == 0:
+        return ops.conv_fused_ok(0, mi[0].shape, mi[1].shape, stride, padding, out_hw=tuple(mo.shape[2:]))
+    # input gradient: x shape = target_shape (= the output's), dy = inputs[0]
+    return len(mo.shape) == 4 and ops.conv_fused_ok(1, mo.shape, mi[1].shape, stride, padding, out_hw=tuple(mi[0].shape[2:]))
+
+
+def find_conv_relu(g: Graph, live: dict[str, Node], meta: dict[str, Meta], users: dict[str, list[str]],
+                   outputs: set[str]) -> list[Match]:
+    found = []
+    for nid, node in live.items():
+        if _op_name(node) != "Relu" or len(node.inputs) != 1:
+            continue
+        conv = live.get(node.inputs[0])
+        if conv is None or _op_name(conv) != "Conv2D" or conv.id in outputs or len(conv.inputs) != 2:
+            continue
+        others = [u for u in users.get(conv.id, []) if u != nid]
+        if not all(_is_zero_mask(g, live.get(u), conv.id) for u in others):
+            continue
+        if meta[nid].shape != meta[conv.id].shape or not _conv_ok(0, conv, meta):
+            continue
+        found.append(Match("conv_relu", {"x": conv.inputs[0], "w": conv.inputs[1], "conv": conv.id, "act": nid},
+                           {conv.id, nid}, {"act": nid, "conv": conv.id}))
+    return found
+
+
+def conv_relu_step(m: Match, g: Graph) -> Step:
+    b = m.bind
+    kw = _conv_attrs(g.nodes[b["conv"]])
+
+    def run(env: dict) -> None:
+        r = ops.op_conv2d(env[b["x"]], env[b["w"]], relu=True, **kw)
+        env[b["act"]] = r
+        env[b["conv"]] = r  # read only by Greater(pre, 0) masks: same mask from relu(pre)
+
+    return Step([b["act"], b["conv"]], [b["x"], b["w"]], run, "conv_relu")
+
+
+def find_conv_dgrad_mask(g: Graph, live: dict[str, Node], meta: dict[str, Meta], users: dict[str, list[str]],
+                         outputs: set[str]) -> list[Match]:
+    found = []
+    pat = Op("Multiply", Op("Conv2DInputGrad", Var("dy"), Var("w"), name="dg"), Op("Greater", Var("pre"), Const(0.0), name="gt"),
+             name="mul")
+    for nid, node in live.items():
+        if _op_name(node) != "Multiply":
+            continue
+        bind: dict[str, str] = {}
+        cov: set[str] = set()
+        if not match(pat, nid, g, bind, cov):
+            continue
+        if any(v in outputs or any(u != nid for u in users.get(v, [])) for v in (bind["dg"], bind["gt"])):
+            continue
+        mp, mo = meta.get(bind["pre"]), meta.get(nid)
+        if mp is None or mo is None or mp.scalar or mp.shape != mo.shape or mp.dtype != torch.float32:
+            continue
+        if meta[bind["dg"]].shape != mo.shape or not _conv_ok(1, g.nodes[bind["dg"]], meta):
+            continue
+        found.append(Match("conv_dgrad_mask", bind, {c for c in cov if c in live or g.nodes[c].op_type == "Constant"},
+                           {"dx": nid}))
+    return found
+
+
+def conv_dgrad_mask_step(m: Match, g: Graph) -> Step:
+    b = m.bind
+    kw = _conv_attrs(g.nodes[b["dg"]])
+
+    def run(env: dict) -> None:
+        env[b["mul"]] = ops.op_conv2d_input_grad(env[b["dy"]], env[b["w"]], mask=env[b["pre"]], **kw)
+
+    return Step([b["mul"]], [b["dy"], b["w"], b["pre"]], run, "conv_dgrad_mask")
+
+
 def _perm_of(n: Node, ndim: int) -> list[int]:
     axes = n.attributes.get("axes", n.attributes.get("perm"))
     if axes is None:
@@ -1335,6 +1434,18 @@ def plan_steps(graph: Graph, nodes: list[Node], sample: dict[str, Any]) -> list[
         if m.covered & taken:
             continue
         groups.append((sorted(m.covered), gemm_epilogue_step(m)))
+        taken |= m.covered
+
+    for m in find_conv_relu(graph, live, meta, users, outputs):
+        if m.covered & taken:
+            continue
+        groups.append((sorted(m.covered), conv_relu_step(m, graph)))
+        taken |= m.covered
+
+    for m in find_conv_dgrad_mask(graph, live, meta, users, outputs):
+        if m.covered & taken:
+            continue
+        groups.append((sorted(m.covered), conv_dgrad_mask_step(m, graph)))
         taken |= m.covered
 
     for m in find_xent(graph, live, meta, users, outputs):

@@ -1135,15 +1135,50 @@ def _conv_dt() -> int:
     return L.BF16 if Config.conv_dtype == "bf16" else L.F32
 
 
-def _conv_call(kind: int, a: torch.Tensor, b: torch.Tensor, out: torch.Tensor, dims: tuple) -> None:
-    """fp32 math: exact CUDA-core kernels; bf16 math: tcgen05 GEMMs over staged operands."""
+def _conv_call(kind: int, a: torch.Tensor, b: torch.Tensor, out: torch.Tensor, dims: tuple, relu: bool = False,
+               mask: torch.Tensor | None = None) -> None:
+    """fp32 math: exact CUDA-core kernels; bf16 math: tcgen05 implicit GEMMs (operand tiles
+    gathered straight into shared memory), or tcgen05 GEMMs over staged operands for shapes
+    the implicit GEMM does not take. ``relu`` (forward) and ``mask`` (input gradient:
+    ``dx * (mask > 0)``) are epilogues of the implicit GEMM only."""
     names = ("b200_conv2d_fwd", "b200_conv2d_dgrad", "b200_conv2d_wgrad")
+    fused = relu or mask is not None
     if Config.conv_dtype != "bf16":
+        if fused:
+            raise UnimplementedMathError("fused convolution epilogues need bf16 convolution math")
         L.call(names[kind], L.F32, a.data_ptr(), b.data_ptr(), out.data_ptr(), *dims, stream_ptr())
         return
+    if L.lib().b200_conv2d_igemm_supported(kind, *dims):
+        if kind == 0:
+            L.call("b200_conv2d_fwd_igemm", a.data_ptr(), b.data_ptr(), out.data_ptr(), *dims, 1 if relu else 0, stream_ptr())
+        elif kind == 1:
+            L.call("b200_conv2d_dgrad_igemm", a.data_ptr(), b.data_ptr(), _ptr(mask), out.data_ptr(), *dims, stream_ptr())
+        else:
+            ws_bytes = int(L.lib().b200_conv2d_wgrad_igemm_workspace_bytes(*dims))
+            ws = torch.empty(max(1, ws_bytes), dtype=torch.uint8, device=device())
+            L.call("b200_conv2d_wgrad_igemm", a.data_ptr(), b.data_ptr(), out.data_ptr(), *dims, ws.data_ptr(), ws_bytes,
+                   stream_ptr())
+        return
+    if fused:
+        raise UnimplementedMathError("fused convolution epilogue for a shape outside the implicit GEMM")
     ws_bytes = int(L.lib().b200_conv2d_tc_workspace_bytes(kind, *dims))
     ws = torch.empty(max(1, ws_bytes), dtype=torch.uint8, device=device())
     L.call(names[kind] + "_tc", a.data_ptr(), b.data_ptr(), out.data_ptr(), *dims, ws.data_ptr(), ws_bytes, stream_ptr())
+
+
+def conv_fused_ok(kind: int, x_shape: tuple, w_shape: tuple, stride, padding, out_hw: tuple | None = None) -> bool:
+    """Whether a fused conv epilogue (forward ReLU, input-gradient mask) has a kernel."""
+    if Config.conv_dtype != "bf16" or len(x_shape) != 4 or len(w_shape) != 4:
+        return False
+    s = _stride2(stride)
+    N, Cc, H, W = (int(v) for v in x_shape)
+    O, _, KH, KW = (int(v) for v in w_shape)
+    try:
+        OH, OW = out_hw if out_hw is not None else _conv_out_hw((H, W), (KH, KW), s, padding)
+        pt, pl = _conv_pads((H, W), (KH, KW), s, padding, (OH, OW))
+    except UnimplementedMathError:
+        return False
+    return bool(L.lib().b200_conv2d_igemm_supported(kind, N, Cc, H, W, O, KH, KW, OH, OW, s[0], s[1], pt, pl))
 
 
 def _check_conv_attrs(groups, dilation):
@@ -1154,7 +1189,9 @@ def _check_conv_attrs(groups, dilation):
         raise UnimplementedMathError("dilated Conv2D")
 
 
-def op_conv2d(x, w, stride=(1, 1), padding="SAME", groups=1, dilation=1, **kw):  # numpy/eager/conv.py:462-489
+def op_conv2d(x, w, stride=(1, 1), padding="SAME", groups=1, dilation=1, relu=False, **kw):  # numpy/eager/conv.py:462-489
+    """Conv2D; ``relu=True`` returns relu(Conv2D(x, w)) from the same kernel (the Relu node
+    that follows it in the graph, fused)."""
     _check_conv_attrs(groups, kw.get("dilations", dilation))
     s = _stride2(kw.get("strides", stride))
     xc, wc = contiguous(cast(x, torch.float32)), contiguous(cast(w, torch.float32))
@@ -1163,12 +1200,13 @@ def op_conv2d(x, w, stride=(1, 1), padding="SAME", groups=1, dilation=1, **kw): 
     OH, OW = _conv_out_hw((H, W), (KH, KW), s, padding)
     pt, pl = _conv_pads((H, W), (KH, KW), s, padding, (OH, OW))
     y = torch.empty(N, O, OH, OW, dtype=torch.float32, device=device())
-    _conv_call(0, xc, wc, y, (N, Cc, H, W, O, KH, KW, OH, OW, s[0], s[1], pt, pl))
+    _conv_call(0, xc, wc, y, (N, Cc, H, W, O, KH, KW, OH, OW, s[0], s[1], pt, pl), relu=bool(relu))
     return y
 
 
-def op_conv2d_input_grad(dy, w, stride=(1, 1), padding="SAME", target_shape=None, groups=1, dilation=1, **kw):
-    # numpy/eager/conv.py:634-697
+def op_conv2d_input_grad(dy, w, stride=(1, 1), padding="SAME", target_shape=None, groups=1, dilation=1, mask=None, **kw):
+    """Conv2DInputGrad (numpy/eager/conv.py:634-697); with ``mask`` (fp32, the input's shape)
+    it returns dx * (mask > 0): the Multiply by the ReLU VJP's Greater(pre, 0) mask, fused."""
     _check_conv_attrs(groups, kw.get("dilations", dilation))
     s = _stride2(kw.get("strides", stride))
     dyc, wc = contiguous(cast(dy, torch.float32)), contiguous(cast(w, torch.float32))
@@ -1177,7 +1215,11 @@ def op_conv2d_input_grad(dy, w, stride=(1, 1), padding="SAME", target_shape=None
     OH, OW = dyc.shape[2], dyc.shape[3]
     pt, pl = _conv_pads((H, W), (KH, KW), s, padding, (OH, OW))
     dx = torch.empty(N, Cc, H, W, dtype=torch.float32, device=device())
-    _conv_call(1, dyc, wc, dx, (N, Cc, H, W, O, KH, KW, OH, OW, s[0], s[1], pt, pl))
+    if mask is not None:
+        mask = contiguous(cast(mask, torch.float32))
+        if tuple(mask.shape) != (N, Cc, H, W):
+            raise ValueError(f"conv input-gradient mask shape {tuple(mask.shape)} != {(N, Cc, H, W)}")
+    _conv_call(1, dyc, wc, dx, (N, Cc, H, W, O, KH, KW, OH, OW, s[0], s[1], pt, pl), mask=mask)
     return dx
 
 

@@ -420,9 +420,14 @@ def test_rowfused_argmax_ties_and_misaligned_rows(C):
 
 
 @pytest.mark.parametrize("N,C,H,O,k,stride,padding", [(2, 3, 32, 64, 3, 1, "VALID"), (3, 64, 30, 64, 3, 2, "VALID"),
-                                                      (2, 64, 14, 128, 3, 2, "VALID"), (2, 5, 11, 7, 3, 2, "SAME")])
+                                                      (2, 64, 14, 128, 3, 2, "VALID"), (2, 5, 11, 7, 3, 2, "SAME"),
+                                                      (3, 9, 13, 300, 5, 3, "SAME"), (2, 16, 9, 24, 4, 1, "SAME"),
+                                                      (2, 8, 12, 16, 3, 3, "SAME"), (1, 240, 6, 8, 3, 1, "VALID")])
 def test_conv2d_tensor_core_path(N, C, H, O, k, stride, padding):
-    """bf16 tcgen05 convolutions against the oracle with the same operand rounding."""
+    """bf16 tcgen05 convolutions against the oracle with the same operand rounding: the
+    implicit GEMM (several column tiles at O = 300, strides 1-3, SAME padding with
+    even and odd kernels) and, above 2048 taps x channels (C = 240, 3 x 3), the GEMM over
+    staged operands."""
     from b200 import ops
     from oracle import evaluator as O_
 
@@ -442,6 +447,66 @@ def test_conv2d_tensor_core_path(N, C, H, O, k, stride, padding):
         dw = ops.op_conv2d_weight_grad(T(x), T(dy), target_shape=list(w.shape), **kw)
         dw_ref = O_.execute_op("Conv2DWeightGrad", x, dy, target_shape=list(w.shape), contraction_rounding="bf16", **kw)
         np.testing.assert_allclose(to_np(dw), dw_ref, rtol=1e-3, atol=2e-3 * np.abs(dw_ref).max())
+    finally:
+        ops.Config.conv_dtype = "f32"
+
+
+@pytest.mark.parametrize("N,C,H,O,stride,padding", [(4, 3, 32, 64, 1, "VALID"), (3, 64, 30, 64, 2, "VALID"),
+                                                    (2, 64, 14, 128, 2, "VALID"), (2, 6, 10, 20, 2, "SAME")])
+def test_conv2d_fused_epilogues(N, C, H, O, stride, padding):
+    """Implicit-GEMM convolution epilogues: relu(Conv2D) from the forward kernel, and
+    Conv2DInputGrad * (pre > 0) from the input-gradient kernel, against the oracle's
+    bf16-operand convolutions followed by the same elementwise ops. The forward with the
+    epilogue also equals the unfused forward then Relu, bit for bit."""
+    from b200 import _lib as L
+    from b200 import ops
+    from oracle import evaluator as O_
+
+    r = rng(15)
+    x = r.standard_normal((N, C, H, H), dtype=np.float32)
+    w = (r.standard_normal((O, C, 3, 3)) * np.sqrt(2.0 / (C * 9))).astype(np.float32)
+    kw = dict(stride=[stride, stride], padding=padding)
+    ops.Config.conv_dtype = "bf16"
+    try:
+        n0 = L.launch_count()
+        y = ops.op_conv2d(T(x), T(w), relu=True, **kw)
+        assert L.launch_count() - n0 == 1  # one implicit-GEMM launch, no staging
+        y_plain = ops.op_conv2d(T(x), T(w), **kw)
+        assert torch.equal(y, torch.where(y_plain > 0, y_plain, torch.zeros_like(y_plain)))
+        pre = O_.execute_op("Conv2D", x, w, contraction_rounding="bf16", **kw)
+        ref = np.maximum(pre, 0)
+        np.testing.assert_allclose(to_np(y), ref, rtol=1e-3, atol=1e-3 * np.abs(ref).max())
+        # the input gradient masked by a pre-activation of the input's shape
+        dy = r.standard_normal(pre.shape, dtype=np.float32)
+        m = r.standard_normal(x.shape, dtype=np.float32)
+        dx = ops.op_conv2d_input_grad(T(dy), T(w), target_shape=list(x.shape), mask=T(m), **kw)
+        dx_ref = O_.execute_op("Conv2DInputGrad", dy, w, target_shape=list(x.shape), contraction_rounding="bf16", **kw)
+        dx_ref = dx_ref * (m > 0)
+        np.testing.assert_allclose(to_np(dx), dx_ref, rtol=1e-3, atol=1e-3 * np.abs(dx_ref).max())
+        assert (to_np(dx)[m <= 0] == 0).all()
+    finally:
+        ops.Config.conv_dtype = "f32"
+
+
+def test_conv2d_implicit_gemm_bounds():
+    """Shapes the implicit GEMM does not take are reported (2048 taps x channels at most),
+    and a fused epilogue for them raises instead of running anything else."""
+    from b200 import _lib as L
+    from b200 import ops
+    from b200.errors import UnimplementedMathError
+
+    lib = L.lib()
+    assert lib.b200_conv2d_igemm_supported(0, 2, 227, 8, 8, 16, 3, 3, 6, 6, 1, 1, 0, 0) == 1  # 2043 taps x channels
+    assert lib.b200_conv2d_igemm_supported(0, 2, 228, 8, 8, 16, 3, 3, 6, 6, 1, 1, 0, 0) == 0  # 2052
+    assert lib.b200_conv2d_igemm_supported(1, 2, 16, 8, 8, 228, 3, 3, 6, 6, 1, 1, 0, 0) == 0  # dgrad: O x taps
+    assert lib.b200_conv2d_igemm_supported(2, 2, 228, 8, 8, 16, 3, 3, 6, 6, 1, 1, 0, 0) == 0  # wgrad: C x taps
+    ops.Config.conv_dtype = "bf16"
+    try:
+        x = torch.zeros(1, 228, 8, 8, device="cuda")
+        w = torch.zeros(4, 228, 3, 3, device="cuda")
+        with pytest.raises(UnimplementedMathError):
+            ops.op_conv2d(x, w, stride=[1, 1], padding="VALID", relu=True)
+        assert ops.op_conv2d(x, w, stride=[1, 1], padding="VALID").shape == (1, 4, 6, 6)  # staged GEMM path
     finally:
         ops.Config.conv_dtype = "f32"
 
