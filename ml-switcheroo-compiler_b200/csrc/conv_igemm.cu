@@ -1,35 +1,43 @@
 // Conv2D forward / input gradient / weight gradient as implicit GEMMs on the tcgen05
 // tensor cores: the im2col operand is never materialised in HBM. Producer warps gather
-// each 128 x 64 operand tile straight from the fp32 NCHW activations (and the fp32 OIHW
-// weights), round it to bf16 and write it into shared memory in the 128-byte swizzled
-// K-major layout the UMMA descriptors read; one thread issues tcgen05.mma into a
-// double-buffered TMEM accumulator; four epilogue warps write the fp32 result in NCHW
-// with the activation / mask fused. Replaces Conv2D (numpy/eager/conv.py:462-489),
-// Conv2DInputGrad (conv.py:634-697) and Conv2DWeightGrad (conv.py:699-764); padding is
+// each 128 x 64 operand tile straight from the fp32 NCHW activations, round it to bf16
+// and write it into shared memory in the 128-byte swizzled K-major layout the UMMA
+// descriptors read; one thread issues tcgen05.mma into a double-buffered TMEM
+// accumulator; four epilogue warps write the fp32 result in NCHW with the activation /
+// mask fused. Replaces Conv2D (numpy/eager/conv.py:462-489), Conv2DInputGrad
+// (conv.py:634-697) and Conv2DWeightGrad (conv.py:699-764); padding is
 // _compute_conv2d_padding_values (conv.py:590-633), passed in as (pt, pl).
 //
-// The three GEMMs (rows M, columns Nc, reduction K; kappa orders taps outermost):
+// The three GEMMs (rows M, columns Nc, reduction K; the reduction index runs over taps
+// outermost):
 //   fwd   rows = output pixels (n, oh, ow)   cols = o   K = (i, j, c)
 //         A[m, k] = x[n, c, oh*sh - pt + i, ow*sw - pl + j]      B[o, k] = w[o, c, i, j]
-//         epilogue: y[n, o, oh, ow] = acc  (optionally relu(acc))
-//   dgrad rows = input pixels (n, h, w)      cols = c   K = (i, j, o)
-//         A[m, k] = dy[n, o, (h + pt - i) / sh, (w + pl - j) / sw]  (0 unless both divide
-//                   exactly and land inside the output)           B[c, k] = w[o, c, i, j]
-//         epilogue: dx[n, c, h, w] = acc  (optionally acc * (mask[n, c, h, w] > 0): the
-//                   ReLU VJP of the layer below)
+//         epilogue: y = acc, or relu(acc)
+//   dgrad rows = input pixels (n, h, w) of one stride-parity class (h % sh, w % sw): only
+//         the taps with i = (h + pt) mod sh and j = (w + pl) mod sw reach such a pixel, so
+//         each class is a dense GEMM over its own taps (at stride 2 a quarter of the taps)
+//         cols = c   K = (class taps, o)
+//         A[m, k] = dy[n, o, (h + pt - i) / sh, (w + pl - j) / sw]   B[c, k] = w[o, c, i, j]
+//         epilogue: dx = acc, or acc * (mask > 0) (the ReLU VJP of the layer below)
 //   wgrad rows = taps (i, j, c)              cols = o   K = output pixels q = (n, oh, ow),
-//         split over CTAs in chunks of 64-multiples
+//         split over CTAs in multiples of 64
 //         A[t, q] = x[n, c, oh*sh - pt + i, ow*sw - pl + j]       B[o, q] = dy[n, o, oh, ow]
 //         epilogue: per-split partials [split][o][tap], then a fixed-order sum into
-//                   dw[o, c, i, j] (deterministic, no float atomics)
+//         dw[o, c, i, j] (deterministic, no float atomics)
 //
 // Persistent kernel, one CTA per SM, 416 threads:
-//   warps 0-7   producers: gather, round to bf16, st.shared.v4 into the stage ring
-//               (16-byte pieces XORed by row & 7: the TMA 128-byte swizzle), then
-//               fence.proxy.async and one mbarrier arrival per warp;
-//   warp 8      allocates TMEM and issues four 128 x BN x 16 MMAs per 64-wide K block;
+//   warps 0-7   producers. fwd / dgrad: two groups of four warps take alternate 64-wide
+//               K blocks (two blocks in flight per SM); a thread owns one tile row and
+//               gathers its 64 values with clamped, unconditional loads (a masked-off
+//               element reads the tensor's first element and is replaced by zero), so all
+//               64 loads are in flight together. The weights (B) are gathered once per CTA
+//               into shared memory and stay resident. wgrad: one group of eight warps
+//               gathers A and B of each block. Pieces of 16 bytes are XORed by row & 7 (the
+//               TMA 128-byte swizzle); then fence.proxy.async and one mbarrier arrival per
+//               warp;
+//   warp 8      allocates TMEM and issues four 128 x BN x 16 MMAs per K block;
 //   warps 9-12  epilogue, one TMEM lane quarter each (warp % 4), lane = GEMM row, so a
-//               store of one column covers 32 consecutive pixels (coalesced in NCHW).
+//               store of one column covers 32 consecutive pixels.
 // Every mbarrier wait is bounded; a warp whose wait gives up stops, and the CTA winds down
 // (the MMA warp drains its MMAs before TMEM is freed).
 #include <algorithm>
@@ -49,20 +57,31 @@ constexpr int THREADS = (PROD_WARPS + 1 + 4) * 32;
 constexpr int BM = 128, BK = 64;
 constexpr uint32_t A_BYTES = BM * BK * 2;
 constexpr int KTAB_MAX = 2048;          // taps x channels one table holds
+constexpr int MAX_CLS = 16;             // stride-parity classes of the input gradient (sh * sw)
 constexpr uint32_t SMEM_LIMIT = 232448;  // opt-in dynamic shared memory per CTA
 
 struct Args {
   int N, C, H, W, O, KH, KW, OH, OW, sh, sw, pt, pl;
   int P, HW;                  // OH * OW, H * W
-  int M, Nc, K;               // GEMM rows, columns, reduction length (wgrad: N * P)
+  int M, Nc, K;               // fwd / wgrad: GEMM rows, columns, reduction length (wgrad: N * P)
   int BN, BNT;                // column tile (multiple of 16, <= 256); its TMEM stride (multiple of 32)
-  int tiles_m, tiles_n, splits, items;
+  int tiles_n, splits, items;
   int lq;                     // wgrad: reduction elements per split (multiple of 64)
-  int ktab;                   // table entries: fwd / dgrad K, wgrad M
+  int ktab;                   // table entries
   int stages;
-  uint32_t stage_bytes;       // A_BYTES + BN * 128
+  uint32_t stage_bytes;       // fwd / dgrad: A_BYTES; wgrad: A_BYTES + BN * 128
+  uint32_t resb_off;          // fwd / dgrad: byte offset of the resident B operand
+  int kb_total;               // fwd / dgrad: K blocks over all classes
   uint32_t tmem_cols;
   int relu;                   // fwd: relu epilogue
+  // classes: fwd / wgrad one (the whole GEMM); dgrad sh * sw parity classes
+  int ncls, max_tiles;        // item = (tile * ncls + class) * tiles_n + column tile
+  int cls_ph[MAX_CLS], cls_pw[MAX_CLS];
+  int cls_hc[MAX_CLS], cls_wc[MAX_CLS];  // dgrad: rows and columns of the class per image
+  int cls_m[MAX_CLS];         // GEMM rows of the class
+  int cls_k[MAX_CLS];         // reduction length of the class
+  int cls_ktab[MAX_CLS];      // first table entry
+  int cls_kb[MAX_CLS];        // first K block in the resident B operand
   const float* asrc;          // fwd: x    dgrad: dy   wgrad: x
   const float* bsrc;          // fwd: w    dgrad: w    wgrad: dy
   float* out;                 // fwd: y    dgrad: dx   wgrad: partials [splits][O][M]
@@ -77,25 +96,42 @@ __device__ __forceinline__ bool warp_wait(uint64_t* bar, uint32_t parity, int sl
   return __shfl_sync(0xffffffffu, ok ? 1 : 0, 0) != 0;
 }
 
-__device__ __forceinline__ float ldf(const float* p) { return __ldg(p); }
-
-// 8 fp32 values -> one 16-byte piece of bf16
-__device__ __forceinline__ void put8(uint32_t addr, const float (&v)[8]) {
+__device__ __forceinline__ void put8(uint32_t addr, const float* v) {
   st_shared_v4(addr, pack_bf16(v[0], v[1]), pack_bf16(v[2], v[3]), pack_bf16(v[4], v[5]), pack_bf16(v[6], v[7]));
 }
 
-// item -> (m tile, n tile, split)
-__device__ __forceinline__ void item_of(const Args& a, int it, int& mt, int& nt, int& sp) {
-  const int per = a.tiles_m * a.tiles_n;
-  sp = it / per;
-  const int r = it - sp * per;
-  mt = r / a.tiles_n;
-  nt = r - mt * a.tiles_n;
+// item -> class, row tile, column tile, split; false for an empty slot (a class with fewer
+// tiles than the largest). Every role walks the same items and skips the same slots.
+struct Item {
+  int cls, mt, nt, sp;
+};
+__device__ __forceinline__ bool item_of(const Args& a, int it, Item& r) {
+  const int per = a.max_tiles * a.ncls * a.tiles_n;
+  r.sp = it / per;
+  int x = it - r.sp * per;
+  r.nt = x % a.tiles_n;
+  x /= a.tiles_n;
+  r.cls = x % a.ncls;
+  r.mt = x / a.ncls;
+  return r.mt * BM < a.cls_m[r.cls];
 }
-__device__ __forceinline__ int kblocks_of(const Args& a, int sp) {
-  if (a.splits == 1 && a.lq == 0) return (a.K + BK - 1) / BK;
-  const int q0 = sp * a.lq, q1 = min(a.K, q0 + a.lq);
+__device__ __forceinline__ int kblocks_of(const Args& a, const Item& r) {
+  if (a.lq == 0) return (a.cls_k[r.cls] + BK - 1) / BK;
+  const int q0 = r.sp * a.lq, q1 = min(a.K, q0 + a.lq);
   return (q1 - q0 + BK - 1) / BK;
+}
+
+// fwd / dgrad: the A element of a row (base offset, position hb / wb) and reduction
+// index k of its class (table entry {offset, dh, dw, B offset}), bounds-checked against
+// the source image (x for fwd, dy for dgrad); a masked-off element loads asrc[0]
+template <int MODE>
+__device__ __forceinline__ float gather_a(const Args& a, const int4* tab, bool rv, int base, int hb, int wb, int k, int kend) {
+  const int4 t = tab[min(k, kend - 1)];
+  const int h = hb + t.y, w = wb + t.z;
+  const int HH = MODE == FWD ? a.H : a.OH, WW = MODE == FWD ? a.W : a.OW;
+  const bool ok = rv && k < kend && (unsigned)h < (unsigned)HH && (unsigned)w < (unsigned)WW;
+  const float x = __ldg(a.asrc + (ok ? base + t.x : 0));
+  return ok ? x : 0.f;
 }
 
 template <int MODE>
@@ -103,7 +139,8 @@ __global__ void __launch_bounds__(THREADS, 1) conv_igemm_kernel(const __grid_con
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* sStages = smem;
-  int4* tab = reinterpret_cast<int4*>(smem + (uint32_t)a.stages * a.stage_bytes);
+  uint8_t* sResB = smem + a.resb_off;
+  int4* tab = reinterpret_cast<int4*>(smem + a.resb_off + (MODE == WGRAD ? 0u : (uint32_t)a.kb_total * a.tiles_n * a.BN * 128u));
   uint64_t* full = reinterpret_cast<uint64_t*>(tab + a.ktab);
   uint64_t* empty = full + a.stages;
   uint64_t* acc_full = empty + a.stages;  // [2]
@@ -112,22 +149,38 @@ __global__ void __launch_bounds__(THREADS, 1) conv_igemm_kernel(const __grid_con
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drained + 1);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  constexpr int GROUPS = MODE == WGRAD ? 1 : 2;  // producer groups taking alternate K blocks
+  constexpr int GROUP_WARPS = PROD_WARPS / GROUPS;
 
-  // tap table: fwd {c*HW + i*W + j, i, j, c*KH*KW + t}, kappa = t*C + c
-  //            dgrad {o*P, i, j, o*C*KH*KW + t},     kappa = t*O + o
-  //            wgrad {c*HW + i*W + j, i, j, 0},      row   = t*C + c
-  for (int k = threadIdx.x; k < a.ktab; k += blockDim.x) {
-    const int inner = MODE == DGRAD ? a.O : a.C;
-    const int t = k / inner, ch = k - t * inner;
-    const int i = t / a.KW, j = t - i * a.KW;
-    int4 e;
-    if (MODE == DGRAD) e = make_int4(ch * a.P, i, j, ch * a.C * a.KH * a.KW + t);
-    else e = make_int4(ch * a.HW + i * a.W + j, i, j, ch * a.KH * a.KW + t);
-    tab[k] = e;
+  // Tables (entry per reduction index k of each class):
+  //   fwd   k = t*C + c:               {c*HW + i*W + j, i, j, c*KH*KW + t}
+  //   dgrad class (ph, pw), k = u*O + o over the class taps u = (i, j):
+  //                                    {o*P + dh*OW + dw, dh, dw, o*C*KH*KW + i*KW + j}
+  //                                    dh = (ph + pt - i) / sh (exact), dw likewise
+  //   wgrad row = t*C + c:             {c*HW + i*W + j, i, j, 0}
+  if (MODE == DGRAD) {
+    for (int c = 0; c < a.ncls; ++c) {
+      const int ph = a.cls_ph[c], pw = a.cls_pw[c];
+      const int i0 = (ph + a.pt) % a.sh, j0 = (pw + a.pl) % a.sw;
+      const int nj = (a.KW - j0 + a.sw - 1) / a.sw;
+      for (int k = threadIdx.x; k < a.cls_k[c]; k += blockDim.x) {
+        const int u = k / a.O, o = k - u * a.O;
+        const int ui = u / nj, uj = u - ui * nj;
+        const int i = i0 + ui * a.sh, j = j0 + uj * a.sw;
+        const int dh = (ph + a.pt - i) / a.sh, dw = (pw + a.pl - j) / a.sw;
+        tab[a.cls_ktab[c] + k] = make_int4(o * a.P + dh * a.OW + dw, dh, dw, o * a.C * a.KH * a.KW + i * a.KW + j);
+      }
+    }
+  } else {
+    for (int k = threadIdx.x; k < a.ktab; k += blockDim.x) {
+      const int t = k / a.C, ch = k - t * a.C;
+      const int i = t / a.KW, j = t - i * a.KW;
+      tab[k] = make_int4(ch * a.HW + i * a.W + j, i, j, ch * a.KH * a.KW + t);
+    }
   }
   if (threadIdx.x == 0) {
     for (int s = 0; s < a.stages; ++s) {
-      mbar_init(&full[s], PROD_WARPS);
+      mbar_init(&full[s], GROUP_WARPS);
       mbar_init(&empty[s], 1);
     }
     for (int b = 0; b < 2; ++b) {
@@ -146,107 +199,100 @@ __global__ void __launch_bounds__(THREADS, 1) conv_igemm_kernel(const __grid_con
   tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
 
+  if constexpr (MODE != WGRAD) {
+    // resident B: [K blocks of all classes][column tiles][BN rows x 64] bf16, gathered once.
+    // A pass keeps 8 pieces per thread in flight (64 loads), then stores them.
+    if (warp < PROD_WARPS) {
+      const int pieces_per_kb = a.tiles_n * a.BN * 8;
+      const int total = a.kb_total * pieces_per_kb;
+      const int KHW = a.KH * a.KW;
+      for (int p0 = threadIdx.x; p0 < total; p0 += 8 * PROD_THREADS) {
+        float v[64];
+#pragma unroll
+        for (int u = 0; u < 8; ++u) {
+          const int p = min(p0 + u * PROD_THREADS, total - 1);
+          const int kbg = p / pieces_per_kb, rem = p - kbg * pieces_per_kb;
+          const int col = rem >> 3, j = rem & 7;  // column over all column tiles
+          int c = 0;
+          while (c + 1 < a.ncls && a.cls_kb[c + 1] <= kbg) ++c;
+          const int kk0 = (kbg - a.cls_kb[c]) * BK + j * 8;
+#pragma unroll
+          for (int e = 0; e < 8; ++e) {
+            const int k = kk0 + e;
+            const int4 t = tab[a.cls_ktab[c] + min(k, a.cls_k[c] - 1)];
+            const bool ok = col < a.Nc && k < a.cls_k[c];
+            const float x = __ldg(a.bsrc + (ok ? (MODE == FWD ? col * a.K + t.w : t.w + col * KHW) : 0));
+            v[u * 8 + e] = ok ? x : 0.f;
+          }
+        }
+#pragma unroll
+        for (int u = 0; u < 8; ++u) {
+          const int p = p0 + u * PROD_THREADS;
+          if (p < total) {
+            const int kbg = p / pieces_per_kb, rem = p - kbg * pieces_per_kb;
+            const int col = rem >> 3, j = rem & 7;
+            const int nt = col / a.BN, rr = col - nt * a.BN;
+            put8(smem_u32(sResB) + (uint32_t)((kbg * a.tiles_n + nt) * a.BN) * 128u + swz(rr, j), &v[u * 8]);
+          }
+        }
+      }
+      fence_proxy_async_smem();
+    }
+    __syncthreads();
+  }
+
   if (warp < PROD_WARPS) {
     // ------------------------------------------------------------ producers
-    const int pt = threadIdx.x;
+    const int grp = warp / GROUP_WARPS, gw = warp % GROUP_WARPS;
     uint32_t L = 0;
     bool ok = true;
     for (int it = blockIdx.x; it < a.items && ok; it += gridDim.x) {
-      int mt, nt, sp;
-      item_of(a, it, mt, nt, sp);
-      const int m0 = mt * BM, n0 = nt * a.BN;
-      const int nkb = kblocks_of(a, sp);
+      Item r;
+      if (!item_of(a, it, r)) continue;
+      const int m0 = r.mt * BM, n0 = r.nt * a.BN;
+      const int nkb = kblocks_of(a, r);
       if constexpr (MODE != WGRAD) {
-        // A: thread = row r, pieces j = half, half + 2, half + 4, half + 6
-        const int r = pt & (BM - 1), half = pt >> 7;
-        const int m = m0 + r;
-        const bool rv = m < a.M;
-        int base = 0, hb = 0, wb = 0;
-        if (rv) {
-          if (MODE == FWD) {
-            const int n = m / a.P, p = m - n * a.P, oh = p / a.OW, ow = p - oh * a.OW;
-            hb = oh * a.sh - a.pt;
-            wb = ow * a.sw - a.pl;
-            base = n * a.C * a.HW + hb * a.W + wb;
-          } else {
-            const int n = m / a.HW, hw = m - n * a.HW, h = hw / a.W, w = hw - h * a.W;
-            hb = h + a.pt;
-            wb = w + a.pl;
-            base = n * a.O * a.P;
-          }
+        // A: thread = tile row, all 8 pieces of it
+        const int row = threadIdx.x & (BM - 1);
+        const int m = m0 + row;
+        const bool rv = m < a.cls_m[r.cls];
+        const int mm = rv ? m : 0;
+        int base, hb, wb;
+        if (MODE == FWD) {
+          const int n = mm / a.P, p = mm - n * a.P, oh = p / a.OW, ow = p - oh * a.OW;
+          hb = oh * a.sh - a.pt;
+          wb = ow * a.sw - a.pl;
+          base = n * a.C * a.HW + hb * a.W + wb;
+        } else {
+          const int hc = a.cls_hc[r.cls], wc = a.cls_wc[r.cls];
+          const int n = mm / (hc * wc), rem = mm - n * (hc * wc), hh = rem / wc, ww = rem - hh * wc;
+          hb = hh;
+          wb = ww;
+          base = n * a.O * a.P + hh * a.OW + ww;
         }
+        const int4* ctab = tab + a.cls_ktab[r.cls];
+        const int kend = a.cls_k[r.cls];
         for (int kb = 0; kb < nkb; ++kb, ++L) {
+          if ((int)(L % GROUPS) != grp) continue;
           const int s = (int)(L % (uint32_t)a.stages);
           if (!warp_wait(&empty[s], ((L / (uint32_t)a.stages) & 1) ^ 1, 0)) {
             ok = false;
             break;
           }
           const uint32_t sA = smem_u32(sStages + (uint32_t)s * a.stage_bytes);
-          const uint32_t sB = sA + A_BYTES;
-          float v[32];
+          float v[64];
 #pragma unroll
-          for (int ue = 0; ue < 32; ++ue) {
-            const int k = kb * BK + (half + 2 * (ue >> 3)) * 8 + (ue & 7);
-            float x = 0.f;
-            if (rv && k < a.K) {
-              const int4 t = tab[k];
-              if (MODE == FWD) {
-                const int h = hb + t.y, w = wb + t.z;
-                if ((unsigned)h < (unsigned)a.H && (unsigned)w < (unsigned)a.W) x = ldf(a.asrc + (base + t.x));
-              } else {
-                int th = hb - t.y, tw = wb - t.z;
-                bool in = th >= 0 && tw >= 0;
-                if (a.sh == 2) {
-                  in = in && !(th & 1);
-                  th >>= 1;
-                } else if (a.sh != 1) {
-                  const int qq = th / a.sh;
-                  in = in && qq * a.sh == th;
-                  th = qq;
-                }
-                if (a.sw == 2) {
-                  in = in && !(tw & 1);
-                  tw >>= 1;
-                } else if (a.sw != 1) {
-                  const int qq = tw / a.sw;
-                  in = in && qq * a.sw == tw;
-                  tw = qq;
-                }
-                in = in && th < a.OH && tw < a.OW;
-                if (in) x = ldf(a.asrc + (base + t.x + th * a.OW + tw));
-              }
-            }
-            v[ue] = x;
-          }
+          for (int e = 0; e < 64; ++e) v[e] = gather_a<MODE>(a, ctab, rv, base, hb, wb, kb * BK + e, kend);
 #pragma unroll
-          for (int u = 0; u < 4; ++u)
-            st_shared_v4(sA + swz(r, half + 2 * u), pack_bf16(v[8 * u], v[8 * u + 1]), pack_bf16(v[8 * u + 2], v[8 * u + 3]),
-                         pack_bf16(v[8 * u + 4], v[8 * u + 5]), pack_bf16(v[8 * u + 6], v[8 * u + 7]));
-          // B: weights, rows = GEMM columns n0 .. n0 + BN
-          for (int cid = pt; cid < a.BN * 8; cid += PROD_THREADS) {
-            const int rr = cid >> 3, j = cid & 7;
-            const int col = n0 + rr;
-            float wv[8];
-#pragma unroll
-            for (int e = 0; e < 8; ++e) {
-              const int k = kb * BK + j * 8 + e;
-              float x = 0.f;
-              if (col < a.Nc && k < a.K) {
-                const int4 t = tab[k];
-                x = ldf(a.bsrc + (MODE == FWD ? col * a.K + t.w : t.w + col * a.KH * a.KW));
-              }
-              wv[e] = x;
-            }
-            put8(sB + swz(rr, j), wv);
-          }
+          for (int j = 0; j < 8; ++j) put8(sA + swz(row, j), &v[8 * j]);
           fence_proxy_async_smem();
           __syncwarp();
           if (lane == 0) mbar_arrive(&full[s]);
         }
       } else {
-        // wgrad: piece j = lane & 7 (8 consecutive output pixels q), rows lane >> 3 + 4 * warp + 32 u
-        const int j = lane & 7, rsub = (lane >> 3) + 4 * warp;
-        const int qs = sp * a.lq, qe = min(a.K, qs + a.lq);
+        // wgrad: piece j = lane & 7 (8 consecutive output pixels q), rows (lane >> 3) + 4 warp + 32 u
+        const int j = lane & 7, rsub = (lane >> 3) + 4 * gw;
+        const int qs = r.sp * a.lq, qe = min(a.K, qs + a.lq);
         for (int kb = 0; kb < nkb; ++kb, ++L) {
           const int s = (int)(L % (uint32_t)a.stages);
           if (!warp_wait(&empty[s], ((L / (uint32_t)a.stages) & 1) ^ 1, 0)) {
@@ -280,31 +326,47 @@ __global__ void __launch_bounds__(THREADS, 1) conv_igemm_kernel(const __grid_con
               }
             }
           }
-          float v[4][8];
+          float v[32], dv[32];
 #pragma unroll
           for (int u = 0; u < 4; ++u) {
             const int row = m0 + rsub + 32 * u;
             const bool rv = row < a.M;
-            int4 t = make_int4(0, 0, 0, 0);
-            if (rv) t = tab[row];
+            const int4 t = tab[min(row, a.M - 1)];
 #pragma unroll
             for (int e = 0; e < 8; ++e) {
-              float x = 0.f;
-              if (rv && ((qv >> e) & 1)) {
-                const int h = hq[e] + t.y, w = wq[e] + t.z;
-                if ((unsigned)h < (unsigned)a.H && (unsigned)w < (unsigned)a.W) x = ldf(a.asrc + (xo[e] + t.x));
-              }
-              v[u][e] = x;
+              const int h = hq[e] + t.y, w = wq[e] + t.z;
+              const bool okk = rv && ((qv >> e) & 1) && (unsigned)h < (unsigned)a.H && (unsigned)w < (unsigned)a.W;
+              const float x = __ldg(a.asrc + (okk ? xo[e] + t.x : 0));
+              v[u * 8 + e] = okk ? x : 0.f;
             }
           }
 #pragma unroll
-          for (int u = 0; u < 4; ++u) put8(sA + swz(rsub + 32 * u, j), v[u]);
-          for (int rr = rsub; rr < a.BN; rr += 32) {
-            const int o = n0 + rr;
-            float dv[8];
+          for (int u = 0; u < 4; ++u) {
+            const int o = n0 + rsub + 32 * u;
+            const bool ov = rsub + 32 * u < a.BN && o < a.Nc;
 #pragma unroll
-            for (int e = 0; e < 8; ++e) dv[e] = (o < a.Nc && ((qv >> e) & 1)) ? ldf(a.bsrc + (dq[e] + o * a.P)) : 0.f;
-            put8(sB + swz(rr, j), dv);
+            for (int e = 0; e < 8; ++e) {
+              const bool okk = ov && ((qv >> e) & 1);
+              const float x = __ldg(a.bsrc + (okk ? dq[e] + o * a.P : 0));
+              dv[u * 8 + e] = okk ? x : 0.f;
+            }
+          }
+#pragma unroll
+          for (int u = 0; u < 4; ++u) put8(sA + swz(rsub + 32 * u, j), &v[8 * u]);
+#pragma unroll
+          for (int u = 0; u < 4; ++u)
+            if (rsub + 32 * u < a.BN) put8(sB + swz(rsub + 32 * u, j), &dv[8 * u]);
+          // B rows beyond 128 (BN > 128): a second pass
+          for (int rr = rsub + 128; rr < a.BN; rr += 32) {
+            const int o = n0 + rr;
+            float ev[8];
+#pragma unroll
+            for (int e = 0; e < 8; ++e) {
+              const bool okk = o < a.Nc && ((qv >> e) & 1);
+              const float x = __ldg(a.bsrc + (okk ? dq[e] + o * a.P : 0));
+              ev[e] = okk ? x : 0.f;
+            }
+            put8(sB + swz(rr, j), ev);
           }
           fence_proxy_async_smem();
           __syncwarp();
@@ -318,10 +380,10 @@ __global__ void __launch_bounds__(THREADS, 1) conv_igemm_kernel(const __grid_con
       const uint32_t idesc = (1u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(a.BN >> 3) << 17) | ((uint32_t)(BM >> 4) << 24);
       uint32_t L = 0, T = 0;
       bool ok = true, issued = false;
-      for (int it = blockIdx.x; it < a.items && ok; it += gridDim.x, ++T) {
-        int mt, nt, sp;
-        item_of(a, it, mt, nt, sp);
-        const int nkb = kblocks_of(a, sp);
+      for (int it = blockIdx.x; it < a.items && ok; it += gridDim.x) {
+        Item r;
+        if (!item_of(a, it, r)) continue;
+        const int nkb = kblocks_of(a, r);
         const uint32_t b = T & 1;
         if (!mbar_wait(&acc_empty[b], ((T >> 1) & 1) ^ 1, 32)) break;
         tc_fence_after();
@@ -334,16 +396,19 @@ __global__ void __launch_bounds__(THREADS, 1) conv_igemm_kernel(const __grid_con
           }
           tc_fence_after();
           const uint32_t sA = smem_u32(sStages + (uint32_t)s * a.stage_bytes);
+          const uint32_t sB = MODE == WGRAD ? sA + A_BYTES
+                                            : smem_u32(sResB) + (uint32_t)(((a.cls_kb[r.cls] + kb) * a.tiles_n + r.nt) * a.BN) * 128u;
 #pragma unroll
           for (int k = 0; k < 4; ++k) {
             const uint64_t ad = smem_desc(sA + k * 32, 16, 1024);
-            const uint64_t bd = smem_desc(sA + A_BYTES + k * 32, 16, 1024);
+            const uint64_t bd = smem_desc(sB + k * 32, 16, 1024);
             mma_bf16(d, ad, bd, idesc, (kb > 0 || k > 0) ? 1u : 0u);
           }
           issued = true;
           mma_commit(&empty[s]);
         }
         if (ok) mma_commit(&acc_full[b]);
+        ++T;
       }
       // every MMA this thread issued has completed before TMEM can be freed
       if (issued) {
@@ -356,36 +421,49 @@ __global__ void __launch_bounds__(THREADS, 1) conv_igemm_kernel(const __grid_con
     const int q = warp & 3;
     uint32_t T = 0;
     bool ok = true;
-    for (int it = blockIdx.x; it < a.items && ok; it += gridDim.x, ++T) {
-      int mt, nt, sp;
-      item_of(a, it, mt, nt, sp);
+    for (int it = blockIdx.x; it < a.items && ok; it += gridDim.x) {
+      Item r;
+      if (!item_of(a, it, r)) continue;
       const uint32_t b = T & 1;
       ok = warp_wait(&acc_full[b], (T >> 1) & 1, 64);
+      ++T;
       if (!ok) break;
       tc_fence_after();
-      const int m = mt * BM + q * 32 + lane;  // this lane's GEMM row
-      const bool rv = m < a.M;
-      int64_t obase = 0, ostride = 0;
-      if (rv) {
+      const int m = r.mt * BM + q * 32 + lane;  // this lane's GEMM row
+      const bool rv = m < a.cls_m[r.cls];
+      int64_t obase, ostride;
+      {
+        const int mm = rv ? m : 0;
         if (MODE == FWD) {
-          const int n = m / a.P, p = m - n * a.P;
+          const int n = mm / a.P, p = mm - n * a.P;
           obase = (int64_t)n * a.O * a.P + p;
           ostride = a.P;
         } else if (MODE == DGRAD) {
-          const int n = m / a.HW, hw = m - n * a.HW;
-          obase = (int64_t)n * a.C * a.HW + hw;
+          const int hc = a.cls_hc[r.cls], wc = a.cls_wc[r.cls];
+          const int n = mm / (hc * wc), rem = mm - n * (hc * wc), hh = rem / wc, ww = rem - hh * wc;
+          const int h = a.cls_ph[r.cls] + a.sh * hh, w = a.cls_pw[r.cls] + a.sw * ww;
+          obase = (int64_t)n * a.C * a.HW + h * a.W + w;
           ostride = a.HW;
         } else {
-          obase = (int64_t)sp * a.O * a.M + m;
+          obase = (int64_t)r.sp * a.O * a.M + mm;
           ostride = a.M;
         }
       }
       const uint32_t tb = tmem_base + ((uint32_t)(q * 32) << 16) + b * (uint32_t)a.BNT;
-      const int n0 = nt * a.BN;
+      const int n0 = r.nt * a.BN;
       const int ncols = min(a.BN, a.Nc - n0);
       for (int c0 = 0; c0 < ncols; c0 += 32) {
         uint32_t v[32];
         tmem_ld32_issue(tb + (uint32_t)c0, v);
+        const int nn = min(32, ncols - c0);
+        float* __restrict__ dst = a.out + obase + (int64_t)(n0 + c0) * ostride;
+        float mv[32];
+        if (MODE == DGRAD && a.mask != nullptr) {
+          // the chunk's 32 mask values are all loaded before its first store
+          const float* __restrict__ mk = a.mask + obase + (int64_t)(n0 + c0) * ostride;
+#pragma unroll
+          for (int i = 0; i < 32; ++i) mv[i] = __ldg(mk + (rv && i < nn ? (int64_t)i * ostride : 0));
+        }
         tmem_wait(v);
         if (c0 + 32 >= ncols) {  // last TMEM read of this item: hand the accumulator back
           tc_fence_before();
@@ -393,13 +471,10 @@ __global__ void __launch_bounds__(THREADS, 1) conv_igemm_kernel(const __grid_con
           if (lane == 0) mbar_arrive(&acc_empty[b]);
         }
         if (!rv) continue;
-        float* dst = a.out + obase + (int64_t)(n0 + c0) * ostride;
-        const int nn = min(32, ncols - c0);
         if (MODE == DGRAD && a.mask != nullptr) {
-          const float* mk = a.mask + obase + (int64_t)(n0 + c0) * ostride;
 #pragma unroll
           for (int i = 0; i < 32; ++i)
-            if (i < nn) dst[(int64_t)i * ostride] = __uint_as_float(v[i]) * (__ldg(mk + (int64_t)i * ostride) > 0.f ? 1.f : 0.f);
+            if (i < nn) dst[(int64_t)i * ostride] = __uint_as_float(v[i]) * (mv[i] > 0.f ? 1.f : 0.f);
         } else if (MODE == FWD && a.relu) {
 #pragma unroll
           for (int i = 0; i < 32; ++i) {
@@ -442,8 +517,9 @@ struct Plan {
   const char* why;
 };
 
-// Shapes the kernel handles: 32-bit element offsets (tensors up to 2^30 elements), at most KTAB_MAX
-// taps x channels, at most 256 x 255 column tiles.
+// Shapes the kernel handles: 32-bit element offsets (tensors up to 2^30 elements), at most
+// KTAB_MAX taps x channels, at most 16 stride-parity classes, and (fwd / dgrad) the whole
+// bf16 weight operand resident in shared memory beside two A stages.
 static Plan plan(int mode, int64_t N, int64_t C, int64_t H, int64_t W, int64_t O, int64_t KH, int64_t KW, int64_t OH, int64_t OW,
                  int64_t sh, int64_t sw, int64_t pt, int64_t pl) {
   Plan p{};
@@ -451,6 +527,10 @@ static Plan plan(int mode, int64_t N, int64_t C, int64_t H, int64_t W, int64_t O
   const int64_t lim = (int64_t)1 << 30;
   if (N * C * H * W > lim || N * O * OH * OW > lim || O * C * KH * KW > lim) {
     p.why = "tensor above 2^30 elements";
+    return p;
+  }
+  if (mode == DGRAD && sh * sw > MAX_CLS) {
+    p.why = "stride above the parity-class limit";
     return p;
   }
   Args& a = p.a;
@@ -474,17 +554,47 @@ static Plan plan(int mode, int64_t N, int64_t C, int64_t H, int64_t W, int64_t O
   uint32_t cols = 32;
   while (cols < (uint32_t)(2 * a.BNT)) cols <<= 1;
   a.tmem_cols = cols;
-  a.tiles_m = (int)ceil_div(M, BM);
   a.tiles_n = (int)ceil_div(Nc, a.BN);
-  if (a.tiles_n > 255) {
-    p.why = "too many column tiles";
+  int64_t max_tiles = 0;
+  if (mode == DGRAD) {
+    a.ncls = (int)(sh * sw);
+    int koff = 0, kboff = 0;
+    for (int c = 0; c < a.ncls; ++c) {
+      const int ph = (int)(c / sw), pw = (int)(c % sw);
+      const int hc = ph < H ? (int)ceil_div(H - ph, sh) : 0, wc = pw < W ? (int)ceil_div(W - pw, sw) : 0;
+      const int i0 = (int)((ph + pt) % sh), j0 = (int)((pw + pl) % sw);
+      const int ni = i0 < KH ? (int)ceil_div(KH - i0, sh) : 0, nj = j0 < KW ? (int)ceil_div(KW - j0, sw) : 0;
+      a.cls_ph[c] = ph, a.cls_pw[c] = pw, a.cls_hc[c] = hc, a.cls_wc[c] = wc;
+      a.cls_k[c] = (int)(O * ni * nj);
+      a.cls_m[c] = a.cls_k[c] > 0 ? (int)(N * hc * wc) : 0;  // pixels no tap reaches are zero-filled by the caller
+      a.cls_ktab[c] = koff;
+      a.cls_kb[c] = kboff;
+      koff += a.cls_k[c];
+      kboff += (int)ceil_div(a.cls_k[c], BK);
+      max_tiles = std::max<int64_t>(max_tiles, ceil_div(a.cls_m[c], BM));
+    }
+    a.kb_total = kboff;
+  } else {
+    a.ncls = 1;
+    a.cls_ph[0] = a.cls_pw[0] = 0;
+    a.cls_hc[0] = a.cls_wc[0] = 1;
+    a.cls_m[0] = (int)M;
+    a.cls_k[0] = (int)(mode == WGRAD ? 0 : K);
+    a.cls_ktab[0] = 0;
+    a.cls_kb[0] = 0;
+    a.kb_total = mode == WGRAD ? 0 : (int)ceil_div(K, BK);
+    max_tiles = ceil_div(M, BM);
+  }
+  a.max_tiles = (int)max_tiles;
+  if (a.tiles_n > 255 || max_tiles < 1) {
+    p.why = "tile count";
     return p;
   }
   const int sms = num_sms();
   if (mode == WGRAD) {
     // split the pixel reduction so that about two items per SM exist
     const int64_t kblocks = ceil_div(K, BK);
-    const int64_t per = (int64_t)a.tiles_m * a.tiles_n;
+    const int64_t per = max_tiles * a.tiles_n;
     int64_t S = std::max<int64_t>(1, std::min<int64_t>(kblocks, ceil_div(2 * (int64_t)sms, per)));
     const int64_t kb_per = ceil_div(kblocks, S);
     a.lq = (int)(kb_per * BK);
@@ -494,20 +604,27 @@ static Plan plan(int mode, int64_t N, int64_t C, int64_t H, int64_t W, int64_t O
     a.splits = 1;
     a.lq = 0;
   }
-  const int64_t items = (int64_t)a.tiles_m * a.tiles_n * a.splits;
+  const int64_t items = max_tiles * a.ncls * a.tiles_n * a.splits;
   if (items > lim) {
     p.why = "too many tiles";
     return p;
   }
   a.items = (int)items;
-  a.stage_bytes = A_BYTES + (uint32_t)a.BN * 128u;
-  const size_t fixed = 1024 + (size_t)a.ktab * 16 + 64 * 8 + 16;
-  int st = (int)std::min<size_t>(8, (SMEM_LIMIT - fixed) / a.stage_bytes);
-  if (st < 2) {
-    p.why = "shared memory";
+  size_t resb = 0;
+  if (mode == WGRAD) {
+    a.stage_bytes = A_BYTES + (uint32_t)a.BN * 128u;
+  } else {
+    a.stage_bytes = A_BYTES;
+    resb = (size_t)a.kb_total * a.tiles_n * a.BN * 128;
+  }
+  const size_t fixed = 1024 + resb + (size_t)a.ktab * 16 + 64 * 8 + 16;
+  if (fixed + 2 * (size_t)a.stage_bytes > SMEM_LIMIT) {
+    p.why = "shared memory (weights too large to stay resident)";
     return p;
   }
+  const int st = (int)std::min<size_t>(8, (SMEM_LIMIT - fixed) / a.stage_bytes);
   a.stages = st;
+  a.resb_off = (uint32_t)st * a.stage_bytes;
   p.smem = fixed + (size_t)st * a.stage_bytes;
   p.ok = true;
   return p;
@@ -586,9 +703,17 @@ extern "C" int b200_conv2d_dgrad_igemm(const float* dy, const float* w, const fl
     set_error("conv2d_dgrad_igemm: unsupported shape (%s)", p.why);
     return B200_ERR_UNSUPPORTED;
   }
+  cudaStream_t s = as_stream(stream);
+  // pixels that no tap reaches (a class without taps: stride above the kernel size) are zero
+  for (int c = 0; c < p.a.ncls; ++c)
+    if (p.a.cls_k[c] == 0) {
+      cudaMemsetAsync(dx, 0, (size_t)N * C * H * W * 4, s);
+      if ((rc = check_launch("conv2d_dgrad_igemm(zero)"))) return rc;
+      break;
+    }
   p.a.relu = 0;
   p.a.asrc = dy, p.a.bsrc = w, p.a.out = dx, p.a.mask = mask;
-  return launch<DGRAD>(p.a, p.smem, as_stream(stream));
+  return launch<DGRAD>(p.a, p.smem, s);
 }
 
 extern "C" int b200_conv2d_wgrad_igemm(const float* x, const float* dy, float* dw, int64_t N, int64_t C, int64_t H, int64_t W,

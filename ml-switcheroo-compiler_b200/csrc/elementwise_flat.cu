@@ -209,14 +209,29 @@ __global__ void __launch_bounds__(THREADS) ew_prog_kernel(const __grid_constant_
     for (int v = 0; v < VG; ++v) R[i][v] = 0.f;
   const int64_t ng = (P.n + VG - 1) / VG;
   const int nins = p.n_ins;
+  const int nin = p.n_in;
   for (int64_t q = blockIdx.x * (int64_t)THREADS + threadIdx.x; q < ng; q += (int64_t)gridDim.x * THREADS) {
     const int64_t base = q * VG;
     const bool full = base + VG <= P.n;
+    // every input of the group is loaded up front, so the loads of all inputs are in
+    // flight together; LOAD instructions then read these registers
+    float IN[B200_EW_MAX_IN][VG];
+#pragma unroll
+    for (int j = 0; j < B200_EW_MAX_IN; ++j)
+      if (j < nin) loadv<VG>(P, j, base, full, IN[j]);
     for (int i = 0; i < nins; ++i) {
       const b200_ew_ins I = p.ins[i];
       float x[VG], y[VG], res[VG];
       if (I.op == B200_EW_LOAD) {
-        loadv<VG>(P, I.a, base, full, res);
+        switch (I.a) {
+#define B200_LDIN(j)                                                  \
+  case j:                                                             \
+    _Pragma("unroll") for (int v = 0; v < VG; ++v) res[v] = IN[j][v]; \
+    break;
+          B200_LDIN(0) B200_LDIN(1) B200_LDIN(2) B200_LDIN(3) B200_LDIN(4) B200_LDIN(5) B200_LDIN(6) B200_LDIN(7)
+#undef B200_LDIN
+          default: break;
+        }
         wr<NREG>(R, I.dst, res);
         continue;
       }

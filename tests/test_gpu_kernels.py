@@ -422,12 +422,14 @@ def test_rowfused_argmax_ties_and_misaligned_rows(C):
 @pytest.mark.parametrize("N,C,H,O,k,stride,padding", [(2, 3, 32, 64, 3, 1, "VALID"), (3, 64, 30, 64, 3, 2, "VALID"),
                                                       (2, 64, 14, 128, 3, 2, "VALID"), (2, 5, 11, 7, 3, 2, "SAME"),
                                                       (3, 9, 13, 300, 5, 3, "SAME"), (2, 16, 9, 24, 4, 1, "SAME"),
-                                                      (2, 8, 12, 16, 3, 3, "SAME"), (1, 240, 6, 8, 3, 1, "VALID")])
+                                                      (2, 8, 12, 16, 3, 3, "SAME"), (1, 240, 6, 8, 3, 1, "VALID"),
+                                                      (1, 2, 10, 3, 1, 2, "VALID"), (1, 2, 9, 3, 2, 4, "SAME")])
 def test_conv2d_tensor_core_path(N, C, H, O, k, stride, padding):
     """bf16 tcgen05 convolutions against the oracle with the same operand rounding: the
-    implicit GEMM (several column tiles at O = 300, strides 1-3, SAME padding with
-    even and odd kernels) and, above 2048 taps x channels (C = 240, 3 x 3), the GEMM over
-    staged operands."""
+    implicit GEMM (several column tiles at O = 300, strides 1-4, SAME padding with
+    even and odd kernels, strides above the kernel size so that some input pixels get no
+    gradient) and, above 2048 taps x channels (C = 240, 3 x 3), the GEMM over staged
+    operands."""
     from b200 import ops
     from oracle import evaluator as O_
 
