@@ -421,29 +421,32 @@ int b200_conv2d_wgrad_tc(const float* x, const float* dy, float* dw, int64_t N, 
                          int64_t KH, int64_t KW, int64_t OH, int64_t OW, int64_t sh, int64_t sw, int64_t pt, int64_t pl,
                          void* workspace, size_t workspace_bytes, void* stream);
 
-/* The same three convolutions as implicit GEMMs on the tcgen05 tensor cores: the bf16
- * operand tiles are gathered from the fp32 NCHW / OIHW tensors straight into shared memory
- * (no im2col buffer), fp32 accumulation, fp32 results written in NCHW / OIHW.
+/* The same three convolutions as implicit GEMMs on the tcgen05 tensor cores (no im2col
+ * buffer): bf16 operand tiles built in shared memory, fp32 accumulation, fp32 results in
+ * NCHW / OIHW.
  *   b200_conv2d_fwd_igemm:   y = Conv2D(x, w)   (numpy/eager/conv.py:462-489); relu != 0
  *                            writes relu(y) instead (the Relu node that follows, fused)
  *   b200_conv2d_dgrad_igemm: dx = Conv2DInputGrad(dy, w) (conv.py:634-697); a non-null
  *                            mask [N, C, H, W] writes dx * (mask > 0) instead (the Multiply
  *                            by the Greater(pre, 0) mask of the ReLU VJP, fused)
- *   b200_conv2d_wgrad_igemm: dw = Conv2DWeightGrad(x, dy) (conv.py:699-764): per-split
- *                            partial sums in `workspace`, then a fixed-order sum
- * b200_conv2d_igemm_supported(op, ...) is 1 when the shape fits the kernel (op 0 fwd,
- * 1 dgrad, 2 wgrad: tensors up to 2^30 elements, at most 2048 taps x channels); the entry
- * points return B200_ERR_UNSUPPORTED otherwise. */
+ *   b200_conv2d_wgrad_igemm: dw = Conv2DWeightGrad(x, dy) (conv.py:699-764)
+ * `workspace` (16-byte aligned, b200_conv2d_igemm_workspace_bytes(op, ...) bytes, op 0
+ * fwd, 1 dgrad, 2 wgrad) holds the bf16 channels-last copy of x (fwd) or dy (dgrad) the
+ * tiles are copied from, or the per-split partial sums of the weight gradient.
+ * b200_conv2d_igemm_supported(op, ...) is 1 when the shape fits the kernel (tensors up to
+ * 2^30 elements, at most 2048 reduction indices with channels padded to 8, the bf16
+ * weights resident in shared memory); the entry points return B200_ERR_UNSUPPORTED
+ * otherwise. */
 int b200_conv2d_igemm_supported(int op, int64_t N, int64_t C, int64_t H, int64_t W, int64_t O, int64_t KH, int64_t KW,
                                 int64_t OH, int64_t OW, int64_t sh, int64_t sw, int64_t pt, int64_t pl);
-size_t b200_conv2d_wgrad_igemm_workspace_bytes(int64_t N, int64_t C, int64_t H, int64_t W, int64_t O, int64_t KH, int64_t KW,
-                                               int64_t OH, int64_t OW, int64_t sh, int64_t sw, int64_t pt, int64_t pl);
+size_t b200_conv2d_igemm_workspace_bytes(int op, int64_t N, int64_t C, int64_t H, int64_t W, int64_t O, int64_t KH, int64_t KW,
+                                         int64_t OH, int64_t OW, int64_t sh, int64_t sw, int64_t pt, int64_t pl);
 int b200_conv2d_fwd_igemm(const float* x, const float* w, float* y, int64_t N, int64_t C, int64_t H, int64_t W, int64_t O,
                           int64_t KH, int64_t KW, int64_t OH, int64_t OW, int64_t sh, int64_t sw, int64_t pt, int64_t pl,
-                          int relu, void* stream);
+                          int relu, void* workspace, size_t workspace_bytes, void* stream);
 int b200_conv2d_dgrad_igemm(const float* dy, const float* w, const float* mask, float* dx, int64_t N, int64_t C, int64_t H,
                             int64_t W, int64_t O, int64_t KH, int64_t KW, int64_t OH, int64_t OW, int64_t sh, int64_t sw,
-                            int64_t pt, int64_t pl, void* stream);
+                            int64_t pt, int64_t pl, void* workspace, size_t workspace_bytes, void* stream);
 int b200_conv2d_wgrad_igemm(const float* x, const float* dy, float* dw, int64_t N, int64_t C, int64_t H, int64_t W, int64_t O,
                             int64_t KH, int64_t KW, int64_t OH, int64_t OW, int64_t sh, int64_t sw, int64_t pt, int64_t pl,
                             void* workspace, size_t workspace_bytes, void* stream);

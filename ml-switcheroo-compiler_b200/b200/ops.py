@@ -1149,13 +1149,15 @@ def _conv_call(kind: int, a: torch.Tensor, b: torch.Tensor, out: torch.Tensor, d
         L.call(names[kind], L.F32, a.data_ptr(), b.data_ptr(), out.data_ptr(), *dims, stream_ptr())
         return
     if L.lib().b200_conv2d_igemm_supported(kind, *dims):
+        ws_bytes = int(L.lib().b200_conv2d_igemm_workspace_bytes(kind, *dims))
+        ws = torch.empty(max(16, ws_bytes), dtype=torch.uint8, device=device())
         if kind == 0:
-            L.call("b200_conv2d_fwd_igemm", a.data_ptr(), b.data_ptr(), out.data_ptr(), *dims, 1 if relu else 0, stream_ptr())
+            L.call("b200_conv2d_fwd_igemm", a.data_ptr(), b.data_ptr(), out.data_ptr(), *dims, 1 if relu else 0, ws.data_ptr(),
+                   ws_bytes, stream_ptr())
         elif kind == 1:
-            L.call("b200_conv2d_dgrad_igemm", a.data_ptr(), b.data_ptr(), _ptr(mask), out.data_ptr(), *dims, stream_ptr())
+            L.call("b200_conv2d_dgrad_igemm", a.data_ptr(), b.data_ptr(), _ptr(mask), out.data_ptr(), *dims, ws.data_ptr(),
+                   ws_bytes, stream_ptr())
         else:
-            ws_bytes = int(L.lib().b200_conv2d_wgrad_igemm_workspace_bytes(*dims))
-            ws = torch.empty(max(1, ws_bytes), dtype=torch.uint8, device=device())
             L.call("b200_conv2d_wgrad_igemm", a.data_ptr(), b.data_ptr(), out.data_ptr(), *dims, ws.data_ptr(), ws_bytes,
                    stream_ptr())
         return

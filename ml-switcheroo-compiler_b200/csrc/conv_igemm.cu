@@ -1,45 +1,47 @@
 // Conv2D forward / input gradient / weight gradient as implicit GEMMs on the tcgen05
-// tensor cores: the im2col operand is never materialised in HBM. Producer warps gather
-// each 128 x 64 operand tile straight from the fp32 NCHW activations, round it to bf16
-// and write it into shared memory in the 128-byte swizzled K-major layout the UMMA
-// descriptors read; one thread issues tcgen05.mma into a double-buffered TMEM
-// accumulator; four epilogue warps write the fp32 result in NCHW with the activation /
-// mask fused. Replaces Conv2D (numpy/eager/conv.py:462-489), Conv2DInputGrad
-// (conv.py:634-697) and Conv2DWeightGrad (conv.py:699-764); padding is
-// _compute_conv2d_padding_values (conv.py:590-633), passed in as (pt, pl).
+// tensor cores: the im2col operand is never materialised in HBM. Operand tiles are built
+// in shared memory in the 128-byte swizzled K-major layout the UMMA descriptors read; one
+// thread issues tcgen05.mma into a double-buffered TMEM accumulator; four epilogue warps
+// write the fp32 result in NCHW with the activation / mask fused. Replaces Conv2D
+// (numpy/eager/conv.py:462-489), Conv2DInputGrad (conv.py:634-697) and Conv2DWeightGrad
+// (conv.py:699-764); padding is _compute_conv2d_padding_values (conv.py:590-633), passed
+// in as (pt, pl).
 //
-// The three GEMMs (rows M, columns Nc, reduction K; the reduction index runs over taps
-// outermost):
-//   fwd   rows = output pixels (n, oh, ow)   cols = o   K = (i, j, c)
+// The three GEMMs (rows M, columns Nc, reduction K):
+//   fwd   rows = output pixels (n, oh, ow)   cols = o   K = (i, j, c), c padded to Cp = 8k
 //         A[m, k] = x[n, c, oh*sh - pt + i, ow*sw - pl + j]      B[o, k] = w[o, c, i, j]
 //         epilogue: y = acc, or relu(acc)
 //   dgrad rows = input pixels (n, h, w) of one stride-parity class (h % sh, w % sw): only
 //         the taps with i = (h + pt) mod sh and j = (w + pl) mod sw reach such a pixel, so
 //         each class is a dense GEMM over its own taps (at stride 2 a quarter of the taps)
-//         cols = c   K = (class taps, o)
+//         cols = c   K = (class taps, o), o padded to Op = 8k
 //         A[m, k] = dy[n, o, (h + pt - i) / sh, (w + pl - j) / sw]   B[c, k] = w[o, c, i, j]
 //         epilogue: dx = acc, or acc * (mask > 0) (the ReLU VJP of the layer below)
-//   wgrad rows = taps (i, j, c)              cols = o   K = output pixels q = (n, oh, ow),
+//   wgrad rows = taps (i, j, c), c padded to Cp  cols = o   K = output pixels q = (n, oh, ow),
 //         split over CTAs in multiples of 64
 //         A[t, q] = x[n, c, oh*sh - pt + i, ow*sw - pl + j]       B[o, q] = dy[n, o, oh, ow]
 //         epilogue: per-split partials [split][o][tap], then a fixed-order sum into
 //         dw[o, c, i, j] (deterministic, no float atomics)
 //
-// Persistent kernel, one CTA per SM, 416 threads:
-//   warps 0-7   producers. fwd / dgrad: two groups of four warps take alternate 64-wide
-//               K blocks (two blocks in flight per SM); a thread owns one tile row and
-//               gathers its 64 values with clamped, unconditional loads (a masked-off
-//               element reads the tensor's first element and is replaced by zero), so all
-//               64 loads are in flight together. The weights (B) are gathered once per CTA
-//               into shared memory and stay resident. wgrad: one group of eight warps
-//               gathers A and B of each block. Pieces of 16 bytes are XORed by row & 7 (the
-//               TMA 128-byte swizzle); then fence.proxy.async and one mbarrier arrival per
-//               warp;
-//   warp 8      allocates TMEM and issues four 128 x BN x 16 MMAs per K block;
-//   warps 9-12  epilogue, one TMEM lane quarter each (warp % 4), lane = GEMM row, so a
-//               store of one column covers 32 consecutive pixels.
-// Every mbarrier wait is bounded; a warp whose wait gives up stops, and the CTA winds down
-// (the MMA warp drains its MMAs before TMEM is freed).
+// fwd / dgrad: a repack kernel first writes the source (x, or dy) as bf16 NHWC with the
+// channels padded to a multiple of 8 into the caller's workspace, so 8 consecutive
+// reduction indices of one tap are 16 contiguous bytes. Each producer warp then builds a
+// whole 128 x 64 A tile with 16-byte cp.async copies (zero-filled where a tap falls
+// outside the image), waits for its own copies, and arrives on the stage's barrier; each
+// producer warp owns one stage and the warps take K blocks round-robin, so up to eight
+// tiles are in flight per SM. The weights (B) are gathered once per CTA into shared memory
+// and stay resident.
+// wgrad: x and dy both get channels-last bf16 copies (dy's channels padded to 64); the
+// pixel index is the GEMM's K, so both operands are MN-major tiles: for each of the 64
+// pixels of a K block, 128-byte rows of 64 GEMM rows (taps x channels) of A and of 64
+// output channels of B, copied by the same one-warp-per-stage cp.async producers.
+//
+// Persistent kernel, one CTA per SM, 416 threads: warps 0-7 producers, warp 8 allocates
+// TMEM and issues four 128 x BN x 16 MMAs per K block, warps 9-12 epilogue (one TMEM lane
+// quarter each, warp % 4; lane = GEMM row, so a store of one column covers 32
+// consecutive pixels). Pieces of 16 bytes are XORed by row & 7 (the TMA 128-byte
+// swizzle). Every mbarrier wait is bounded; a warp whose wait gives up stops, and the CTA
+// winds down (the MMA warp drains its MMAs before TMEM is freed).
 #include <algorithm>
 
 #include "tc_common.cuh"
@@ -56,18 +58,20 @@ constexpr int MMA_WARP = PROD_WARPS;
 constexpr int THREADS = (PROD_WARPS + 1 + 4) * 32;
 constexpr int BM = 128, BK = 64;
 constexpr uint32_t A_BYTES = BM * BK * 2;
-constexpr int KTAB_MAX = 2048;          // taps x channels one table holds
+constexpr int KTAB_MAX = 2048;          // reduction indices (fwd / dgrad) or taps x channels (wgrad) one table holds
 constexpr int MAX_CLS = 16;             // stride-parity classes of the input gradient (sh * sw)
 constexpr uint32_t SMEM_LIMIT = 232448;  // opt-in dynamic shared memory per CTA
 
 struct Args {
   int N, C, H, W, O, KH, KW, OH, OW, sh, sw, pt, pl;
   int P, HW;                  // OH * OW, H * W
-  int M, Nc, K;               // fwd / wgrad: GEMM rows, columns, reduction length (wgrad: N * P)
+  int M, Nc, K;               // GEMM rows, columns, reduction length (wgrad: N * P; fwd: taps * Cp)
+  int CP;                     // fwd / wgrad: Cp, dgrad: Op (channels of the NHWC x or dy copy, a multiple of 8)
+  int OPW;                    // wgrad: channels of the NHWC dy copy (O padded to a multiple of 64)
   int BN, BNT;                // column tile (multiple of 16, <= 256); its TMEM stride (multiple of 32)
   int tiles_n, splits, items;
   int lq;                     // wgrad: reduction elements per split (multiple of 64)
-  int ktab;                   // table entries
+  int ktab;                   // table entries (fwd / dgrad: 8-element chunks; wgrad: tap rows)
   int stages;
   uint32_t stage_bytes;       // fwd / dgrad: A_BYTES; wgrad: A_BYTES + BN * 128
   uint32_t resb_off;          // fwd / dgrad: byte offset of the resident B operand
@@ -75,15 +79,17 @@ struct Args {
   uint32_t tmem_cols;
   int relu;                   // fwd: relu epilogue
   // classes: fwd / wgrad one (the whole GEMM); dgrad sh * sw parity classes
-  int ncls, max_tiles;        // item = (tile * ncls + class) * tiles_n + column tile
+  int ncls, max_tiles;        // item = ((split * max_tiles + tile) * ncls + class) * tiles_n + column tile
   int cls_ph[MAX_CLS], cls_pw[MAX_CLS];
   int cls_hc[MAX_CLS], cls_wc[MAX_CLS];  // dgrad: rows and columns of the class per image
+  int cls_nj[MAX_CLS];        // dgrad: class taps along w
   int cls_m[MAX_CLS];         // GEMM rows of the class
-  int cls_k[MAX_CLS];         // reduction length of the class
+  int cls_k[MAX_CLS];         // reduction length of the class (a multiple of 8)
   int cls_ktab[MAX_CLS];      // first table entry
   int cls_kb[MAX_CLS];        // first K block in the resident B operand
-  const float* asrc;          // fwd: x    dgrad: dy   wgrad: x
-  const float* bsrc;          // fwd: w    dgrad: w    wgrad: dy
+  const __nv_bfloat16* an;    // fwd / wgrad: x, dgrad: dy, as bf16 NHWC [n][h][w][CP]
+  const __nv_bfloat16* bn;    // wgrad: dy as bf16 NHWC [n][oh][ow][OPW]
+  const float* bsrc;          // fwd / dgrad: w (fp32 OIHW)
   float* out;                 // fwd: y    dgrad: dx   wgrad: partials [splits][O][M]
   const float* mask;          // dgrad: dx *= (mask > 0) when not null
 };
@@ -99,6 +105,13 @@ __device__ __forceinline__ bool warp_wait(uint64_t* bar, uint32_t parity, int sl
 __device__ __forceinline__ void put8(uint32_t addr, const float* v) {
   st_shared_v4(addr, pack_bf16(v[0], v[1]), pack_bf16(v[2], v[3]), pack_bf16(v[4], v[5]), pack_bf16(v[6], v[7]));
 }
+
+// 16-byte copy global -> shared through L2 (the little L1 left beside the shared memory
+// would not hold the taps' reuse anyway); src_bytes = 0 writes zeros (nothing is read)
+__device__ __forceinline__ void cp16(uint32_t dst, const void* src, uint32_t src_bytes) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(dst), "l"(src), "r"(src_bytes) : "memory");
+}
+__device__ __forceinline__ void cp_wait_all() { asm volatile("cp.async.wait_all;" ::: "memory"); }
 
 // item -> class, row tile, column tile, split; false for an empty slot (a class with fewer
 // tiles than the largest). Every role walks the same items and skips the same slots.
@@ -121,17 +134,27 @@ __device__ __forceinline__ int kblocks_of(const Args& a, const Item& r) {
   return (q1 - q0 + BK - 1) / BK;
 }
 
-// fwd / dgrad: the A element of a row (base offset, position hb / wb) and reduction
-// index k of its class (table entry {offset, dh, dw, B offset}), bounds-checked against
-// the source image (x for fwd, dy for dgrad); a masked-off element loads asrc[0]
-template <int MODE>
-__device__ __forceinline__ float gather_a(const Args& a, const int4* tab, bool rv, int base, int hb, int wb, int k, int kend) {
-  const int4 t = tab[min(k, kend - 1)];
-  const int h = hb + t.y, w = wb + t.z;
-  const int HH = MODE == FWD ? a.H : a.OH, WW = MODE == FWD ? a.W : a.OW;
-  const bool ok = rv && k < kend && (unsigned)h < (unsigned)HH && (unsigned)w < (unsigned)WW;
-  const float x = __ldg(a.asrc + (ok ? base + t.x : 0));
-  return ok ? x : 0.f;
+// fp32 NCHW [N, C, HW] -> bf16 NHWC [N, HW, Cp] (channels >= C zero): a thread writes 8
+// channels of one pixel (one 16-byte store); consecutive threads take consecutive pixels,
+// so every fp32 read of a warp is one contiguous run
+__global__ void __launch_bounds__(256) nchw_to_nhwc_bf16_kernel(const float* __restrict__ src, __nv_bfloat16* __restrict__ dst,
+                                                                int64_t N, int C, int64_t HW, int Cp) {
+  const int cg = Cp / 8;
+  const int64_t total = N * HW * cg;
+  for (int64_t e = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; e < total; e += (int64_t)gridDim.x * blockDim.x) {
+    const int g = (int)(e / (N * HW));  // channel group outermost: a warp reads 32 consecutive pixels
+    const int64_t pix = e - (int64_t)g * (N * HW);
+    const int64_t n = pix / HW, hw = pix - n * HW;
+    const float* s = src + (n * C) * HW + hw;
+    float v[8];
+#pragma unroll
+    for (int k = 0; k < 8; ++k) {
+      const int c = g * 8 + k;
+      v[k] = c < C ? __ldg(s + (int64_t)c * HW) : 0.f;
+    }
+    *reinterpret_cast<uint4*>(dst + pix * Cp + g * 8) =
+        make_uint4(pack_bf16(v[0], v[1]), pack_bf16(v[2], v[3]), pack_bf16(v[4], v[5]), pack_bf16(v[6], v[7]));
+  }
 }
 
 template <int MODE>
@@ -149,38 +172,37 @@ __global__ void __launch_bounds__(THREADS, 1) conv_igemm_kernel(const __grid_con
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drained + 1);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  constexpr int GROUPS = MODE == WGRAD ? 1 : 2;  // producer groups taking alternate K blocks
-  constexpr int GROUP_WARPS = PROD_WARPS / GROUPS;
 
-  // Tables (entry per reduction index k of each class):
-  //   fwd   k = t*C + c:               {c*HW + i*W + j, i, j, c*KH*KW + t}
-  //   dgrad class (ph, pw), k = u*O + o over the class taps u = (i, j):
-  //                                    {o*P + dh*OW + dw, dh, dw, o*C*KH*KW + i*KW + j}
-  //                                    dh = (ph + pt - i) / sh (exact), dw likewise
-  //   wgrad row = t*C + c:             {c*HW + i*W + j, i, j, 0}
+  // Tables:
+  //   fwd   per 8-element chunk k0 = t*Cp + c0 of the reduction:  {(i*W + j)*Cp + c0, i, j, 0}
+  //   wgrad the same per 8-row chunk t*Cp + c0 of the GEMM rows
+  //   dgrad per chunk of class (ph, pw), k0 = u*Op + o0 over the class taps u = (i, j):
+  //                              {(dh*OW + dw)*Op + o0, dh, dw, 0},  dh = (ph + pt - i) / sh (exact)
   if (MODE == DGRAD) {
     for (int c = 0; c < a.ncls; ++c) {
       const int ph = a.cls_ph[c], pw = a.cls_pw[c];
       const int i0 = (ph + a.pt) % a.sh, j0 = (pw + a.pl) % a.sw;
-      const int nj = (a.KW - j0 + a.sw - 1) / a.sw;
-      for (int k = threadIdx.x; k < a.cls_k[c]; k += blockDim.x) {
-        const int u = k / a.O, o = k - u * a.O;
+      const int nj = a.cls_nj[c];
+      for (int kc = threadIdx.x; kc < a.cls_k[c] / 8; kc += blockDim.x) {
+        const int k0 = kc * 8;
+        const int u = k0 / a.CP, o0 = k0 - u * a.CP;
         const int ui = u / nj, uj = u - ui * nj;
         const int i = i0 + ui * a.sh, j = j0 + uj * a.sw;
         const int dh = (ph + a.pt - i) / a.sh, dw = (pw + a.pl - j) / a.sw;
-        tab[a.cls_ktab[c] + k] = make_int4(o * a.P + dh * a.OW + dw, dh, dw, o * a.C * a.KH * a.KW + i * a.KW + j);
+        tab[a.cls_ktab[c] + kc] = make_int4((dh * a.OW + dw) * a.CP + o0, dh, dw, 0);
       }
     }
   } else {
-    for (int k = threadIdx.x; k < a.ktab; k += blockDim.x) {
-      const int t = k / a.C, ch = k - t * a.C;
+    for (int kc = threadIdx.x; kc < a.ktab; kc += blockDim.x) {
+      const int k0 = kc * 8;
+      const int t = k0 / a.CP, c0 = k0 - t * a.CP;
       const int i = t / a.KW, j = t - i * a.KW;
-      tab[k] = make_int4(ch * a.HW + i * a.W + j, i, j, ch * a.KH * a.KW + t);
+      tab[kc] = make_int4((i * a.W + j) * a.CP + c0, i, j, 0);
     }
   }
   if (threadIdx.x == 0) {
     for (int s = 0; s < a.stages; ++s) {
-      mbar_init(&full[s], GROUP_WARPS);
+      mbar_init(&full[s], 1);  // one producer warp per stage
       mbar_init(&empty[s], 1);
     }
     for (int b = 0; b < 2; ++b) {
@@ -200,8 +222,10 @@ __global__ void __launch_bounds__(THREADS, 1) conv_igemm_kernel(const __grid_con
   const uint32_t tmem_base = *tmem_slot;
 
   if constexpr (MODE != WGRAD) {
-    // resident B: [K blocks of all classes][column tiles][BN rows x 64] bf16, gathered once.
-    // A pass keeps 8 pieces per thread in flight (64 loads), then stores them.
+    // resident B: [K blocks of all classes][column tiles][BN rows x 64] bf16, gathered once
+    // from the fp32 OIHW weights. A pass keeps 8 pieces per thread in flight (64 loads).
+    //   fwd:   B[o, k = t*Cp + c]            = w[o, c, i, j]   (0 for c >= C)
+    //   dgrad: B[c, k = u*Op + o] of a class = w[o, c, i, j]   (0 for o >= O)
     if (warp < PROD_WARPS) {
       const int pieces_per_kb = a.tiles_n * a.BN * 8;
       const int total = a.kb_total * pieces_per_kb;
@@ -212,16 +236,28 @@ __global__ void __launch_bounds__(THREADS, 1) conv_igemm_kernel(const __grid_con
         for (int u = 0; u < 8; ++u) {
           const int p = min(p0 + u * PROD_THREADS, total - 1);
           const int kbg = p / pieces_per_kb, rem = p - kbg * pieces_per_kb;
-          const int col = rem >> 3, j = rem & 7;  // column over all column tiles
+          const int col = rem >> 3, j8 = rem & 7;  // column over all column tiles
           int c = 0;
           while (c + 1 < a.ncls && a.cls_kb[c + 1] <= kbg) ++c;
-          const int kk0 = (kbg - a.cls_kb[c]) * BK + j * 8;
+          const int k0 = (kbg - a.cls_kb[c]) * BK + j8 * 8;  // chunk start within the class
+          int tap = 0, ch0 = 0;
+          if (MODE == FWD) {
+            tap = k0 / a.CP;
+            ch0 = k0 - tap * a.CP;
+          } else {
+            const int uu = k0 / a.CP, nj = a.cls_nj[c];
+            const int ui = uu / nj, uj = uu - ui * nj;
+            const int i = (a.cls_ph[c] + a.pt) % a.sh + ui * a.sh, j = (a.cls_pw[c] + a.pl) % a.sw + uj * a.sw;
+            tap = i * a.KW + j;
+            ch0 = k0 - uu * a.CP;
+          }
+          const bool kin = k0 < a.cls_k[c] && col < a.Nc;
 #pragma unroll
           for (int e = 0; e < 8; ++e) {
-            const int k = kk0 + e;
-            const int4 t = tab[a.cls_ktab[c] + min(k, a.cls_k[c] - 1)];
-            const bool ok = col < a.Nc && k < a.cls_k[c];
-            const float x = __ldg(a.bsrc + (ok ? (MODE == FWD ? col * a.K + t.w : t.w + col * KHW) : 0));
+            const int ch = ch0 + e;  // fwd: input channel c; dgrad: output channel o
+            const bool ok = kin && ch < (MODE == FWD ? a.C : a.O);
+            const int off = MODE == FWD ? (col * a.C + ch) * KHW + tap : (ch * a.C + col) * KHW + tap;
+            const float x = __ldg(a.bsrc + (ok ? off : 0));
             v[u * 8 + e] = ok ? x : 0.f;
           }
         }
@@ -230,9 +266,9 @@ __global__ void __launch_bounds__(THREADS, 1) conv_igemm_kernel(const __grid_con
           const int p = p0 + u * PROD_THREADS;
           if (p < total) {
             const int kbg = p / pieces_per_kb, rem = p - kbg * pieces_per_kb;
-            const int col = rem >> 3, j = rem & 7;
+            const int col = rem >> 3, j8 = rem & 7;
             const int nt = col / a.BN, rr = col - nt * a.BN;
-            put8(smem_u32(sResB) + (uint32_t)((kbg * a.tiles_n + nt) * a.BN) * 128u + swz(rr, j), &v[u * 8]);
+            put8(smem_u32(sResB) + (uint32_t)((kbg * a.tiles_n + nt) * a.BN) * 128u + swz(rr, j8), &v[u * 8]);
           }
         }
       }
@@ -243,7 +279,6 @@ __global__ void __launch_bounds__(THREADS, 1) conv_igemm_kernel(const __grid_con
 
   if (warp < PROD_WARPS) {
     // ------------------------------------------------------------ producers
-    const int grp = warp / GROUP_WARPS, gw = warp % GROUP_WARPS;
     uint32_t L = 0;
     bool ok = true;
     for (int it = blockIdx.x; it < a.items && ok; it += gridDim.x) {
@@ -252,122 +287,119 @@ __global__ void __launch_bounds__(THREADS, 1) conv_igemm_kernel(const __grid_con
       const int m0 = r.mt * BM, n0 = r.nt * a.BN;
       const int nkb = kblocks_of(a, r);
       if constexpr (MODE != WGRAD) {
-        // A: thread = tile row, all 8 pieces of it
-        const int row = threadIdx.x & (BM - 1);
-        const int m = m0 + row;
-        const bool rv = m < a.cls_m[r.cls];
-        const int mm = rv ? m : 0;
-        int base, hb, wb;
-        if (MODE == FWD) {
-          const int n = mm / a.P, p = mm - n * a.P, oh = p / a.OW, ow = p - oh * a.OW;
-          hb = oh * a.sh - a.pt;
-          wb = ow * a.sw - a.pl;
-          base = n * a.C * a.HW + hb * a.W + wb;
-        } else {
-          const int hc = a.cls_hc[r.cls], wc = a.cls_wc[r.cls];
-          const int n = mm / (hc * wc), rem = mm - n * (hc * wc), hh = rem / wc, ww = rem - hh * wc;
-          hb = hh;
-          wb = ww;
-          base = n * a.O * a.P + hh * a.OW + ww;
+        // K block L goes to warp L % stages into stage L % stages: every stage has one
+        // producer warp that refills it in order, so a parity wait can never pass a phase
+        // that is two uses ahead. Lane = rows lane + 32 q, all 8 chunks of each.
+        if (nkb <= 0) continue;
+        const uint32_t np = (uint32_t)a.stages;
+        const uint32_t first = L;
+        L += (uint32_t)nkb;
+        if ((uint32_t)warp >= np) continue;
+        uint32_t mine = first + ((uint32_t)warp + np - first % np) % np;
+        if (mine >= L) continue;
+        int base[4], hb[4], wb[4];
+        bool rv[4];
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {
+          const int m = m0 + lane + 32 * q;
+          rv[q] = m < a.cls_m[r.cls];
+          const int mm = rv[q] ? m : 0;
+          if (MODE == FWD) {
+            const int n = mm / a.P, p = mm - n * a.P, oh = p / a.OW, ow = p - oh * a.OW;
+            hb[q] = oh * a.sh - a.pt;
+            wb[q] = ow * a.sw - a.pl;
+            base[q] = ((n * a.H + hb[q]) * a.W + wb[q]) * a.CP;
+          } else {
+            const int hc = a.cls_hc[r.cls], wc = a.cls_wc[r.cls];
+            const int n = mm / (hc * wc), rem = mm - n * (hc * wc), hh = rem / wc, ww = rem - hh * wc;
+            hb[q] = hh;
+            wb[q] = ww;
+            base[q] = ((n * a.OH + hh) * a.OW + ww) * a.CP;
+          }
         }
         const int4* ctab = tab + a.cls_ktab[r.cls];
-        const int kend = a.cls_k[r.cls];
-        for (int kb = 0; kb < nkb; ++kb, ++L) {
-          if ((int)(L % GROUPS) != grp) continue;
-          const int s = (int)(L % (uint32_t)a.stages);
-          if (!warp_wait(&empty[s], ((L / (uint32_t)a.stages) & 1) ^ 1, 0)) {
+        const int nchunks = a.cls_k[r.cls] / 8;
+        const int HH = MODE == FWD ? a.H : a.OH, WW = MODE == FWD ? a.W : a.OW;
+        for (; mine < L; mine += np) {
+          const int kb = (int)(mine - first);
+          const int s = (int)(mine % (uint32_t)a.stages);
+          if (!warp_wait(&empty[s], ((mine / (uint32_t)a.stages) & 1) ^ 1, 0)) {
             ok = false;
             break;
           }
           const uint32_t sA = smem_u32(sStages + (uint32_t)s * a.stage_bytes);
-          float v[64];
 #pragma unroll
-          for (int e = 0; e < 64; ++e) v[e] = gather_a<MODE>(a, ctab, rv, base, hb, wb, kb * BK + e, kend);
+          for (int j8 = 0; j8 < 8; ++j8) {
+            const int kc = kb * 8 + j8;
+            const int4 t = ctab[min(kc, nchunks - 1)];
 #pragma unroll
-          for (int j = 0; j < 8; ++j) put8(sA + swz(row, j), &v[8 * j]);
+            for (int q = 0; q < 4; ++q) {
+              const int h = hb[q] + t.y, w = wb[q] + t.z;
+              const bool okk = rv[q] && kc < nchunks && (unsigned)h < (unsigned)HH && (unsigned)w < (unsigned)WW;
+              cp16(sA + swz(lane + 32 * q, j8), a.an + (okk ? base[q] + t.x : 0), okk ? 16u : 0u);
+            }
+          }
+          cp_wait_all();
           fence_proxy_async_smem();
           __syncwarp();
           if (lane == 0) mbar_arrive(&full[s]);
         }
       } else {
-        // wgrad: piece j = lane & 7 (8 consecutive output pixels q), rows (lane >> 3) + 4 warp + 32 u
-        const int j = lane & 7, rsub = (lane >> 3) + 4 * gw;
+        // wgrad: K block L (64 output pixels q) goes to warp L % stages into stage L % stages,
+        // as for fwd / dgrad. Both operands are MN-major (the pixel index q is K): for each
+        // q a 128-byte row holds 64 consecutive GEMM rows (taps x channels) of A, or 64
+        // output channels of B, copied from the channels-last copies of x and dy. Lane = q
+        // rows lane and lane + 32.
+        if (nkb <= 0) continue;
+        const uint32_t np = (uint32_t)a.stages;
+        const uint32_t first = L;
+        L += (uint32_t)nkb;
+        if ((uint32_t)warp >= np) continue;
+        uint32_t mine = first + ((uint32_t)warp + np - first % np) % np;
         const int qs = r.sp * a.lq, qe = min(a.K, qs + a.lq);
-        for (int kb = 0; kb < nkb; ++kb, ++L) {
-          const int s = (int)(L % (uint32_t)a.stages);
-          if (!warp_wait(&empty[s], ((L / (uint32_t)a.stages) & 1) ^ 1, 0)) {
+        const int mchunks = a.M / 8;  // M = taps * Cp
+        const int nb = a.BN / 64;     // 64-column blocks of B
+        for (; mine < L; mine += np) {
+          const int kb = (int)(mine - first);
+          const int s = (int)(mine % (uint32_t)a.stages);
+          if (!warp_wait(&empty[s], ((mine / (uint32_t)a.stages) & 1) ^ 1, 0)) {
             ok = false;
             break;
           }
           const uint32_t sA = smem_u32(sStages + (uint32_t)s * a.stage_bytes);
           const uint32_t sB = sA + A_BYTES;
-          // decode the 8 pixels q0 .. q0 + 7 once
-          const int q0 = qs + kb * BK + j * 8;
-          int xo[8], hq[8], wq[8], dq[8];
-          uint32_t qv = 0;
-          {
-            int n = q0 / a.P, p = q0 - n * a.P;
-            int oh = p / a.OW, ow = p - oh * a.OW;
 #pragma unroll
-            for (int e = 0; e < 8; ++e) {
-              if (q0 + e < qe) qv |= 1u << e;
-              hq[e] = oh * a.sh - a.pt;
-              wq[e] = ow * a.sw - a.pl;
-              xo[e] = n * a.C * a.HW + hq[e] * a.W + wq[e];
-              dq[e] = n * a.O * a.P + p;
-              ++p;
-              if (++ow == a.OW) {
-                ow = 0;
-                if (++oh == a.OH) {
-                  oh = 0;
-                  p = 0;
-                  ++n;
-                }
+          for (int h2 = 0; h2 < 2; ++h2) {
+            const int qr = lane + 32 * h2;  // K row of the tile
+            const int q = qs + kb * BK + qr;
+            const bool qv = q < qe;
+            const int qq = qv ? q : 0;
+            const int n = qq / a.P, p = qq - n * a.P, oh = p / a.OW, ow = p - oh * a.OW;
+            const int hq = oh * a.sh - a.pt, wq = ow * a.sw - a.pl;
+            const int xbase = ((n * a.H + hq) * a.W + wq) * a.CP;
+            const int dbase = ((n * a.OH + oh) * a.OW + ow) * a.OPW;
+            const uint32_t rowoff = (uint32_t)qr * 128u;
+#pragma unroll
+            for (int b = 0; b < 2; ++b)
+#pragma unroll
+              for (int j8 = 0; j8 < 8; ++j8) {
+                const int mc = (m0 + 64 * b) / 8 + j8;
+                const int4 t = tab[min(mc, mchunks - 1)];
+                const int hh = hq + t.y, ww = wq + t.z;
+                const bool okk = qv && mc < mchunks && (unsigned)hh < (unsigned)a.H && (unsigned)ww < (unsigned)a.W;
+                cp16(sA + (uint32_t)b * 8192u + rowoff + ((uint32_t)(j8 ^ (qr & 7)) << 4), a.an + (okk ? xbase + t.x : 0),
+                     okk ? 16u : 0u);
               }
-            }
+            for (int b = 0; b < nb; ++b)
+#pragma unroll
+              for (int j8 = 0; j8 < 8; ++j8) {
+                const int o0 = n0 + 64 * b + 8 * j8;
+                const bool okk = qv && o0 < a.OPW;
+                cp16(sB + (uint32_t)b * 8192u + rowoff + ((uint32_t)(j8 ^ (qr & 7)) << 4), a.bn + (okk ? dbase + o0 : 0),
+                     okk ? 16u : 0u);
+              }
           }
-          float v[32], dv[32];
-#pragma unroll
-          for (int u = 0; u < 4; ++u) {
-            const int row = m0 + rsub + 32 * u;
-            const bool rv = row < a.M;
-            const int4 t = tab[min(row, a.M - 1)];
-#pragma unroll
-            for (int e = 0; e < 8; ++e) {
-              const int h = hq[e] + t.y, w = wq[e] + t.z;
-              const bool okk = rv && ((qv >> e) & 1) && (unsigned)h < (unsigned)a.H && (unsigned)w < (unsigned)a.W;
-              const float x = __ldg(a.asrc + (okk ? xo[e] + t.x : 0));
-              v[u * 8 + e] = okk ? x : 0.f;
-            }
-          }
-#pragma unroll
-          for (int u = 0; u < 4; ++u) {
-            const int o = n0 + rsub + 32 * u;
-            const bool ov = rsub + 32 * u < a.BN && o < a.Nc;
-#pragma unroll
-            for (int e = 0; e < 8; ++e) {
-              const bool okk = ov && ((qv >> e) & 1);
-              const float x = __ldg(a.bsrc + (okk ? dq[e] + o * a.P : 0));
-              dv[u * 8 + e] = okk ? x : 0.f;
-            }
-          }
-#pragma unroll
-          for (int u = 0; u < 4; ++u) put8(sA + swz(rsub + 32 * u, j), &v[8 * u]);
-#pragma unroll
-          for (int u = 0; u < 4; ++u)
-            if (rsub + 32 * u < a.BN) put8(sB + swz(rsub + 32 * u, j), &dv[8 * u]);
-          // B rows beyond 128 (BN > 128): a second pass
-          for (int rr = rsub + 128; rr < a.BN; rr += 32) {
-            const int o = n0 + rr;
-            float ev[8];
-#pragma unroll
-            for (int e = 0; e < 8; ++e) {
-              const bool okk = o < a.Nc && ((qv >> e) & 1);
-              const float x = __ldg(a.bsrc + (okk ? dq[e] + o * a.P : 0));
-              ev[e] = okk ? x : 0.f;
-            }
-            put8(sB + swz(rr, j), ev);
-          }
+          cp_wait_all();
           fence_proxy_async_smem();
           __syncwarp();
           if (lane == 0) mbar_arrive(&full[s]);
@@ -377,13 +409,16 @@ __global__ void __launch_bounds__(THREADS, 1) conv_igemm_kernel(const __grid_con
   } else if (warp == MMA_WARP) {
     // ------------------------------------------------------------ MMA issuer
     if (lane == 0) {
-      const uint32_t idesc = (1u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(a.BN >> 3) << 17) | ((uint32_t)(BM >> 4) << 24);
+      // wgrad: A and B MN-major (bits 15, 16)
+      const uint32_t mn = MODE == WGRAD ? (1u << 15) | (1u << 16) : 0u;
+      const uint32_t idesc = (1u << 4) | (1u << 7) | (1u << 10) | mn | ((uint32_t)(a.BN >> 3) << 17) | ((uint32_t)(BM >> 4) << 24);
       uint32_t L = 0, T = 0;
       bool ok = true, issued = false;
       for (int it = blockIdx.x; it < a.items && ok; it += gridDim.x) {
         Item r;
         if (!item_of(a, it, r)) continue;
         const int nkb = kblocks_of(a, r);
+        if (nkb <= 0) continue;
         const uint32_t b = T & 1;
         if (!mbar_wait(&acc_empty[b], ((T >> 1) & 1) ^ 1, 32)) break;
         tc_fence_after();
@@ -400,8 +435,10 @@ __global__ void __launch_bounds__(THREADS, 1) conv_igemm_kernel(const __grid_con
                                             : smem_u32(sResB) + (uint32_t)(((a.cls_kb[r.cls] + kb) * a.tiles_n + r.nt) * a.BN) * 128u;
 #pragma unroll
           for (int k = 0; k < 4; ++k) {
-            const uint64_t ad = smem_desc(sA + k * 32, 16, 1024);
-            const uint64_t bd = smem_desc(sB + k * 32, 16, 1024);
+            // K-major: +32 B per 16-wide K step inside the swizzled rows; MN-major: +2048 B
+            // (16 K rows of 128 B), 64-element blocks 8192 B apart
+            const uint64_t ad = MODE == WGRAD ? smem_desc(sA + k * 2048, 8192, 1024) : smem_desc(sA + k * 32, 16, 1024);
+            const uint64_t bd = MODE == WGRAD ? smem_desc(sB + k * 2048, 8192, 1024) : smem_desc(sB + k * 32, 16, 1024);
             mma_bf16(d, ad, bd, idesc, (kb > 0 || k > 0) ? 1u : 0u);
           }
           issued = true;
@@ -424,6 +461,7 @@ __global__ void __launch_bounds__(THREADS, 1) conv_igemm_kernel(const __grid_con
     for (int it = blockIdx.x; it < a.items && ok; it += gridDim.x) {
       Item r;
       if (!item_of(a, it, r)) continue;
+      if (kblocks_of(a, r) <= 0) continue;
       const uint32_t b = T & 1;
       ok = warp_wait(&acc_full[b], (T >> 1) & 1, 64);
       ++T;
@@ -498,34 +536,45 @@ __global__ void __launch_bounds__(THREADS, 1) conv_igemm_kernel(const __grid_con
   }
 }
 
-// partials [S][O][M] (row = t*C + c) -> dw [O, C, KH, KW], summed over S in order
-__global__ void wgrad_reduce_kernel(const float* __restrict__ part, float* __restrict__ dw, int S, int O, int M, int C, int KHW) {
-  const int64_t total = (int64_t)O * M;
-  for (int64_t e = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; e < total; e += (int64_t)gridDim.x * blockDim.x) {
-    const int o = (int)(e / M), row = (int)(e - (int64_t)o * M);
-    float acc = 0.f;
-    for (int s = 0; s < S; ++s) acc += part[((int64_t)s * O + o) * M + row];
-    const int t = row / C, c = row - t * C;
-    dw[((int64_t)o * C + c) * KHW + t] = acc;
-  }
+// partials [S][O][M] (row = t*Cp + c, channels padded to Cp) -> dw [O, C, KH, KW]: one
+// warp per output, lane l sums splits l, l + 32, ... in order, then a fixed xor-butterfly
+// over the lanes, so the result is the same on every run
+__global__ void __launch_bounds__(256) wgrad_reduce_kernel(const float* __restrict__ part, float* __restrict__ dw, int S, int O,
+                                                           int M, int C, int Cp, int KHW) {
+  const int64_t e = (blockIdx.x * (int64_t)blockDim.x + threadIdx.x) >> 5;
+  const int lane = threadIdx.x & 31;
+  if (e >= (int64_t)O * M) return;
+  const int o = (int)(e / M), row = (int)(e - (int64_t)o * M);
+  const int t = row / Cp, c = row - t * Cp;
+  if (c >= C) return;
+  float acc = 0.f;
+  for (int s = lane; s < S; s += 32) acc += __ldg(part + ((int64_t)s * O + o) * M + row);
+#pragma unroll
+  for (int k = 16; k > 0; k >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, k);
+  if (lane == 0) dw[((int64_t)o * C + c) * KHW + t] = acc;
 }
 
 struct Plan {
   Args a;
   size_t smem;
+  size_t ws;  // workspace: fwd / dgrad the NHWC bf16 source, wgrad the split partials
   bool ok;
   const char* why;
 };
 
+inline size_t al256(size_t v) { return (v + 255) & ~size_t(255); }
+
 // Shapes the kernel handles: 32-bit element offsets (tensors up to 2^30 elements), at most
-// KTAB_MAX taps x channels, at most 16 stride-parity classes, and (fwd / dgrad) the whole
-// bf16 weight operand resident in shared memory beside two A stages.
+// KTAB_MAX reduction indices (fwd / dgrad, channels padded to 8) or taps x channels
+// (wgrad), at most 16 stride-parity classes, and (fwd / dgrad) the whole bf16 weight
+// operand resident in shared memory beside two A stages.
 static Plan plan(int mode, int64_t N, int64_t C, int64_t H, int64_t W, int64_t O, int64_t KH, int64_t KW, int64_t OH, int64_t OW,
                  int64_t sh, int64_t sw, int64_t pt, int64_t pl) {
   Plan p{};
   p.ok = false;
   const int64_t lim = (int64_t)1 << 30;
-  if (N * C * H * W > lim || N * O * OH * OW > lim || O * C * KH * KW > lim) {
+  const int64_t Cp = (C + 7) / 8 * 8, Op = (O + 7) / 8 * 8;
+  if (N * Cp * H * W > lim || N * Op * OH * OW > lim || O * C * KH * KW > lim) {
     p.why = "tensor above 2^30 elements";
     return p;
   }
@@ -540,16 +589,22 @@ static Plan plan(int mode, int64_t N, int64_t C, int64_t H, int64_t W, int64_t O
   a.HW = (int)(H * W);
   const int64_t taps = KH * KW;
   int64_t M, Nc, K;
-  if (mode == FWD) M = N * OH * OW, Nc = O, K = C * taps;
-  else if (mode == DGRAD) M = N * H * W, Nc = C, K = O * taps;
-  else M = C * taps, Nc = O, K = N * OH * OW;
-  const int64_t ktab = mode == WGRAD ? M : K;
-  if (ktab > KTAB_MAX) {
-    p.why = "more than 2048 taps x channels";
+  const int64_t Opw = (O + 63) / 64 * 64;
+  if (mode == WGRAD && N * Opw * OH * OW > lim) {
+    p.why = "tensor above 2^30 elements";
     return p;
   }
-  a.M = (int)M, a.Nc = (int)Nc, a.K = (int)K, a.ktab = (int)ktab;
-  a.BN = (int)std::min<int64_t>(256, (Nc + 15) / 16 * 16);
+  a.OPW = (int)Opw;
+  if (mode == FWD) M = N * OH * OW, Nc = O, K = Cp * taps, a.CP = (int)Cp;
+  else if (mode == DGRAD) M = N * H * W, Nc = C, K = Op * taps, a.CP = (int)Op;
+  else M = Cp * taps, Nc = O, K = N * OH * OW, a.CP = (int)Cp;
+  if ((mode == WGRAD ? M : K) > KTAB_MAX) {
+    p.why = "more than 2048 reduction indices (or taps x channels)";
+    return p;
+  }
+  a.M = (int)M, a.Nc = (int)Nc, a.K = (int)K;
+  // wgrad: B is MN-major in 64-column blocks
+  a.BN = mode == WGRAD ? (int)std::min<int64_t>(256, Opw) : (int)std::min<int64_t>(256, (Nc + 15) / 16 * 16);
   a.BNT = (a.BN + 31) / 32 * 32;
   uint32_t cols = 32;
   while (cols < (uint32_t)(2 * a.BNT)) cols <<= 1;
@@ -564,25 +619,27 @@ static Plan plan(int mode, int64_t N, int64_t C, int64_t H, int64_t W, int64_t O
       const int hc = ph < H ? (int)ceil_div(H - ph, sh) : 0, wc = pw < W ? (int)ceil_div(W - pw, sw) : 0;
       const int i0 = (int)((ph + pt) % sh), j0 = (int)((pw + pl) % sw);
       const int ni = i0 < KH ? (int)ceil_div(KH - i0, sh) : 0, nj = j0 < KW ? (int)ceil_div(KW - j0, sw) : 0;
-      a.cls_ph[c] = ph, a.cls_pw[c] = pw, a.cls_hc[c] = hc, a.cls_wc[c] = wc;
-      a.cls_k[c] = (int)(O * ni * nj);
+      a.cls_ph[c] = ph, a.cls_pw[c] = pw, a.cls_hc[c] = hc, a.cls_wc[c] = wc, a.cls_nj[c] = nj;
+      a.cls_k[c] = (int)(Op * ni * nj);
       a.cls_m[c] = a.cls_k[c] > 0 ? (int)(N * hc * wc) : 0;  // pixels no tap reaches are zero-filled by the caller
       a.cls_ktab[c] = koff;
       a.cls_kb[c] = kboff;
-      koff += a.cls_k[c];
+      koff += a.cls_k[c] / 8;
       kboff += (int)ceil_div(a.cls_k[c], BK);
       max_tiles = std::max<int64_t>(max_tiles, ceil_div(a.cls_m[c], BM));
     }
     a.kb_total = kboff;
+    a.ktab = koff;
   } else {
     a.ncls = 1;
     a.cls_ph[0] = a.cls_pw[0] = 0;
-    a.cls_hc[0] = a.cls_wc[0] = 1;
+    a.cls_hc[0] = a.cls_wc[0] = a.cls_nj[0] = 1;
     a.cls_m[0] = (int)M;
     a.cls_k[0] = (int)(mode == WGRAD ? 0 : K);
     a.cls_ktab[0] = 0;
     a.cls_kb[0] = 0;
     a.kb_total = mode == WGRAD ? 0 : (int)ceil_div(K, BK);
+    a.ktab = (int)(mode == WGRAD ? M / 8 : K / 8);
     max_tiles = ceil_div(M, BM);
   }
   a.max_tiles = (int)max_tiles;
@@ -613,16 +670,20 @@ static Plan plan(int mode, int64_t N, int64_t C, int64_t H, int64_t W, int64_t O
   size_t resb = 0;
   if (mode == WGRAD) {
     a.stage_bytes = A_BYTES + (uint32_t)a.BN * 128u;
+    // channels-last x, channels-last dy, then the split partials
+    p.ws = al256((size_t)N * H * W * Cp * 2) + al256((size_t)N * OH * OW * Opw * 2) + (size_t)a.splits * (size_t)O * (size_t)M * 4;
   } else {
     a.stage_bytes = A_BYTES;
     resb = (size_t)a.kb_total * a.tiles_n * a.BN * 128;
+    p.ws = mode == FWD ? (size_t)N * H * W * Cp * 2 : (size_t)N * OH * OW * Op * 2;
   }
   const size_t fixed = 1024 + resb + (size_t)a.ktab * 16 + 64 * 8 + 16;
   if (fixed + 2 * (size_t)a.stage_bytes > SMEM_LIMIT) {
     p.why = "shared memory (weights too large to stay resident)";
     return p;
   }
-  const int st = (int)std::min<size_t>(8, (SMEM_LIMIT - fixed) / a.stage_bytes);
+  // fwd / dgrad: one producer warp per stage, so at most PROD_WARPS stages
+  const int st = (int)std::min<size_t>(PROD_WARPS, (SMEM_LIMIT - fixed) / a.stage_bytes);
   a.stages = st;
   a.resb_off = (uint32_t)st * a.stage_bytes;
   p.smem = fixed + (size_t)st * a.stage_bytes;
@@ -642,6 +703,13 @@ static int launch(Args a, size_t smem, cudaStream_t s) {
   const unsigned grid = (unsigned)std::max(1, std::min(a.items, num_sms()));
   conv_igemm_kernel<MODE><<<grid, THREADS, smem, s>>>(a);
   return check_launch("conv2d(implicit GEMM)");
+}
+
+static int repack(const float* src, __nv_bfloat16* dst, int64_t N, int64_t C, int64_t HW, int64_t Cp, cudaStream_t s) {
+  const int64_t total = N * HW * (Cp / 8);
+  const unsigned grid = (unsigned)std::max<int64_t>(1, std::min<int64_t>(ceil_div(total, 256), (int64_t)num_sms() * 16));
+  nchw_to_nhwc_bf16_kernel<<<grid, 256, 0, s>>>(src, dst, N, (int)C, HW, (int)Cp);
+  return check_launch("conv2d(implicit GEMM, NHWC repack)");
 }
 
 static int check_dims(int64_t N, int64_t C, int64_t H, int64_t W, int64_t O, int64_t KH, int64_t KW, int64_t OH, int64_t OW,
@@ -665,18 +733,17 @@ extern "C" int b200_conv2d_igemm_supported(int op, int64_t N, int64_t C, int64_t
   return plan(op, N, C, H, W, O, KH, KW, OH, OW, sh, sw, pt, pl).ok ? 1 : 0;
 }
 
-extern "C" size_t b200_conv2d_wgrad_igemm_workspace_bytes(int64_t N, int64_t C, int64_t H, int64_t W, int64_t O, int64_t KH,
-                                                          int64_t KW, int64_t OH, int64_t OW, int64_t sh, int64_t sw, int64_t pt,
-                                                          int64_t pl) {
-  if (N < 1) return 0;
-  Plan p = plan(WGRAD, N, C, H, W, O, KH, KW, OH, OW, sh, sw, pt, pl);
-  if (!p.ok) return 0;
-  return (size_t)p.a.splits * (size_t)O * (size_t)p.a.M * 4;
+extern "C" size_t b200_conv2d_igemm_workspace_bytes(int op, int64_t N, int64_t C, int64_t H, int64_t W, int64_t O, int64_t KH,
+                                                    int64_t KW, int64_t OH, int64_t OW, int64_t sh, int64_t sw, int64_t pt,
+                                                    int64_t pl) {
+  if (op < 0 || op > 2 || N < 1) return 0;
+  Plan p = plan(op, N, C, H, W, O, KH, KW, OH, OW, sh, sw, pt, pl);
+  return p.ok ? p.ws : 0;
 }
 
 extern "C" int b200_conv2d_fwd_igemm(const float* x, const float* w, float* y, int64_t N, int64_t C, int64_t H, int64_t W,
                                      int64_t O, int64_t KH, int64_t KW, int64_t OH, int64_t OW, int64_t sh, int64_t sw,
-                                     int64_t pt, int64_t pl, int relu, void* stream) {
+                                     int64_t pt, int64_t pl, int relu, void* ws, size_t ws_bytes, void* stream) {
   int rc = check_dims(N, C, H, W, O, KH, KW, OH, OW, sh, sw, pt, pl);
   if (rc) return rc;
   if (N == 0) return B200_OK;
@@ -686,14 +753,20 @@ extern "C" int b200_conv2d_fwd_igemm(const float* x, const float* w, float* y, i
     set_error("conv2d_fwd_igemm: unsupported shape (%s)", p.why);
     return B200_ERR_UNSUPPORTED;
   }
+  B200_REQUIRE(ws && ws_bytes >= p.ws && (reinterpret_cast<uintptr_t>(ws) & 15) == 0,
+               "conv2d_fwd_igemm: workspace %zu < %zu (16-byte aligned)", ws_bytes, p.ws);
+  cudaStream_t s = as_stream(stream);
+  auto* xn = reinterpret_cast<__nv_bfloat16*>(ws);
+  if ((rc = repack(x, xn, N, C, H * W, p.a.CP, s))) return rc;
   p.a.relu = relu ? 1 : 0;
-  p.a.asrc = x, p.a.bsrc = w, p.a.out = y, p.a.mask = nullptr;
-  return launch<FWD>(p.a, p.smem, as_stream(stream));
+  p.a.an = xn, p.a.bn = nullptr, p.a.bsrc = w, p.a.out = y, p.a.mask = nullptr;
+  return launch<FWD>(p.a, p.smem, s);
 }
 
 extern "C" int b200_conv2d_dgrad_igemm(const float* dy, const float* w, const float* mask, float* dx, int64_t N, int64_t C,
                                        int64_t H, int64_t W, int64_t O, int64_t KH, int64_t KW, int64_t OH, int64_t OW,
-                                       int64_t sh, int64_t sw, int64_t pt, int64_t pl, void* stream) {
+                                       int64_t sh, int64_t sw, int64_t pt, int64_t pl, void* ws, size_t ws_bytes,
+                                       void* stream) {
   int rc = check_dims(N, C, H, W, O, KH, KW, OH, OW, sh, sw, pt, pl);
   if (rc) return rc;
   if (N == 0) return B200_OK;
@@ -703,6 +776,8 @@ extern "C" int b200_conv2d_dgrad_igemm(const float* dy, const float* w, const fl
     set_error("conv2d_dgrad_igemm: unsupported shape (%s)", p.why);
     return B200_ERR_UNSUPPORTED;
   }
+  B200_REQUIRE(ws && ws_bytes >= p.ws && (reinterpret_cast<uintptr_t>(ws) & 15) == 0,
+               "conv2d_dgrad_igemm: workspace %zu < %zu (16-byte aligned)", ws_bytes, p.ws);
   cudaStream_t s = as_stream(stream);
   // pixels that no tap reaches (a class without taps: stride above the kernel size) are zero
   for (int c = 0; c < p.a.ncls; ++c)
@@ -711,8 +786,10 @@ extern "C" int b200_conv2d_dgrad_igemm(const float* dy, const float* w, const fl
       if ((rc = check_launch("conv2d_dgrad_igemm(zero)"))) return rc;
       break;
     }
+  auto* dyn = reinterpret_cast<__nv_bfloat16*>(ws);
+  if ((rc = repack(dy, dyn, N, O, OH * OW, p.a.CP, s))) return rc;
   p.a.relu = 0;
-  p.a.asrc = dy, p.a.bsrc = w, p.a.out = dx, p.a.mask = mask;
+  p.a.an = dyn, p.a.bn = nullptr, p.a.bsrc = w, p.a.out = dx, p.a.mask = mask;
   return launch<DGRAD>(p.a, p.smem, s);
 }
 
@@ -732,15 +809,22 @@ extern "C" int b200_conv2d_wgrad_igemm(const float* x, const float* dy, float* d
     set_error("conv2d_wgrad_igemm: unsupported shape (%s)", p.why);
     return B200_ERR_UNSUPPORTED;
   }
-  const size_t need = (size_t)p.a.splits * (size_t)O * (size_t)p.a.M * 4;
-  B200_REQUIRE(ws && ws_bytes >= need, "conv2d_wgrad_igemm: workspace %zu < %zu", ws_bytes, need);
+  B200_REQUIRE(ws && ws_bytes >= p.ws && (reinterpret_cast<uintptr_t>(ws) & 255) == 0,
+               "conv2d_wgrad_igemm: workspace %zu < %zu (256-byte aligned)", ws_bytes, p.ws);
+  uint8_t* base = reinterpret_cast<uint8_t*>(ws);
+  auto* xn = reinterpret_cast<__nv_bfloat16*>(base);
+  base += al256((size_t)N * H * W * p.a.CP * 2);
+  auto* dyn = reinterpret_cast<__nv_bfloat16*>(base);
+  base += al256((size_t)N * OH * OW * p.a.OPW * 2);
+  float* part = reinterpret_cast<float*>(base);
+  if ((rc = repack(x, xn, N, C, H * W, p.a.CP, s))) return rc;
+  if ((rc = repack(dy, dyn, N, O, OH * OW, p.a.OPW, s))) return rc;
   p.a.relu = 0;
-  p.a.asrc = x, p.a.bsrc = dy, p.a.out = reinterpret_cast<float*>(ws), p.a.mask = nullptr;
+  p.a.an = xn, p.a.bn = dyn, p.a.bsrc = nullptr, p.a.out = part, p.a.mask = nullptr;
   rc = launch<WGRAD>(p.a, p.smem, s);
   if (rc) return rc;
   const int64_t total = O * (int64_t)p.a.M;
-  const unsigned grid = (unsigned)std::max<int64_t>(1, std::min<int64_t>(ceil_div(total, 256), (int64_t)num_sms() * 8));
-  wgrad_reduce_kernel<<<grid, 256, 0, s>>>(reinterpret_cast<const float*>(ws), dw, p.a.splits, (int)O, p.a.M, (int)C,
-                                           (int)(KH * KW));
+  wgrad_reduce_kernel<<<(unsigned)ceil_div(total * 32, 256), 256, 0, s>>>(part, dw, p.a.splits, (int)O, p.a.M, (int)C, p.a.CP,
+                                                                          (int)(KH * KW));
   return check_launch("conv2d_wgrad_igemm(sum)");
 }

@@ -315,6 +315,73 @@ __global__ void __launch_bounds__(THREADS) ew_un8_kernel(const __grid_constant__
   }
 }
 
+// sum of inputs as a left fold, ((in[o0] + in[o1]) + in[o2]) + ..., stored to every output:
+// all inputs of a group are loaded before the first addition
+__global__ void __launch_bounds__(THREADS) ew_sum8_kernel(const __grid_constant__ EwParams P) {
+  const int64_t ng = (P.n + V - 1) / V;
+  const int nout = P.p.n_out, nsum = P.nsum;
+  for (int64_t q = blockIdx.x * (int64_t)THREADS + threadIdx.x; q < ng; q += (int64_t)gridDim.x * THREADS) {
+    const int64_t base = q * V;
+    const bool full = base + V <= P.n;
+    float x[B200_EW_MAX_IN][V];
+#pragma unroll
+    for (int k = 0; k < B200_EW_MAX_IN; ++k)
+      if (k < nsum) loadv<V>(P, P.sumord[k], base, full, x[k]);
+    float r[V];
+#pragma unroll
+    for (int v = 0; v < V; ++v) r[v] = x[0][v];
+#pragma unroll
+    for (int k = 1; k < B200_EW_MAX_IN; ++k)
+      if (k < nsum) {
+#pragma unroll
+        for (int v = 0; v < V; ++v) r[v] = r[v] + x[k][v];
+      }
+    for (int o = 0; o < nout; ++o) storev<V>(P, o, base, full, r);
+  }
+}
+
+// Recognise a program that adds its loaded inputs one after another (a left fold of ADD
+// instructions) and stores only the final sum.
+static bool classify_sum(EwParams& P) {
+  const b200_ew_program& p = P.p;
+  int reg_in[B200_EW_MAX_REG];
+  for (int i = 0; i < B200_EW_MAX_REG; ++i) reg_in[i] = -1;
+  int acc = -1, n = 0, stores = 0;
+  for (int i = 0; i < p.n_ins; ++i) {
+    const b200_ew_ins& I = p.ins[i];
+    if (I.op == B200_EW_LOAD) {
+      if (I.dst >= B200_EW_MAX_REG || I.dst == acc) return false;
+      reg_in[I.dst] = I.a;
+    } else if (I.op == B200_EW_ADD) {
+      if (I.a >= B200_EW_MAX_REG || I.b >= B200_EW_MAX_REG || I.dst >= B200_EW_MAX_REG || stores) return false;
+      if (acc < 0) {
+        if (reg_in[I.a] < 0 || reg_in[I.b] < 0) return false;
+        P.sumord[0] = reg_in[I.a];
+        P.sumord[1] = reg_in[I.b];
+        n = 2;
+      } else {
+        int other;
+        if (I.a == acc && I.b != acc) other = I.b;
+        else if (I.b == acc && I.a != acc) other = I.a;
+        else return false;
+        if (reg_in[other] < 0 || n >= B200_EW_MAX_IN) return false;
+        P.sumord[n++] = reg_in[other];
+      }
+      acc = I.dst;
+      reg_in[acc] = -1;
+    } else if (I.op == B200_EW_STORE) {
+      if (acc < 0 || I.a != acc) return false;
+      ++stores;
+    } else {
+      return false;
+    }
+  }
+  if (acc < 0 || stores == 0) return false;
+  P.nsum = n;
+  P.kind = 4;
+  return true;
+}
+
 // Recognise a program that is LOADs, one op, and STOREs of that op's result only (or
 // LOADs and STOREs of a single loaded register: a copy / cast).
 static void classify(EwParams& P) {
@@ -382,6 +449,11 @@ int ew_flat_launch(EwParams& P, cudaStream_t s) {
   if (P.kind == 1 || P.kind == 2) {
     ew_un8_kernel<<<blocks, THREADS, 0, s>>>(P);
     return check_launch("ew_run(unary)");
+  }
+  if (P.kind == 0) classify_sum(P);
+  if (P.kind == 4) {
+    ew_sum8_kernel<<<blocks, THREADS, 0, s>>>(P);
+    return check_launch("ew_run(sum)");
   }
   if (P.kind == 3) {
     switch (P.sop) {

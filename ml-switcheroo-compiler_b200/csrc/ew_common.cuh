@@ -24,6 +24,8 @@ struct EwParams {
   // specialised straight-line programs: kind (0 generic, 1 copy/cast, 2 unary, 3 binary),
   // op, and the input feeding each operand
   int32_t kind, sop, sa, sb;
+  // kind 4: a left fold of additions over inputs sumord[0 .. nsum) (in that order)
+  int32_t nsum, sumord[B200_EW_MAX_IN];
 };
 
 // n / d for 32-bit n with a precomputed (mul, shr): q = (umulhi(n, mul) + n) >> shr

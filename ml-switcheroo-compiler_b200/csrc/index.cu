@@ -60,6 +60,23 @@ __global__ void take_rows_kernel(const T* __restrict__ table, const int64_t* __r
   }
 }
 
+// fp32 rows of D % 4 == 0 (16-byte aligned): one warp per output row, 16-byte accesses
+__global__ void __launch_bounds__(256) take_rows4_kernel(const float* __restrict__ table, const int64_t* __restrict__ ids,
+                                                         float* __restrict__ y, int64_t n, int64_t V, int64_t D) {
+  const int64_t i = (int64_t)blockIdx.x * 8 + (threadIdx.x >> 5);
+  if (i >= n) return;
+  const int lane = threadIdx.x & 31;
+  int64_t v = ids[i];
+  if (v < 0) v += V;
+  if (v < 0 || v >= V) {
+    if (lane == 0) raise_device_error(B200_ERR_ARG);
+    return;
+  }
+  const float4* src = reinterpret_cast<const float4*>(table + v * D);
+  float4* dst = reinterpret_cast<float4*>(y + i * D);
+  for (int64_t c = lane; c < D / 4; c += 32) dst[c] = __ldg(src + c);
+}
+
 // Deterministic row scatter-add: positions are bucketed by their row id with a stable
 // counting sort (integer atomics only; stable order from in-block ranks), then every
 // output row sums its source rows in increasing position order. Float results therefore
@@ -156,6 +173,30 @@ __global__ void __launch_bounds__(256) sa_sum_kernel(const float* __restrict__ s
   y[v * D + d] = acc;
 }
 
+// the same sums, one warp per row v with 16-byte accesses (D % 4 == 0, 16-byte aligned
+// rows): each float4 column group is summed over v's positions in position order, so the
+// result is bit-identical to sa_sum_kernel
+__global__ void __launch_bounds__(256) sa_sum4_kernel(const float* __restrict__ src, const int* __restrict__ perm,
+                                                      const int* __restrict__ off, float* __restrict__ y, int64_t V, int64_t D,
+                                                      int accumulate) {
+  const int64_t v = (int64_t)blockIdx.x * 8 + (threadIdx.x >> 5);
+  if (v >= V) return;
+  const int lane = threadIdx.x & 31;
+  const int a = off[v], b = off[v + 1];
+  float4* yr = reinterpret_cast<float4*>(y + v * D);
+  for (int64_t c = lane; c < D / 4; c += 32) {
+    float4 acc = accumulate ? yr[c] : make_float4(0.f, 0.f, 0.f, 0.f);
+    for (int k = a; k < b; ++k) {
+      const float4 t = __ldg(reinterpret_cast<const float4*>(src + (int64_t)perm[k] * D) + c);
+      acc.x += t.x;
+      acc.y += t.y;
+      acc.z += t.z;
+      acc.w += t.w;
+    }
+    yr[c] = acc;
+  }
+}
+
 inline int64_t sa_blocks(int64_t n) { return ceil_div(n, (int64_t)SA_B); }
 
 static unsigned grid_for(int64_t n, int threads) {
@@ -193,7 +234,9 @@ extern "C" int b200_take_rows(int dt, const void* table, const int64_t* ids, voi
   B200_REQUIRE(n >= 0 && V >= 1 && D >= 0, "take_rows: bad sizes");
   if (n * D == 0) return B200_OK;
   cudaStream_t s = as_stream(stream);
-  if (dt == B200_F32)
+  if (dt == B200_F32 && D % 4 == 0 && (reinterpret_cast<uintptr_t>(table) & 15) == 0 && (reinterpret_cast<uintptr_t>(y) & 15) == 0)
+    take_rows4_kernel<<<(unsigned)ceil_div(n, (int64_t)8), 256, 0, s>>>((const float*)table, ids, (float*)y, n, V, D);
+  else if (dt == B200_F32)
     take_rows_kernel<float><<<grid_for(n * D, 256), 256, 0, s>>>((const float*)table, ids, (float*)y, n, V, D);
   else if (dt == B200_BF16)
     take_rows_kernel<__nv_bfloat16><<<grid_for(n * D, 256), 256, 0, s>>>((const __nv_bfloat16*)table, ids,
@@ -248,6 +291,10 @@ extern "C" int b200_scatter_add_rows(const float* src, const int64_t* ids, float
   if ((rc = check_launch("scatter_add_rows(scan)"))) return rc;
   sa_place_kernel<<<(unsigned)ceil_div(n, (int64_t)256), 256, 0, s>>>(ids, rank, cnt, off, perm, n, V);
   if ((rc = check_launch("scatter_add_rows(place)"))) return rc;
+  if (D % 4 == 0 && (reinterpret_cast<uintptr_t>(src) & 15) == 0 && (reinterpret_cast<uintptr_t>(y) & 15) == 0) {
+    sa_sum4_kernel<<<(unsigned)ceil_div(V, (int64_t)8), 256, 0, s>>>(src, perm, off, y, V, D, accumulate);
+    return check_launch("scatter_add_rows(sum)");
+  }
   const int64_t dblocks = ceil_div(D, (int64_t)256);
   sa_sum_kernel<<<(unsigned)(V * dblocks), 256, 0, s>>>(src, perm, off, y, D, dblocks, accumulate);
   return check_launch("scatter_add_rows(sum)");

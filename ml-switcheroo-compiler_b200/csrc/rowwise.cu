@@ -54,18 +54,27 @@ __global__ void __launch_bounds__(256) reduce_cols_kernel(const void* __restrict
   }
 }
 
+// one warp per output: lane l combines chunks l, l + 32, ... in order, then a fixed
+// xor-butterfly combines the lanes, so the result is the same on every run
 template <int OP>
-__global__ void reduce_splits_kernel(const float* __restrict__ part, float* __restrict__ y, int64_t n, int64_t split,
-                                     int64_t red) {
-  const int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x;
+__global__ void __launch_bounds__(256) reduce_splits_kernel(const float* __restrict__ part, float* __restrict__ y, int64_t n,
+                                                            int64_t split, int64_t red) {
+  const int64_t i = (blockIdx.x * (int64_t)blockDim.x + threadIdx.x) >> 5;
+  const int lane = threadIdx.x & 31;
   if (i >= n) return;
   float acc = (OP == B200_RED_MAX) ? -INFINITY : 0.f;
-  for (int64_t z = 0; z < split; ++z) {
-    const float v = part[z * n + i];
+  for (int64_t z = lane; z < split; z += 32) {
+    const float v = __ldg(part + z * n + i);
     if (OP == B200_RED_MAX) acc = fmaxf(acc, v);
     else acc += v;
   }
-  y[i] = (OP == B200_RED_MEAN) ? acc / (float)red : acc;
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) {
+    const float v = __shfl_xor_sync(0xffffffffu, acc, o);
+    if (OP == B200_RED_MAX) acc = fmaxf(acc, v);
+    else acc += v;
+  }
+  if (lane == 0) y[i] = (OP == B200_RED_MEAN) ? acc / (float)red : acc;
 }
 
 __global__ void fill_kernel(float* y, int64_t n, float v) {
@@ -346,7 +355,7 @@ extern "C" int b200_reduce(int dt, const void* x, float* y, int64_t outer, int64
   int rc = check_launch("reduce(cols)");
   if (rc || split == 1) return rc;
   const int64_t n = outer * inner;
-  const unsigned g2 = (unsigned)ceil_div(n, 256);
+  const unsigned g2 = (unsigned)ceil_div(n * 32, 256);
   switch (op) {
     case B200_RED_SUM: reduce_splits_kernel<B200_RED_SUM><<<g2, 256, 0, s>>>(part, y, n, split, red); break;
     case B200_RED_MEAN: reduce_splits_kernel<B200_RED_MEAN><<<g2, 256, 0, s>>>(part, y, n, split, red); break;

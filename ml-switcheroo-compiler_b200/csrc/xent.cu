@@ -80,16 +80,31 @@ __device__ __forceinline__ void xr_cp_async_wait_all() { asm volatile("cp.async.
 // Persistent over rows (one CTA per SM): while a row is reduced and its gradient written
 // from registers, the CTA's next row streams into shared memory with cp.async, so HBM
 // reads overlap the math and the stores. Thread t copies and later reads only its own
-// float4 slots, so the staging buffer needs no barrier.
+// float4 slots, so the staging buffer needs no barrier. Each thread keeps its own
+// (max m_t, sum of exp(x - m_t)) over its columns and the exponentials themselves; one
+// block-wide merge of the (m, s) pairs gives the row's max M and sum S, and the gradient
+// is then e * exp(m_t - M) / S per element: one exp2 per element and two barriers per row.
+constexpr float XR_LOG2E = 1.4426950408889634f;
+
+// (m, s) pairs: s sums exp(x - m); merged with the larger maximum
+__device__ __forceinline__ void xr_merge(float& m, float& s, float m2, float s2) {
+  const float M = fmaxf(m, m2);
+  const float a = m == -INFINITY ? 0.f : s * exp2f((m - M) * XR_LOG2E);
+  const float b = m2 == -INFINITY ? 0.f : s2 * exp2f((m2 - M) * XR_LOG2E);
+  m = M;
+  s = a + b;
+}
+
 template <int VPT>
 __global__ void __launch_bounds__(XR_T, 1) xent_reg_kernel(const float* __restrict__ x, const int64_t* __restrict__ label,
                                                            const float* __restrict__ d, float* __restrict__ picked,
                                                            float* __restrict__ dx, __nv_bfloat16* __restrict__ dxb, int64_t V,
                                                            int64_t rows) {
-  __shared__ float red[32];
+  __shared__ float redm[32], reds[32], fin[2];
   extern __shared__ float4 stage[];  // [NC][XR_T]: the next row
   constexpr int NC = VPT / 4;
   const int64_t G = gridDim.x;
+  const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5;
   auto prefetch = [&](int64_t r) {
     if (r < rows) {
       const float* xr = x + r * V;
@@ -103,6 +118,9 @@ __global__ void __launch_bounds__(XR_T, 1) xent_reg_kernel(const float* __restri
   };
   prefetch(blockIdx.x);
   for (int64_t r = blockIdx.x; r < rows; r += G) {
+    int64_t lab = label[r];
+    if (lab < 0) lab += V;
+    const bool ok = lab >= 0 && lab < V;
     xr_cp_async_wait_all();
     float v[NC][4];
     float m = -INFINITY;
@@ -119,40 +137,62 @@ __global__ void __launch_bounds__(XR_T, 1) xent_reg_kernel(const float* __restri
       for (int k = 0; k < 4; ++k) m = fmaxf(m, v[c][k]);
     }
     prefetch(r + G);  // this thread's slots are in registers now
-    const float M = block_max(m, red);
-    int64_t lab = label[r];
-    if (lab < 0) lab += V;
-    const bool ok = lab >= 0 && lab < V;
-    float xl = 0.f, s = 0.f;
+    // e = exp(x - m_t), kept in place of x
+    float s = 0.f;
+    const float ml = m * XR_LOG2E;
 #pragma unroll
-    for (int c = 0; c < NC; ++c) {
-      const int64_t col = ((int64_t)c * XR_T + threadIdx.x) * 4;
+    for (int c = 0; c < NC; ++c)
 #pragma unroll
       for (int k = 0; k < 4; ++k) {
-        if (col + k == lab) xl = v[c][k];
-        const float e = (v[c][k] == -INFINITY) ? 0.f : expf(v[c][k] - M);
+        const float e = v[c][k] == -INFINITY ? 0.f : exp2f(fmaf(v[c][k], XR_LOG2E, -ml));
         v[c][k] = e;
         s += e;
       }
+    // block merge of the (m, s) pairs
+    float bm = m, bs = s;
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+      const float m2 = __shfl_xor_sync(0xffffffffu, bm, o), s2 = __shfl_xor_sync(0xffffffffu, bs, o);
+      xr_merge(bm, bs, m2, s2);
     }
-    const float S = block_sum(s, red);
+    if (lane == 0) {
+      redm[wid] = bm;
+      reds[wid] = bs;
+    }
+    __syncthreads();
+    if (wid == 0) {
+      constexpr int NW = XR_T / 32;
+      bm = lane < NW ? redm[lane] : -INFINITY;
+      bs = lane < NW ? reds[lane] : 0.f;
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) {
+        const float m2 = __shfl_xor_sync(0xffffffffu, bm, o), s2 = __shfl_xor_sync(0xffffffffu, bs, o);
+        xr_merge(bm, bs, m2, s2);
+      }
+      if (lane == 0) {
+        fin[0] = bm;
+        fin[1] = bs;
+      }
+    }
+    __syncthreads();
+    const float M = fin[0], S = fin[1];
     const float lse = M + logf(S);
-    // the label's logit: exactly one thread holds it
-    const bool holder = ok && ((lab >> 2) % XR_T) == threadIdx.x;
-    if (holder && picked) picked[r] = xl - lse;
-    if (threadIdx.x == 0 && !ok) {
-      raise_device_error(B200_ERR_ARG);
-      if (picked) picked[r] = 0.f;
+    // the label's logit, read back by one thread (the row is in L2)
+    if (threadIdx.x == 0) {
+      if (!ok) raise_device_error(B200_ERR_ARG);
+      if (picked) picked[r] = ok ? __ldg(x + r * V + lab) - lse : 0.f;
     }
     if (!dx && !dxb) continue;
-    const float dr = d[r], inv = 1.f / S;
+    // softmax = e * exp(m_t - M) / S; dx = d * ([j == label] - softmax)
+    const float dr = d[r];
+    const float sc = m == -INFINITY ? 0.f : exp2f((m - M) * XR_LOG2E) / S;
 #pragma unroll
     for (int c = 0; c < NC; ++c) {
       const int64_t col = ((int64_t)c * XR_T + threadIdx.x) * 4;
       if (col >= V) continue;
       float o[4];
 #pragma unroll
-      for (int k = 0; k < 4; ++k) o[k] = dr * ((col + k == lab ? 1.f : 0.f) - v[c][k] * inv);
+      for (int k = 0; k < 4; ++k) o[k] = dr * ((col + k == lab ? 1.f : 0.f) - v[c][k] * sc);
       if (dx) __stcs(reinterpret_cast<float4*>(dx + r * V + col), make_float4(o[0], o[1], o[2], o[3]));
       if (dxb) {
         __nv_bfloat162 lo = __floats2bfloat162_rn(o[0], o[1]), hi = __floats2bfloat162_rn(o[2], o[3]);

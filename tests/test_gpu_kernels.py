@@ -138,6 +138,8 @@ def test_indexing_ops():
     table = r.standard_normal((50, 8), dtype=np.float32)
     ids = r.integers(0, 50, 200)
     np.testing.assert_array_equal(to_np(ops.op_take(T(table), T(ids), axis=0)), np.take(table, ids, axis=0))
+    table6 = r.standard_normal((50, 6), dtype=np.float32)  # rows not a whole number of 16-byte groups
+    np.testing.assert_array_equal(to_np(ops.op_take(T(table6), T(ids), axis=0)), np.take(table6, ids, axis=0))
     upd = r.standard_normal((200, 8), dtype=np.float32)
     ref = O.execute_op("TensorScatterAdd", np.zeros_like(table), ids.reshape(200, 1), upd)
     np.testing.assert_allclose(to_np(ops.op_tensor_scatter_add(T(np.zeros_like(table)), T(ids.reshape(200, 1)), T(upd))), ref, rtol=1e-5, atol=1e-5)
@@ -472,7 +474,7 @@ def test_conv2d_fused_epilogues(N, C, H, O, stride, padding):
     try:
         n0 = L.launch_count()
         y = ops.op_conv2d(T(x), T(w), relu=True, **kw)
-        assert L.launch_count() - n0 == 1  # one implicit-GEMM launch, no staging
+        assert L.launch_count() - n0 == 2  # the bf16 channels-last copy of x, then the implicit GEMM
         y_plain = ops.op_conv2d(T(x), T(w), **kw)
         assert torch.equal(y, torch.where(y_plain > 0, y_plain, torch.zeros_like(y_plain)))
         pre = O_.execute_op("Conv2D", x, w, contraction_rounding="bf16", **kw)
@@ -491,15 +493,16 @@ def test_conv2d_fused_epilogues(N, C, H, O, stride, padding):
 
 
 def test_conv2d_implicit_gemm_bounds():
-    """Shapes the implicit GEMM does not take are reported (2048 taps x channels at most),
+    """Shapes the implicit GEMM does not take are reported (2048 reduction indices at most,
+    channels padded to a multiple of 8),
     and a fused epilogue for them raises instead of running anything else."""
     from b200 import _lib as L
     from b200 import ops
     from b200.errors import UnimplementedMathError
 
     lib = L.lib()
-    assert lib.b200_conv2d_igemm_supported(0, 2, 227, 8, 8, 16, 3, 3, 6, 6, 1, 1, 0, 0) == 1  # 2043 taps x channels
-    assert lib.b200_conv2d_igemm_supported(0, 2, 228, 8, 8, 16, 3, 3, 6, 6, 1, 1, 0, 0) == 0  # 2052
+    assert lib.b200_conv2d_igemm_supported(0, 2, 224, 8, 8, 16, 3, 3, 6, 6, 1, 1, 0, 0) == 1  # 2016 reduction indices
+    assert lib.b200_conv2d_igemm_supported(0, 2, 228, 8, 8, 16, 3, 3, 6, 6, 1, 1, 0, 0) == 0  # 232 padded x 9 = 2088
     assert lib.b200_conv2d_igemm_supported(1, 2, 16, 8, 8, 228, 3, 3, 6, 6, 1, 1, 0, 0) == 0  # dgrad: O x taps
     assert lib.b200_conv2d_igemm_supported(2, 2, 228, 8, 8, 16, 3, 3, 6, 6, 1, 1, 0, 0) == 0  # wgrad: C x taps
     ops.Config.conv_dtype = "bf16"
@@ -716,6 +719,20 @@ def test_elementwise_flat_modes_dtypes(shape):
     ref = np.tanh(x * y + rowv)
     np.testing.assert_allclose(to_np(out[0]), ref, rtol=1e-5, atol=1e-6)
     np.testing.assert_allclose(to_np(out[1].float()), ref, rtol=1e-2, atol=1e-2)
+    # sums of several inputs (the straight-line sum kernel) keep the program's left-to-right
+    # order: bit-identical to numpy's fp32 ((a + b) + c) + d, with a vector operand and a
+    # repeated input
+    z = r.standard_normal(shape).astype(np.float32)
+    p = ops.Prog()
+    la, lb, lc, lv = p.load(X), p.load(Y), p.load(T(z)), p.load(T(vec))
+    s1 = p.op("ADD", la, lb)
+    s2 = p.op("ADD", lc, s1)
+    s3 = p.op("ADD", s2, lv)
+    s4 = p.op("ADD", s3, la)
+    out = p.run([(s4, torch.float32), (s4, torch.bfloat16)], shape)
+    ref = (((x + y) + z) + vec) + x
+    np.testing.assert_array_equal(to_np(out[0]), ref)
+    np.testing.assert_array_equal(to_np(out[1].float()), to_np(T(ref).to(torch.bfloat16).float()))
 
 
 @pytest.mark.parametrize("R,V", [(33, 32000), (17, 1000), (9, 4096), (5, 12)])
