@@ -1149,23 +1149,48 @@ def _conv_call(kind: int, a: torch.Tensor, b: torch.Tensor, out: torch.Tensor, d
         L.call(names[kind], L.F32, a.data_ptr(), b.data_ptr(), out.data_ptr(), *dims, stream_ptr())
         return
     if L.lib().b200_conv2d_igemm_supported(kind, *dims):
+        N, Cc, H, W, O = dims[:5]
+        # the packed weight image (fwd / dgrad) or the split partials (wgrad); the
+        # channels-last copies come from channels_last() and are shared within a run
         ws_bytes = int(L.lib().b200_conv2d_igemm_workspace_bytes(kind, *dims))
-        ws = torch.empty(max(16, ws_bytes), dtype=torch.uint8, device=device())
+        ws = torch.empty(max(256, ws_bytes), dtype=torch.uint8, device=device())
+        ws_ptr = ws.data_ptr()
         if kind == 0:
-            L.call("b200_conv2d_fwd_igemm", a.data_ptr(), b.data_ptr(), out.data_ptr(), *dims, 1 if relu else 0, ws.data_ptr(),
-                   ws_bytes, stream_ptr())
+            L.call("b200_conv2d_fwd_igemm", a.data_ptr(), channels_last(a, _rup(Cc, 8)).data_ptr(), b.data_ptr(),
+                   out.data_ptr(), *dims, 1 if relu else 0, ws_ptr, ws_bytes, stream_ptr())
         elif kind == 1:
-            L.call("b200_conv2d_dgrad_igemm", a.data_ptr(), b.data_ptr(), _ptr(mask), out.data_ptr(), *dims, ws.data_ptr(),
-                   ws_bytes, stream_ptr())
+            L.call("b200_conv2d_dgrad_igemm", a.data_ptr(), channels_last(a, _rup(O, 8)).data_ptr(), b.data_ptr(), _ptr(mask),
+                   out.data_ptr(), *dims, ws_ptr, ws_bytes, stream_ptr())
         else:
-            L.call("b200_conv2d_wgrad_igemm", a.data_ptr(), b.data_ptr(), out.data_ptr(), *dims, ws.data_ptr(), ws_bytes,
-                   stream_ptr())
+            L.call("b200_conv2d_wgrad_igemm", a.data_ptr(), channels_last(a, _rup(Cc, 8)).data_ptr(), b.data_ptr(),
+                   channels_last(b, _rup(O, 64)).data_ptr(), out.data_ptr(), *dims, ws_ptr, ws_bytes, stream_ptr())
         return
     if fused:
         raise UnimplementedMathError("fused convolution epilogue for a shape outside the implicit GEMM")
     ws_bytes = int(L.lib().b200_conv2d_tc_workspace_bytes(kind, *dims))
     ws = torch.empty(max(1, ws_bytes), dtype=torch.uint8, device=device())
     L.call(names[kind] + "_tc", a.data_ptr(), b.data_ptr(), out.data_ptr(), *dims, ws.data_ptr(), ws_bytes, stream_ptr())
+
+
+def _rup(v: int, m: int) -> int:
+    return (int(v) + m - 1) // m * m
+
+
+def channels_last(t: torch.Tensor, cp: int) -> torch.Tensor:
+    """bf16 channels-last copy [N, H, W, cp] (channels >= C zero) of a dense fp32 NCHW
+    tensor, the layout the implicit-GEMM convolutions copy their tiles from. Within a plan
+    run the copy is kept beside the bf16 operand casts, so the forward convolution and the
+    weight gradient of the same activation (or the input and weight gradients of the same
+    cotangent) share one."""
+    key = (t.data_ptr(), t.numel(), t.dtype, t._version, ("channels_last", cp))
+    hit = _CAST_CACHE.get(key)
+    if hit is not None and hit[0] is t:
+        return hit[1]
+    N, Cc, H, W = (int(v) for v in t.shape)
+    y = torch.empty((N, H, W, cp), dtype=torch.bfloat16, device=device())
+    L.call("b200_conv2d_channels_last", t.data_ptr(), y.data_ptr(), N, Cc, H * W, cp, stream_ptr())
+    _CAST_CACHE[key] = (t, y)
+    return y
 
 
 def conv_fused_ok(kind: int, x_shape: tuple, w_shape: tuple, stride, padding, out_hw: tuple | None = None) -> bool:

@@ -28,7 +28,7 @@
 // reduction indices of one tap are 16 contiguous bytes. Each producer warp then builds a
 // whole 128 x 64 A tile with 16-byte cp.async copies (zero-filled where a tap falls
 // outside the image), waits for its own copies, and arrives on the stage's barrier; each
-// producer warp owns one stage and the warps take K blocks round-robin, so up to eight
+// producer warp owns one stage and the warps take K blocks round-robin, so up to seven
 // tiles are in flight per SM. The weights (B) are gathered once per CTA into shared memory
 // and stay resident.
 // wgrad: x and dy both get channels-last bf16 copies (dy's channels padded to 64); the
@@ -36,10 +36,10 @@
 // pixels of a K block, 128-byte rows of 64 GEMM rows (taps x channels) of A and of 64
 // output channels of B, copied by the same one-warp-per-stage cp.async producers.
 //
-// Persistent kernel, one CTA per SM, 416 threads: warps 0-7 producers, warp 8 allocates
-// TMEM and issues four 128 x BN x 16 MMAs per K block, warps 9-12 epilogue (one TMEM lane
-// quarter each, warp % 4; lane = GEMM row, so a store of one column covers 32
-// consecutive pixels). Pieces of 16 bytes are XORed by row & 7 (the TMA 128-byte
+// Persistent kernel, one CTA per SM, 512 threads: warps 0-6 producers, warp 7 allocates
+// TMEM and issues four 128 x BN x 16 MMAs per K block, warps 8-15 epilogue (two per TMEM
+// lane quarter, warp % 4, on alternate 32-column chunks; lane = GEMM row, so a store of one
+// column covers 32 consecutive pixels). Pieces of 16 bytes are XORed by row & 7 (the TMA 128-byte
 // swizzle). Every mbarrier wait is bounded; a warp whose wait gives up stops, and the CTA
 // winds down (the MMA warp drains its MMAs before TMEM is freed).
 #include <algorithm>
@@ -53,9 +53,12 @@ using namespace tc;
 
 enum Mode { FWD = 0, DGRAD = 1, WGRAD = 2 };
 
-constexpr int PROD_WARPS = 8, PROD_THREADS = PROD_WARPS * 32;
+// seven producer warps, the MMA warp and eight epilogue warps: 16 warps, four per SM
+// sub-partition, so each thread may hold 128 registers
+constexpr int PROD_WARPS = 7, PROD_THREADS = PROD_WARPS * 32;
 constexpr int MMA_WARP = PROD_WARPS;
-constexpr int THREADS = (PROD_WARPS + 1 + 4) * 32;
+constexpr int EPI_WARPS = 8;  // two per TMEM lane quarter, on alternate 32-column chunks
+constexpr int THREADS = (PROD_WARPS + 1 + EPI_WARPS) * 32;
 constexpr int BM = 128, BK = 64;
 constexpr uint32_t A_BYTES = BM * BK * 2;
 constexpr int KTAB_MAX = 2048;          // reduction indices (fwd / dgrad) or taps x channels (wgrad) one table holds
@@ -90,8 +93,14 @@ struct Args {
   const __nv_bfloat16* an;    // fwd / wgrad: x, dgrad: dy, as bf16 NHWC [n][h][w][CP]
   const __nv_bfloat16* bn;    // wgrad: dy as bf16 NHWC [n][oh][ow][OPW]
   const float* bsrc;          // fwd / dgrad: w (fp32 OIHW)
+  const uint8_t* bimg;        // fwd / dgrad: the resident B operand, bf16 and swizzled as in shared memory
   float* out;                 // fwd: y    dgrad: dx   wgrad: partials [splits][O][M]
   const float* mask;          // dgrad: dx *= (mask > 0) when not null
+  // fwd / dgrad with 64-channel K blocks: one TMA box per K block instead of cp.async.
+  // A tile is tn images x th rows x tw columns of output pixels (fwd) or class pixels
+  // (dgrad); tile = image block * tiles_h + row block
+  int tma, tw, th, tn, tiles_h;
+  uint32_t box_bytes;         // tw * th * tn * 128
 };
 
 __device__ __forceinline__ uint32_t swz(int r, int j) { return (uint32_t)r * 128u + ((uint32_t)(j ^ (r & 7)) << 4); }
@@ -126,7 +135,19 @@ __device__ __forceinline__ bool item_of(const Args& a, int it, Item& r) {
   x /= a.tiles_n;
   r.cls = x % a.ncls;
   r.mt = x / a.ncls;
+  if (a.tma) {  // row block inside the image (fwd: OH rows, dgrad: the class's rows)
+    return a.cls_k[r.cls] > 0 && (r.mt % a.tiles_h) * a.th < a.cls_hc[r.cls];
+  }
   return r.mt * BM < a.cls_m[r.cls];
+}
+
+// TMA tiles: tile row r -> (image, row, column); false past the tile's pixels
+__device__ __forceinline__ bool tile_pixel(const Args& a, const Item& it, int r, int& n, int& hh, int& ww) {
+  const int wi = r % a.tw, q = r / a.tw, hi = q % a.th, ni = q / a.th;
+  n = (it.mt / a.tiles_h) * a.tn + ni;
+  hh = (it.mt % a.tiles_h) * a.th + hi;
+  ww = wi;
+  return ni < a.tn && n < a.N && hh < a.cls_hc[it.cls] && ww < a.cls_wc[it.cls];
 }
 __device__ __forceinline__ int kblocks_of(const Args& a, const Item& r) {
   if (a.lq == 0) return (a.cls_k[r.cls] + BK - 1) / BK;
@@ -157,8 +178,51 @@ __global__ void __launch_bounds__(256) nchw_to_nhwc_bf16_kernel(const float* __r
   }
 }
 
+// The fwd / dgrad weight operand as the kernel keeps it in shared memory: [K blocks of all
+// classes][column tiles][BN rows x 64] bf16 in the 128-byte swizzle, built once per call
+// from the fp32 OIHW weights (one 16-byte piece per thread), so each CTA only copies it.
+//   fwd:   B[o, k = t*Cp + c]            = w[o, c, i, j]   (0 for c >= C)
+//   dgrad: B[c, k = u*Op + o] of a class = w[o, c, i, j]   (0 for o >= O)
 template <int MODE>
-__global__ void __launch_bounds__(THREADS, 1) conv_igemm_kernel(const __grid_constant__ Args a) {
+__global__ void __launch_bounds__(256) pack_b_kernel(const __grid_constant__ Args a, uint8_t* __restrict__ img) {
+  const int pieces_per_kb = a.tiles_n * a.BN * 8;
+  const int total = a.kb_total * pieces_per_kb;
+  const int KHW = a.KH * a.KW;
+  for (int p = blockIdx.x * blockDim.x + threadIdx.x; p < total; p += gridDim.x * blockDim.x) {
+    const int kbg = p / pieces_per_kb, rem = p - kbg * pieces_per_kb;
+    const int col = rem >> 3, j8 = rem & 7;  // column over all column tiles
+    int c = 0;
+    while (c + 1 < a.ncls && a.cls_kb[c + 1] <= kbg) ++c;
+    const int k0 = (kbg - a.cls_kb[c]) * BK + j8 * 8;  // chunk start within the class
+    int tap = 0, ch0 = 0;
+    if (MODE == FWD) {
+      tap = k0 / a.CP;
+      ch0 = k0 - tap * a.CP;
+    } else {
+      const int uu = k0 / a.CP, nj = a.cls_nj[c];
+      const int ui = uu / nj, uj = uu - ui * nj;
+      const int i = (a.cls_ph[c] + a.pt) % a.sh + ui * a.sh, j = (a.cls_pw[c] + a.pl) % a.sw + uj * a.sw;
+      tap = i * a.KW + j;
+      ch0 = k0 - uu * a.CP;
+    }
+    const bool kin = k0 < a.cls_k[c] && col < a.Nc;
+    float v[8];
+#pragma unroll
+    for (int e = 0; e < 8; ++e) {
+      const int ch = ch0 + e;  // fwd: input channel c; dgrad: output channel o
+      const bool ok = kin && ch < (MODE == FWD ? a.C : a.O);
+      const int off = MODE == FWD ? (col * a.C + ch) * KHW + tap : (ch * a.C + col) * KHW + tap;
+      v[e] = ok ? __ldg(a.bsrc + off) : 0.f;
+    }
+    const int nt = col / a.BN, rr = col - nt * a.BN;
+    *reinterpret_cast<uint4*>(img + (size_t)((kbg * a.tiles_n + nt) * a.BN) * 128u + swz(rr, j8)) =
+        make_uint4(pack_bf16(v[0], v[1]), pack_bf16(v[2], v[3]), pack_bf16(v[4], v[5]), pack_bf16(v[6], v[7]));
+  }
+}
+
+template <int MODE>
+__global__ void __launch_bounds__(THREADS, 1) conv_igemm_kernel(const __grid_constant__ Args a,
+                                                                const __grid_constant__ CUtensorMap amap) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* sStages = smem;
@@ -207,7 +271,7 @@ __global__ void __launch_bounds__(THREADS, 1) conv_igemm_kernel(const __grid_con
     }
     for (int b = 0; b < 2; ++b) {
       mbar_init(&acc_full[b], 1);
-      mbar_init(&acc_empty[b], 4);
+      mbar_init(&acc_empty[b], EPI_WARPS);
     }
     mbar_init(drained, 1);
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
@@ -222,55 +286,14 @@ __global__ void __launch_bounds__(THREADS, 1) conv_igemm_kernel(const __grid_con
   const uint32_t tmem_base = *tmem_slot;
 
   if constexpr (MODE != WGRAD) {
-    // resident B: [K blocks of all classes][column tiles][BN rows x 64] bf16, gathered once
-    // from the fp32 OIHW weights. A pass keeps 8 pieces per thread in flight (64 loads).
-    //   fwd:   B[o, k = t*Cp + c]            = w[o, c, i, j]   (0 for c >= C)
-    //   dgrad: B[c, k = u*Op + o] of a class = w[o, c, i, j]   (0 for o >= O)
+    // resident B: the packed image (pack_b_kernel) copied in with coalesced 16-byte loads
     if (warp < PROD_WARPS) {
-      const int pieces_per_kb = a.tiles_n * a.BN * 8;
-      const int total = a.kb_total * pieces_per_kb;
-      const int KHW = a.KH * a.KW;
-      for (int p0 = threadIdx.x; p0 < total; p0 += 8 * PROD_THREADS) {
-        float v[64];
-#pragma unroll
-        for (int u = 0; u < 8; ++u) {
-          const int p = min(p0 + u * PROD_THREADS, total - 1);
-          const int kbg = p / pieces_per_kb, rem = p - kbg * pieces_per_kb;
-          const int col = rem >> 3, j8 = rem & 7;  // column over all column tiles
-          int c = 0;
-          while (c + 1 < a.ncls && a.cls_kb[c + 1] <= kbg) ++c;
-          const int k0 = (kbg - a.cls_kb[c]) * BK + j8 * 8;  // chunk start within the class
-          int tap = 0, ch0 = 0;
-          if (MODE == FWD) {
-            tap = k0 / a.CP;
-            ch0 = k0 - tap * a.CP;
-          } else {
-            const int uu = k0 / a.CP, nj = a.cls_nj[c];
-            const int ui = uu / nj, uj = uu - ui * nj;
-            const int i = (a.cls_ph[c] + a.pt) % a.sh + ui * a.sh, j = (a.cls_pw[c] + a.pl) % a.sw + uj * a.sw;
-            tap = i * a.KW + j;
-            ch0 = k0 - uu * a.CP;
-          }
-          const bool kin = k0 < a.cls_k[c] && col < a.Nc;
-#pragma unroll
-          for (int e = 0; e < 8; ++e) {
-            const int ch = ch0 + e;  // fwd: input channel c; dgrad: output channel o
-            const bool ok = kin && ch < (MODE == FWD ? a.C : a.O);
-            const int off = MODE == FWD ? (col * a.C + ch) * KHW + tap : (ch * a.C + col) * KHW + tap;
-            const float x = __ldg(a.bsrc + (ok ? off : 0));
-            v[u * 8 + e] = ok ? x : 0.f;
-          }
-        }
-#pragma unroll
-        for (int u = 0; u < 8; ++u) {
-          const int p = p0 + u * PROD_THREADS;
-          if (p < total) {
-            const int kbg = p / pieces_per_kb, rem = p - kbg * pieces_per_kb;
-            const int col = rem >> 3, j8 = rem & 7;
-            const int nt = col / a.BN, rr = col - nt * a.BN;
-            put8(smem_u32(sResB) + (uint32_t)((kbg * a.tiles_n + nt) * a.BN) * 128u + swz(rr, j8), &v[u * 8]);
-          }
-        }
+      const int n16 = (int)((uint32_t)a.kb_total * a.tiles_n * a.BN * 8u);
+      const uint4* src = reinterpret_cast<const uint4*>(a.bimg);
+      const uint32_t dst = smem_u32(sResB);
+      for (int i = threadIdx.x; i < n16; i += PROD_THREADS) {
+        const uint4 u = __ldg(src + i);
+        st_shared_v4(dst + (uint32_t)i * 16u, u.x, u.y, u.z, u.w);
       }
       fence_proxy_async_smem();
     }
@@ -286,6 +309,41 @@ __global__ void __launch_bounds__(THREADS, 1) conv_igemm_kernel(const __grid_con
       if (!item_of(a, it, r)) continue;
       const int m0 = r.mt * BM, n0 = r.nt * a.BN;
       const int nkb = kblocks_of(a, r);
+      if (MODE != WGRAD && a.tma) {
+        // one thread loads each K block as one TMA box: 64 channels of one tap for every
+        // pixel of the tile (fwd: the box walks the input with the convolution's stride;
+        // dgrad: dy at the class tap's offset); taps falling outside the image read zeros
+        if (nkb <= 0) continue;
+        const uint32_t first = L;
+        L += (uint32_t)nkb;
+        if (warp != 0 || lane != 0) continue;
+        const int cbs = a.CP / 64;  // 64-channel blocks per tap
+        const int nb = r.mt / a.tiles_h, hb0 = (r.mt % a.tiles_h) * a.th;
+        for (int kb = 0; kb < nkb; ++kb) {
+          const uint32_t Lk = first + (uint32_t)kb;
+          const int s = (int)(Lk % (uint32_t)a.stages);
+          if (!mbar_wait(&empty[s], ((Lk / (uint32_t)a.stages) & 1) ^ 1)) {
+            ok = false;
+            break;
+          }
+          const int u = kb / cbs, cb = kb - u * cbs;
+          int c1, c2;
+          if (MODE == FWD) {
+            const int i = u / a.KW, j = u - i * a.KW;
+            c1 = j - a.pl;                       // input column of output column 0
+            c2 = hb0 * a.sh - a.pt + i;          // input row of the tile's first output row
+          } else {
+            const int nj = a.cls_nj[r.cls];
+            const int ui = u / nj, uj = u - ui * nj;
+            const int i = (a.cls_ph[r.cls] + a.pt) % a.sh + ui * a.sh, j = (a.cls_pw[r.cls] + a.pl) % a.sw + uj * a.sw;
+            c1 = (a.cls_pw[r.cls] + a.pl - j) / a.sw;        // dw
+            c2 = hb0 + (a.cls_ph[r.cls] + a.pt - i) / a.sh;  // first class row + dh
+          }
+          mbar_expect_tx(&full[s], a.box_bytes);
+          tma_load_4d(sStages + (uint32_t)s * a.stage_bytes, &amap, &full[s], cb * 64, c1, c2, nb * a.tn);
+        }
+        continue;
+      }
       if constexpr (MODE != WGRAD) {
         // K block L goes to warp L % stages into stage L % stages: every stage has one
         // producer warp that refills it in order, so a parity wait can never pass a phase
@@ -455,7 +513,7 @@ __global__ void __launch_bounds__(THREADS, 1) conv_igemm_kernel(const __grid_con
     }
   } else {
     // ------------------------------------------------------------ epilogue
-    const int q = warp & 3;
+    const int q = warp & 3, half = (warp - MMA_WARP - 1) >> 2;
     uint32_t T = 0;
     bool ok = true;
     for (int it = blockIdx.x; it < a.items && ok; it += gridDim.x) {
@@ -468,9 +526,21 @@ __global__ void __launch_bounds__(THREADS, 1) conv_igemm_kernel(const __grid_con
       if (!ok) break;
       tc_fence_after();
       const int m = r.mt * BM + q * 32 + lane;  // this lane's GEMM row
-      const bool rv = m < a.cls_m[r.cls];
+      bool rv = m < a.cls_m[r.cls];
       int64_t obase, ostride;
-      {
+      if (MODE != WGRAD && a.tma) {
+        int n, hh, ww;
+        rv = tile_pixel(a, r, q * 32 + lane, n, hh, ww);
+        if (!rv) n = hh = ww = 0;
+        if (MODE == FWD) {
+          obase = (int64_t)n * a.O * a.P + hh * a.OW + ww;
+          ostride = a.P;
+        } else {
+          const int h = a.cls_ph[r.cls] + a.sh * hh, w = a.cls_pw[r.cls] + a.sw * ww;
+          obase = (int64_t)n * a.C * a.HW + h * a.W + w;
+          ostride = a.HW;
+        }
+      } else {
         const int mm = rv ? m : 0;
         if (MODE == FWD) {
           const int n = mm / a.P, p = mm - n * a.P;
@@ -490,7 +560,12 @@ __global__ void __launch_bounds__(THREADS, 1) conv_igemm_kernel(const __grid_con
       const uint32_t tb = tmem_base + ((uint32_t)(q * 32) << 16) + b * (uint32_t)a.BNT;
       const int n0 = r.nt * a.BN;
       const int ncols = min(a.BN, a.Nc - n0);
-      for (int c0 = 0; c0 < ncols; c0 += 32) {
+      if (half * 32 >= ncols) {  // no chunk for this warp: hand the accumulator back at once
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&acc_empty[b]);
+      }
+      for (int c0 = half * 32; c0 < ncols; c0 += 64) {
         uint32_t v[32];
         tmem_ld32_issue(tb + (uint32_t)c0, v);
         const int nn = min(32, ncols - c0);
@@ -503,7 +578,7 @@ __global__ void __launch_bounds__(THREADS, 1) conv_igemm_kernel(const __grid_con
           for (int i = 0; i < 32; ++i) mv[i] = __ldg(mk + (rv && i < nn ? (int64_t)i * ostride : 0));
         }
         tmem_wait(v);
-        if (c0 + 32 >= ncols) {  // last TMEM read of this item: hand the accumulator back
+        if (c0 + 64 >= ncols) {  // this warp's last TMEM read of the item: hand the accumulator back
           tc_fence_before();
           __syncwarp();
           if (lane == 0) mbar_arrive(&acc_empty[b]);
@@ -642,6 +717,32 @@ static Plan plan(int mode, int64_t N, int64_t C, int64_t H, int64_t W, int64_t O
     a.ktab = (int)(mode == WGRAD ? M / 8 : K / 8);
     max_tiles = ceil_div(M, BM);
   }
+  // fwd / dgrad with whole 64-channel K blocks: TMA boxes over tiles of whole pixel rows
+  a.tma = 0;
+  if (mode != WGRAD && a.CP % 64 == 0) {
+    int rows = 0, cols = 0;  // output rows / columns (fwd), largest class rows / columns (dgrad)
+    for (int c = 0; c < a.ncls; ++c) {
+      rows = std::max(rows, mode == FWD ? (int)OH : a.cls_hc[c]);
+      cols = std::max(cols, mode == FWD ? (int)OW : a.cls_wc[c]);
+    }
+    const int64_t wbox = mode == FWD ? (int64_t)cols * sw : cols;  // elements the box traverses along w
+    if (cols >= 1 && cols <= BM && wbox <= 256) {
+      int th, tn, tiles_h;
+      if ((int64_t)cols * rows <= BM) {
+        th = rows, tiles_h = 1, tn = (int)std::min<int64_t>(BM / (cols * rows), N);
+      } else {
+        tn = 1;
+        tiles_h = (int)ceil_div(rows, BM / cols);
+        th = (int)ceil_div(rows, tiles_h);
+      }
+      if ((mode == FWD ? (int64_t)th * sh : th) <= 256 && tn <= 256) {
+        a.tma = 1, a.tw = cols, a.th = th, a.tn = tn, a.tiles_h = tiles_h;
+        a.box_bytes = (uint32_t)(cols * th * tn) * 128u;
+        if (mode == FWD) a.cls_hc[0] = (int)OH, a.cls_wc[0] = (int)OW;
+        max_tiles = ceil_div(N, (int64_t)tn) * tiles_h;
+      }
+    }
+  }
   a.max_tiles = (int)max_tiles;
   if (a.tiles_n > 255 || max_tiles < 1) {
     p.why = "tile count";
@@ -675,7 +776,8 @@ static Plan plan(int mode, int64_t N, int64_t C, int64_t H, int64_t W, int64_t O
   } else {
     a.stage_bytes = A_BYTES;
     resb = (size_t)a.kb_total * a.tiles_n * a.BN * 128;
-    p.ws = mode == FWD ? (size_t)N * H * W * Cp * 2 : (size_t)N * OH * OW * Op * 2;
+    // the packed weight image, then (when the caller passes none) the channels-last copy
+    p.ws = al256(resb) + (mode == FWD ? (size_t)N * H * W * Cp * 2 : (size_t)N * OH * OW * Op * 2);
   }
   const size_t fixed = 1024 + resb + (size_t)a.ktab * 16 + 64 * 8 + 16;
   if (fixed + 2 * (size_t)a.stage_bytes > SMEM_LIMIT) {
@@ -691,6 +793,31 @@ static Plan plan(int mode, int64_t N, int64_t C, int64_t H, int64_t W, int64_t O
   return p;
 }
 
+// tensor map of a TMA-mode source: the channels-last copy [N, rows, cols, CP] (fwd: x, dgrad:
+// dy), box = 64 channels x the tile's pixels; the fwd box steps through the input with the
+// convolution's stride (element strides sw, sh)
+static int make_source_map(int mode, const Args& a, CUtensorMap* map) {
+  auto enc = get_encode();
+  if (!enc) {
+    set_error("conv2d(implicit GEMM): cuTensorMapEncodeTiled unavailable");
+    return B200_ERR_CUDA;
+  }
+  const uint64_t W = mode == FWD ? a.W : a.OW, H = mode == FWD ? a.H : a.OH;
+  cuuint64_t dims[4] = {(cuuint64_t)a.CP, W, H, (cuuint64_t)a.N};
+  cuuint64_t strides[3] = {(cuuint64_t)a.CP * 2, W * a.CP * 2, H * W * a.CP * 2};
+  cuuint32_t box[4] = {64, (cuuint32_t)(mode == FWD ? a.tw * a.sw : a.tw), (cuuint32_t)(mode == FWD ? a.th * a.sh : a.th),
+                       (cuuint32_t)a.tn};
+  cuuint32_t estr[4] = {1, (cuuint32_t)(mode == FWD ? a.sw : 1), (cuuint32_t)(mode == FWD ? a.sh : 1), 1};
+  const CUresult r = enc(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 4, const_cast<__nv_bfloat16*>(a.an), dims, strides, box, estr,
+                         CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                         CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) {
+    set_error("conv2d(implicit GEMM): cuTensorMapEncodeTiled failed (%d)", (int)r);
+    return B200_ERR_ARG;
+  }
+  return B200_OK;
+}
+
 template <int MODE>
 static int launch(Args a, size_t smem, cudaStream_t s) {
   static bool attr_set[64] = {false};
@@ -700,8 +827,14 @@ static int launch(Args a, size_t smem, cudaStream_t s) {
     cudaFuncSetAttribute(conv_igemm_kernel<MODE>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)SMEM_LIMIT);
     if (dev >= 0 && dev < 64) attr_set[dev] = true;
   }
+  CUtensorMap map;
+  memset(&map, 0, sizeof(map));
+  if (MODE != WGRAD && a.tma) {
+    const int rc = make_source_map(MODE, a, &map);
+    if (rc) return rc;
+  }
   const unsigned grid = (unsigned)std::max(1, std::min(a.items, num_sms()));
-  conv_igemm_kernel<MODE><<<grid, THREADS, smem, s>>>(a);
+  conv_igemm_kernel<MODE><<<grid, THREADS, smem, s>>>(a, map);
   return check_launch("conv2d(implicit GEMM)");
 }
 
@@ -710,6 +843,15 @@ static int repack(const float* src, __nv_bfloat16* dst, int64_t N, int64_t C, in
   const unsigned grid = (unsigned)std::max<int64_t>(1, std::min<int64_t>(ceil_div(total, 256), (int64_t)num_sms() * 16));
   nchw_to_nhwc_bf16_kernel<<<grid, 256, 0, s>>>(src, dst, N, (int)C, HW, (int)Cp);
   return check_launch("conv2d(implicit GEMM, NHWC repack)");
+}
+
+template <int MODE>
+static int pack_b(Args a, const float* w, uint8_t* img, cudaStream_t s) {
+  a.bsrc = w;
+  const int64_t total = (int64_t)a.kb_total * a.tiles_n * a.BN * 8;
+  const unsigned grid = (unsigned)std::max<int64_t>(1, std::min<int64_t>(ceil_div(total, 256), (int64_t)num_sms() * 8));
+  pack_b_kernel<MODE><<<grid, 256, 0, s>>>(a, img);
+  return check_launch("conv2d(implicit GEMM, weight image)");
 }
 
 static int check_dims(int64_t N, int64_t C, int64_t H, int64_t W, int64_t O, int64_t KH, int64_t KW, int64_t OH, int64_t OW,
@@ -741,9 +883,17 @@ extern "C" size_t b200_conv2d_igemm_workspace_bytes(int op, int64_t N, int64_t C
   return p.ok ? p.ws : 0;
 }
 
-extern "C" int b200_conv2d_fwd_igemm(const float* x, const float* w, float* y, int64_t N, int64_t C, int64_t H, int64_t W,
-                                     int64_t O, int64_t KH, int64_t KW, int64_t OH, int64_t OW, int64_t sh, int64_t sw,
-                                     int64_t pt, int64_t pl, int relu, void* ws, size_t ws_bytes, void* stream) {
+extern "C" int b200_conv2d_channels_last(const float* src, void* dst, int64_t N, int64_t C, int64_t HW, int64_t Cp,
+                                         void* stream) {
+  B200_REQUIRE(src && dst && (reinterpret_cast<uintptr_t>(dst) & 15) == 0, "conv2d_channels_last: null or unaligned pointer");
+  B200_REQUIRE(N >= 0 && C >= 1 && HW >= 1 && Cp >= C && Cp % 8 == 0, "conv2d_channels_last: bad sizes");
+  if (N == 0) return B200_OK;
+  return repack(src, reinterpret_cast<__nv_bfloat16*>(dst), N, C, HW, Cp, as_stream(stream));
+}
+
+extern "C" int b200_conv2d_fwd_igemm(const float* x, const void* x_cl, const float* w, float* y, int64_t N, int64_t C, int64_t H,
+                                     int64_t W, int64_t O, int64_t KH, int64_t KW, int64_t OH, int64_t OW, int64_t sh,
+                                     int64_t sw, int64_t pt, int64_t pl, int relu, void* ws, size_t ws_bytes, void* stream) {
   int rc = check_dims(N, C, H, W, O, KH, KW, OH, OW, sh, sw, pt, pl);
   if (rc) return rc;
   if (N == 0) return B200_OK;
@@ -753,20 +903,28 @@ extern "C" int b200_conv2d_fwd_igemm(const float* x, const float* w, float* y, i
     set_error("conv2d_fwd_igemm: unsupported shape (%s)", p.why);
     return B200_ERR_UNSUPPORTED;
   }
-  B200_REQUIRE(ws && ws_bytes >= p.ws && (reinterpret_cast<uintptr_t>(ws) & 15) == 0,
-               "conv2d_fwd_igemm: workspace %zu < %zu (16-byte aligned)", ws_bytes, p.ws);
   cudaStream_t s = as_stream(stream);
-  auto* xn = reinterpret_cast<__nv_bfloat16*>(ws);
-  if ((rc = repack(x, xn, N, C, H * W, p.a.CP, s))) return rc;
+  B200_REQUIRE(ws && ws_bytes >= p.ws && (reinterpret_cast<uintptr_t>(ws) & 255) == 0,
+               "conv2d_fwd_igemm: workspace %zu < %zu (256-byte aligned)", ws_bytes, p.ws);
+  uint8_t* img = reinterpret_cast<uint8_t*>(ws);
+  const __nv_bfloat16* xn = reinterpret_cast<const __nv_bfloat16*>(x_cl);
+  if (xn) {
+    B200_REQUIRE((reinterpret_cast<uintptr_t>(xn) & 15) == 0, "conv2d_fwd_igemm: x_cl not 16-byte aligned");
+  } else {
+    auto* cp = reinterpret_cast<__nv_bfloat16*>(img + al256((size_t)p.a.kb_total * p.a.tiles_n * p.a.BN * 128));
+    if ((rc = repack(x, cp, N, C, H * W, p.a.CP, s))) return rc;
+    xn = cp;
+  }
+  if ((rc = pack_b<FWD>(p.a, w, img, s))) return rc;
   p.a.relu = relu ? 1 : 0;
-  p.a.an = xn, p.a.bn = nullptr, p.a.bsrc = w, p.a.out = y, p.a.mask = nullptr;
+  p.a.an = xn, p.a.bn = nullptr, p.a.bsrc = w, p.a.bimg = img, p.a.out = y, p.a.mask = nullptr;
   return launch<FWD>(p.a, p.smem, s);
 }
 
-extern "C" int b200_conv2d_dgrad_igemm(const float* dy, const float* w, const float* mask, float* dx, int64_t N, int64_t C,
-                                       int64_t H, int64_t W, int64_t O, int64_t KH, int64_t KW, int64_t OH, int64_t OW,
-                                       int64_t sh, int64_t sw, int64_t pt, int64_t pl, void* ws, size_t ws_bytes,
-                                       void* stream) {
+extern "C" int b200_conv2d_dgrad_igemm(const float* dy, const void* dy_cl, const float* w, const float* mask, float* dx,
+                                       int64_t N, int64_t C, int64_t H, int64_t W, int64_t O, int64_t KH, int64_t KW,
+                                       int64_t OH, int64_t OW, int64_t sh, int64_t sw, int64_t pt, int64_t pl, void* ws,
+                                       size_t ws_bytes, void* stream) {
   int rc = check_dims(N, C, H, W, O, KH, KW, OH, OW, sh, sw, pt, pl);
   if (rc) return rc;
   if (N == 0) return B200_OK;
@@ -776,9 +934,11 @@ extern "C" int b200_conv2d_dgrad_igemm(const float* dy, const float* w, const fl
     set_error("conv2d_dgrad_igemm: unsupported shape (%s)", p.why);
     return B200_ERR_UNSUPPORTED;
   }
-  B200_REQUIRE(ws && ws_bytes >= p.ws && (reinterpret_cast<uintptr_t>(ws) & 15) == 0,
-               "conv2d_dgrad_igemm: workspace %zu < %zu (16-byte aligned)", ws_bytes, p.ws);
   cudaStream_t s = as_stream(stream);
+  B200_REQUIRE(ws && ws_bytes >= p.ws && (reinterpret_cast<uintptr_t>(ws) & 255) == 0,
+               "conv2d_dgrad_igemm: workspace %zu < %zu (256-byte aligned)", ws_bytes, p.ws);
+  B200_REQUIRE((reinterpret_cast<uintptr_t>(dy_cl) & 15) == 0, "conv2d_dgrad_igemm: dy_cl not 16-byte aligned");
+  uint8_t* img = reinterpret_cast<uint8_t*>(ws);
   // pixels that no tap reaches (a class without taps: stride above the kernel size) are zero
   for (int c = 0; c < p.a.ncls; ++c)
     if (p.a.cls_k[c] == 0) {
@@ -786,16 +946,22 @@ extern "C" int b200_conv2d_dgrad_igemm(const float* dy, const float* w, const fl
       if ((rc = check_launch("conv2d_dgrad_igemm(zero)"))) return rc;
       break;
     }
-  auto* dyn = reinterpret_cast<__nv_bfloat16*>(ws);
-  if ((rc = repack(dy, dyn, N, O, OH * OW, p.a.CP, s))) return rc;
+  const __nv_bfloat16* dyn = reinterpret_cast<const __nv_bfloat16*>(dy_cl);
+  if (!dyn) {
+    auto* cp = reinterpret_cast<__nv_bfloat16*>(img + al256((size_t)p.a.kb_total * p.a.tiles_n * p.a.BN * 128));
+    if ((rc = repack(dy, cp, N, O, OH * OW, p.a.CP, s))) return rc;
+    dyn = cp;
+  }
+  if ((rc = pack_b<DGRAD>(p.a, w, img, s))) return rc;
   p.a.relu = 0;
-  p.a.an = dyn, p.a.bn = nullptr, p.a.bsrc = w, p.a.out = dx, p.a.mask = mask;
+  p.a.an = dyn, p.a.bn = nullptr, p.a.bsrc = w, p.a.bimg = img, p.a.out = dx, p.a.mask = mask;
   return launch<DGRAD>(p.a, p.smem, s);
 }
 
-extern "C" int b200_conv2d_wgrad_igemm(const float* x, const float* dy, float* dw, int64_t N, int64_t C, int64_t H, int64_t W,
-                                       int64_t O, int64_t KH, int64_t KW, int64_t OH, int64_t OW, int64_t sh, int64_t sw,
-                                       int64_t pt, int64_t pl, void* ws, size_t ws_bytes, void* stream) {
+extern "C" int b200_conv2d_wgrad_igemm(const float* x, const void* x_cl, const float* dy, const void* dy_cl, float* dw,
+                                       int64_t N, int64_t C, int64_t H, int64_t W, int64_t O, int64_t KH, int64_t KW,
+                                       int64_t OH, int64_t OW, int64_t sh, int64_t sw, int64_t pt, int64_t pl, void* ws,
+                                       size_t ws_bytes, void* stream) {
   int rc = check_dims(N, C, H, W, O, KH, KW, OH, OW, sh, sw, pt, pl);
   if (rc) return rc;
   B200_REQUIRE(x && dy && dw, "conv2d_wgrad_igemm: null pointer");
@@ -817,8 +983,12 @@ extern "C" int b200_conv2d_wgrad_igemm(const float* x, const float* dy, float* d
   auto* dyn = reinterpret_cast<__nv_bfloat16*>(base);
   base += al256((size_t)N * OH * OW * p.a.OPW * 2);
   float* part = reinterpret_cast<float*>(base);
-  if ((rc = repack(x, xn, N, C, H * W, p.a.CP, s))) return rc;
-  if ((rc = repack(dy, dyn, N, O, OH * OW, p.a.OPW, s))) return rc;
+  B200_REQUIRE((reinterpret_cast<uintptr_t>(x_cl) & 15) == 0 && (reinterpret_cast<uintptr_t>(dy_cl) & 15) == 0,
+               "conv2d_wgrad_igemm: channels-last copies not 16-byte aligned");
+  if (x_cl) xn = reinterpret_cast<__nv_bfloat16*>(const_cast<void*>(x_cl));
+  else if ((rc = repack(x, xn, N, C, H * W, p.a.CP, s))) return rc;
+  if (dy_cl) dyn = reinterpret_cast<__nv_bfloat16*>(const_cast<void*>(dy_cl));
+  else if ((rc = repack(dy, dyn, N, O, OH * OW, p.a.OPW, s))) return rc;
   p.a.relu = 0;
   p.a.an = xn, p.a.bn = dyn, p.a.bsrc = nullptr, p.a.out = part, p.a.mask = nullptr;
   rc = launch<WGRAD>(p.a, p.smem, s);

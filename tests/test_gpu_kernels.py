@@ -425,13 +425,15 @@ def test_rowfused_argmax_ties_and_misaligned_rows(C):
                                                       (2, 64, 14, 128, 3, 2, "VALID"), (2, 5, 11, 7, 3, 2, "SAME"),
                                                       (3, 9, 13, 300, 5, 3, "SAME"), (2, 16, 9, 24, 4, 1, "SAME"),
                                                       (2, 8, 12, 16, 3, 3, "SAME"), (1, 240, 6, 8, 3, 1, "VALID"),
-                                                      (1, 2, 10, 3, 1, 2, "VALID"), (1, 2, 9, 3, 2, 4, "SAME")])
+                                                      (1, 2, 10, 3, 1, 2, "VALID"), (1, 2, 9, 3, 2, 4, "SAME"),
+                                                      (2, 64, 13, 64, 3, 1, "SAME"), (5, 128, 6, 64, 3, 1, "VALID")])
 def test_conv2d_tensor_core_path(N, C, H, O, k, stride, padding):
     """bf16 tcgen05 convolutions against the oracle with the same operand rounding: the
     implicit GEMM (several column tiles at O = 300, strides 1-4, SAME padding with
     even and odd kernels, strides above the kernel size so that some input pixels get no
-    gradient) and, above 2048 taps x channels (C = 240, 3 x 3), the GEMM over staged
-    operands."""
+    gradient; with 64-channel blocks the tiles come in as TMA boxes, several images per
+    tile when the images are small) and, above 2048 taps x channels (C = 240, 3 x 3), the
+    GEMM over staged operands."""
     from b200 import ops
     from oracle import evaluator as O_
 
@@ -474,7 +476,8 @@ def test_conv2d_fused_epilogues(N, C, H, O, stride, padding):
     try:
         n0 = L.launch_count()
         y = ops.op_conv2d(T(x), T(w), relu=True, **kw)
-        assert L.launch_count() - n0 == 2  # the bf16 channels-last copy of x, then the implicit GEMM
+        # the bf16 channels-last copy of x, the packed bf16 weights, the implicit GEMM
+        assert L.launch_count() - n0 == 3
         y_plain = ops.op_conv2d(T(x), T(w), **kw)
         assert torch.equal(y, torch.where(y_plain > 0, y_plain, torch.zeros_like(y_plain)))
         pre = O_.execute_op("Conv2D", x, w, contraction_rounding="bf16", **kw)
