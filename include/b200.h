@@ -436,7 +436,8 @@ int b200_conv2d_wgrad_tc(const float* x, const float* dy, float* dw, int64_t N, 
  * sums. A caller that already holds such a copy passes it as x_cl / dy_cl (NULL: the
  * call makes it): b200_conv2d_channels_last writes src [N, C, HW] fp32 as [N, HW, Cp]
  * bf16, channels >= C zero; Cp = C rounded up to 8 for x and for dgrad's dy, O rounded up
- * to 64 for wgrad's dy.
+ * to 64 for wgrad's dy. A non-null y_cl / dx_cl receives the result's own copy in that
+ * layout (channels rounded up to 8) from the same epilogue, for the next convolution.
  * b200_conv2d_igemm_supported(op, ...) is 1 when the shape fits the kernel (tensors up to
  * 2^30 elements, at most 2048 reduction indices with channels padded to 8, the bf16
  * weights resident in shared memory); the entry points return B200_ERR_UNSUPPORTED
@@ -446,13 +447,14 @@ int b200_conv2d_igemm_supported(int op, int64_t N, int64_t C, int64_t H, int64_t
 size_t b200_conv2d_igemm_workspace_bytes(int op, int64_t N, int64_t C, int64_t H, int64_t W, int64_t O, int64_t KH, int64_t KW,
                                          int64_t OH, int64_t OW, int64_t sh, int64_t sw, int64_t pt, int64_t pl);
 int b200_conv2d_channels_last(const float* src, void* dst, int64_t N, int64_t C, int64_t HW, int64_t Cp, void* stream);
-int b200_conv2d_fwd_igemm(const float* x, const void* x_cl, const float* w, float* y, int64_t N, int64_t C, int64_t H,
-                          int64_t W, int64_t O, int64_t KH, int64_t KW, int64_t OH, int64_t OW, int64_t sh, int64_t sw,
-                          int64_t pt, int64_t pl, int relu, void* workspace, size_t workspace_bytes, void* stream);
-int b200_conv2d_dgrad_igemm(const float* dy, const void* dy_cl, const float* w, const float* mask, float* dx, int64_t N,
-                            int64_t C, int64_t H, int64_t W, int64_t O, int64_t KH, int64_t KW, int64_t OH, int64_t OW,
-                            int64_t sh, int64_t sw, int64_t pt, int64_t pl, void* workspace, size_t workspace_bytes,
-                            void* stream);
+int b200_conv2d_fwd_igemm(const float* x, const void* x_cl, const float* w, float* y, void* y_cl, int64_t N, int64_t C,
+                          int64_t H, int64_t W, int64_t O, int64_t KH, int64_t KW, int64_t OH, int64_t OW, int64_t sh,
+                          int64_t sw, int64_t pt, int64_t pl, int relu, void* workspace, size_t workspace_bytes,
+                          void* stream);
+int b200_conv2d_dgrad_igemm(const float* dy, const void* dy_cl, const float* w, const float* mask, float* dx, void* dx_cl,
+                            int64_t N, int64_t C, int64_t H, int64_t W, int64_t O, int64_t KH, int64_t KW, int64_t OH,
+                            int64_t OW, int64_t sh, int64_t sw, int64_t pt, int64_t pl, void* workspace,
+                            size_t workspace_bytes, void* stream);
 int b200_conv2d_wgrad_igemm(const float* x, const void* x_cl, const float* dy, const void* dy_cl, float* dw, int64_t N,
                             int64_t C, int64_t H, int64_t W, int64_t O, int64_t KH, int64_t KW, int64_t OH, int64_t OW,
                             int64_t sh, int64_t sw, int64_t pt, int64_t pl, void* workspace, size_t workspace_bytes,

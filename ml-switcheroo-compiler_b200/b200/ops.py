@@ -1155,13 +1155,21 @@ def _conv_call(kind: int, a: torch.Tensor, b: torch.Tensor, out: torch.Tensor, d
         ws_bytes = int(L.lib().b200_conv2d_igemm_workspace_bytes(kind, *dims))
         ws = torch.empty(max(256, ws_bytes), dtype=torch.uint8, device=device())
         ws_ptr = ws.data_ptr()
+        # a planner-fused convolution (ReLU / mask epilogue) feeds the next convolution of
+        # the chain: its epilogue also writes the result's channels-last copy, kept for it
+        twin = None
+        if fused and kind in (0, 1):
+            cp = _rup(O if kind == 0 else Cc, 8)
+            twin = torch.empty((out.shape[0], out.shape[2], out.shape[3], cp), dtype=torch.bfloat16, device=device())
         if kind == 0:
             L.call("b200_conv2d_fwd_igemm", a.data_ptr(), channels_last(a, _rup(Cc, 8)).data_ptr(), b.data_ptr(),
-                   out.data_ptr(), *dims, 1 if relu else 0, ws_ptr, ws_bytes, stream_ptr())
+                   out.data_ptr(), _ptr(twin), *dims, 1 if relu else 0, ws_ptr, ws_bytes, stream_ptr())
         elif kind == 1:
             L.call("b200_conv2d_dgrad_igemm", a.data_ptr(), channels_last(a, _rup(O, 8)).data_ptr(), b.data_ptr(), _ptr(mask),
-                   out.data_ptr(), *dims, ws_ptr, ws_bytes, stream_ptr())
-        else:
+                   out.data_ptr(), _ptr(twin), *dims, ws_ptr, ws_bytes, stream_ptr())
+        if twin is not None:
+            _CAST_CACHE[(out.data_ptr(), out.numel(), out.dtype, out._version, ("channels_last", twin.shape[3]))] = (out, twin)
+        if kind == 2:
             L.call("b200_conv2d_wgrad_igemm", a.data_ptr(), channels_last(a, _rup(Cc, 8)).data_ptr(), b.data_ptr(),
                    channels_last(b, _rup(O, 64)).data_ptr(), out.data_ptr(), *dims, ws_ptr, ws_bytes, stream_ptr())
         return

@@ -96,6 +96,8 @@ struct Args {
   const uint8_t* bimg;        // fwd / dgrad: the resident B operand, bf16 and swizzled as in shared memory
   float* out;                 // fwd: y    dgrad: dx   wgrad: partials [splits][O][M]
   const float* mask;          // dgrad: dx *= (mask > 0) when not null
+  __nv_bfloat16* out_cl;      // fwd / dgrad, optional: the result's bf16 channels-last copy [pixels][out_cp]
+  int out_cp;                 // its channels (Nc rounded up to 8; channels >= Nc are written as zero)
   // fwd / dgrad with 64-channel K blocks: one TMA box per K block instead of cp.async.
   // A tile is tn images x th rows x tw columns of output pixels (fwd) or class pixels
   // (dgrad); tile = image block * tiles_h + row block
@@ -527,7 +529,7 @@ __global__ void __launch_bounds__(THREADS, 1) conv_igemm_kernel(const __grid_con
       tc_fence_after();
       const int m = r.mt * BM + q * 32 + lane;  // this lane's GEMM row
       bool rv = m < a.cls_m[r.cls];
-      int64_t obase, ostride;
+      int64_t obase, ostride, pix = 0;  // pix: the row's pixel in the channels-last copy
       if (MODE != WGRAD && a.tma) {
         int n, hh, ww;
         rv = tile_pixel(a, r, q * 32 + lane, n, hh, ww);
@@ -535,10 +537,12 @@ __global__ void __launch_bounds__(THREADS, 1) conv_igemm_kernel(const __grid_con
         if (MODE == FWD) {
           obase = (int64_t)n * a.O * a.P + hh * a.OW + ww;
           ostride = a.P;
+          pix = (int64_t)n * a.P + hh * a.OW + ww;
         } else {
           const int h = a.cls_ph[r.cls] + a.sh * hh, w = a.cls_pw[r.cls] + a.sw * ww;
           obase = (int64_t)n * a.C * a.HW + h * a.W + w;
           ostride = a.HW;
+          pix = (int64_t)n * a.HW + h * a.W + w;
         }
       } else {
         const int mm = rv ? m : 0;
@@ -546,12 +550,14 @@ __global__ void __launch_bounds__(THREADS, 1) conv_igemm_kernel(const __grid_con
           const int n = mm / a.P, p = mm - n * a.P;
           obase = (int64_t)n * a.O * a.P + p;
           ostride = a.P;
+          pix = mm;
         } else if (MODE == DGRAD) {
           const int hc = a.cls_hc[r.cls], wc = a.cls_wc[r.cls];
           const int n = mm / (hc * wc), rem = mm - n * (hc * wc), hh = rem / wc, ww = rem - hh * wc;
           const int h = a.cls_ph[r.cls] + a.sh * hh, w = a.cls_pw[r.cls] + a.sw * ww;
           obase = (int64_t)n * a.C * a.HW + h * a.W + w;
           ostride = a.HW;
+          pix = (int64_t)n * a.HW + h * a.W + w;
         } else {
           obase = (int64_t)r.sp * a.O * a.M + mm;
           ostride = a.M;
@@ -584,20 +590,30 @@ __global__ void __launch_bounds__(THREADS, 1) conv_igemm_kernel(const __grid_con
           if (lane == 0) mbar_arrive(&acc_empty[b]);
         }
         if (!rv) continue;
-        if (MODE == DGRAD && a.mask != nullptr) {
+        float o[32];
 #pragma unroll
-          for (int i = 0; i < 32; ++i)
-            if (i < nn) dst[(int64_t)i * ostride] = __uint_as_float(v[i]) * (mv[i] > 0.f ? 1.f : 0.f);
-        } else if (MODE == FWD && a.relu) {
+        for (int i = 0; i < 32; ++i) {
+          const float x = __uint_as_float(v[i]);
+          if (MODE == DGRAD && a.mask != nullptr) o[i] = x * (mv[i] > 0.f ? 1.f : 0.f);
+          else if (MODE == FWD && a.relu) o[i] = x > 0.f ? x : 0.f;
+          else o[i] = x;
+        }
 #pragma unroll
-          for (int i = 0; i < 32; ++i) {
-            const float x = __uint_as_float(v[i]);
-            if (i < nn) dst[(int64_t)i * ostride] = x > 0.f ? x : 0.f;
-          }
-        } else {
+        for (int i = 0; i < 32; ++i)
+          if (i < nn) dst[(int64_t)i * ostride] = o[i];
+        if (MODE != WGRAD && a.out_cl != nullptr) {
+          // the row's channels n0 + c0 .. + 31 of the channels-last bf16 copy, 16 bytes at a
+          // time; channels past Nc (up to out_cp) are zero
+          __nv_bfloat16* cl = a.out_cl + pix * a.out_cp + n0 + c0;
+          const int room = a.out_cp - (n0 + c0);
 #pragma unroll
-          for (int i = 0; i < 32; ++i)
-            if (i < nn) dst[(int64_t)i * ostride] = __uint_as_float(v[i]);
+          for (int k = 0; k < 4; ++k)
+            if (8 * k < room)
+              *reinterpret_cast<uint4*>(cl + 8 * k) =
+                  make_uint4(pack_bf16(8 * k < nn ? o[8 * k] : 0.f, 8 * k + 1 < nn ? o[8 * k + 1] : 0.f),
+                             pack_bf16(8 * k + 2 < nn ? o[8 * k + 2] : 0.f, 8 * k + 3 < nn ? o[8 * k + 3] : 0.f),
+                             pack_bf16(8 * k + 4 < nn ? o[8 * k + 4] : 0.f, 8 * k + 5 < nn ? o[8 * k + 5] : 0.f),
+                             pack_bf16(8 * k + 6 < nn ? o[8 * k + 6] : 0.f, 8 * k + 7 < nn ? o[8 * k + 7] : 0.f));
         }
       }
     }
@@ -891,9 +907,10 @@ extern "C" int b200_conv2d_channels_last(const float* src, void* dst, int64_t N,
   return repack(src, reinterpret_cast<__nv_bfloat16*>(dst), N, C, HW, Cp, as_stream(stream));
 }
 
-extern "C" int b200_conv2d_fwd_igemm(const float* x, const void* x_cl, const float* w, float* y, int64_t N, int64_t C, int64_t H,
-                                     int64_t W, int64_t O, int64_t KH, int64_t KW, int64_t OH, int64_t OW, int64_t sh,
-                                     int64_t sw, int64_t pt, int64_t pl, int relu, void* ws, size_t ws_bytes, void* stream) {
+extern "C" int b200_conv2d_fwd_igemm(const float* x, const void* x_cl, const float* w, float* y, void* y_cl, int64_t N,
+                                     int64_t C, int64_t H, int64_t W, int64_t O, int64_t KH, int64_t KW, int64_t OH,
+                                     int64_t OW, int64_t sh, int64_t sw, int64_t pt, int64_t pl, int relu, void* ws,
+                                     size_t ws_bytes, void* stream) {
   int rc = check_dims(N, C, H, W, O, KH, KW, OH, OW, sh, sw, pt, pl);
   if (rc) return rc;
   if (N == 0) return B200_OK;
@@ -917,14 +934,16 @@ extern "C" int b200_conv2d_fwd_igemm(const float* x, const void* x_cl, const flo
   }
   if ((rc = pack_b<FWD>(p.a, w, img, s))) return rc;
   p.a.relu = relu ? 1 : 0;
+  B200_REQUIRE((reinterpret_cast<uintptr_t>(y_cl) & 15) == 0, "conv2d_fwd_igemm: y_cl not 16-byte aligned");
   p.a.an = xn, p.a.bn = nullptr, p.a.bsrc = w, p.a.bimg = img, p.a.out = y, p.a.mask = nullptr;
+  p.a.out_cl = reinterpret_cast<__nv_bfloat16*>(y_cl), p.a.out_cp = (int)((O + 7) / 8 * 8);
   return launch<FWD>(p.a, p.smem, s);
 }
 
 extern "C" int b200_conv2d_dgrad_igemm(const float* dy, const void* dy_cl, const float* w, const float* mask, float* dx,
-                                       int64_t N, int64_t C, int64_t H, int64_t W, int64_t O, int64_t KH, int64_t KW,
-                                       int64_t OH, int64_t OW, int64_t sh, int64_t sw, int64_t pt, int64_t pl, void* ws,
-                                       size_t ws_bytes, void* stream) {
+                                       void* dx_cl, int64_t N, int64_t C, int64_t H, int64_t W, int64_t O, int64_t KH,
+                                       int64_t KW, int64_t OH, int64_t OW, int64_t sh, int64_t sw, int64_t pt, int64_t pl,
+                                       void* ws, size_t ws_bytes, void* stream) {
   int rc = check_dims(N, C, H, W, O, KH, KW, OH, OW, sh, sw, pt, pl);
   if (rc) return rc;
   if (N == 0) return B200_OK;
@@ -943,6 +962,7 @@ extern "C" int b200_conv2d_dgrad_igemm(const float* dy, const void* dy_cl, const
   for (int c = 0; c < p.a.ncls; ++c)
     if (p.a.cls_k[c] == 0) {
       cudaMemsetAsync(dx, 0, (size_t)N * C * H * W * 4, s);
+      if (dx_cl) cudaMemsetAsync(dx_cl, 0, (size_t)N * H * W * ((C + 7) / 8 * 8) * 2, s);
       if ((rc = check_launch("conv2d_dgrad_igemm(zero)"))) return rc;
       break;
     }
@@ -954,7 +974,9 @@ extern "C" int b200_conv2d_dgrad_igemm(const float* dy, const void* dy_cl, const
   }
   if ((rc = pack_b<DGRAD>(p.a, w, img, s))) return rc;
   p.a.relu = 0;
+  B200_REQUIRE((reinterpret_cast<uintptr_t>(dx_cl) & 15) == 0, "conv2d_dgrad_igemm: dx_cl not 16-byte aligned");
   p.a.an = dyn, p.a.bn = nullptr, p.a.bsrc = w, p.a.bimg = img, p.a.out = dx, p.a.mask = mask;
+  p.a.out_cl = reinterpret_cast<__nv_bfloat16*>(dx_cl), p.a.out_cp = (int)((C + 7) / 8 * 8);
   return launch<DGRAD>(p.a, p.smem, s);
 }
 

@@ -27,6 +27,29 @@ __global__ void __launch_bounds__(256) reduce_rows_kernel(const void* __restrict
   if (threadIdx.x == 0) y[row] = (OP == B200_RED_MEAN) ? t / (float)red : t;
 }
 
+// inner == 1 with short rows (red <= 1024): one warp per row, lane l combines elements
+// l, l + 32, ... in order, then a fixed xor-butterfly (the same result on every run)
+template <int OP>
+__global__ void __launch_bounds__(256) reduce_rows_warp_kernel(const void* __restrict__ x, int dt, float* __restrict__ y,
+                                                               int64_t rows, int64_t red) {
+  const int64_t row = (blockIdx.x * (int64_t)blockDim.x + threadIdx.x) >> 5;
+  const int lane = threadIdx.x & 31;
+  if (row >= rows) return;
+  float acc = (OP == B200_RED_MAX) ? -INFINITY : 0.f;
+  for (int64_t i = lane; i < red; i += 32) {
+    const float v = load_as_f32(x, row * red + i, dt);
+    if (OP == B200_RED_MAX) acc = fmaxf(acc, v);
+    else acc += v;
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) {
+    const float v = __shfl_xor_sync(0xffffffffu, acc, o);
+    if (OP == B200_RED_MAX) acc = fmaxf(acc, v);
+    else acc += v;
+  }
+  if (lane == 0) y[row] = (OP == B200_RED_MEAN) ? acc / (float)red : acc;
+}
+
 // inner > 1: each thread owns one (outer, inner) column over a chunk of `red`. With one
 // chunk the result goes straight to y; with several, chunk z writes its partial to
 // part[z][outer][inner] and reduce_splits_kernel combines them in chunk order, so the
@@ -331,6 +354,15 @@ extern "C" int b200_reduce(int dt, const void* x, float* y, int64_t outer, int64
   }
   if (inner == 1) {
     B200_REQUIRE(outer <= 2147483647LL, "reduce: too many rows");
+    if (red <= 1024) {
+      const unsigned g = (unsigned)ceil_div(outer * 32, (int64_t)256);
+      switch (op) {
+        case B200_RED_SUM: reduce_rows_warp_kernel<B200_RED_SUM><<<g, 256, 0, s>>>(x, dt, y, outer, red); break;
+        case B200_RED_MEAN: reduce_rows_warp_kernel<B200_RED_MEAN><<<g, 256, 0, s>>>(x, dt, y, outer, red); break;
+        default: reduce_rows_warp_kernel<B200_RED_MAX><<<g, 256, 0, s>>>(x, dt, y, outer, red); break;
+      }
+      return check_launch("reduce(rows)");
+    }
     switch (op) {
       case B200_RED_SUM: reduce_rows_kernel<B200_RED_SUM><<<(unsigned)outer, 256, 0, s>>>(x, dt, y, red); break;
       case B200_RED_MEAN: reduce_rows_kernel<B200_RED_MEAN><<<(unsigned)outer, 256, 0, s>>>(x, dt, y, red); break;

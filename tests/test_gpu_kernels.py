@@ -478,6 +478,14 @@ def test_conv2d_fused_epilogues(N, C, H, O, stride, padding):
         y = ops.op_conv2d(T(x), T(w), relu=True, **kw)
         # the bf16 channels-last copy of x, the packed bf16 weights, the implicit GEMM
         assert L.launch_count() - n0 == 3
+        # the epilogue's channels-last bf16 copy of relu(y) (kept for the next convolution)
+        # equals a fresh copy of y, padding channels included
+        cp = (O + 7) // 8 * 8
+        twin = ops.channels_last(y, cp)
+        fresh = torch.empty_like(twin)
+        L.call("b200_conv2d_channels_last", y.data_ptr(), fresh.data_ptr(), y.shape[0], O, y.shape[2] * y.shape[3], cp,
+               ops.stream_ptr())
+        assert torch.equal(twin, fresh)
         y_plain = ops.op_conv2d(T(x), T(w), **kw)
         assert torch.equal(y, torch.where(y_plain > 0, y_plain, torch.zeros_like(y_plain)))
         pre = O_.execute_op("Conv2D", x, w, contraction_rounding="bf16", **kw)
@@ -491,6 +499,11 @@ def test_conv2d_fused_epilogues(N, C, H, O, stride, padding):
         dx_ref = dx_ref * (m > 0)
         np.testing.assert_allclose(to_np(dx), dx_ref, rtol=1e-3, atol=1e-3 * np.abs(dx_ref).max())
         assert (to_np(dx)[m <= 0] == 0).all()
+        cpx = (C + 7) // 8 * 8
+        twin = ops.channels_last(dx, cpx)
+        fresh = torch.empty_like(twin)
+        L.call("b200_conv2d_channels_last", dx.data_ptr(), fresh.data_ptr(), N, C, H * H, cpx, ops.stream_ptr())
+        assert torch.equal(twin, fresh)
     finally:
         ops.Config.conv_dtype = "f32"
 
