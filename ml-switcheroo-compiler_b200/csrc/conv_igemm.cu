@@ -288,15 +288,15 @@ __global__ void __launch_bounds__(THREADS, 1) conv_igemm_kernel(const __grid_con
   const uint32_t tmem_base = *tmem_slot;
 
   if constexpr (MODE != WGRAD) {
-    // resident B: the packed image (pack_b_kernel) copied in with coalesced 16-byte loads
+    // resident B: the packed image (pack_b_kernel) copied in with 16-byte cp.async, every
+    // piece of a thread in flight at once (a load-then-store loop would pay one L2 round
+    // trip per piece: about 40 in a row for a 147 KB image)
     if (warp < PROD_WARPS) {
       const int n16 = (int)((uint32_t)a.kb_total * a.tiles_n * a.BN * 8u);
-      const uint4* src = reinterpret_cast<const uint4*>(a.bimg);
+      const uint8_t* src = reinterpret_cast<const uint8_t*>(a.bimg);
       const uint32_t dst = smem_u32(sResB);
-      for (int i = threadIdx.x; i < n16; i += PROD_THREADS) {
-        const uint4 u = __ldg(src + i);
-        st_shared_v4(dst + (uint32_t)i * 16u, u.x, u.y, u.z, u.w);
-      }
+      for (int i = threadIdx.x; i < n16; i += PROD_THREADS) cp16(dst + (uint32_t)i * 16u, src + (size_t)i * 16u, 16u);
+      cp_wait_all();
       fence_proxy_async_smem();
     }
     __syncthreads();
@@ -627,22 +627,32 @@ __global__ void __launch_bounds__(THREADS, 1) conv_igemm_kernel(const __grid_con
   }
 }
 
-// partials [S][O][M] (row = t*Cp + c, channels padded to Cp) -> dw [O, C, KH, KW]: one
-// warp per output, lane l sums splits l, l + 32, ... in order, then a fixed xor-butterfly
-// over the lanes, so the result is the same on every run
+// partials [S][O][M] (row = t*Cp + c, channels padded to Cp) -> dw [O, C, KH, KW]. A block
+// takes 32 consecutive (o, row) outputs; warp k sums splits k, k + 8, k + 16, ... of them in
+// order (each split's 32 values are one 128-byte read), then lane l adds the 8 warp sums
+// in warp order, so the result is the same on every run
 __global__ void __launch_bounds__(256) wgrad_reduce_kernel(const float* __restrict__ part, float* __restrict__ dw, int S, int O,
                                                            int M, int C, int Cp, int KHW) {
-  const int64_t e = (blockIdx.x * (int64_t)blockDim.x + threadIdx.x) >> 5;
-  const int lane = threadIdx.x & 31;
-  if (e >= (int64_t)O * M) return;
-  const int o = (int)(e / M), row = (int)(e - (int64_t)o * M);
-  const int t = row / Cp, c = row - t * Cp;
-  if (c >= C) return;
+  __shared__ float sh[8][33];
+  const int lane = threadIdx.x & 31, k = threadIdx.x >> 5;
+  const int64_t total = (int64_t)O * M;
+  const int64_t e = (int64_t)blockIdx.x * 32 + lane;
   float acc = 0.f;
-  for (int s = lane; s < S; s += 32) acc += __ldg(part + ((int64_t)s * O + o) * M + row);
+  if (e < total) {
+    const float* p = part + e;
+#pragma unroll 4
+    for (int sp = k; sp < S; sp += 8) acc += __ldg(p + (int64_t)sp * total);
+  }
+  sh[k][lane] = acc;
+  __syncthreads();
+  if (k == 0 && e < total) {
+    float t = sh[0][lane];
 #pragma unroll
-  for (int k = 16; k > 0; k >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, k);
-  if (lane == 0) dw[((int64_t)o * C + c) * KHW + t] = acc;
+    for (int i = 1; i < 8; ++i) t += sh[i][lane];
+    const int o = (int)(e / M), row = (int)(e - (int64_t)o * M);
+    const int tap = row / Cp, c = row - tap * Cp;
+    if (c < C) dw[((int64_t)o * C + c) * KHW + tap] = t;
+  }
 }
 
 struct Plan {
@@ -1016,7 +1026,7 @@ extern "C" int b200_conv2d_wgrad_igemm(const float* x, const void* x_cl, const f
   rc = launch<WGRAD>(p.a, p.smem, s);
   if (rc) return rc;
   const int64_t total = O * (int64_t)p.a.M;
-  wgrad_reduce_kernel<<<(unsigned)ceil_div(total * 32, 256), 256, 0, s>>>(part, dw, p.a.splits, (int)O, p.a.M, (int)C, p.a.CP,
+  wgrad_reduce_kernel<<<(unsigned)ceil_div(total, 32), 256, 0, s>>>(part, dw, p.a.splits, (int)O, p.a.M, (int)C, p.a.CP,
                                                                           (int)(KH * KW));
   return check_launch("conv2d_wgrad_igemm(sum)");
 }

@@ -115,6 +115,40 @@ __global__ void __launch_bounds__(256) ew_strided32_kernel(const __grid_constant
   }
 }
 
+// Merges adjacent dims of the index space wherever every input's strides allow it
+// (stride[d] == stride[d + 1] * shape[d + 1], broadcast dims included) and drops size-1
+// dims, so that e.g. a [N, C, 1, 1] operand broadcast over [N, C, H, W] becomes one value
+// per row of H * W elements. The output is dense, so any merge keeps its addressing.
+static void coalesce_dims(b200_ew_program& q) {
+  int64_t sh[B200_EW_MAX_DIM], st[B200_EW_MAX_IN][B200_EW_MAX_DIM];
+  int nd = 0;
+  for (int d = 0; d < q.ndim; ++d) {
+    if (q.shape[d] == 1) continue;
+    if (nd > 0) {
+      bool ok = true;
+      for (int j = 0; j < q.n_in && ok; ++j) ok = st[j][nd - 1] == q.in_strides[j][d] * q.shape[d];
+      if (ok) {
+        sh[nd - 1] *= q.shape[d];
+        for (int j = 0; j < q.n_in; ++j) st[j][nd - 1] = q.in_strides[j][d];
+        continue;
+      }
+    }
+    sh[nd] = q.shape[d];
+    for (int j = 0; j < q.n_in; ++j) st[j][nd] = q.in_strides[j][d];
+    ++nd;
+  }
+  if (nd == 0) {  // every dim is 1: one element
+    sh[0] = 1;
+    for (int j = 0; j < q.n_in; ++j) st[j][0] = 0;
+    nd = q.ndim > 0 ? 1 : 0;
+  }
+  q.ndim = nd;
+  for (int d = 0; d < nd; ++d) {
+    q.shape[d] = sh[d];
+    for (int j = 0; j < q.n_in; ++j) q.in_strides[j][d] = st[j][d];
+  }
+}
+
 static bool dtype_ok(int dt) { return dt == B200_F32 || dt == B200_BF16 || dt == B200_I64 || dt == B200_BOOL || dt == B200_I32; }
 
 }  // namespace b200
@@ -122,19 +156,21 @@ static bool dtype_ok(int dt) { return dt == B200_F32 || dt == B200_BF16 || dt ==
 extern "C" int b200_ew_run(const b200_ew_program* prog, const void* const* inputs, void* const* outputs, void* stream) {
   using namespace b200;
   B200_REQUIRE(prog != nullptr, "ew_run: null program");
-  const b200_ew_program& p = *prog;
-  B200_REQUIRE(p.ndim >= 0 && p.ndim <= B200_EW_MAX_DIM, "ew_run: ndim %d out of range", p.ndim);
-  B200_REQUIRE(p.n_in >= 0 && p.n_in <= B200_EW_MAX_IN, "ew_run: n_in %d out of range", p.n_in);
-  B200_REQUIRE(p.n_out >= 1 && p.n_out <= B200_EW_MAX_OUT, "ew_run: n_out %d out of range", p.n_out);
-  B200_REQUIRE(p.n_ins >= 1 && p.n_ins <= B200_EW_MAX_INS, "ew_run: n_ins %d out of range", p.n_ins);
+  const b200_ew_program& p0 = *prog;
+  B200_REQUIRE(p0.ndim >= 0 && p0.ndim <= B200_EW_MAX_DIM, "ew_run: ndim %d out of range", p0.ndim);
+  B200_REQUIRE(p0.n_in >= 0 && p0.n_in <= B200_EW_MAX_IN, "ew_run: n_in %d out of range", p0.n_in);
+  B200_REQUIRE(p0.n_out >= 1 && p0.n_out <= B200_EW_MAX_OUT, "ew_run: n_out %d out of range", p0.n_out);
+  B200_REQUIRE(p0.n_ins >= 1 && p0.n_ins <= B200_EW_MAX_INS, "ew_run: n_ins %d out of range", p0.n_ins);
   int64_t n = 1;
-  for (int d = 0; d < p.ndim; ++d) {
-    B200_REQUIRE(p.shape[d] >= 0, "ew_run: negative dim");
-    n *= p.shape[d];
+  for (int d = 0; d < p0.ndim; ++d) {
+    B200_REQUIRE(p0.shape[d] >= 0, "ew_run: negative dim");
+    n *= p0.shape[d];
   }
   EwParams P;
-  P.p = p;
+  P.p = p0;
   P.n = n;
+  if (n > 0) coalesce_dims(P.p);
+  const b200_ew_program& p = P.p;
   for (int j = 0; j < p.n_in; ++j) {
     B200_REQUIRE(inputs && inputs[j], "ew_run: null input %d", j);
     if (!dtype_ok(p.in_dtype[j])) {

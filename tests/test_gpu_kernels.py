@@ -751,6 +751,31 @@ def test_elementwise_flat_modes_dtypes(shape):
     np.testing.assert_array_equal(to_np(out[1].float()), to_np(T(ref).to(torch.bfloat16).float()))
 
 
+def test_elementwise_merged_dims():
+    """Adjacent dims whose strides line up are merged before the path is chosen: a
+    [N, C, 1, 1] operand broadcast over [N, C, H, W] becomes one value per row of H * W
+    (row length 36, not a multiple of 8), a [1, C, 1, 1] operand stays a broadcast that no
+    merge can flatten, and a permuted view keeps its own strides."""
+    from b200 import ops
+
+    r = rng(5)
+    x = r.standard_normal((64, 128, 6, 6)).astype(np.float32)
+    g = r.standard_normal((64, 128, 1, 1)).astype(np.float32)
+    ch = r.standard_normal((1, 128, 1, 1)).astype(np.float32)
+    X = T(x)
+    np.testing.assert_allclose(to_np(ops.op_multiply(X, T(g))), x * g, rtol=1e-6)
+    np.testing.assert_allclose(to_np(ops.op_add(X, T(ch))), x + ch, rtol=1e-6)
+    p = ops.Prog()
+    a, b, c = p.load(X), p.load(T(g)), p.load(T(ch))
+    t1 = p.op("GT", a, c)
+    t2 = p.op("MUL", t1, b)
+    out = p.run([(t2, torch.float32)], x.shape)
+    np.testing.assert_array_equal(to_np(out[0]), (x > ch) * g)
+    xp = X.permute(0, 2, 3, 1)  # [64, 6, 6, 128] view over NCHW storage
+    gp = T(g).permute(0, 2, 3, 1)
+    np.testing.assert_allclose(to_np(ops.op_multiply(xp, gp)), x.transpose(0, 2, 3, 1) * g.transpose(0, 2, 3, 1), rtol=1e-6)
+
+
 @pytest.mark.parametrize("R,V", [(33, 32000), (17, 1000), (9, 4096), (5, 12)])
 def test_logsoftmax_pick_register_rows_bf16_dx(R, V):
     from b200 import _lib as L
