@@ -428,7 +428,9 @@ int b200_conv2d_wgrad_tc(const float* x, const float* dy, float* dw, int64_t N, 
  *                            writes relu(y) instead (the Relu node that follows, fused)
  *   b200_conv2d_dgrad_igemm: dx = Conv2DInputGrad(dy, w) (conv.py:634-697); a non-null
  *                            mask [N, C, H, W] writes dx * (mask > 0) instead (the Multiply
- *                            by the Greater(pre, 0) mask of the ReLU VJP, fused)
+ *                            by the Greater(pre, 0) mask of the ReLU VJP, fused); a non-null
+ *                            mask_cl [N, H, W, mask_cp] bf16 (the channels-last copy that a
+ *                            relu != 0 forward wrote as y_cl) writes dx * (mask_cl != 0)
  *   b200_conv2d_wgrad_igemm: dw = Conv2DWeightGrad(x, dy) (conv.py:699-764)
  * `workspace` (256-byte aligned, b200_conv2d_igemm_workspace_bytes(op, ...) bytes, op 0
  * fwd, 1 dgrad, 2 wgrad) holds the bf16 channels-last copies the tiles are copied from
@@ -437,7 +439,10 @@ int b200_conv2d_wgrad_tc(const float* x, const float* dy, float* dw, int64_t N, 
  * call makes it): b200_conv2d_channels_last writes src [N, C, HW] fp32 as [N, HW, Cp]
  * bf16, channels >= C zero; Cp = C rounded up to 8 for x and for dgrad's dy, O rounded up
  * to 64 for wgrad's dy. A non-null y_cl / dx_cl receives the result's own copy in that
- * layout (channels rounded up to 8) from the same epilogue, for the next convolution.
+ * layout (channels rounded up to 8) from the same epilogue, for the next convolution; y /
+ * dx may then be NULL (only the copy is written). With relu != 0 the copy keeps positive
+ * values nonzero (values below 2^-133 become the smallest bf16 subnormal instead of +0), so
+ * it is nonzero exactly where y > 0.
  * b200_conv2d_igemm_supported(op, ...) is 1 when the shape fits the kernel (tensors up to
  * 2^30 elements, at most 2048 reduction indices with channels padded to 8, the bf16
  * weights resident in shared memory); the entry points return B200_ERR_UNSUPPORTED
@@ -451,10 +456,10 @@ int b200_conv2d_fwd_igemm(const float* x, const void* x_cl, const float* w, floa
                           int64_t H, int64_t W, int64_t O, int64_t KH, int64_t KW, int64_t OH, int64_t OW, int64_t sh,
                           int64_t sw, int64_t pt, int64_t pl, int relu, void* workspace, size_t workspace_bytes,
                           void* stream);
-int b200_conv2d_dgrad_igemm(const float* dy, const void* dy_cl, const float* w, const float* mask, float* dx, void* dx_cl,
-                            int64_t N, int64_t C, int64_t H, int64_t W, int64_t O, int64_t KH, int64_t KW, int64_t OH,
-                            int64_t OW, int64_t sh, int64_t sw, int64_t pt, int64_t pl, void* workspace,
-                            size_t workspace_bytes, void* stream);
+int b200_conv2d_dgrad_igemm(const float* dy, const void* dy_cl, const float* w, const float* mask, const void* mask_cl,
+                            int64_t mask_cp, float* dx, void* dx_cl, int64_t N, int64_t C, int64_t H, int64_t W,
+                            int64_t O, int64_t KH, int64_t KW, int64_t OH, int64_t OW, int64_t sh, int64_t sw, int64_t pt,
+                            int64_t pl, void* workspace, size_t workspace_bytes, void* stream);
 int b200_conv2d_wgrad_igemm(const float* x, const void* x_cl, const float* dy, const void* dy_cl, float* dw, int64_t N,
                             int64_t C, int64_t H, int64_t W, int64_t O, int64_t KH, int64_t KW, int64_t OH, int64_t OW,
                             int64_t sh, int64_t sw, int64_t pt, int64_t pl, void* workspace, size_t workspace_bytes,

@@ -436,13 +436,16 @@ def find_conv_relu(g: Graph, live: dict[str, Node], meta: dict[str, Meta], users
 def conv_relu_step(m: Match, g: Graph) -> Step:
     b = m.bind
     kw = _conv_attrs(g.nodes[b["conv"]])
+    info = {"values": [b["act"], b["conv"]], "x": b["x"], "relu": True, "fp32": True}
 
     def run(env: dict) -> None:
-        r = ops.op_conv2d(env[b["x"]], env[b["w"]], relu=True, **kw)
+        r = ops.op_conv2d(env[b["x"]], env[b["w"]], relu=True, fp32_out=info["fp32"], **kw)
         env[b["act"]] = r
         env[b["conv"]] = r  # read only by Greater(pre, 0) masks: same mask from relu(pre)
 
-    return Step([b["act"], b["conv"]], [b["x"], b["w"]], run, "conv_relu")
+    st = Step([b["act"], b["conv"]], [b["x"], b["w"]], run, "conv_relu")
+    st.conv_copy = info
+    return st
 
 
 def find_conv_dgrad_mask(g: Graph, live: dict[str, Node], meta: dict[str, Meta], users: dict[str, list[str]],
@@ -472,11 +475,63 @@ def find_conv_dgrad_mask(g: Graph, live: dict[str, Node], meta: dict[str, Meta],
 def conv_dgrad_mask_step(m: Match, g: Graph) -> Step:
     b = m.bind
     kw = _conv_attrs(g.nodes[b["dg"]])
+    info = {"values": [b["mul"]], "dy": b["dy"], "pre": b["pre"], "relu": False, "fp32": True}
 
     def run(env: dict) -> None:
-        env[b["mul"]] = ops.op_conv2d_input_grad(env[b["dy"]], env[b["w"]], mask=env[b["pre"]], **kw)
+        env[b["mul"]] = ops.op_conv2d_input_grad(env[b["dy"]], env[b["w"]], mask=env[b["pre"]], fp32_out=info["fp32"], **kw)
 
-    return Step([b["mul"]], [b["dy"], b["w"], b["pre"]], run, "conv_dgrad_mask")
+    st = Step([b["mul"]], [b["dy"], b["w"], b["pre"]], run, "conv_dgrad_mask")
+    st.conv_copy = info
+    return st
+
+
+def _reads_copy(r: Step, v: str, producer: dict, meta: dict[str, Meta], g: Graph) -> bool:
+    """Whether step ``r`` reads value ``v`` only through the bf16 channels-last copy that the
+    fused convolution ``producer`` writes beside it (same channel padding)."""
+    mv = meta.get(v)
+    if mv is None or mv.scalar or len(mv.shape) != 4:
+        return False
+    cp = ops._rup(mv.shape[1], 8)
+    info = getattr(r, "conv_copy", None)
+    if r.label == "conv_relu" and info is not None:
+        return info["x"] == v  # channels_last(x, C rounded up to 8)
+    if r.label == "conv_dgrad_mask" and info is not None:
+        if info["pre"] == v:
+            return producer["relu"]  # the mask from the ReLU output's copy (nonzero where > 0)
+        return info["dy"] == v  # channels_last(dy, O rounded up to 8)
+    if r.label == "Conv2DWeightGrad" and len(r.inputs) >= 2 and v in r.inputs[:2]:
+        node = g.nodes.get(r.outputs[0])
+        mx, mdy = meta.get(r.inputs[0]), meta.get(r.inputs[1])
+        if node is None or mx is None or mdy is None or mx.scalar or mdy.scalar or len(mdy.shape) != 4:
+            return False
+        a = node.attributes
+        ts = a.get("target_shape")
+        if ts is None or len(ts) != 4:
+            return False
+        if not ops.conv_fused_ok(2, mx.shape, tuple(int(t) for t in ts), a.get("strides", a.get("stride", (1, 1))),
+                                 a.get("padding", "SAME"), out_hw=tuple(mdy.shape[2:])):
+            return False  # the staged (non-implicit) weight gradient reads fp32
+        if r.inputs[1] == v and cp != ops._rup(mv.shape[1], 64):
+            return False  # its dy copy has the channels padded to 64
+        return True
+    return False
+
+
+def _conv_copy_only(steps: list[Step], outputs: set[str], meta: dict[str, Meta], g: Graph) -> None:
+    """Fused convolution results that every reader takes from the channels-last bf16 copy
+    of the fused epilogue (the next convolution's operand, the weight gradient's operands,
+    the ReLU VJP mask of an input gradient) skip their fp32 NCHW write: the step still
+    returns an fp32 tensor (the copy's cache key), left unwritten."""
+    readers: dict[str, list[Step]] = {}
+    for st in steps:
+        for v in st.inputs:
+            readers.setdefault(v, []).append(st)
+    for st in steps:
+        info = getattr(st, "conv_copy", None)
+        if info is None or any(v in outputs for v in info["values"]):
+            continue
+        if all(_reads_copy(r, v, info, meta, g) for v in info["values"] for r in readers.get(v, []) if r is not st):
+            info["fp32"] = False
 
 
 def _perm_of(n: Node, ndim: int) -> list[int]:
@@ -1544,7 +1599,9 @@ def plan_steps(graph: Graph, nodes: list[Node], sample: dict[str, Any]) -> list[
                 groups.append(([n.id], shape_only_step(n, meta)))
             else:
                 groups.append(([n.id], node_step(n)))
-    return _schedule(groups)
+    steps = _schedule(groups)
+    _conv_copy_only(steps, outputs, meta, graph)
+    return steps
 
 
 def _schedule(groups: list[tuple[list[str], Step]]) -> list[Step]:

@@ -1136,11 +1136,13 @@ def _conv_dt() -> int:
 
 
 def _conv_call(kind: int, a: torch.Tensor, b: torch.Tensor, out: torch.Tensor, dims: tuple, relu: bool = False,
-               mask: torch.Tensor | None = None) -> None:
+               mask: torch.Tensor | None = None, fp32_out: bool = True) -> None:
     """fp32 math: exact CUDA-core kernels; bf16 math: tcgen05 implicit GEMMs (operand tiles
     gathered straight into shared memory), or tcgen05 GEMMs over staged operands for shapes
     the implicit GEMM does not take. ``relu`` (forward) and ``mask`` (input gradient:
-    ``dx * (mask > 0)``) are epilogues of the implicit GEMM only."""
+    ``dx * (mask > 0)``) are epilogues of the implicit GEMM only. ``fp32_out=False`` (fused
+    epilogues only, for results whose every reader takes the channels-last copy) leaves
+    ``out`` unwritten and writes only the copy."""
     names = ("b200_conv2d_fwd", "b200_conv2d_dgrad", "b200_conv2d_wgrad")
     fused = relu or mask is not None
     if Config.conv_dtype != "bf16":
@@ -1161,14 +1163,21 @@ def _conv_call(kind: int, a: torch.Tensor, b: torch.Tensor, out: torch.Tensor, d
         if fused and kind in (0, 1):
             cp = _rup(O if kind == 0 else Cc, 8)
             twin = torch.empty((out.shape[0], out.shape[2], out.shape[3], cp), dtype=torch.bfloat16, device=device())
+        if not fp32_out and twin is None:
+            raise UnimplementedMathError("a convolution result without fp32 output needs a fused epilogue")
+        optr = out.data_ptr() if fp32_out else None
         if kind == 0:
             L.call("b200_conv2d_fwd_igemm", a.data_ptr(), channels_last(a, _rup(Cc, 8)).data_ptr(), b.data_ptr(),
-                   out.data_ptr(), _ptr(twin), *dims, 1 if relu else 0, ws_ptr, ws_bytes, stream_ptr())
+                   optr, _ptr(twin), *dims, 1 if relu else 0, ws_ptr, ws_bytes, stream_ptr())
         elif kind == 1:
-            L.call("b200_conv2d_dgrad_igemm", a.data_ptr(), channels_last(a, _rup(O, 8)).data_ptr(), b.data_ptr(), _ptr(mask),
-                   out.data_ptr(), _ptr(twin), *dims, ws_ptr, ws_bytes, stream_ptr())
+            # a ReLU output's own channels-last copy is the exact mask (nonzero where > 0)
+            mcl = relu_copy(mask, _rup(Cc, 8)) if mask is not None else None
+            L.call("b200_conv2d_dgrad_igemm", a.data_ptr(), channels_last(a, _rup(O, 8)).data_ptr(), b.data_ptr(),
+                   None if mcl is not None else _ptr(mask), _ptr(mcl), int(mcl.shape[3]) if mcl is not None else 0,
+                   optr, _ptr(twin), *dims, ws_ptr, ws_bytes, stream_ptr())
         if twin is not None:
-            _CAST_CACHE[(out.data_ptr(), out.numel(), out.dtype, out._version, ("channels_last", twin.shape[3]))] = (out, twin)
+            _CAST_CACHE[(out.data_ptr(), out.numel(), out.dtype, out._version, ("channels_last", twin.shape[3]))] = (
+                out, twin, "relu" if (kind == 0 and relu) else "")
         if kind == 2:
             L.call("b200_conv2d_wgrad_igemm", a.data_ptr(), channels_last(a, _rup(Cc, 8)).data_ptr(), b.data_ptr(),
                    channels_last(b, _rup(O, 64)).data_ptr(), out.data_ptr(), *dims, ws_ptr, ws_bytes, stream_ptr())
@@ -1201,6 +1210,15 @@ def channels_last(t: torch.Tensor, cp: int) -> torch.Tensor:
     return y
 
 
+def relu_copy(t: torch.Tensor, cp: int) -> torch.Tensor | None:
+    """The channels-last copy that a fused ReLU convolution wrote beside ``t`` in this run
+    (nonzero exactly where ``t`` > 0), or None."""
+    hit = _CAST_CACHE.get((t.data_ptr(), t.numel(), t.dtype, t._version, ("channels_last", cp)))
+    if hit is not None and hit[0] is t and len(hit) > 2 and hit[2] == "relu":
+        return hit[1]
+    return None
+
+
 def conv_fused_ok(kind: int, x_shape: tuple, w_shape: tuple, stride, padding, out_hw: tuple | None = None) -> bool:
     """Whether a fused conv epilogue (forward ReLU, input-gradient mask) has a kernel."""
     if Config.conv_dtype != "bf16" or len(x_shape) != 4 or len(w_shape) != 4:
@@ -1224,9 +1242,12 @@ def _check_conv_attrs(groups, dilation):
         raise UnimplementedMathError("dilated Conv2D")
 
 
-def op_conv2d(x, w, stride=(1, 1), padding="SAME", groups=1, dilation=1, relu=False, **kw):  # numpy/eager/conv.py:462-489
+def op_conv2d(x, w, stride=(1, 1), padding="SAME", groups=1, dilation=1, relu=False, fp32_out=True,
+              **kw):  # numpy/eager/conv.py:462-489
     """Conv2D; ``relu=True`` returns relu(Conv2D(x, w)) from the same kernel (the Relu node
-    that follows it in the graph, fused)."""
+    that follows it in the graph, fused). ``fp32_out=False`` (with ``relu``): the returned
+    tensor is left unwritten and only its channels-last copy exists, for a planner that has
+    checked that every reader takes that copy."""
     _check_conv_attrs(groups, kw.get("dilations", dilation))
     s = _stride2(kw.get("strides", stride))
     xc, wc = contiguous(cast(x, torch.float32)), contiguous(cast(w, torch.float32))
@@ -1235,13 +1256,16 @@ def op_conv2d(x, w, stride=(1, 1), padding="SAME", groups=1, dilation=1, relu=Fa
     OH, OW = _conv_out_hw((H, W), (KH, KW), s, padding)
     pt, pl = _conv_pads((H, W), (KH, KW), s, padding, (OH, OW))
     y = torch.empty(N, O, OH, OW, dtype=torch.float32, device=device())
-    _conv_call(0, xc, wc, y, (N, Cc, H, W, O, KH, KW, OH, OW, s[0], s[1], pt, pl), relu=bool(relu))
+    _conv_call(0, xc, wc, y, (N, Cc, H, W, O, KH, KW, OH, OW, s[0], s[1], pt, pl), relu=bool(relu), fp32_out=fp32_out)
     return y
 
 
-def op_conv2d_input_grad(dy, w, stride=(1, 1), padding="SAME", target_shape=None, groups=1, dilation=1, mask=None, **kw):
+def op_conv2d_input_grad(dy, w, stride=(1, 1), padding="SAME", target_shape=None, groups=1, dilation=1, mask=None,
+                         fp32_out=True, **kw):
     """Conv2DInputGrad (numpy/eager/conv.py:634-697); with ``mask`` (fp32, the input's shape)
-    it returns dx * (mask > 0): the Multiply by the ReLU VJP's Greater(pre, 0) mask, fused."""
+    it returns dx * (mask > 0): the Multiply by the ReLU VJP's Greater(pre, 0) mask, fused
+    (read from the mask's own channels-last copy when a fused ReLU convolution wrote one).
+    ``fp32_out=False`` (with ``mask``) as for op_conv2d."""
     _check_conv_attrs(groups, kw.get("dilations", dilation))
     s = _stride2(kw.get("strides", stride))
     dyc, wc = contiguous(cast(dy, torch.float32)), contiguous(cast(w, torch.float32))
@@ -1254,7 +1278,7 @@ def op_conv2d_input_grad(dy, w, stride=(1, 1), padding="SAME", target_shape=None
         mask = contiguous(cast(mask, torch.float32))
         if tuple(mask.shape) != (N, Cc, H, W):
             raise ValueError(f"conv input-gradient mask shape {tuple(mask.shape)} != {(N, Cc, H, W)}")
-    _conv_call(1, dyc, wc, dx, (N, Cc, H, W, O, KH, KW, OH, OW, s[0], s[1], pt, pl), mask=mask)
+    _conv_call(1, dyc, wc, dx, (N, Cc, H, W, O, KH, KW, OH, OW, s[0], s[1], pt, pl), mask=mask, fp32_out=fp32_out)
     return dx
 
 

@@ -1,7 +1,7 @@
 // Conv2D forward / input gradient / weight gradient as implicit GEMMs on the tcgen05
 // tensor cores: the im2col operand is never materialised in HBM. Operand tiles are built
 // in shared memory in the 128-byte swizzled K-major layout the UMMA descriptors read; one
-// thread issues tcgen05.mma into a double-buffered TMEM accumulator; four epilogue warps
+// thread issues tcgen05.mma into up to four TMEM accumulators; eight epilogue warps
 // write the fp32 result in NCHW with the activation / mask fused. Replaces Conv2D
 // (numpy/eager/conv.py:462-489), Conv2DInputGrad (conv.py:634-697) and Conv2DWeightGrad
 // (conv.py:699-764); padding is _compute_conv2d_padding_values (conv.py:590-633), passed
@@ -37,9 +37,10 @@
 // output channels of B, copied by the same one-warp-per-stage cp.async producers.
 //
 // Persistent kernel, one CTA per SM, 512 threads: warps 0-6 producers, warp 7 allocates
-// TMEM and issues four 128 x BN x 16 MMAs per K block, warps 8-15 epilogue (two per TMEM
-// lane quarter, warp % 4, on alternate 32-column chunks; lane = GEMM row, so a store of one
-// column covers 32 consecutive pixels). Pieces of 16 bytes are XORed by row & 7 (the TMA 128-byte
+// TMEM and issues four 128 x BN x 16 MMAs per K block into accumulator T % 4 (T % 2 for
+// tiles over 128 columns), warps 8-15 epilogue in two groups of four on alternate tiles
+// (warp % 4 = TMEM lane quarter, all column chunks of it; lane = GEMM row, so a store of one
+// column covers 32 consecutive pixels): two tiles drain at once while the MMA runs ahead. Pieces of 16 bytes are XORed by row & 7 (the TMA 128-byte
 // swizzle). Every mbarrier wait is bounded; a warp whose wait gives up stops, and the CTA
 // winds down (the MMA warp drains its MMAs before TMEM is freed).
 #include <algorithm>
@@ -57,7 +58,7 @@ enum Mode { FWD = 0, DGRAD = 1, WGRAD = 2 };
 // sub-partition, so each thread may hold 128 registers
 constexpr int PROD_WARPS = 7, PROD_THREADS = PROD_WARPS * 32;
 constexpr int MMA_WARP = PROD_WARPS;
-constexpr int EPI_WARPS = 8;  // two per TMEM lane quarter, on alternate 32-column chunks
+constexpr int EPI_WARPS = 8;  // two groups of four (one per TMEM lane quarter), on alternate tiles
 constexpr int THREADS = (PROD_WARPS + 1 + EPI_WARPS) * 32;
 constexpr int BM = 128, BK = 64;
 constexpr uint32_t A_BYTES = BM * BK * 2;
@@ -80,6 +81,7 @@ struct Args {
   uint32_t resb_off;          // fwd / dgrad: byte offset of the resident B operand
   int kb_total;               // fwd / dgrad: K blocks over all classes
   uint32_t tmem_cols;
+  int nacc;                   // TMEM accumulators (4, or 2 when a tile is wider than 128 columns)
   int relu;                   // fwd: relu epilogue
   // classes: fwd / wgrad one (the whole GEMM); dgrad sh * sw parity classes
   int ncls, max_tiles;        // item = ((split * max_tiles + tile) * ncls + class) * tiles_n + column tile
@@ -94,8 +96,11 @@ struct Args {
   const __nv_bfloat16* bn;    // wgrad: dy as bf16 NHWC [n][oh][ow][OPW]
   const float* bsrc;          // fwd / dgrad: w (fp32 OIHW)
   const uint8_t* bimg;        // fwd / dgrad: the resident B operand, bf16 and swizzled as in shared memory
-  float* out;                 // fwd: y    dgrad: dx   wgrad: partials [splits][O][M]
+  float* out;                 // fwd: y    dgrad: dx   wgrad: partials [splits][O][M]; fwd / dgrad: null
+                              // when only the channels-last copy is wanted
   const float* mask;          // dgrad: dx *= (mask > 0) when not null
+  const __nv_bfloat16* mask_cl;  // dgrad, instead: dx *= (mask_cl != 0), the ReLU output's channels-last copy
+  int mask_cp;                // its channels
   __nv_bfloat16* out_cl;      // fwd / dgrad, optional: the result's bf16 channels-last copy [pixels][out_cp]
   int out_cp;                 // its channels (Nc rounded up to 8; channels >= Nc are written as zero)
   // fwd / dgrad with 64-channel K blocks: one TMA box per K block instead of cp.async.
@@ -232,9 +237,9 @@ __global__ void __launch_bounds__(THREADS, 1) conv_igemm_kernel(const __grid_con
   int4* tab = reinterpret_cast<int4*>(smem + a.resb_off + (MODE == WGRAD ? 0u : (uint32_t)a.kb_total * a.tiles_n * a.BN * 128u));
   uint64_t* full = reinterpret_cast<uint64_t*>(tab + a.ktab);
   uint64_t* empty = full + a.stages;
-  uint64_t* acc_full = empty + a.stages;  // [2]
-  uint64_t* acc_empty = acc_full + 2;     // [2]
-  uint64_t* drained = acc_empty + 2;
+  uint64_t* acc_full = empty + a.stages;  // [4]
+  uint64_t* acc_empty = acc_full + 4;     // [4]
+  uint64_t* drained = acc_empty + 4;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drained + 1);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -271,9 +276,9 @@ __global__ void __launch_bounds__(THREADS, 1) conv_igemm_kernel(const __grid_con
       mbar_init(&full[s], 1);  // one producer warp per stage
       mbar_init(&empty[s], 1);
     }
-    for (int b = 0; b < 2; ++b) {
+    for (int b = 0; b < 4; ++b) {
       mbar_init(&acc_full[b], 1);
-      mbar_init(&acc_empty[b], EPI_WARPS);
+      mbar_init(&acc_empty[b], EPI_WARPS / 2);  // the four warps of the group that drains it
     }
     mbar_init(drained, 1);
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
@@ -479,8 +484,8 @@ __global__ void __launch_bounds__(THREADS, 1) conv_igemm_kernel(const __grid_con
         if (!item_of(a, it, r)) continue;
         const int nkb = kblocks_of(a, r);
         if (nkb <= 0) continue;
-        const uint32_t b = T & 1;
-        if (!mbar_wait(&acc_empty[b], ((T >> 1) & 1) ^ 1, 32)) break;
+        const uint32_t b = T % (uint32_t)a.nacc;
+        if (!mbar_wait(&acc_empty[b], ((T / (uint32_t)a.nacc) & 1) ^ 1, 32)) break;
         tc_fence_after();
         const uint32_t d = tmem_base + b * (uint32_t)a.BNT;
         for (int kb = 0; kb < nkb; ++kb, ++L) {
@@ -515,16 +520,19 @@ __global__ void __launch_bounds__(THREADS, 1) conv_igemm_kernel(const __grid_con
     }
   } else {
     // ------------------------------------------------------------ epilogue
-    const int q = warp & 3, half = (warp - MMA_WARP - 1) >> 2;
+    // warps 8-11 drain the even accumulator tiles, warps 12-15 the odd ones: one warp per
+    // TMEM lane quarter, every 32-column chunk of its quarter, so two tiles drain at once
+    const int q = warp & 3, grp = (warp - MMA_WARP - 1) >> 2;
     uint32_t T = 0;
     bool ok = true;
     for (int it = blockIdx.x; it < a.items && ok; it += gridDim.x) {
       Item r;
       if (!item_of(a, it, r)) continue;
       if (kblocks_of(a, r) <= 0) continue;
-      const uint32_t b = T & 1;
-      ok = warp_wait(&acc_full[b], (T >> 1) & 1, 64);
-      ++T;
+      const uint32_t tt = T++;
+      if ((int)(tt & 1u) != grp) continue;
+      const uint32_t b = tt % (uint32_t)a.nacc;
+      ok = warp_wait(&acc_full[b], (tt / (uint32_t)a.nacc) & 1, 64);
       if (!ok) break;
       tc_fence_after();
       const int m = r.mt * BM + q * 32 + lane;  // this lane's GEMM row
@@ -566,25 +574,33 @@ __global__ void __launch_bounds__(THREADS, 1) conv_igemm_kernel(const __grid_con
       const uint32_t tb = tmem_base + ((uint32_t)(q * 32) << 16) + b * (uint32_t)a.BNT;
       const int n0 = r.nt * a.BN;
       const int ncols = min(a.BN, a.Nc - n0);
-      if (half * 32 >= ncols) {  // no chunk for this warp: hand the accumulator back at once
-        tc_fence_before();
-        __syncwarp();
-        if (lane == 0) mbar_arrive(&acc_empty[b]);
-      }
-      for (int c0 = half * 32; c0 < ncols; c0 += 64) {
+      for (int c0 = 0; c0 < ncols; c0 += 32) {
         uint32_t v[32];
         tmem_ld32_issue(tb + (uint32_t)c0, v);
         const int nn = min(32, ncols - c0);
-        float* __restrict__ dst = a.out + obase + (int64_t)(n0 + c0) * ostride;
         float mv[32];
         if (MODE == DGRAD && a.mask != nullptr) {
           // the chunk's 32 mask values are all loaded before its first store
           const float* __restrict__ mk = a.mask + obase + (int64_t)(n0 + c0) * ostride;
 #pragma unroll
           for (int i = 0; i < 32; ++i) mv[i] = __ldg(mk + (rv && i < nn ? (int64_t)i * ostride : 0));
+        } else if (MODE == DGRAD && a.mask_cl != nullptr) {
+          // the mask from the ReLU output's bf16 channels-last copy (nonzero exactly where
+          // the output is positive): this row's 32 channels in four 16-byte loads
+          const uint4* mk = reinterpret_cast<const uint4*>(a.mask_cl + (rv ? pix : 0) * a.mask_cp + n0 + c0);
+#pragma unroll
+          for (int k = 0; k < 4; ++k) {
+            const uint4 u = 8 * k < nn ? __ldg(mk + k) : make_uint4(0u, 0u, 0u, 0u);
+            const uint32_t wv[4] = {u.x, u.y, u.z, u.w};
+#pragma unroll
+            for (int h = 0; h < 4; ++h) {
+              mv[8 * k + 2 * h] = (wv[h] & 0xFFFFu) ? 1.f : 0.f;
+              mv[8 * k + 2 * h + 1] = (wv[h] >> 16) ? 1.f : 0.f;
+            }
+          }
         }
         tmem_wait(v);
-        if (c0 + 64 >= ncols) {  // this warp's last TMEM read of the item: hand the accumulator back
+        if (c0 + 32 >= ncols) {  // this warp's last TMEM read of the item: hand the accumulator back
           tc_fence_before();
           __syncwarp();
           if (lane == 0) mbar_arrive(&acc_empty[b]);
@@ -594,26 +610,42 @@ __global__ void __launch_bounds__(THREADS, 1) conv_igemm_kernel(const __grid_con
 #pragma unroll
         for (int i = 0; i < 32; ++i) {
           const float x = __uint_as_float(v[i]);
-          if (MODE == DGRAD && a.mask != nullptr) o[i] = x * (mv[i] > 0.f ? 1.f : 0.f);
+          if (MODE == DGRAD && (a.mask != nullptr || a.mask_cl != nullptr)) o[i] = x * (mv[i] > 0.f ? 1.f : 0.f);
           else if (MODE == FWD && a.relu) o[i] = x > 0.f ? x : 0.f;
           else o[i] = x;
         }
+        if (a.out != nullptr) {
+          float* __restrict__ dst = a.out + obase + (int64_t)(n0 + c0) * ostride;
 #pragma unroll
-        for (int i = 0; i < 32; ++i)
-          if (i < nn) dst[(int64_t)i * ostride] = o[i];
+          for (int i = 0; i < 32; ++i)
+            if (i < nn) dst[(int64_t)i * ostride] = o[i];
+        }
         if (MODE != WGRAD && a.out_cl != nullptr) {
           // the row's channels n0 + c0 .. + 31 of the channels-last bf16 copy, 16 bytes at a
           // time; channels past Nc (up to out_cp) are zero
           __nv_bfloat16* cl = a.out_cl + pix * a.out_cp + n0 + c0;
           const int room = a.out_cp - (n0 + c0);
+          // a ReLU output's copy keeps every positive value nonzero (below 2^-133, where
+          // round-to-nearest would give +0, the smallest bf16 subnormal instead), so the
+          // copy is also the exact Greater(pre, 0) mask of the ReLU VJP
+          const bool keep = MODE == FWD && a.relu;
 #pragma unroll
           for (int k = 0; k < 4; ++k)
-            if (8 * k < room)
-              *reinterpret_cast<uint4*>(cl + 8 * k) =
-                  make_uint4(pack_bf16(8 * k < nn ? o[8 * k] : 0.f, 8 * k + 1 < nn ? o[8 * k + 1] : 0.f),
-                             pack_bf16(8 * k + 2 < nn ? o[8 * k + 2] : 0.f, 8 * k + 3 < nn ? o[8 * k + 3] : 0.f),
-                             pack_bf16(8 * k + 4 < nn ? o[8 * k + 4] : 0.f, 8 * k + 5 < nn ? o[8 * k + 5] : 0.f),
-                             pack_bf16(8 * k + 6 < nn ? o[8 * k + 6] : 0.f, 8 * k + 7 < nn ? o[8 * k + 7] : 0.f));
+            if (8 * k < room) {
+              uint32_t wv[4];
+#pragma unroll
+              for (int h = 0; h < 4; ++h) {
+                const int i0 = 8 * k + 2 * h;
+                const float lo = i0 < nn ? o[i0] : 0.f, hi = i0 + 1 < nn ? o[i0 + 1] : 0.f;
+                uint32_t pw = pack_bf16(lo, hi);
+                if (keep) {
+                  if (lo > 0.f && (pw & 0xFFFFu) == 0u) pw |= 1u;
+                  if (hi > 0.f && (pw >> 16) == 0u) pw |= 1u << 16;
+                }
+                wv[h] = pw;
+              }
+              *reinterpret_cast<uint4*>(cl + 8 * k) = make_uint4(wv[0], wv[1], wv[2], wv[3]);
+            }
         }
       }
     }
@@ -707,8 +739,9 @@ static Plan plan(int mode, int64_t N, int64_t C, int64_t H, int64_t W, int64_t O
   // wgrad: B is MN-major in 64-column blocks
   a.BN = mode == WGRAD ? (int)std::min<int64_t>(256, Opw) : (int)std::min<int64_t>(256, (Nc + 15) / 16 * 16);
   a.BNT = (a.BN + 31) / 32 * 32;
+  a.nacc = 4 * a.BNT <= 512 ? 4 : 2;
   uint32_t cols = 32;
-  while (cols < (uint32_t)(2 * a.BNT)) cols <<= 1;
+  while (cols < (uint32_t)(a.nacc * a.BNT)) cols <<= 1;
   a.tmem_cols = cols;
   a.tiles_n = (int)ceil_div(Nc, a.BN);
   int64_t max_tiles = 0;
@@ -924,7 +957,7 @@ extern "C" int b200_conv2d_fwd_igemm(const float* x, const void* x_cl, const flo
   int rc = check_dims(N, C, H, W, O, KH, KW, OH, OW, sh, sw, pt, pl);
   if (rc) return rc;
   if (N == 0) return B200_OK;
-  B200_REQUIRE(x && w && y, "conv2d_fwd_igemm: null pointer");
+  B200_REQUIRE(x && w && (y || y_cl), "conv2d_fwd_igemm: null pointer");
   Plan p = plan(FWD, N, C, H, W, O, KH, KW, OH, OW, sh, sw, pt, pl);
   if (!p.ok) {
     set_error("conv2d_fwd_igemm: unsupported shape (%s)", p.why);
@@ -946,18 +979,24 @@ extern "C" int b200_conv2d_fwd_igemm(const float* x, const void* x_cl, const flo
   p.a.relu = relu ? 1 : 0;
   B200_REQUIRE((reinterpret_cast<uintptr_t>(y_cl) & 15) == 0, "conv2d_fwd_igemm: y_cl not 16-byte aligned");
   p.a.an = xn, p.a.bn = nullptr, p.a.bsrc = w, p.a.bimg = img, p.a.out = y, p.a.mask = nullptr;
+  p.a.mask_cl = nullptr, p.a.mask_cp = 0;
   p.a.out_cl = reinterpret_cast<__nv_bfloat16*>(y_cl), p.a.out_cp = (int)((O + 7) / 8 * 8);
   return launch<FWD>(p.a, p.smem, s);
 }
 
-extern "C" int b200_conv2d_dgrad_igemm(const float* dy, const void* dy_cl, const float* w, const float* mask, float* dx,
-                                       void* dx_cl, int64_t N, int64_t C, int64_t H, int64_t W, int64_t O, int64_t KH,
-                                       int64_t KW, int64_t OH, int64_t OW, int64_t sh, int64_t sw, int64_t pt, int64_t pl,
-                                       void* ws, size_t ws_bytes, void* stream) {
+extern "C" int b200_conv2d_dgrad_igemm(const float* dy, const void* dy_cl, const float* w, const float* mask,
+                                       const void* mask_cl, int64_t mask_cp, float* dx, void* dx_cl, int64_t N, int64_t C,
+                                       int64_t H, int64_t W, int64_t O, int64_t KH, int64_t KW, int64_t OH, int64_t OW,
+                                       int64_t sh, int64_t sw, int64_t pt, int64_t pl, void* ws, size_t ws_bytes,
+                                       void* stream) {
   int rc = check_dims(N, C, H, W, O, KH, KW, OH, OW, sh, sw, pt, pl);
   if (rc) return rc;
   if (N == 0) return B200_OK;
-  B200_REQUIRE(dy && w && dx, "conv2d_dgrad_igemm: null pointer");
+  B200_REQUIRE(dy && w && (dx || dx_cl), "conv2d_dgrad_igemm: null pointer");
+  B200_REQUIRE(!(mask && mask_cl), "conv2d_dgrad_igemm: mask and mask_cl both given");
+  B200_REQUIRE(!mask_cl || (mask_cp >= (C + 7) / 8 * 8 && mask_cp % 8 == 0 && (reinterpret_cast<uintptr_t>(mask_cl) & 15) == 0),
+               "conv2d_dgrad_igemm: mask_cl needs >= %lld channels (a multiple of 8) and 16-byte alignment",
+               (long long)((C + 7) / 8 * 8));
   Plan p = plan(DGRAD, N, C, H, W, O, KH, KW, OH, OW, sh, sw, pt, pl);
   if (!p.ok) {
     set_error("conv2d_dgrad_igemm: unsupported shape (%s)", p.why);
@@ -971,7 +1010,7 @@ extern "C" int b200_conv2d_dgrad_igemm(const float* dy, const void* dy_cl, const
   // pixels that no tap reaches (a class without taps: stride above the kernel size) are zero
   for (int c = 0; c < p.a.ncls; ++c)
     if (p.a.cls_k[c] == 0) {
-      cudaMemsetAsync(dx, 0, (size_t)N * C * H * W * 4, s);
+      if (dx) cudaMemsetAsync(dx, 0, (size_t)N * C * H * W * 4, s);
       if (dx_cl) cudaMemsetAsync(dx_cl, 0, (size_t)N * H * W * ((C + 7) / 8 * 8) * 2, s);
       if ((rc = check_launch("conv2d_dgrad_igemm(zero)"))) return rc;
       break;
@@ -986,6 +1025,7 @@ extern "C" int b200_conv2d_dgrad_igemm(const float* dy, const void* dy_cl, const
   p.a.relu = 0;
   B200_REQUIRE((reinterpret_cast<uintptr_t>(dx_cl) & 15) == 0, "conv2d_dgrad_igemm: dx_cl not 16-byte aligned");
   p.a.an = dyn, p.a.bn = nullptr, p.a.bsrc = w, p.a.bimg = img, p.a.out = dx, p.a.mask = mask;
+  p.a.mask_cl = reinterpret_cast<const __nv_bfloat16*>(mask_cl), p.a.mask_cp = (int)mask_cp;
   p.a.out_cl = reinterpret_cast<__nv_bfloat16*>(dx_cl), p.a.out_cp = (int)((C + 7) / 8 * 8);
   return launch<DGRAD>(p.a, p.smem, s);
 }
@@ -1022,7 +1062,7 @@ extern "C" int b200_conv2d_wgrad_igemm(const float* x, const void* x_cl, const f
   if (dy_cl) dyn = reinterpret_cast<__nv_bfloat16*>(const_cast<void*>(dy_cl));
   else if ((rc = repack(dy, dyn, N, O, OH * OW, p.a.OPW, s))) return rc;
   p.a.relu = 0;
-  p.a.an = xn, p.a.bn = dyn, p.a.bsrc = nullptr, p.a.out = part, p.a.mask = nullptr;
+  p.a.an = xn, p.a.bn = dyn, p.a.bsrc = nullptr, p.a.out = part, p.a.mask = nullptr, p.a.mask_cl = nullptr;
   rc = launch<WGRAD>(p.a, p.smem, s);
   if (rc) return rc;
   const int64_t total = O * (int64_t)p.a.M;
