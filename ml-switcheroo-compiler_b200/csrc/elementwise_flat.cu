@@ -199,7 +199,10 @@ __device__ __forceinline__ void wr(float (&R)[NREG][VG], int k, const float (&x)
 #undef B200_WR
 }
 
-template <int NREG>
+// NIN: input slots held in registers (2, 4 or the maximum 8): the loaded-up-front inputs
+// take NIN x VG registers, so small programs keep their register count (and the SM's
+// occupancy) low
+template <int NREG, int NIN>
 __global__ void __launch_bounds__(THREADS) ew_prog_kernel(const __grid_constant__ EwParams P) {
   const b200_ew_program& p = P.p;
   float R[NREG][VG];
@@ -215,18 +218,20 @@ __global__ void __launch_bounds__(THREADS) ew_prog_kernel(const __grid_constant_
     const bool full = base + VG <= P.n;
     // every input of the group is loaded up front, so the loads of all inputs are in
     // flight together; LOAD instructions then read these registers
-    float IN[B200_EW_MAX_IN][VG];
+    float IN[NIN][VG];
 #pragma unroll
-    for (int j = 0; j < B200_EW_MAX_IN; ++j)
+    for (int j = 0; j < NIN; ++j)
       if (j < nin) loadv<VG>(P, j, base, full, IN[j]);
     for (int i = 0; i < nins; ++i) {
       const b200_ew_ins I = p.ins[i];
       float x[VG], y[VG], res[VG];
       if (I.op == B200_EW_LOAD) {
         switch (I.a) {
-#define B200_LDIN(j)                                                  \
-  case j:                                                             \
-    _Pragma("unroll") for (int v = 0; v < VG; ++v) res[v] = IN[j][v]; \
+#define B200_LDIN(j)                                                                          \
+  case j:                                                                                     \
+    if constexpr (j < NIN) {                                                                  \
+      _Pragma("unroll") for (int v = 0; v < VG; ++v) res[v] = IN[j][v];                       \
+    }                                                                                         \
     break;
           B200_LDIN(0) B200_LDIN(1) B200_LDIN(2) B200_LDIN(3) B200_LDIN(4) B200_LDIN(5) B200_LDIN(6) B200_LDIN(7)
 #undef B200_LDIN
@@ -315,6 +320,57 @@ __global__ void __launch_bounds__(THREADS) ew_un8_kernel(const __grid_constant__
   }
 }
 
+// a chain of up to 4 ops, each operand an input, an immediate or the previous result
+// (e.g. (x > 0) * dy, or g * 1/36): straight-line per op (one warp-uniform dispatch per
+// op and 8 elements), no register file
+template <int OPK>
+__device__ __forceinline__ void apply_rt(int op, const float (&x)[V], const float (&y)[V], float (&r)[V]) {
+  switch (op) {
+#define B200_CH2(OPC)                                         \
+  case OPC:                                                   \
+    _Pragma("unroll") for (int v = 0; v < V; ++v) r[v] = apply2<OPC>(x[v], y[v]); \
+    return;
+    B200_CH2(B200_EW_ADD) B200_CH2(B200_EW_SUB) B200_CH2(B200_EW_MUL) B200_CH2(B200_EW_DIV) B200_CH2(B200_EW_MAX)
+    B200_CH2(B200_EW_MIN) B200_CH2(B200_EW_POW) B200_CH2(B200_EW_GT) B200_CH2(B200_EW_GE) B200_CH2(B200_EW_LT)
+    B200_CH2(B200_EW_EQ)
+#undef B200_CH2
+    default:
+#pragma unroll
+      for (int v = 0; v < V; ++v) r[v] = apply1(op, x[v]);
+  }
+}
+
+__global__ void __launch_bounds__(THREADS) ew_chain8_kernel(const __grid_constant__ EwParams P) {
+  const int64_t ng = (P.n + V - 1) / V;
+  const int nout = P.p.n_out, nch = P.nchain;
+  for (int64_t q = blockIdx.x * (int64_t)THREADS + threadIdx.x; q < ng; q += (int64_t)gridDim.x * THREADS) {
+    const int64_t base = q * V;
+    const bool full = base + V <= P.n;
+    float t[V];
+#pragma unroll
+    for (int v = 0; v < V; ++v) t[v] = 0.f;
+    for (int k = 0; k < nch; ++k) {
+      float xy[2][V];
+#pragma unroll
+      for (int i = 0; i < 2; ++i) {
+        const int src = P.csrc[k][i];
+        if (src >= 0) {
+          loadv<V>(P, src, base, full, xy[i]);
+        } else if (src == -1) {
+          const float c = P.cimm[k][i];
+#pragma unroll
+          for (int v = 0; v < V; ++v) xy[i][v] = c;
+        } else {
+#pragma unroll
+          for (int v = 0; v < V; ++v) xy[i][v] = t[v];
+        }
+      }
+      apply_rt<0>(P.cop[k], xy[0], xy[1], t);
+    }
+    for (int o = 0; o < nout; ++o) storev<V>(P, o, base, full, t);
+  }
+}
+
 // sum of inputs as a left fold, ((in[o0] + in[o1]) + in[o2]) + ..., stored to every output:
 // all inputs of a group are loaded before the first addition
 __global__ void __launch_bounds__(THREADS) ew_sum8_kernel(const __grid_constant__ EwParams P) {
@@ -379,6 +435,60 @@ static bool classify_sum(EwParams& P) {
   if (acc < 0 || stores == 0) return false;
   P.nsum = n;
   P.kind = 4;
+  return true;
+}
+
+// Recognise a chain: every op reads inputs, immediates or the result of the op just
+// before it (which nothing else reads), and the stores take the last op's result.
+static bool classify_chain(EwParams& P) {
+  const b200_ew_program& p = P.p;
+  int kind_of[B200_EW_MAX_REG];  // >= 0 input, -1 immediate, -2 the current result, -3 dead / unset
+  float imm_of[B200_EW_MAX_REG];
+  for (int i = 0; i < B200_EW_MAX_REG; ++i) kind_of[i] = -3, imm_of[i] = 0.f;
+  int n = 0, treg = -1;
+  bool stored = false;
+  for (int i = 0; i < p.n_ins; ++i) {
+    const b200_ew_ins& I = p.ins[i];
+    if (stored && I.op != B200_EW_STORE) return false;  // stores come last
+    if (I.op == B200_EW_LOAD) {
+      if ((int)I.dst == treg) return false;
+      kind_of[I.dst] = I.a;
+    } else if (I.op == B200_EW_IMM) {
+      if ((int)I.dst == treg) return false;
+      kind_of[I.dst] = -1;
+      imm_of[I.dst] = I.imm;
+    } else if (I.op == B200_EW_STORE) {
+      if (treg < 0 || (int)I.a != treg) return false;
+      stored = true;
+    } else if (I.op == B200_EW_WHERE || I.op == B200_EW_FMA) {
+      return false;
+    } else {
+      if (n >= 4) return false;
+      const bool unary = !(I.op == B200_EW_ADD || I.op == B200_EW_SUB || I.op == B200_EW_MUL || I.op == B200_EW_DIV ||
+                           I.op == B200_EW_MAX || I.op == B200_EW_MIN || I.op == B200_EW_POW || I.op == B200_EW_GT ||
+                           I.op == B200_EW_GE || I.op == B200_EW_LT || I.op == B200_EW_EQ);
+      const int regs[2] = {I.a, unary ? I.a : I.b};
+      int uses_t = 0;
+      for (int k = 0; k < 2; ++k) {
+        const int kd = kind_of[regs[k]];
+        if (kd == -3) return false;
+        if (kd == -2) {
+          if (regs[k] != treg) return false;
+          ++uses_t;
+        }
+        P.csrc[n][k] = kd;
+        P.cimm[n][k] = imm_of[regs[k]];
+      }
+      if (n > 0 && uses_t == 0) return false;  // the previous result would be lost
+      if (treg >= 0) kind_of[treg] = -3;      // read once: the chain moves on
+      P.cop[n++] = I.op;
+      treg = I.dst;
+      kind_of[treg] = -2;
+    }
+  }
+  if (n == 0 || treg < 0) return false;
+  P.nchain = n;
+  P.kind = 5;
   return true;
 }
 
@@ -451,6 +561,11 @@ int ew_flat_launch(EwParams& P, cudaStream_t s) {
     return check_launch("ew_run(unary)");
   }
   if (P.kind == 0) classify_sum(P);
+  if (P.kind == 0) classify_chain(P);
+  if (P.kind == 5) {
+    ew_chain8_kernel<<<blocks, THREADS, 0, s>>>(P);
+    return check_launch("ew_run(chain)");
+  }
   if (P.kind == 4) {
     ew_sum8_kernel<<<blocks, THREADS, 0, s>>>(P);
     return check_launch("ew_run(sum)");
@@ -475,9 +590,16 @@ int ew_flat_launch(EwParams& P, cudaStream_t s) {
     else hi = std::max<int>(std::max<int>(I.dst, I.a), std::max<int>(I.b, I.c));
     nreg = std::max(nreg, hi + 1);
   }
-  if (nreg <= 4) ew_prog_kernel<4><<<gblocks, THREADS, 0, s>>>(P);
-  else if (nreg <= 8) ew_prog_kernel<8><<<gblocks, THREADS, 0, s>>>(P);
-  else ew_prog_kernel<16><<<gblocks, THREADS, 0, s>>>(P);
+#define B200_PROG(NR)                                                                      \
+  do {                                                                                     \
+    if (p.n_in <= 2) ew_prog_kernel<NR, 2><<<gblocks, THREADS, 0, s>>>(P);                 \
+    else if (p.n_in <= 4) ew_prog_kernel<NR, 4><<<gblocks, THREADS, 0, s>>>(P);            \
+    else ew_prog_kernel<NR, B200_EW_MAX_IN><<<gblocks, THREADS, 0, s>>>(P);                \
+  } while (0)
+  if (nreg <= 4) B200_PROG(4);
+  else if (nreg <= 8) B200_PROG(8);
+  else B200_PROG(16);
+#undef B200_PROG
   return check_launch("ew_run(program)");
 }
 

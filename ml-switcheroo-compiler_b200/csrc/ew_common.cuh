@@ -26,6 +26,10 @@ struct EwParams {
   int32_t kind, sop, sa, sb;
   // kind 4: a left fold of additions over inputs sumord[0 .. nsum) (in that order)
   int32_t nsum, sumord[B200_EW_MAX_IN];
+  // kind 5: a chain of up to 4 unary / binary ops, t = op_k(x, y), each operand an input
+  // (index >= 0), an immediate (-1, value in cimm) or the previous op's result (-2)
+  int32_t nchain, cop[4], csrc[4][2];
+  float cimm[4][2];
 };
 
 // n / d for 32-bit n with a precomputed (mul, shr): q = (umulhi(n, mul) + n) >> shr

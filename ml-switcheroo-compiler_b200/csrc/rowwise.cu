@@ -50,6 +50,33 @@ __global__ void __launch_bounds__(256) reduce_rows_warp_kernel(const void* __res
   if (lane == 0) y[row] = (OP == B200_RED_MEAN) ? acc / (float)red : acc;
 }
 
+// inner == 1 with very short rows (red <= 64): G = 8 lanes per row, four rows per warp
+// (a warp reads four consecutive rows at once); lane l of a group combines elements l,
+// l + 8, ... in order, then a fixed xor-butterfly over the group
+template <int OP>
+__global__ void __launch_bounds__(256) reduce_rows_group_kernel(const void* __restrict__ x, int dt, float* __restrict__ y,
+                                                                int64_t rows, int64_t red) {
+  constexpr int G = 8;
+  const int64_t row = (blockIdx.x * (int64_t)blockDim.x + threadIdx.x) / G;
+  const int sub = threadIdx.x % G;
+  const bool live = row < rows;
+  float acc = (OP == B200_RED_MAX) ? -INFINITY : 0.f;
+  if (live) {
+    for (int64_t i = sub; i < red; i += G) {
+      const float v = load_as_f32(x, row * red + i, dt);
+      if (OP == B200_RED_MAX) acc = fmaxf(acc, v);
+      else acc += v;
+    }
+  }
+#pragma unroll
+  for (int o = G / 2; o > 0; o >>= 1) {
+    const float v = __shfl_xor_sync(0xffffffffu, acc, o);
+    if (OP == B200_RED_MAX) acc = fmaxf(acc, v);
+    else acc += v;
+  }
+  if (live && sub == 0) y[row] = (OP == B200_RED_MEAN) ? acc / (float)red : acc;
+}
+
 // inner > 1: each thread owns one (outer, inner) column over a chunk of `red`. With one
 // chunk the result goes straight to y; with several, chunk z writes its partial to
 // part[z][outer][inner] and reduce_splits_kernel combines them in chunk order, so the
@@ -354,6 +381,15 @@ extern "C" int b200_reduce(int dt, const void* x, float* y, int64_t outer, int64
   }
   if (inner == 1) {
     B200_REQUIRE(outer <= 2147483647LL, "reduce: too many rows");
+    if (red <= 64) {
+      const unsigned g = (unsigned)ceil_div(outer * 8, (int64_t)256);
+      switch (op) {
+        case B200_RED_SUM: reduce_rows_group_kernel<B200_RED_SUM><<<g, 256, 0, s>>>(x, dt, y, outer, red); break;
+        case B200_RED_MEAN: reduce_rows_group_kernel<B200_RED_MEAN><<<g, 256, 0, s>>>(x, dt, y, outer, red); break;
+        default: reduce_rows_group_kernel<B200_RED_MAX><<<g, 256, 0, s>>>(x, dt, y, outer, red); break;
+      }
+      return check_launch("reduce(short rows)");
+    }
     if (red <= 1024) {
       const unsigned g = (unsigned)ceil_div(outer * 32, (int64_t)256);
       switch (op) {

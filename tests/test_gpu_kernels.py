@@ -67,6 +67,12 @@ def test_reductions_axes_and_split():
             np.testing.assert_allclose(got, np.mean(x, axis=axis, keepdims=kd), rtol=1e-5, atol=1e-5)
             got = to_np(ops.op_reduce_max(T(x), axis=axis, keepdims=kd))
             np.testing.assert_array_equal(got, np.max(x, axis=axis, keepdims=kd))
+    # short rows (8 lanes per row), a partial last warp, a bf16 source
+    z = r.standard_normal((1001, 36), dtype=np.float32)
+    np.testing.assert_allclose(to_np(ops.op_reduce_mean(T(z), axis=-1)), z.mean(-1), rtol=1e-5, atol=1e-6)
+    np.testing.assert_array_equal(to_np(ops.op_reduce_max(T(z), axis=-1)), z.max(-1))
+    zb = T(z).to(torch.bfloat16)
+    np.testing.assert_allclose(to_np(ops.op_reduce_sum(zb, axis=-1)), to_np(zb.float()).sum(-1), rtol=1e-5, atol=1e-5)
     # column reduction with many rows (split + atomics path)
     y = r.standard_normal((8192, 64), dtype=np.float32)
     np.testing.assert_allclose(to_np(ops.op_reduce_sum(T(y), axis=0)), y.sum(0), rtol=1e-4, atol=1e-3)
@@ -774,6 +780,37 @@ def test_elementwise_merged_dims():
     xp = X.permute(0, 2, 3, 1)  # [64, 6, 6, 128] view over NCHW storage
     gp = T(g).permute(0, 2, 3, 1)
     np.testing.assert_allclose(to_np(ops.op_multiply(xp, gp)), x.transpose(0, 2, 3, 1) * g.transpose(0, 2, 3, 1), rtol=1e-6)
+
+
+def test_elementwise_chains_and_programs():
+    """Straight-line op chains (immediates on either side, the previous result on the right,
+    unary links, ragged length) and a program that reuses an earlier value (the general
+    register-program kernel) agree with numpy's fp32 results."""
+    from b200 import ops
+
+    r = rng(9)
+    n = 1000003
+    x = r.standard_normal(n).astype(np.float32)
+    y = r.standard_normal(n).astype(np.float32)
+    X, Y = T(x), T(y)
+    p = ops.Prog()
+    a, b = p.load(X), p.load(Y)
+    c = p.imm(0.5)
+    t1 = p.op("SUB", c, a)       # 0.5 - x
+    t2 = p.op("MUL", b, t1)      # y * (0.5 - x): the result on the right
+    t3 = p.op("TANH", t2)
+    t4 = p.op("MAX", t3, p.imm(-0.25))
+    out = p.run([(t4, torch.float32), (t4, torch.bfloat16)], (n,))
+    ref = np.maximum(np.tanh(y * (np.float32(0.5) - x)), np.float32(-0.25))
+    np.testing.assert_allclose(to_np(out[0]), ref, rtol=1e-5, atol=1e-6)
+    np.testing.assert_allclose(to_np(out[1].float()), ref, rtol=1e-2, atol=1e-2)
+    p = ops.Prog()
+    a, b = p.load(X), p.load(Y)
+    t1 = p.op("MUL", a, b)
+    t2 = p.op("ADD", t1, a)
+    t3 = p.op("MUL", t1, t2)     # t1 read again after t2: not a chain
+    out = p.run([(t3, torch.float32)], (n,))
+    np.testing.assert_array_equal(to_np(out[0]), (x * y) * ((x * y) + x))
 
 
 @pytest.mark.parametrize("R,V", [(33, 32000), (17, 1000), (9, 4096), (5, 12)])
