@@ -234,6 +234,15 @@ int b200_gemm_batched2(int ab_dtype, int c_dtype, const void* A, const void* B, 
                        int64_t sB_out, int64_t sB_in, int64_t rsB, int64_t csB, int64_t sC_out, int64_t sC_in, int64_t ldc,
                        float alpha, const float* bias, int epilogue, void* aux, void* C2, void* stream);
 
+/* The same bf16 tensor-core matmul with fp32 C = (A.B + bias) + resid: the Add of a residual
+ * connection that follows a bias Add (numpy/eager/math_binary.py:9-20 twice), fused into
+ * the epilogue and rounded as the two Adds are (the bias sum first). resid (F32) has C's
+ * layout (batch strides sC_out / sC_in, leading dimension ldc); bias may be NULL. */
+int b200_gemm_batched2_residual(const void* A, const void* B, float* C, int64_t b_out, int64_t b_in, int64_t M, int64_t N,
+                                int64_t K, int64_t sA_out, int64_t sA_in, int64_t rsA, int64_t csA, int64_t sB_out,
+                                int64_t sB_in, int64_t rsB, int64_t csB, int64_t sC_out, int64_t sC_in, int64_t ldc,
+                                const float* bias, const float* resid, void* stream);
+
 /* Conv2D (numpy/eager/conv.py:462-489) and its VJPs Conv2DInputGrad (conv.py:634-697),
  * Conv2DWeightGrad (conv.py:699-764): NCHW activations (F32), OIHW weights (F32),
  * explicit zero padding (pt, pl; bottom/right implied by the output size), stride

@@ -126,6 +126,7 @@ SIGNATURES = {
     "b200_conv2d_igemm_workspace_bytes": ([_I32] + [_I64] * 13, C.c_size_t),
     "b200_conv2d_channels_last": ([_P, _P] + [_I64] * 4 + [_P], C.c_int),
     "b200_conv2d_fwd_igemm": ([_P, _P, _P, _P, _P] + [_I64] * 13 + [_I32, _P, C.c_size_t, _P], C.c_int),
+    "b200_gemm_batched2_residual": ([_P, _P, _P] + [_I64] * 16 + [_P, _P, _P], C.c_int),
     "b200_conv2d_dgrad_igemm": ([_P, _P, _P, _P, _P, _I64, _P, _P] + [_I64] * 13 + [_P, C.c_size_t, _P], C.c_int),
     "b200_conv2d_wgrad_igemm": ([_P, _P, _P, _P, _P] + [_I64] * 13 + [_P, C.c_size_t, _P], C.c_int),
     "b200_conv2d_fwd": ([_I32, _P, _P, _P] + [_I64] * 13 + [_P], C.c_int),

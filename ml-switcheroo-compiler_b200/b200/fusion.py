@@ -349,6 +349,53 @@ def find_gemm_epilogue(g: Graph, live: dict[str, Node], meta: dict[str, Meta], u
     return found
 
 
+def find_gemm_residual(g: Graph, live: dict[str, Node], meta: dict[str, Meta], users: dict[str, list[str]],
+                       outputs: set[str]) -> list[Match]:
+    """Add(R, Add(Matmul(A, B), bias)), either operand order of the outer Add, where the
+    matmul and the bias sum feed nothing else: one GEMM whose epilogue adds the bias and
+    then R (a transformer's residual connection after an output projection)."""
+    found = []
+    pat = Op("Add", Op("Matmul", Var("A"), Var("B"), name="mm"), Var("bias"), name="pre")
+    for nid, node in live.items():
+        if _op_name(node) != "Add" or len(node.inputs) != 2:
+            continue
+        for k in (0, 1):
+            inner, rid = live.get(node.inputs[k]), node.inputs[1 - k]
+            if inner is None or _op_name(inner) != "Add":
+                continue
+            bind: dict[str, str] = {}
+            cov: set[str] = set()
+            if not match(pat, inner.id, g, bind, cov):
+                continue
+            mm = g.nodes[bind["mm"]]
+            if mm.attributes.get("transpose_a") or mm.attributes.get("transpose_b"):
+                continue
+            mo, mr, mbias, mB = meta.get(nid), meta.get(rid), meta.get(bind["bias"]), meta.get(bind["B"])
+            if any(x is None or x.scalar for x in (mo, mr, mbias, mB)) or len(mB.shape) != 2:
+                continue
+            N = mo.shape[-1]
+            if mbias.shape != (N,) or mr.shape != mo.shape or meta[bind["pre"]].shape != mo.shape or \
+                    meta[bind["mm"]].shape != mo.shape or mr.dtype != torch.float32 or mo.dtype != torch.float32:
+                continue
+            cov.add(nid)
+            if rid in cov or any(v in outputs or any(u not in cov for u in users.get(v, [])) for v in (bind["mm"], bind["pre"])):
+                continue
+            bind.update({"R": rid, "act": nid})
+            found.append(Match("gemm_bias_residual", bind, {c for c in cov if c in live or g.nodes[c].op_type == "Constant"},
+                               {"act": nid}))
+            break
+    return found
+
+
+def gemm_residual_step(m: Match) -> Step:
+    b = m.bind
+
+    def run(env: dict) -> None:
+        env[b["act"]] = ops.gemm(env[b["A"]], env[b["B"]], bias=env[b["bias"]], resid=env[b["R"]])
+
+    return Step([b["act"]], [b["A"], b["B"], b["bias"], b["R"]], run, "gemm_bias_residual")
+
+
 def gemm_epilogue_step(m: Match) -> Step:
     b, o = m.bind, m.outputs
     kind = m.kind.replace("_dual", "")
@@ -1484,6 +1531,12 @@ def plan_steps(graph: Graph, nodes: list[Node], sample: dict[str, Any]) -> list[
             m.extra_inputs = list(m.mm_node.inputs)
             groups.append((sorted(m.covered), stepper(m)))
             taken |= m.covered
+
+    for m in find_gemm_residual(graph, live, meta, users, outputs):
+        if m.covered & taken:
+            continue
+        groups.append((sorted(m.covered), gemm_residual_step(m)))
+        taken |= m.covered
 
     for m in find_gemm_epilogue(graph, live, meta, users, outputs):
         if m.covered & taken:

@@ -814,12 +814,26 @@ def _gemm_operand(t: torch.Tensor, ab: torch.dtype) -> torch.Tensor:
 
 def gemm(a: torch.Tensor, b: torch.Tensor, *, bias: torch.Tensor | None = None, epilogue: int = L.EPI_NONE,
          alpha: float = 1.0, out_dtype: torch.dtype = torch.float32, want_mask: bool = False,
-         ab_dtype: torch.dtype | None = None, act_bf16: bool = False):
+         ab_dtype: torch.dtype | None = None, act_bf16: bool = False, resid: torch.Tensor | None = None):
     """numpy-style matmul of a [..., M, K] and b [..., K, N] with broadcast batch dims.
 
     Returns C = act(alpha a.b + bias) [, mask]. With ``act_bf16`` it returns
     (pre, act_in_bf16[, mask]): C holds the pre-activation and the activation is written
-    in bf16 by the same epilogue."""
+    in bf16 by the same epilogue. ``resid`` (fp32, C's shape; no activation, mask or
+    alpha): C = (a.b + bias) + resid, the residual Add in the epilogue of the bf16 kernel,
+    else as a separate Add."""
+    if resid is not None:
+        fused = (not act_bf16 and not want_mask and epilogue == L.EPI_NONE and alpha == 1.0 and out_dtype == torch.float32
+                 and resid.dtype == torch.float32)
+        if fused:
+            y = _gemm_residual(a, b, bias, resid, ab_dtype)
+            if y is not None:
+                return y
+        y = gemm(a, b, bias=bias, epilogue=epilogue, alpha=alpha, out_dtype=out_dtype, want_mask=want_mask,
+                 ab_dtype=ab_dtype, act_bf16=act_bf16)
+        if want_mask or act_bf16:
+            raise UnimplementedMathError("gemm residual with a mask or a dual output")
+        return op_add(y, resid)
     if act_bf16:
         return _gemm_dual(a, b, bias=bias, epilogue=epilogue, alpha=alpha, out_dtype=out_dtype, want_mask=want_mask,
                           ab_dtype=ab_dtype)
@@ -1021,6 +1035,36 @@ def _gemm_split_k(A: torch.Tensor, B: torch.Tensor, S: int, out_dtype: torch.dty
     # S chunks summed in order (M N columns fill the GPU: no further split)
     L.call("b200_reduce", code(part), part.data_ptr(), C_.data_ptr(), 1, S, M * N, L.RED_SUM, None, 0, stream_ptr())
     return C_ if out_dtype == torch.float32 else cast(C_, out_dtype)
+
+
+def _gemm_residual(a: torch.Tensor, b: torch.Tensor, bias: torch.Tensor | None, resid: torch.Tensor,
+                   ab_dtype: torch.dtype | None) -> torch.Tensor | None:
+    """(a.b + bias) + resid for a [..., M, K] (contiguous or 2-D) and a 2-D b [K, N] on the
+    tcgen05 kernel, or None when the operands do not fit it."""
+    if ab_dtype is None:
+        ab_dtype = torch.bfloat16 if Config.matmul_dtype == "bf16" else torch.float32
+    if ab_dtype != torch.bfloat16 or a.dim() < 2 or b.dim() != 2 or (a.dim() > 2 and not a.is_contiguous()):
+        return None
+    K, N = b.shape
+    if a.shape[-1] != K:
+        raise ValueError(f"matmul: shapes {tuple(a.shape)} and {tuple(b.shape)} not aligned")
+    out_shape = (*a.shape[:-1], N)
+    if tuple(resid.shape) != out_shape or not resid.is_contiguous():
+        return None
+    a2 = a.reshape(-1, K)
+    M = a2.shape[0]
+    A = _gemm_operand(a2, torch.bfloat16)
+    B = _gemm_operand(b, torch.bfloat16) if A is not None else None
+    if A is None or B is None:
+        return None
+    bc = None if bias is None else contiguous(cast(bias, torch.float32))
+    if bc is not None and bc.numel() != N:
+        return None
+    C_ = torch.empty(out_shape, dtype=torch.float32, device=device())
+    if M and N:
+        L.call("b200_gemm_batched2_residual", A.data_ptr(), B.data_ptr(), C_.data_ptr(), 1, 1, M, N, K, 0, 0, A.stride(-2),
+               A.stride(-1), 0, 0, B.stride(-2), B.stride(-1), 0, 0, N, _ptr(bc), resid.data_ptr(), stream_ptr())
+    return C_
 
 
 def gemm_out(a: torch.Tensor, b: torch.Tensor, out: torch.Tensor, out2: torch.Tensor | None = None,

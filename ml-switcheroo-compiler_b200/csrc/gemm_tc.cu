@@ -53,6 +53,7 @@ struct Args {
   int b_in;                          // inner batch count (z = z_out * b_in + z_in)
   int a_bc_out, a_bc_in, b_bc_out, b_bc_in;  // operand shared along that batch level (stride 0)
   int64_t sC_in;                     // C stride of the inner batch level (sC = outer)
+  const float* resid;                // optional fp32 residual in C's layout, added after the bias
 };
 
 // ---- CTA pairs (tcgen05 cta_group::2) ----
@@ -306,6 +307,21 @@ __device__ __forceinline__ void gemm_body(const CUtensorMap& mapA, const CUtenso
 #pragma unroll
           for (int i = 0; i < 32; ++i) v[i] = args.alpha * __uint_as_float(cur[i]);
         }
+        if (args.resid && row < args.M) {
+          // the residual Add that follows the bias Add: y = (acc + bias) + r, rounded twice
+          // as the two Adds are
+          const float* rp = args.resid + (int64_t)zo * args.sC + (int64_t)zi * args.sC_in + row * args.ldc + cbase;
+          if (cbase + 32 <= args.N && ((reinterpret_cast<uintptr_t>(rp) & 15) == 0)) {
+#pragma unroll
+            for (int i = 0; i < 32; i += 4) {
+              const float4 t = __ldg(reinterpret_cast<const float4*>(rp + i));
+              v[i] += t.x; v[i + 1] += t.y; v[i + 2] += t.z; v[i + 3] += t.w;
+            }
+          } else {
+            for (int i = 0; i < 32; ++i)
+              if (cbase + i < args.N) v[i] += __ldg(rp + i);
+          }
+        }
         if (args.aux) {
 #pragma unroll
           for (int i = 0; i < 32; ++i) mbits |= (v[i] > 0.f ? 1u : 0u) << i;
@@ -531,7 +547,7 @@ static bool use_pairs(int64_t M, int64_t N) {
 int gemm_bf16_tcgen05_b2(int c_dt, const void* A, const void* B, void* C, int64_t b_out, int64_t b_in, int64_t M, int64_t N,
                          int64_t K, int64_t sA_out, int64_t sA_in, int64_t rsA, int64_t csA, int64_t sB_out, int64_t sB_in,
                          int64_t rsB, int64_t csB, int64_t sC_out, int64_t sC_in, int64_t ldc, float alpha, const float* bias,
-                         int epi, void* aux, void* C2, cudaStream_t s) {
+                         int epi, void* aux, void* C2, const float* resid, cudaStream_t s) {
   using namespace tc;
   // operand majors: A K-major if csA == 1, MN-major if rsA == 1; B K-major if rsB == 1, MN-major if csB == 1
   int a_mn, b_mn;
@@ -601,6 +617,7 @@ int gemm_bf16_tcgen05_b2(int c_dt, const void* A, const void* B, void* C, int64_
   a.a_bc_in = a_bc_in;
   a.b_bc_out = b_bc_out;
   a.b_bc_in = b_bc_in;
+  a.resid = resid;
   B200_REQUIRE(ceil_div(M, BM) <= 65535, "gemm(bf16): M too large");
   CUtensorMap mc, mc2, maux;
   memset(&mc, 0, sizeof(mc));
@@ -629,7 +646,7 @@ int gemm_bf16_tcgen05(int c_dt, const void* A, const void* B, void* C, int64_t b
                       int64_t sA, int64_t rsA, int64_t csA, int64_t sB, int64_t rsB, int64_t csB, int64_t sC, int64_t ldc,
                       float alpha, const float* bias, int epi, void* aux, cudaStream_t s) {
   return gemm_bf16_tcgen05_b2(c_dt, A, B, C, batch, 1, M, N, K, sA, 0, rsA, csA, sB, 0, rsB, csB, sC, 0, ldc, alpha, bias, epi,
-                              aux, nullptr, s);
+                              aux, nullptr, nullptr, s);
 }
 
 }  // namespace b200
@@ -654,5 +671,17 @@ extern "C" int b200_gemm_batched2(int ab_dt, int c_dt, const void* A, const void
   }
   if (b_out == 0 || b_in == 0 || M == 0 || N == 0) return B200_OK;
   return gemm_bf16_tcgen05_b2(c_dt, A, B, C, b_out, b_in, M, N, K, sA_out, sA_in, rsA, csA, sB_out, sB_in, rsB, csB, sC_out,
-                              sC_in, ldc, alpha, bias, epi, aux, C2, as_stream(stream));
+                              sC_in, ldc, alpha, bias, epi, aux, C2, nullptr, as_stream(stream));
+}
+
+extern "C" int b200_gemm_batched2_residual(const void* A, const void* B, float* C, int64_t b_out, int64_t b_in, int64_t M,
+                                           int64_t N, int64_t K, int64_t sA_out, int64_t sA_in, int64_t rsA, int64_t csA,
+                                           int64_t sB_out, int64_t sB_in, int64_t rsB, int64_t csB, int64_t sC_out,
+                                           int64_t sC_in, int64_t ldc, const float* bias, const float* resid, void* stream) {
+  B200_REQUIRE(A && B && C && resid, "gemm_batched2_residual: null operand");
+  B200_REQUIRE(b_out >= 0 && b_in >= 0 && M >= 0 && N >= 0 && K >= 0, "gemm_batched2_residual: negative size");
+  B200_REQUIRE(ldc >= N, "gemm_batched2_residual: ldc < N");
+  if (b_out == 0 || b_in == 0 || M == 0 || N == 0) return B200_OK;
+  return gemm_bf16_tcgen05_b2(B200_F32, A, B, C, b_out, b_in, M, N, K, sA_out, sA_in, rsA, csA, sB_out, sB_in, rsB, csB, sC_out,
+                              sC_in, ldc, 1.f, bias, B200_EPI_NONE, nullptr, nullptr, resid, as_stream(stream));
 }

@@ -538,6 +538,31 @@ def test_conv2d_implicit_gemm_bounds():
         ops.Config.conv_dtype = "f32"
 
 
+@pytest.mark.parametrize("shape", [((300, 256), (256, 384), True), ((4, 64, 128), (128, 200), True),
+                                   ((512, 1024), (1024, 1024), False)])
+def test_gemm_residual_epilogue_matches_separate_add(shape):
+    """(a.b + bias) + r from the GEMM epilogue is bit-identical to the GEMM with its bias
+    followed by a separate Add (the same two fp32 roundings), for single-CTA and CTA-pair
+    tiles, a ragged N, a folded batch and no bias; the planner's pattern picks it up."""
+    from b200 import ops
+
+    (sa, sb, with_bias) = shape
+    r = rng(sum(sa) + sum(sb))
+    a = T(r.standard_normal(sa).astype(np.float32))
+    b = T((r.standard_normal(sb) / np.sqrt(sb[0])).astype(np.float32))
+    bias = T(r.standard_normal(sb[1]).astype(np.float32)) if with_bias else None
+    res = T(r.standard_normal(sa[:-1] + (sb[1],)).astype(np.float32))
+    ops.Config.matmul_dtype = "bf16"
+    try:
+        fused = ops.gemm(a, b, bias=bias, resid=res)
+        # a zero bias keeps the reference GEMM off the split-K path (same summation order)
+        zb = bias if bias is not None else torch.zeros(sb[1], device="cuda")
+        ref = ops.op_add(ops.gemm(a, b, bias=zb), res)
+    finally:
+        ops.Config.matmul_dtype = "f32"
+    np.testing.assert_array_equal(to_np(fused), to_np(ref))
+
+
 def test_gemm_bf16_two_level_batch_views():
     """Attention-style head-split views go to the tensor cores without copies."""
     from b200 import ops
